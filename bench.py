@@ -1,0 +1,364 @@
+"""Benchmark of the q8-block32 MoE decode path.
+
+A step is one token through one MoE FFN layer (Decoder::experts at decode):
+router logits -> top-6 of 64 experts -> six SwiGLU experts (gate/up
+[896x1280], down [1280x896]) plus the fused shared expert (width 1792), all
+q8-block32, FP32 activations -> ordered combine.  Inputs are seeded synthetic
+data with the configuration's distributions (x ~ N(0,1), logits ~ N(0,1),
+int8 weights uniform in [-127,127], scales ~ U(1e-4,1e-2)).
+
+metric  : q8-block32 expert GEMV GB/s = algorithmic bytes / time, where the
+          algorithmic bytes of a step are the int8 weights + fp32 scales of
+          the 7 FFNs it touches + x + logits + y (30,976,256 B).
+value   : device-resident inputs, K steps replayed from CUDA graphs; each
+          step uses the next of 8 distinct layers (2.0 GB > 126 MB L2), so
+          weights come from HBM.
+e2e     : the same metric through the C ABI's host-buffer entry point
+          (uocr_moe_forward_host): pinned host x/logits copied in and y copied
+          out inside the timed region, one synchronous call per step.
+--impl reference: the reference's scalar CPU path (oracle port, all host
+          threads) on the same workload.
+Multi-GPU (torchrun): every rank runs its own token stream (weak scaling,
+no collective on the data path); time is the max over ranks.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "unlimited-ocr-kernel_b200")
+for p in (ROOT, PKG):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+H, F, FS, E, TOPK = 1280, 896, 1792, 64, 6
+MAT_BYTES = lambda r, c: r * c + r * ((c + 31) // 32) * 4
+STEP_WEIGHT_BYTES = TOPK * 3 * MAT_BYTES(F, H) + 3 * MAT_BYTES(FS, H)  # 30,965,760
+STEP_BYTES = STEP_WEIGHT_BYTES + H * 4 + E * 4 + H * 4
+METRIC = "q8-block32 expert GEMV GB/s (MoE decode layer, config 1)"
+PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FALLBACK_HBM = 6650.0
+
+
+def peak_hbm():
+    try:
+        with open(PEAKS_PATH) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lines:
+            parts = [p.strip() for p in l.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl" if os.environ.get("BENCH_BACKEND") != "gloo" else "gloo",
+                                timeout=datetime.timedelta(seconds=120))
+    return world, rank, local
+
+
+def build_layers(ctx, n_layers, device, seed):
+    """n_layers MoE layers of config-1 shapes, generated on the device."""
+    import torch
+
+    import uocr_q8
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    layers = []
+
+    def mat(r, c):
+        w = torch.randint(-127, 128, (r, c), dtype=torch.int8, device=device, generator=g)
+        s = (torch.rand((r, (c + 31) // 32), device=device, generator=g) * (1e-2 - 1e-4) + 1e-4)
+        return uocr_q8.Int8Matrix.from_device(r, c, w, s.float().contiguous(), ctx)
+
+    for _ in range(n_layers):
+        shared = [mat(FS, H), mat(FS, H), mat(H, FS)]
+        experts = [[mat(F, H), mat(F, H), mat(H, F)] for _ in range(E)]
+        layers.append(uocr_q8.MoeLayer(ctx, shared, experts, TOPK))
+    return layers
+
+
+def run_ours(args):
+    import torch
+
+    import uocr_q8
+    world, rank, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    ctx = uocr_q8.GpuContext(local)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream)
+    n_layers = args.layers
+    layers = build_layers(ctx, n_layers, dev, 1234 + rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(99 + rank)
+    chunk = args.graph_steps
+    n_inputs = chunk
+    xs = torch.randn((n_inputs, 1, H), device=dev, generator=gen)
+    lg = torch.randn((n_inputs, 1, E), device=dev, generator=gen)
+    ys = torch.empty((n_inputs, 1, H), device=dev)
+    torch.cuda.synchronize()
+
+    def enqueue(i):
+        layers[i % n_layers].forward_device(xs[i % n_inputs], lg[i % n_inputs], 0, ys[i % n_inputs])
+
+    with torch.cuda.stream(stream):  # eager pass: sizes the context workspace
+        for i in range(chunk):
+            enqueue(i)
+    ctx.sync()
+    # capture `chunk` consecutive steps (distinct layers and tokens) in a graph
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(chunk):
+            enqueue(i)
+    reps = max(1, args.steps // chunk)
+    steps = reps * chunk
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    ctx.sync()
+
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            stop.record(stream)
+        stop.synchronize()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(stop)
+    ctx.sync()
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    ms_step = ms / steps
+    value = world * STEP_BYTES * steps / (ms * 1e-3) / 1e9
+
+    # ---- end to end: host buffers through the C ABI, one call per step
+    e2e_steps = min(steps, args.e2e_steps)
+    hx = torch.empty((n_inputs, 1, H), pin_memory=True)
+    hl = torch.empty((n_inputs, 1, E), pin_memory=True)
+    hy = torch.empty((n_inputs, 1, H), pin_memory=True)
+    hx.copy_(xs.cpu())
+    hl.copy_(lg.cpu())
+    for i in range(3):
+        layers[i % n_layers].forward_host_ptrs(hx[i].data_ptr(), hl[i].data_ptr(), 1, hy[i].data_ptr())
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        j = i % n_inputs
+        layers[i % n_layers].forward_host_ptrs(hx[j].data_ptr(), hl[j].data_ptr(), 1, hy[j].data_ptr())
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = world * STEP_BYTES * e2e_steps / e2e_s / 1e9
+
+    peak, peak_kind = peak_hbm()
+    result = None
+    if rank == 0:
+        cpu = cpu_baseline(args) if (world == 1 and not args.no_cpu) else None
+        result = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms_step, 6),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic (seeded; config-1 distributions)",
+            "config": {"workload": "config1_moe_decode_layer", "tokens_per_step": 1,
+                       "hidden": H, "experts": E, "top_k": TOPK, "expert_width": F,
+                       "shared_width": FS, "mode": "weights_only (fp32 activations)",
+                       "l2": f"rotating pool of {n_layers} layers x 255.5 MB (> 126 MB L2)",
+                       "parallelism": f"dp{world} (independent token streams)",
+                       "bytes_per_step": STEP_BYTES},
+            "e2e": {"value": round(e2e, 3), "unit": "GB/s", "steps": e2e_steps,
+                    "us_per_step": round(e2e_s / e2e_steps * 1e6, 3),
+                    "h2d_bytes_per_step": (H + E) * 4, "d2h_bytes_per_step": H * 4},
+            "roofline": {"bound": "hbm", "kernel": "moe_up_kernel+moe_down_kernel (one PDL pair per step)",
+                         "achieved": round(STEP_BYTES / (ms_step * 1e-3) / 1e9, 2),
+                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(STEP_BYTES / (ms_step * 1e-3) / 1e9 / peak, 4),
+                         "traffic": args.traffic},
+            "gpu_launches": 2 * steps,
+            "clocks": clocks.summary(),
+        }
+        if cpu:
+            result["cpu_baseline"] = cpu
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        del graph
+        dist.destroy_process_group()
+    return result
+
+
+def make_cpu_layer(seed):
+    import oracle
+    rng = np.random.default_rng(seed)
+
+    def m(r, c):
+        return oracle.Matrix(rng.integers(-127, 128, size=(r, c), dtype=np.int8),
+                             rng.uniform(1e-4, 1e-2, size=(r, (c + 31) // 32)).astype(np.float32))
+
+    def ffn(w):
+        return oracle.Ffn(m(w, H), m(w, H), m(H, w))
+
+    return ffn(FS), [ffn(F) for _ in range(E)], rng
+
+
+def cpu_baseline(args, seconds=None):
+    """Reference scalar path (oracle port) on all host threads, bounded sample."""
+    import oracle
+    oracle.set_threads(0)
+    shared, routed, rng = make_cpu_layer(7)
+    budget = seconds if seconds is not None else args.cpu_seconds
+    x = rng.standard_normal((1, H)).astype(np.float32)
+    lg = rng.standard_normal((1, E)).astype(np.float32)
+    oracle.experts(shared, routed, lg, x, TOPK, 0)  # warm
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget:
+        x = rng.standard_normal((1, H)).astype(np.float32)
+        lg = rng.standard_normal((1, E)).astype(np.float32)
+        oracle.experts(shared, routed, lg, x, TOPK, 0)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(STEP_BYTES * n / dt / 1e9, 3), "unit": "GB/s",
+            "cores": oracle.get_threads(), "kind": "port",
+            "sample": f"{n} tokens of config 1 (one MoE decode layer each) in {dt:.1f} s",
+            "ms_per_step": round(dt / n * 1e3, 3)}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    import oracle
+    oracle.set_threads(0)
+    shared, routed, rng = make_cpu_layer(7)
+    xs = rng.standard_normal((16, 1, H)).astype(np.float32)
+    lgs = rng.standard_normal((16, 1, E)).astype(np.float32)
+    for i in range(max(args.warmup, 3)):
+        oracle.experts(shared, routed, lgs[i % 16], xs[i % 16], TOPK, 0)
+    steps = args.steps if args.ref_steps is None else args.ref_steps
+    t0 = time.perf_counter()
+    for i in range(steps):
+        oracle.experts(shared, routed, lgs[i % 16], xs[i % 16], TOPK, 0)
+    dt = time.perf_counter() - t0
+    v = STEP_BYTES * steps / dt / 1e9
+    return {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s",
+            "n_gpus": world, "steps": steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": round(dt / steps * 1e3, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic (seeded; config-1 distributions)",
+            "config": {"workload": "config1_moe_decode_layer", "tokens_per_step": 1,
+                       "hidden": H, "experts": E, "top_k": TOPK, "expert_width": F,
+                       "shared_width": FS, "mode": "weights_only (fp32 activations)",
+                       "parallelism": "rank 0 only (host CPU)", "bytes_per_step": STEP_BYTES},
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": oracle.get_threads(),
+                             "kind": "port",
+                             "sample": f"{steps} tokens, one MoE decode layer each (scalar "
+                                       "restatement of the reference's Rust path; the Rust "
+                                       "crate cannot be built here)"},
+            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=32768)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=8)
+    ap.add_argument("--graph-steps", type=int, default=256)
+    ap.add_argument("--e2e-steps", type=int, default=4000)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--ref-steps", type=int, default=None)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--traffic", type=float, default=None,
+                    help="dram bytes per step from an ncu capture (reported as roofline.traffic)")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        if args.ref_steps is None:
+            args.ref_steps = min(args.steps, 1500)
+        res = run_reference(args)
+    else:
+        res = run_ours(args)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,185 @@
+/*
+ * uocr_q8.h — C ABI of the B200 q8-block32 quantized matrix-product path.
+ *
+ * Drop-in boundary for the reference runtime's INT8 block-32 operator surface
+ * (ezgamehost/unlimited-ocr-kernel, Rust crate `uocr`).  The reference has no
+ * FFI of its own: each entry point below replaces the Rust method cited beside
+ * it, with the same argument meaning and the same error variants.  All
+ * signatures use plain pointers and sizes.  `stream` arguments are
+ * cudaStream_t values passed as void* (NULL = the context's stream).
+ *
+ * Storage format (src/cpu/quantized.rs:9-16; overlay contract
+ * docs/benchmarks/2026-09-28-int8-kernels/README.md "uocr-q8-block32-v1"):
+ * row-major int8 weights [rows x cols] and one float32 scale per 32
+ * consecutive columns of a row, [rows x ceil(cols/32)]; the last block of a
+ * row may be short.  Dequantized weight = (float)w * scale.
+ *
+ * Arithmetic contract:
+ *   - DYNAMIC (int8-activation) results are bit-identical to the reference's
+ *     scalar path: activation block quantization (IEEE division, round half
+ *     to even), exact int32 block dots, and the ordered per-block float
+ *     accumulation of linear_dynamic_int8 (src/cpu/quantized.rs:190-198).
+ *   - WEIGHTS_ONLY (FP32-activation) results reorder the float accumulation;
+ *     max relative error <= 1e-4 of max(|y|, sum|w'x| * 2^-10).
+ *   - dequantize and quantize are bit-identical.
+ *
+ * Error convention: every function returns a uocr_status; uocr_last_error()
+ * returns the calling thread's last message.  Input errors detected on the
+ * device (nonfinite activations, scale underflow, invalid router rows) do not
+ * trap: they are recorded in the context and returned by the next
+ * synchronising call (uocr_ctx_sync, or any *_host function).
+ *
+ * Threading: a context is used by one host thread at a time (the reference's
+ * `&mut CpuContext`, src/cpu/mod.rs:68-71); matrices and MoE layers are
+ * immutable after creation and may be shared by contexts on the same device.
+ */
+#ifndef UOCR_Q8_H
+#define UOCR_Q8_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define UOCR_Q8_BLOCK 32
+#define UOCR_Q8_ABI_VERSION 1
+
+/* One code per OcrError variant (src/error.rs:1-17) plus device codes. */
+typedef enum uocr_status {
+  UOCR_OK = 0,
+  UOCR_ERR_IO = 1,          /* OcrError::Io */
+  UOCR_ERR_JSON = 2,        /* OcrError::Json */
+  UOCR_ERR_FORMAT = 3,      /* OcrError::Format */
+  UOCR_ERR_SHAPE = 4,       /* OcrError::Shape */
+  UOCR_ERR_UNSUPPORTED = 5, /* OcrError::Unsupported */
+  UOCR_ERR_RESOURCE = 6,    /* OcrError::Resource */
+  UOCR_ERR_NUMERICAL = 7,   /* OcrError::Numerical */
+  UOCR_ERR_CUDA = 8,        /* CUDA runtime error */
+  UOCR_ERR_NCCL = 9,        /* NCCL error (expert-parallel exchange) */
+  UOCR_ERR_TIMEOUT = 10,    /* a bounded device wait expired */
+  UOCR_ERR_INVALID = 11     /* null handle / pointer */
+} uocr_status;
+
+/* QuantizationMode (src/cpu/quantized.rs:242-247) and the row-wise
+ * extension.  Decoder::projection (src/decoder/mod.rs:99-112) uses int8
+ * activations only for a single-row input in DynamicActivations mode. */
+typedef enum uocr_mode {
+  UOCR_WEIGHTS_ONLY = 0,          /* QuantizationMode::WeightsOnly */
+  UOCR_DYNAMIC_ACTIVATIONS = 1,   /* QuantizationMode::DynamicActivations */
+  UOCR_DYNAMIC_ROWWISE = 2        /* int8 activations for every row (extension) */
+} uocr_mode;
+
+typedef struct uocr_ctx uocr_ctx;
+typedef struct uocr_q8 uocr_q8;
+typedef struct uocr_moe uocr_moe;
+
+/* ---- library ------------------------------------------------------------ */
+int uocr_abi_version(void);
+const char *uocr_last_error(void);
+const char *uocr_status_name(int status);
+
+/* ---- context: CpuContext::new (src/cpu/mod.rs:26-49) ---------------------
+ * device: CUDA ordinal.  scratch_limit: bytes, the reference's scratch_limit
+ * (0 -> Resource error, like threads/scratch 0 in CpuContext::new); every
+ * operation applies the reference's check_elements rule (count*4 > limit ->
+ * Resource, src/cpu/mod.rs:73-78) with the reference's element counts. */
+int uocr_ctx_create(int device, size_t scratch_limit, uocr_ctx **out);
+int uocr_ctx_destroy(uocr_ctx *ctx);
+int uocr_ctx_set_stream(uocr_ctx *ctx, void *stream);
+/* Wait for the context's stream; return and clear device-detected errors. */
+int uocr_ctx_sync(uocr_ctx *ctx);
+int uocr_ctx_device(const uocr_ctx *ctx, int *device, int *sm_count);
+
+/* ---- matrices: Int8Matrix (src/cpu/quantized.rs:11-237) -----------------
+ * Int8Matrix::from_parts (:18-42): copies host weights/scales to the device.
+ * Shape if rows/cols is 0 or a length disagrees; Numerical if a scale is
+ * NaN, infinite or negative (-0.0 is accepted). */
+int uocr_q8_from_parts(uocr_ctx *ctx, size_t rows, size_t cols, const int8_t *weights,
+                       size_t weights_len, const float *scales, size_t scales_len,
+                       uocr_q8 **out);
+/* Same validation for device-resident storage; the handle borrows (does not
+ * free) the memory.  Scale validation runs on the device and is reported
+ * synchronously. */
+int uocr_q8_from_device(uocr_ctx *ctx, size_t rows, size_t cols, const int8_t *weights_dev,
+                        const float *scales_dev, uocr_q8 **out);
+/* Int8Matrix::quantize (:43-74) of a host float matrix, on the device. */
+int uocr_q8_quantize(uocr_ctx *ctx, size_t rows, size_t cols, const float *values,
+                     uocr_q8 **out);
+int uocr_q8_free(uocr_q8 *m);
+int uocr_q8_shape(const uocr_q8 *m, size_t *rows, size_t *cols);
+/* Int8Matrix::storage_bytes (:96-98). */
+size_t uocr_q8_storage_bytes(const uocr_q8 *m);
+int uocr_q8_device_ptrs(const uocr_q8 *m, const int8_t **weights_dev, const float **scales_dev);
+int uocr_q8_download(uocr_ctx *ctx, const uocr_q8 *m, int8_t *weights, float *scales);
+
+/* Int8Matrix::dequantize (:75-95): out_dev is rows*cols floats. */
+int uocr_q8_dequantize(uocr_ctx *ctx, const uocr_q8 *m, float *out_dev);
+int uocr_q8_dequantize_host(uocr_ctx *ctx, const uocr_q8 *m, float *out, size_t out_len);
+
+/* Int8Matrix::linear (:99-149): y[r, :] = W x[r, :] for `batch` rows.
+ * Device buffers, asynchronous on the context stream. */
+int uocr_q8_linear(uocr_ctx *ctx, const uocr_q8 *m, const float *x_dev, size_t batch,
+                   float *y_dev);
+/* Host tensors like the reference: x has shape x_shape[0..ndim) whose last
+ * extent must equal cols (Shape otherwise); y receives the same shape with
+ * the last extent replaced by rows.  Synchronous. */
+int uocr_q8_linear_host(uocr_ctx *ctx, const uocr_q8 *m, const float *x, const size_t *x_shape,
+                        size_t ndim, float *y, size_t y_len);
+
+/* Int8Matrix::linear_dynamic_int8 (:155-236).  Device form: each of `batch`
+ * rows is quantized and multiplied independently (row-wise extension; batch
+ * 1 is the reference operation). */
+int uocr_q8_linear_dynamic_int8(uocr_ctx *ctx, const uocr_q8 *m, const float *x_dev,
+                                size_t batch, float *y_dev);
+/* Host form with the reference's rule: exactly one input row, else Shape. */
+int uocr_q8_linear_dynamic_int8_host(uocr_ctx *ctx, const uocr_q8 *m, const float *x,
+                                     const size_t *x_shape, size_t ndim, float *y,
+                                     size_t y_len);
+
+/* Block quantization of `rows` float rows on the device (the activation step
+ * of linear_dynamic_int8, :169): q_dev rows*cols int8, s_dev
+ * rows*ceil(cols/32) floats. */
+int uocr_q8_quantize_rows(uocr_ctx *ctx, const float *x_dev, size_t rows, size_t cols,
+                          int8_t *q_dev, float *s_dev);
+
+/* Several matrices of equal cols applied to one shared input row, one launch
+ * (the batched-stream GEMV; all experts of a token share their input). */
+int uocr_q8_linear_multi(uocr_ctx *ctx, const uocr_q8 *const *mats, size_t n, int mode,
+                         const float *x_dev, float *const *y_dev);
+
+/* ---- routing: moe::route (src/decoder/moe.rs:7-30) -----------------------
+ * logits_dev tokens*n_experts; ids_dev/weights_dev tokens*top_k in the
+ * reference's order (probability descending, expert id ascending).  Shape if
+ * top_k == 0, top_k > n_experts or scale is not finite and > 0; Numerical if
+ * a row holds NaN/+inf or no finite maximum (ops::softmax). */
+int uocr_moe_route(uocr_ctx *ctx, const float *logits_dev, size_t tokens, size_t n_experts,
+                   size_t top_k, int normalize, float scale, int32_t *ids_dev,
+                   float *weights_dev);
+
+/* ---- MoE layer: Decoder::experts (src/decoder/mod.rs:124-220) ------------
+ * shared_*: the fused shared-expert FFN (width n_shared*moe_intermediate);
+ * gate/up/down: n_experts routed FFNs.  All gate/up are [width x hidden],
+ * down [hidden x width].  The layer keeps the handles' device pointers; the
+ * matrices must outlive it. */
+int uocr_moe_create(uocr_ctx *ctx, const uocr_q8 *shared_gate, const uocr_q8 *shared_up,
+                    const uocr_q8 *shared_down, const uocr_q8 *const *gate,
+                    const uocr_q8 *const *up, const uocr_q8 *const *down, size_t n_experts,
+                    size_t top_k, int normalize_topk, float routed_scale, uocr_moe **out);
+int uocr_moe_free(uocr_moe *layer);
+/* One MoE FFN over `tokens` rows: x_dev tokens*hidden, router logits
+ * tokens*n_experts, y_dev tokens*hidden.  ids/weights (optional, may be
+ * NULL) receive each token's routing.  mode: uocr_mode.  Asynchronous. */
+int uocr_moe_forward(uocr_ctx *ctx, const uocr_moe *layer, int mode, const float *x_dev,
+                     const float *logits_dev, size_t tokens, float *y_dev, int32_t *ids_dev,
+                     float *weights_dev);
+/* Host-buffer form: copies in, runs, copies out, synchronises. */
+int uocr_moe_forward_host(uocr_ctx *ctx, const uocr_moe *layer, int mode, const float *x,
+                          const float *logits, size_t tokens, float *y, int32_t *ids,
+                          float *weights);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* UOCR_Q8_H */

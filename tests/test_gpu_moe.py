@@ -1,0 +1,175 @@
+"""GPU parity of routing and the MoE FFN layer (Decoder::experts) vs the oracle.
+
+Routing: selected ids exact, weights bit-exact (exp is evaluated so that it
+rounds like libm's expf except in rare boundary cases; a one-ulp difference
+is tolerated and counted).  FP32-activation layer: max |y - ref| <=
+1e-4 * max |ref|.  int8-activation layer: every projection is bit-exact given
+identical inputs; end to end, a silu value that rounds differently can flip
+one activation rounding, so >= 99% of outputs must be bit-identical and the
+rest within 1e-3 * max |ref|.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from helpers import bits_equal, random_q8
+
+pytestmark = pytest.mark.gpu
+
+LAYER_FP32_TOL = 1e-4
+LAYER_INT8_TOL = 1e-3
+
+
+def q8():
+    import uocr_q8
+    return uocr_q8
+
+
+def make_layer(ctx, rng, H, F, FS, E, k, normalize=False, scale=1.0):
+    M = q8().Int8Matrix
+
+    def ffn(width):
+        mats, host = [], []
+        for r, c in ((width, H), (width, H), (H, width)):
+            w, s = random_q8(rng, r, c)
+            mats.append(M.from_parts(r, c, w, s, ctx))
+            host.append(oracle.Matrix(w, s))
+        return mats, oracle.Ffn(*host)
+
+    shared, shared_o = ffn(FS)
+    experts, experts_o = zip(*[ffn(F) for _ in range(E)])
+    layer = q8().MoeLayer(ctx, shared, experts, k, normalize, scale)
+    return layer, shared_o, list(experts_o)
+
+
+def ulps(a, b):
+    a = np.asarray(a, np.float32).view(np.int32).astype(np.int64)
+    b = np.asarray(b, np.float32).view(np.int32).astype(np.int64)
+    return np.abs(a - b)
+
+
+# ---------------------------------------------------------------- routing
+def test_route_known_answers(ctx):
+    import torch
+    logits = torch.zeros((1, 4), device="cuda")
+    ids, w = q8().route_device(ctx, logits, 2)
+    ctx.sync()
+    assert ids.cpu().tolist() == [[0, 1]] and w.cpu().tolist() == [[0.25, 0.25]]
+    ids, w = q8().route_device(ctx, logits, 2, True, 2.0)
+    ctx.sync()
+    assert ids.cpu().tolist() == [[0, 1]] and w.cpu().tolist() == [[1.0, 1.0]]
+
+
+@pytest.mark.parametrize("normalize,scale", [(False, 1.0), (True, 2.5)])
+def test_route_vs_oracle(ctx, normalize, scale):
+    import torch
+    rng = np.random.default_rng(7)
+    logits = rng.standard_normal((300, 64)).astype(np.float32)
+    ids, w = q8().route_device(ctx, torch.from_numpy(logits).cuda(), 6, normalize, scale)
+    ctx.sync()
+    ids, w = ids.cpu().numpy(), w.cpu().numpy()
+    for t in range(300):
+        ref = oracle.route(logits[t], 6, normalize, scale)
+        assert ids[t].tolist() == [i for i, _ in ref]
+        assert ulps(w[t], [p for _, p in ref]).max() <= 1
+
+
+def test_route_errors(ctx):
+    import torch
+    bad = torch.zeros((2, 8), device="cuda")
+    bad[1, 3] = float("nan")
+    q8().route_device(ctx, bad, 2)
+    with pytest.raises(q8().OcrError) as e:
+        ctx.sync()
+    assert e.value.kind == "Numerical"
+    with pytest.raises(q8().OcrError) as e:
+        q8().route_device(ctx, bad, 9)
+    assert e.value.kind == "Shape"
+    with pytest.raises(q8().OcrError) as e:
+        q8().route_device(ctx, bad, 2, False, 0.0)
+    assert e.value.kind == "Shape"
+
+
+# ---------------------------------------------------------------- decode (1 token)
+@pytest.fixture(scope="module")
+def config1(ctx):
+    """hidden 1280, 64 experts of width 896, top-6, shared 1792."""
+    rng = np.random.default_rng(1)
+    return make_layer(ctx, rng, 1280, 896, 1792, 64, 6)
+
+
+def _check_layer(y, ref, ids, ids_ref, wts, wts_ref, int8):
+    assert np.array_equal(ids, ids_ref)
+    assert ulps(wts, wts_ref).max() <= 1
+    scale = float(np.max(np.abs(ref)))
+    err = float(np.max(np.abs(y.astype(np.float64) - ref)))
+    if int8:
+        same = float(np.mean(y.view(np.uint32) == ref.view(np.uint32)))
+        assert same >= 0.99, same
+        assert err <= LAYER_INT8_TOL * scale
+    else:
+        assert err <= LAYER_FP32_TOL * scale
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_decode_config1(ctx, config1, mode):
+    layer, sh, ex = config1
+    rng = np.random.default_rng(100 + mode)
+    for trial in range(3):
+        x = rng.standard_normal((1, 1280)).astype(np.float32)
+        logits = rng.standard_normal((1, 64)).astype(np.float32)
+        y, ids, wts = layer.forward(x, logits, mode)
+        ref, ids_ref, wts_ref = oracle.experts(sh, ex, logits, x, 6, mode)
+        _check_layer(y, ref, ids, ids_ref, wts, wts_ref, mode != 0)
+
+
+def test_decode_device_repeatable(ctx, config1):
+    import torch
+    layer = config1[0]
+    rng = np.random.default_rng(5)
+    x = torch.from_numpy(rng.standard_normal((1, 1280)).astype(np.float32)).cuda()
+    lg = torch.from_numpy(rng.standard_normal((1, 64)).astype(np.float32)).cuda()
+    a = layer.forward_device(x, lg, 0).clone()
+    for _ in range(5):
+        b = layer.forward_device(x, lg, 0)
+    ctx.sync()
+    assert torch.equal(a, b)
+
+
+def test_decode_rejects_bad_logits(ctx, config1):
+    layer = config1[0]
+    x = np.zeros((1, 1280), np.float32)
+    logits = np.zeros((1, 64), np.float32)
+    logits[0, 3] = np.inf
+    with pytest.raises(q8().OcrError) as e:
+        layer.forward(x, logits, 0)
+    assert e.value.kind == "Numerical"
+
+
+# ---------------------------------------------------------------- prefill (many tokens)
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_prefill_small(ctx, mode):
+    rng = np.random.default_rng(40 + mode)
+    layer, sh, ex = make_layer(ctx, rng, 128, 64, 128, 8, 3)
+    T = 37
+    x = rng.standard_normal((T, 128)).astype(np.float32)
+    logits = rng.standard_normal((T, 8)).astype(np.float32)
+    logits[5, 2] += 4.0  # a group of size one for expert 2 is likely
+    y, ids, wts = layer.forward(x, logits, mode)
+    ref, ids_ref, wts_ref = oracle.experts(sh, ex, logits, x, 3, mode)
+    _check_layer(y, ref, ids, ids_ref, wts, wts_ref, mode != 0)
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("mode", [0, 2])
+def test_prefill_config2_shape(ctx, config1, mode):
+    """Config-2 shapes with Zipf-skewed routing, 192 tokens (oracle-sized)."""
+    layer, sh, ex = config1
+    rng = np.random.default_rng(77)
+    T = 192
+    x = rng.standard_normal((T, 1280)).astype(np.float32)
+    bias = (1.0 / np.arange(1, 65) ** 1.1).astype(np.float32) * 4.0
+    logits = (rng.standard_normal((T, 64)).astype(np.float32) + rng.permutation(bias)).astype(np.float32)
+    y, ids, wts = layer.forward(x, logits, mode)
+    ref, ids_ref, wts_ref = oracle.experts(sh, ex, logits, x, 6, mode)
+    _check_layer(y, ref, ids, ids_ref, wts, wts_ref, mode != 0)

@@ -1,0 +1,902 @@
+// capi.cu — the C ABI declared in include/uocr_q8.h.
+//
+// Host-side validation restates the reference's checks (file:line beside each
+// rule) so that every entry point fails with the same OcrError variant as the
+// Rust method it replaces.  Device work is enqueued on the context's stream;
+// *_host entry points copy in, run and copy out synchronously, like the
+// reference's Tensor-in / Tensor-out methods.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <limits>
+#include <string>
+#include <vector>
+
+#include "../../include/uocr_q8.h"
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace uocr;
+
+struct uocr_ctx {
+  int device = 0;
+  int sms = 0;
+  size_t scratch_limit = 0;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  unsigned* status_dev = nullptr;
+  unsigned* status_host = nullptr;  // pinned
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  void* pinned = nullptr;
+  size_t pinned_bytes = 0;
+  void* io = nullptr;  // device staging of the *_host MoE entry point
+  size_t io_bytes = 0;
+};
+
+struct uocr_q8 {
+  int device = 0;
+  size_t rows = 0, cols = 0;
+  int8_t* w = nullptr;
+  float* s = nullptr;
+  bool owns = false;
+};
+
+struct uocr_moe {
+  int device = 0;
+  size_t n_experts = 0, top_k = 0;
+  int normalize = 0;
+  float scale = 1.0f;
+  int hidden = 0, width = 0, shared_width = 0;
+  FfnView shared{};
+  FfnView* experts_dev = nullptr;
+  bool aligned = true;
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+int ok() { return UOCR_OK; }
+
+#define CUDA_TRY(expr)                                                                  \
+  do {                                                                                  \
+    cudaError_t e_ = (expr);                                                            \
+    if (e_ != cudaSuccess)                                                              \
+      return fail(UOCR_ERR_CUDA, "%s: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, \
+                  __LINE__);                                                            \
+  } while (0)
+
+// Switches to the context's device for the lifetime of a call.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+bool mul_ok(size_t a, size_t b, size_t* out) {
+  if (a != 0 && b > std::numeric_limits<size_t>::max() / a) return false;
+  *out = a * b;
+  return true;
+}
+
+size_t nblocks(size_t cols) { return (cols + kBlock - 1) / kBlock; }
+
+// CpuContext::check_elements (src/cpu/mod.rs:73-78).
+int check_elements(const uocr_ctx* ctx, size_t count) {
+  size_t bytes;
+  if (!mul_ok(count, 4, &bytes) || bytes > ctx->scratch_limit)
+    return fail(UOCR_ERR_RESOURCE, "resource limit: operation exceeds scratch limit");
+  return ok();
+}
+
+int ensure_ws(uocr_ctx* ctx, size_t bytes) {
+  if (bytes <= ctx->ws_bytes) return ok();
+  CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  if (ctx->ws) CUDA_TRY(cudaFree(ctx->ws));
+  ctx->ws = nullptr;
+  ctx->ws_bytes = 0;
+  size_t want = bytes + (bytes >> 2);
+  want = (want + 0xFFFFF) & ~static_cast<size_t>(0xFFFFF);
+  CUDA_TRY(cudaMalloc(&ctx->ws, want));
+  ctx->ws_bytes = want;
+  return ok();
+}
+
+int ensure_pinned(uocr_ctx* ctx, size_t bytes) {
+  if (bytes <= ctx->pinned_bytes) return ok();
+  CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  if (ctx->pinned) CUDA_TRY(cudaFreeHost(ctx->pinned));
+  ctx->pinned = nullptr;
+  ctx->pinned_bytes = 0;
+  size_t want = (bytes + 0xFFFF) & ~static_cast<size_t>(0xFFFF);
+  CUDA_TRY(cudaMallocHost(&ctx->pinned, want));
+  ctx->pinned_bytes = want;
+  return ok();
+}
+
+bool is_pinned(const void* p) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeHost;
+}
+
+// Maps the device status word to the reference's error variants.
+int take_device_status(uocr_ctx* ctx) {
+  CUDA_TRY(cudaMemcpyAsync(ctx->status_host, ctx->status_dev, sizeof(unsigned),
+                           cudaMemcpyDeviceToHost, ctx->stream));
+  CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  const unsigned st = *ctx->status_host;
+  if (!st) return ok();
+  CUDA_TRY(cudaMemsetAsync(ctx->status_dev, 0, sizeof(unsigned), ctx->stream));
+  CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  if (st & DEV_TIMEOUT) return fail(UOCR_ERR_TIMEOUT, "a bounded device wait expired");
+  if (st & DEV_NONFINITE)
+    return fail(UOCR_ERR_NUMERICAL, "nonfinite numerical input: nonfinite quantization input");
+  if (st & DEV_UNDERFLOW) return fail(UOCR_ERR_NUMERICAL, "nonfinite numerical input: INT8 scale underflow");
+  if (st & DEV_BAD_SCALE)
+    return fail(UOCR_ERR_NUMERICAL,
+                "nonfinite numerical input: INT8 scales must be finite and nonnegative");
+  if (st & DEV_SOFTMAX)
+    return fail(UOCR_ERR_NUMERICAL, "nonfinite numerical input: invalid or fully masked softmax row");
+  if (st & DEV_RANGE) return fail(UOCR_ERR_FORMAT, "invalid checkpoint: INT8 byte -128");
+  if (st & DEV_BAD_ROUTE) return fail(UOCR_ERR_SHAPE, "invalid tensor shape: invalid expert routing");
+  return fail(UOCR_ERR_CUDA, "unknown device status 0x%x", st);
+}
+
+int check_launch() {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+  return ok();
+}
+
+Q8View view(const uocr_q8* m) {
+  return Q8View{m->w, m->s, static_cast<int>(m->rows), static_cast<int>(m->cols)};
+}
+
+bool fits_int(size_t v) { return v <= static_cast<size_t>(std::numeric_limits<int>::max()); }
+
+// Host-tensor shape rules shared by the *_host entry points.
+int tensor_len(const size_t* shape, size_t ndim, size_t* len) {
+  size_t n = 1;
+  for (size_t i = 0; i < ndim; ++i)
+    if (!mul_ok(n, shape[i], &n)) return fail(UOCR_ERR_SHAPE, "invalid tensor shape: element count overflow");
+  *len = n;
+  return ok();
+}
+
+}  // namespace
+
+// ===========================================================================
+extern "C" {
+
+int uocr_abi_version(void) { return UOCR_Q8_ABI_VERSION; }
+
+const char* uocr_last_error(void) { return g_last_error.c_str(); }
+
+const char* uocr_status_name(int status) {
+  switch (status) {
+    case UOCR_OK: return "Ok";
+    case UOCR_ERR_IO: return "Io";
+    case UOCR_ERR_JSON: return "Json";
+    case UOCR_ERR_FORMAT: return "Format";
+    case UOCR_ERR_SHAPE: return "Shape";
+    case UOCR_ERR_UNSUPPORTED: return "Unsupported";
+    case UOCR_ERR_RESOURCE: return "Resource";
+    case UOCR_ERR_NUMERICAL: return "Numerical";
+    case UOCR_ERR_CUDA: return "Cuda";
+    case UOCR_ERR_NCCL: return "Nccl";
+    case UOCR_ERR_TIMEOUT: return "Timeout";
+    case UOCR_ERR_INVALID: return "Invalid";
+    default: return "Unknown";
+  }
+}
+
+// ---- context ---------------------------------------------------------------
+int uocr_ctx_create(int device, size_t scratch_limit, uocr_ctx** out) {
+  if (!out) return fail(UOCR_ERR_INVALID, "null output");
+  *out = nullptr;
+  // CpuContext::new (src/cpu/mod.rs:27-31)
+  if (scratch_limit == 0)
+    return fail(UOCR_ERR_RESOURCE, "resource limit: threads and scratch limit must be nonzero");
+  int count = 0;
+  CUDA_TRY(cudaGetDeviceCount(&count));
+  if (device < 0 || device >= count)
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: no CUDA device %d", device);
+  cudaDeviceProp prop{};
+  CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10)
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: sm_%d%d is not sm_100",
+                prop.major, prop.minor);
+  DeviceGuard g(device);
+  auto* c = new uocr_ctx();
+  c->device = device;
+  c->sms = prop.multiProcessorCount;
+  c->scratch_limit = scratch_limit;
+  cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMalloc(&c->status_dev, 256);
+  if (e == cudaSuccess) e = cudaMemset(c->status_dev, 0, 256);
+  if (e == cudaSuccess) e = cudaMallocHost(&c->status_host, sizeof(unsigned) * 4);
+  if (e != cudaSuccess) {
+    uocr_ctx_destroy(c);
+    return fail(UOCR_ERR_CUDA, "context: %s", cudaGetErrorString(e));
+  }
+  c->own_stream = true;
+  *out = c;
+  return ok();
+}
+
+int uocr_ctx_destroy(uocr_ctx* ctx) {
+  if (!ctx) return ok();
+  DeviceGuard g(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  if (ctx->ws) cudaFree(ctx->ws);
+  if (ctx->io) cudaFree(ctx->io);
+  if (ctx->pinned) cudaFreeHost(ctx->pinned);
+  if (ctx->status_dev) cudaFree(ctx->status_dev);
+  if (ctx->status_host) cudaFreeHost(ctx->status_host);
+  if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+  return ok();
+}
+
+int uocr_ctx_set_stream(uocr_ctx* ctx, void* stream) {
+  if (!ctx) return fail(UOCR_ERR_INVALID, "null context");
+  DeviceGuard g(ctx->device);
+  CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
+  ctx->own_stream = false;
+  ctx->stream = static_cast<cudaStream_t>(stream);
+  return ok();
+}
+
+int uocr_ctx_sync(uocr_ctx* ctx) {
+  if (!ctx) return fail(UOCR_ERR_INVALID, "null context");
+  DeviceGuard g(ctx->device);
+  CUDA_TRY(cudaGetLastError());
+  return take_device_status(ctx);
+}
+
+int uocr_ctx_device(const uocr_ctx* ctx, int* device, int* sm_count) {
+  if (!ctx) return fail(UOCR_ERR_INVALID, "null context");
+  if (device) *device = ctx->device;
+  if (sm_count) *sm_count = ctx->sms;
+  return ok();
+}
+
+// ---- matrices --------------------------------------------------------------
+int uocr_q8_from_parts(uocr_ctx* ctx, size_t rows, size_t cols, const int8_t* weights,
+                       size_t weights_len, const float* scales, size_t scales_len,
+                       uocr_q8** out) {
+  if (!ctx || !out) return fail(UOCR_ERR_INVALID, "null argument");
+  *out = nullptr;
+  // src/cpu/quantized.rs:24-30
+  size_t n, ns;
+  if (rows == 0 || cols == 0 || !mul_ok(rows, cols, &n) || n != weights_len ||
+      !mul_ok(rows, nblocks(cols), &ns) || ns != scales_len)
+    return fail(UOCR_ERR_SHAPE, "invalid tensor shape: INT8 matrix storage");
+  if (!weights || !scales) return fail(UOCR_ERR_INVALID, "null storage");
+  // src/cpu/quantized.rs:31-35 (so -0.0 passes)
+  for (size_t i = 0; i < scales_len; ++i)
+    if (!std::isfinite(scales[i]) || scales[i] < 0.0f)
+      return fail(UOCR_ERR_NUMERICAL,
+                  "nonfinite numerical input: INT8 scales must be finite and nonnegative");
+  if (!fits_int(rows) || !fits_int(cols))
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: matrix extent above 2^31");
+  DeviceGuard g(ctx->device);
+  auto* m = new uocr_q8();
+  m->device = ctx->device;
+  m->rows = rows;
+  m->cols = cols;
+  m->owns = true;
+  cudaError_t e = cudaMalloc(&m->w, (n + 15) & ~static_cast<size_t>(15));
+  if (e == cudaSuccess) e = cudaMalloc(&m->s, ns * sizeof(float));
+  if (e == cudaSuccess) e = cudaMemcpy(m->w, weights, n, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(m->s, scales, ns * sizeof(float), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    uocr_q8_free(m);
+    return fail(UOCR_ERR_CUDA, "from_parts: %s", cudaGetErrorString(e));
+  }
+  *out = m;
+  return ok();
+}
+
+int uocr_q8_from_device(uocr_ctx* ctx, size_t rows, size_t cols, const int8_t* weights_dev,
+                        const float* scales_dev, uocr_q8** out) {
+  if (!ctx || !out) return fail(UOCR_ERR_INVALID, "null argument");
+  *out = nullptr;
+  size_t n, ns;
+  if (rows == 0 || cols == 0 || !mul_ok(rows, cols, &n) || !mul_ok(rows, nblocks(cols), &ns))
+    return fail(UOCR_ERR_SHAPE, "invalid tensor shape: INT8 matrix storage");
+  if (!weights_dev || !scales_dev) return fail(UOCR_ERR_INVALID, "null storage");
+  if (!fits_int(rows) || !fits_int(cols))
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: matrix extent above 2^31");
+  DeviceGuard g(ctx->device);
+  int st = take_device_status(ctx);
+  if (st) return st;
+  launch_validate_q8(weights_dev, static_cast<long long>(n), scales_dev,
+                     static_cast<long long>(ns), 0, ctx->status_dev, ctx->sms, ctx->stream);
+  if ((st = check_launch())) return st;
+  if ((st = take_device_status(ctx))) return st;
+  auto* m = new uocr_q8();
+  m->device = ctx->device;
+  m->rows = rows;
+  m->cols = cols;
+  m->w = const_cast<int8_t*>(weights_dev);
+  m->s = const_cast<float*>(scales_dev);
+  m->owns = false;
+  *out = m;
+  return ok();
+}
+
+int uocr_q8_quantize(uocr_ctx* ctx, size_t rows, size_t cols, const float* values,
+                     uocr_q8** out) {
+  if (!ctx || !out) return fail(UOCR_ERR_INVALID, "null argument");
+  *out = nullptr;
+  // src/cpu/quantized.rs:45-49
+  size_t n;
+  if (rows == 0 || cols == 0 || !mul_ok(rows, cols, &n))
+    return fail(UOCR_ERR_SHAPE, "invalid tensor shape: quantization expects a nonempty matrix");
+  if (!values) return fail(UOCR_ERR_INVALID, "null values");
+  if (!fits_int(rows) || !fits_int(cols))
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: matrix extent above 2^31");
+  DeviceGuard g(ctx->device);
+  int st = take_device_status(ctx);
+  if (st) return st;
+  if ((st = ensure_ws(ctx, n * sizeof(float)))) return st;
+  auto* m = new uocr_q8();
+  m->device = ctx->device;
+  m->rows = rows;
+  m->cols = cols;
+  m->owns = true;
+  const size_t ns = rows * nblocks(cols);
+  cudaError_t e = cudaMalloc(&m->w, (n + 15) & ~static_cast<size_t>(15));
+  if (e == cudaSuccess) e = cudaMalloc(&m->s, ns * sizeof(float));
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(ctx->ws, values, n * sizeof(float), cudaMemcpyHostToDevice, ctx->stream);
+  if (e != cudaSuccess) {
+    uocr_q8_free(m);
+    return fail(UOCR_ERR_CUDA, "quantize: %s", cudaGetErrorString(e));
+  }
+  launch_quantize_rows(static_cast<const float*>(ctx->ws), static_cast<long long>(cols),
+                       static_cast<int>(rows), static_cast<int>(cols), m->w, m->s, ctx->status_dev,
+                       ctx->sms, ctx->stream);
+  if ((st = check_launch()) || (st = take_device_status(ctx))) {
+    uocr_q8_free(m);
+    return st;
+  }
+  *out = m;
+  return ok();
+}
+
+int uocr_q8_free(uocr_q8* m) {
+  if (!m) return ok();
+  DeviceGuard g(m->device);
+  if (m->owns) {
+    if (m->w) cudaFree(m->w);
+    if (m->s) cudaFree(m->s);
+  }
+  delete m;
+  return ok();
+}
+
+int uocr_q8_shape(const uocr_q8* m, size_t* rows, size_t* cols) {
+  if (!m) return fail(UOCR_ERR_INVALID, "null matrix");
+  if (rows) *rows = m->rows;
+  if (cols) *cols = m->cols;
+  return ok();
+}
+
+size_t uocr_q8_storage_bytes(const uocr_q8* m) {
+  // src/cpu/quantized.rs:96-98
+  return m ? m->rows * m->cols + m->rows * nblocks(m->cols) * 4 : 0;
+}
+
+int uocr_q8_device_ptrs(const uocr_q8* m, const int8_t** w, const float** s) {
+  if (!m) return fail(UOCR_ERR_INVALID, "null matrix");
+  if (w) *w = m->w;
+  if (s) *s = m->s;
+  return ok();
+}
+
+int uocr_q8_download(uocr_ctx* ctx, const uocr_q8* m, int8_t* weights, float* scales) {
+  if (!ctx || !m) return fail(UOCR_ERR_INVALID, "null argument");
+  DeviceGuard g(ctx->device);
+  if (weights)
+    CUDA_TRY(cudaMemcpyAsync(weights, m->w, m->rows * m->cols, cudaMemcpyDeviceToHost, ctx->stream));
+  if (scales)
+    CUDA_TRY(cudaMemcpyAsync(scales, m->s, m->rows * nblocks(m->cols) * 4, cudaMemcpyDeviceToHost,
+                             ctx->stream));
+  CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  return ok();
+}
+
+int uocr_q8_dequantize(uocr_ctx* ctx, const uocr_q8* m, float* out_dev) {
+  if (!ctx || !m || !out_dev) return fail(UOCR_ERR_INVALID, "null argument");
+  DeviceGuard g(ctx->device);
+  launch_dequantize(m->w, m->s, static_cast<int>(m->rows), static_cast<int>(m->cols), out_dev,
+                    ctx->sms, ctx->stream);
+  return check_launch();
+}
+
+int uocr_q8_dequantize_host(uocr_ctx* ctx, const uocr_q8* m, float* out, size_t out_len) {
+  if (!ctx || !m || !out) return fail(UOCR_ERR_INVALID, "null argument");
+  const size_t n = m->rows * m->cols;
+  if (out_len != n) return fail(UOCR_ERR_SHAPE, "invalid tensor shape: output length");
+  DeviceGuard g(ctx->device);
+  int st = ensure_ws(ctx, n * 4);
+  if (st) return st;
+  launch_dequantize(m->w, m->s, static_cast<int>(m->rows), static_cast<int>(m->cols),
+                    static_cast<float*>(ctx->ws), ctx->sms, ctx->stream);
+  if ((st = check_launch())) return st;
+  CUDA_TRY(cudaMemcpyAsync(out, ctx->ws, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  return take_device_status(ctx);
+}
+
+// Int8Matrix::linear element-count rules (src/cpu/quantized.rs:104-115).
+static int linear_checks(const uocr_ctx* ctx, const uocr_q8* m, size_t batch) {
+  size_t count;
+  if (!mul_ok(batch, m->rows, &count))
+    return fail(UOCR_ERR_RESOURCE, "resource limit: INT8 output overflow");
+  int st = check_elements(ctx, count);
+  if (st) return st;
+  if (batch != 1) {
+    const size_t w = m->rows * m->cols;
+    if (w > std::numeric_limits<size_t>::max() - count)
+      return fail(UOCR_ERR_RESOURCE, "resource limit: INT8 scratch overflow");
+    if ((st = check_elements(ctx, w + count))) return st;
+  }
+  return ok();
+}
+
+// linear_dynamic_int8 scratch rule (src/cpu/quantized.rs:162-168).
+static int dynamic_checks(const uocr_ctx* ctx, const uocr_q8* m) {
+  return check_elements(ctx, m->cols * 2 + m->rows + nblocks(m->cols));
+}
+
+static int run_linear(uocr_ctx* ctx, const uocr_q8* m, int mode, const float* x_dev, size_t batch,
+                      float* y_dev) {
+  if (batch == 0) return ok();
+  if (!fits_int(batch)) return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: batch");
+  int8_t* xq = nullptr;
+  float* xs = nullptr;
+  if (mode == MODE_INT8) {
+    const size_t qbytes = (batch * m->cols + 255) & ~static_cast<size_t>(255);
+    int st = ensure_ws(ctx, qbytes + batch * nblocks(m->cols) * 4);
+    if (st) return st;
+    xq = static_cast<int8_t*>(ctx->ws);
+    xs = reinterpret_cast<float*>(static_cast<char*>(ctx->ws) + qbytes);
+  }
+  launch_gemv(mode, view(m), x_dev, static_cast<long long>(m->cols), static_cast<int>(batch), y_dev,
+              static_cast<long long>(m->rows), xq, xs, ctx->status_dev, ctx->sms, ctx->stream);
+  return check_launch();
+}
+
+int uocr_q8_linear(uocr_ctx* ctx, const uocr_q8* m, const float* x_dev, size_t batch,
+                   float* y_dev) {
+  if (!ctx || !m || (batch && (!x_dev || !y_dev))) return fail(UOCR_ERR_INVALID, "null argument");
+  int st = linear_checks(ctx, m, batch);
+  if (st) return st;
+  DeviceGuard g(ctx->device);
+  return run_linear(ctx, m, MODE_FP32, x_dev, batch, y_dev);
+}
+
+int uocr_q8_linear_dynamic_int8(uocr_ctx* ctx, const uocr_q8* m, const float* x_dev,
+                                size_t batch, float* y_dev) {
+  if (!ctx || !m || (batch && (!x_dev || !y_dev))) return fail(UOCR_ERR_INVALID, "null argument");
+  int st = dynamic_checks(ctx, m);
+  if (st) return st;
+  DeviceGuard g(ctx->device);
+  return run_linear(ctx, m, MODE_INT8, x_dev, batch, y_dev);
+}
+
+// Copies x in, runs, copies y out (through pinned staging unless the caller's
+// buffers are already pinned), synchronises and reports device errors.
+static int host_linear(uocr_ctx* ctx, const uocr_q8* m, int mode, const float* x, size_t batch,
+                       float* y) {
+  const size_t xn = batch * m->cols, yn = batch * m->rows;
+  const size_t xb = (xn * 4 + 255) & ~static_cast<size_t>(255);
+  const size_t qb = mode == MODE_INT8 ? ((batch * m->cols + 255) & ~static_cast<size_t>(255)) +
+                                            batch * nblocks(m->cols) * 4 + 256
+                                      : 0;
+  int st = take_device_status(ctx);
+  if (st) return st;
+  if ((st = ensure_ws(ctx, xb + ((yn * 4 + 255) & ~static_cast<size_t>(255)) + qb))) return st;
+  float* xd = static_cast<float*>(ctx->ws);
+  float* yd = reinterpret_cast<float*>(static_cast<char*>(ctx->ws) + xb);
+  int8_t* xq = nullptr;
+  float* xs = nullptr;
+  if (mode == MODE_INT8) {
+    xq = reinterpret_cast<int8_t*>(static_cast<char*>(ctx->ws) + xb +
+                                   ((yn * 4 + 255) & ~static_cast<size_t>(255)));
+    xs = reinterpret_cast<float*>(reinterpret_cast<char*>(xq) +
+                                  ((batch * m->cols + 255) & ~static_cast<size_t>(255)));
+  }
+  const bool xp = is_pinned(x), yp = is_pinned(y);
+  if ((!xp || !yp) && (st = ensure_pinned(ctx, (xp ? 0 : xn * 4) + (yp ? 0 : yn * 4) + 256)))
+    return st;
+  float* xs_h = xp ? const_cast<float*>(x) : static_cast<float*>(ctx->pinned);
+  float* ys_h = yp ? y : reinterpret_cast<float*>(static_cast<char*>(ctx->pinned) +
+                                                  ((xp ? 0 : xn * 4) + 255) / 256 * 256);
+  if (!xp) std::memcpy(xs_h, x, xn * 4);
+  CUDA_TRY(cudaMemcpyAsync(xd, xs_h, xn * 4, cudaMemcpyHostToDevice, ctx->stream));
+  launch_gemv(mode, view(m), xd, static_cast<long long>(m->cols), static_cast<int>(batch), yd,
+              static_cast<long long>(m->rows), xq, xs, ctx->status_dev, ctx->sms, ctx->stream);
+  if ((st = check_launch())) return st;
+  CUDA_TRY(cudaMemcpyAsync(ys_h, yd, yn * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  st = take_device_status(ctx);
+  if (st) return st;
+  if (!yp) std::memcpy(y, ys_h, yn * 4);
+  return ok();
+}
+
+int uocr_q8_linear_host(uocr_ctx* ctx, const uocr_q8* m, const float* x, const size_t* x_shape,
+                        size_t ndim, float* y, size_t y_len) {
+  if (!ctx || !m || (ndim && !x_shape)) return fail(UOCR_ERR_INVALID, "null argument");
+  // src/cpu/quantized.rs:101-103
+  if (ndim == 0 || x_shape[ndim - 1] != m->cols)
+    return fail(UOCR_ERR_SHAPE, "invalid tensor shape: INT8 linear input width");
+  size_t len;
+  int st = tensor_len(x_shape, ndim, &len);
+  if (st) return st;
+  const size_t batch = len / m->cols;
+  if ((st = linear_checks(ctx, m, batch))) return st;
+  if (y_len != batch * m->rows) return fail(UOCR_ERR_SHAPE, "invalid tensor shape: output length");
+  if (batch == 0) return ok();
+  if (!x || !y) return fail(UOCR_ERR_INVALID, "null buffer");
+  DeviceGuard g(ctx->device);
+  return host_linear(ctx, m, MODE_FP32, x, batch, y);
+}
+
+int uocr_q8_linear_dynamic_int8_host(uocr_ctx* ctx, const uocr_q8* m, const float* x,
+                                     const size_t* x_shape, size_t ndim, float* y,
+                                     size_t y_len) {
+  if (!ctx || !m || (ndim && !x_shape)) return fail(UOCR_ERR_INVALID, "null argument");
+  size_t len;
+  int st = tensor_len(x_shape, ndim, &len);
+  if (st) return st;
+  // src/cpu/quantized.rs:157-161
+  if (ndim == 0 || x_shape[ndim - 1] != m->cols || len != m->cols)
+    return fail(UOCR_ERR_SHAPE, "invalid tensor shape: dynamic INT8 requires one input row");
+  if ((st = dynamic_checks(ctx, m))) return st;
+  if (y_len != m->rows) return fail(UOCR_ERR_SHAPE, "invalid tensor shape: output length");
+  if (!x || !y) return fail(UOCR_ERR_INVALID, "null buffer");
+  DeviceGuard g(ctx->device);
+  return host_linear(ctx, m, MODE_INT8, x, 1, y);
+}
+
+int uocr_q8_quantize_rows(uocr_ctx* ctx, const float* x_dev, size_t rows, size_t cols,
+                          int8_t* q_dev, float* s_dev) {
+  if (!ctx || (rows && cols && (!x_dev || !q_dev || !s_dev)))
+    return fail(UOCR_ERR_INVALID, "null argument");
+  if (rows == 0 || cols == 0)
+    return fail(UOCR_ERR_SHAPE, "invalid tensor shape: quantization expects a nonempty matrix");
+  if (!fits_int(rows) || !fits_int(cols))
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: matrix extent above 2^31");
+  DeviceGuard g(ctx->device);
+  launch_quantize_rows(x_dev, static_cast<long long>(cols), static_cast<int>(rows),
+                       static_cast<int>(cols), q_dev, s_dev, ctx->status_dev, ctx->sms,
+                       ctx->stream);
+  return check_launch();
+}
+
+int uocr_q8_linear_multi(uocr_ctx* ctx, const uocr_q8* const* mats, size_t n, int mode,
+                         const float* x_dev, float* const* y_dev) {
+  if (!ctx || !mats || !y_dev || !x_dev) return fail(UOCR_ERR_INVALID, "null argument");
+  if (n == 0) return ok();
+  if (mode != UOCR_WEIGHTS_ONLY && mode != UOCR_DYNAMIC_ACTIVATIONS && mode != UOCR_DYNAMIC_ROWWISE)
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: mode %d", mode);
+  std::vector<Q8View> v(n);
+  for (size_t i = 0; i < n; ++i) {
+    if (!mats[i] || !y_dev[i]) return fail(UOCR_ERR_INVALID, "null matrix or output");
+    if (mats[i]->cols != mats[0]->cols)
+      return fail(UOCR_ERR_SHAPE, "invalid tensor shape: INT8 linear input width");
+    v[i] = view(mats[i]);
+  }
+  DeviceGuard g(ctx->device);
+  const int dmode = mode == UOCR_WEIGHTS_ONLY ? MODE_FP32 : MODE_INT8;
+  bool fast = reinterpret_cast<uintptr_t>(x_dev) % 16 == 0;
+  for (size_t i = 0; i < n; ++i) fast = fast && gemv_fast_path_ok(v[i]);
+  if (fast) {
+    launch_gemv_multi(dmode, v.data(), static_cast<int>(n), x_dev, y_dev, ctx->status_dev,
+                      ctx->sms, ctx->stream);
+    return check_launch();
+  }
+  for (size_t i = 0; i < n; ++i) {
+    int st = run_linear(ctx, mats[i], dmode, x_dev, 1, y_dev[i]);
+    if (st) return st;
+  }
+  return ok();
+}
+
+// ---- routing -----------------------------------------------------------------
+static int route_checks(size_t n_experts, size_t top_k, float scale) {
+  // src/decoder/moe.rs:13-15
+  if (top_k == 0 || top_k > n_experts || !std::isfinite(scale) || scale <= 0.0f)
+    return fail(UOCR_ERR_SHAPE, "invalid tensor shape: invalid expert routing");
+  if (n_experts > 1024 || top_k > 32)
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: routing extent");
+  return ok();
+}
+
+int uocr_moe_route(uocr_ctx* ctx, const float* logits_dev, size_t tokens, size_t n_experts,
+                   size_t top_k, int normalize, float scale, int32_t* ids_dev,
+                   float* weights_dev) {
+  if (!ctx) return fail(UOCR_ERR_INVALID, "null context");
+  int st = route_checks(n_experts, top_k, scale);
+  if (st) return st;
+  if (tokens == 0) return ok();
+  if (!logits_dev || !ids_dev || !weights_dev) return fail(UOCR_ERR_INVALID, "null argument");
+  DeviceGuard g(ctx->device);
+  launch_route(logits_dev, static_cast<int>(tokens), static_cast<int>(n_experts),
+               static_cast<int>(top_k), normalize, scale, ids_dev, weights_dev, ctx->status_dev,
+               ctx->sms, ctx->stream);
+  return check_launch();
+}
+
+// ---- MoE layer ---------------------------------------------------------------
+int uocr_moe_create(uocr_ctx* ctx, const uocr_q8* shared_gate, const uocr_q8* shared_up,
+                    const uocr_q8* shared_down, const uocr_q8* const* gate,
+                    const uocr_q8* const* up, const uocr_q8* const* down, size_t n_experts,
+                    size_t top_k, int normalize_topk, float routed_scale, uocr_moe** out) {
+  if (!ctx || !out || !shared_gate || !shared_up || !shared_down || !gate || !up || !down)
+    return fail(UOCR_ERR_INVALID, "null argument");
+  *out = nullptr;
+  if (n_experts == 0) return fail(UOCR_ERR_SHAPE, "invalid tensor shape: no routed experts");
+  int st = route_checks(n_experts, top_k, routed_scale);
+  if (st) return st;
+  if (top_k > 8 || n_experts > 256)
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: top_k <= 8, experts <= 256");
+  const size_t H = shared_gate->cols, FS = shared_gate->rows;
+  // Decoder::new shape expectations (src/decoder/mod.rs:58-80)
+  auto expect = [&](const uocr_q8* m, size_t r, size_t c, const char* what) -> int {
+    if (!m) return fail(UOCR_ERR_INVALID, "null %s", what);
+    if (m->device != ctx->device)
+      return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: %s on another device", what);
+    if (m->rows != r || m->cols != c)
+      return fail(UOCR_ERR_SHAPE, "invalid tensor shape: %s: expected [%zu, %zu], got [%zu, %zu]",
+                  what, r, c, m->rows, m->cols);
+    return ok();
+  };
+  if ((st = expect(shared_up, FS, H, "shared_experts.up_proj")) ||
+      (st = expect(shared_down, H, FS, "shared_experts.down_proj")))
+    return st;
+  if (!gate[0]) return fail(UOCR_ERR_INVALID, "null experts.0.gate_proj");
+  const size_t F = gate[0]->rows;
+  std::vector<FfnView> views(n_experts);
+  bool aligned = true;
+  auto al = [](const uocr_q8* m) {
+    return reinterpret_cast<uintptr_t>(m->w) % 16 == 0 && reinterpret_cast<uintptr_t>(m->s) % 16 == 0;
+  };
+  for (size_t e = 0; e < n_experts; ++e) {
+    if ((st = expect(gate[e], F, H, "experts.gate_proj")) ||
+        (st = expect(up[e], F, H, "experts.up_proj")) ||
+        (st = expect(down[e], H, F, "experts.down_proj")))
+      return st;
+    views[e] = FfnView{view(gate[e]), view(up[e]), view(down[e])};
+    aligned = aligned && al(gate[e]) && al(up[e]) && al(down[e]);
+  }
+  aligned = aligned && al(shared_gate) && al(shared_up) && al(shared_down);
+  DeviceGuard g(ctx->device);
+  auto* L = new uocr_moe();
+  L->device = ctx->device;
+  L->n_experts = n_experts;
+  L->top_k = top_k;
+  L->normalize = normalize_topk ? 1 : 0;
+  L->scale = routed_scale;
+  L->hidden = static_cast<int>(H);
+  L->width = static_cast<int>(F);
+  L->shared_width = static_cast<int>(FS);
+  L->shared = FfnView{view(shared_gate), view(shared_up), view(shared_down)};
+  L->aligned = aligned;
+  cudaError_t e = cudaMalloc(&L->experts_dev, sizeof(FfnView) * n_experts);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(L->experts_dev, views.data(), sizeof(FfnView) * n_experts,
+                   cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    uocr_moe_free(L);
+    return fail(UOCR_ERR_CUDA, "moe_create: %s", cudaGetErrorString(e));
+  }
+  *out = L;
+  return ok();
+}
+
+int uocr_moe_free(uocr_moe* layer) {
+  if (!layer) return ok();
+  DeviceGuard g(layer->device);
+  if (layer->experts_dev) cudaFree(layer->experts_dev);
+  delete layer;
+  return ok();
+}
+
+// Reference element-count checks for the shared expert's projections at
+// `tokens` rows; the routed groups (<= tokens rows, width <= shared width)
+// are bounded by them.
+static int moe_checks(const uocr_ctx* ctx, const uocr_moe* L, size_t tokens) {
+  const size_t H = L->hidden, FS = L->shared_width;
+  const size_t counts[2] = {tokens * FS, tokens * H};
+  const size_t mats[2] = {FS * H, H * FS};
+  for (int i = 0; i < 2; ++i) {
+    int st = check_elements(ctx, counts[i]);
+    if (st) return st;
+    if (tokens != 1 && (st = check_elements(ctx, counts[i] + mats[i]))) return st;
+  }
+  return ok();
+}
+
+static int moe_run(uocr_ctx* ctx, const uocr_moe* L, int mode, const float* x, const float* logits,
+                   size_t tokens, float* y, int32_t* ids, float* wts) {
+  const int k = static_cast<int>(L->top_k);
+  // decode fast path: one token, every projection single-row
+  if (tokens == 1) {
+    MoeDecodeArgs a{};
+    a.experts = L->experts_dev;
+    a.shared = L->shared;
+    a.n_experts = static_cast<int>(L->n_experts);
+    a.top_k = k;
+    a.normalize = L->normalize;
+    a.scale = L->scale;
+    a.hidden = L->hidden;
+    a.width = L->width;
+    a.shared_width = L->shared_width;
+    if (L->aligned && moe_decode_supported(a) && reinterpret_cast<uintptr_t>(x) % 16 == 0) {
+      const size_t hn = L->shared_width + static_cast<size_t>(k) * L->width;
+      const size_t hb = (hn * 4 + 255) & ~static_cast<size_t>(255);
+      const bool own_route = !ids || !wts;
+      int st = ensure_ws(ctx, hb + (own_route ? 512 : 0));
+      if (st) return st;
+      a.x = x;
+      a.logits = logits;
+      a.h = static_cast<float*>(ctx->ws);
+      a.route_ids = own_route ? reinterpret_cast<int32_t*>(static_cast<char*>(ctx->ws) + hb) : ids;
+      a.route_weights = own_route ? reinterpret_cast<float*>(static_cast<char*>(ctx->ws) + hb + 256)
+                                  : wts;
+      a.y = y;
+      a.status = ctx->status_dev;
+      cudaError_t e = launch_moe_decode(mode == UOCR_WEIGHTS_ONLY ? MODE_FP32 : MODE_INT8, a,
+                                        ctx->sms, ctx->stream);
+      if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "moe decode launch: %s", cudaGetErrorString(e));
+      return check_launch();
+    }
+  }
+  MoePrefillArgs a{};
+  a.experts = L->experts_dev;
+  a.shared = L->shared;
+  a.n_experts = static_cast<int>(L->n_experts);
+  a.top_k = k;
+  a.normalize = L->normalize;
+  a.scale = L->scale;
+  a.hidden = L->hidden;
+  a.width = L->width;
+  a.shared_width = L->shared_width;
+  a.tokens = static_cast<int>(tokens);
+  a.x = x;
+  a.logits = logits;
+  a.y = y;
+  a.status = ctx->status_dev;
+  const size_t rb = (tokens * k * 4 + 255) & ~static_cast<size_t>(255);
+  const bool own_route = !ids || !wts;
+  const size_t need = moe_prefill_workspace(a, mode) + (own_route ? 2 * rb : 0) + 256;
+  int st = ensure_ws(ctx, need);
+  if (st) return st;
+  char* base = static_cast<char*>(ctx->ws);
+  if (own_route) {
+    a.route_ids = reinterpret_cast<int32_t*>(base);
+    a.route_weights = reinterpret_cast<float*>(base + rb);
+    base += 2 * rb;
+  } else {
+    a.route_ids = ids;
+    a.route_weights = wts;
+  }
+  a.workspace = base;
+  a.workspace_bytes = ctx->ws_bytes - (base - static_cast<char*>(ctx->ws));
+  cudaError_t e = launch_moe_prefill(mode, a, ctx->sms, ctx->stream);
+  if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "moe prefill launch: %s", cudaGetErrorString(e));
+  return check_launch();
+}
+
+int uocr_moe_forward(uocr_ctx* ctx, const uocr_moe* layer, int mode, const float* x_dev,
+                     const float* logits_dev, size_t tokens, float* y_dev, int32_t* ids_dev,
+                     float* weights_dev) {
+  if (!ctx || !layer) return fail(UOCR_ERR_INVALID, "null argument");
+  if (mode != UOCR_WEIGHTS_ONLY && mode != UOCR_DYNAMIC_ACTIVATIONS && mode != UOCR_DYNAMIC_ROWWISE)
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: mode %d", mode);
+  if (layer->device != ctx->device)
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: layer on another device");
+  if (tokens == 0) return ok();
+  if (!x_dev || !logits_dev || !y_dev) return fail(UOCR_ERR_INVALID, "null argument");
+  if (!fits_int(tokens * layer->top_k)) return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: tokens");
+  int st = moe_checks(ctx, layer, tokens);
+  if (st) return st;
+  DeviceGuard g(ctx->device);
+  return moe_run(ctx, layer, mode, x_dev, logits_dev, tokens, y_dev, ids_dev, weights_dev);
+}
+
+int uocr_moe_forward_host(uocr_ctx* ctx, const uocr_moe* layer, int mode, const float* x,
+                          const float* logits, size_t tokens, float* y, int32_t* ids,
+                          float* weights) {
+  if (!ctx || !layer) return fail(UOCR_ERR_INVALID, "null argument");
+  if (mode != UOCR_WEIGHTS_ONLY && mode != UOCR_DYNAMIC_ACTIVATIONS && mode != UOCR_DYNAMIC_ROWWISE)
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: mode %d", mode);
+  if (tokens == 0) return ok();
+  if (!x || !logits || !y) return fail(UOCR_ERR_INVALID, "null argument");
+  int st = moe_checks(ctx, layer, tokens);
+  if (st) return st;
+  DeviceGuard g(ctx->device);
+  if ((st = take_device_status(ctx))) return st;
+  const size_t H = layer->hidden, E = layer->n_experts, k = layer->top_k;
+  auto al = [](size_t b) { return (b + 255) & ~static_cast<size_t>(255); };
+  const size_t xb = al(tokens * H * 4), lb = al(tokens * E * 4), yb = al(tokens * H * 4),
+               rb = al(tokens * k * 4);
+  // Device staging has its own allocation so the layer's workspace (ctx->ws)
+  // can grow independently.
+  const size_t need = xb + lb + yb + 2 * rb;
+  if (ctx->io_bytes < need) {
+    CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    if (ctx->io) CUDA_TRY(cudaFree(ctx->io));
+    ctx->io = nullptr;
+    ctx->io_bytes = 0;
+    CUDA_TRY(cudaMalloc(&ctx->io, need));
+    ctx->io_bytes = need;
+  }
+  char* d = static_cast<char*>(ctx->io);
+  float* xd = reinterpret_cast<float*>(d);
+  float* ld = reinterpret_cast<float*>(d + xb);
+  float* yd = reinterpret_cast<float*>(d + xb + lb);
+  int32_t* id = reinterpret_cast<int32_t*>(d + xb + lb + yb);
+  float* wd = reinterpret_cast<float*>(d + xb + lb + yb + rb);
+  const bool pin = is_pinned(x) && is_pinned(logits) && is_pinned(y) && (!ids || is_pinned(ids)) &&
+                   (!weights || is_pinned(weights));
+  char* hp = nullptr;
+  if (!pin) {
+    if ((st = ensure_pinned(ctx, need))) return st;
+    hp = static_cast<char*>(ctx->pinned);
+    std::memcpy(hp, x, tokens * H * 4);
+    std::memcpy(hp + xb, logits, tokens * E * 4);
+  }
+  CUDA_TRY(cudaMemcpyAsync(xd, pin ? x : reinterpret_cast<float*>(hp), tokens * H * 4,
+                           cudaMemcpyHostToDevice, ctx->stream));
+  CUDA_TRY(cudaMemcpyAsync(ld, pin ? logits : reinterpret_cast<float*>(hp + xb), tokens * E * 4,
+                           cudaMemcpyHostToDevice, ctx->stream));
+  if ((st = moe_run(ctx, layer, mode, xd, ld, tokens, yd, id, wd))) return st;
+  CUDA_TRY(cudaMemcpyAsync(pin ? y : reinterpret_cast<float*>(hp + xb + lb), yd, tokens * H * 4,
+                           cudaMemcpyDeviceToHost, ctx->stream));
+  if (ids)
+    CUDA_TRY(cudaMemcpyAsync(pin ? ids : reinterpret_cast<int32_t*>(hp + xb + lb + yb), id,
+                             tokens * k * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  if (weights)
+    CUDA_TRY(cudaMemcpyAsync(pin ? weights : reinterpret_cast<float*>(hp + xb + lb + yb + rb), wd,
+                             tokens * k * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  if ((st = take_device_status(ctx))) return st;
+  if (!pin) {
+    std::memcpy(y, hp + xb + lb, tokens * H * 4);
+    if (ids) std::memcpy(ids, hp + xb + lb + yb, tokens * k * 4);
+    if (weights) std::memcpy(weights, hp + xb + lb + yb + rb, tokens * k * 4);
+  }
+  return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,92 @@
+// kernels.h — internal launcher declarations shared by the .cu files and the
+// C ABI (capi.cu).  Nothing here is part of the public interface.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace uocr {
+
+// Device view of one q8-block32 matrix.
+struct Q8View {
+  const int8_t* w;  // rows*cols
+  const float* s;   // rows*ceil(cols/32)
+  int rows, cols;
+};
+
+// Device view of one SwiGLU FFN (gate/up [width x hidden], down [hidden x width]).
+struct FfnView {
+  Q8View gate, up, down;
+};
+
+// Arithmetic of one projection.
+enum Mode : int { MODE_FP32 = 0, MODE_INT8 = 1 };
+
+// q8_elementwise.cu
+void launch_dequantize(const int8_t* w, const float* s, int rows, int cols, float* out, int sms,
+                       cudaStream_t st);
+void launch_quantize_rows(const float* x, long long ld_x, int rows, int cols, int8_t* q, float* s,
+                          unsigned* status, int sms, cudaStream_t st);
+void launch_validate_q8(const int8_t* w, long long n_w, const float* s, long long n_s,
+                        int check_range, unsigned* status, int sms, cudaStream_t st);
+
+// q8_gemv.cu — y[r, :] = W x[r, :] for `batch` rows of x (float, ld_x).
+//   MODE_FP32: reordered fp32 accumulation.
+//   MODE_INT8: each row block-quantized (into the xq/xs scratch of
+//              batch*cols bytes and batch*ceil(cols/32) floats, or in shared
+//              memory on the fast path), then the bit-exact ordered
+//              accumulation of linear_dynamic_int8.
+void launch_gemv(int mode, const Q8View& m, const float* x, long long ld_x, int batch, float* y,
+                 long long ld_y, int8_t* xq, float* xs, unsigned* status, int sms,
+                 cudaStream_t st);
+// Several matrices with the same cols and the same single input row: the
+// batched-stream form used to measure GEMV bandwidth (fast path only).
+void launch_gemv_multi(int mode, const Q8View* mats, int n, const float* x, float* const* ys,
+                       unsigned* status, int sms, cudaStream_t st);
+bool gemv_fast_path_ok(const Q8View& m);
+
+// moe_route.cu — moe::route for `tokens` rows of logits.  ids/weights are
+// tokens*top_k in the reference's order (probability desc, id asc).
+void launch_route(const float* logits, int tokens, int n_experts, int top_k, int normalize,
+                  float scale, int32_t* ids, float* weights, unsigned* status, int sms,
+                  cudaStream_t st);
+
+// moe_decode.cu — one token through Decoder::experts, two PDL-chained kernels.
+struct MoeDecodeArgs {
+  const FfnView* experts;  // device array [n_experts]
+  FfnView shared;
+  int n_experts, top_k, normalize;
+  float scale;
+  int hidden, width, shared_width;
+  const float* x;       // [hidden]
+  const float* logits;  // [n_experts]
+  float* h;             // scratch [shared_width + top_k*width]
+  int32_t* route_ids;   // [top_k] (route order)
+  float* route_weights; // [top_k]
+  float* y;             // [hidden]
+  unsigned* status;
+};
+bool moe_decode_supported(const MoeDecodeArgs& a);
+cudaError_t launch_moe_decode(int mode, const MoeDecodeArgs& a, int sms, cudaStream_t st);
+
+// moe_prefill.cu — many tokens: route, group by expert, grouped projections,
+// ordered combine.
+struct MoePrefillArgs {
+  const FfnView* experts;  // device [n_experts]
+  FfnView shared;
+  int n_experts, top_k, normalize;
+  float scale;
+  int hidden, width, shared_width, tokens;
+  const float* x;        // [tokens x hidden]
+  const float* logits;   // [tokens x n_experts]
+  float* y;              // [tokens x hidden]
+  int32_t* route_ids;    // [tokens x top_k]
+  float* route_weights;  // [tokens x top_k]
+  void* workspace;
+  size_t workspace_bytes;
+  unsigned* status;
+};
+size_t moe_prefill_workspace(const MoePrefillArgs& a, int mode);
+cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaStream_t st);
+
+}  // namespace uocr

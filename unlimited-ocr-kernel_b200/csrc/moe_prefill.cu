@@ -1,0 +1,415 @@
+// moe_prefill.cu — Decoder::experts for many tokens (src/decoder/mod.rs:124-220,
+// serial branch :197-219): route every token, group the (token, expert) pairs
+// by expert with tokens ascending inside a group (the order in which
+// `assignments[expert].push((row, p))` fills them), run each expert's SwiGLU
+// FFN on its gathered rows, and add p * out to the shared expert's output in
+// ascending expert id.
+//
+// Projection dispatch per group follows Decoder::projection
+// (src/decoder/mod.rs:99-112):
+//   mode WEIGHTS_ONLY        -> FP32 activations for every group;
+//   mode DYNAMIC (reference) -> int8 activations only for a group of exactly
+//                               one row, FP32 otherwise (so the shared expert
+//                               is FP32 whenever tokens > 1);
+//   mode DYNAMIC_ROWWISE     -> int8 activations for every row (extension).
+//
+// This file holds the grouping, combine and a CUDA-core grouped projection
+// kernel that serves every shape; the tensor-core grouped GEMM in
+// moe_grouped_tc.cu takes the groups it supports.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace uocr {
+
+constexpr int kGroupThreads = 1024;
+constexpr int kMaxGroupExperts = 256;
+
+// Stable counting sort of the tokens*top_k (token, expert) pairs by expert.
+// Pair i = t*top_k + j is visited in increasing i, i.e. increasing token, so
+// each expert's slice lists its tokens in ascending order.
+__global__ void __launch_bounds__(kGroupThreads) group_pairs_kernel(
+    const int32_t* __restrict__ ids, const float* __restrict__ wts, int tokens, int top_k,
+    int n_experts, int* __restrict__ counts, int* __restrict__ offsets,
+    int* __restrict__ pair_token, float* __restrict__ pair_weight, int* __restrict__ token_pos,
+    unsigned* status) {
+  __shared__ int cnt[kGroupThreads / 32][kMaxGroupExperts];
+  __shared__ int base[kMaxGroupExperts];
+  __shared__ int off[kMaxGroupExperts + 1];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int npairs = tokens * top_k;
+  for (int e = tid; e < n_experts; e += blockDim.x) base[e] = 0;
+  for (int i = tid; i < (kGroupThreads / 32) * kMaxGroupExperts; i += blockDim.x)
+    (&cnt[0][0])[i] = 0;
+  __syncthreads();
+  // pass 1: histogram
+  for (int i = tid; i < npairs; i += blockDim.x) {
+    int e = ids[i];
+    if (e < 0 || e >= n_experts) {
+      flag(status, DEV_BAD_ROUTE);
+      e = 0;
+    }
+    atomicAdd(&base[e], 1);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int run = 0;
+    for (int e = 0; e < n_experts; ++e) {
+      off[e] = run;
+      counts[e] = base[e];
+      offsets[e] = run;
+      run += base[e];
+      base[e] = 0;
+    }
+    off[n_experts] = run;
+    offsets[n_experts] = run;
+  }
+  __syncthreads();
+  // pass 2: stable positions, chunk by chunk
+  for (int c0 = 0; c0 < npairs; c0 += blockDim.x) {
+    const int i = c0 + tid;
+    const bool valid = i < npairs;
+    int e = valid ? ids[i] : -1;
+    if (valid && (e < 0 || e >= n_experts)) e = 0;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(peers & ((1u << lane) - 1));
+    if (valid && rank == 0) cnt[warp][e] = __popc(peers);
+    __syncthreads();
+    for (int x = tid; x < n_experts; x += blockDim.x) {
+      int run = base[x];
+      for (int w = 0; w < kGroupThreads / 32; ++w) {
+        const int v = cnt[w][x];
+        cnt[w][x] = run;
+        run += v;
+      }
+      base[x] = run;
+    }
+    __syncthreads();
+    if (valid) {
+      const int pos = off[e] + cnt[warp][e] + rank;
+      pair_token[pos] = i / top_k;
+      pair_weight[pos] = wts[i];
+      token_pos[i] = pos;
+    }
+    __syncthreads();
+    for (int x = tid; x < (kGroupThreads / 32) * n_experts; x += blockDim.x)
+      cnt[x / n_experts][x % n_experts] = 0;
+    __syncthreads();
+  }
+}
+
+// y[t] = shared_out[t] (already in y); then for t's experts in ascending id:
+// y[t] += p * out[pos] — src/decoder/mod.rs:208-217, one rounding per op.
+__global__ void combine_kernel(const int32_t* __restrict__ ids, const int* __restrict__ token_pos,
+                               const float* __restrict__ pair_weight,
+                               const float* __restrict__ out_routed, int tokens, int top_k,
+                               int hidden, float* __restrict__ y) {
+  const int t = blockIdx.x;
+  if (t >= tokens) return;
+  int e[8], pos[8];
+  float w[8];
+  for (int j = 0; j < top_k; ++j) {
+    e[j] = ids[t * top_k + j];
+    pos[j] = token_pos[t * top_k + j];
+    w[j] = pair_weight[pos[j]];
+  }
+  for (int i = 1; i < top_k; ++i)
+    for (int j = i; j > 0 && e[j - 1] > e[j]; --j) {
+      int te = e[j]; e[j] = e[j - 1]; e[j - 1] = te;
+      int tp = pos[j]; pos[j] = pos[j - 1]; pos[j - 1] = tp;
+      float tw = w[j]; w[j] = w[j - 1]; w[j - 1] = tw;
+    }
+  for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
+    float acc = y[static_cast<long long>(t) * hidden + c];
+    for (int j = 0; j < top_k; ++j)
+      acc = __fadd_rn(acc, __fmul_rn(w[j], out_routed[static_cast<long long>(pos[j]) * hidden + c]));
+    y[static_cast<long long>(t) * hidden + c] = acc;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CUDA-core grouped projection.  Problem p < E is expert p over its pair
+// slice; p == E is the shared expert over all tokens.
+struct GroupSet {
+  const FfnView* experts;
+  FfnView shared;
+  int E, T, H, F, FS, mode, stage;  // stage 0: gate/up -> h, stage 1: down -> out
+  const int* counts;
+  const int* offsets;
+  const int* pair_token;
+  // stage 0 inputs: x rows by token (float / block-quantized)
+  const float* x;
+  const int8_t* xq;
+  const float* xs;
+  // stage 0 outputs / stage 1 inputs: h rows (routed by pair slot, shared by token)
+  float* h_r;
+  float* h_s;
+  const int8_t* hq_r;
+  const float* hs_r;
+  const int8_t* hq_s;
+  const float* hs_s;
+  // stage 1 outputs
+  float* out_r;
+  float* y;
+};
+
+constexpr int kTM = 32, kTN = 64, kCCThreads = 256;
+
+__device__ __forceinline__ bool group_int8(int mode, int count) {
+  return mode == 2 || (mode == 1 && count == 1);
+}
+
+// Locate the m-tile `bx` among problems 0..E (tiles of kTM rows).
+__device__ __forceinline__ bool find_tile(const GroupSet& g, int bx, int& p, int& m0, int& count) {
+  int run = 0;
+  for (int q = 0; q <= g.E; ++q) {
+    const int c = q < g.E ? g.counts[q] : g.T;
+    const int tiles = (c + kTM - 1) / kTM;
+    if (bx < run + tiles) {
+      p = q;
+      m0 = (bx - run) * kTM;
+      count = c;
+      return true;
+    }
+    run += tiles;
+  }
+  return false;
+}
+
+template <bool PAIRED>
+__global__ void __launch_bounds__(kCCThreads) grouped_cc_kernel(const __grid_constant__ GroupSet g) {
+  __shared__ int s_p, s_m0, s_count;
+  __shared__ __align__(16) float xt[kTM][kBlock + 1];
+  __shared__ __align__(16) int8_t xqt[kTM][kBlock];
+  __shared__ float xst[kTM];
+  __shared__ __align__(16) int8_t wt[2][kTN][kBlock];
+  __shared__ float wst[2][kTN];
+  __shared__ int rowsrc[kTM];
+  if (threadIdx.x == 0) {
+    int p, m0, c;
+    if (!find_tile(g, blockIdx.x, p, m0, c)) p = -1;
+    s_p = p;
+    s_m0 = m0;
+    s_count = c;
+  }
+  __syncthreads();
+  const int p = s_p;
+  if (p < 0) return;
+  const int m0 = s_m0, count = s_count;
+  const bool is_shared = p == g.E;
+  const FfnView& f = is_shared ? g.shared : g.experts[p];
+  const Q8View& A = g.stage == 0 ? f.gate : f.down;
+  const Q8View& B = f.up;  // only used when PAIRED
+  const int N = A.rows, K = A.cols, nbK = blocks_of(K);
+  const int n0 = blockIdx.y * kTN;
+  if (n0 >= N) return;
+  const bool i8 = group_int8(g.mode, count);
+  const int off = is_shared ? 0 : g.offsets[p];
+  // row sources
+  if (threadIdx.x < kTM) {
+    const int i = m0 + threadIdx.x;
+    int src = -1;
+    if (i < count) src = g.stage == 0 ? (is_shared ? i : g.pair_token[off + i]) : i;
+    rowsrc[threadIdx.x] = src;
+  }
+  __syncthreads();
+  // input row pointers
+  const float* in_f = nullptr;
+  const int8_t* in_q = nullptr;
+  const float* in_s = nullptr;
+  long long in_ld = K;
+  if (g.stage == 0) {
+    in_f = g.x;
+    in_q = g.xq;
+    in_s = g.xs;
+  } else if (is_shared) {
+    in_f = g.h_s;
+    in_q = g.hq_s;
+    in_s = g.hs_s;
+  } else {
+    in_f = g.h_r + static_cast<long long>(off) * K;
+    in_q = g.hq_r + static_cast<long long>(off) * K;
+    in_s = g.hs_r + static_cast<long long>(off) * nbK;
+  }
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;  // 4 n-rows x 2 tokens
+  float acc[2][2][4];
+  for (int a = 0; a < 2; ++a)
+    for (int b = 0; b < 2; ++b)
+      for (int c = 0; c < 4; ++c) acc[a][b][c] = i8 ? -0.0f : 0.0f;
+  for (int blk = 0; blk < nbK; ++blk) {
+    const int k0 = blk * kBlock, kw = min(kBlock, K - k0);
+    // stage X tile
+    for (int e = threadIdx.x; e < kTM * kBlock; e += kCCThreads) {
+      const int r = e / kBlock, c = e % kBlock;
+      const int src = rowsrc[r];
+      if (i8) {
+        xqt[r][c] = (src >= 0 && c < kw) ? in_q[src * in_ld + k0 + c] : 0;
+        if (c == 0) xst[r] = src >= 0 ? in_s[src * static_cast<long long>(nbK) + blk] : 0.0f;
+      } else {
+        xt[r][c] = (src >= 0 && c < kw) ? in_f[src * in_ld + k0 + c] : 0.0f;
+      }
+    }
+    // stage W tiles
+    for (int e = threadIdx.x; e < kTN * kBlock; e += kCCThreads) {
+      const int r = e / kBlock, c = e % kBlock;
+      const int n = n0 + r;
+      wt[0][r][c] = (n < N && c < kw) ? A.w[static_cast<long long>(n) * K + k0 + c] : 0;
+      if (PAIRED) wt[1][r][c] = (n < N && c < kw) ? B.w[static_cast<long long>(n) * K + k0 + c] : 0;
+      if (c == 0) {
+        wst[0][r] = n < N ? A.s[static_cast<long long>(n) * nbK + blk] : 0.0f;
+        if (PAIRED) wst[1][r] = n < N ? B.s[static_cast<long long>(n) * nbK + blk] : 0.0f;
+      }
+    }
+    __syncthreads();
+    for (int mat = 0; mat < (PAIRED ? 2 : 1); ++mat)
+      for (int a = 0; a < 2; ++a) {
+        const int r = ty * 2 + a;
+        for (int c = 0; c < 4; ++c) {
+          const int nr = tx * 4 + c;
+          if (i8) {
+            int S = 0;
+            const int* wq = reinterpret_cast<const int*>(&wt[mat][nr][0]);
+            const int* xqq = reinterpret_cast<const int*>(&xqt[r][0]);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) S = __dp4a(wq[q], xqq[q], S);
+            acc[mat][a][c] = __fadd_rn(acc[mat][a][c],
+                                       __fmul_rn(__fmul_rn(static_cast<float>(S), wst[mat][nr]), xst[r]));
+          } else {
+            float d = 0.0f;
+#pragma unroll 8
+            for (int q = 0; q < kBlock; ++q) d = fmaf(static_cast<float>(wt[mat][nr][q]), xt[r][q], d);
+            acc[mat][a][c] = fmaf(wst[mat][nr], d, acc[mat][a][c]);
+          }
+        }
+      }
+    __syncthreads();
+  }
+  for (int a = 0; a < 2; ++a) {
+    const int r = ty * 2 + a;
+    const int i = m0 + r;
+    if (i >= count) continue;
+    for (int c = 0; c < 4; ++c) {
+      const int n = n0 + tx * 4 + c;
+      if (n >= N) continue;
+      if (g.stage == 0) {
+        const float h = __fmul_rn(silu_ref(acc[0][a][c]), acc[PAIRED ? 1 : 0][a][c]);
+        if (is_shared)
+          g.h_s[static_cast<long long>(i) * N + n] = h;
+        else
+          g.h_r[static_cast<long long>(off + i) * N + n] = h;
+      } else {
+        if (is_shared)
+          g.y[static_cast<long long>(i) * N + n] = acc[0][a][c];
+        else
+          g.out_r[static_cast<long long>(off + i) * N + n] = acc[0][a][c];
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+static size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+struct PrefillWs {
+  int* counts;
+  int* offsets;
+  int* pair_token;
+  float* pair_weight;
+  int* token_pos;
+  int8_t* xq;
+  float* xs;
+  float* h_r;
+  float* h_s;
+  int8_t* hq_r;
+  float* hs_r;
+  int8_t* hq_s;
+  float* hs_s;
+  float* out_r;
+  size_t bytes;
+};
+
+static PrefillWs carve(const MoePrefillArgs& a, void* base) {
+  PrefillWs w{};
+  const size_t T = a.tokens, P = static_cast<size_t>(a.tokens) * a.top_k;
+  const size_t H = a.hidden, F = a.width, FS = a.shared_width;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align256(off + bytes);
+    return base ? static_cast<char*>(base) + o : nullptr;
+  };
+  w.counts = reinterpret_cast<int*>(take(sizeof(int) * (a.n_experts + 1)));
+  w.offsets = reinterpret_cast<int*>(take(sizeof(int) * (a.n_experts + 1)));
+  w.pair_token = reinterpret_cast<int*>(take(sizeof(int) * P));
+  w.pair_weight = reinterpret_cast<float*>(take(sizeof(float) * P));
+  w.token_pos = reinterpret_cast<int*>(take(sizeof(int) * P));
+  w.xq = reinterpret_cast<int8_t*>(take(T * H));
+  w.xs = reinterpret_cast<float*>(take(sizeof(float) * T * blocks_of(a.hidden)));
+  w.h_r = reinterpret_cast<float*>(take(sizeof(float) * P * F));
+  w.h_s = reinterpret_cast<float*>(take(sizeof(float) * T * FS));
+  w.hq_r = reinterpret_cast<int8_t*>(take(P * F));
+  w.hs_r = reinterpret_cast<float*>(take(sizeof(float) * P * blocks_of(a.width)));
+  w.hq_s = reinterpret_cast<int8_t*>(take(T * FS));
+  w.hs_s = reinterpret_cast<float*>(take(sizeof(float) * T * blocks_of(a.shared_width)));
+  w.out_r = reinterpret_cast<float*>(take(sizeof(float) * P * H));
+  w.bytes = off;
+  return w;
+}
+
+size_t moe_prefill_workspace(const MoePrefillArgs& a, int mode) {
+  (void)mode;
+  return carve(a, nullptr).bytes;
+}
+
+cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaStream_t st) {
+  if (a.n_experts > kMaxGroupExperts || a.top_k > 8) return cudaErrorInvalidValue;
+  PrefillWs w = carve(a, a.workspace);
+  if (w.bytes > a.workspace_bytes) return cudaErrorInvalidValue;
+  const int T = a.tokens, k = a.top_k, E = a.n_experts;
+  launch_route(a.logits, T, E, k, a.normalize, a.scale, a.route_ids, a.route_weights, a.status,
+               sms, st);
+  group_pairs_kernel<<<1, kGroupThreads, 0, st>>>(a.route_ids, a.route_weights, T, k, E, w.counts,
+                                                 w.offsets, w.pair_token, w.pair_weight,
+                                                 w.token_pos, a.status);
+  if (mode != 0) launch_quantize_rows(a.x, a.hidden, T, a.hidden, w.xq, w.xs, a.status, sms, st);
+
+  GroupSet g{};
+  g.experts = a.experts;
+  g.shared = a.shared;
+  g.E = E;
+  g.T = T;
+  g.H = a.hidden;
+  g.F = a.width;
+  g.FS = a.shared_width;
+  g.mode = mode;
+  g.counts = w.counts;
+  g.offsets = w.offsets;
+  g.pair_token = w.pair_token;
+  g.x = a.x;
+  g.xq = w.xq;
+  g.xs = w.xs;
+  g.h_r = w.h_r;
+  g.h_s = w.h_s;
+  g.hq_r = w.hq_r;
+  g.hs_r = w.hs_r;
+  g.hq_s = w.hq_s;
+  g.hs_s = w.hs_s;
+  g.out_r = w.out_r;
+  g.y = a.y;
+  // an upper bound on m-tiles over all problems
+  const int mtiles = (T * k) / kTM + E + (T + kTM - 1) / kTM + 1;
+  const int wmax = a.width > a.shared_width ? a.width : a.shared_width;
+  g.stage = 0;
+  grouped_cc_kernel<true><<<dim3(mtiles, (wmax + kTN - 1) / kTN), kCCThreads, 0, st>>>(g);
+  if (mode != 0) {
+    launch_quantize_rows(w.h_r, a.width, T * k, a.width, w.hq_r, w.hs_r, a.status, sms, st);
+    launch_quantize_rows(w.h_s, a.shared_width, T, a.shared_width, w.hq_s, w.hs_s, a.status, sms,
+                         st);
+  }
+  g.stage = 1;
+  grouped_cc_kernel<false><<<dim3(mtiles, (a.hidden + kTN - 1) / kTN), kCCThreads, 0, st>>>(g);
+  combine_kernel<<<T, 256, 0, st>>>(a.route_ids, w.token_pos, w.pair_weight, w.out_r, T, k,
+                                    a.hidden, a.y);
+  return cudaGetLastError();
+}
+
+}  // namespace uocr

@@ -1,0 +1,136 @@
+// q8_elementwise.cu — dequantize, block quantize and storage validation.
+//
+// All three are HBM-streaming kernels: one pass over the input bytes, one
+// pass over the output bytes, no reuse.  Grids are sized in multiples of the
+// SM count by the launchers in capi.cu.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace uocr {
+
+// Int8Matrix::dequantize (src/cpu/quantized.rs:75-95): out = (w as f32) * scale,
+// one IEEE product per element (bit-exact).  Fast path: cols % 16 == 0 and
+// 16-byte aligned rows, one 16-byte weight chunk per thread (a chunk never
+// straddles a 32-column block).
+__global__ void __launch_bounds__(256) dequantize_vec16_kernel(const int8_t* __restrict__ w,
+                                                               const float* __restrict__ s,
+                                                               int rows, int cols,
+                                                               float* __restrict__ out) {
+  const int chunks_per_row = cols >> 4, nb = blocks_of(cols);
+  const long long total = static_cast<long long>(rows) * chunks_per_row;
+  for (long long c = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; c < total;
+       c += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = c / chunks_per_row;
+    const int k0 = static_cast<int>(c - r * chunks_per_row) << 4;
+    const uint4 v = __ldcs(reinterpret_cast<const uint4*>(w + r * cols + k0));
+    const float sc = __ldg(s + r * nb + (k0 >> 5));
+    const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+    float4* o = reinterpret_cast<float4*>(out + r * cols + k0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t x = words[q];
+      float4 f;
+      f.x = __fmul_rn(static_cast<float>(static_cast<int8_t>(x & 0xff)), sc);
+      f.y = __fmul_rn(static_cast<float>(static_cast<int8_t>((x >> 8) & 0xff)), sc);
+      f.z = __fmul_rn(static_cast<float>(static_cast<int8_t>((x >> 16) & 0xff)), sc);
+      f.w = __fmul_rn(static_cast<float>(static_cast<int8_t>(x >> 24)), sc);
+      __stcs(o + q, f);
+    }
+  }
+}
+
+__global__ void dequantize_generic_kernel(const int8_t* __restrict__ w, const float* __restrict__ s,
+                                          int rows, int cols, float* __restrict__ out) {
+  const int nb = blocks_of(cols);
+  const long long total = static_cast<long long>(rows) * cols;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / cols;
+    const int k = static_cast<int>(i - r * cols);
+    out[i] = __fmul_rn(static_cast<float>(w[i]), s[r * nb + k / kBlock]);
+  }
+}
+
+// Int8Matrix::quantize (src/cpu/quantized.rs:43-74), used for weights and for
+// the per-row activation quantization of linear_dynamic_int8 (:169).  One
+// warp per (row, 32-column block); lane = column within the block.  The block
+// max is an order-free reduction (fmaxf is exact), the scale an IEEE division
+// by 127, each value an IEEE division then round-half-even: bit-exact.
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restrict__ x,
+                                                            long long ld_x, int rows, int cols,
+                                                            int8_t* __restrict__ q,
+                                                            float* __restrict__ s,
+                                                            unsigned* status) {
+  const int nb = blocks_of(cols);
+  const int lane = threadIdx.x & 31;
+  const long long warps = static_cast<long long>(rows) * nb;
+  for (long long t = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) >> 5;
+       t < warps; t += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
+    const long long r = t / nb;
+    const int b = static_cast<int>(t - r * nb);
+    const int k = b * kBlock + lane;
+    const bool in = k < cols;
+    const float v = in ? x[r * ld_x + k] : 0.0f;
+    const bool bad = in && !isfinite(v);
+    if (__any_sync(0xffffffffu, bad) && lane == 0) flag(status, DEV_NONFINITE);
+    const float mx = warp_max(in ? fabsf(v) : 0.0f);
+    const float scale = __fdiv_rn(mx, 127.0f);
+    if (lane == 0) {
+      if (mx > 0.0f && scale == 0.0f) flag(status, DEV_UNDERFLOW);
+      s[r * nb + b] = scale;
+    }
+    if (in) q[r * static_cast<long long>(cols) + k] = quantize_elem(v, scale);
+  }
+}
+
+// from_parts scale rule (src/cpu/quantized.rs:31-35): finite and not < 0
+// (so -0.0 passes).  Overlay byte rule (src/cpu/quantized.rs:351): no -128.
+__global__ void validate_q8_kernel(const int8_t* __restrict__ w, long long n_w,
+                                   const float* __restrict__ s, long long n_s, int check_range,
+                                   unsigned* status) {
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  const long long tid = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  bool bad_scale = false, bad_byte = false;
+  for (long long i = tid; i < n_s; i += stride) {
+    const float v = s[i];
+    bad_scale |= !isfinite(v) || v < 0.0f;
+  }
+  if (check_range)
+    for (long long i = tid; i < n_w; i += stride) bad_byte |= w[i] == -128;
+  if (bad_scale) flag(status, DEV_BAD_SCALE);
+  if (bad_byte) flag(status, DEV_RANGE);
+}
+
+// ---------------------------------------------------------------------------
+// launchers
+void launch_dequantize(const int8_t* w, const float* s, int rows, int cols, float* out, int sms,
+                       cudaStream_t st) {
+  const bool vec = (cols % 16 == 0) && (reinterpret_cast<uintptr_t>(w) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(out) % 16 == 0);
+  if (vec) {
+    const long long chunks = static_cast<long long>(rows) * (cols / 16);
+    long long grid = (chunks + 255) / 256;
+    grid = grid < 1 ? 1 : (grid > sms * 8LL ? sms * 8LL : grid);
+    dequantize_vec16_kernel<<<static_cast<int>(grid), 256, 0, st>>>(w, s, rows, cols, out);
+  } else {
+    const long long n = static_cast<long long>(rows) * cols;
+    long long grid = (n + 255) / 256;
+    grid = grid < 1 ? 1 : (grid > sms * 8LL ? sms * 8LL : grid);
+    dequantize_generic_kernel<<<static_cast<int>(grid), 256, 0, st>>>(w, s, rows, cols, out);
+  }
+}
+
+void launch_quantize_rows(const float* x, long long ld_x, int rows, int cols, int8_t* q, float* s,
+                          unsigned* status, int sms, cudaStream_t st) {
+  const long long warps = static_cast<long long>(rows) * blocks_of(cols);
+  long long grid = (warps + 7) / 8;
+  grid = grid < 1 ? 1 : (grid > sms * 16LL ? sms * 16LL : grid);
+  quantize_rows_kernel<<<static_cast<int>(grid), 256, 0, st>>>(x, ld_x, rows, cols, q, s, status);
+}
+
+void launch_validate_q8(const int8_t* w, long long n_w, const float* s, long long n_s,
+                        int check_range, unsigned* status, int sms, cudaStream_t st) {
+  validate_q8_kernel<<<sms * 4, 256, 0, st>>>(w, n_w, s, n_s, check_range, status);
+}
+
+}  // namespace uocr

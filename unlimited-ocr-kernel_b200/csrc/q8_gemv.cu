@@ -1,0 +1,314 @@
+// q8_gemv.cu — q8-block32 matrix-vector products (decode, M = 1).
+//
+// Two paths:
+//  * gemv_tma_kernel  — the HBM-streaming path.  Persistent CTAs walk row
+//    tiles of one or more matrices that share the input row.  A producer warp
+//    moves each tile (int8 rows + their fp32 block scales, both contiguous in
+//    HBM) into a ring of shared-memory stages with 1-D bulk async copies
+//    completed on mbarriers; eight consumer warps compute from shared memory.
+//    Requires cols % 128 == 0 and 16-byte aligned storage.
+//  * gemv_generic_kernel — any shape and any batch; one warp per output row.
+//
+// Lane mapping of the fast path: lane l owns bytes [4l, 4l+4) of every
+// 128-byte window of a row, so a lane's 4 weights always sit inside one
+// 32-column scale block (block = window*4 + l/8).
+//
+// FP32-activation mode (Int8Matrix::linear, src/cpu/quantized.rs:99-149):
+//   y = sum_b s_b * sum_{k in b} w_k x_k, fp32 FMA accumulation, reordered
+//   relative to the reference's left-to-right sum (tolerance-checked).
+// int8-activation mode (linear_dynamic_int8, src/cpu/quantized.rs:155-236):
+//   S_b = sum_{k in b} w_k xq_k exactly in int32 (dp4a), then
+//   acc = acc + (float(S_b) * ws_b) * xs_b over b = 0,1,2,... with _rn
+//   intrinsics starting from -0.0: the reference's exact rounding sequence.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace uocr {
+
+// ---------------------------------------------------------------------------
+// generic path
+template <int MODE>
+__global__ void __launch_bounds__(256) gemv_generic_kernel(Q8View m, const float* __restrict__ x,
+                                                           long long ld_x,
+                                                           const int8_t* __restrict__ xq,
+                                                           const float* __restrict__ xs,
+                                                           int batch, float* __restrict__ y,
+                                                           long long ld_y) {
+  const int lane = threadIdx.x & 31;
+  const int nb = blocks_of(m.cols);
+  const long long warps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+  for (long long n = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) >> 5;
+       n < m.rows; n += warps) {
+    const int8_t* wr = m.w + n * m.cols;
+    const float* sr = m.s + n * nb;
+    for (int r = 0; r < batch; ++r) {
+      if (MODE == MODE_FP32) {
+        const float* xr = x + r * ld_x;
+        float acc = 0.0f;
+        for (int k = lane; k < m.cols; k += 32)
+          acc = fmaf(__fmul_rn(static_cast<float>(wr[k]), sr[k >> 5]), xr[k], acc);
+        acc = warp_sum(acc);
+        if (lane == 0) y[r * ld_y + n] = acc;
+      } else {
+        const int8_t* qr = xq + static_cast<long long>(r) * m.cols;
+        const float* sx = xs + static_cast<long long>(r) * nb;
+        float acc = -0.0f;
+        for (int b0 = 0; b0 < nb; b0 += 32) {
+          const int b = b0 + lane;
+          float t = 0.0f;
+          if (b < nb) {
+            const int k0 = b * kBlock, k1 = min(k0 + kBlock, m.cols);
+            int sum = 0;
+            for (int k = k0; k < k1; ++k) sum += static_cast<int>(wr[k]) * static_cast<int>(qr[k]);
+            t = __fmul_rn(__fmul_rn(static_cast<float>(sum), sr[b]), sx[b]);
+          }
+          const int lim = min(32, nb - b0);
+          for (int i = 0; i < lim; ++i) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, t, i));
+        }
+        if (lane == 0) y[r * ld_y + n] = acc;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// fast path
+constexpr int kGemvConsumerWarps = 8;
+constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;
+constexpr int kGemvStages = 4;
+constexpr int kGemvMaxMats = 16;
+
+struct GemvTmaParams {
+  const int8_t* w[kGemvMaxMats];
+  const float* s[kGemvMaxMats];
+  float* y[kGemvMaxMats];
+  int tile_begin[kGemvMaxMats + 1];  // prefix of tiles per matrix
+  int rows[kGemvMaxMats];
+  int n_mats, cols, tile_rows, total_tiles;
+  const float* x;
+  unsigned* status;
+};
+
+// Per-warp dot of one smem row (FP32 mode).  xsm: cols floats in smem.
+__device__ __forceinline__ float row_dot_fp32(const int8_t* wrow, const float* srow,
+                                              const float* xsm, int cols, int lane) {
+  float acc = 0.0f;
+#pragma unroll 2
+  for (int k0 = lane * 4; k0 < cols; k0 += 128) {
+    const float4 xv = *reinterpret_cast<const float4*>(xsm + k0);
+    const uint32_t wv = *reinterpret_cast<const uint32_t*>(wrow + k0);
+    acc = fmaf(srow[k0 >> 5], dot4_i8_f32(wv, xv), acc);
+  }
+  return warp_sum(acc);
+}
+
+// Per-warp ordered dot of one smem row (int8 mode).  xq: cols int8 in smem,
+// xs: nb floats in smem.  Every lane returns the same value.
+__device__ __forceinline__ float row_dot_int8(const int8_t* wrow, const float* srow,
+                                              const int8_t* xq, const float* xs, int cols,
+                                              int lane) {
+  float acc = -0.0f;
+  for (int k0 = lane * 4; k0 < cols; k0 += 128) {
+    const int b = k0 >> 5;
+    int p = __dp4a(*reinterpret_cast<const int*>(wrow + k0), *reinterpret_cast<const int*>(xq + k0),
+                   0);
+    p += __shfl_xor_sync(0xffffffffu, p, 1);
+    p += __shfl_xor_sync(0xffffffffu, p, 2);
+    p += __shfl_xor_sync(0xffffffffu, p, 4);
+    const float t = __fmul_rn(__fmul_rn(static_cast<float>(p), srow[b]), xs[b]);
+    acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, t, 0));
+    acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, t, 8));
+    acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, t, 16));
+    acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, t, 24));
+  }
+  return acc;
+}
+
+// Block-quantize the CTA's copy of x (cols floats, smem) into xq/xs (smem),
+// the activation step of linear_dynamic_int8 (src/cpu/quantized.rs:169).
+// One warp per 32-column block.  Uses all threads of the CTA.
+__device__ __forceinline__ void quantize_x_smem(const float* xsm, int cols, int8_t* xq, float* xs,
+                                               unsigned* status) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int nb = blocks_of(cols);
+  for (int b = warp; b < nb; b += nw) {
+    const int k = b * kBlock + lane;
+    const bool in = k < cols;
+    const float v = in ? xsm[k] : 0.0f;
+    const bool bad = in && !isfinite(v);
+    if (__any_sync(0xffffffffu, bad) && lane == 0) flag(status, DEV_NONFINITE);
+    const float mx = warp_max(in ? fabsf(v) : 0.0f);
+    const float scale = __fdiv_rn(mx, 127.0f);
+    if (lane == 0) {
+      if (mx > 0.0f && scale == 0.0f) flag(status, DEV_UNDERFLOW);
+      xs[b] = scale;
+    }
+    if (in) xq[k] = quantize_elem(v, scale);
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const __grid_constant__ GemvTmaParams p) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int cols = p.cols, nb = cols >> 5, TR = p.tile_rows;
+  const int w_bytes = TR * cols, s_bytes = TR * nb * 4;
+  const int stage_bytes = w_bytes + s_bytes;
+  unsigned char* ring = smem;
+  float* xsm = reinterpret_cast<float*>(smem + kGemvStages * stage_bytes);
+  int8_t* xq = reinterpret_cast<int8_t*>(xsm + cols);
+  float* xs = reinterpret_cast<float*>(xq + cols);
+  uint64_t* full = reinterpret_cast<uint64_t*>(
+      (reinterpret_cast<uintptr_t>(xs + nb) + 15) & ~static_cast<uintptr_t>(15));
+  uint64_t* empty = full + kGemvStages;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kGemvStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kGemvConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  for (int k = threadIdx.x; k < cols; k += blockDim.x) xsm[k] = p.x[k];
+  __syncthreads();
+  if (MODE == MODE_INT8) {
+    quantize_x_smem(xsm, cols, xq, xs, p.status);
+    __syncthreads();
+  }
+
+  if (warp == kGemvConsumerWarps) {
+    // producer
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++it) {
+        const int stage = it % kGemvStages;
+        if (it >= kGemvStages) ok = mbar_wait(&empty[stage], ((it / kGemvStages) - 1) & 1, p.status);
+        if (!ok) break;
+        int mi = 0;
+        while (tile >= p.tile_begin[mi + 1]) ++mi;
+        const int r0 = (tile - p.tile_begin[mi]) * TR;
+        const int nr = min(TR, p.rows[mi] - r0);
+        unsigned char* dst = ring + stage * stage_bytes;
+        mbar_arrive_expect_tx(&full[stage], nr * cols + nr * nb * 4);
+        bulk_g2s(dst, p.w[mi] + static_cast<long long>(r0) * cols, nr * cols, &full[stage]);
+        bulk_g2s(dst + w_bytes, p.s[mi] + static_cast<long long>(r0) * nb, nr * nb * 4, &full[stage]);
+      }
+      // drain: every issued copy has landed before the CTA may exit
+      const int issued = it;
+      for (int j = issued - kGemvStages; j < issued; ++j)
+        if (j >= 0) mbar_wait(&full[j % kGemvStages], (j / kGemvStages) & 1, p.status);
+    }
+    return;
+  }
+
+  // consumers
+  int it = 0;
+  for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++it) {
+    const int stage = it % kGemvStages;
+    if (!mbar_wait(&full[stage], (it / kGemvStages) & 1, p.status)) break;
+    int mi = 0;
+    while (tile >= p.tile_begin[mi + 1]) ++mi;
+    const int r0 = (tile - p.tile_begin[mi]) * TR;
+    const int nr = min(TR, p.rows[mi] - r0);
+    const int8_t* wt = reinterpret_cast<const int8_t*>(ring + stage * stage_bytes);
+    const float* st = reinterpret_cast<const float*>(ring + stage * stage_bytes + w_bytes);
+    for (int r = warp; r < nr; r += kGemvConsumerWarps) {
+      float v;
+      if (MODE == MODE_FP32)
+        v = row_dot_fp32(wt + r * cols, st + r * nb, xsm, cols, lane);
+      else
+        v = row_dot_int8(wt + r * cols, st + r * nb, xq, xs, cols, lane);
+      if (lane == 0) p.y[mi][r0 + r] = v;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
+  }
+}
+
+bool gemv_fast_path_ok(const Q8View& m) {
+  return m.cols % 128 == 0 && m.cols <= 8192 && reinterpret_cast<uintptr_t>(m.w) % 16 == 0 &&
+         reinterpret_cast<uintptr_t>(m.s) % 16 == 0;
+}
+
+static size_t gemv_tma_smem(int cols, int tile_rows) {
+  const int nb = cols / 32;
+  const size_t stage = static_cast<size_t>(tile_rows) * cols + static_cast<size_t>(tile_rows) * nb * 4;
+  return kGemvStages * stage + cols * 4 + cols + nb * 4 + 16 + 2 * kGemvStages * 8 + 16;
+}
+
+template <int MODE>
+static void launch_gemv_tma(const Q8View* mats, int n, const float* x, float* const* ys,
+                            unsigned* status, int sms, cudaStream_t st) {
+  GemvTmaParams p{};
+  const int cols = mats[0].cols;
+  long long total_rows = 0;
+  for (int i = 0; i < n; ++i) total_rows += mats[i].rows;
+  // ~4 tiles per SM, 4..32 rows per tile
+  int tr = static_cast<int>((total_rows + sms * 4LL - 1) / (sms * 4LL));
+  tr = tr < 4 ? 4 : (tr > 32 ? 32 : tr);
+  while (tr > 4 && gemv_tma_smem(cols, tr) > 200 * 1024) tr -= 4;
+  p.n_mats = n;
+  p.cols = cols;
+  p.tile_rows = tr;
+  p.x = x;
+  p.status = status;
+  int tiles = 0;
+  for (int i = 0; i < n; ++i) {
+    p.w[i] = mats[i].w;
+    p.s[i] = mats[i].s;
+    p.y[i] = ys[i];
+    p.rows[i] = mats[i].rows;
+    p.tile_begin[i] = tiles;
+    tiles += (mats[i].rows + tr - 1) / tr;
+  }
+  p.tile_begin[n] = tiles;
+  for (int i = n + 1; i <= kGemvMaxMats; ++i) p.tile_begin[i] = tiles;
+  p.total_tiles = tiles;
+  const size_t smem = gemv_tma_smem(cols, tr);
+  static unsigned configured = 0;  // one bit per device ordinal
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured & (1u << (dev & 31)))) {
+    cudaFuncSetAttribute(gemv_tma_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         210 * 1024);
+    configured |= 1u << (dev & 31);
+  }
+  const int grid = tiles < sms ? tiles : sms;
+  gemv_tma_kernel<MODE><<<grid, kGemvThreads, smem, st>>>(p);
+}
+
+void launch_gemv_multi(int mode, const Q8View* mats, int n, const float* x, float* const* ys,
+                       unsigned* status, int sms, cudaStream_t st) {
+  for (int base = 0; base < n; base += kGemvMaxMats) {
+    const int cnt = n - base < kGemvMaxMats ? n - base : kGemvMaxMats;
+    if (mode == MODE_FP32)
+      launch_gemv_tma<MODE_FP32>(mats + base, cnt, x, ys + base, status, sms, st);
+    else
+      launch_gemv_tma<MODE_INT8>(mats + base, cnt, x, ys + base, status, sms, st);
+  }
+}
+
+void launch_gemv(int mode, const Q8View& m, const float* x, long long ld_x, int batch, float* y,
+                 long long ld_y, int8_t* xq, float* xs, unsigned* status, int sms,
+                 cudaStream_t st) {
+  if (batch == 1 && gemv_fast_path_ok(m) && reinterpret_cast<uintptr_t>(x) % 16 == 0) {
+    float* ys[1] = {y};
+    if (mode == MODE_FP32)
+      launch_gemv_tma<MODE_FP32>(&m, 1, x, ys, status, sms, st);
+    else
+      launch_gemv_tma<MODE_INT8>(&m, 1, x, ys, status, sms, st);
+    return;
+  }
+  long long grid = (static_cast<long long>(m.rows) + 7) / 8;
+  grid = grid < 1 ? 1 : (grid > sms * 16LL ? sms * 16LL : grid);
+  if (mode == MODE_INT8) launch_quantize_rows(x, ld_x, batch, m.cols, xq, xs, status, sms, st);
+  if (mode == MODE_FP32)
+    gemv_generic_kernel<MODE_FP32><<<static_cast<int>(grid), 256, 0, st>>>(m, x, ld_x, xq, xs,
+                                                                          batch, y, ld_y);
+  else
+    gemv_generic_kernel<MODE_INT8><<<static_cast<int>(grid), 256, 0, st>>>(m, x, ld_x, xq, xs,
+                                                                          batch, y, ld_y);
+}
+
+}  // namespace uocr

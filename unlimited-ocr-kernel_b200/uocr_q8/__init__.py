@@ -1,0 +1,334 @@
+"""uocr_q8 — Python front end of the B200 q8-block32 library (libuocr_q8.so).
+
+Mirrors the reference's operator surface (Rust crate `uocr`):
+
+* ``Int8Matrix`` — ``from_parts``, ``quantize``, ``dequantize``,
+  ``storage_bytes``, ``linear``, ``linear_dynamic_int8``
+  (src/cpu/quantized.rs:11-237);
+* ``QuantizationMode`` (src/cpu/quantized.rs:242-247);
+* ``GpuContext`` — stands where ``CpuContext`` stands (src/cpu/mod.rs:18-79):
+  the device, the scratch limit and the stream every call runs on;
+* ``route`` (src/decoder/moe.rs:7-30) and ``MoeLayer`` — ``Decoder::experts``
+  (src/decoder/mod.rs:124-220);
+* ``QuantizedWeights`` — the ``uocr-q8-block32-v1`` overlay loader
+  (src/cpu/quantized.rs:305-369), in ``uocr_q8.overlay``.
+
+Errors raise ``OcrError`` whose ``kind`` is the reference's OcrError variant
+name.  Host methods take and return numpy arrays (Tensor in, Tensor out);
+``*_device`` methods take torch CUDA tensors and run asynchronously on the
+context's stream.  Every compute call goes to the CUDA library; nothing here
+computes on the CPU.
+"""
+from __future__ import annotations
+
+import ctypes
+import enum
+from typing import Optional, Sequence
+
+import numpy as np
+
+from . import _lib
+from ._lib import LibraryMissing
+
+BLOCK = 32
+
+_KINDS = {1: "Io", 2: "Json", 3: "Format", 4: "Shape", 5: "Unsupported", 6: "Resource",
+          7: "Numerical", 8: "Cuda", 9: "Nccl", 10: "Timeout", 11: "Invalid"}
+
+
+class OcrError(RuntimeError):
+    """A failed call; ``kind`` names the reference's OcrError variant."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(f"{_KINDS.get(code, code)}: {message}")
+        self.code = code
+        self.kind = _KINDS.get(code, "Unknown")
+        self.message = message
+
+
+def _check(code: int) -> None:
+    if code:
+        L = _lib.load()
+        raise OcrError(code, L.uocr_last_error().decode(errors="replace"))
+
+
+def lib():
+    return _lib.load()
+
+
+class QuantizationMode(enum.IntEnum):
+    WEIGHTS_ONLY = 0
+    DYNAMIC_ACTIVATIONS = 1
+    DYNAMIC_ROWWISE = 2  # extension: int8 activations for every row
+
+
+def _ptr(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _tptr(t) -> int:
+    return int(t.data_ptr())
+
+
+class GpuContext:
+    """Device, scratch limit and stream of a sequence of calls."""
+
+    def __init__(self, device: int = 0, scratch_limit: int = 1 << 34):
+        h = ctypes.c_void_p()
+        _check(lib().uocr_ctx_create(int(device), int(scratch_limit), ctypes.byref(h)))
+        self._h = h
+        self.device = int(device)
+        self.scratch_limit = int(scratch_limit)
+
+    @property
+    def handle(self):
+        return self._h
+
+    def set_stream(self, stream) -> None:
+        """Run on a torch.cuda.Stream (or a raw cudaStream_t int)."""
+        raw = getattr(stream, "cuda_stream", stream)
+        _check(lib().uocr_ctx_set_stream(self._h, ctypes.c_void_p(int(raw))))
+
+    def sync(self) -> None:
+        _check(lib().uocr_ctx_sync(self._h))
+
+    def sm_count(self) -> int:
+        d, s = ctypes.c_int(), ctypes.c_int()
+        _check(lib().uocr_ctx_device(self._h, ctypes.byref(d), ctypes.byref(s)))
+        return s.value
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().uocr_ctx_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_default_ctx = {}
+
+
+def default_context(device: int = 0) -> GpuContext:
+    if device not in _default_ctx:
+        _default_ctx[device] = GpuContext(device)
+    return _default_ctx[device]
+
+
+class Int8Matrix:
+    """Device-resident q8-block32 matrix (src/cpu/quantized.rs:11-16)."""
+
+    def __init__(self, handle, ctx: GpuContext, keepalive=None):
+        self._h = handle
+        self.ctx = ctx
+        self._keep = keepalive
+        r, c = ctypes.c_size_t(), ctypes.c_size_t()
+        _check(lib().uocr_q8_shape(self._h, ctypes.byref(r), ctypes.byref(c)))
+        self.rows, self.cols = r.value, c.value
+
+    # -- constructors -----------------------------------------------------
+    @classmethod
+    def from_parts(cls, rows: int, cols: int, weights, scales,
+                   ctx: Optional[GpuContext] = None) -> "Int8Matrix":
+        ctx = ctx or default_context()
+        w = np.ascontiguousarray(weights, dtype=np.int8).reshape(-1)
+        s = np.ascontiguousarray(scales, dtype=np.float32).reshape(-1)
+        h = ctypes.c_void_p()
+        _check(lib().uocr_q8_from_parts(ctx.handle, rows, cols, _ptr(w), w.size, _ptr(s), s.size,
+                                        ctypes.byref(h)))
+        return cls(h, ctx)
+
+    @classmethod
+    def quantize(cls, matrix, ctx: Optional[GpuContext] = None) -> "Int8Matrix":
+        ctx = ctx or default_context()
+        x = np.ascontiguousarray(matrix, dtype=np.float32)
+        if x.ndim != 2:
+            raise OcrError(4, "invalid tensor shape: quantization expects a nonempty matrix")
+        h = ctypes.c_void_p()
+        _check(lib().uocr_q8_quantize(ctx.handle, x.shape[0], x.shape[1], _ptr(x),
+                                      ctypes.byref(h)))
+        return cls(h, ctx)
+
+    @classmethod
+    def from_device(cls, rows: int, cols: int, weights_t, scales_t,
+                    ctx: Optional[GpuContext] = None) -> "Int8Matrix":
+        """Borrow torch CUDA tensors (int8 rows*cols, float32 rows*blocks)."""
+        ctx = ctx or default_context()
+        h = ctypes.c_void_p()
+        _check(lib().uocr_q8_from_device(ctx.handle, rows, cols, ctypes.c_void_p(_tptr(weights_t)),
+                                         ctypes.c_void_p(_tptr(scales_t)), ctypes.byref(h)))
+        return cls(h, ctx, keepalive=(weights_t, scales_t))
+
+    # -- properties -------------------------------------------------------
+    @property
+    def handle(self):
+        return self._h
+
+    def storage_bytes(self) -> int:
+        return int(lib().uocr_q8_storage_bytes(self._h))
+
+    def download(self):
+        w = np.empty((self.rows, self.cols), np.int8)
+        s = np.empty((self.rows, (self.cols + BLOCK - 1) // BLOCK), np.float32)
+        _check(lib().uocr_q8_download(self.ctx.handle, self._h, _ptr(w), _ptr(s)))
+        return w, s
+
+    def device_ptrs(self):
+        w, s = ctypes.c_void_p(), ctypes.c_void_p()
+        _check(lib().uocr_q8_device_ptrs(self._h, ctypes.byref(w), ctypes.byref(s)))
+        return w.value, s.value
+
+    # -- reference operations (host tensors) --------------------------------
+    def dequantize(self) -> np.ndarray:
+        out = np.empty((self.rows, self.cols), np.float32)
+        _check(lib().uocr_q8_dequantize_host(self.ctx.handle, self._h, _ptr(out), out.size))
+        return out
+
+    def _host_call(self, fn, x):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        shape = (ctypes.c_size_t * max(x.ndim, 1))(*x.shape)
+        out_shape = tuple(x.shape[:-1]) + (self.rows,) if x.ndim else (self.rows,)
+        y_len = int(np.prod(out_shape)) if x.ndim and x.shape[-1] == self.cols else 0
+        y = np.empty((max(y_len, 1),), np.float32)
+        _check(fn(self.ctx.handle, self._h, _ptr(x), shape, x.ndim, _ptr(y), y_len))
+        return y[:y_len].reshape(out_shape)
+
+    def linear(self, x) -> np.ndarray:
+        return self._host_call(lib().uocr_q8_linear_host, x)
+
+    def linear_dynamic_int8(self, x) -> np.ndarray:
+        return self._host_call(lib().uocr_q8_linear_dynamic_int8_host, x)
+
+    # -- device forms (torch CUDA tensors, asynchronous) ---------------------
+    def linear_device(self, x_t, y_t=None, dynamic: bool = False):
+        import torch
+        batch = x_t.numel() // self.cols
+        if y_t is None:
+            y_t = torch.empty((batch, self.rows), dtype=torch.float32, device=x_t.device)
+        fn = lib().uocr_q8_linear_dynamic_int8 if dynamic else lib().uocr_q8_linear
+        _check(fn(self.ctx.handle, self._h, ctypes.c_void_p(_tptr(x_t)), batch,
+                  ctypes.c_void_p(_tptr(y_t))))
+        return y_t
+
+    def dequantize_device(self, out_t=None):
+        import torch
+        if out_t is None:
+            out_t = torch.empty((self.rows, self.cols), dtype=torch.float32,
+                                device=f"cuda:{self.ctx.device}")
+        _check(lib().uocr_q8_dequantize(self.ctx.handle, self._h, ctypes.c_void_p(_tptr(out_t))))
+        return out_t
+
+    def free(self) -> None:
+        if getattr(self, "_h", None):
+            lib().uocr_q8_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def quantize_rows_device(ctx: GpuContext, x_t, q_t=None, s_t=None):
+    import torch
+    rows, cols = x_t.shape
+    nb = (cols + BLOCK - 1) // BLOCK
+    q_t = q_t if q_t is not None else torch.empty((rows, cols), dtype=torch.int8, device=x_t.device)
+    s_t = s_t if s_t is not None else torch.empty((rows, nb), dtype=torch.float32, device=x_t.device)
+    _check(lib().uocr_q8_quantize_rows(ctx.handle, ctypes.c_void_p(_tptr(x_t)), rows, cols,
+                                       ctypes.c_void_p(_tptr(q_t)), ctypes.c_void_p(_tptr(s_t))))
+    return q_t, s_t
+
+
+def linear_multi_device(ctx: GpuContext, mats: Sequence[Int8Matrix], x_t, ys: Sequence,
+                        mode: int = QuantizationMode.WEIGHTS_ONLY) -> None:
+    n = len(mats)
+    mh = (ctypes.c_void_p * n)(*[m.handle.value for m in mats])
+    yh = (ctypes.c_void_p * n)(*[_tptr(y) for y in ys])
+    _check(lib().uocr_q8_linear_multi(ctx.handle, mh, n, int(mode), ctypes.c_void_p(_tptr(x_t)),
+                                      yh))
+
+
+def route_device(ctx: GpuContext, logits_t, top_k: int, normalize: bool = False,
+                 scale: float = 1.0):
+    """moe::route for every row of logits (torch CUDA tensor [tokens, experts])."""
+    import torch
+    tokens, n = logits_t.shape
+    ids = torch.empty((tokens, top_k), dtype=torch.int32, device=logits_t.device)
+    wts = torch.empty((tokens, top_k), dtype=torch.float32, device=logits_t.device)
+    _check(lib().uocr_moe_route(ctx.handle, ctypes.c_void_p(_tptr(logits_t)), tokens, n, top_k,
+                                int(bool(normalize)), float(scale), ctypes.c_void_p(_tptr(ids)),
+                                ctypes.c_void_p(_tptr(wts))))
+    return ids, wts
+
+
+class MoeLayer:
+    """Decoder::experts over device-resident q8 FFNs (src/decoder/mod.rs:124-220)."""
+
+    def __init__(self, ctx: GpuContext, shared: Sequence[Int8Matrix],
+                 experts: Sequence[Sequence[Int8Matrix]], top_k: int,
+                 normalize_topk: bool = False, routed_scale: float = 1.0):
+        n = len(experts)
+        arr = lambda i: (ctypes.c_void_p * n)(*[e[i].handle.value for e in experts])
+        h = ctypes.c_void_p()
+        _check(lib().uocr_moe_create(ctx.handle, shared[0].handle, shared[1].handle,
+                                     shared[2].handle, arr(0), arr(1), arr(2), n, top_k,
+                                     int(bool(normalize_topk)), float(routed_scale),
+                                     ctypes.byref(h)))
+        self._h = h
+        self.ctx = ctx
+        self._keep = (list(shared), [list(e) for e in experts])
+        self.top_k = top_k
+        self.n_experts = n
+        self.hidden = shared[0].cols
+
+    def forward(self, x, logits, mode: int = QuantizationMode.WEIGHTS_ONLY):
+        """Host tensors in, host tensors out: (y, ids, weights)."""
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, self.hidden)
+        logits = np.ascontiguousarray(logits, dtype=np.float32).reshape(x.shape[0], self.n_experts)
+        t = x.shape[0]
+        y = np.empty_like(x)
+        ids = np.empty((t, self.top_k), np.int32)
+        wts = np.empty((t, self.top_k), np.float32)
+        _check(lib().uocr_moe_forward_host(self.ctx.handle, self._h, int(mode), _ptr(x),
+                                           _ptr(logits), t, _ptr(y), _ptr(ids), _ptr(wts)))
+        return y, ids, wts
+
+    def forward_device(self, x_t, logits_t, mode: int = QuantizationMode.WEIGHTS_ONLY, y_t=None,
+                       ids_t=None, wts_t=None):
+        import torch
+        t = x_t.shape[0]
+        y_t = y_t if y_t is not None else torch.empty_like(x_t)
+        ip = ctypes.c_void_p(_tptr(ids_t)) if ids_t is not None else None
+        wp = ctypes.c_void_p(_tptr(wts_t)) if wts_t is not None else None
+        _check(lib().uocr_moe_forward(self.ctx.handle, self._h, int(mode),
+                                      ctypes.c_void_p(_tptr(x_t)), ctypes.c_void_p(_tptr(logits_t)),
+                                      t, ctypes.c_void_p(_tptr(y_t)), ip, wp))
+        return y_t
+
+    def forward_host_ptrs(self, x_ptr: int, logits_ptr: int, tokens: int, y_ptr: int,
+                          mode: int = QuantizationMode.WEIGHTS_ONLY) -> None:
+        """Raw host-pointer form (pinned buffers), for end-to-end timing."""
+        _check(lib().uocr_moe_forward_host(self.ctx.handle, self._h, int(mode),
+                                           ctypes.c_void_p(x_ptr), ctypes.c_void_p(logits_ptr),
+                                           tokens, ctypes.c_void_p(y_ptr), None, None))
+
+    def free(self) -> None:
+        if getattr(self, "_h", None):
+            lib().uocr_moe_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+__all__ = ["BLOCK", "OcrError", "QuantizationMode", "GpuContext", "Int8Matrix", "MoeLayer",
+           "route_device", "quantize_rows_device", "linear_multi_device", "default_context",
+           "LibraryMissing"]

@@ -1,0 +1,78 @@
+"""Loader and ctypes signatures of libuocr_q8.so (include/uocr_q8.h).
+
+The product path is the CUDA library; there is no CPU fallback.  If the
+library is missing, importing the package still works (so CPU-only tooling
+can inspect it) but every call raises ``LibraryMissing``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(PKG_DIR, "libuocr_q8.so")
+
+
+class LibraryMissing(RuntimeError):
+    pass
+
+
+P = ctypes.c_void_p
+S = ctypes.c_size_t
+I = ctypes.c_int
+F = ctypes.c_float
+PP = ctypes.POINTER(ctypes.c_void_p)
+
+# name -> (restype, argtypes); mirrors include/uocr_q8.h one to one.
+SIGNATURES = {
+    "uocr_abi_version": (I, []),
+    "uocr_last_error": (ctypes.c_char_p, []),
+    "uocr_status_name": (ctypes.c_char_p, [I]),
+    "uocr_ctx_create": (I, [I, S, PP]),
+    "uocr_ctx_destroy": (I, [P]),
+    "uocr_ctx_set_stream": (I, [P, P]),
+    "uocr_ctx_sync": (I, [P]),
+    "uocr_ctx_device": (I, [P, ctypes.POINTER(I), ctypes.POINTER(I)]),
+    "uocr_q8_from_parts": (I, [P, S, S, P, S, P, S, PP]),
+    "uocr_q8_from_device": (I, [P, S, S, P, P, PP]),
+    "uocr_q8_quantize": (I, [P, S, S, P, PP]),
+    "uocr_q8_free": (I, [P]),
+    "uocr_q8_shape": (I, [P, ctypes.POINTER(S), ctypes.POINTER(S)]),
+    "uocr_q8_storage_bytes": (S, [P]),
+    "uocr_q8_device_ptrs": (I, [P, PP, PP]),
+    "uocr_q8_download": (I, [P, P, P, P]),
+    "uocr_q8_dequantize": (I, [P, P, P]),
+    "uocr_q8_dequantize_host": (I, [P, P, P, S]),
+    "uocr_q8_linear": (I, [P, P, P, S, P]),
+    "uocr_q8_linear_host": (I, [P, P, P, P, S, P, S]),
+    "uocr_q8_linear_dynamic_int8": (I, [P, P, P, S, P]),
+    "uocr_q8_linear_dynamic_int8_host": (I, [P, P, P, P, S, P, S]),
+    "uocr_q8_quantize_rows": (I, [P, P, S, S, P, P]),
+    "uocr_q8_linear_multi": (I, [P, P, S, I, P, P]),
+    "uocr_moe_route": (I, [P, P, S, S, S, I, F, P, P]),
+    "uocr_moe_create": (I, [P, P, P, P, P, P, P, S, S, I, F, PP]),
+    "uocr_moe_free": (I, [P]),
+    "uocr_moe_forward": (I, [P, P, I, P, P, S, P, P, P]),
+    "uocr_moe_forward_host": (I, [P, P, I, P, P, S, P, P, P]),
+}
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise LibraryMissing(
+                f"{LIB_PATH} is not built; run `make -C {PKG_DIR}` or __graft_entry__.build()")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def exported_symbols() -> list:
+    return sorted(SIGNATURES)
