@@ -157,7 +157,9 @@ def test_prefill_small(ctx, mode):
     logits[5, 2] += 4.0  # a group of size one for expert 2 is likely
     y, ids, wts = layer.forward(x, logits, mode)
     ref, ids_ref, wts_ref = oracle.experts(sh, ex, logits, x, 3, mode)
-    _check_layer(y, ref, ids, ids_ref, wts, wts_ref, mode != 0)
+    # mode 1 (the reference's dispatch) runs every multi-row group, and the
+    # shared expert, with FP32 activations: FP32 tolerance applies.
+    _check_layer(y, ref, ids, ids_ref, wts, wts_ref, mode == 2)
 
 
 @pytest.mark.slow

@@ -153,7 +153,7 @@ __device__ __forceinline__ int h_base(int unit, int shared_width, int width) {
 }
 
 // ---------------------------------------------------------------------------
-template <int MODE>
+template <int MODE, int CPL>
 __global__ void __launch_bounds__(kUpThreads, 1) moe_up_kernel(const __grid_constant__ MoeDecodeArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int H = a.hidden, nbH = H >> 5;
@@ -164,7 +164,9 @@ __global__ void __launch_bounds__(kUpThreads, 1) moe_up_kernel(const __grid_cons
   int8_t* xq = reinterpret_cast<int8_t*>(xsm + H);
   float* xs = reinterpret_cast<float*>(xq + H);
   float* rp = xs + nbH;                                  // routing scratch [n_experts]
-  int* sel = reinterpret_cast<int*>(rp + a.n_experts);   // [kMaxTopK] route order
+  float* red = rp + a.n_experts;                         // [32]
+  int* bad = reinterpret_cast<int*>(red + 32);           // [1] (+3 pad)
+  int* sel = bad + 4;                                    // [kMaxTopK] route order
   float* selw = reinterpret_cast<float*>(sel + kMaxTopK);
   int* sorted = reinterpret_cast<int*>(selw + kMaxTopK); // [kMaxTopK] ascending id
   float* sortedw = reinterpret_cast<float*>(sorted + kMaxTopK);
@@ -173,6 +175,7 @@ __global__ void __launch_bounds__(kUpThreads, 1) moe_up_kernel(const __grid_cons
   uint64_t* empty = full + kUpStages;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool producer = warp == kUpConsumerWarps && lane == 0;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kUpStages; ++i) {
       mbar_init(&full[i], 1);
@@ -182,59 +185,61 @@ __global__ void __launch_bounds__(kUpThreads, 1) moe_up_kernel(const __grid_cons
   }
   __syncthreads();
 
-  if (warp == kUpConsumerWarps) {
-    // ---------------- producer warp ----------------
-    StageIter itp;
-    itp.init(blockIdx.x, gridDim.x, a.shared_width, a.top_k * a.width, a.width);
-    int it = 0;
-    bool ok = true;
-    auto issue = [&](const StageDesc& d) {
-      const FfnView* f = nullptr;
-      FfnView fv;
-      if (d.unit == 0) {
-        fv = a.shared;
-      } else {
-        fv = a.experts[sorted[d.unit - 1]];
-      }
-      f = &fv;
-      const int stage = it % kUpStages;
-      if (it >= kUpStages) ok = mbar_wait(&empty[stage], ((it / kUpStages) - 1) & 1, a.status);
-      if (!ok) return;
-      unsigned char* dst = ring + stage * stage_bytes;
-      const int wb = d.nr * H, sb = d.nr * nbH * 4;
-      mbar_arrive_expect_tx(&full[stage], 2 * wb + 2 * sb);
-      bulk_g2s(dst, f->gate.w + static_cast<long long>(d.j0) * H, wb, &full[stage]);
-      bulk_g2s(dst + stage_w, f->up.w + static_cast<long long>(d.j0) * H, wb, &full[stage]);
-      bulk_g2s(dst + 2 * stage_w, f->gate.s + static_cast<long long>(d.j0) * nbH, sb, &full[stage]);
-      bulk_g2s(dst + 2 * stage_w + stage_s, f->up.s + static_cast<long long>(d.j0) * nbH, sb,
-               &full[stage]);
-      ++it;
-    };
-    StageDesc d;
-    // 1. shared-expert stages need no routing: start streaming immediately.
-    if (lane == 0)
-      while (ok && it < kUpStages && itp.next_is_shared() && itp.next(d)) issue(d);
-    __syncwarp();
-    // 2. routing (the logits may come from the previous kernel in the stream).
-    pdl_wait_prior_grids();
-    const bool routed = route_row_warp(a.logits, a.n_experts, a.top_k, a.normalize, a.scale, rp,
-                                       sel, selw, a.status);
-    if (lane == 0) {
-      for (int r = 0; r < a.top_k; ++r) {
-        sorted[r] = routed ? sel[r] : r;  // invalid row: keep addresses valid, status flagged
-        sortedw[r] = routed ? selw[r] : 0.0f;
-      }
-      sort_by_id(sorted, sortedw, a.top_k);
-      if (blockIdx.x == 0)
-        for (int r = 0; r < a.top_k; ++r) {
-          a.route_ids[r] = routed ? sel[r] : -1;
-          a.route_weights[r] = routed ? selw[r] : 0.0f;
-        }
+  // Producer state (used by one thread).
+  StageIter itp;
+  itp.init(blockIdx.x, gridDim.x, a.shared_width, a.top_k * a.width, a.width);
+  int it = 0;
+  bool ok = true;
+  auto issue = [&](const StageDesc& d) {
+    const FfnView fv = d.unit == 0 ? a.shared : a.experts[sorted[d.unit - 1]];
+    const int stage = it % kUpStages;
+    if (it >= kUpStages) ok = mbar_wait(&empty[stage], ((it / kUpStages) - 1) & 1, a.status);
+    if (!ok) return;
+    unsigned char* dst = ring + stage * stage_bytes;
+    const int wb = d.nr * H, sb = d.nr * nbH * 4;
+    mbar_arrive_expect_tx(&full[stage], 2 * wb + 2 * sb);
+    bulk_g2s(dst, fv.gate.w + static_cast<long long>(d.j0) * H, wb, &full[stage]);
+    bulk_g2s(dst + stage_w, fv.up.w + static_cast<long long>(d.j0) * H, wb, &full[stage]);
+    bulk_g2s(dst + 2 * stage_w, fv.gate.s + static_cast<long long>(d.j0) * nbH, sb, &full[stage]);
+    bulk_g2s(dst + 2 * stage_w + stage_s, fv.up.s + static_cast<long long>(d.j0) * nbH, sb,
+             &full[stage]);
+    ++it;
+  };
+  StageDesc d;
+  // 1. shared-expert stages need neither routing nor the previous kernel's
+  //    output: start streaming them immediately.
+  if (producer)
+    while (ok && it < kUpStages && itp.next_is_shared() && itp.next(d)) issue(d);
+
+  // 2. x and the router logits may come from the previous kernel.
+  pdl_wait_prior_grids();
+  for (int k = threadIdx.x; k < H; k += blockDim.x) xsm[k] = a.x[k];
+  const bool routed = route_row_block(a.logits, a.n_experts, a.top_k, a.normalize, a.scale, rp,
+                                      red, sel, selw, bad, a.status);
+  if (threadIdx.x == 0) {
+    for (int r = 0; r < a.top_k; ++r) {
+      sorted[r] = routed ? sel[r] : r;  // invalid row: keep addresses valid, status flagged
+      sortedw[r] = routed ? selw[r] : 0.0f;
     }
-    __syncwarp();
-    pdl_launch_dependents();
-    // 3. the rest of the stages
-    if (lane == 0) {
+    sort_by_id(sorted, sortedw, a.top_k);
+    if (blockIdx.x == 0)
+      for (int r = 0; r < a.top_k; ++r) {
+        a.route_ids[r] = routed ? sel[r] : -1;
+        a.route_weights[r] = routed ? selw[r] : 0.0f;
+      }
+  }
+  __syncthreads();
+  // Every prerequisite of this grid is complete: the dependent down kernel
+  // may now launch and read the logits.
+  pdl_launch_dependents();
+  if (MODE == MODE_INT8) {
+    quantize_vec_smem(xsm, H, xq, xs, warp, blockDim.x >> 5, a.status);
+    __syncthreads();
+  }
+
+  if (warp == kUpConsumerWarps) {
+    // 3. the remaining stages
+    if (producer) {
       while (ok && itp.next(d)) issue(d);
       const int issued = it;
       for (int j = issued - kUpStages; j < issued; ++j)
@@ -244,21 +249,16 @@ __global__ void __launch_bounds__(kUpThreads, 1) moe_up_kernel(const __grid_cons
   }
 
   // ---------------- consumer warps ----------------
-  pdl_wait_prior_grids();
-  pdl_launch_dependents();
-  for (int k = threadIdx.x; k < H; k += kUpConsumerWarps * 32) xsm[k] = a.x[k];
-  named_barrier(1, kUpConsumerWarps * 32);
-  if (MODE == MODE_INT8) {
-    quantize_vec_smem(xsm, H, xq, xs, warp, kUpConsumerWarps, a.status);
-    named_barrier(1, kUpConsumerWarps * 32);
-  }
+  // FP32 mode with hidden = 256*CPL: this lane's x chunks live in registers.
+  float4 xr[CPL > 0 ? CPL : 1][4];
+  if constexpr (CPL > 0)
+    if (MODE == MODE_FP32) load_pair_x<CPL>(xsm, H, lane, xr);
   StageIter itc;
   itc.init(blockIdx.x, gridDim.x, a.shared_width, a.top_k * a.width, a.width);
-  StageDesc d;
-  int it = 0;
+  int ct = 0;
   while (itc.next(d)) {
-    const int stage = it % kUpStages;
-    if (!mbar_wait(&full[stage], (it / kUpStages) & 1, a.status)) break;
+    const int stage = ct % kUpStages;
+    if (!mbar_wait(&full[stage], (ct / kUpStages) & 1, a.status)) break;
     const unsigned char* base = ring + stage * stage_bytes;
     const int8_t* gw = reinterpret_cast<const int8_t*>(base);
     const int8_t* uw = reinterpret_cast<const int8_t*>(base + stage_w);
@@ -267,7 +267,10 @@ __global__ void __launch_bounds__(kUpThreads, 1) moe_up_kernel(const __grid_cons
     for (int r = warp; r < d.nr; r += kUpConsumerWarps) {
       float g, u;
       if (MODE == MODE_FP32) {
-        pair_dot_fp32(gw + r * H, gs + r * nbH, uw + r * H, us + r * nbH, xsm, H, lane, g, u);
+        if constexpr (CPL > 0)
+          pair_dot_xregs<CPL>(gw + r * H, gs + r * nbH, uw + r * H, us + r * nbH, H, xr, lane, g, u);
+        else
+          pair_dot_fp32(gw + r * H, gs + r * nbH, uw + r * H, us + r * nbH, xsm, H, lane, g, u);
       } else {
         g = dot_int8_ordered(gw + r * H, gs + r * nbH, xq, xs, H, lane);
         u = dot_int8_ordered(uw + r * H, us + r * nbH, xq, xs, H, lane);
@@ -277,7 +280,7 @@ __global__ void __launch_bounds__(kUpThreads, 1) moe_up_kernel(const __grid_cons
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[stage]);
-    ++it;
+    ++ct;
   }
 }
 
@@ -315,7 +318,7 @@ static DownLayout down_layout(const MoeDecodeArgs& a, int grid) {
   L.out_off = off;
   off += (a.top_k + 1) * L.rows_max * 4;
   L.route_off = off;
-  off += (a.n_experts + 4 * kMaxTopK) * 4;
+  off += (a.n_experts + 36 + 4 * kMaxTopK) * 4;
   off = (off + 15) & ~15;
   L.bar_off = off;
   off += 16;
@@ -338,43 +341,44 @@ __global__ void __launch_bounds__(kDownThreads, 1) moe_down_kernel(const __grid_
   float* hs = reinterpret_cast<float*>(smem + L.hs_off);
   float* outs = reinterpret_cast<float*>(smem + L.out_off);
   float* rp = reinterpret_cast<float*>(smem + L.route_off);
-  int* sel = reinterpret_cast<int*>(rp + a.n_experts);
+  float* red = rp + a.n_experts;
+  int* bad = reinterpret_cast<int*>(red + 32);
+  int* sel = bad + 4;
   float* selw = reinterpret_cast<float*>(sel + kMaxTopK);
   int* sorted = reinterpret_cast<int*>(selw + kMaxTopK);
   float* sortedw = reinterpret_cast<float*>(sorted + kMaxTopK);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar_off);
 
   if (threadIdx.x == 0) {
-    mbar_init(bar, 1);
+    mbar_init(bar, 2);  // one arrival for the shared rows, one for the routed rows
     fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue_unit = [&](int u) {
+    const Q8View& dm = u == 0 ? a.shared.down : a.experts[sorted[u - 1]].down;
+    const int K = dm.cols, nbK = K / 32;
+    bulk_g2s(smem + L.w_off[u], dm.w + static_cast<long long>(i0) * K, nr * K, bar);
+    bulk_g2s(smem + L.s_off[u], dm.s + static_cast<long long>(i0) * nbK, nr * nbK * 4, bar);
+  };
+  // The shared expert's down rows do not depend on routing: fetch them first.
+  if (threadIdx.x == 0 && nr > 0) {
+    mbar_arrive_expect_tx(bar, nr * a.shared_width + nr * (a.shared_width / 32) * 4);
+    issue_unit(0);
   }
   // Routing again (identical arithmetic, so identical result): this CTA
   // needs the selected experts to prefetch their down rows.  The logits were
   // complete before moe_up_kernel triggered this launch.
-  if (warp == 0) {
-    const bool routed = route_row_warp(a.logits, a.n_experts, a.top_k, a.normalize, a.scale, rp,
-                                       sel, selw, nullptr);
-    if (lane == 0) {
-      for (int r = 0; r < a.top_k; ++r) {
-        sorted[r] = routed ? sel[r] : r;
-        sortedw[r] = routed ? selw[r] : 0.0f;
-      }
-      sort_by_id(sorted, sortedw, a.top_k);
+  const bool routed = route_row_block(a.logits, a.n_experts, a.top_k, a.normalize, a.scale, rp,
+                                      red, sel, selw, bad, nullptr);
+  if (threadIdx.x == 0) {
+    for (int r = 0; r < a.top_k; ++r) {
+      sorted[r] = routed ? sel[r] : r;
+      sortedw[r] = routed ? selw[r] : 0.0f;
     }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0 && nr > 0) {
-    int bytes = 0;
-    for (int u = 0; u < units; ++u) {
-      const int K = unit_width(u, a.shared_width, a.width);
-      bytes += nr * K + nr * (K / 32) * 4;
-    }
-    mbar_arrive_expect_tx(bar, bytes);
-    for (int u = 0; u < units; ++u) {
-      const Q8View& dm = u == 0 ? a.shared.down : a.experts[sorted[u - 1]].down;
-      const int K = dm.cols, nbK = K / 32;
-      bulk_g2s(smem + L.w_off[u], dm.w + static_cast<long long>(i0) * K, nr * K, bar);
-      bulk_g2s(smem + L.s_off[u], dm.s + static_cast<long long>(i0) * nbK, nr * nbK * 4, bar);
+    sort_by_id(sorted, sortedw, a.top_k);
+    if (nr > 0) {
+      mbar_arrive_expect_tx(bar, a.top_k * (nr * a.width + nr * (a.width / 32) * 4));
+      for (int u = 1; u < units; ++u) issue_unit(u);
     }
   }
   // h is written by moe_up_kernel.
@@ -398,7 +402,7 @@ __global__ void __launch_bounds__(kDownThreads, 1) moe_down_kernel(const __grid_
       const int hb = h_base(u, a.shared_width, a.width);
       float v;
       if (MODE == MODE_FP32)
-        v = dot_fp32_smem(wrow, srow, hsm + hb, K, lane);
+        v = row_dot_xsmem(wrow, srow, hsm + hb, K, lane);
       else
         v = dot_int8_ordered(wrow, srow, hq + hb, hs + hb / 32, K, lane);
       if (lane == 0) outs[u * L.rows_max + r] = v;
@@ -418,7 +422,7 @@ __global__ void __launch_bounds__(kDownThreads, 1) moe_down_kernel(const __grid_
 static size_t up_smem(const MoeDecodeArgs& a) {
   const int H = a.hidden, nbH = H / 32;
   const size_t stage = 2 * static_cast<size_t>(kUpTileRows) * H + 2 * kUpTileRows * nbH * 4;
-  return kUpStages * stage + H * 4 + H + nbH * 4 + (a.n_experts + 4 * kMaxTopK) * 4 + 16 +
+  return kUpStages * stage + H * 4 + H + nbH * 4 + (a.n_experts + 36 + 4 * kMaxTopK) * 4 + 16 +
          2 * kUpStages * 8 + 16;
 }
 
@@ -441,14 +445,26 @@ cudaError_t launch_moe_decode(int mode, const MoeDecodeArgs& a, int sms, cudaStr
   if (L.total > 200 * 1024) return cudaErrorInvalidConfiguration;
   const size_t us = up_smem(a);
 
+  // Up kernel variants: FP32 with x in registers (hidden = 256*CPL), FP32
+  // generic, int8.
+  const int cpl = (a.hidden % 256 == 0) ? a.hidden / 256 : 0;
+  using UpFn = void (*)(MoeDecodeArgs);
+  UpFn up = mode == MODE_INT8 ? moe_up_kernel<MODE_INT8, 0>
+            : cpl == 4        ? moe_up_kernel<MODE_FP32, 4>
+            : cpl == 5        ? moe_up_kernel<MODE_FP32, 5>
+                              : moe_up_kernel<MODE_FP32, 0>;
+
   static unsigned configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(configured & (1u << (dev & 31)))) {
-    set_smem_attr(reinterpret_cast<const void*>(moe_up_kernel<MODE_FP32>), 200 * 1024);
-    set_smem_attr(reinterpret_cast<const void*>(moe_up_kernel<MODE_INT8>), 200 * 1024);
-    set_smem_attr(reinterpret_cast<const void*>(moe_down_kernel<MODE_FP32>), 200 * 1024);
-    set_smem_attr(reinterpret_cast<const void*>(moe_down_kernel<MODE_INT8>), 200 * 1024);
+    const void* fns[] = {reinterpret_cast<const void*>(moe_up_kernel<MODE_FP32, 0>),
+                         reinterpret_cast<const void*>(moe_up_kernel<MODE_FP32, 4>),
+                         reinterpret_cast<const void*>(moe_up_kernel<MODE_FP32, 5>),
+                         reinterpret_cast<const void*>(moe_up_kernel<MODE_INT8, 0>),
+                         reinterpret_cast<const void*>(moe_down_kernel<MODE_FP32>),
+                         reinterpret_cast<const void*>(moe_down_kernel<MODE_INT8>)};
+    for (const void* f : fns) set_smem_attr(f, 200 * 1024);
     configured |= 1u << (dev & 31);
   }
 
@@ -463,8 +479,7 @@ cudaError_t launch_moe_decode(int mode, const MoeDecodeArgs& a, int sms, cudaStr
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = mode == MODE_FP32 ? cudaLaunchKernelEx(&cfg, moe_up_kernel<MODE_FP32>, a)
-                                    : cudaLaunchKernelEx(&cfg, moe_up_kernel<MODE_INT8>, a);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, up, a);
   if (e != cudaSuccess) return e;
 
   cudaLaunchConfig_t cfg2{};

@@ -147,7 +147,7 @@ __device__ __forceinline__ void quantize_x_smem(const float* xsm, int cols, int8
   }
 }
 
-template <int MODE>
+template <int MODE, int CPL>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const __grid_constant__ GemvTmaParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int cols = p.cols, nb = cols >> 5, TR = p.tile_rows;
@@ -203,6 +203,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const __grid_
   }
 
   // consumers
+  float4 xr[CPL > 0 ? CPL : 1][4];
+  if constexpr (CPL > 0)
+    if (MODE == MODE_FP32) load_pair_x<CPL>(xsm, cols, lane, xr);
   int it = 0;
   for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++it) {
     const int stage = it % kGemvStages;
@@ -213,13 +216,27 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const __grid_
     const int nr = min(TR, p.rows[mi] - r0);
     const int8_t* wt = reinterpret_cast<const int8_t*>(ring + stage * stage_bytes);
     const float* st = reinterpret_cast<const float*>(ring + stage * stage_bytes + w_bytes);
-    for (int r = warp; r < nr; r += kGemvConsumerWarps) {
-      float v;
-      if (MODE == MODE_FP32)
-        v = row_dot_fp32(wt + r * cols, st + r * nb, xsm, cols, lane);
-      else
-        v = row_dot_int8(wt + r * cols, st + r * nb, xq, xs, cols, lane);
-      if (lane == 0) p.y[mi][r0 + r] = v;
+    if (MODE == MODE_FP32 && CPL > 0) {
+      // row pairs (r, r+1); an odd last row pairs with itself
+      for (int r = 2 * warp; r < nr; r += 2 * kGemvConsumerWarps) {
+        const int r1 = r + 1 < nr ? r + 1 : r;
+        float v0, v1;
+        pair_dot_xregs<(CPL > 0 ? CPL : 1)>(wt + r * cols, st + r * nb, wt + r1 * cols,
+                                            st + r1 * nb, cols, xr, lane, v0, v1);
+        if (lane == 0) {
+          p.y[mi][r0 + r] = v0;
+          if (r1 != r) p.y[mi][r0 + r1] = v1;
+        }
+      }
+    } else {
+      for (int r = warp; r < nr; r += kGemvConsumerWarps) {
+        float v;
+        if (MODE == MODE_FP32)
+          v = row_dot_xsmem(wt + r * cols, st + r * nb, xsm, cols, lane);
+        else
+          v = row_dot_int8(wt + r * cols, st + r * nb, xq, xs, cols, lane);
+        if (lane == 0) p.y[mi][r0 + r] = v;
+      }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[stage]);
@@ -237,7 +254,7 @@ static size_t gemv_tma_smem(int cols, int tile_rows) {
   return kGemvStages * stage + cols * 4 + cols + nb * 4 + 16 + 2 * kGemvStages * 8 + 16;
 }
 
-template <int MODE>
+template <int MODE, int CPL>
 static void launch_gemv_tma(const Q8View* mats, int n, const float* x, float* const* ys,
                             unsigned* status, int sms, cudaStream_t st) {
   GemvTmaParams p{};
@@ -270,22 +287,36 @@ static void launch_gemv_tma(const Q8View* mats, int n, const float* x, float* co
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(configured & (1u << (dev & 31)))) {
-    cudaFuncSetAttribute(gemv_tma_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(gemv_tma_kernel<MODE, CPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          210 * 1024);
     configured |= 1u << (dev & 31);
   }
   const int grid = tiles < sms ? tiles : sms;
-  gemv_tma_kernel<MODE><<<grid, kGemvThreads, smem, st>>>(p);
+  gemv_tma_kernel<MODE, CPL><<<grid, kGemvThreads, smem, st>>>(p);
+}
+
+// FP32 variants keep x in registers when cols = 256*CPL (row pairs).
+static void dispatch_gemv_tma(int mode, const Q8View* mats, int n, const float* x,
+                              float* const* ys, unsigned* status, int sms, cudaStream_t st) {
+  const int cols = mats[0].cols;
+  const int cpl = cols % 256 == 0 ? cols / 256 : 0;
+  if (mode == MODE_INT8)
+    launch_gemv_tma<MODE_INT8, 0>(mats, n, x, ys, status, sms, st);
+  else if (cpl == 4)
+    launch_gemv_tma<MODE_FP32, 4>(mats, n, x, ys, status, sms, st);
+  else if (cpl == 5)
+    launch_gemv_tma<MODE_FP32, 5>(mats, n, x, ys, status, sms, st);
+  else if (cpl == 7)
+    launch_gemv_tma<MODE_FP32, 7>(mats, n, x, ys, status, sms, st);
+  else
+    launch_gemv_tma<MODE_FP32, 0>(mats, n, x, ys, status, sms, st);
 }
 
 void launch_gemv_multi(int mode, const Q8View* mats, int n, const float* x, float* const* ys,
                        unsigned* status, int sms, cudaStream_t st) {
   for (int base = 0; base < n; base += kGemvMaxMats) {
     const int cnt = n - base < kGemvMaxMats ? n - base : kGemvMaxMats;
-    if (mode == MODE_FP32)
-      launch_gemv_tma<MODE_FP32>(mats + base, cnt, x, ys + base, status, sms, st);
-    else
-      launch_gemv_tma<MODE_INT8>(mats + base, cnt, x, ys + base, status, sms, st);
+    dispatch_gemv_tma(mode, mats + base, cnt, x, ys + base, status, sms, st);
   }
 }
 
@@ -294,10 +325,7 @@ void launch_gemv(int mode, const Q8View& m, const float* x, long long ld_x, int 
                  cudaStream_t st) {
   if (batch == 1 && gemv_fast_path_ok(m) && reinterpret_cast<uintptr_t>(x) % 16 == 0) {
     float* ys[1] = {y};
-    if (mode == MODE_FP32)
-      launch_gemv_tma<MODE_FP32>(&m, 1, x, ys, status, sms, st);
-    else
-      launch_gemv_tma<MODE_INT8>(&m, 1, x, ys, status, sms, st);
+    dispatch_gemv_tma(mode, &m, 1, x, ys, status, sms, st);
     return;
   }
   long long grid = (static_cast<long long>(m.rows) + 7) / 8;

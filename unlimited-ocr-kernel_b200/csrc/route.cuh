@@ -71,6 +71,72 @@ __device__ __forceinline__ bool route_row_warp(const float* __restrict__ logits,
   return true;
 }
 
+// CTA-wide form of route_row_warp for the decode kernels: thread i owns
+// expert i (n <= blockDim.x), so max, exp, division and the rank count run in
+// parallel; only the sum stays sequential (thread 0, left to right) because
+// its rounding order is part of the result.  Every thread of the block must
+// call it.  Shared scratch: p[n], red[32], ids/wts[top_k], flag[1].
+__device__ __forceinline__ bool route_row_block(const float* __restrict__ logits, int n,
+                                                int top_k, int normalize, float scale, float* p,
+                                                float* red, int* ids, float* wts, int* bad_flag,
+                                                unsigned* status) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nwarps = (blockDim.x + 31) >> 5;
+  if (tid == 0) *bad_flag = 0;
+  const bool mine = tid < n;
+  const float v = mine ? logits[tid] : -INFINITY;
+  const bool bad = mine && (isnan(v) || v == INFINITY);
+  const float wm = warp_max(v);
+  const bool wbad = __any_sync(0xffffffffu, bad);
+  __syncthreads();
+  if (lane == 0) {
+    red[warp] = wm;
+    if (wbad) *bad_flag = 1;
+  }
+  __syncthreads();
+  float mx = -INFINITY;
+  for (int w = 0; w < nwarps; ++w) mx = fmaxf(mx, red[w]);
+  if (*bad_flag || !isfinite(mx)) {
+    if (tid == 0) flag(status, DEV_SOFTMAX);
+    return false;
+  }
+  if (mine) p[tid] = exp_f32_via_f64(__fsub_rn(v, mx));
+  __syncthreads();
+  if (tid == 0) {
+    float s = -0.0f;
+    for (int i = 0; i < n; ++i) s = __fadd_rn(s, p[i]);
+    red[0] = s;
+  }
+  __syncthreads();
+  const float pi = mine ? __fdiv_rn(p[tid], red[0]) : 0.0f;
+  __syncthreads();
+  if (mine) p[tid] = pi;
+  __syncthreads();
+  if (mine) {
+    int rank = 0;
+    for (int j = 0; j < n; ++j) {
+      const float pj = p[j];
+      rank += (pj > pi) || (pj == pi && j < tid);
+    }
+    if (rank < top_k) {
+      ids[rank] = tid;
+      wts[rank] = pi;
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float denominator = 1.0f;
+    if (normalize) {
+      float s = -0.0f;
+      for (int r = 0; r < top_k; ++r) s = __fadd_rn(s, wts[r]);
+      denominator = __fadd_rn(s, 1e-20f);
+    }
+    for (int r = 0; r < top_k; ++r) wts[r] = __fmul_rn(__fdiv_rn(wts[r], denominator), scale);
+  }
+  __syncthreads();
+  return true;
+}
+
 // Sort the top_k (id, weight) pairs by ascending id: the order in which
 // Decoder::experts adds routed outputs (src/decoder/mod.rs:186-194,198-218).
 __device__ __forceinline__ void sort_by_id(int* ids, float* wts, int k) {
