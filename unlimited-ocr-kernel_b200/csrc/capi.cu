@@ -21,40 +21,7 @@
 
 using namespace uocr;
 
-struct uocr_ctx {
-  int device = 0;
-  int sms = 0;
-  size_t scratch_limit = 0;
-  cudaStream_t stream = nullptr;
-  bool own_stream = false;
-  unsigned* status_dev = nullptr;
-  unsigned* status_host = nullptr;  // pinned
-  void* ws = nullptr;
-  size_t ws_bytes = 0;
-  void* pinned = nullptr;
-  size_t pinned_bytes = 0;
-  void* io = nullptr;  // device staging of the *_host MoE entry point
-  size_t io_bytes = 0;
-};
-
-struct uocr_q8 {
-  int device = 0;
-  size_t rows = 0, cols = 0;
-  int8_t* w = nullptr;
-  float* s = nullptr;
-  bool owns = false;
-};
-
-struct uocr_moe {
-  int device = 0;
-  size_t n_experts = 0, top_k = 0;
-  int normalize = 0;
-  float scale = 1.0f;
-  int hidden = 0, width = 0, shared_width = 0;
-  FfnView shared{};
-  FfnView* experts_dev = nullptr;
-  bool aligned = true;
-};
+#include "handles.h"
 
 namespace {
 
@@ -189,6 +156,14 @@ int tensor_len(const size_t* shape, size_t ndim, size_t* len) {
 }
 
 }  // namespace
+
+namespace uocr {
+// Error reporting for entry points defined in other translation units.
+int record_error(int status, const char* message) {
+  g_last_error = message ? message : "";
+  return status;
+}
+}  // namespace uocr
 
 // ===========================================================================
 extern "C" {

@@ -1,0 +1,43 @@
+// handles.h — the opaque handle types of include/uocr_q8.h (library-internal).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "kernels.h"
+
+struct uocr_ctx {
+  int device = 0;
+  int sms = 0;
+  size_t scratch_limit = 0;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  unsigned* status_dev = nullptr;
+  unsigned* status_host = nullptr;  // pinned
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  void* pinned = nullptr;
+  size_t pinned_bytes = 0;
+  void* io = nullptr;  // device staging of the *_host MoE entry point
+  size_t io_bytes = 0;
+};
+
+struct uocr_q8 {
+  int device = 0;
+  size_t rows = 0, cols = 0;
+  int8_t* w = nullptr;
+  float* s = nullptr;
+  bool owns = false;
+};
+
+struct uocr_moe {
+  int device = 0;
+  size_t n_experts = 0, top_k = 0;
+  int normalize = 0;
+  float scale = 1.0f;
+  int hidden = 0, width = 0, shared_width = 0;
+  uocr::FfnView shared{};
+  uocr::FfnView* experts_dev = nullptr;
+  bool aligned = true;
+};
