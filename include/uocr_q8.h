@@ -179,6 +179,24 @@ int uocr_moe_forward_host(uocr_ctx *ctx, const uocr_moe *layer, int mode, const 
                           const float *logits, size_t tokens, float *y, int32_t *ids,
                           float *weights);
 
+/* ---- allocation-free decode ------------------------------------------------
+ * No counterpart in the reference.  For callers that may not allocate device
+ * memory while inference runs (a serving loop that reserves everything at
+ * start-up, a host whose pool allocator owns all device memory): the same
+ * one-token MoE FFN as uocr_moe_forward(tokens = 1), bit-identical results,
+ * but it calls no cudaMalloc/cudaFree.  Its scratch is a fixed array inside
+ * the library (UOCR_NOALLOC_MAX_H floats for h, plus the routing), held by
+ * every GPU that loads the library until the process exits; layers needing
+ * more are rejected with UOCR_ERR_RESOURCE, layers outside the single-token
+ * decode kernels with UOCR_ERR_UNSUPPORTED.  The first call on a device looks
+ * up the array's device address (make it before any stream capture).  All
+ * calls on a device share the array: calls that overlap on the GPU race, so
+ * serialise them.  x_dev hidden floats (16-byte aligned), logits_dev
+ * n_experts floats, y_dev hidden floats; asynchronous on the context stream. */
+#define UOCR_NOALLOC_MAX_H 16384
+int uocr_moe_forward_decode_noalloc(uocr_ctx *ctx, const uocr_moe *layer, int mode,
+                                    const float *x_dev, const float *logits_dev, float *y_dev);
+
 #ifdef __cplusplus
 }
 #endif

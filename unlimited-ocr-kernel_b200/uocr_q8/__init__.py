@@ -310,6 +310,17 @@ class MoeLayer:
                                       t, ctypes.c_void_p(_tptr(y_t)), ip, wp))
         return y_t
 
+    def forward_decode_noalloc(self, x_t, logits_t, mode: int = QuantizationMode.WEIGHTS_ONLY,
+                               y_t=None):
+        """One token through the allocation-free entry point (fixed library
+        scratch; see include/uocr_q8.h).  Asynchronous on the context stream."""
+        import torch
+        y_t = y_t if y_t is not None else torch.empty_like(x_t)
+        _check(lib().uocr_moe_forward_decode_noalloc(
+            self.ctx.handle, self._h, int(mode), ctypes.c_void_p(_tptr(x_t)),
+            ctypes.c_void_p(_tptr(logits_t)), ctypes.c_void_p(_tptr(y_t))))
+        return y_t
+
     def forward_host_ptrs(self, x_ptr: int, logits_ptr: int, tokens: int, y_ptr: int,
                           mode: int = QuantizationMode.WEIGHTS_ONLY) -> None:
         """Raw host-pointer form (pinned buffers), for end-to-end timing."""

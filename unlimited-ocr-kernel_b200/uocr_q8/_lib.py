@@ -54,6 +54,7 @@ SIGNATURES = {
     "uocr_moe_free": (I, [P]),
     "uocr_moe_forward": (I, [P, P, I, P, P, S, P, P, P]),
     "uocr_moe_forward_host": (I, [P, P, I, P, P, S, P, P, P]),
+    "uocr_moe_forward_decode_noalloc": (I, [P, P, I, P, P, P]),
 }
 
 _lib = None
