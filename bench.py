@@ -245,12 +245,12 @@ def run_ours(args):
             "e2e": {"value": round(e2e, 3), "unit": "GB/s", "steps": e2e_steps,
                     "us_per_step": round(e2e_s / e2e_steps * 1e6, 3),
                     "h2d_bytes_per_step": (H + E) * 4, "d2h_bytes_per_step": H * 4},
-            "roofline": {"bound": "hbm", "kernel": "moe_up_kernel+moe_down_kernel (one PDL pair per step)",
+            "roofline": {"bound": "hbm", "kernel": "moe_decode_kernel (one cooperative launch per step)",
                          "achieved": round(STEP_BYTES / (ms_step * 1e-3) / 1e9, 2),
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(STEP_BYTES / (ms_step * 1e-3) / 1e9 / peak, 4),
                          "traffic": args.traffic},
-            "gpu_launches": 2 * steps,
+            "gpu_launches": steps,
             "clocks": clocks.summary(),
         }
         if cpu:

@@ -737,7 +737,7 @@ static int moe_run(uocr_ctx* ctx, const uocr_moe* L, int mode, const float* x, c
     a.hidden = L->hidden;
     a.width = L->width;
     a.shared_width = L->shared_width;
-    if (L->aligned && moe_decode_supported(a) && reinterpret_cast<uintptr_t>(x) % 16 == 0) {
+    if (L->aligned && moe_decode_supported(a, ctx->sms) && reinterpret_cast<uintptr_t>(x) % 16 == 0) {
       const size_t hn = L->shared_width + static_cast<size_t>(k) * L->width;
       const size_t hb = (hn * 4 + 255) & ~static_cast<size_t>(255);
       const bool own_route = !ids || !wts;
@@ -751,6 +751,7 @@ static int moe_run(uocr_ctx* ctx, const uocr_moe* L, int mode, const float* x, c
                                   : wts;
       a.y = y;
       a.status = ctx->status_dev;
+      a.grid_sync = ctx->status_dev + 16;  // zeroed at context creation, decode-only
       cudaError_t e = launch_moe_decode(mode == UOCR_WEIGHTS_ONLY ? MODE_FP32 : MODE_INT8, a,
                                         ctx->sms, ctx->stream);
       if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "moe decode launch: %s", cudaGetErrorString(e));

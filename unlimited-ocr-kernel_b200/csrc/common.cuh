@@ -132,83 +132,70 @@ __device__ __forceinline__ float chunk16_dot(uint4 w, const float4 (&x)[4]) {
   return s.x + s.y;
 }
 
-// Two rows of the same width K (K % 256 == 0) treated as one 2K-byte vector of
-// 16-byte chunks; lane l owns chunks l, l+32, ... (CPL = K/256 of them), so a
-// lane always meets the same x positions and keeps them in registers.
-template <int CPL>
-__device__ __forceinline__ void load_pair_x(const float* xsm, int K, int lane, float4 (&xr)[CPL][4]) {
-  const int per_row = K >> 4;
+// x staged in shared memory in "chunk-transposed" order: float4 q (q = 0..3)
+// of 16-float chunk c is stored at index q*C + c (C = n/16 chunks), so when
+// lane l reads part q of chunk l, consecutive lanes read consecutive 16-byte
+// words (no bank conflicts).  n % 16 == 0.
+__device__ __forceinline__ void stage_x_transposed(float* dst, const float* __restrict__ src, int n,
+                                                   int tid, int nthreads) {
+  const int C = n >> 4;
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+  float4* d4 = reinterpret_cast<float4*>(dst);
+  int i = tid;
+  for (; i + 3 * nthreads < 4 * C; i += 4 * nthreads) {  // 4 loads in flight per thread
+    float4 v[4];
 #pragma unroll
-  for (int j = 0; j < CPL; ++j) {
-    const int c = lane + 32 * j;
-    const int kc = c < per_row ? c : c - per_row;
+    for (int u = 0; u < 4; ++u) v[u] = __ldg(s4 + i + u * nthreads);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) xr[j][q] = *reinterpret_cast<const float4*>(xsm + 16 * kc + 4 * q);
-  }
-}
-
-// FP32-mode dots of two rows sharing x (gate/up rows of one index, or two
-// rows of one matrix).  Returns the warp-reduced sums in o0 / o1.
-template <int CPL>
-__device__ __forceinline__ void pair_dot_xregs(const int8_t* r0, const float* s0, const int8_t* r1,
-                                               const float* s1, int K, const float4 (&xr)[CPL][4],
-                                               int lane, float& o0, float& o1) {
-  const int per_row = K >> 4;
-  float a0 = 0.0f, a1 = 0.0f;
-  uint4 w[CPL];
-  float s[CPL];
-#pragma unroll
-  for (int j = 0; j < CPL; ++j) {
-    const int c = lane + 32 * j;
-    const bool second = c >= per_row;
-    const int kc = second ? c - per_row : c;
-    w[j] = *reinterpret_cast<const uint4*>((second ? r1 : r0) + 16 * kc);
-    s[j] = (second ? s1 : s0)[kc >> 1];
-  }
-#pragma unroll
-  for (int j = 0; j < CPL; ++j) {
-    const int c = lane + 32 * j;
-    const float v = chunk16_dot(w[j], xr[j]);
-    if (c >= per_row)
-      a1 = fmaf(s[j], v, a1);
-    else
-      a0 = fmaf(s[j], v, a0);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    a0 += __shfl_xor_sync(0xffffffffu, a0, o);
-    a1 += __shfl_xor_sync(0xffffffffu, a1, o);
-  }
-  o0 = a0;
-  o1 = a1;
-}
-
-// FP32-mode dot of one row against x in shared memory (any K % 16 == 0).
-__device__ __forceinline__ float row_dot_xsmem(const int8_t* wrow, const float* srow,
-                                               const float* xsm, int K, int lane) {
-  float acc0 = 0.0f, acc1 = 0.0f;
-  const int chunks = K >> 4;
-  int c = lane;
-  for (; c + 32 < chunks; c += 64) {
-    const uint4 wa = *reinterpret_cast<const uint4*>(wrow + 16 * c);
-    const uint4 wb = *reinterpret_cast<const uint4*>(wrow + 16 * (c + 32));
-    float4 xa[4], xb[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      xa[q] = *reinterpret_cast<const float4*>(xsm + 16 * c + 4 * q);
-      xb[q] = *reinterpret_cast<const float4*>(xsm + 16 * (c + 32) + 4 * q);
+    for (int u = 0; u < 4; ++u) {
+      const int k = i + u * nthreads;
+      d4[(k & 3) * C + (k >> 2)] = v[u];
     }
-    acc0 = fmaf(srow[c >> 1], chunk16_dot(wa, xa), acc0);
-    acc1 = fmaf(srow[(c + 32) >> 1], chunk16_dot(wb, xb), acc1);
   }
-  if (c < chunks) {
-    const uint4 wa = *reinterpret_cast<const uint4*>(wrow + 16 * c);
-    float4 xa[4];
+  for (; i < 4 * C; i += nthreads) d4[(i & 3) * C + (i >> 2)] = __ldg(s4 + i);
+}
+
+// FP32-mode dots of 4 rows of width K (K % 16 == 0) against one x vector
+// staged chunk-transposed in shared memory (xT).  Lane l walks the 16-byte
+// weight chunks l, l+32, ...; each x chunk is loaded once and used by all 4
+// rows (4 independent accumulation chains).  The 4 warp sums are formed by a
+// transposed butterfly (6 shuffles instead of 20): afterwards lane l holds the
+// sum of row 2*bit4(l) + bit3(l), i.e. row 0 in lanes 0-7, row 1 in lanes
+// 8-15, row 2 in lanes 16-23, row 3 in lanes 24-31.
+__device__ __forceinline__ float rows4_dot_xsmem(const int8_t* r0, const int8_t* r1,
+                                                 const int8_t* r2, const int8_t* r3,
+                                                 const float* s0, const float* s1,
+                                                 const float* s2, const float* s3,
+                                                 const float* xT, int K, int lane) {
+  float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+  const int chunks = K >> 4;
+  const float4* x4 = reinterpret_cast<const float4*>(xT);
+#pragma unroll 1
+  for (int c = lane; c < chunks; c += 32) {
+    float4 xv[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) xa[q] = *reinterpret_cast<const float4*>(xsm + 16 * c + 4 * q);
-    acc0 = fmaf(srow[c >> 1], chunk16_dot(wa, xa), acc0);
+    for (int q = 0; q < 4; ++q) xv[q] = x4[q * chunks + c];
+    const uint4 w0 = *reinterpret_cast<const uint4*>(r0 + 16 * c);
+    const uint4 w1 = *reinterpret_cast<const uint4*>(r1 + 16 * c);
+    const uint4 w2 = *reinterpret_cast<const uint4*>(r2 + 16 * c);
+    const uint4 w3 = *reinterpret_cast<const uint4*>(r3 + 16 * c);
+    const int b = c >> 1;
+    a0 = fmaf(s0[b], chunk16_dot(w0, xv), a0);
+    a1 = fmaf(s1[b], chunk16_dot(w1, xv), a1);
+    a2 = fmaf(s2[b], chunk16_dot(w2, xv), a2);
+    a3 = fmaf(s3[b], chunk16_dot(w3, xv), a3);
   }
-  return warp_sum(acc0 + acc1);
+  const bool hi16 = lane & 16;
+  float k0 = hi16 ? a2 : a0, k1 = hi16 ? a3 : a1;
+  k0 += __shfl_xor_sync(0xffffffffu, hi16 ? a0 : a2, 16);
+  k1 += __shfl_xor_sync(0xffffffffu, hi16 ? a1 : a3, 16);
+  const bool hi8 = lane & 8;
+  float k = hi8 ? k1 : k0;
+  k += __shfl_xor_sync(0xffffffffu, hi8 ? k0 : k1, 8);
+  k += __shfl_xor_sync(0xffffffffu, k, 4);
+  k += __shfl_xor_sync(0xffffffffu, k, 2);
+  k += __shfl_xor_sync(0xffffffffu, k, 1);
+  return k;
 }
 
 // ---- mbarrier / bulk-copy PTX wrappers --------------------------------------
@@ -252,18 +239,36 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-// Bounded wait on an mbarrier phase: gives up after kWaitLimitNs of wall
-// time (measured on the global nanosecond timer), flags DEV_TIMEOUT and
-// returns false.  Every phase a kernel waits on is completed by its own
-// bulk copies or by its own warps, so the limit is only a safety net.
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+// Wait limits.  Bounds are measured with the SM's cycle counter (clock64 is
+// a cheap register read; the global nanosecond timer is a slow
+// memory-mapped read that would delay every retry).  4e9 cycles is about
+// 2 s at the 1.965 GHz maximum clock and longer at lower clocks.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // for global_ns() users
+constexpr long long kWaitLimitCycles = 4000000000ll;
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes or the hint (ns) expires, instead of spinning.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(100000u)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase: gives up after kWaitLimitCycles, flags
+// DEV_TIMEOUT and returns false.  Every phase a kernel waits on is completed
+// by its own bulk copies or by its own warps, so the limit is a safety net.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* status) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
+  const long long t0 = clock64();
   for (;;) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (global_ns() - t0 > kWaitLimitNs) break;
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    if (clock64() - t0 > kWaitLimitCycles) break;
   }
   flag(status, DEV_TIMEOUT);
   return false;

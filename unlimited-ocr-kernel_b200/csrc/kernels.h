@@ -65,8 +65,9 @@ struct MoeDecodeArgs {
   float* route_weights; // [top_k]
   float* y;             // [hidden]
   unsigned* status;
+  unsigned* grid_sync;  // 4 words, zero before first use, owned by this stream
 };
-bool moe_decode_supported(const MoeDecodeArgs& a);
+bool moe_decode_supported(const MoeDecodeArgs& a, int sms);
 cudaError_t launch_moe_decode(int mode, const MoeDecodeArgs& a, int sms, cudaStream_t st);
 
 // moe_prefill.cu — many tokens: route, group by expert, grouped projections,

@@ -12,12 +12,13 @@
 // exits.
 //
 // Contract:
-//  * runs the same two decode kernels as uocr_moe_forward with tokens == 1, so
+//  * runs the same decode kernel as uocr_moe_forward with tokens == 1, so
 //    results are identical; layers outside the fast decode path are rejected
 //    with UOCR_ERR_UNSUPPORTED;
 //  * the scratch is kNoAllocScratchFloats floats: the intermediate vector h
 //    (shared_width + top_k*width floats, at most UOCR_NOALLOC_MAX_H) plus the
-//    token's routing; larger layers are rejected with UOCR_ERR_RESOURCE;
+//    token's routing, and four words for the kernel's grid barrier; larger
+//    layers are rejected with UOCR_ERR_RESOURCE;
 //  * set-up happens on the first call on each device: with that device
 //    current, the device address of the scratch array is looked up once with
 //    cudaGetSymbolAddress and cached.  That first call may load the library's
@@ -48,24 +49,33 @@ constexpr size_t kRouteSlots = 64;  // ids then weights, top_k <= 8 used
 constexpr size_t kNoAllocScratchFloats = kMaxH + 2 * kRouteSlots;
 
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+// The decode kernel's grid-barrier words (arrival count, generation).  They
+// start at zero when the library is loaded and the barrier leaves the count
+// at zero after every use.
+static __device__ __align__(16) unsigned g_noalloc_sync[4];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 float* g_scratch_ptr[kMaxDevices] = {};
+unsigned* g_sync_ptr[kMaxDevices] = {};
 
 // Set-up, once per device, with that device current.
-int scratch_address(int device, float** out) {
+int scratch_address(int device, float** out, unsigned** sync) {
   if (device < 0 || device >= kMaxDevices)
     return uocr::record_error(UOCR_ERR_UNSUPPORTED, "unsupported configuration: device ordinal");
   std::lock_guard<std::mutex> lock(g_mu);
   if (!g_scratch_ptr[device]) {
     void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || !p)
+    void* q = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e == cudaSuccess) e = cudaGetSymbolAddress(&q, g_noalloc_sync);
+    if (e != cudaSuccess || !p || !q)
       return uocr::record_error(UOCR_ERR_CUDA, cudaGetErrorString(e));
     g_scratch_ptr[device] = static_cast<float*>(p);
+    g_sync_ptr[device] = static_cast<unsigned*>(q);
   }
   *out = g_scratch_ptr[device];
+  *sync = g_sync_ptr[device];
   return UOCR_OK;
 }
 
@@ -112,18 +122,19 @@ extern "C" int uocr_moe_forward_decode_noalloc(uocr_ctx* ctx, const uocr_moe* la
   a.hidden = layer->hidden;
   a.width = layer->width;
   a.shared_width = layer->shared_width;
-  if (!layer->aligned || !moe_decode_supported(a) || reinterpret_cast<uintptr_t>(x_dev) % 16 != 0)
-    return record_error(UOCR_ERR_UNSUPPORTED,
-                        "unsupported configuration: layer outside the single-token decode kernels");
   const size_t hn = static_cast<size_t>(a.shared_width) + static_cast<size_t>(a.top_k) * a.width;
   if (hn > kMaxH)
     return record_error(UOCR_ERR_RESOURCE,
                         "resource limit: layer needs more than the fixed no-allocation scratch "
                         "(UOCR_NOALLOC_MAX_H floats)");
+  if (!layer->aligned || !moe_decode_supported(a, ctx->sms) || reinterpret_cast<uintptr_t>(x_dev) % 16 != 0)
+    return record_error(UOCR_ERR_UNSUPPORTED,
+                        "unsupported configuration: layer outside the single-token decode kernels");
 
   Device guard(ctx->device);
   float* scratch = nullptr;
-  int st = scratch_address(ctx->device, &scratch);
+  unsigned* sync = nullptr;
+  int st = scratch_address(ctx->device, &scratch, &sync);
   if (st) return st;
   a.x = x_dev;
   a.logits = logits_dev;
@@ -132,6 +143,7 @@ extern "C" int uocr_moe_forward_decode_noalloc(uocr_ctx* ctx, const uocr_moe* la
   a.route_weights = scratch + kMaxH + kRouteSlots;
   a.y = y_dev;
   a.status = ctx->status_dev;
+  a.grid_sync = sync;
   const cudaError_t e =
       launch_moe_decode(mode == UOCR_WEIGHTS_ONLY ? MODE_FP32 : MODE_INT8, a, ctx->sms, ctx->stream);
   if (e != cudaSuccess) return record_error(UOCR_ERR_CUDA, cudaGetErrorString(e));

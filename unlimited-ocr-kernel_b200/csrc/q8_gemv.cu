@@ -5,13 +5,14 @@
 //    tiles of one or more matrices that share the input row.  A producer warp
 //    moves each tile (int8 rows + their fp32 block scales, both contiguous in
 //    HBM) into a ring of shared-memory stages with 1-D bulk async copies
-//    completed on mbarriers; eight consumer warps compute from shared memory.
-//    Requires cols % 128 == 0 and 16-byte aligned storage.
+//    completed on mbarriers; sixteen consumer warps (four groups) compute from
+//    shared memory.  Requires cols % 128 == 0 and 16-byte aligned storage.
 //  * gemv_generic_kernel — any shape and any batch; one warp per output row.
 //
-// Lane mapping of the fast path: lane l owns bytes [4l, 4l+4) of every
-// 128-byte window of a row, so a lane's 4 weights always sit inside one
-// 32-column scale block (block = window*4 + l/8).
+// Lane mapping of the fast path: FP32 mode — lane l owns the 16-byte chunks
+// l, l+32, ... of a row (a chunk never straddles a 32-column scale block) and
+// four rows share each x chunk; int8 mode — lane l owns bytes [4l, 4l+4) of
+// every 128-byte window (block = window*4 + l/8).
 //
 // FP32-activation mode (Int8Matrix::linear, src/cpu/quantized.rs:99-149):
 //   y = sum_b s_b * sum_{k in b} w_k x_k, fp32 FMA accumulation, reordered
@@ -73,10 +74,20 @@ __global__ void __launch_bounds__(256) gemv_generic_kernel(Q8View m, const float
 
 // ---------------------------------------------------------------------------
 // fast path
-constexpr int kGemvConsumerWarps = 8;
+// ---------------------------------------------------------------------------
+// fast path
+//
+// 16 consumer warps form 4 groups of 4.  The CTA's i-th tile goes to ring stage
+// i % kGemvStages and is consumed by group i % 4, so each group owns two stages
+// and double-buffers while the other groups work on theirs.  Inside a group,
+// each warp takes 4 rows of the tile at a time (rows4_dot_xsmem).
+constexpr int kGemvGroups = 4;
+constexpr int kGemvWarpsPerGroup = 4;
+constexpr int kGemvConsumerWarps = kGemvGroups * kGemvWarpsPerGroup;
 constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;
-constexpr int kGemvStages = 4;
+constexpr int kGemvStages = 8;
 constexpr int kGemvMaxMats = 16;
+constexpr int kGemvStageBudget = 24 * 1024;  // bytes of one stage (weights + scales)
 
 struct GemvTmaParams {
   const int8_t* w[kGemvMaxMats];
@@ -89,18 +100,6 @@ struct GemvTmaParams {
   unsigned* status;
 };
 
-// Per-warp dot of one smem row (FP32 mode).  xsm: cols floats in smem.
-__device__ __forceinline__ float row_dot_fp32(const int8_t* wrow, const float* srow,
-                                              const float* xsm, int cols, int lane) {
-  float acc = 0.0f;
-#pragma unroll 2
-  for (int k0 = lane * 4; k0 < cols; k0 += 128) {
-    const float4 xv = *reinterpret_cast<const float4*>(xsm + k0);
-    const uint32_t wv = *reinterpret_cast<const uint32_t*>(wrow + k0);
-    acc = fmaf(srow[k0 >> 5], dot4_i8_f32(wv, xv), acc);
-  }
-  return warp_sum(acc);
-}
 
 // Per-warp ordered dot of one smem row (int8 mode).  xq: cols int8 in smem,
 // xs: nb floats in smem.  Every lane returns the same value.
@@ -147,7 +146,8 @@ __device__ __forceinline__ void quantize_x_smem(const float* xsm, int cols, int8
   }
 }
 
-template <int MODE, int CPL>
+
+template <int MODE>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const __grid_constant__ GemvTmaParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int cols = p.cols, nb = cols >> 5, TR = p.tile_rows;
@@ -165,13 +165,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const __grid_
   if (threadIdx.x == 0) {
     for (int i = 0; i < kGemvStages; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kGemvConsumerWarps);
+      mbar_init(&empty[i], kGemvWarpsPerGroup);
     }
     fence_mbar_init();
   }
-  for (int k = threadIdx.x; k < cols; k += blockDim.x) xsm[k] = p.x[k];
-  __syncthreads();
-  if (MODE == MODE_INT8) {
+  if (MODE == MODE_FP32) {
+    stage_x_transposed(xsm, p.x, cols, threadIdx.x, blockDim.x);
+    __syncthreads();
+  } else {
+    for (int k = threadIdx.x; k < cols; k += blockDim.x) xsm[k] = p.x[k];
+    __syncthreads();
     quantize_x_smem(xsm, cols, xq, xs, p.status);
     __syncthreads();
   }
@@ -202,12 +205,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const __grid_
     return;
   }
 
-  // consumers
-  float4 xr[CPL > 0 ? CPL : 1][4];
-  if constexpr (CPL > 0)
-    if (MODE == MODE_FP32) load_pair_x<CPL>(xsm, cols, lane, xr);
-  int it = 0;
-  for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++it) {
+  // consumers: group g takes this CTA's tiles g, g+4, g+8, ...
+  const int group = warp / kGemvWarpsPerGroup, wg = warp % kGemvWarpsPerGroup;
+  for (int it = group, tile = blockIdx.x + group * gridDim.x; tile < p.total_tiles;
+       it += kGemvGroups, tile += kGemvGroups * gridDim.x) {
     const int stage = it % kGemvStages;
     if (!mbar_wait(&full[stage], (it / kGemvStages) & 1, p.status)) break;
     int mi = 0;
@@ -216,26 +217,22 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const __grid_
     const int nr = min(TR, p.rows[mi] - r0);
     const int8_t* wt = reinterpret_cast<const int8_t*>(ring + stage * stage_bytes);
     const float* st = reinterpret_cast<const float*>(ring + stage * stage_bytes + w_bytes);
-    if (MODE == MODE_FP32 && CPL > 0) {
-      // row pairs (r, r+1); an odd last row pairs with itself
-      for (int r = 2 * warp; r < nr; r += 2 * kGemvConsumerWarps) {
-        const int r1 = r + 1 < nr ? r + 1 : r;
-        float v0, v1;
-        pair_dot_xregs<(CPL > 0 ? CPL : 1)>(wt + r * cols, st + r * nb, wt + r1 * cols,
-                                            st + r1 * nb, cols, xr, lane, v0, v1);
-        if (lane == 0) {
-          p.y[mi][r0 + r] = v0;
-          if (r1 != r) p.y[mi][r0 + r1] = v1;
+    float* y = p.y[mi] + r0;
+    for (int r = 4 * wg; r < nr; r += 4 * kGemvWarpsPerGroup) {
+      const int q1 = min(r + 1, nr - 1), q2 = min(r + 2, nr - 1), q3 = min(r + 3, nr - 1);
+      if (MODE == MODE_FP32) {
+        const float v = rows4_dot_xsmem(wt + r * cols, wt + q1 * cols, wt + q2 * cols,
+                                        wt + q3 * cols, st + r * nb, st + q1 * nb, st + q2 * nb,
+                                        st + q3 * nb, xsm, cols, lane);
+        const int j = ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);
+        if ((lane & 7) == 0 && r + j < nr) y[r + j] = v;
+      } else {
+        const int rr[4] = {r, q1, q2, q3};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float v = row_dot_int8(wt + rr[j] * cols, st + rr[j] * nb, xq, xs, cols, lane);
+          if (lane == 0 && r + j < nr) y[r + j] = v;
         }
-      }
-    } else {
-      for (int r = warp; r < nr; r += kGemvConsumerWarps) {
-        float v;
-        if (MODE == MODE_FP32)
-          v = row_dot_xsmem(wt + r * cols, st + r * nb, xsm, cols, lane);
-        else
-          v = row_dot_int8(wt + r * cols, st + r * nb, xq, xs, cols, lane);
-        if (lane == 0) p.y[mi][r0 + r] = v;
       }
     }
     __syncwarp();
@@ -248,23 +245,25 @@ bool gemv_fast_path_ok(const Q8View& m) {
          reinterpret_cast<uintptr_t>(m.s) % 16 == 0;
 }
 
+static int gemv_tile_rows(int cols) {
+  int tr = kGemvStageBudget / (cols + cols / 8);
+  tr = tr > 32 ? 32 : tr;
+  tr &= ~3;
+  return tr < 4 ? 4 : tr;
+}
+
 static size_t gemv_tma_smem(int cols, int tile_rows) {
   const int nb = cols / 32;
   const size_t stage = static_cast<size_t>(tile_rows) * cols + static_cast<size_t>(tile_rows) * nb * 4;
   return kGemvStages * stage + cols * 4 + cols + nb * 4 + 16 + 2 * kGemvStages * 8 + 16;
 }
 
-template <int MODE, int CPL>
+template <int MODE>
 static void launch_gemv_tma(const Q8View* mats, int n, const float* x, float* const* ys,
                             unsigned* status, int sms, cudaStream_t st) {
   GemvTmaParams p{};
   const int cols = mats[0].cols;
-  long long total_rows = 0;
-  for (int i = 0; i < n; ++i) total_rows += mats[i].rows;
-  // ~4 tiles per SM, 4..32 rows per tile
-  int tr = static_cast<int>((total_rows + sms * 4LL - 1) / (sms * 4LL));
-  tr = tr < 4 ? 4 : (tr > 32 ? 32 : tr);
-  while (tr > 4 && gemv_tma_smem(cols, tr) > 200 * 1024) tr -= 4;
+  const int tr = gemv_tile_rows(cols);
   p.n_mats = n;
   p.cols = cols;
   p.tile_rows = tr;
@@ -279,37 +278,27 @@ static void launch_gemv_tma(const Q8View* mats, int n, const float* x, float* co
     p.tile_begin[i] = tiles;
     tiles += (mats[i].rows + tr - 1) / tr;
   }
-  p.tile_begin[n] = tiles;
-  for (int i = n + 1; i <= kGemvMaxMats; ++i) p.tile_begin[i] = tiles;
+  for (int i = n; i <= kGemvMaxMats; ++i) p.tile_begin[i] = tiles;
   p.total_tiles = tiles;
   const size_t smem = gemv_tma_smem(cols, tr);
   static unsigned configured = 0;  // one bit per device ordinal
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(configured & (1u << (dev & 31)))) {
-    cudaFuncSetAttribute(gemv_tma_kernel<MODE, CPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         210 * 1024);
+    cudaFuncSetAttribute(gemv_tma_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         220 * 1024);
     configured |= 1u << (dev & 31);
   }
   const int grid = tiles < sms ? tiles : sms;
-  gemv_tma_kernel<MODE, CPL><<<grid, kGemvThreads, smem, st>>>(p);
+  gemv_tma_kernel<MODE><<<grid, kGemvThreads, smem, st>>>(p);
 }
 
-// FP32 variants keep x in registers when cols = 256*CPL (row pairs).
 static void dispatch_gemv_tma(int mode, const Q8View* mats, int n, const float* x,
                               float* const* ys, unsigned* status, int sms, cudaStream_t st) {
-  const int cols = mats[0].cols;
-  const int cpl = cols % 256 == 0 ? cols / 256 : 0;
   if (mode == MODE_INT8)
-    launch_gemv_tma<MODE_INT8, 0>(mats, n, x, ys, status, sms, st);
-  else if (cpl == 4)
-    launch_gemv_tma<MODE_FP32, 4>(mats, n, x, ys, status, sms, st);
-  else if (cpl == 5)
-    launch_gemv_tma<MODE_FP32, 5>(mats, n, x, ys, status, sms, st);
-  else if (cpl == 7)
-    launch_gemv_tma<MODE_FP32, 7>(mats, n, x, ys, status, sms, st);
+    launch_gemv_tma<MODE_INT8>(mats, n, x, ys, status, sms, st);
   else
-    launch_gemv_tma<MODE_FP32, 0>(mats, n, x, ys, status, sms, st);
+    launch_gemv_tma<MODE_FP32>(mats, n, x, ys, status, sms, st);
 }
 
 void launch_gemv_multi(int mode, const Q8View* mats, int n, const float* x, float* const* ys,

@@ -71,87 +71,101 @@ __device__ __forceinline__ bool route_row_warp(const float* __restrict__ logits,
   return true;
 }
 
-// CTA-wide form of route_row_warp for the decode kernels: thread i owns
-// expert i (n <= blockDim.x), so max, exp, division and the rank count run in
-// parallel; only the sum stays sequential (thread 0, left to right) because
-// its rounding order is part of the result.  Every thread of the block must
-// call it.  Shared scratch: p[n], red[32], ids/wts[top_k], flag[1].
-__device__ __forceinline__ bool route_row_block(const float* __restrict__ logits, int n,
-                                                int top_k, int normalize, float scale, float* p,
-                                                float* red, int* ids, float* wts, int* bad_flag,
-                                                unsigned* status) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nwarps = (blockDim.x + 31) >> 5;
-  if (tid == 0) *bad_flag = 0;
-  const bool mine = tid < n;
-  const float v = mine ? logits[tid] : -INFINITY;
-  const bool bad = mine && (isnan(v) || v == INFINITY);
-  const float wm = warp_max(v);
-  const bool wbad = __any_sync(0xffffffffu, bad);
-  __syncthreads();
-  if (lane == 0) {
-    red[warp] = wm;
-    if (wbad) *bad_flag = 1;
-  }
-  __syncthreads();
-  float mx = -INFINITY;
-  for (int w = 0; w < nwarps; ++w) mx = fmaxf(mx, red[w]);
-  if (*bad_flag || !isfinite(mx)) {
-    if (tid == 0) flag(status, DEV_SOFTMAX);
-    return false;
-  }
-  if (mine) p[tid] = exp_f32_via_f64(__fsub_rn(v, mx));
-  __syncthreads();
-  if (tid == 0) {
-    float s = -0.0f;
-    for (int i = 0; i < n; ++i) s = __fadd_rn(s, p[i]);
-    red[0] = s;
-  }
-  __syncthreads();
-  const float pi = mine ? __fdiv_rn(p[tid], red[0]) : 0.0f;
-  __syncthreads();
-  if (mine) p[tid] = pi;
-  __syncthreads();
-  if (mine) {
-    int rank = 0;
-    for (int j = 0; j < n; ++j) {
-      const float pj = p[j];
-      rank += (pj > pi) || (pj == pi && j < tid);
-    }
-    if (rank < top_k) {
-      ids[rank] = tid;
-      wts[rank] = pi;
-    }
-  }
-  __syncthreads();
-  if (tid == 0) {
-    float denominator = 1.0f;
-    if (normalize) {
-      float s = -0.0f;
-      for (int r = 0; r < top_k; ++r) s = __fadd_rn(s, wts[r]);
-      denominator = __fadd_rn(s, 1e-20f);
-    }
-    for (int r = 0; r < top_k; ++r) wts[r] = __fmul_rn(__fdiv_rn(wts[r], denominator), scale);
-  }
-  __syncthreads();
-  return true;
+// Low-latency single-warp form for up to 64 experts (the decode kernels).
+// Lane l holds experts l and l+32.  Same arithmetic as route_row_warp,
+// arranged around the warp's latency:
+//  * the max is one redux.sync over order-preserving integer keys;
+//  * lane 0 sums the exponentials in index order from vector loads out of
+//    `p` (64 floats of 16-byte-aligned warp-private shared scratch);
+//  * the top_k experts are taken one per round, already in route order: a
+//    redux.sync max over the remaining probabilities (all >= +0, so their bit
+//    patterns order like their values; a taken or absent expert has key 0,
+//    the others bits + 1), then the lowest expert id holding that key from
+//    two ballots (ids 0-31 come before 32-63);
+//  * the renormalisation sum accumulates in the same rank order.
+// Writes ids/wts (route order) and sorted_ids/sorted_wts (ascending id, the
+// order Decoder::experts adds the routed outputs), top_k entries each.
+// Requires top_k <= n <= 64 and top_k <= 32.  Every lane must call it.
+__device__ __forceinline__ int float_order_key(float v) {
+  const int b = __float_as_int(v);
+  return b >= 0 ? b : b ^ 0x7FFFFFFF;
 }
 
-// Sort the top_k (id, weight) pairs by ascending id: the order in which
-// Decoder::experts adds routed outputs (src/decoder/mod.rs:186-194,198-218).
-__device__ __forceinline__ void sort_by_id(int* ids, float* wts, int k) {
-  for (int i = 1; i < k; ++i) {
-    const int id = ids[i];
-    const float w = wts[i];
-    int j = i - 1;
-    while (j >= 0 && ids[j] > id) {
-      ids[j + 1] = ids[j];
-      wts[j + 1] = wts[j];
-      --j;
-    }
-    ids[j + 1] = id;
-    wts[j + 1] = w;
+__device__ __forceinline__ bool route_row_warp64(const float* __restrict__ logits, int n,
+                                                 int top_k, int normalize, float scale, float* p,
+                                                 int* ids, float* wts, int* sorted_ids,
+                                                 float* sorted_wts, unsigned* status) {
+  const int lane = threadIdx.x & 31;
+  const bool in0 = lane < n, in1 = lane + 32 < n;
+  const float v0 = in0 ? logits[lane] : -INFINITY;
+  const float v1 = in1 ? logits[lane + 32] : -INFINITY;
+  const bool bad = __any_sync(0xffffffffu, (in0 && (isnan(v0) || v0 == INFINITY)) ||
+                                               (in1 && (isnan(v1) || v1 == INFINITY)));
+  if (bad) {
+    if (lane == 0) flag(status, DEV_SOFTMAX);
+    return false;
   }
+  const int mk = __reduce_max_sync(0xffffffffu, max(float_order_key(v0), float_order_key(v1)));
+  const float mx = __int_as_float(mk >= 0 ? mk : mk ^ 0x7FFFFFFF);
+  if (!isfinite(mx)) {  // every logit is -inf
+    if (lane == 0) flag(status, DEV_SOFTMAX);
+    return false;
+  }
+  const float e0 = in0 ? exp_f32_via_f64(__fsub_rn(v0, mx)) : 0.0f;
+  const float e1 = in1 ? exp_f32_via_f64(__fsub_rn(v1, mx)) : 0.0f;
+  p[lane] = e0;
+  p[lane + 32] = e1;
+  __syncwarp();
+  float sum = -0.0f;  // left to right over expert ids
+  if (lane == 0) {
+    const float4* p4 = reinterpret_cast<const float4*>(p);
+    float4 t[16];
+#pragma unroll
+    for (int q = 0; q < 16; ++q) t[q] = p4[q];
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      if (4 * q < n) sum = __fadd_rn(sum, t[q].x);
+      if (4 * q + 1 < n) sum = __fadd_rn(sum, t[q].y);
+      if (4 * q + 2 < n) sum = __fadd_rn(sum, t[q].z);
+      if (4 * q + 3 < n) sum = __fadd_rn(sum, t[q].w);
+    }
+  }
+  sum = __shfl_sync(0xffffffffu, sum, 0);
+  unsigned k0 = in0 ? __float_as_uint(__fdiv_rn(e0, sum)) + 1u : 0u;
+  unsigned k1 = in1 ? __float_as_uint(__fdiv_rn(e1, sum)) + 1u : 0u;
+  int my_id = 0;
+  float my_p = 0.0f, kept = -0.0f;
+  for (int r = 0; r < top_k; ++r) {
+    const unsigned m = __reduce_max_sync(0xffffffffu, max(k0, k1));
+    const unsigned b0 = __ballot_sync(0xffffffffu, k0 == m);
+    const unsigned b1 = __ballot_sync(0xffffffffu, k1 == m);
+    const int id = b0 ? __ffs(b0) - 1 : 31 + __ffs(b1);
+    const float pr = __uint_as_float(m - 1u);
+    if (lane == (id & 31)) {
+      if (id < 32) k0 = 0u;
+      else k1 = 0u;
+    }
+    if (lane == r) {
+      my_id = id;
+      my_p = pr;
+    }
+    kept = __fadd_rn(kept, pr);  // rank order, from -0.0
+  }
+  // The selected experts are exactly the present ones whose key is now 0.
+  const unsigned lo = __ballot_sync(0xffffffffu, in0 && k0 == 0u);
+  const unsigned hi = __ballot_sync(0xffffffffu, in1 && k1 == 0u);
+  if (lane < top_k) {
+    const float denominator = normalize ? __fadd_rn(kept, 1e-20f) : 1.0f;
+    const float w = __fmul_rn(__fdiv_rn(my_p, denominator), scale);
+    const unsigned long long sel = (static_cast<unsigned long long>(hi) << 32) | lo;
+    const int pos = __popcll(sel & ((1ull << my_id) - 1ull));
+    ids[lane] = my_id;
+    wts[lane] = w;
+    sorted_ids[pos] = my_id;
+    sorted_wts[pos] = w;
+  }
+  __syncwarp();
+  return true;
 }
 
 }  // namespace uocr
