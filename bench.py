@@ -42,6 +42,11 @@ MAT_BYTES = lambda r, c: r * c + r * ((c + 31) // 32) * 4
 STEP_WEIGHT_BYTES = TOPK * 3 * MAT_BYTES(F, H) + 3 * MAT_BYTES(FS, H)  # 30,965,760
 STEP_BYTES = STEP_WEIGHT_BYTES + H * 4 + E * 4 + H * 4
 METRIC = "q8-block32 expert GEMV GB/s (MoE decode layer, config 1)"
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch, from the
+# ncu captures summarised in profiles/moe_decode_kernel_config1.md and
+# profiles/gemv_tma_kernel_config0.md (16 matrices per GEMV launch).
+DECODE_TRAFFIC = 31_045_632
+GEMV_TRAFFIC = 20_668_928
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_HBM = 6650.0
 
@@ -249,7 +254,7 @@ def run_ours(args):
                          "achieved": round(STEP_BYTES / (ms_step * 1e-3) / 1e9, 2),
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(STEP_BYTES / (ms_step * 1e-3) / 1e9 / peak, 4),
-                         "traffic": args.traffic},
+                         "traffic": args.traffic if args.traffic is not None else DECODE_TRAFFIC},
             "gpu_launches": steps,
             "clocks": clocks.summary(),
         }
@@ -336,7 +341,8 @@ def run_gemv(args):
             "single_call_us": round(single_us, 3),
             "roofline": {"bound": "hbm", "kernel": "gemv_tma_kernel", "achieved": round(gbs, 2),
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                         "frac": round(gbs / peak, 4), "traffic": None},
+                         "frac": round(gbs / peak, 4),
+                         "traffic": args.traffic if args.traffic is not None else GEMV_TRAFFIC},
             "gpu_launches": steps // 16, "clocks": clocks.summary()}
 
 
@@ -425,7 +431,8 @@ def main():
     ap.add_argument("--ref-steps", type=int, default=None)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--traffic", type=float, default=None,
-                    help="dram bytes per step from an ncu capture (reported as roofline.traffic)")
+                    help="dram bytes per launch from an ncu capture (roofline.traffic); "
+                         "defaults to the committed capture of the workload's kernel")
     ap.add_argument("--workload", choices=["moe_decode", "gemv"], default="moe_decode")
     ap.add_argument("--gemv-int8", action="store_true")
     args = ap.parse_args()
