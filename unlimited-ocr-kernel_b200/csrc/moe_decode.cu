@@ -13,7 +13,7 @@
 // copies of (a) the expert descriptor table, (b) this CTA's rows [i0, i1) of
 // the shared expert's down matrix into a dedicated shared-memory region,
 // (c) the first stages of this CTA's slice of the shared expert's gate/up
-// rows into a 4-stage ring.  None of these depend on the token.
+// rows into a ring of up to 6 stages.  None of these depend on the token.
 // Router warp, at the same time: griddepcontrol.wait (the logits may come
 // from the previous kernel), then moe::route (src/decoder/moe.rs:7-30) with
 // the logits in registers; it publishes the selection through shared memory.
@@ -47,7 +47,9 @@ constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kProducerWarp = kConsumerWarps;
 constexpr int kRouterWarp = kConsumerWarps + 1;
 constexpr int kThreads = kConsumerThreads + 64;
-constexpr int kStages = 4;
+constexpr int kMaxStages = 6;  // ring slots: as many as shared memory allows
+constexpr int kMinStages = 4;
+constexpr int kSmemBudget = 220 * 1024;
 constexpr int kTileRows = 8;
 constexpr int kMaxTopK = 8;
 constexpr int kMaxDecodeExperts = 64;
@@ -239,6 +241,7 @@ __host__ __device__ __forceinline__ int piece_blocks(int hn) {
 struct DecodeLayout {
   int rows_max;             // output rows owned by one CTA (max)
   int stage_bytes;          // one ring stage (gate + up rows and scales)
+  int slots;                // ring stages
   int x_off, xq_off, xs_off;
   // Down rows of unit u at w_off(u), their block scales at s_off(u): unit 0
   // (rows_max x shared_width), then the routed units (rows_max x width
@@ -257,12 +260,13 @@ struct DecodeLayout {
 
 static int align16(int v) { return (v + 15) & ~15; }
 
-static DecodeLayout decode_layout(const MoeDecodeArgs& a, int grid) {
+static DecodeLayout decode_layout_with(const MoeDecodeArgs& a, int grid, int slots) {
   DecodeLayout L{};
   const int H = a.hidden, nbH = H / 32;
   L.rows_max = (H + grid - 1) / grid;
   L.stage_bytes = 2 * kTileRows * H + 2 * kTileRows * nbH * 4;
-  int off = kStages * L.stage_bytes;  // ring; phase B stages h (float) here
+  L.slots = slots;
+  int off = slots * L.stage_bytes;  // ring; phase B stages h (float) here
   L.x_off = off;
   off += H * 4;
   L.xq_off = off;
@@ -292,9 +296,16 @@ static DecodeLayout decode_layout(const MoeDecodeArgs& a, int grid) {
   L.desc_off = align16(off);
   off = L.desc_off + a.n_experts * static_cast<int>(sizeof(FfnView));
   L.bar_off = align16(off);
-  off = L.bar_off + (2 * kStages + 3) * 8;
+  off = L.bar_off + (2 * kMaxStages + 3) * 8;
   L.total = align16(off);
   return L;
+}
+
+// The layout with as many ring slots (up to kMaxStages) as the budget allows.
+static DecodeLayout decode_layout(const MoeDecodeArgs& a, int grid) {
+  const DecodeLayout base = decode_layout_with(a, grid, 0);
+  const int room = (kSmemBudget - base.total) / base.stage_bytes;
+  return decode_layout_with(a, grid, room < kMaxStages ? room : kMaxStages);
 }
 
 // Phase-B partial storage: weights-only keeps one float per (piece, row),
@@ -321,6 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const __grid_co
   const int nr = i1 - i0;
   const int units = a.top_k + 1;
   const int hn = a.shared_width + a.top_k * a.width;
+  const int slots = L.slots;
   unsigned char* ring = smem;
   float* xsm = reinterpret_cast<float*>(smem + L.x_off);
   int8_t* xq = reinterpret_cast<int8_t*>(smem + L.xq_off);
@@ -337,14 +349,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const __grid_co
   float* sortedw = reinterpret_cast<float*>(sorted + kMaxTopK);
   FfnView* edesc = reinterpret_cast<FfnView*>(smem + L.desc_off);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
-  uint64_t* empty = full + kStages;
-  uint64_t* down_bar = empty + kStages;  // down rows landed (2 arrivals)
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* down_bar = empty + kMaxStages;  // down rows landed (2 arrivals)
   uint64_t* desc_bar = down_bar + 1;     // descriptor table landed
   uint64_t* route_bar = desc_bar + 1;    // routing result in shared memory
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < slots; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], kWarpsPerGroup);
     }
@@ -383,8 +395,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const __grid_co
     bool ok = true;
     auto issue = [&](const StageDesc& sd) {
       const FfnView fv = sd.unit == 0 ? a.shared : edesc[sorted[sd.unit - 1]];
-      const int stage = it % kStages;
-      if (it >= kStages) ok = mbar_wait(&empty[stage], ((it / kStages) - 1) & 1, a.status);
+      const int stage = it % slots;
+      if (it >= slots) ok = mbar_wait(&empty[stage], ((it / slots) - 1) & 1, a.status);
       if (!ok) return;
       unsigned char* dst = ring + stage * L.stage_bytes;
       const int wb = sd.nr * H, sb = sd.nr * nbH * 4;
@@ -406,19 +418,19 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const __grid_co
     const int desc_bytes = a.n_experts * static_cast<int>(sizeof(FfnView));
     mbar_arrive_expect_tx(desc_bar, desc_bytes);
     bulk_g2s(edesc, a.experts, desc_bytes, desc_bar);
-    while (ok && it < kStages && itp.next_is_shared() && itp.next(d)) issue(d);
+    while (ok && it < slots && itp.next_is_shared() && itp.next(d)) issue(d);
     mbar_arrive_expect_tx(down_bar, nr * a.shared_width + nr * (a.shared_width / 32) * 4);
     if (nr > 0) issue_down(a.shared.down, 0);
     // Then the selected experts: free ring slots, their down rows, the rest.
     ok = mbar_wait(route_bar, 0, a.status) && mbar_wait(desc_bar, 0, a.status);
-    while (ok && it < kStages && itp.next(d)) issue(d);
+    while (ok && it < slots && itp.next(d)) issue(d);
     mbar_arrive_expect_tx(down_bar, a.top_k * (nr * a.width + nr * (a.width / 32) * 4));
     if (ok && nr > 0)
       for (int u = 1; u < units; ++u) issue_down(edesc[sorted[u - 1]].down, u);
     while (ok && itp.next(d)) issue(d);
     const int issued = it;
-    for (int j = issued - kStages; j < issued; ++j)
-      if (j >= 0) mbar_wait(&full[j % kStages], (j / kStages) & 1, a.status);
+    for (int j = issued - slots; j < issued; ++j)
+      if (j >= 0) mbar_wait(&full[j % slots], (j / slots) & 1, a.status);
     return;
   }
 
@@ -444,8 +456,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const __grid_co
     itc.init(blockIdx.x, gridDim.x, a.shared_width, a.top_k * a.width, a.width);
     for (int ct = 0; itc.next(d); ++ct) {
       if (ct % kGroups != group) continue;
-      const int stage = ct % kStages;
-      if (!mbar_wait(&full[stage], (ct / kStages) & 1, a.status)) break;
+      const int stage = ct % slots;
+      if (!mbar_wait(&full[stage], (ct / slots) & 1, a.status)) break;
       const unsigned char* base = ring + stage * L.stage_bytes;
       const int8_t* gw = reinterpret_cast<const int8_t*>(base);
       const int8_t* uw = reinterpret_cast<const int8_t*>(base + stage_w);
@@ -618,7 +630,8 @@ bool moe_decode_supported(const MoeDecodeArgs& a, int sms) {
   if (grid < 1) return false;
   const DecodeLayout L = decode_layout(a, grid);
   // shared memory, and h plus the phase-B partials inside the idle ring
-  return L.total <= 220 * 1024 && L.part_off + part_bytes(a, L.rows_max) <= kStages * L.stage_bytes;
+  return L.slots >= kMinStages && L.total <= kSmemBudget &&
+         L.part_off + part_bytes(a, L.rows_max) <= L.slots * L.stage_bytes;
 }
 
 cudaError_t launch_moe_decode(int mode, const MoeDecodeArgs& a, int sms, cudaStream_t st) {
@@ -642,9 +655,9 @@ cudaError_t launch_moe_decode(int mode, const MoeDecodeArgs& a, int sms, cudaStr
   cudaGetDevice(&dev);
   if (!(configured & (1u << (dev & 31)))) {
     cudaFuncSetAttribute(moe_decode_kernel<MODE_FP32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         220 * 1024);
+                         kSmemBudget);
     cudaFuncSetAttribute(moe_decode_kernel<MODE_INT8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         220 * 1024);
+                         kSmemBudget);
     configured |= 1u << (dev & 31);
   }
   // Cooperative: all CTAs co-resident (the grid barrier needs it).  PDL: the
