@@ -418,6 +418,182 @@ def run_reference(args):
                     "d2h_bytes_per_step": 0}}
 
 
+PREFILL_TOKENS = 1024
+# config 2 algorithmic work: 6144 (token, expert) pairs x 3 projections of [896x1280]
+# plus 1024 tokens through the shared expert's 3 projections of [1792x1280]
+PREFILL_OPS = PREFILL_TOKENS * TOPK * 3 * 2 * F * H + PREFILL_TOKENS * 3 * 2 * FS * H
+PREFILL_WEIGHT_BYTES = E * 3 * MAT_BYTES(F, H) + 3 * MAT_BYTES(FS, H)  # 255,467,520
+
+
+def peak_tensor():
+    try:
+        with open(PEAKS_PATH) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def zipf_logits(gen, tokens, experts, s=1.1):
+    """Router logits with a Zipf(s) popularity bias over a random expert order
+    plus N(0,1) noise (the config-2 stand-in for a real prefill)."""
+    import torch
+    order = torch.randperm(experts, generator=gen, device=gen.device)
+    bias = torch.empty(experts, device=gen.device)
+    bias[order] = -s * torch.log(torch.arange(1, experts + 1, device=gen.device, dtype=torch.float32))
+    return (torch.randn((tokens, experts), device=gen.device, generator=gen) + bias).contiguous()
+
+
+def run_prefill(args):
+    """Config 2: grouped prefill through one MoE layer, 1024 tokens, top-6 of
+    64 experts with a Zipf(1.1) router bias, one mode per run (--prefill-mode
+    0 = weights-only fp32 activations, 2 = int8 activations for every row)."""
+    import torch
+
+    import uocr_q8
+    dev = "cuda:0"
+    torch.cuda.set_device(0)
+    ctx = uocr_q8.GpuContext(0)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream)
+    layer = build_layers(ctx, 1, dev, 4321)[0]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7)
+    T = PREFILL_TOKENS
+    x = torch.randn((T, H), device=dev, generator=gen)
+    lg = zipf_logits(gen, T, E)
+    y = torch.empty((T, H), device=dev)
+    mode = args.prefill_mode
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            layer.forward_device(x, lg, mode, y)
+    ctx.sync()
+    steps = max(1, args.steps)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(steps):
+                layer.forward_device(x, lg, mode, y)
+            stop.record(stream)
+        stop.synchronize()
+    ms = start.elapsed_time(stop) / steps
+    ctx.sync()
+    # end to end: pinned host x/logits in, y out, one synchronous call per step
+    hx = torch.empty((T, H), pin_memory=True)
+    hl = torch.empty((T, E), pin_memory=True)
+    hy = torch.empty((T, H), pin_memory=True)
+    hx.copy_(x.cpu())
+    hl.copy_(lg.cpu())
+    layer.forward_host_ptrs(hx.data_ptr(), hl.data_ptr(), T, hy.data_ptr(), mode)
+    e2e_n = max(1, min(steps, 10))
+    t0 = time.perf_counter()
+    for _ in range(e2e_n):
+        layer.forward_host_ptrs(hx.data_ptr(), hl.data_ptr(), T, hy.data_ptr(), mode)
+    e2e_s = (time.perf_counter() - t0) / e2e_n
+    tops = PREFILL_OPS / (ms * 1e-3) / 1e12
+    peak_t, kind_t = peak_tensor()
+    hbm, kind_h = peak_hbm()
+    attainable = min(peak_t, PREFILL_OPS / PREFILL_WEIGHT_BYTES * hbm / 1e3)  # TFLOP/s
+    return {"metric": "q8-block32 grouped prefill TOP/s (MoE layer, config 2)",
+            "value": round(tops, 3), "unit": "TOP/s", "n_gpus": 1, "steps": steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8-act" if mode else "fp32",
+            "data": "synthetic (seeded; x ~ N(0,1), Zipf(1.1)-biased router logits)",
+            "config": {"workload": "config2_grouped_prefill", "tokens": T, "experts": E,
+                       "top_k": TOPK, "hidden": H, "expert_width": F, "shared_width": FS,
+                       "mode": "weights_only (fp32 activations)" if mode == 0 else
+                               "dynamic int8 activations, every row",
+                       "ops_per_step": PREFILL_OPS, "weight_bytes": PREFILL_WEIGHT_BYTES,
+                       "l2": "one layer = 255.5 MB of weights (> 126 MB L2)"},
+            "e2e": {"value": round(PREFILL_OPS / e2e_s / 1e12, 3), "unit": "TOP/s",
+                    "steps": e2e_n, "ms_per_step": round(e2e_s * 1e3, 3),
+                    "h2d_bytes_per_step": T * (H + E) * 4, "d2h_bytes_per_step": T * H * 4},
+            "roofline": {"bound": "tensor", "kernel": "grouped_cc_kernel (CUDA cores)",
+                         "achieved": round(tops, 3), "peak": round(attainable, 1),
+                         "peak_kind": f"min(bf16 dense {kind_t}, AI x HBM {kind_h})",
+                         "unit": "TFLOP/s", "frac": round(tops / attainable, 5), "traffic": None},
+            "gpu_launches": steps * 7, "clocks": clocks.summary()}
+
+
+def run_int8suite(args):
+    """Config 3: linear_dynamic_int8 (row-wise, bit-exact) for M in
+    {1,16,128,512} x N in {896,1280,3840}, K = 1280; a pool of distinct
+    matrices per shape keeps the weights coming from HBM."""
+    import torch
+
+    import uocr_q8
+    dev = "cuda:0"
+    torch.cuda.set_device(0)
+    ctx = uocr_q8.GpuContext(0)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream)
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    K = H
+    cases = []
+    total_ops = 0.0
+    total_s = 0.0
+    with ClockSampler(0) as clocks:
+        for N in (896, 1280, 3840):
+            pool = max(2, (400 << 20) // MAT_BYTES(N, K))
+            mats = []
+            for _ in range(pool):
+                w = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=g)
+                sc = (torch.rand((N, K // 32), device=dev, generator=g) * (1e-2 - 1e-4) + 1e-4)
+                mats.append(uocr_q8.Int8Matrix.from_device(N, K, w, sc.contiguous(), ctx))
+            for M in (1, 16, 128, 512):
+                x = (torch.randn((M, K), device=dev, generator=g) *
+                     (torch.rand((M, 1), device=dev, generator=g) * 9.9 + 0.1)).contiguous()
+                y = torch.empty((M, N), device=dev)
+                # one call per matrix of the pool, captured once and replayed:
+                # device time without the host's per-call cost
+                with torch.cuda.stream(stream):
+                    for i in range(pool):
+                        mats[i].linear_device(x, y, dynamic=True)
+                ctx.sync()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    for i in range(pool):
+                        mats[i].linear_device(x, y, dynamic=True)
+                replays = max(1, 2048 // pool)
+                for _ in range(3):
+                    graph.replay()
+                torch.cuda.synchronize()
+                t0 = torch.cuda.Event(enable_timing=True)
+                t1 = torch.cuda.Event(enable_timing=True)
+                with torch.cuda.stream(stream):
+                    t0.record(stream)
+                    for _ in range(replays):
+                        graph.replay()
+                    t1.record(stream)
+                t1.synchronize()
+                reps = replays * pool
+                us = t0.elapsed_time(t1) * 1e3 / reps
+                del graph
+                ops = 2.0 * M * N * K
+                byts = MAT_BYTES(N, K) + M * K * 4 + M * N * 4
+                cases.append({"M": M, "N": N, "K": K, "us": round(us, 3),
+                              "TOP/s": round(ops / (us * 1e-6) / 1e12, 3),
+                              "GB/s": round(byts / (us * 1e-6) / 1e9, 1)})
+                total_ops += ops
+                total_s += us * 1e-6
+            del mats
+            ctx.sync()
+    ctx.sync()
+    agg = total_ops / total_s / 1e12
+    return {"metric": "q8-block32 linear_dynamic_int8 micro-suite TOP/s (config 3)",
+            "value": round(agg, 3), "unit": "TOP/s", "n_gpus": 1, "steps": len(cases),
+            "warmup": 3, "ms_per_step": round(total_s * 1e3 / len(cases), 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8-act",
+            "data": "synthetic (seeded; rows ~ N(0,1) * U(0.1,10))",
+            "config": {"workload": "config3_int8_micro_suite", "K": K,
+                       "aggregate": "total ops / total time over the 12 cases",
+                       "timing": "CUDA graph of one call per pool matrix, replayed; "
+                                 "pool > 400 MB so weights come from HBM"},
+            "cases": cases, "clocks": clocks.summary()}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -433,11 +609,19 @@ def main():
     ap.add_argument("--traffic", type=float, default=None,
                     help="dram bytes per launch from an ncu capture (roofline.traffic); "
                          "defaults to the committed capture of the workload's kernel")
-    ap.add_argument("--workload", choices=["moe_decode", "gemv"], default="moe_decode")
+    ap.add_argument("--workload", choices=["moe_decode", "gemv", "prefill", "int8suite"],
+                    default="moe_decode")
     ap.add_argument("--gemv-int8", action="store_true")
+    ap.add_argument("--prefill-mode", type=int, choices=[0, 2], default=0)
     args = ap.parse_args()
     if args.workload == "gemv" and args.impl == "ours":
         print(json.dumps(run_gemv(args)), flush=True)
+        return
+    if args.workload == "prefill" and args.impl == "ours":
+        print(json.dumps(run_prefill(args)), flush=True)
+        return
+    if args.workload == "int8suite" and args.impl == "ours":
+        print(json.dumps(run_int8suite(args)), flush=True)
         return
     if args.impl == "reference":
         if args.ref_steps is None:

@@ -165,6 +165,21 @@ def test_prefill_small(ctx, mode):
     _check_layer(y, ref, ids, ids_ref, wts, wts_ref, mode == 2)
 
 
+@pytest.mark.parametrize("T", [2, 65, 150])
+def test_prefill_tensor_core_int8(ctx, T):
+    """Int8 activations for every row on shapes the tensor-core path takes
+    (every dimension a multiple of 128): gathered rows per expert, grouped
+    projections, ragged groups and tiles."""
+    rng = np.random.default_rng(900 + T)
+    layer, sh, ex = make_layer(ctx, rng, 256, 128, 256, 8, 2)
+    x = rng.standard_normal((T, 256)).astype(np.float32)
+    logits = rng.standard_normal((T, 8)).astype(np.float32)
+    logits[:, 5] += 1.5  # one popular expert: a group of several tiles
+    y, ids, wts = layer.forward(x, logits, 2)
+    ref, ids_ref, wts_ref = oracle.experts(sh, ex, logits, x, 2, 2)
+    _check_layer(y, ref, ids, ids_ref, wts, wts_ref, True)
+
+
 @pytest.mark.slow
 @pytest.mark.parametrize("mode", [0, 2])
 def test_prefill_config2_shape(ctx, config1, mode):

@@ -460,10 +460,26 @@ static int run_linear(uocr_ctx* ctx, const uocr_q8* m, int mode, const float* x_
   float* xs = nullptr;
   if (mode == MODE_INT8) {
     const size_t qbytes = (batch * m->cols + 255) & ~static_cast<size_t>(255);
-    int st = ensure_ws(ctx, qbytes + batch * nblocks(m->cols) * 4);
+    const size_t sbytes = (batch * nblocks(m->cols) * 4 + 255) & ~static_cast<size_t>(255);
+    const bool tc = batch > 1 &&
+                    q8_tc_supported(static_cast<int>(m->rows), static_cast<int>(m->cols)) &&
+                    reinterpret_cast<uintptr_t>(m->w) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(m->s) % 16 == 0;
+    int st = ensure_ws(ctx, qbytes + sbytes);
     if (st) return st;
     xq = static_cast<int8_t*>(ctx->ws);
     xs = reinterpret_cast<float*>(static_cast<char*>(ctx->ws) + qbytes);
+    if (tc) {
+      // many rows: quantize them, then the tensor-core GEMM (bit-exact)
+      const int b = static_cast<int>(batch);
+      launch_quantize_rows(x_dev, static_cast<long long>(m->cols), b, static_cast<int>(m->cols), xq,
+                           xs, ctx->status_dev, ctx->sms, ctx->stream);
+      const cudaError_t e = launch_q8_tc_single_i8(view(m), xq, xs, b, y_dev,
+                                                   static_cast<long long>(m->rows),
+                                                   ctx->status_dev, ctx->stream);
+      if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "tensor-core linear: %s", cudaGetErrorString(e));
+      return check_launch();
+    }
   }
   launch_gemv(mode, view(m), x_dev, static_cast<long long>(m->cols), static_cast<int>(batch), y_dev,
               static_cast<long long>(m->rows), xq, xs, ctx->status_dev, ctx->sms, ctx->stream);
@@ -695,6 +711,24 @@ int uocr_moe_create(uocr_ctx* ctx, const uocr_q8* shared_gate, const uocr_q8* sh
     uocr_moe_free(L);
     return fail(UOCR_ERR_CUDA, "moe_create: %s", cudaGetErrorString(e));
   }
+  // TMA maps for the tensor-core prefill, when every matrix qualifies
+  if (aligned && q8_tc_supported(static_cast<int>(F), static_cast<int>(H)) &&
+      q8_tc_supported(static_cast<int>(H), static_cast<int>(F))) {
+    const size_t mb = q8_tc_maps_bytes();
+    std::vector<unsigned char> maps(3 * n_experts * mb);
+    bool made = true;
+    for (size_t i = 0; i < n_experts && made; ++i) {
+      const Q8View m3[3] = {views[i].gate, views[i].up, views[i].down};
+      for (int j = 0; j < 3 && made; ++j)
+        made = q8_tc_weight_maps(maps.data() + (j * n_experts + i) * mb, m3[j]);
+    }
+    if (!made || cudaMalloc(&L->tc_maps, maps.size()) != cudaSuccess ||
+        cudaMemcpy(L->tc_maps, maps.data(), maps.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+      cudaGetLastError();
+      if (L->tc_maps) cudaFree(L->tc_maps);
+      L->tc_maps = nullptr;
+    }
+  }
   *out = L;
   return ok();
 }
@@ -703,6 +737,7 @@ int uocr_moe_free(uocr_moe* layer) {
   if (!layer) return ok();
   DeviceGuard g(layer->device);
   if (layer->experts_dev) cudaFree(layer->experts_dev);
+  if (layer->tc_maps) cudaFree(layer->tc_maps);
   delete layer;
   return ok();
 }
@@ -773,6 +808,7 @@ static int moe_run(uocr_ctx* ctx, const uocr_moe* L, int mode, const float* x, c
   a.logits = logits;
   a.y = y;
   a.status = ctx->status_dev;
+  a.tc_maps = L->tc_maps;
   const size_t rb = (tokens * k * 4 + 255) & ~static_cast<size_t>(255);
   const bool own_route = !ids || !wts;
   const size_t need = moe_prefill_workspace(a, mode) + (own_route ? 2 * rb : 0) + 256;

@@ -274,6 +274,32 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   return false;
 }
 
+// Latency-critical bounded wait: polls with test_wait (never suspends the
+// thread), for hand-offs where a suspended waiter would wake late.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, unsigned* status) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_test_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitLimitCycles) {
+      flag(status, DEV_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
 // 1-D bulk copy global -> shared, completion signalled on `bar` as tx bytes.
 // Both addresses 16-byte aligned, bytes a multiple of 16 (checked by callers).
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,

@@ -40,4 +40,8 @@ struct uocr_moe {
   uocr::FfnView shared{};
   uocr::FfnView* experts_dev = nullptr;
   bool aligned = true;
+  // Tensor-core prefill: TMA maps of every routed expert's weights and
+  // scales, [3][n_experts] (gate, up, down); null when a shape does not
+  // qualify.
+  void* tc_maps = nullptr;
 };

@@ -45,6 +45,28 @@ void launch_gemv_multi(int mode, const Q8View* mats, int n, const float* x, floa
                        unsigned* status, int sms, cudaStream_t st);
 bool gemv_fast_path_ok(const Q8View& m);
 
+// q8_tc.cu — linear_dynamic_int8 for many rows on the tensor cores
+// (bit-exact).  Activations are block-quantized rows (launch_quantize_rows):
+// xq [rows][cols] int8, xs [rows][cols/32].  Weights: rows % 128 == 0,
+// cols % 128 == 0, both arrays 16-byte aligned.
+bool q8_tc_supported(int rows, int cols);
+size_t q8_tc_maps_bytes();                          // two TMA maps per matrix
+bool q8_tc_weight_maps(void* maps, const Q8View& m);  // m's weight and scale maps
+cudaError_t launch_q8_tc_single_i8(const Q8View& m, const int8_t* xq, const float* xs, int batch,
+                                   float* y, long long ldy, unsigned* status, cudaStream_t st);
+// Group g: rows [offsets[g], offsets[g] + counts[g]) of xq/xs times the
+// matrix whose q8_tc_weight_maps are maps[g] (device array, 64-byte aligned).
+cudaError_t launch_q8_tc_grouped_i8(const void* maps, int groups, const int* counts,
+                                    const int* offsets, int max_tiles, int N, int K,
+                                    const int8_t* xq, const float* xs, int total_rows, float* y,
+                                    long long ldy, unsigned* status, cudaStream_t st);
+// xq_p[p] = xq[src[p]], xs_p[p] = xs[src[p]]
+void launch_gather_rows(const int8_t* xq, const float* xs, const int* src, int rows, int cols,
+                        int8_t* xq_p, float* xs_p, int sms, cudaStream_t st);
+// hq/hs = block-quantized silu(g) * u
+void launch_swiglu_quantize(const float* g, const float* u, int rows, int cols, int8_t* hq,
+                            float* hs, unsigned* status, int sms, cudaStream_t st);
+
 // moe_route.cu — moe::route for `tokens` rows of logits.  ids/weights are
 // tokens*top_k in the reference's order (probability desc, id asc).
 void launch_route(const float* logits, int tokens, int n_experts, int top_k, int normalize,
@@ -86,6 +108,9 @@ struct MoePrefillArgs {
   void* workspace;
   size_t workspace_bytes;
   unsigned* status;
+  // tensor-core int8 path (optional): [3][n_experts] q8_tc_weight_maps
+  // (gate, up, down) in device memory
+  const void* tc_maps;
 };
 size_t moe_prefill_workspace(const MoePrefillArgs& a, int mode);
 cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaStream_t st);

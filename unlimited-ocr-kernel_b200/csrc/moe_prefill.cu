@@ -14,8 +14,9 @@
 //   mode DYNAMIC_ROWWISE     -> int8 activations for every row (extension).
 //
 // This file holds the grouping, combine and a CUDA-core grouped projection
-// kernel that serves every shape; the tensor-core grouped GEMM in
-// moe_grouped_tc.cu takes the groups it supports.
+// kernel that serves every shape.  In int8 mode for every row, layers whose
+// shapes qualify run every projection on the tensor cores instead
+// (q8_tc.cu): rows gathered per expert, one grouped launch per projection.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -324,10 +325,21 @@ struct PrefillWs {
   int8_t* hq_s;
   float* hs_s;
   float* out_r;
+  // tensor-core int8 path
+  float* u_r;
+  float* u_s;
+  int8_t* xq_p;
+  float* xs_p;
   size_t bytes;
 };
 
-static PrefillWs carve(const MoePrefillArgs& a, void* base) {
+static bool use_tc(const MoePrefillArgs& a, int mode) {
+  return mode == 2 && a.tc_maps &&
+         q8_tc_supported(a.shared_width, a.hidden) && q8_tc_supported(a.hidden, a.shared_width) &&
+         q8_tc_supported(a.width, a.hidden) && q8_tc_supported(a.hidden, a.width);
+}
+
+static PrefillWs carve(const MoePrefillArgs& a, void* base, bool tc) {
   PrefillWs w{};
   const size_t T = a.tokens, P = static_cast<size_t>(a.tokens) * a.top_k;
   const size_t H = a.hidden, F = a.width, FS = a.shared_width;
@@ -351,18 +363,51 @@ static PrefillWs carve(const MoePrefillArgs& a, void* base) {
   w.hq_s = reinterpret_cast<int8_t*>(take(T * FS));
   w.hs_s = reinterpret_cast<float*>(take(sizeof(float) * T * blocks_of(a.shared_width)));
   w.out_r = reinterpret_cast<float*>(take(sizeof(float) * P * H));
+  if (tc) {
+    w.u_r = reinterpret_cast<float*>(take(sizeof(float) * P * F));
+    w.u_s = reinterpret_cast<float*>(take(sizeof(float) * T * FS));
+    w.xq_p = reinterpret_cast<int8_t*>(take(P * H));
+    w.xs_p = reinterpret_cast<float*>(take(sizeof(float) * P * blocks_of(a.hidden)));
+  }
   w.bytes = off;
   return w;
 }
 
 size_t moe_prefill_workspace(const MoePrefillArgs& a, int mode) {
-  (void)mode;
-  return carve(a, nullptr).bytes;
+  return carve(a, nullptr, use_tc(a, mode)).bytes;
+}
+
+// Int8 activations for every row, all projections on the tensor cores.
+static cudaError_t prefill_tc(const MoePrefillArgs& a, const PrefillWs& w, int sms, cudaStream_t st) {
+  const int T = a.tokens, k = a.top_k, E = a.n_experts, P = T * k;
+  const int H = a.hidden, F = a.width, FS = a.shared_width;
+  const int max_tiles = P / 64 + E + 1;  // sum over experts of ceil(count / 64)
+  const unsigned char* maps = static_cast<const unsigned char*>(a.tc_maps);
+  const size_t mb = q8_tc_maps_bytes();  // per matrix
+  cudaError_t e;
+  // routed experts: rows gathered per expert, gate and up, SwiGLU + quantize, down
+  launch_gather_rows(w.xq, w.xs, w.pair_token, P, H, w.xq_p, w.xs_p, sms, st);
+  if ((e = launch_q8_tc_grouped_i8(maps, E, w.counts, w.offsets, max_tiles, F, H, w.xq_p, w.xs_p,
+                                   P, w.h_r, F, a.status, st)) ||
+      (e = launch_q8_tc_grouped_i8(maps + E * mb, E, w.counts, w.offsets, max_tiles, F, H, w.xq_p,
+                                   w.xs_p, P, w.u_r, F, a.status, st)))
+    return e;
+  launch_swiglu_quantize(w.h_r, w.u_r, P, F, w.hq_r, w.hs_r, a.status, sms, st);
+  if ((e = launch_q8_tc_grouped_i8(maps + 2 * E * mb, E, w.counts, w.offsets, max_tiles, H, F,
+                                   w.hq_r, w.hs_r, P, w.out_r, H, a.status, st)))
+    return e;
+  // shared expert over every token; its down projection writes y
+  if ((e = launch_q8_tc_single_i8(a.shared.gate, w.xq, w.xs, T, w.h_s, FS, a.status, st)) ||
+      (e = launch_q8_tc_single_i8(a.shared.up, w.xq, w.xs, T, w.u_s, FS, a.status, st)))
+    return e;
+  launch_swiglu_quantize(w.h_s, w.u_s, T, FS, w.hq_s, w.hs_s, a.status, sms, st);
+  return launch_q8_tc_single_i8(a.shared.down, w.hq_s, w.hs_s, T, a.y, H, a.status, st);
 }
 
 cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaStream_t st) {
   if (a.n_experts > kMaxGroupExperts || a.top_k > 8) return cudaErrorInvalidValue;
-  PrefillWs w = carve(a, a.workspace);
+  const bool tc = use_tc(a, mode);
+  PrefillWs w = carve(a, a.workspace, tc);
   if (w.bytes > a.workspace_bytes) return cudaErrorInvalidValue;
   const int T = a.tokens, k = a.top_k, E = a.n_experts;
   launch_route(a.logits, T, E, k, a.normalize, a.scale, a.route_ids, a.route_weights, a.status,
@@ -371,6 +416,13 @@ cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaS
                                                  w.offsets, w.pair_token, w.pair_weight,
                                                  w.token_pos, a.status);
   if (mode != 0) launch_quantize_rows(a.x, a.hidden, T, a.hidden, w.xq, w.xs, a.status, sms, st);
+  if (tc) {
+    const cudaError_t e = prefill_tc(a, w, sms, st);
+    if (e != cudaSuccess) return e;
+    combine_kernel<<<T, 256, 0, st>>>(a.route_ids, w.token_pos, w.pair_weight, w.out_r, T, k,
+                                      a.hidden, a.y);
+    return cudaGetLastError();
+  }
 
   GroupSet g{};
   g.experts = a.experts;

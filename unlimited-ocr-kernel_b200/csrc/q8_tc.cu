@@ -1,0 +1,520 @@
+// q8_tc.cu — Int8Matrix::linear_dynamic_int8 for many rows
+// (src/cpu/quantized.rs:155-236, applied row by row) on the 5th-generation
+// tensor cores.
+//
+// y[m][n] = sum over blocks b, in order, from -0.0:
+//             ((float)S[m][n][b] * ws[n][b]) * xs[m][b]
+// with S the exact int32 sum of one 32-wide block of int8 products.
+//
+// One tcgen05.mma of kind::i8 has K = 32: exactly one q8 block.  So every
+// block gets its own MMA into its own TMEM buffer (no accumulation across
+// blocks on the tensor core), and the epilogue warps apply the reference's
+// float steps block by block, in order, each one an IEEE round-to-nearest
+// operation — bit-identical to the scalar reference.
+//
+// Tile: 128 weight rows (MMA M, one TMEM lane each) x 64 activation rows
+// (MMA N).  Each stage of a 6-stage shared-memory ring holds 128 bytes of K
+// (4 blocks) of both operands (TMA, 128-byte swizzle, K-major as both
+// matrices are stored) and the stage's block scales of both (TMA, 16-byte
+// rows: [128][4] weight scales, [64][4] activation scales), all on one
+// mbarrier.  Warp 0: TMA producer (one thread).  Warp 1: TMEM owner and MMA
+// issuer (one thread).  Warps 2-17: epilogue, four per TMEM lane quarter, one
+// weight row and 16 activation rows per thread, the TMEM load of the next
+// block in flight while the current one is applied.  Eight 64-column TMEM
+// buffers (all of TMEM) let the MMA run up to 7 blocks ahead of the epilogue,
+// covering the MMA's completion latency; a ring slot is
+// reused once its MMAs have completed and every epilogue warp has read its
+// scales.
+//
+// A "group" launch serves the MoE prefill: group g owns activation rows
+// [offsets[g], offsets[g] + counts[g]) and multiplies them by its own
+// weights; the grid's y dimension enumerates 64-row tiles over the groups.
+#include <cuda.h>  // CUtensorMap and its enums (types only)
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace uocr {
+
+namespace {
+
+constexpr int kBN = 128;       // weight rows per tile (MMA M)
+constexpr int kBM = 64;        // activation rows per tile (MMA N)
+constexpr int kBK = 128;       // bytes of K per stage (4 blocks)
+constexpr int kStages = 6;
+constexpr int kAccBufs = 8;    // TMEM buffers of kBM columns: all of TMEM (one CTA per SM)
+constexpr int kTmemCols = kAccBufs * kBM;  // 512
+constexpr int kEpiWarps = 16;  // four per TMEM lane quarter, 16 columns each
+constexpr int kEpiCols = kBM / (kEpiWarps / 4);
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, epilogue
+constexpr int kABytes = kBN * kBK;     // 16 KB weights
+constexpr int kBBytes = kBM * kBK;     // 8 KB activations
+constexpr int kWsBytes = kBN * 4 * 4;  // weight scales [128][4]
+constexpr int kXsBytes = kBM * 4 * 4;  // activation scales [64][4]
+constexpr int kStageBytes = kABytes + kBBytes + kWsBytes + kXsBytes;  // 27 KB (1024-multiple)
+constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*alignment*/ + 512 /*barriers*/;
+static_assert(kStageBytes % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+
+struct TcArgs {
+  const CUtensorMap* maps;  // grouped: [groups][2] (weights, weight scales)
+  const int* counts;        // grouped: rows per group
+  const int* offsets;       // grouped: first row of each group
+  int groups;
+  float* y;  // [rows][ldy]
+  int M, N, K, ldy;
+  unsigned* status;
+};
+
+// ---- PTX wrappers ----------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* holder, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_addr(holder)),
+               "r"(cols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] = A[smem] x B[smem]^T (accumulate = 0: overwrite), kind::i8, s32.
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(0)
+      : "memory");
+}
+
+// Arrive on `bar` once every MMA issued so far by this thread has completed.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_addr(bar))
+               : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+// Waits for this thread's TMEM loads.  The loaded registers are operands so
+// that no use of them can be scheduled before the wait.
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (tiles are 128 bytes of K wide).
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void* p) {
+  const uint64_t addr = smem_addr(p);
+  uint64_t d = (addr >> 4) & 0x3FFF;    // start address
+  d |= static_cast<uint64_t>(1) << 16;  // leading byte offset (unused for swizzled K-major)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;  // stride byte offset
+  d |= static_cast<uint64_t>(1) << 46;          // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(2) << 61;          // layout: SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: kind::i8, signed A and B, s32 D, both K-major,
+// M = 128, N = 64.
+constexpr uint32_t kIdescI8 = (2u << 4)               // D format: s32
+                              | (1u << 7)             // A: signed 8-bit
+                              | (1u << 10)            // B: signed 8-bit
+                              | ((kBM >> 3) << 17)    // N
+                              | ((kBN >> 4) << 24);   // M
+
+// ---- the kernel --------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads, 1)
+    q8_tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
+                         const __grid_constant__ CUtensorMap tmap_ws,
+                         const __grid_constant__ CUtensorMap tmap_x,
+                         const __grid_constant__ CUtensorMap tmap_xs, const TcArgs a) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + kAccBufs;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + kAccBufs);
+  int* tile = reinterpret_cast<int*>(tmem_holder + 1);  // group, first row, rows
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kBN;
+  const int nbk = a.K >> 5, kstages = a.K / kBK;
+  // this CTA's 64-row tile: blockIdx.y counts tiles over the groups in order
+  if (threadIdx.x == 0) {
+    int g = 0, r0 = blockIdx.y * kBM, rows = a.M - blockIdx.y * kBM;
+    if (a.counts) {
+      int t = blockIdx.y;
+      rows = 0;
+      for (g = 0; g < a.groups; ++g) {
+        const int c = a.counts[g], tiles = (c + kBM - 1) / kBM;
+        if (t < tiles) {
+          r0 = a.offsets[g] + t * kBM;
+          rows = c - t * kBM;
+          break;
+        }
+        t -= tiles;
+      }
+    }
+    tile[0] = g;
+    tile[1] = r0;
+    tile[2] = rows > kBM ? kBM : rows;
+  }
+  __syncthreads();
+  const int group = tile[0], row0 = tile[1], rows = tile[2];
+  if (rows <= 0) return;  // past the last tile (the grid is an upper bound)
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1 + kEpiWarps);  // the MMAs' commit + every epilogue warp
+    }
+    for (int b = 0; b < kAccBufs; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kEpiWarps);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_holder, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    // ---- TMA producer: operands and their block scales, one barrier a stage
+    if (lane == 0) {
+      const CUtensorMap* wmap = a.counts ? &a.maps[2 * group] : &tmap_w;
+      const CUtensorMap* smap = a.counts ? &a.maps[2 * group + 1] : &tmap_ws;
+      for (int ks = 0; ks < kstages; ++ks) {
+        const int s = ks % kStages;
+        if (ks >= kStages && !mbar_wait_spin(&empty[s], ((ks / kStages) - 1) & 1, a.status)) break;
+        unsigned char* st = smem + s * kStageBytes;
+        mbar_arrive_expect_tx(&full[s], kStageBytes);
+        tma_load_2d(st, wmap, ks * kBK, n0, &full[s]);
+        tma_load_2d(st + kABytes, &tmap_x, ks * kBK, row0, &full[s]);
+        tma_load_2d(st + kABytes + kBBytes, smap, 4 * ks, n0, &full[s]);
+        tma_load_2d(st + kABytes + kBBytes + kWsBytes, &tmap_xs, 4 * ks, row0, &full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer: one MMA per q8 block, each into its own TMEM buffer
+    if (lane == 0) {
+      int blk = 0;
+      bool ok = true;
+      for (int ks = 0; ks < kstages && ok; ++ks) {
+        const int s = ks % kStages;
+        ok = mbar_wait_spin(&full[s], (ks / kStages) & 1, a.status);
+        if (!ok) break;
+        tc_fence_after();
+        const unsigned char* st = smem + s * kStageBytes;
+        for (int j = 0; j < kBK / 32; ++j, ++blk) {
+          const int buf = blk % kAccBufs;
+          if (blk >= kAccBufs) {
+            ok = mbar_wait_spin(&tempty[buf], ((blk / kAccBufs) - 1) & 1, a.status);
+            if (!ok) break;
+            tc_fence_after();
+          }
+          mma_i8(tmem + buf * kBM, smem_desc_sw128(st + 32 * j),
+                 smem_desc_sw128(st + kABytes + 32 * j), kIdescI8);
+          mma_commit(&tfull[buf]);
+        }
+        mma_commit(&empty[s]);  // one of the slot's arrivals: its MMAs are done
+      }
+    }
+  } else {
+    // ---- epilogue: warp w reads TMEM lanes 32*(w % 4) .. + 31 (the rows it
+    // may access) and kEpiCols of the 64 columns; one weight row per thread.
+    // The TMEM load of block b + 1 is in flight while block b is applied.
+    const int q = warp & 3, part = (warp - 2) / 4;
+    const int rl = 32 * q + lane, n = n0 + rl, c0 = kEpiCols * part;
+    const bool row_ok = n < a.N;
+    const uint32_t tlane = tmem + (static_cast<uint32_t>(32 * q) << 16) + c0;
+    float acc[kEpiCols];
+#pragma unroll
+    for (int i = 0; i < kEpiCols; ++i) acc[i] = -0.0f;
+    bool ok = true;
+    // Block b: its S values are in `now`; start loading block b + 1 into
+    // `next`, apply block b, then wait for the load.  Called with the two
+    // register sets alternating, so no copies are needed.
+    auto step = [&](uint32_t (&now)[kEpiCols], uint32_t (&next)[kEpiCols], int b) {
+      const int buf = b % kAccBufs, ks = b >> 2, jb = b & 3, s = ks % kStages;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);  // block b is in registers
+      if (b + 1 < nbk) {
+        const int b1 = b + 1, buf1 = b1 % kAccBufs, ks1 = b1 >> 2;
+        if ((b1 & 3) == 0 && ok) ok = mbar_wait_spin(&full[ks1 % kStages], (ks1 / kStages) & 1, a.status);
+        if (ok) ok = mbar_wait_spin(&tfull[buf1], (b1 / kAccBufs) & 1, a.status);
+        tc_fence_after();
+        tmem_ld16(tlane + buf1 * kBM, next);
+      }
+      const unsigned char* st = smem + s * kStageBytes;
+      const float* ws_s = reinterpret_cast<const float*>(st + kABytes + kBBytes);  // [128][4]
+      const float* xs_s = reinterpret_cast<const float*>(st + kABytes + kBBytes + kWsBytes);  // [64][4]
+      const float wsb = ws_s[4 * rl + jb];
+      // columns past the tile's last row are padding: nothing to apply
+      // (the warp still takes part in every barrier)
+#pragma unroll
+      for (int c = 0; c < kEpiCols && c0 < rows; ++c) {
+        const float xsc = xs_s[4 * (c0 + c) + jb];
+        // exact int32 -> float: |S| < 2^22 (32 * 127 * 127)
+        const float sf = __int_as_float(0x4B400000 + static_cast<int>(now[c])) - 12582912.0f;
+        // ((float)S * ws) * xs, then the running sum: each step rounded on
+        // its own (the reference never contracts into an fma)
+        acc[c] = __fadd_rn(acc[c], __fmul_rn(__fmul_rn(sf, wsb), xsc));
+      }
+      if (jb == 3) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the slot's scales
+      }
+      if (b + 1 < nbk) tmem_ld_wait(next);
+    };
+    uint32_t ra[kEpiCols], rb[kEpiCols];
+    // block 0: its stage and its TMEM buffer
+    ok = mbar_wait_spin(&full[0], 0, a.status) && mbar_wait_spin(&tfull[0], 0, a.status);
+    tc_fence_after();
+    tmem_ld16(tlane, ra);
+    tmem_ld_wait(ra);
+    for (int b = 0; b < nbk; b += 2) {  // nbk is a multiple of 4
+      step(ra, rb, b);
+      step(rb, ra, b + 1);
+    }
+    if (row_ok) {
+#pragma unroll
+      for (int i = 0; i < kEpiCols; ++i)
+        if (c0 + i < rows) a.y[static_cast<long long>(row0 + c0 + i) * a.ldy + n] = acc[i];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---- prefill helpers ---------------------------------------------------------
+// Rows of the block-quantized activations gathered in pair order:
+// xq_p[p] = xq[src[p]], xs_p[p] = xs[src[p]].
+__global__ void gather_rows_kernel(const int8_t* __restrict__ xq, const float* __restrict__ xs,
+                                   const int* __restrict__ src, int rows, int cols,
+                                   int8_t* __restrict__ xq_p, float* __restrict__ xs_p) {
+  const int nb = cols / 32, c16 = cols / 16;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+       i < static_cast<long long>(rows) * c16; i += stride) {
+    const int p = static_cast<int>(i / c16), c = static_cast<int>(i % c16);
+    reinterpret_cast<uint4*>(xq_p)[i] =
+        reinterpret_cast<const uint4*>(xq)[static_cast<long long>(src[p]) * c16 + c];
+  }
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+       i < static_cast<long long>(rows) * nb; i += stride) {
+    const int p = static_cast<int>(i / nb), b = static_cast<int>(i % nb);
+    xs_p[i] = xs[static_cast<long long>(src[p]) * nb + b];
+  }
+}
+
+// h = silu(gate) * up (Decoder::feed_forward, src/decoder/mod.rs:114-122),
+// block-quantized per row for the down projection in int8 mode
+// (src/cpu/quantized.rs:43-74): one warp per 32-wide block.
+__global__ void swiglu_quantize_kernel(const float* __restrict__ g, const float* __restrict__ u,
+                                       int rows, int cols, int8_t* __restrict__ hq,
+                                       float* __restrict__ hs, unsigned* status) {
+  const int lane = threadIdx.x & 31, nb = cols / 32;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long w = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
+       w < static_cast<long long>(rows) * nb; w += warps) {
+    const long long k = w * 32 + lane;  // rows are cols = 32 * nb wide
+    const float h = __fmul_rn(silu_ref(g[k]), u[k]);
+    if (__any_sync(0xffffffffu, !isfinite(h)) && lane == 0) flag(status, DEV_NONFINITE);
+    const float mx = warp_max(fabsf(h));
+    const float scale = __fdiv_rn(mx, 127.0f);
+    if (lane == 0) {
+      if (mx > 0.0f && scale == 0.0f) flag(status, DEV_UNDERFLOW);
+      hs[w] = scale;
+    }
+    hq[k] = quantize_elem(h, scale);
+  }
+}
+
+int grid_for(long long work, int sms) {
+  const long long g = (work + 255) / 256;
+  return static_cast<int>(g < 1 ? 1 : (g > 8LL * sms ? 8LL * sms : g));
+}
+
+// ---- host: tensor maps ------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D int8 tensor [rows][cols] (cols contiguous), box = box_rows x 128 bytes,
+// 128-byte swizzle (the UMMA K-major layout).
+bool make_map_i8(CUtensorMap* map, const void* base, long long rows, long long cols, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 2-D float tensor [rows][nb] of block scales, box = box_rows x 4 blocks.
+bool make_map_f32(CUtensorMap* map, const float* base, long long rows, long long nb, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(nb), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(nb * 4)};
+  const cuuint32_t box[2] = {4, static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The dynamic shared-memory opt-in, once per device.
+void configure() {
+  static std::mutex mu;
+  static unsigned long long done = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 64 && !(done & (1ull << dev))) {
+    cudaFuncSetAttribute(q8_tc_gemm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         kSmemBytes);
+    done |= 1ull << dev;
+  }
+}
+
+bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+}  // namespace
+
+bool q8_tc_supported(int rows, int cols) {
+  return rows > 0 && cols > 0 && rows % kBN == 0 && cols % kBK == 0 && encode_fn() != nullptr;
+}
+
+size_t q8_tc_maps_bytes() { return 2 * sizeof(CUtensorMap); }
+
+bool q8_tc_weight_maps(void* maps, const Q8View& m) {
+  CUtensorMap* mp = static_cast<CUtensorMap*>(maps);
+  return q8_tc_supported(static_cast<int>(m.rows), static_cast<int>(m.cols)) && aligned16(m.w) &&
+         aligned16(m.s) && make_map_i8(&mp[0], m.w, m.rows, m.cols, kBN) &&
+         make_map_f32(&mp[1], m.s, m.rows, m.cols / 32, kBN);
+}
+
+cudaError_t launch_q8_tc_single_i8(const Q8View& m, const int8_t* xq, const float* xs, int batch,
+                                   float* y, long long ldy, unsigned* status, cudaStream_t st) {
+  if (!q8_tc_supported(static_cast<int>(m.rows), static_cast<int>(m.cols)) || batch < 1)
+    return cudaErrorInvalidValue;
+  if (!aligned16(m.w) || !aligned16(m.s) || !aligned16(xq) || !aligned16(xs))
+    return cudaErrorMisalignedAddress;
+  const int N = static_cast<int>(m.rows), K = static_cast<int>(m.cols);
+  CUtensorMap maps[2], tx, txs;
+  if (!q8_tc_weight_maps(maps, m) || !make_map_i8(&tx, xq, batch, K, kBM) ||
+      !make_map_f32(&txs, xs, batch, K / 32, kBM))
+    return cudaErrorInvalidValue;
+  configure();
+  TcArgs a{};
+  a.groups = 1;
+  a.y = y;
+  a.M = batch;
+  a.N = N;
+  a.K = K;
+  a.ldy = static_cast<int>(ldy);
+  a.status = status;
+  q8_tc_gemm_i8_kernel<<<dim3(N / kBN, (batch + kBM - 1) / kBM), kThreads, kSmemBytes, st>>>(
+      maps[0], maps[1], tx, txs, a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_q8_tc_grouped_i8(const void* maps, int groups, const int* counts,
+                                    const int* offsets, int max_tiles, int N, int K,
+                                    const int8_t* xq, const float* xs, int total_rows, float* y,
+                                    long long ldy, unsigned* status, cudaStream_t st) {
+  if (N % kBN || K % kBK || total_rows < 1 || max_tiles < 1) return cudaErrorInvalidValue;
+  if (!aligned16(xq) || !aligned16(xs) || reinterpret_cast<uintptr_t>(maps) % 64)
+    return cudaErrorMisalignedAddress;
+  CUtensorMap tx, txs;
+  if (!make_map_i8(&tx, xq, total_rows, K, kBM) || !make_map_f32(&txs, xs, total_rows, K / 32, kBM))
+    return cudaErrorInvalidValue;
+  configure();
+  TcArgs a{};
+  a.maps = static_cast<const CUtensorMap*>(maps);
+  a.counts = counts;
+  a.offsets = offsets;
+  a.groups = groups;
+  a.y = y;
+  a.M = total_rows;
+  a.N = N;
+  a.K = K;
+  a.ldy = static_cast<int>(ldy);
+  a.status = status;
+  // the weight-map parameters are unused when grouped (the maps array is)
+  q8_tc_gemm_i8_kernel<<<dim3(N / kBN, max_tiles), kThreads, kSmemBytes, st>>>(tx, txs, tx, txs, a);
+  return cudaGetLastError();
+}
+
+void launch_gather_rows(const int8_t* xq, const float* xs, const int* src, int rows, int cols,
+                        int8_t* xq_p, float* xs_p, int sms, cudaStream_t st) {
+  gather_rows_kernel<<<grid_for(static_cast<long long>(rows) * (cols / 16), sms), 256, 0, st>>>(
+      xq, xs, src, rows, cols, xq_p, xs_p);
+}
+
+void launch_swiglu_quantize(const float* g, const float* u, int rows, int cols, int8_t* hq,
+                            float* hs, unsigned* status, int sms, cudaStream_t st) {
+  const long long warps = static_cast<long long>(rows) * (cols / 32);
+  swiglu_quantize_kernel<<<grid_for(warps * 32, sms), 256, 0, st>>>(g, u, rows, cols, hq, hs,
+                                                                     status);
+}
+
+}  // namespace uocr
