@@ -594,6 +594,183 @@ def run_int8suite(args):
             "cases": cases, "clocks": clocks.summary()}
 
 
+EP_TOKENS = 64  # config 4: a decode batch of 64 independent sequences
+EP_EXPERT_BYTES = 3 * MAT_BYTES(F, H)
+EP_SHARED_BYTES = 3 * MAT_BYTES(FS, H)
+
+
+def ep_init(world, rank, local):
+    """Process group of the EP workload: torchrun's, or one NCCL rank."""
+    import datetime
+    import socket
+
+    import torch.distributed as dist
+    if dist.is_initialized():
+        return
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        return
+    with socket.socket() as s_:
+        s_.bind(("127.0.0.1", 0))
+        port = s_.getsockname()[1]
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1,
+                            timeout=datetime.timedelta(seconds=120))
+
+
+def run_ep(args):
+    """Config 4's MoE layer at decode with expert parallelism: a global batch
+    of 64 tokens split evenly over the ranks (strong scaling); each rank holds
+    the shared expert and a contiguous block of the 64 routed experts; rows
+    travel by NCCL all_to_all.  One step = one forward of the layer for the
+    whole batch (route, dispatch, experts, return, combine).  Weights depend
+    only on the expert id, so every N runs the same layer."""
+    import math
+
+    import torch
+    import torch.distributed as dist
+
+    import uocr_q8
+    from uocr_q8.expert_parallel import ExpertParallelMoe, LibraryBackend, expert_bounds
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    ep_init(world, rank, local)
+    ctx = uocr_q8.GpuContext(local)
+    stream = torch.cuda.Stream(device=dev)
+    bounds = expert_bounds(E, world)
+    mine = range(bounds[rank], bounds[rank + 1])
+    per_rank_bytes = len(mine) * EP_EXPERT_BYTES + EP_SHARED_BYTES
+    n_layers = max(2, math.ceil(3 * 126e6 / per_rank_bytes))  # > L2 between reuses
+
+    def mat(seed, r, c):
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        w = torch.randint(-127, 128, (r, c), dtype=torch.int8, device=dev, generator=g)
+        sc = torch.rand((r, (c + 31) // 32), device=dev, generator=g) * (1e-2 - 1e-4) + 1e-4
+        return uocr_q8.Int8Matrix.from_device(r, c, w, sc.float().contiguous(), ctx)
+
+    eps = []
+    with torch.cuda.stream(stream):
+        for li in range(n_layers):
+            base = 100000 * (li + 1)
+            shared = [mat(base + i, *rc) for i, rc in enumerate(((FS, H), (FS, H), (H, FS)))]
+            experts = [[mat(base + 10 * (e + 1) + i, *rc)
+                        for i, rc in enumerate(((F, H), (F, H), (H, F)))] for e in mine]
+            layer = uocr_q8.MoeLayer(ctx, shared, experts, top_k=1)
+            eps.append(ExpertParallelMoe(LibraryBackend(ctx, layer, E, TOPK), E, TOPK, H))
+    torch.cuda.synchronize()
+    T = EP_TOKENS // world
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(555 + rank)
+    n_in = 8
+    xs = torch.randn((n_in, T, H), device=dev, generator=gen)
+    lg = torch.randn((n_in, T, E), device=dev, generator=gen)
+    mode = args.ep_mode
+
+    def step(i, x, l):
+        return eps[i % n_layers].forward(x, l, mode)[0]
+
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            step(i, xs[i % n_in], lg[i % n_in])
+    torch.cuda.synchronize()
+    steps = max(1, args.steps)
+    dist.barrier()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for i in range(steps):
+                step(i, xs[i % n_in], lg[i % n_in])
+            stop.record(stream)
+        stop.synchronize()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(stop)
+    t = torch.tensor([ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    ms_step = ms / steps
+    value = EP_TOKENS * steps / (ms * 1e-3)
+
+    # end to end: pinned host x/logits in, y out, every step
+    hx = torch.empty((n_in, T, H), pin_memory=True)
+    hl = torch.empty((n_in, T, E), pin_memory=True)
+    hy = torch.empty((n_in, T, H), pin_memory=True)
+    hx.copy_(xs.cpu())
+    hl.copy_(lg.cpu())
+    e2e_steps = max(1, min(steps, args.e2e_steps))
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        for i in range(e2e_steps):
+            j = i % n_in
+            x = hx[j].to(dev, non_blocking=True)
+            l = hl[j].to(dev, non_blocking=True)
+            hy[j].copy_(step(i, x, l), non_blocking=True)
+        stream.synchronize()
+    e2e_s = time.perf_counter() - t0
+    t = torch.tensor([e2e_s], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_s = float(t.item())
+    e2e = EP_TOKENS * e2e_steps / e2e_s
+    ctx.sync()
+
+    peak, peak_kind = peak_hbm()
+    # bytes a rank must read per step: its experts' weights (at a batch of 64
+    # nearly every expert is selected) and the shared expert's
+    achieved = per_rank_bytes / (ms_step * 1e-3) / 1e9
+    result = None
+    if rank == 0:
+        cpu = ep_cpu_baseline(args) if (world == 1 and not args.no_cpu) else None
+        result = {
+            "metric": "MoE layer decode tok/s (config-4 layer, batch 64, expert-parallel)",
+            "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp32" if mode == 0 else "int8-act",
+            "data": "synthetic (seeded; config-1 weight distributions)",
+            "config": {"workload": "config4_moe_layer_ep_decode", "global_batch": EP_TOKENS,
+                       "tokens_per_rank": T, "hidden": H, "experts": E, "top_k": TOPK,
+                       "experts_per_rank": len(mine), "expert_width": F, "shared_width": FS,
+                       "mode": mode, "parallelism": f"ep{world} (NCCL all_to_all)",
+                       "l2": f"rotating pool of {n_layers} layers x "
+                             f"{per_rank_bytes / 1e6:.1f} MB per rank (> 126 MB L2)"},
+            "e2e": {"value": round(e2e, 1), "unit": "tok/s", "steps": e2e_steps,
+                    "h2d_bytes_per_step": T * (H + E) * 4, "d2h_bytes_per_step": T * H * 4},
+            "roofline": {"bound": "hbm", "kernel": "whole EP step (per-rank weight bytes)",
+                         "achieved": round(achieved, 2), "peak": peak, "peak_kind": peak_kind,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None},
+            "gpu_launches": steps * 8 if mode == 0 else None,
+            "clocks": clocks.summary(),
+        }
+        if cpu:
+            result["cpu_baseline"] = cpu
+    dist.barrier()
+    dist.destroy_process_group()
+    return result
+
+
+def ep_cpu_baseline(args):
+    """The reference's scalar path (oracle port, all host threads) on a
+    bounded sample: batches of 64 tokens through one MoE layer."""
+    import oracle
+    oracle.set_threads(0)
+    shared, routed, rng = make_cpu_layer(7)
+    x = rng.standard_normal((EP_TOKENS, H)).astype(np.float32)
+    lg = rng.standard_normal((EP_TOKENS, E)).astype(np.float32)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < args.cpu_seconds:
+        oracle.experts(shared, routed, lg, x, TOPK, args.ep_mode)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(EP_TOKENS * n / dt, 2), "unit": "tok/s", "cores": oracle.get_threads(),
+            "kind": "port", "sample": f"{n} batches of 64 tokens through one MoE layer in {dt:.1f} s"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -609,16 +786,23 @@ def main():
     ap.add_argument("--traffic", type=float, default=None,
                     help="dram bytes per launch from an ncu capture (roofline.traffic); "
                          "defaults to the committed capture of the workload's kernel")
-    ap.add_argument("--workload", choices=["moe_decode", "gemv", "prefill", "int8suite"],
+    ap.add_argument("--workload",
+                    choices=["moe_decode", "gemv", "prefill", "int8suite", "ep_decode"],
                     default="moe_decode")
     ap.add_argument("--gemv-int8", action="store_true")
     ap.add_argument("--prefill-mode", type=int, choices=[0, 2], default=0)
+    ap.add_argument("--ep-mode", type=int, choices=[0, 1, 2], default=0)
     args = ap.parse_args()
     if args.workload == "gemv" and args.impl == "ours":
         print(json.dumps(run_gemv(args)), flush=True)
         return
     if args.workload == "prefill" and args.impl == "ours":
         print(json.dumps(run_prefill(args)), flush=True)
+        return
+    if args.workload == "ep_decode" and args.impl == "ours":
+        res = run_ep(args)
+        if res is not None:
+            print(json.dumps(res), flush=True)
         return
     if args.workload == "int8suite" and args.impl == "ours":
         print(json.dumps(run_int8suite(args)), flush=True)

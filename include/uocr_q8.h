@@ -179,6 +179,37 @@ int uocr_moe_forward_host(uocr_ctx *ctx, const uocr_moe *layer, int mode, const 
                           const float *logits, size_t tokens, float *y, int32_t *ids,
                           float *weights);
 
+/* ---- expert parallelism: uocr_moe_forward in parts ------------------------
+ * No counterpart in the reference: Decoder::experts (src/decoder/mod.rs:
+ * 124-220) runs every expert where the tokens are.  A caller that places the
+ * routed experts of a layer on several GPUs splits the forward into
+ *   uocr_moe_route        routing of this GPU's tokens (ids, weights)
+ *   uocr_moe_expert_rows  the experts this GPU holds, applied to rows sent
+ *                         to it (each with its expert id local to `layer`)
+ *   uocr_moe_shared_rows  the shared expert over this GPU's tokens, into y
+ *   uocr_moe_combine      y[t] += weight * expert output, ascending expert id
+ * and moves rows between GPUs itself.  With the routed rows of each expert
+ * applied in one uocr_moe_expert_rows call per source GPU (in
+ * UOCR_DYNAMIC_ACTIVATIONS an expert's row count selects its arithmetic), the
+ * result is uocr_moe_forward's on this GPU's tokens, bit for bit.  A layer
+ * made for these calls holds only its own experts; its top_k and routing
+ * arguments are not used by them.  All asynchronous on the context stream. */
+/* out_dev[i] = FFN_{expert_ids_dev[i]}(x_dev[i]): x_dev/out_dev rows*hidden.
+ * Rows of one expert form one group, as the tokens an expert receives in
+ * Decoder::experts.  An id outside [0, n_experts) is Shape at the next
+ * synchronising call. */
+int uocr_moe_expert_rows(uocr_ctx *ctx, const uocr_moe *layer, int mode, const float *x_dev,
+                         const int32_t *expert_ids_dev, size_t rows, float *out_dev);
+/* y_dev = shared FFN(x_dev), rows*hidden each. */
+int uocr_moe_shared_rows(uocr_ctx *ctx, const uocr_moe *layer, int mode, const float *x_dev,
+                         size_t rows, float *y_dev);
+/* For each token t: y[t] += weights[t,j] * pair_out[t*top_k + j] over its
+ * top_k pairs in ascending ids[t,j], one rounding per operation (the combine
+ * of src/decoder/mod.rs:208-217; y holds the shared output).  top_k <= 8. */
+int uocr_moe_combine(uocr_ctx *ctx, const int32_t *ids_dev, const float *weights_dev,
+                     const float *pair_out_dev, size_t tokens, size_t top_k, size_t hidden,
+                     float *y_dev);
+
 /* ---- allocation-free decode ------------------------------------------------
  * No counterpart in the reference.  For callers that may not allocate device
  * memory while inference runs (a serving loop that reserves everything at

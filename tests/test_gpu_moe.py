@@ -193,3 +193,78 @@ def test_prefill_config2_shape(ctx, config1, mode):
     y, ids, wts = layer.forward(x, logits, mode)
     ref, ids_ref, wts_ref = oracle.experts(sh, ex, logits, x, 6, mode)
     _check_layer(y, ref, ids, ids_ref, wts, wts_ref, mode != 0)
+
+
+# ------------------------------------------------- the layer in parts (expert parallelism)
+def _parts_forward(ctx, layer, x_t, lg_t, mode, top_k, per_source=None):
+    """uocr_moe_forward rebuilt from route, expert_rows, shared_rows and
+    combine on one GPU; `per_source` splits the routed rows into that many
+    consecutive calls (the grouping a multi-GPU dispatch produces)."""
+    import torch
+    q = q8()
+    ids, wts = q.route_device(ctx, lg_t, top_k)
+    T = x_t.shape[0]
+    rows = x_t.repeat_interleave(top_k, dim=0)
+    eids = ids.reshape(-1).contiguous()
+    out = torch.empty_like(rows)
+    cuts = [0, T * top_k] if not per_source else \
+        [round(i * T * top_k / per_source) for i in range(per_source + 1)]
+    for a, b in zip(cuts[:-1], cuts[1:]):
+        if b > a:
+            layer.expert_rows_device(rows[a:b], eids[a:b], mode, out[a:b])
+    y = layer.shared_rows_device(x_t, mode)
+    q.combine_device(ctx, ids, wts, out, y)
+    return y, ids, wts
+
+
+@pytest.mark.parametrize("mode", [0, 2])
+@pytest.mark.parametrize("shape", [(128, 64, 128, 8, 3), (256, 128, 256, 8, 2)])
+def test_parts_equal_forward(ctx, mode, shape):
+    """route + expert_rows + shared_rows + combine == uocr_moe_forward, bit for
+    bit (both CUDA-core and tensor-core grouped projections)."""
+    import torch
+    H, F, FS, E, k = shape
+    rng = np.random.default_rng(300 + mode + H)
+    layer, sh, ex = make_layer(ctx, rng, H, F, FS, E, k)
+    x = torch.from_numpy(rng.standard_normal((41, H)).astype(np.float32)).cuda()
+    lg = torch.from_numpy(rng.standard_normal((41, E)).astype(np.float32)).cuda()
+    y1 = layer.forward_device(x, lg, mode)
+    y2, _, _ = _parts_forward(ctx, layer, x, lg, mode, k, per_source=3)
+    ctx.sync()
+    assert bits_equal(y1.cpu().numpy(), y2.cpu().numpy())
+
+
+def test_parts_dynamic_groups_per_source(ctx):
+    """DynamicActivations picks int8 for a one-row group: the parts reproduce
+    the single-device layer when each source's rows are one call."""
+    import torch
+    rng = np.random.default_rng(311)
+    layer, sh, ex = make_layer(ctx, rng, 128, 64, 128, 8, 3)
+    x = rng.standard_normal((2, 128)).astype(np.float32)
+    lg = rng.standard_normal((2, 8)).astype(np.float32)
+    y1, _, _ = layer.forward(x, lg, 1)
+    y2, _, _ = _parts_forward(ctx, layer, torch.from_numpy(x).cuda(), torch.from_numpy(lg).cuda(),
+                              1, 3)
+    ctx.sync()
+    assert bits_equal(y1, y2.cpu().numpy())
+
+
+def test_parts_errors(ctx):
+    import torch
+    q = q8()
+    rng = np.random.default_rng(312)
+    layer, _, _ = make_layer(ctx, rng, 128, 64, 128, 4, 2)
+    x = torch.zeros((3, 128), device="cuda")
+    bad = torch.tensor([0, 4, 1], dtype=torch.int32, device="cuda")
+    layer.expert_rows_device(x, bad, 0)
+    with pytest.raises(q.OcrError) as e:
+        ctx.sync()
+    assert e.value.kind == "Shape"
+    ids = torch.zeros((3, 9), dtype=torch.int32, device="cuda")
+    with pytest.raises(q.OcrError) as e:
+        q.combine_device(ctx, ids, ids.float(), torch.zeros((27, 128), device="cuda"), x)
+    assert e.value.kind == "Unsupported"
+    # empty inputs are no-ops
+    layer.expert_rows_device(x[:0], bad[:0], 2)
+    layer.shared_rows_device(x[:0], 2)
+    ctx.sync()

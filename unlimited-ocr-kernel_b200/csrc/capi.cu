@@ -847,6 +847,82 @@ int uocr_moe_forward(uocr_ctx* ctx, const uocr_moe* layer, int mode, const float
   return moe_run(ctx, layer, mode, x_dev, logits_dev, tokens, y_dev, ids_dev, weights_dev);
 }
 
+// One part of the layer over `rows` rows: the routed experts (expert_ids
+// given, outputs in row order) or the shared expert (into y).
+static int moe_part(uocr_ctx* ctx, const uocr_moe* L, int mode, const float* x, size_t rows,
+                    const int32_t* expert_ids, float* out, bool routed) {
+  if (!ctx || !L) return fail(UOCR_ERR_INVALID, "null argument");
+  if (mode != UOCR_WEIGHTS_ONLY && mode != UOCR_DYNAMIC_ACTIVATIONS && mode != UOCR_DYNAMIC_ROWWISE)
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: mode %d", mode);
+  if (L->device != ctx->device)
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: layer on another device");
+  if (rows == 0) return ok();
+  if (!x || !out || (routed && !expert_ids)) return fail(UOCR_ERR_INVALID, "null argument");
+  if (!fits_int(rows)) return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: rows");
+  int st = moe_checks(ctx, L, rows);
+  if (st) return st;
+  if (routed && (st = check_elements(ctx, rows * L->width))) return st;
+  DeviceGuard g(ctx->device);
+  MoePrefillArgs a{};
+  a.experts = L->experts_dev;
+  a.shared = L->shared;
+  a.n_experts = static_cast<int>(L->n_experts);
+  a.top_k = 1;  // one (row, expert) pair per row
+  a.scale = 1.0f;
+  a.hidden = L->hidden;
+  a.width = L->width;
+  a.shared_width = L->shared_width;
+  a.tokens = static_cast<int>(rows);
+  a.x = x;
+  a.status = ctx->status_dev;
+  a.tc_maps = L->tc_maps;
+  a.route_given = 1;
+  if (routed) {
+    a.skip_shared = 1;
+    a.pair_out = out;
+  } else {
+    a.skip_routed = 1;
+    a.y = out;
+  }
+  const size_t rb = (rows * 4 + 255) & ~static_cast<size_t>(255);
+  const size_t need = moe_prefill_workspace(a, mode) + rb + 256;
+  if ((st = ensure_ws(ctx, need))) return st;
+  char* base = static_cast<char*>(ctx->ws);
+  // grouping reads a weight per pair; the routed part never applies it
+  a.route_ids = const_cast<int32_t*>(expert_ids);
+  a.route_weights = reinterpret_cast<float*>(base);
+  a.workspace = base + rb;
+  a.workspace_bytes = ctx->ws_bytes - rb;
+  cudaError_t e = launch_moe_prefill(mode, a, ctx->sms, ctx->stream);
+  if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "moe part launch: %s", cudaGetErrorString(e));
+  return check_launch();
+}
+
+int uocr_moe_expert_rows(uocr_ctx* ctx, const uocr_moe* layer, int mode, const float* x_dev,
+                         const int32_t* expert_ids_dev, size_t rows, float* out_dev) {
+  return moe_part(ctx, layer, mode, x_dev, rows, expert_ids_dev, out_dev, true);
+}
+
+int uocr_moe_shared_rows(uocr_ctx* ctx, const uocr_moe* layer, int mode, const float* x_dev,
+                         size_t rows, float* y_dev) {
+  return moe_part(ctx, layer, mode, x_dev, rows, nullptr, y_dev, false);
+}
+
+int uocr_moe_combine(uocr_ctx* ctx, const int32_t* ids_dev, const float* weights_dev,
+                     const float* pair_out_dev, size_t tokens, size_t top_k, size_t hidden,
+                     float* y_dev) {
+  if (!ctx) return fail(UOCR_ERR_INVALID, "null argument");
+  if (top_k == 0 || top_k > 8) return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: top_k <= 8");
+  if (tokens == 0 || hidden == 0) return ok();
+  if (!ids_dev || !weights_dev || !pair_out_dev || !y_dev) return fail(UOCR_ERR_INVALID, "null argument");
+  if (!fits_int(tokens * top_k) || !fits_int(hidden))
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: tokens");
+  DeviceGuard g(ctx->device);
+  launch_moe_combine_pairs(ids_dev, weights_dev, pair_out_dev, static_cast<int>(tokens),
+                           static_cast<int>(top_k), static_cast<int>(hidden), y_dev, ctx->stream);
+  return check_launch();
+}
+
 int uocr_moe_forward_host(uocr_ctx* ctx, const uocr_moe* layer, int mode, const float* x,
                           const float* logits, size_t tokens, float* y, int32_t* ids,
                           float* weights) {

@@ -111,8 +111,20 @@ struct MoePrefillArgs {
   // tensor-core int8 path (optional): [3][n_experts] q8_tc_weight_maps
   // (gate, up, down) in device memory
   const void* tc_maps;
+  // Parts of the layer, for callers that split it (expert parallelism):
+  // route_given: route_ids/route_weights are inputs (logits unused);
+  // skip_shared / skip_routed: leave that part out; pair_out (non-null):
+  // the routed outputs, row t*top_k + j for pair (t, j), instead of
+  // combining into y.
+  int route_given, skip_shared, skip_routed;
+  float* pair_out;
 };
 size_t moe_prefill_workspace(const MoePrefillArgs& a, int mode);
 cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaStream_t st);
+// y[t] += p * out for token t's pairs in ascending expert id (y holds the
+// shared expert's output): the combine of Decoder::experts on outputs given
+// in pair order (row t*top_k + j).
+void launch_moe_combine_pairs(const int32_t* ids, const float* weights, const float* pair_out,
+                              int tokens, int top_k, int hidden, float* y, cudaStream_t st);
 
 }  // namespace uocr

@@ -127,6 +127,49 @@ __global__ void combine_kernel(const int32_t* __restrict__ ids, const int* __res
   }
 }
 
+// The same combine for outputs in pair order (row t*top_k + j).
+__global__ void combine_pairs_kernel(const int32_t* __restrict__ ids,
+                                     const float* __restrict__ weights,
+                                     const float* __restrict__ pair_out, int tokens, int top_k,
+                                     int hidden, float* __restrict__ y) {
+  const int t = blockIdx.x;
+  if (t >= tokens) return;
+  int e[8], j[8];
+  for (int i = 0; i < top_k; ++i) {
+    e[i] = ids[t * top_k + i];
+    j[i] = i;
+  }
+  for (int i = 1; i < top_k; ++i)
+    for (int m = i; m > 0 && e[m - 1] > e[m]; --m) {
+      int te = e[m]; e[m] = e[m - 1]; e[m - 1] = te;
+      int tj = j[m]; j[m] = j[m - 1]; j[m - 1] = tj;
+    }
+  for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
+    float acc = y[static_cast<long long>(t) * hidden + c];
+    for (int i = 0; i < top_k; ++i) {
+      const long long row = static_cast<long long>(t) * top_k + j[i];
+      acc = __fadd_rn(acc, __fmul_rn(weights[row], pair_out[row * hidden + c]));
+    }
+    y[static_cast<long long>(t) * hidden + c] = acc;
+  }
+}
+
+// pair_out[i] = out_r[token_pos[i]]: routed outputs back in pair order.
+__global__ void unpermute_kernel(const int* __restrict__ token_pos, const float* __restrict__ out_r,
+                                 int pairs, int hidden, float* __restrict__ pair_out) {
+  const int i = blockIdx.x;
+  if (i >= pairs) return;
+  const float* src = out_r + static_cast<long long>(token_pos[i]) * hidden;
+  float* dst = pair_out + static_cast<long long>(i) * hidden;
+  for (int c = threadIdx.x; c < hidden; c += blockDim.x) dst[c] = src[c];
+}
+
+void launch_moe_combine_pairs(const int32_t* ids, const float* weights, const float* pair_out,
+                              int tokens, int top_k, int hidden, float* y, cudaStream_t st) {
+  if (tokens > 0)
+    combine_pairs_kernel<<<tokens, 256, 0, st>>>(ids, weights, pair_out, tokens, top_k, hidden, y);
+}
+
 // ---------------------------------------------------------------------------
 // CUDA-core grouped projection.  Problem p < E is expert p over its pair
 // slice; p == E is the shared expert over all tokens.
@@ -385,17 +428,20 @@ static cudaError_t prefill_tc(const MoePrefillArgs& a, const PrefillWs& w, int s
   const unsigned char* maps = static_cast<const unsigned char*>(a.tc_maps);
   const size_t mb = q8_tc_maps_bytes();  // per matrix
   cudaError_t e;
-  // routed experts: rows gathered per expert, gate and up, SwiGLU + quantize, down
-  launch_gather_rows(w.xq, w.xs, w.pair_token, P, H, w.xq_p, w.xs_p, sms, st);
-  if ((e = launch_q8_tc_grouped_i8(maps, E, w.counts, w.offsets, max_tiles, F, H, w.xq_p, w.xs_p,
-                                   P, w.h_r, F, a.status, st)) ||
-      (e = launch_q8_tc_grouped_i8(maps + E * mb, E, w.counts, w.offsets, max_tiles, F, H, w.xq_p,
-                                   w.xs_p, P, w.u_r, F, a.status, st)))
-    return e;
-  launch_swiglu_quantize(w.h_r, w.u_r, P, F, w.hq_r, w.hs_r, a.status, sms, st);
-  if ((e = launch_q8_tc_grouped_i8(maps + 2 * E * mb, E, w.counts, w.offsets, max_tiles, H, F,
-                                   w.hq_r, w.hs_r, P, w.out_r, H, a.status, st)))
-    return e;
+  if (!a.skip_routed) {
+    // routed experts: rows gathered per expert, gate and up, SwiGLU + quantize, down
+    launch_gather_rows(w.xq, w.xs, w.pair_token, P, H, w.xq_p, w.xs_p, sms, st);
+    if ((e = launch_q8_tc_grouped_i8(maps, E, w.counts, w.offsets, max_tiles, F, H, w.xq_p,
+                                     w.xs_p, P, w.h_r, F, a.status, st)) ||
+        (e = launch_q8_tc_grouped_i8(maps + E * mb, E, w.counts, w.offsets, max_tiles, F, H,
+                                     w.xq_p, w.xs_p, P, w.u_r, F, a.status, st)))
+      return e;
+    launch_swiglu_quantize(w.h_r, w.u_r, P, F, w.hq_r, w.hs_r, a.status, sms, st);
+    if ((e = launch_q8_tc_grouped_i8(maps + 2 * E * mb, E, w.counts, w.offsets, max_tiles, H, F,
+                                     w.hq_r, w.hs_r, P, w.out_r, H, a.status, st)))
+      return e;
+  }
+  if (a.skip_shared) return cudaSuccess;
   // shared expert over every token; its down projection writes y
   if ((e = launch_q8_tc_single_i8(a.shared.gate, w.xq, w.xs, T, w.h_s, FS, a.status, st)) ||
       (e = launch_q8_tc_single_i8(a.shared.up, w.xq, w.xs, T, w.u_s, FS, a.status, st)))
@@ -406,61 +452,70 @@ static cudaError_t prefill_tc(const MoePrefillArgs& a, const PrefillWs& w, int s
 
 cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaStream_t st) {
   if (a.n_experts > kMaxGroupExperts || a.top_k > 8) return cudaErrorInvalidValue;
+  if (a.skip_shared && a.skip_routed) return cudaErrorInvalidValue;
+  if (a.skip_shared && !a.skip_routed && !a.pair_out) return cudaErrorInvalidValue;
   const bool tc = use_tc(a, mode);
   PrefillWs w = carve(a, a.workspace, tc);
   if (w.bytes > a.workspace_bytes) return cudaErrorInvalidValue;
   const int T = a.tokens, k = a.top_k, E = a.n_experts;
-  launch_route(a.logits, T, E, k, a.normalize, a.scale, a.route_ids, a.route_weights, a.status,
-               sms, st);
-  group_pairs_kernel<<<1, kGroupThreads, 0, st>>>(a.route_ids, a.route_weights, T, k, E, w.counts,
-                                                 w.offsets, w.pair_token, w.pair_weight,
-                                                 w.token_pos, a.status);
+  if (!a.skip_routed) {
+    if (!a.route_given)
+      launch_route(a.logits, T, E, k, a.normalize, a.scale, a.route_ids, a.route_weights,
+                   a.status, sms, st);
+    group_pairs_kernel<<<1, kGroupThreads, 0, st>>>(a.route_ids, a.route_weights, T, k, E,
+                                                   w.counts, w.offsets, w.pair_token,
+                                                   w.pair_weight, w.token_pos, a.status);
+  }
   if (mode != 0) launch_quantize_rows(a.x, a.hidden, T, a.hidden, w.xq, w.xs, a.status, sms, st);
   if (tc) {
     const cudaError_t e = prefill_tc(a, w, sms, st);
     if (e != cudaSuccess) return e;
-    combine_kernel<<<T, 256, 0, st>>>(a.route_ids, w.token_pos, w.pair_weight, w.out_r, T, k,
-                                      a.hidden, a.y);
-    return cudaGetLastError();
+  } else {
+    GroupSet g{};
+    g.experts = a.experts;
+    g.shared = a.shared;
+    g.E = a.skip_routed ? 0 : E;      // no routed problems
+    g.T = a.skip_shared ? 0 : T;      // the shared problem has no rows
+    g.H = a.hidden;
+    g.F = a.width;
+    g.FS = a.shared_width;
+    g.mode = mode;
+    g.counts = w.counts;
+    g.offsets = w.offsets;
+    g.pair_token = w.pair_token;
+    g.x = a.x;
+    g.xq = w.xq;
+    g.xs = w.xs;
+    g.h_r = w.h_r;
+    g.h_s = w.h_s;
+    g.hq_r = w.hq_r;
+    g.hs_r = w.hs_r;
+    g.hq_s = w.hq_s;
+    g.hs_s = w.hs_s;
+    g.out_r = w.out_r;
+    g.y = a.y;
+    // an upper bound on m-tiles over all problems
+    const int mtiles = (T * k) / kTM + E + (T + kTM - 1) / kTM + 1;
+    const int wmax = a.width > a.shared_width ? a.width : a.shared_width;
+    g.stage = 0;
+    grouped_cc_kernel<true><<<dim3(mtiles, (wmax + kTN - 1) / kTN), kCCThreads, 0, st>>>(g);
+    if (mode != 0) {
+      if (!a.skip_routed)
+        launch_quantize_rows(w.h_r, a.width, T * k, a.width, w.hq_r, w.hs_r, a.status, sms, st);
+      if (!a.skip_shared)
+        launch_quantize_rows(w.h_s, a.shared_width, T, a.shared_width, w.hq_s, w.hs_s, a.status,
+                             sms, st);
+    }
+    g.stage = 1;
+    grouped_cc_kernel<false><<<dim3(mtiles, (a.hidden + kTN - 1) / kTN), kCCThreads, 0, st>>>(g);
   }
-
-  GroupSet g{};
-  g.experts = a.experts;
-  g.shared = a.shared;
-  g.E = E;
-  g.T = T;
-  g.H = a.hidden;
-  g.F = a.width;
-  g.FS = a.shared_width;
-  g.mode = mode;
-  g.counts = w.counts;
-  g.offsets = w.offsets;
-  g.pair_token = w.pair_token;
-  g.x = a.x;
-  g.xq = w.xq;
-  g.xs = w.xs;
-  g.h_r = w.h_r;
-  g.h_s = w.h_s;
-  g.hq_r = w.hq_r;
-  g.hs_r = w.hs_r;
-  g.hq_s = w.hq_s;
-  g.hs_s = w.hs_s;
-  g.out_r = w.out_r;
-  g.y = a.y;
-  // an upper bound on m-tiles over all problems
-  const int mtiles = (T * k) / kTM + E + (T + kTM - 1) / kTM + 1;
-  const int wmax = a.width > a.shared_width ? a.width : a.shared_width;
-  g.stage = 0;
-  grouped_cc_kernel<true><<<dim3(mtiles, (wmax + kTN - 1) / kTN), kCCThreads, 0, st>>>(g);
-  if (mode != 0) {
-    launch_quantize_rows(w.h_r, a.width, T * k, a.width, w.hq_r, w.hs_r, a.status, sms, st);
-    launch_quantize_rows(w.h_s, a.shared_width, T, a.shared_width, w.hq_s, w.hs_s, a.status, sms,
-                         st);
+  if (!a.skip_routed) {
+    if (a.pair_out)
+      unpermute_kernel<<<T * k, 256, 0, st>>>(w.token_pos, w.out_r, T * k, a.hidden, a.pair_out);
+    else
+      combine_kernel<<<T, 256, 0, st>>>(a.route_ids, w.token_pos, w.pair_weight, w.out_r, T, k,
+                                        a.hidden, a.y);
   }
-  g.stage = 1;
-  grouped_cc_kernel<false><<<dim3(mtiles, (a.hidden + kTN - 1) / kTN), kCCThreads, 0, st>>>(g);
-  combine_kernel<<<T, 256, 0, st>>>(a.route_ids, w.token_pos, w.pair_weight, w.out_r, T, k,
-                                    a.hidden, a.y);
   return cudaGetLastError();
 }
 

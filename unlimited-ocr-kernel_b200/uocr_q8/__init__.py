@@ -266,6 +266,17 @@ def route_device(ctx: GpuContext, logits_t, top_k: int, normalize: bool = False,
     return ids, wts
 
 
+def combine_device(ctx: GpuContext, ids_t, wts_t, pair_out_t, y_t):
+    """y[t] += wts[t, j] * pair_out[t * top_k + j] over t's pairs in ascending
+    expert id (the combine of src/decoder/mod.rs:208-217).  Asynchronous."""
+    tokens, top_k = ids_t.shape
+    _check(lib().uocr_moe_combine(ctx.handle, ctypes.c_void_p(_tptr(ids_t)),
+                                  ctypes.c_void_p(_tptr(wts_t)),
+                                  ctypes.c_void_p(_tptr(pair_out_t)), tokens, top_k,
+                                  y_t.shape[1], ctypes.c_void_p(_tptr(y_t))))
+    return y_t
+
+
 class MoeLayer:
     """Decoder::experts over device-resident q8 FFNs (src/decoder/mod.rs:124-220)."""
 
@@ -321,6 +332,27 @@ class MoeLayer:
             ctypes.c_void_p(_tptr(logits_t)), ctypes.c_void_p(_tptr(y_t))))
         return y_t
 
+    def expert_rows_device(self, x_t, expert_ids_t, mode: int = QuantizationMode.WEIGHTS_ONLY,
+                           out_t=None):
+        """out[i] = FFN_{expert_ids[i]}(x[i]) for the layer's own experts (ids
+        local to the layer); rows of one expert form one group.  Asynchronous."""
+        import torch
+        out_t = out_t if out_t is not None else torch.empty_like(x_t)
+        _check(lib().uocr_moe_expert_rows(self.ctx.handle, self._h, int(mode),
+                                          ctypes.c_void_p(_tptr(x_t)),
+                                          ctypes.c_void_p(_tptr(expert_ids_t)), x_t.shape[0],
+                                          ctypes.c_void_p(_tptr(out_t))))
+        return out_t
+
+    def shared_rows_device(self, x_t, mode: int = QuantizationMode.WEIGHTS_ONLY, y_t=None):
+        """y = the shared expert's FFN of every row of x.  Asynchronous."""
+        import torch
+        y_t = y_t if y_t is not None else torch.empty_like(x_t)
+        _check(lib().uocr_moe_shared_rows(self.ctx.handle, self._h, int(mode),
+                                          ctypes.c_void_p(_tptr(x_t)), x_t.shape[0],
+                                          ctypes.c_void_p(_tptr(y_t))))
+        return y_t
+
     def forward_host_ptrs(self, x_ptr: int, logits_ptr: int, tokens: int, y_ptr: int,
                           mode: int = QuantizationMode.WEIGHTS_ONLY) -> None:
         """Raw host-pointer form (pinned buffers), for end-to-end timing."""
@@ -342,4 +374,5 @@ class MoeLayer:
 
 __all__ = ["BLOCK", "OcrError", "QuantizationMode", "GpuContext", "Int8Matrix", "MoeLayer",
            "route_device", "quantize_rows_device", "linear_multi_device", "default_context",
+           "combine_device",
            "LibraryMissing"]

@@ -55,6 +55,9 @@ SIGNATURES = {
     "uocr_moe_forward": (I, [P, P, I, P, P, S, P, P, P]),
     "uocr_moe_forward_host": (I, [P, P, I, P, P, S, P, P, P]),
     "uocr_moe_forward_decode_noalloc": (I, [P, P, I, P, P, P]),
+    "uocr_moe_expert_rows": (I, [P, P, I, P, P, S, P]),
+    "uocr_moe_shared_rows": (I, [P, P, I, P, S, P]),
+    "uocr_moe_combine": (I, [P, P, P, P, S, S, S, P]),
 }
 
 _lib = None

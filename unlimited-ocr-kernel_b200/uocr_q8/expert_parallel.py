@@ -1,0 +1,170 @@
+"""Expert parallelism for Decoder::experts (src/decoder/mod.rs:124-220).
+
+The reference runs every expert of a MoE layer where the layer's tokens are.
+Here the routed experts of one layer are split over the ranks of a
+torch.distributed process group in contiguous blocks (rank r holds experts
+[bounds[r], bounds[r + 1]) ), the shared expert and the router are on every
+rank, and every rank brings its own tokens.  One forward:
+
+  route     every rank routes its tokens (moe::route): top_k (expert, weight)
+            pairs per token, in the reference's order.
+  dispatch  the pairs, sorted by owning rank (stable: (token, j) order within
+            a rank); one all_to_all of the per-rank counts, then two of the
+            payload: the pair's row of x, and its expert id local to the owner.
+  experts   the owner applies its experts to the rows it received.
+  return    one all_to_all of the expert outputs back to the source rank,
+            where they are put back in pair order (t * top_k + j).
+  combine   the shared expert over the local tokens into y, then
+            y[t] += weight * output over t's pairs in ascending expert id.
+
+The result on each rank is Decoder::experts of that rank's tokens, bit for
+bit.  The rows an expert receives are applied in one group per source rank
+under QuantizationMode::DynamicActivations, whose arithmetic depends on the
+group's row count (src/decoder/mod.rs:103-106: int8 for a single row); in the
+other modes every row's result is independent of its group, so one call
+covers all received rows.
+
+The collectives are torch.distributed's all_to_all_single: NCCL over NVLink on
+GPUs, gloo on the CPU.  The compute is a backend with four methods
+(``route``, ``expert_rows``, ``shared_rows``, ``combine``); on GPUs it is
+``LibraryBackend``, the CUDA library's C ABI (uocr_moe_route,
+uocr_moe_expert_rows, uocr_moe_shared_rows, uocr_moe_combine), which runs on
+the torch stream current at construction so that collectives and kernels are
+ordered on one stream.
+"""
+from __future__ import annotations
+
+from typing import List, Sequence
+
+import torch
+import torch.distributed as dist
+
+DYNAMIC_ACTIVATIONS = 1
+
+
+def expert_bounds(n_experts: int, world: int) -> List[int]:
+    """Contiguous expert blocks: the first n_experts % world ranks hold one more."""
+    if world <= 0 or n_experts < world:
+        raise ValueError(f"{n_experts} experts cannot be split over {world} ranks")
+    base, extra = divmod(n_experts, world)
+    bounds = [0]
+    for r in range(world):
+        bounds.append(bounds[-1] + base + (1 if r < extra else 0))
+    return bounds
+
+
+class ExpertParallelMoe:
+    """One MoE layer whose routed experts are spread over a process group."""
+
+    def __init__(self, backend, n_experts: int, top_k: int, hidden: int, group=None):
+        self.backend = backend
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.n_experts = n_experts
+        self.top_k = top_k
+        self.hidden = hidden
+        self.bounds = expert_bounds(n_experts, self.world)
+        owner = torch.empty(n_experts, dtype=torch.int64)
+        first = torch.empty(n_experts, dtype=torch.int64)
+        for r in range(self.world):
+            owner[self.bounds[r]:self.bounds[r + 1]] = r
+            first[self.bounds[r]:self.bounds[r + 1]] = self.bounds[r]
+        self._owner_cpu, self._first_cpu = owner, first
+        self._tables = {}
+
+    @property
+    def local_experts(self) -> range:
+        return range(self.bounds[self.rank], self.bounds[self.rank + 1])
+
+    def _table(self, device):
+        key = str(device)
+        if key not in self._tables:
+            self._tables[key] = (self._owner_cpu.to(device), self._first_cpu.to(device))
+        return self._tables[key]
+
+    def dispatch_plan(self, ids):
+        """Send order of the pairs, their owners and the per-rank counts."""
+        owner, first = self._table(ids.device)
+        flat = ids.reshape(-1).to(torch.int64)
+        dest = owner[flat]
+        order = torch.argsort(dest, stable=True)
+        send_counts = torch.bincount(dest, minlength=self.world)
+        local_ids = (flat - first[flat]).index_select(0, order).to(torch.int32)
+        return order, local_ids, send_counts
+
+    def forward(self, x, logits, mode: int):
+        """(y, ids, weights) for this rank's tokens x [T, hidden] with router
+        logits [T, n_experts]."""
+        k, H = self.top_k, self.hidden
+        T = x.shape[0]
+        ids, wts = self.backend.route(logits)
+        order, local_ids, send_counts = self.dispatch_plan(ids)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        sc = send_counts.tolist()
+        rc = recv_counts.tolist()
+        n_recv = sum(rc)
+        send_x = x.index_select(0, torch.div(order, k, rounding_mode="floor"))
+        recv_x = x.new_empty((n_recv, H))
+        recv_ids = local_ids.new_empty((n_recv,))
+        dist.all_to_all_single(recv_x, send_x, rc, sc, group=self.group)
+        dist.all_to_all_single(recv_ids, local_ids, rc, sc, group=self.group)
+        out = x.new_empty((n_recv, H))
+        if mode == DYNAMIC_ACTIVATIONS:
+            pos = 0
+            for c in rc:
+                if c:
+                    self.backend.expert_rows(recv_x[pos:pos + c], recv_ids[pos:pos + c], mode,
+                                             out[pos:pos + c])
+                pos += c
+        elif n_recv:
+            self.backend.expert_rows(recv_x, recv_ids, mode, out)
+        back = x.new_empty((T * k, H))
+        dist.all_to_all_single(back, out, sc, rc, group=self.group)
+        pair_out = torch.empty_like(back)
+        pair_out.index_copy_(0, order, back)
+        y = self.backend.shared_rows(x, mode)
+        self.backend.combine(ids, wts, pair_out, y)
+        return y, ids, wts
+
+
+class LibraryBackend:
+    """The CUDA library behind ExpertParallelMoe on one GPU.
+
+    ``layer`` is a uocr_q8.MoeLayer holding this rank's experts (ids local to
+    it) and the shared expert; routing uses the whole layer's expert count."""
+
+    def __init__(self, ctx, layer, n_experts: int, top_k: int, normalize: bool = False,
+                 scale: float = 1.0):
+        import uocr_q8
+        self._q8 = uocr_q8
+        self.ctx = ctx
+        self.layer = layer
+        self.n_experts = n_experts
+        self.top_k = top_k
+        self.normalize = normalize
+        self.scale = scale
+        ctx.set_stream(torch.cuda.current_stream(ctx.device))
+
+    def route(self, logits):
+        return self._q8.route_device(self.ctx, logits, self.top_k, self.normalize, self.scale)
+
+    def expert_rows(self, x, local_ids, mode, out):
+        self.layer.expert_rows_device(x, local_ids, mode, out)
+
+    def shared_rows(self, x, mode):
+        return self.layer.shared_rows_device(x, mode)
+
+    def combine(self, ids, wts, pair_out, y):
+        self._q8.combine_device(self.ctx, ids, wts, pair_out, y)
+
+
+def local_layer(ctx, shared: Sequence, experts: Sequence[Sequence], bounds: Sequence[int],
+                rank: int):
+    """The MoeLayer of rank ``rank``: the shared expert and experts
+    [bounds[rank], bounds[rank + 1]) of ``experts`` (gate, up, down each)."""
+    import uocr_q8
+    mine = list(experts[bounds[rank]:bounds[rank + 1]])
+    # top_k and the routing arguments are not used by the per-part calls
+    return uocr_q8.MoeLayer(ctx, shared, mine, top_k=1)
