@@ -509,11 +509,16 @@ def run_prefill(args):
             "e2e": {"value": round(PREFILL_OPS / e2e_s / 1e12, 3), "unit": "TOP/s",
                     "steps": e2e_n, "ms_per_step": round(e2e_s * 1e3, 3),
                     "h2d_bytes_per_step": T * (H + E) * 4, "d2h_bytes_per_step": T * H * 4},
-            "roofline": {"bound": "tensor", "kernel": "grouped_cc_kernel (CUDA cores)",
+            "roofline": {"bound": "tensor",
+                         "kernel": "whole step: grouped + shared " +
+                                   ("q8_tc_gemm_f32_kernel (3 bf16 pieces)" if mode == 0 else
+                                    "q8_tc_gemm_i8_kernel"),
                          "achieved": round(tops, 3), "peak": round(attainable, 1),
                          "peak_kind": f"min(bf16 dense {kind_t}, AI x HBM {kind_h})",
                          "unit": "TFLOP/s", "frac": round(tops / attainable, 5), "traffic": None},
-            "gpu_launches": steps * 7, "clocks": clocks.summary()}
+            # route, grouping, split or quantize (+ gather), 3 grouped GEMMs, SwiGLU,
+            # shared: split/quantize + 3 GEMMs + SwiGLU, combine
+            "gpu_launches": steps * 13, "clocks": clocks.summary()}
 
 
 def run_int8suite(args):

@@ -166,6 +166,20 @@ def test_prefill_small(ctx, mode):
 
 
 @pytest.mark.parametrize("T", [2, 65, 150])
+def test_prefill_tensor_core_fp32(ctx, T):
+    """FP32 activations on the tensor cores (exact bf16 pieces): gathered
+    rows per expert, grouped projections, ragged groups and tiles."""
+    rng = np.random.default_rng(800 + T)
+    layer, sh, ex = make_layer(ctx, rng, 256, 128, 256, 8, 2)
+    x = rng.standard_normal((T, 256)).astype(np.float32)
+    logits = rng.standard_normal((T, 8)).astype(np.float32)
+    logits[:, 5] += 1.5
+    y, ids, wts = layer.forward(x, logits, 0)
+    ref, ids_ref, wts_ref = oracle.experts(sh, ex, logits, x, 2, 0)
+    _check_layer(y, ref, ids, ids_ref, wts, wts_ref, False)
+
+
+@pytest.mark.parametrize("T", [2, 65, 150])
 def test_prefill_tensor_core_int8(ctx, T):
     """Int8 activations for every row on shapes the tensor-core path takes
     (every dimension a multiple of 128): gathered rows per expert, grouped

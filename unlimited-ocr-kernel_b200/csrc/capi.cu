@@ -452,38 +452,78 @@ static int dynamic_checks(const uocr_ctx* ctx, const uocr_q8* m) {
   return check_elements(ctx, m->cols * 2 + m->rows + nblocks(m->cols));
 }
 
+// Which kernel a linear of `batch` rows runs on: the GEMV kernels, or one of
+// the tensor-core GEMMs (every row int8-quantized, bit-exact; or FP32
+// activations as exact bf16 pieces, FP32 tolerance) when the shape allows.
+enum class LinearPath { Gemv, TcInt8, TcFp32 };
+constexpr size_t kTcFp32MinBatch = 8;
+
+static LinearPath linear_path(const uocr_q8* m, int mode, size_t batch) {
+  const bool tc = q8_tc_supported(static_cast<int>(m->rows), static_cast<int>(m->cols)) &&
+                  reinterpret_cast<uintptr_t>(m->w) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(m->s) % 16 == 0;
+  if (mode == MODE_INT8) return batch > 1 && tc ? LinearPath::TcInt8 : LinearPath::Gemv;
+  return batch >= kTcFp32MinBatch && tc ? LinearPath::TcFp32 : LinearPath::Gemv;
+}
+
+static size_t al256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
+
+// Device scratch of a linear: quantized rows and their scales, or the pieces.
+static size_t linear_scratch_bytes(const uocr_q8* m, int mode, size_t batch) {
+  if (linear_path(m, mode, batch) == LinearPath::TcFp32)
+    return al256(3 * batch * m->cols * 2) + al256(batch * 4);
+  if (mode == MODE_INT8) return al256(batch * m->cols) + al256(batch * nblocks(m->cols) * 4);
+  return 0;
+}
+
+// x_dev rows of m->cols floats (16-byte aligned for the tensor-core paths),
+// y_dev rows of m->rows; `scratch` holds linear_scratch_bytes.
+static int linear_launch(uocr_ctx* ctx, const uocr_q8* m, int mode, const float* x_dev,
+                         size_t batch, float* y_dev, char* scratch) {
+  const int b = static_cast<int>(batch);
+  LinearPath path = linear_path(m, mode, batch);
+  // the pieces are read as float4 rows
+  if (path == LinearPath::TcFp32 && reinterpret_cast<uintptr_t>(x_dev) % 16 != 0)
+    path = LinearPath::Gemv;
+  if (path == LinearPath::TcFp32) {
+    uint16_t* pieces = reinterpret_cast<uint16_t*>(scratch);
+    float* rinv = reinterpret_cast<float*>(scratch + al256(3 * batch * m->cols * 2));
+    launch_split_rows(x_dev, static_cast<long long>(m->cols), nullptr, b, static_cast<int>(m->cols),
+                      pieces, rinv, ctx->sms, ctx->stream);
+    const cudaError_t e = launch_q8_tc_single_f32(view(m), pieces, rinv, b, y_dev,
+                                                  static_cast<long long>(m->rows), ctx->status_dev,
+                                                  ctx->stream);
+    if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "tensor-core linear: %s", cudaGetErrorString(e));
+    return check_launch();
+  }
+  int8_t* xq = nullptr;
+  float* xs = nullptr;
+  if (mode == MODE_INT8) {
+    xq = reinterpret_cast<int8_t*>(scratch);
+    xs = reinterpret_cast<float*>(scratch + al256(batch * m->cols));
+  }
+  if (path == LinearPath::TcInt8) {
+    // many rows: quantize them, then the tensor-core GEMM (bit-exact)
+    launch_quantize_rows(x_dev, static_cast<long long>(m->cols), b, static_cast<int>(m->cols), xq,
+                         xs, ctx->status_dev, ctx->sms, ctx->stream);
+    const cudaError_t e = launch_q8_tc_single_i8(view(m), xq, xs, b, y_dev,
+                                                 static_cast<long long>(m->rows), ctx->status_dev,
+                                                 ctx->stream);
+    if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "tensor-core linear: %s", cudaGetErrorString(e));
+    return check_launch();
+  }
+  launch_gemv(mode, view(m), x_dev, static_cast<long long>(m->cols), b, y_dev,
+              static_cast<long long>(m->rows), xq, xs, ctx->status_dev, ctx->sms, ctx->stream);
+  return check_launch();
+}
+
 static int run_linear(uocr_ctx* ctx, const uocr_q8* m, int mode, const float* x_dev, size_t batch,
                       float* y_dev) {
   if (batch == 0) return ok();
   if (!fits_int(batch)) return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: batch");
-  int8_t* xq = nullptr;
-  float* xs = nullptr;
-  if (mode == MODE_INT8) {
-    const size_t qbytes = (batch * m->cols + 255) & ~static_cast<size_t>(255);
-    const size_t sbytes = (batch * nblocks(m->cols) * 4 + 255) & ~static_cast<size_t>(255);
-    const bool tc = batch > 1 &&
-                    q8_tc_supported(static_cast<int>(m->rows), static_cast<int>(m->cols)) &&
-                    reinterpret_cast<uintptr_t>(m->w) % 16 == 0 &&
-                    reinterpret_cast<uintptr_t>(m->s) % 16 == 0;
-    int st = ensure_ws(ctx, qbytes + sbytes);
-    if (st) return st;
-    xq = static_cast<int8_t*>(ctx->ws);
-    xs = reinterpret_cast<float*>(static_cast<char*>(ctx->ws) + qbytes);
-    if (tc) {
-      // many rows: quantize them, then the tensor-core GEMM (bit-exact)
-      const int b = static_cast<int>(batch);
-      launch_quantize_rows(x_dev, static_cast<long long>(m->cols), b, static_cast<int>(m->cols), xq,
-                           xs, ctx->status_dev, ctx->sms, ctx->stream);
-      const cudaError_t e = launch_q8_tc_single_i8(view(m), xq, xs, b, y_dev,
-                                                   static_cast<long long>(m->rows),
-                                                   ctx->status_dev, ctx->stream);
-      if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "tensor-core linear: %s", cudaGetErrorString(e));
-      return check_launch();
-    }
-  }
-  launch_gemv(mode, view(m), x_dev, static_cast<long long>(m->cols), static_cast<int>(batch), y_dev,
-              static_cast<long long>(m->rows), xq, xs, ctx->status_dev, ctx->sms, ctx->stream);
-  return check_launch();
+  int st = ensure_ws(ctx, linear_scratch_bytes(m, mode, batch));
+  if (st) return st;
+  return linear_launch(ctx, m, mode, x_dev, batch, y_dev, static_cast<char*>(ctx->ws));
 }
 
 int uocr_q8_linear(uocr_ctx* ctx, const uocr_q8* m, const float* x_dev, size_t batch,
@@ -509,23 +549,13 @@ int uocr_q8_linear_dynamic_int8(uocr_ctx* ctx, const uocr_q8* m, const float* x_
 static int host_linear(uocr_ctx* ctx, const uocr_q8* m, int mode, const float* x, size_t batch,
                        float* y) {
   const size_t xn = batch * m->cols, yn = batch * m->rows;
-  const size_t xb = (xn * 4 + 255) & ~static_cast<size_t>(255);
-  const size_t qb = mode == MODE_INT8 ? ((batch * m->cols + 255) & ~static_cast<size_t>(255)) +
-                                            batch * nblocks(m->cols) * 4 + 256
-                                      : 0;
+  const size_t xb = al256(xn * 4), yb = al256(yn * 4);
   int st = take_device_status(ctx);
   if (st) return st;
-  if ((st = ensure_ws(ctx, xb + ((yn * 4 + 255) & ~static_cast<size_t>(255)) + qb))) return st;
+  if ((st = ensure_ws(ctx, xb + yb + linear_scratch_bytes(m, mode, batch)))) return st;
   float* xd = static_cast<float*>(ctx->ws);
   float* yd = reinterpret_cast<float*>(static_cast<char*>(ctx->ws) + xb);
-  int8_t* xq = nullptr;
-  float* xs = nullptr;
-  if (mode == MODE_INT8) {
-    xq = reinterpret_cast<int8_t*>(static_cast<char*>(ctx->ws) + xb +
-                                   ((yn * 4 + 255) & ~static_cast<size_t>(255)));
-    xs = reinterpret_cast<float*>(reinterpret_cast<char*>(xq) +
-                                  ((batch * m->cols + 255) & ~static_cast<size_t>(255)));
-  }
+  char* scratch = static_cast<char*>(ctx->ws) + xb + yb;
   const bool xp = is_pinned(x), yp = is_pinned(y);
   if ((!xp || !yp) && (st = ensure_pinned(ctx, (xp ? 0 : xn * 4) + (yp ? 0 : yn * 4) + 256)))
     return st;
@@ -534,9 +564,7 @@ static int host_linear(uocr_ctx* ctx, const uocr_q8* m, int mode, const float* x
                                                   ((xp ? 0 : xn * 4) + 255) / 256 * 256);
   if (!xp) std::memcpy(xs_h, x, xn * 4);
   CUDA_TRY(cudaMemcpyAsync(xd, xs_h, xn * 4, cudaMemcpyHostToDevice, ctx->stream));
-  launch_gemv(mode, view(m), xd, static_cast<long long>(m->cols), static_cast<int>(batch), yd,
-              static_cast<long long>(m->rows), xq, xs, ctx->status_dev, ctx->sms, ctx->stream);
-  if ((st = check_launch())) return st;
+  if ((st = linear_launch(ctx, m, mode, xd, batch, yd, scratch))) return st;
   CUDA_TRY(cudaMemcpyAsync(ys_h, yd, yn * 4, cudaMemcpyDeviceToHost, ctx->stream));
   st = take_device_status(ctx);
   if (st) return st;

@@ -60,6 +60,24 @@ cudaError_t launch_q8_tc_grouped_i8(const void* maps, int groups, const int* cou
                                     const int* offsets, int max_tiles, int N, int K,
                                     const int8_t* xq, const float* xs, int total_rows, float* y,
                                     long long ldy, unsigned* status, cudaStream_t st);
+// Int8Matrix::linear (FP32 activations) for many rows on the tensor cores
+// (FP32 tolerance).  Activations come as exact three-way bf16 splits of each
+// row scaled by 2^e: pieces [3][rows][cols] and rinv[rows] = 2^-e
+// (launch_split_rows / launch_swiglu_split); same weight conditions as the
+// int8 kernel.
+cudaError_t launch_q8_tc_single_f32(const Q8View& m, const uint16_t* pieces, const float* rinv,
+                                    int batch, float* y, long long ldy, unsigned* status,
+                                    cudaStream_t st);
+cudaError_t launch_q8_tc_grouped_f32(const void* maps, int groups, const int* counts,
+                                     const int* offsets, int max_tiles, int N, int K,
+                                     const uint16_t* pieces, const float* rinv, int total_rows,
+                                     float* y, long long ldy, unsigned* status, cudaStream_t st);
+// pieces and rinv of rows x[src ? src[r] : r] (cols % 4 == 0, x rows 16-byte aligned)
+void launch_split_rows(const float* x, long long ld_x, const int* src, int rows, int cols,
+                       uint16_t* pieces, float* rinv, int sms, cudaStream_t st);
+// pieces and rinv of silu(g) * u
+void launch_swiglu_split(const float* g, const float* u, int rows, int cols, uint16_t* pieces,
+                         float* rinv, int sms, cudaStream_t st);
 // xq_p[p] = xq[src[p]], xs_p[p] = xs[src[p]]
 void launch_gather_rows(const int8_t* xq, const float* xs, const int* src, int rows, int cols,
                         int8_t* xq_p, float* xs_p, int sms, cudaStream_t st);

@@ -368,21 +368,36 @@ struct PrefillWs {
   int8_t* hq_s;
   float* hs_s;
   float* out_r;
-  // tensor-core int8 path
+  // tensor-core paths
   float* u_r;
   float* u_s;
-  int8_t* xq_p;
+  int8_t* xq_p;  // int8: gathered rows
   float* xs_p;
+  uint16_t* xp_r;  // FP32 activations: bf16 pieces of the gathered rows,
+  uint16_t* hp_r;  // of the routed hidden rows,
+  uint16_t* xp_s;  // of the tokens,
+  uint16_t* hp_s;  // of the shared hidden rows
+  float* xr_r;     // their rows' 2^-e
+  float* hr_r;
+  float* xr_s;
+  float* hr_s;
   size_t bytes;
 };
 
-static bool use_tc(const MoePrefillArgs& a, int mode) {
-  return mode == 2 && a.tc_maps &&
-         q8_tc_supported(a.shared_width, a.hidden) && q8_tc_supported(a.hidden, a.shared_width) &&
-         q8_tc_supported(a.width, a.hidden) && q8_tc_supported(a.hidden, a.width);
+// Which kernels run the projections.
+enum class Path { CudaCore, TcInt8, TcFp32 };
+
+static Path prefill_path(const MoePrefillArgs& a, int mode) {
+  const bool shapes = a.tc_maps && q8_tc_supported(a.shared_width, a.hidden) &&
+                      q8_tc_supported(a.hidden, a.shared_width) &&
+                      q8_tc_supported(a.width, a.hidden) && q8_tc_supported(a.hidden, a.width);
+  if (!shapes) return Path::CudaCore;
+  if (mode == 2) return Path::TcInt8;
+  if (mode == 0 && reinterpret_cast<uintptr_t>(a.x) % 16 == 0) return Path::TcFp32;
+  return Path::CudaCore;
 }
 
-static PrefillWs carve(const MoePrefillArgs& a, void* base, bool tc) {
+static PrefillWs carve(const MoePrefillArgs& a, void* base, Path path) {
   PrefillWs w{};
   const size_t T = a.tokens, P = static_cast<size_t>(a.tokens) * a.top_k;
   const size_t H = a.hidden, F = a.width, FS = a.shared_width;
@@ -397,27 +412,71 @@ static PrefillWs carve(const MoePrefillArgs& a, void* base, bool tc) {
   w.pair_token = reinterpret_cast<int*>(take(sizeof(int) * P));
   w.pair_weight = reinterpret_cast<float*>(take(sizeof(float) * P));
   w.token_pos = reinterpret_cast<int*>(take(sizeof(int) * P));
-  w.xq = reinterpret_cast<int8_t*>(take(T * H));
-  w.xs = reinterpret_cast<float*>(take(sizeof(float) * T * blocks_of(a.hidden)));
   w.h_r = reinterpret_cast<float*>(take(sizeof(float) * P * F));
   w.h_s = reinterpret_cast<float*>(take(sizeof(float) * T * FS));
-  w.hq_r = reinterpret_cast<int8_t*>(take(P * F));
-  w.hs_r = reinterpret_cast<float*>(take(sizeof(float) * P * blocks_of(a.width)));
-  w.hq_s = reinterpret_cast<int8_t*>(take(T * FS));
-  w.hs_s = reinterpret_cast<float*>(take(sizeof(float) * T * blocks_of(a.shared_width)));
   w.out_r = reinterpret_cast<float*>(take(sizeof(float) * P * H));
-  if (tc) {
+  if (path != Path::TcFp32) {
+    w.xq = reinterpret_cast<int8_t*>(take(T * H));
+    w.xs = reinterpret_cast<float*>(take(sizeof(float) * T * blocks_of(a.hidden)));
+    w.hq_r = reinterpret_cast<int8_t*>(take(P * F));
+    w.hs_r = reinterpret_cast<float*>(take(sizeof(float) * P * blocks_of(a.width)));
+    w.hq_s = reinterpret_cast<int8_t*>(take(T * FS));
+    w.hs_s = reinterpret_cast<float*>(take(sizeof(float) * T * blocks_of(a.shared_width)));
+  }
+  if (path != Path::CudaCore) {
     w.u_r = reinterpret_cast<float*>(take(sizeof(float) * P * F));
     w.u_s = reinterpret_cast<float*>(take(sizeof(float) * T * FS));
+  }
+  if (path == Path::TcInt8) {
     w.xq_p = reinterpret_cast<int8_t*>(take(P * H));
     w.xs_p = reinterpret_cast<float*>(take(sizeof(float) * P * blocks_of(a.hidden)));
+  }
+  if (path == Path::TcFp32) {
+    w.xp_r = reinterpret_cast<uint16_t*>(take(2 * 3 * P * H));
+    w.hp_r = reinterpret_cast<uint16_t*>(take(2 * 3 * P * F));
+    w.xp_s = reinterpret_cast<uint16_t*>(take(2 * 3 * T * H));
+    w.hp_s = reinterpret_cast<uint16_t*>(take(2 * 3 * T * FS));
+    w.xr_r = reinterpret_cast<float*>(take(sizeof(float) * P));
+    w.hr_r = reinterpret_cast<float*>(take(sizeof(float) * P));
+    w.xr_s = reinterpret_cast<float*>(take(sizeof(float) * T));
+    w.hr_s = reinterpret_cast<float*>(take(sizeof(float) * T));
   }
   w.bytes = off;
   return w;
 }
 
 size_t moe_prefill_workspace(const MoePrefillArgs& a, int mode) {
-  return carve(a, nullptr, use_tc(a, mode)).bytes;
+  return carve(a, nullptr, prefill_path(a, mode)).bytes;
+}
+
+// FP32 activations, all projections on the tensor cores (exact bf16 pieces).
+static cudaError_t prefill_tc_f32(const MoePrefillArgs& a, const PrefillWs& w, int sms,
+                                  cudaStream_t st) {
+  const int T = a.tokens, k = a.top_k, E = a.n_experts, P = T * k;
+  const int H = a.hidden, F = a.width, FS = a.shared_width;
+  const int max_tiles = P / 64 + E + 1;
+  const unsigned char* maps = static_cast<const unsigned char*>(a.tc_maps);
+  const size_t mb = q8_tc_maps_bytes();
+  cudaError_t e;
+  if (!a.skip_routed) {
+    launch_split_rows(a.x, H, w.pair_token, P, H, w.xp_r, w.xr_r, sms, st);
+    if ((e = launch_q8_tc_grouped_f32(maps, E, w.counts, w.offsets, max_tiles, F, H, w.xp_r,
+                                      w.xr_r, P, w.h_r, F, a.status, st)) ||
+        (e = launch_q8_tc_grouped_f32(maps + E * mb, E, w.counts, w.offsets, max_tiles, F, H,
+                                      w.xp_r, w.xr_r, P, w.u_r, F, a.status, st)))
+      return e;
+    launch_swiglu_split(w.h_r, w.u_r, P, F, w.hp_r, w.hr_r, sms, st);
+    if ((e = launch_q8_tc_grouped_f32(maps + 2 * E * mb, E, w.counts, w.offsets, max_tiles, H, F,
+                                      w.hp_r, w.hr_r, P, w.out_r, H, a.status, st)))
+      return e;
+  }
+  if (a.skip_shared) return cudaSuccess;
+  launch_split_rows(a.x, H, nullptr, T, H, w.xp_s, w.xr_s, sms, st);
+  if ((e = launch_q8_tc_single_f32(a.shared.gate, w.xp_s, w.xr_s, T, w.h_s, FS, a.status, st)) ||
+      (e = launch_q8_tc_single_f32(a.shared.up, w.xp_s, w.xr_s, T, w.u_s, FS, a.status, st)))
+    return e;
+  launch_swiglu_split(w.h_s, w.u_s, T, FS, w.hp_s, w.hr_s, sms, st);
+  return launch_q8_tc_single_f32(a.shared.down, w.hp_s, w.hr_s, T, a.y, H, a.status, st);
 }
 
 // Int8 activations for every row, all projections on the tensor cores.
@@ -454,8 +513,8 @@ cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaS
   if (a.n_experts > kMaxGroupExperts || a.top_k > 8) return cudaErrorInvalidValue;
   if (a.skip_shared && a.skip_routed) return cudaErrorInvalidValue;
   if (a.skip_shared && !a.skip_routed && !a.pair_out) return cudaErrorInvalidValue;
-  const bool tc = use_tc(a, mode);
-  PrefillWs w = carve(a, a.workspace, tc);
+  const Path path = prefill_path(a, mode);
+  PrefillWs w = carve(a, a.workspace, path);
   if (w.bytes > a.workspace_bytes) return cudaErrorInvalidValue;
   const int T = a.tokens, k = a.top_k, E = a.n_experts;
   if (!a.skip_routed) {
@@ -467,8 +526,9 @@ cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaS
                                                    w.pair_weight, w.token_pos, a.status);
   }
   if (mode != 0) launch_quantize_rows(a.x, a.hidden, T, a.hidden, w.xq, w.xs, a.status, sms, st);
-  if (tc) {
-    const cudaError_t e = prefill_tc(a, w, sms, st);
+  if (path != Path::CudaCore) {
+    const cudaError_t e =
+        path == Path::TcInt8 ? prefill_tc(a, w, sms, st) : prefill_tc_f32(a, w, sms, st);
     if (e != cudaSuccess) return e;
   } else {
     GroupSet g{};

@@ -30,6 +30,7 @@
 // [offsets[g], offsets[g] + counts[g]) and multiplies them by its own
 // weights; the grid's y dimension enumerates 64-row tiles over the groups.
 #include <cuda.h>  // CUtensorMap and its enums (types only)
+#include <cuda_bf16.h>
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -58,8 +59,19 @@ constexpr int kStageBytes = kABytes + kBBytes + kWsBytes + kXsBytes;  // 27 KB (
 constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*alignment*/ + 512 /*barriers*/;
 static_assert(kStageBytes % 1024 == 0, "swizzled tiles need 1024-byte alignment");
 
+// Everything the tensor-core kernels need of one weight matrix, built once
+// per matrix on the host (q8_tc_weight_maps) and read by the kernels from
+// device memory in grouped launches.
+struct alignas(64) TcMatrixMaps {
+  CUtensorMap w_sw128;   // int8 weights, 128-byte K boxes x 128 rows, 128-byte swizzle
+  CUtensorMap ws;        // weight scales, 4-block boxes x 128 rows
+  CUtensorMap w_rows64;  // int8 weights, 64-byte K boxes x 128 rows, unswizzled
+  const float* s;        // weight scales [rows][nb] (FP32-activation epilogue)
+  int nb;                // scale blocks per row
+};
+
 struct TcArgs {
-  const CUtensorMap* maps;  // grouped: [groups][2] (weights, weight scales)
+  const TcMatrixMaps* maps;  // grouped: [groups]
   const int* counts;        // grouped: rows per group
   const int* offsets;       // grouped: first row of each group
   int groups;
@@ -220,8 +232,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---- TMA producer: operands and their block scales, one barrier a stage
     if (lane == 0) {
-      const CUtensorMap* wmap = a.counts ? &a.maps[2 * group] : &tmap_w;
-      const CUtensorMap* smap = a.counts ? &a.maps[2 * group + 1] : &tmap_ws;
+      const CUtensorMap* wmap = a.counts ? &a.maps[group].w_sw128 : &tmap_w;
+      const CUtensorMap* smap = a.counts ? &a.maps[group].ws : &tmap_ws;
       for (int ks = 0; ks < kstages; ++ks) {
         const int s = ks % kStages;
         if (ks >= kStages && !mbar_wait_spin(&empty[s], ((ks / kStages) - 1) & 1, a.status)) break;
@@ -330,6 +342,369 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+
+// ---- FP32 activations ------------------------------------------------------------
+// Int8Matrix::linear for many rows (src/cpu/quantized.rs:101-153; for a batch
+// the reference multiplies the dequantized weights by the activations with an
+// SGEMM, src/cpu/ops.rs:62-133):
+//   y[m][n] = sum over blocks b of ws[n][b] * (sum over the block of w[n][k] * x[m][k])
+// The int8 weights are exact in bf16.  Every activation row is first scaled
+// by a power of two 2^e that brings its largest magnitude into [1, 2) (so no
+// piece or product lands in the subnormal range the tensor cores flush, and
+// none can overflow), then split exactly into three bf16 pieces
+// x' = x1 + x2 + x3 (x1 = x' truncated to bf16, x2 = the rest truncated,
+// x3 = what remains: 8 significant bits each, fp32's 24 in all).  So every
+// product on the tensor core is exact and only the FP32 accumulation differs
+// from the reference's order.  Three kind::f16 MMAs (one per piece) per 16
+// elements of K accumulate one block's sum in a TMEM buffer; the epilogue
+// adds ws * sum block by block with one fma and multiplies the row's total by
+// 2^-e (exact unless the result is subnormal, then rounded once).
+//
+// A stage is 64 elements of K (two q8 blocks): the weights' int8 tile
+// [128][64] (TMA, unswizzled), converted by four warps into bf16 in the UMMA
+// layout (K-major, 128-byte swizzle) inside the same stage, and the three
+// activation pieces [64][64] bf16 (TMA, 128-byte swizzle).  Warp 0: TMA.
+// Warp 1: TMEM owner and MMA issuer.  Warps 2-5: conversion.  Warps 6-21:
+// epilogue, laid out as in the int8 kernel.  The MMA's N is the tile's row
+// count rounded up to 16, so small expert groups cost few tensor-core cycles.
+constexpr int kFK = 64;
+constexpr int kFStages = 4;
+constexpr int kFConvWarps = 4;
+constexpr int kFThreads = 64 + 32 * (kFConvWarps + kEpiWarps);  // 704
+constexpr int kFWbf = kBN * kFK * 2;                            // 16 KB bf16 weights
+constexpr int kFXp = kBM * kFK * 2;                             // 8 KB per activation piece
+constexpr int kFWi8 = kBN * kFK;                                // 8 KB int8 weights
+constexpr int kFStageBytes = kFWbf + 3 * kFXp + kFWi8;          // 48 KB
+constexpr int kFSmemBytes = kFStages * kFStageBytes + 1024 + 512;
+static_assert(kFStageBytes % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+
+// kind::f16 with bf16 A and B, f32 D, both K-major, M = 128 (N is added at run time).
+constexpr uint32_t kIdescBf16 = (1u << 4)              // D format: f32
+                                | (1u << 7)            // A: bf16
+                                | (1u << 10)           // B: bf16
+                                | ((kBN >> 4) << 24);  // M
+
+struct TcF32Args {
+  const TcMatrixMaps* maps;  // grouped: [groups]
+  const int* counts;
+  const int* offsets;
+  int groups;
+  const float* s;     // single: weight scales [N][K / 32]
+  const float* rinv;  // 2^-e of each activation row
+  float* y;
+  int M, N, K, ldy;
+  int piece_rows;  // rows of each activation piece tensor
+  unsigned* status;
+};
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy (tensor core) reads.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Four int8 (one word, lowest byte first) -> four bf16, exact.
+__device__ __forceinline__ uint2 i8x4_to_bf16x4(uint32_t w) {
+  const float f0 = static_cast<float>(static_cast<int8_t>(w & 0xff));
+  const float f1 = static_cast<float>(static_cast<int8_t>((w >> 8) & 0xff));
+  const float f2 = static_cast<float>(static_cast<int8_t>((w >> 16) & 0xff));
+  const float f3 = static_cast<float>(static_cast<int8_t>(w >> 24));
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(f0, f1);
+  const __nv_bfloat162 hi = __floats2bfloat162_rn(f2, f3);
+  return make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+}
+
+__global__ void __launch_bounds__(kFThreads, 1)
+    q8_tc_gemm_f32_kernel(const __grid_constant__ CUtensorMap tmap_w,
+                          const __grid_constant__ CUtensorMap tmap_xp, const TcF32Args a) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kFStages * kFStageBytes);
+  uint64_t* conv = full + kFStages;
+  uint64_t* empty = conv + kFStages;
+  uint64_t* tfull = empty + kFStages;
+  uint64_t* tempty = tfull + kAccBufs;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + kAccBufs);
+  int* tile = reinterpret_cast<int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kBN;
+  const int nbk = a.K >> 5, kstages = a.K / kFK;
+  if (threadIdx.x == 0) {
+    int g = 0, r0 = blockIdx.y * kBM, rows = a.M - blockIdx.y * kBM;
+    if (a.counts) {
+      int t = blockIdx.y;
+      rows = 0;
+      for (g = 0; g < a.groups; ++g) {
+        const int c = a.counts[g], tiles = (c + kBM - 1) / kBM;
+        if (t < tiles) {
+          r0 = a.offsets[g] + t * kBM;
+          rows = c - t * kBM;
+          break;
+        }
+        t -= tiles;
+      }
+    }
+    tile[0] = g;
+    tile[1] = r0;
+    tile[2] = rows > kBM ? kBM : rows;
+  }
+  __syncthreads();
+  const int group = tile[0], row0 = tile[1], rows = tile[2];
+  if (rows <= 0) return;
+  const uint32_t nmma = static_cast<uint32_t>((rows + 15) & ~15);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kFStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], kFConvWarps);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < kAccBufs; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kEpiWarps);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_holder, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    // ---- TMA producer
+    if (lane == 0) {
+      const CUtensorMap* wmap = a.counts ? &a.maps[group].w_rows64 : &tmap_w;
+      for (int ks = 0; ks < kstages; ++ks) {
+        const int s = ks % kFStages;
+        if (ks >= kFStages && !mbar_wait_spin(&empty[s], ((ks / kFStages) - 1) & 1, a.status)) break;
+        unsigned char* st = smem + s * kFStageBytes;
+        mbar_arrive_expect_tx(&full[s], 3 * kFXp + kFWi8);
+        tma_load_2d(st + kFWbf + 3 * kFXp, wmap, ks * kFK, n0, &full[s]);
+#pragma unroll
+        for (int p = 0; p < 3; ++p)
+          tma_load_2d(st + kFWbf + p * kFXp, &tmap_xp, ks * kFK, p * a.piece_rows + row0, &full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer: per q8 block, 2 x 3 MMAs (K halves x pieces) into one buffer
+    if (lane == 0) {
+      const uint32_t idesc = kIdescBf16 | ((nmma >> 3) << 17);
+      int blk = 0;
+      bool ok = true;
+      for (int ks = 0; ks < kstages && ok; ++ks) {
+        const int s = ks % kFStages;
+        ok = mbar_wait_spin(&full[s], (ks / kFStages) & 1, a.status) &&
+             mbar_wait_spin(&conv[s], (ks / kFStages) & 1, a.status);
+        if (!ok) break;
+        tc_fence_after();
+        const unsigned char* st = smem + s * kFStageBytes;
+        for (int j = 0; j < kFK / 32; ++j, ++blk) {
+          const int buf = blk % kAccBufs;
+          if (blk >= kAccBufs) {
+            ok = mbar_wait_spin(&tempty[buf], ((blk / kAccBufs) - 1) & 1, a.status);
+            if (!ok) break;
+            tc_fence_after();
+          }
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int p = 0; p < 3; ++p)
+              mma_bf16(tmem + buf * kBM, smem_desc_sw128(st + 64 * j + 32 * h),
+                       smem_desc_sw128(st + kFWbf + p * kFXp + 64 * j + 32 * h), idesc,
+                       static_cast<uint32_t>(h | p));
+          mma_commit(&tfull[buf]);
+        }
+        mma_commit(&empty[s]);
+      }
+    }
+  } else if (warp < 2 + kFConvWarps) {
+    // ---- int8 -> bf16 weights: thread ct converts 16-byte chunks ct, ct + 128, ...
+    // (row c / 4, elements 16 * (c % 4) ..) into the swizzled layout: row r's
+    // 16-byte unit j sits at (r / 8) * 1024 + (r % 8) * 128 + ((j ^ (r % 8)) * 16).
+    const int ct = threadIdx.x - 64;
+    for (int ks = 0; ks < kstages; ++ks) {
+      const int s = ks % kFStages;
+      if (!mbar_wait_spin(&full[s], (ks / kFStages) & 1, a.status)) break;
+      unsigned char* st = smem + s * kFStageBytes;
+      const unsigned char* wi8 = st + kFWbf + 3 * kFXp;
+#pragma unroll
+      for (int i = 0; i < (kBN * kFK / 16) / (32 * kFConvWarps); ++i) {
+        const int c = ct + 32 * kFConvWarps * i, r = c >> 2, q = c & 3;
+        const uint4 v = *reinterpret_cast<const uint4*>(wi8 + r * kFK + q * 16);
+        const uint2 a0 = i8x4_to_bf16x4(v.x), a1 = i8x4_to_bf16x4(v.y);
+        const uint2 a2 = i8x4_to_bf16x4(v.z), a3 = i8x4_to_bf16x4(v.w);
+        unsigned char* rowp = st + (r >> 3) * 1024 + (r & 7) * 128;
+        *reinterpret_cast<uint4*>(rowp + (((2 * q) ^ (r & 7)) << 4)) = make_uint4(a0.x, a0.y, a1.x, a1.y);
+        *reinterpret_cast<uint4*>(rowp + (((2 * q + 1) ^ (r & 7)) << 4)) = make_uint4(a2.x, a2.y, a3.x, a3.y);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&conv[s]);
+    }
+  } else {
+    // ---- epilogue: one weight row and 16 activation rows per thread
+    const int ew = warp - 2 - kFConvWarps;
+    const int q = warp & 3, part = ew / 4;
+    const int rl = 32 * q + lane, n = n0 + rl, c0 = kEpiCols * part;
+    const bool active = c0 < rows;
+    const uint32_t tlane = tmem + (static_cast<uint32_t>(32 * q) << 16) + c0;
+    const float* srow = (a.counts ? a.maps[group].s : a.s) + static_cast<long long>(n) * nbk;
+    float acc[kEpiCols];
+#pragma unroll
+    for (int i = 0; i < kEpiCols; ++i) acc[i] = 0.0f;
+    float4 s_cur = __ldg(reinterpret_cast<const float4*>(srow));
+    float4 s_nxt = nbk > 4 ? __ldg(reinterpret_cast<const float4*>(srow + 4)) : s_cur;
+    bool ok = true;
+    auto step = [&](uint32_t (&now)[kEpiCols], uint32_t (&next)[kEpiCols], int b) {
+      const int buf = b % kAccBufs;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);  // block b is in registers
+      if (b + 1 < nbk) {
+        const int b1 = b + 1, buf1 = b1 % kAccBufs;
+        if (ok) ok = mbar_wait_spin(&tfull[buf1], (b1 / kAccBufs) & 1, a.status);
+        tc_fence_after();
+        tmem_ld16(tlane + buf1 * kBM, next);
+      }
+      const int jb = b & 3;
+      const float sc = jb == 0 ? s_cur.x : jb == 1 ? s_cur.y : jb == 2 ? s_cur.z : s_cur.w;
+      if (active) {
+#pragma unroll
+        for (int c = 0; c < kEpiCols; ++c) acc[c] = fmaf(__uint_as_float(now[c]), sc, acc[c]);
+      }
+      if (jb == 3) {
+        s_cur = s_nxt;
+        if (b + 5 < nbk) s_nxt = __ldg(reinterpret_cast<const float4*>(srow + b + 5));
+      }
+      if (b + 1 < nbk) tmem_ld_wait(next);
+    };
+    uint32_t ra[kEpiCols], rb[kEpiCols];
+    ok = mbar_wait_spin(&tfull[0], 0, a.status);
+    tc_fence_after();
+    tmem_ld16(tlane, ra);
+    tmem_ld_wait(ra);
+    for (int b = 0; b < nbk; b += 2) {  // nbk is a multiple of 4
+      step(ra, rb, b);
+      step(rb, ra, b + 1);
+    }
+    if (active) {
+#pragma unroll
+      for (int i = 0; i < kEpiCols; ++i)
+        if (c0 + i < rows)
+          a.y[static_cast<long long>(row0 + c0 + i) * a.ldy + n] =
+              __fmul_rn(acc[i], __ldg(a.rinv + row0 + c0 + i));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// Power-of-two exponent e with max * 2^e in [1, 2); 0 for a zero row or one
+// holding a non-finite value (whose pieces then carry the inf or NaN).
+__device__ __forceinline__ int row_norm_exp(float mx) {
+  if (!(mx > 0.0f) || !isfinite(mx)) return 0;
+  return -ilogbf(mx);
+}
+
+// v * 2^e in two exact steps (each factor a normal float for e in [-149, 149]).
+__device__ __forceinline__ float4 scale_pow2(float4 v, int e) {
+  const float f1 = __int_as_float((127 + e / 2) << 23), f2 = __int_as_float((127 + e - e / 2) << 23);
+  return make_float4(__fmul_rn(__fmul_rn(v.x, f1), f2), __fmul_rn(__fmul_rn(v.y, f1), f2),
+                     __fmul_rn(__fmul_rn(v.z, f1), f2), __fmul_rn(__fmul_rn(v.w, f1), f2));
+}
+
+__device__ __forceinline__ float max_abs4(float4 v) {
+  return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+}
+
+// The exact three-way bf16 split of one fp32 value (see above): the first two
+// pieces truncate (so no piece can round up past the value), the last holds
+// at most 8 significant bits and is exact.
+__device__ __forceinline__ void split3(float v, uint32_t& p0, uint32_t& p1, uint32_t& p2) {
+  const uint32_t b0 = __float_as_uint(v) & 0xFFFF0000u;
+  const float r1 = v - __uint_as_float(b0);
+  const uint32_t b1 = __float_as_uint(r1) & 0xFFFF0000u;
+  const float r2 = r1 - __uint_as_float(b1);
+  p0 = b0 >> 16;
+  p1 = b1 >> 16;
+  p2 = __float_as_uint(r2) >> 16;
+}
+
+__device__ __forceinline__ void store_split4(float4 v, uint16_t* pieces, long long off,
+                                             long long piece_elems) {
+  uint32_t a[4], b[4], c[4];
+  split3(v.x, a[0], b[0], c[0]);
+  split3(v.y, a[1], b[1], c[1]);
+  split3(v.z, a[2], b[2], c[2]);
+  split3(v.w, a[3], b[3], c[3]);
+  *reinterpret_cast<uint2*>(pieces + off) = make_uint2(a[0] | (a[1] << 16), a[2] | (a[3] << 16));
+  *reinterpret_cast<uint2*>(pieces + piece_elems + off) =
+      make_uint2(b[0] | (b[1] << 16), b[2] | (b[3] << 16));
+  *reinterpret_cast<uint2*>(pieces + 2 * piece_elems + off) =
+      make_uint2(c[0] | (c[1] << 16), c[2] | (c[3] << 16));
+}
+
+// One warp per row: pieces[p][r][k] = the split of x[src ? src[r] : r][k] * 2^e
+// and rinv[r] = 2^-e.
+__global__ void split_rows_kernel(const float* __restrict__ x, long long ld_x,
+                                  const int* __restrict__ src, int rows, int cols,
+                                  uint16_t* __restrict__ pieces, float* __restrict__ rinv,
+                                  long long piece_elems) {
+  const int lane = threadIdx.x & 31, c4 = cols / 4;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long r = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
+       r < rows; r += warps) {
+    const float4* xr = reinterpret_cast<const float4*>(x + (src ? src[r] : r) * ld_x);
+    float mx = 0.0f;
+    for (int c = lane; c < c4; c += 32) mx = fmaxf(mx, max_abs4(xr[c]));
+    const int e = row_norm_exp(warp_max(mx));
+    for (int c = lane; c < c4; c += 32)
+      store_split4(scale_pow2(xr[c], e), pieces, r * cols + 4 * c, piece_elems);
+    if (lane == 0) rinv[r] = ldexpf(1.0f, -e);
+  }
+}
+
+__device__ __forceinline__ float4 swiglu4(float4 g, float4 u) {
+  return make_float4(__fmul_rn(silu_ref(g.x), u.x), __fmul_rn(silu_ref(g.y), u.y),
+                     __fmul_rn(silu_ref(g.z), u.z), __fmul_rn(silu_ref(g.w), u.w));
+}
+
+// h = silu(gate) * up (src/decoder/mod.rs:114-122), one warp per row, split
+// into pieces as split_rows_kernel does.
+__global__ void swiglu_split_kernel(const float* __restrict__ g, const float* __restrict__ u,
+                                    int rows, int cols, uint16_t* __restrict__ pieces,
+                                    float* __restrict__ rinv, long long piece_elems) {
+  const int lane = threadIdx.x & 31, c4 = cols / 4;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long r = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
+       r < rows; r += warps) {
+    const float4* gr = reinterpret_cast<const float4*>(g + r * cols);
+    const float4* ur = reinterpret_cast<const float4*>(u + r * cols);
+    float mx = 0.0f;
+    for (int c = lane; c < c4; c += 32) mx = fmaxf(mx, max_abs4(swiglu4(gr[c], ur[c])));
+    const int e = row_norm_exp(warp_max(mx));
+    for (int c = lane; c < c4; c += 32)
+      store_split4(scale_pow2(swiglu4(gr[c], ur[c]), e), pieces, r * cols + 4 * c, piece_elems);
+    if (lane == 0) rinv[r] = ldexpf(1.0f, -e);
+  }
+}
+
 // ---- prefill helpers ---------------------------------------------------------
 // Rows of the block-quantized activations gathered in pair order:
 // xq_p[p] = xq[src[p]], xs_p[p] = xs[src[p]].
@@ -421,6 +796,34 @@ bool make_map_f32(CUtensorMap* map, const float* base, long long rows, long long
             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// int8 weights [rows][cols] for the FP32-activation kernel: 64-byte K boxes
+// x 128 rows, unswizzled (the conversion warps read them).
+bool make_map_w_rows64(CUtensorMap* map, const void* base, long long rows, long long cols) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kFK), static_cast<cuuint32_t>(kBN)};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// bf16 activation pieces [3 * piece_rows][cols]: 64-element K boxes x 64 rows,
+// 128-byte swizzle (the UMMA K-major layout).
+bool make_map_pieces(CUtensorMap* map, const uint16_t* base, long long piece_rows, long long cols) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(3 * piece_rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 2)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kFK), static_cast<cuuint32_t>(kBM)};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(base), dims, strides,
+            box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // The dynamic shared-memory opt-in, once per device.
 void configure() {
   static std::mutex mu;
@@ -431,6 +834,8 @@ void configure() {
   if (dev < 64 && !(done & (1ull << dev))) {
     cudaFuncSetAttribute(q8_tc_gemm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          kSmemBytes);
+    cudaFuncSetAttribute(q8_tc_gemm_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         kFSmemBytes);
     done |= 1ull << dev;
   }
 }
@@ -443,13 +848,18 @@ bool q8_tc_supported(int rows, int cols) {
   return rows > 0 && cols > 0 && rows % kBN == 0 && cols % kBK == 0 && encode_fn() != nullptr;
 }
 
-size_t q8_tc_maps_bytes() { return 2 * sizeof(CUtensorMap); }
+size_t q8_tc_maps_bytes() { return sizeof(TcMatrixMaps); }
 
 bool q8_tc_weight_maps(void* maps, const Q8View& m) {
-  CUtensorMap* mp = static_cast<CUtensorMap*>(maps);
-  return q8_tc_supported(static_cast<int>(m.rows), static_cast<int>(m.cols)) && aligned16(m.w) &&
-         aligned16(m.s) && make_map_i8(&mp[0], m.w, m.rows, m.cols, kBN) &&
-         make_map_f32(&mp[1], m.s, m.rows, m.cols / 32, kBN);
+  TcMatrixMaps* mp = static_cast<TcMatrixMaps*>(maps);
+  if (!q8_tc_supported(static_cast<int>(m.rows), static_cast<int>(m.cols)) || !aligned16(m.w) ||
+      !aligned16(m.s))
+    return false;
+  mp->s = m.s;
+  mp->nb = m.cols / 32;
+  return make_map_i8(&mp->w_sw128, m.w, m.rows, m.cols, kBN) &&
+         make_map_f32(&mp->ws, m.s, m.rows, m.cols / 32, kBN) &&
+         make_map_w_rows64(&mp->w_rows64, m.w, m.rows, m.cols);
 }
 
 cudaError_t launch_q8_tc_single_i8(const Q8View& m, const int8_t* xq, const float* xs, int batch,
@@ -459,8 +869,9 @@ cudaError_t launch_q8_tc_single_i8(const Q8View& m, const int8_t* xq, const floa
   if (!aligned16(m.w) || !aligned16(m.s) || !aligned16(xq) || !aligned16(xs))
     return cudaErrorMisalignedAddress;
   const int N = static_cast<int>(m.rows), K = static_cast<int>(m.cols);
-  CUtensorMap maps[2], tx, txs;
-  if (!q8_tc_weight_maps(maps, m) || !make_map_i8(&tx, xq, batch, K, kBM) ||
+  TcMatrixMaps mm;
+  CUtensorMap tx, txs;
+  if (!q8_tc_weight_maps(&mm, m) || !make_map_i8(&tx, xq, batch, K, kBM) ||
       !make_map_f32(&txs, xs, batch, K / 32, kBM))
     return cudaErrorInvalidValue;
   configure();
@@ -473,7 +884,7 @@ cudaError_t launch_q8_tc_single_i8(const Q8View& m, const int8_t* xq, const floa
   a.ldy = static_cast<int>(ldy);
   a.status = status;
   q8_tc_gemm_i8_kernel<<<dim3(N / kBN, (batch + kBM - 1) / kBM), kThreads, kSmemBytes, st>>>(
-      maps[0], maps[1], tx, txs, a);
+      mm.w_sw128, mm.ws, tx, txs, a);
   return cudaGetLastError();
 }
 
@@ -489,7 +900,7 @@ cudaError_t launch_q8_tc_grouped_i8(const void* maps, int groups, const int* cou
     return cudaErrorInvalidValue;
   configure();
   TcArgs a{};
-  a.maps = static_cast<const CUtensorMap*>(maps);
+  a.maps = static_cast<const TcMatrixMaps*>(maps);
   a.counts = counts;
   a.offsets = offsets;
   a.groups = groups;
@@ -502,6 +913,72 @@ cudaError_t launch_q8_tc_grouped_i8(const void* maps, int groups, const int* cou
   // the weight-map parameters are unused when grouped (the maps array is)
   q8_tc_gemm_i8_kernel<<<dim3(N / kBN, max_tiles), kThreads, kSmemBytes, st>>>(tx, txs, tx, txs, a);
   return cudaGetLastError();
+}
+
+cudaError_t launch_q8_tc_single_f32(const Q8View& m, const uint16_t* pieces, const float* rinv,
+                                    int batch, float* y, long long ldy, unsigned* status,
+                                    cudaStream_t st) {
+  if (!q8_tc_supported(static_cast<int>(m.rows), static_cast<int>(m.cols)) || batch < 1)
+    return cudaErrorInvalidValue;
+  if (!aligned16(m.w) || !aligned16(m.s) || !aligned16(pieces)) return cudaErrorMisalignedAddress;
+  const int N = static_cast<int>(m.rows), K = static_cast<int>(m.cols);
+  CUtensorMap tw, tp;
+  if (!make_map_w_rows64(&tw, m.w, N, K) || !make_map_pieces(&tp, pieces, batch, K))
+    return cudaErrorInvalidValue;
+  configure();
+  TcF32Args a{};
+  a.groups = 1;
+  a.s = m.s;
+  a.rinv = rinv;
+  a.y = y;
+  a.M = batch;
+  a.N = N;
+  a.K = K;
+  a.ldy = static_cast<int>(ldy);
+  a.piece_rows = batch;
+  a.status = status;
+  q8_tc_gemm_f32_kernel<<<dim3(N / kBN, (batch + kBM - 1) / kBM), kFThreads, kFSmemBytes, st>>>(
+      tw, tp, a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_q8_tc_grouped_f32(const void* maps, int groups, const int* counts,
+                                     const int* offsets, int max_tiles, int N, int K,
+                                     const uint16_t* pieces, const float* rinv, int total_rows,
+                                     float* y, long long ldy, unsigned* status, cudaStream_t st) {
+  if (N % kBN || K % kBK || total_rows < 1 || max_tiles < 1) return cudaErrorInvalidValue;
+  if (!aligned16(pieces) || reinterpret_cast<uintptr_t>(maps) % 64) return cudaErrorMisalignedAddress;
+  CUtensorMap tp;
+  if (!make_map_pieces(&tp, pieces, total_rows, K)) return cudaErrorInvalidValue;
+  configure();
+  TcF32Args a{};
+  a.maps = static_cast<const TcMatrixMaps*>(maps);
+  a.counts = counts;
+  a.offsets = offsets;
+  a.groups = groups;
+  a.rinv = rinv;
+  a.y = y;
+  a.M = total_rows;
+  a.N = N;
+  a.K = K;
+  a.ldy = static_cast<int>(ldy);
+  a.piece_rows = total_rows;
+  a.status = status;
+  // the weight-map parameter is unused when grouped (the maps array is)
+  q8_tc_gemm_f32_kernel<<<dim3(N / kBN, max_tiles), kFThreads, kFSmemBytes, st>>>(tp, tp, a);
+  return cudaGetLastError();
+}
+
+void launch_split_rows(const float* x, long long ld_x, const int* src, int rows, int cols,
+                       uint16_t* pieces, float* rinv, int sms, cudaStream_t st) {
+  split_rows_kernel<<<grid_for(static_cast<long long>(rows) * 32, sms), 256, 0, st>>>(
+      x, ld_x, src, rows, cols, pieces, rinv, static_cast<long long>(rows) * cols);
+}
+
+void launch_swiglu_split(const float* g, const float* u, int rows, int cols, uint16_t* pieces,
+                         float* rinv, int sms, cudaStream_t st) {
+  swiglu_split_kernel<<<grid_for(static_cast<long long>(rows) * 32, sms), 256, 0, st>>>(
+      g, u, rows, cols, pieces, rinv, static_cast<long long>(rows) * cols);
 }
 
 void launch_gather_rows(const int8_t* xq, const float* xs, const int* src, int rows, int cols,
