@@ -300,6 +300,22 @@ __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, u
   return true;
 }
 
+// Bounded wait through mbarrier.try_wait without a time hint: between polls
+// the hardware may suspend the thread until the phase completes, so warps
+// that wait leave their issue slots to the warps doing the work (a test_wait
+// spin by many warps starves the workers of the same scheduler).
+__device__ __forceinline__ bool mbar_wait_try(uint64_t* bar, uint32_t parity, unsigned* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitLimitCycles) {
+      flag(status, DEV_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
 // 1-D bulk copy global -> shared, completion signalled on `bar` as tx bytes.
 // Both addresses 16-byte aligned, bytes a multiple of 16 (checked by callers).
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,

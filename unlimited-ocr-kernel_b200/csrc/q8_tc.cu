@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const CUtensorMap* smap = a.counts ? &a.maps[group].ws : &tmap_ws;
       for (int ks = 0; ks < kstages; ++ks) {
         const int s = ks % kStages;
-        if (ks >= kStages && !mbar_wait_spin(&empty[s], ((ks / kStages) - 1) & 1, a.status)) break;
+        if (ks >= kStages && !mbar_wait_try(&empty[s], ((ks / kStages) - 1) & 1, a.status)) break;
         unsigned char* st = smem + s * kStageBytes;
         mbar_arrive_expect_tx(&full[s], kStageBytes);
         tma_load_2d(st, wmap, ks * kBK, n0, &full[s]);
@@ -252,14 +252,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int ks = 0; ks < kstages && ok; ++ks) {
         const int s = ks % kStages;
-        ok = mbar_wait_spin(&full[s], (ks / kStages) & 1, a.status);
+        ok = mbar_wait_try(&full[s], (ks / kStages) & 1, a.status);
         if (!ok) break;
         tc_fence_after();
         const unsigned char* st = smem + s * kStageBytes;
         for (int j = 0; j < kBK / 32; ++j, ++blk) {
           const int buf = blk % kAccBufs;
           if (blk >= kAccBufs) {
-            ok = mbar_wait_spin(&tempty[buf], ((blk / kAccBufs) - 1) & 1, a.status);
+            ok = mbar_wait_try(&tempty[buf], ((blk / kAccBufs) - 1) & 1, a.status);
             if (!ok) break;
             tc_fence_after();
           }
@@ -292,8 +292,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&tempty[buf]);  // block b is in registers
       if (b + 1 < nbk) {
         const int b1 = b + 1, buf1 = b1 % kAccBufs, ks1 = b1 >> 2;
-        if ((b1 & 3) == 0 && ok) ok = mbar_wait_spin(&full[ks1 % kStages], (ks1 / kStages) & 1, a.status);
-        if (ok) ok = mbar_wait_spin(&tfull[buf1], (b1 / kAccBufs) & 1, a.status);
+        if ((b1 & 3) == 0 && ok) ok = mbar_wait_try(&full[ks1 % kStages], (ks1 / kStages) & 1, a.status);
+        if (ok) ok = mbar_wait_try(&tfull[buf1], (b1 / kAccBufs) & 1, a.status);
         tc_fence_after();
         tmem_ld16(tlane + buf1 * kBM, next);
       }
@@ -320,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     uint32_t ra[kEpiCols], rb[kEpiCols];
     // block 0: its stage and its TMEM buffer
-    ok = mbar_wait_spin(&full[0], 0, a.status) && mbar_wait_spin(&tfull[0], 0, a.status);
+    ok = mbar_wait_try(&full[0], 0, a.status) && mbar_wait_try(&tfull[0], 0, a.status);
     tc_fence_after();
     tmem_ld16(tlane, ra);
     tmem_ld_wait(ra);
@@ -355,18 +355,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 // x' = x1 + x2 + x3 (x1 = x' truncated to bf16, x2 = the rest truncated,
 // x3 = what remains: 8 significant bits each, fp32's 24 in all).  So every
 // product on the tensor core is exact and only the FP32 accumulation differs
-// from the reference's order.  Three kind::f16 MMAs (one per piece) per 16
-// elements of K accumulate one block's sum in a TMEM buffer; the epilogue
-// adds ws * sum block by block with one fma and multiplies the row's total by
-// 2^-e (exact unless the result is subnormal, then rounded once).
+// from the reference's order.  One kind::f16 MMA per 16 elements of K, with
+// the three pieces stacked as one B operand, puts a block's three partial sums
+// in a TMEM buffer; the epilogue adds them (smallest first), adds ws * sum
+// block by block with one fma and multiplies the row's total by 2^-e (exact
+// unless the result is subnormal, then rounded once).
 //
 // A stage is 64 elements of K (two q8 blocks): the weights' int8 tile
 // [128][64] (TMA, unswizzled), converted by four warps into bf16 in the UMMA
 // layout (K-major, 128-byte swizzle) inside the same stage, and the three
-// activation pieces [64][64] bf16 (TMA, 128-byte swizzle).  Warp 0: TMA.
-// Warp 1: TMEM owner and MMA issuer.  Warps 2-5: conversion.  Warps 6-21:
-// epilogue, laid out as in the int8 kernel.  The MMA's N is the tile's row
-// count rounded up to 16, so small expert groups cost few tensor-core cycles.
+// activation pieces [box][64] bf16 (TMA, 128-byte swizzle; box = the tile's
+// rows rounded up to 16, 32 or 64).  Warp 0: TMA.  Warp 1: TMEM owner and MMA issuer.
+// Warps 2-5: conversion.  Warps 6-21: epilogue, laid out as in the int8
+// kernel.  The MMA's N is the tile's row count rounded up to 16, so small
+// expert groups cost few tensor-core cycles.  The single-thread roles and the
+// conversion warps poll their barriers (they are on the critical path and a
+// suspended waiter wakes late); the epilogue warps wait suspended, leaving
+// their issue slots to the conversion.  The conversion uses integer and
+// FP32 operations only (the int -> float conversion instructions have a
+// quarter of their throughput and made the conversion the bottleneck).
 constexpr int kFK = 64;
 constexpr int kFStages = 4;
 constexpr int kFConvWarps = 4;
@@ -412,20 +419,26 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// Four int8 (one word, lowest byte first) -> four bf16, exact.
+// Four int8 (one word, lowest byte first) -> four bf16, exact.  Each byte,
+// offset to u = v + 128, is placed under the exponent of 2^23 (the float
+// 2^23 + u); subtracting 2^23 + 128 leaves v exactly.  |v| <= 128 has at
+// most 8 significant bits, so its bf16 is the float's high half.
 __device__ __forceinline__ uint2 i8x4_to_bf16x4(uint32_t w) {
-  const float f0 = static_cast<float>(static_cast<int8_t>(w & 0xff));
-  const float f1 = static_cast<float>(static_cast<int8_t>((w >> 8) & 0xff));
-  const float f2 = static_cast<float>(static_cast<int8_t>((w >> 16) & 0xff));
-  const float f3 = static_cast<float>(static_cast<int8_t>(w >> 24));
-  const __nv_bfloat162 lo = __floats2bfloat162_rn(f0, f1);
-  const __nv_bfloat162 hi = __floats2bfloat162_rn(f2, f3);
-  return make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+  const uint32_t u = w ^ 0x80808080u;
+  const float magic = 8388736.0f;  // 2^23 + 128
+  const float f0 = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440)), magic);
+  const float f1 = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441)), magic);
+  const float f2 = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442)), magic);
+  const float f3 = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443)), magic);
+  return make_uint2(__byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632),
+                    __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632));
 }
 
 __global__ void __launch_bounds__(kFThreads, 1)
     q8_tc_gemm_f32_kernel(const __grid_constant__ CUtensorMap tmap_w,
-                          const __grid_constant__ CUtensorMap tmap_xp, const TcF32Args a) {
+                          const __grid_constant__ CUtensorMap tmap_xp,
+                          const __grid_constant__ CUtensorMap tmap_xp16,
+                          const __grid_constant__ CUtensorMap tmap_xp32, const TcF32Args a) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -462,7 +475,14 @@ __global__ void __launch_bounds__(kFThreads, 1)
   __syncthreads();
   const int group = tile[0], row0 = tile[1], rows = tile[2];
   if (rows <= 0) return;
-  const uint32_t nmma = static_cast<uint32_t>((rows + 15) & ~15);
+  // The activation tile's height: the rows rounded up to 16, 32 or 64.  The
+  // three pieces sit one above the other as one B operand of 3 * box rows, so
+  // one MMA per 16 elements of K covers all three (the MMA instruction, not
+  // the tensor-core arithmetic, is what a stage pays for with small tiles);
+  // a block's sums take 3 * box TMEM columns and the epilogue adds the pieces.
+  const int box = rows <= 16 ? 16 : rows <= 32 ? 32 : 64;
+  const int bufcols = 3 * box;
+  const int nbuf = kTmemCols / bufcols < kAccBufs ? kTmemCols / bufcols : kAccBufs;  // 8, 5 or 2
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kFStages; ++s) {
@@ -486,22 +506,27 @@ __global__ void __launch_bounds__(kFThreads, 1)
     // ---- TMA producer
     if (lane == 0) {
       const CUtensorMap* wmap = a.counts ? &a.maps[group].w_rows64 : &tmap_w;
+      const CUtensorMap* xmap = box == 16 ? &tmap_xp16 : box == 32 ? &tmap_xp32 : &tmap_xp;
+      const uint32_t tx = kFWi8 + 3 * box * 128;
       for (int ks = 0; ks < kstages; ++ks) {
         const int s = ks % kFStages;
         if (ks >= kFStages && !mbar_wait_spin(&empty[s], ((ks / kFStages) - 1) & 1, a.status)) break;
         unsigned char* st = smem + s * kFStageBytes;
-        mbar_arrive_expect_tx(&full[s], 3 * kFXp + kFWi8);
+        mbar_arrive_expect_tx(&full[s], tx);
         tma_load_2d(st + kFWbf + 3 * kFXp, wmap, ks * kFK, n0, &full[s]);
 #pragma unroll
         for (int p = 0; p < 3; ++p)
-          tma_load_2d(st + kFWbf + p * kFXp, &tmap_xp, ks * kFK, p * a.piece_rows + row0, &full[s]);
+          tma_load_2d(st + kFWbf + p * box * 128, xmap, ks * kFK, p * a.piece_rows + row0, &full[s]);
       }
     }
   } else if (warp == 1) {
-    // ---- MMA issuer: per q8 block, 2 x 3 MMAs (K halves x pieces) into one buffer
+    // ---- MMA issuer: per q8 block, one MMA per 16 elements of K into the
+    // block's buffer (N = 3 * box: all pieces at once)
     if (lane == 0) {
-      const uint32_t idesc = kIdescBf16 | ((nmma >> 3) << 17);
-      int blk = 0;
+      const uint32_t idesc = kIdescBf16 | (static_cast<uint32_t>(bufcols >> 3) << 17);
+      // buffer index and lap count kept incrementally: a division by the
+      // run-time nbuf costs the issuing thread more than an MMA
+      int buf = 0, lap = 0;
       bool ok = true;
       for (int ks = 0; ks < kstages && ok; ++ks) {
         const int s = ks % kFStages;
@@ -510,22 +535,24 @@ __global__ void __launch_bounds__(kFThreads, 1)
         if (!ok) break;
         tc_fence_after();
         const unsigned char* st = smem + s * kFStageBytes;
-        for (int j = 0; j < kFK / 32; ++j, ++blk) {
-          const int buf = blk % kAccBufs;
-          if (blk >= kAccBufs) {
-            ok = mbar_wait_spin(&tempty[buf], ((blk / kAccBufs) - 1) & 1, a.status);
+        for (int j = 0; j < kFK / 32; ++j) {
+          if (lap > 0) {
+            ok = mbar_wait_spin(&tempty[buf], (lap - 1) & 1, a.status);
             if (!ok) break;
             tc_fence_after();
           }
 #pragma unroll
           for (int h = 0; h < 2; ++h)
-#pragma unroll
-            for (int p = 0; p < 3; ++p)
-              mma_bf16(tmem + buf * kBM, smem_desc_sw128(st + 64 * j + 32 * h),
-                       smem_desc_sw128(st + kFWbf + p * kFXp + 64 * j + 32 * h), idesc,
-                       static_cast<uint32_t>(h | p));
-          mma_commit(&tfull[buf]);
+            mma_bf16(tmem + buf * bufcols, smem_desc_sw128(st + 64 * j + 32 * h),
+                     smem_desc_sw128(st + kFWbf + 64 * j + 32 * h), idesc,
+                     static_cast<uint32_t>(h));
+          if (++buf == nbuf) {
+            buf = 0;
+            ++lap;
+          }
         }
+        // one commit per stage: it frees the slot and publishes both blocks
+        // (a commit costs the issuing thread far more than an MMA)
         mma_commit(&empty[s]);
       }
     }
@@ -554,50 +581,51 @@ __global__ void __launch_bounds__(kFThreads, 1)
       if (lane == 0) mbar_arrive(&conv[s]);
     }
   } else {
-    // ---- epilogue: one weight row and 16 activation rows per thread
+    // ---- epilogue: one weight row and 16 activation rows per thread; per
+    // block, the three pieces' sums (smallest first) times the block scale
     const int ew = warp - 2 - kFConvWarps;
     const int q = warp & 3, part = ew / 4;
     const int rl = 32 * q + lane, n = n0 + rl, c0 = kEpiCols * part;
-    const bool active = c0 < rows;
+    const bool active = c0 < rows;  // warp-uniform
     const uint32_t tlane = tmem + (static_cast<uint32_t>(32 * q) << 16) + c0;
     const float* srow = (a.counts ? a.maps[group].s : a.s) + static_cast<long long>(n) * nbk;
     float acc[kEpiCols];
 #pragma unroll
     for (int i = 0; i < kEpiCols; ++i) acc[i] = 0.0f;
-    float4 s_cur = __ldg(reinterpret_cast<const float4*>(srow));
-    float4 s_nxt = nbk > 4 ? __ldg(reinterpret_cast<const float4*>(srow + 4)) : s_cur;
     bool ok = true;
-    auto step = [&](uint32_t (&now)[kEpiCols], uint32_t (&next)[kEpiCols], int b) {
-      const int buf = b % kAccBufs;
+    int buf = 0;
+    for (int b = 0; b < nbk; ++b) {
+      const float sc = __ldg(srow + b);  // its latency hides behind the wait
+      // the stage's commit (its slot's `empty` phase): the MMA cannot run
+      // kFStages stages ahead of this warp (it waits for the TMEM buffers),
+      // so the phase waited for is the latest one
+      const int ks = b >> 1;
+      if (ok) ok = mbar_wait_try(&empty[ks % kFStages], (ks / kFStages) & 1, a.status);
+      tc_fence_after();
+      // the two small pieces' sums first, then the leading piece's (two
+      // rounds of loads keep the epilogue within the register budget)
+      uint32_t ra[kEpiCols], rb[kEpiCols];
+      if (active) {
+        const uint32_t tb = tlane + buf * bufcols;
+        tmem_ld16(tb + 2 * box, ra);
+        tmem_ld16(tb + box, rb);
+        tmem_ld_wait(ra);
+        tmem_ld_wait(rb);
+#pragma unroll
+        for (int c = 0; c < kEpiCols; ++c)
+          ra[c] = __float_as_uint(__fadd_rn(__uint_as_float(ra[c]), __uint_as_float(rb[c])));
+        tmem_ld16(tb, rb);
+        tmem_ld_wait(rb);
+      }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[buf]);  // block b is in registers
-      if (b + 1 < nbk) {
-        const int b1 = b + 1, buf1 = b1 % kAccBufs;
-        if (ok) ok = mbar_wait_spin(&tfull[buf1], (b1 / kAccBufs) & 1, a.status);
-        tc_fence_after();
-        tmem_ld16(tlane + buf1 * kBM, next);
-      }
-      const int jb = b & 3;
-      const float sc = jb == 0 ? s_cur.x : jb == 1 ? s_cur.y : jb == 2 ? s_cur.z : s_cur.w;
+      if (lane == 0) mbar_arrive(&tempty[buf]);
       if (active) {
 #pragma unroll
-        for (int c = 0; c < kEpiCols; ++c) acc[c] = fmaf(__uint_as_float(now[c]), sc, acc[c]);
+        for (int c = 0; c < kEpiCols; ++c)
+          acc[c] = fmaf(__fadd_rn(__uint_as_float(ra[c]), __uint_as_float(rb[c])), sc, acc[c]);
       }
-      if (jb == 3) {
-        s_cur = s_nxt;
-        if (b + 5 < nbk) s_nxt = __ldg(reinterpret_cast<const float4*>(srow + b + 5));
-      }
-      if (b + 1 < nbk) tmem_ld_wait(next);
-    };
-    uint32_t ra[kEpiCols], rb[kEpiCols];
-    ok = mbar_wait_spin(&tfull[0], 0, a.status);
-    tc_fence_after();
-    tmem_ld16(tlane, ra);
-    tmem_ld_wait(ra);
-    for (int b = 0; b < nbk; b += 2) {  // nbk is a multiple of 4
-      step(ra, rb, b);
-      step(rb, ra, b + 1);
+      if (++buf == nbuf) buf = 0;
     }
     if (active) {
 #pragma unroll
@@ -810,14 +838,15 @@ bool make_map_w_rows64(CUtensorMap* map, const void* base, long long rows, long 
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// bf16 activation pieces [3 * piece_rows][cols]: 64-element K boxes x 64 rows,
-// 128-byte swizzle (the UMMA K-major layout).
-bool make_map_pieces(CUtensorMap* map, const uint16_t* base, long long piece_rows, long long cols) {
+// bf16 activation pieces [3 * piece_rows][cols]: 64-element K boxes x box_rows
+// rows, 128-byte swizzle (the UMMA K-major layout).
+bool make_map_pieces(CUtensorMap* map, const uint16_t* base, long long piece_rows, long long cols,
+                     int box_rows) {
   auto fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(3 * piece_rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 2)};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kFK), static_cast<cuuint32_t>(kBM)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kFK), static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t estr[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(base), dims, strides,
             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -922,8 +951,9 @@ cudaError_t launch_q8_tc_single_f32(const Q8View& m, const uint16_t* pieces, con
     return cudaErrorInvalidValue;
   if (!aligned16(m.w) || !aligned16(m.s) || !aligned16(pieces)) return cudaErrorMisalignedAddress;
   const int N = static_cast<int>(m.rows), K = static_cast<int>(m.cols);
-  CUtensorMap tw, tp;
-  if (!make_map_w_rows64(&tw, m.w, N, K) || !make_map_pieces(&tp, pieces, batch, K))
+  CUtensorMap tw, tp, tp16, tp32;
+  if (!make_map_w_rows64(&tw, m.w, N, K) || !make_map_pieces(&tp, pieces, batch, K, kBM) ||
+      !make_map_pieces(&tp16, pieces, batch, K, 16) || !make_map_pieces(&tp32, pieces, batch, K, 32))
     return cudaErrorInvalidValue;
   configure();
   TcF32Args a{};
@@ -938,7 +968,7 @@ cudaError_t launch_q8_tc_single_f32(const Q8View& m, const uint16_t* pieces, con
   a.piece_rows = batch;
   a.status = status;
   q8_tc_gemm_f32_kernel<<<dim3(N / kBN, (batch + kBM - 1) / kBM), kFThreads, kFSmemBytes, st>>>(
-      tw, tp, a);
+      tw, tp, tp16, tp32, a);
   return cudaGetLastError();
 }
 
@@ -948,8 +978,11 @@ cudaError_t launch_q8_tc_grouped_f32(const void* maps, int groups, const int* co
                                      float* y, long long ldy, unsigned* status, cudaStream_t st) {
   if (N % kBN || K % kBK || total_rows < 1 || max_tiles < 1) return cudaErrorInvalidValue;
   if (!aligned16(pieces) || reinterpret_cast<uintptr_t>(maps) % 64) return cudaErrorMisalignedAddress;
-  CUtensorMap tp;
-  if (!make_map_pieces(&tp, pieces, total_rows, K)) return cudaErrorInvalidValue;
+  CUtensorMap tp, tp16, tp32;
+  if (!make_map_pieces(&tp, pieces, total_rows, K, kBM) ||
+      !make_map_pieces(&tp16, pieces, total_rows, K, 16) ||
+      !make_map_pieces(&tp32, pieces, total_rows, K, 32))
+    return cudaErrorInvalidValue;
   configure();
   TcF32Args a{};
   a.maps = static_cast<const TcMatrixMaps*>(maps);
@@ -965,7 +998,7 @@ cudaError_t launch_q8_tc_grouped_f32(const void* maps, int groups, const int* co
   a.piece_rows = total_rows;
   a.status = status;
   // the weight-map parameter is unused when grouped (the maps array is)
-  q8_tc_gemm_f32_kernel<<<dim3(N / kBN, max_tiles), kFThreads, kFSmemBytes, st>>>(tp, tp, a);
+  q8_tc_gemm_f32_kernel<<<dim3(N / kBN, max_tiles), kFThreads, kFSmemBytes, st>>>(tp, tp, tp16, tp32, a);
   return cudaGetLastError();
 }
 
