@@ -179,6 +179,48 @@ def test_prefill_tensor_core_fp32(ctx, T):
     _check_layer(y, ref, ids, ids_ref, wts, wts_ref, False)
 
 
+@pytest.mark.parametrize("T", [2, 3, 65, 150])
+def test_prefill_tensor_core_dynamic(ctx, T):
+    """QuantizationMode::DynamicActivations on tensor-core shapes: groups of
+    one row take the bit-exact int8 kernel, the others the FP32 kernel (the
+    reference's dispatch, src/decoder/mod.rs:103-106); the shared expert runs
+    FP32 for more than one token.  FP32 tolerance end to end; a layer whose
+    tokens each choose distinct experts (every group one row) is checked
+    against the all-int8 layer bit for bit in the routed part."""
+    rng = np.random.default_rng(700 + T)
+    layer, sh, ex = make_layer(ctx, rng, 256, 128, 256, 8, 2)
+    x = rng.standard_normal((T, 256)).astype(np.float32)
+    logits = rng.standard_normal((T, 8)).astype(np.float32)
+    if T > 3:
+        logits[:, 5] += 1.5
+    y, ids, wts = layer.forward(x, logits, 1)
+    ref, ids_ref, wts_ref = oracle.experts(sh, ex, logits, x, 2, 1)
+    _check_layer(y, ref, ids, ids_ref, wts, wts_ref, False)
+
+
+def test_prefill_dynamic_single_row_groups_are_int8(ctx):
+    """Tokens routed to disjoint experts: every routed group has one row, so
+    the routed part equals int8 activations; with the shared expert's FP32
+    part identical in both runs, mode 1 and mode 2 differ only through it."""
+    import torch
+    rng = np.random.default_rng(71)
+    layer, sh, ex = make_layer(ctx, rng, 256, 128, 256, 8, 2)
+    x = rng.standard_normal((3, 256)).astype(np.float32)
+    logits = np.full((3, 8), -5.0, np.float32)
+    for t, (e0, e1) in enumerate([(0, 1), (2, 3), (4, 5)]):
+        logits[t, e0] = 3.0
+        logits[t, e1] = 2.0
+    xt = torch.from_numpy(x).cuda()
+    lt = torch.from_numpy(logits).cuda()
+    ids, wts = q8().route_device(ctx, lt, 2)
+    rows = xt.repeat_interleave(2, dim=0)
+    eids = ids.reshape(-1).contiguous()
+    out1 = layer.expert_rows_device(rows, eids, 1)
+    out2 = layer.expert_rows_device(rows, eids, 2)
+    ctx.sync()
+    assert bits_equal(out1.cpu().numpy(), out2.cpu().numpy())
+
+
 @pytest.mark.parametrize("T", [2, 65, 150])
 def test_prefill_tensor_core_int8(ctx, T):
     """Int8 activations for every row on shapes the tensor-core path takes

@@ -381,11 +381,15 @@ struct PrefillWs {
   float* hr_r;
   float* xr_s;
   float* hr_s;
+  int* counts_i8;   // DynamicActivations: single-row groups (int8) and the rest (FP32)
+  int* counts_f32;
   size_t bytes;
 };
 
-// Which kernels run the projections.
-enum class Path { CudaCore, TcInt8, TcFp32 };
+// Which kernels run the projections.  TcMixed is QuantizationMode::
+// DynamicActivations (src/decoder/mod.rs:103-106): int8 activations for a
+// group of one row, FP32 for the others, each on its tensor-core kernel.
+enum class Path { CudaCore, TcInt8, TcFp32, TcMixed };
 
 static Path prefill_path(const MoePrefillArgs& a, int mode) {
   const bool shapes = a.tc_maps && q8_tc_supported(a.shared_width, a.hidden) &&
@@ -393,8 +397,8 @@ static Path prefill_path(const MoePrefillArgs& a, int mode) {
                       q8_tc_supported(a.width, a.hidden) && q8_tc_supported(a.hidden, a.width);
   if (!shapes) return Path::CudaCore;
   if (mode == 2) return Path::TcInt8;
-  if (mode == 0 && reinterpret_cast<uintptr_t>(a.x) % 16 == 0) return Path::TcFp32;
-  return Path::CudaCore;
+  if (reinterpret_cast<uintptr_t>(a.x) % 16 != 0) return Path::CudaCore;
+  return mode == 0 ? Path::TcFp32 : Path::TcMixed;
 }
 
 static PrefillWs carve(const MoePrefillArgs& a, void* base, Path path) {
@@ -415,7 +419,7 @@ static PrefillWs carve(const MoePrefillArgs& a, void* base, Path path) {
   w.h_r = reinterpret_cast<float*>(take(sizeof(float) * P * F));
   w.h_s = reinterpret_cast<float*>(take(sizeof(float) * T * FS));
   w.out_r = reinterpret_cast<float*>(take(sizeof(float) * P * H));
-  if (path != Path::TcFp32) {
+  if (path != Path::TcFp32) {  // int8 activations somewhere
     w.xq = reinterpret_cast<int8_t*>(take(T * H));
     w.xs = reinterpret_cast<float*>(take(sizeof(float) * T * blocks_of(a.hidden)));
     w.hq_r = reinterpret_cast<int8_t*>(take(P * F));
@@ -427,11 +431,15 @@ static PrefillWs carve(const MoePrefillArgs& a, void* base, Path path) {
     w.u_r = reinterpret_cast<float*>(take(sizeof(float) * P * F));
     w.u_s = reinterpret_cast<float*>(take(sizeof(float) * T * FS));
   }
-  if (path == Path::TcInt8) {
+  if (path == Path::TcInt8 || path == Path::TcMixed) {
     w.xq_p = reinterpret_cast<int8_t*>(take(P * H));
     w.xs_p = reinterpret_cast<float*>(take(sizeof(float) * P * blocks_of(a.hidden)));
   }
-  if (path == Path::TcFp32) {
+  if (path == Path::TcMixed) {
+    w.counts_i8 = reinterpret_cast<int*>(take(sizeof(int) * (a.n_experts + 1)));
+    w.counts_f32 = reinterpret_cast<int*>(take(sizeof(int) * (a.n_experts + 1)));
+  }
+  if (path == Path::TcFp32 || path == Path::TcMixed) {
     w.xp_r = reinterpret_cast<uint16_t*>(take(2 * 3 * P * H));
     w.hp_r = reinterpret_cast<uint16_t*>(take(2 * 3 * P * F));
     w.xp_s = reinterpret_cast<uint16_t*>(take(2 * 3 * T * H));
@@ -509,6 +517,65 @@ static cudaError_t prefill_tc(const MoePrefillArgs& a, const PrefillWs& w, int s
   return launch_q8_tc_single_i8(a.shared.down, w.hq_s, w.hs_s, T, a.y, H, a.status, st);
 }
 
+// counts_i8[g] = counts[g] if it is 1 else 0; counts_f32[g] = the others.
+__global__ void split_counts_kernel(const int* __restrict__ counts, int groups,
+                                    int* __restrict__ counts_i8, int* __restrict__ counts_f32) {
+  for (int g = threadIdx.x; g < groups; g += blockDim.x) {
+    const int c = counts[g];
+    counts_i8[g] = c == 1 ? 1 : 0;
+    counts_f32[g] = c == 1 ? 0 : c;
+  }
+}
+
+// QuantizationMode::DynamicActivations on the tensor cores: a group of one
+// row (src/decoder/mod.rs:103-106: projection of a single-row input) runs the
+// bit-exact int8 kernel, every other group the FP32 kernel; the two write
+// disjoint rows.  Both SwiGLU forms run over all rows (each down kernel reads
+// its own).  The shared expert sees every token: int8 for one token, else FP32.
+static cudaError_t prefill_tc_mixed(const MoePrefillArgs& a, const PrefillWs& w, int sms,
+                                    cudaStream_t st) {
+  const int T = a.tokens, k = a.top_k, E = a.n_experts, P = T * k;
+  const int H = a.hidden, F = a.width, FS = a.shared_width;
+  const int max_tiles = P / 64 + E + 1;
+  const unsigned char* maps = static_cast<const unsigned char*>(a.tc_maps);
+  const size_t mb = q8_tc_maps_bytes();
+  cudaError_t e;
+  if (!a.skip_routed) {
+    split_counts_kernel<<<1, 256, 0, st>>>(w.counts, E, w.counts_i8, w.counts_f32);
+    launch_gather_rows(w.xq, w.xs, w.pair_token, P, H, w.xq_p, w.xs_p, sms, st);
+    launch_split_rows(a.x, H, w.pair_token, P, H, w.xp_r, w.xr_r, sms, st);
+    for (int j = 0; j < 2; ++j) {  // gate, up
+      float* out = j == 0 ? w.h_r : w.u_r;
+      if ((e = launch_q8_tc_grouped_i8(maps + j * E * mb, E, w.counts_i8, w.offsets, E + 1, F, H,
+                                       w.xq_p, w.xs_p, P, out, F, a.status, st)) ||
+          (e = launch_q8_tc_grouped_f32(maps + j * E * mb, E, w.counts_f32, w.offsets, max_tiles,
+                                        F, H, w.xp_r, w.xr_r, P, out, F, a.status, st)))
+        return e;
+    }
+    launch_swiglu_quantize(w.h_r, w.u_r, P, F, w.hq_r, w.hs_r, a.status, sms, st);
+    launch_swiglu_split(w.h_r, w.u_r, P, F, w.hp_r, w.hr_r, sms, st);
+    if ((e = launch_q8_tc_grouped_i8(maps + 2 * E * mb, E, w.counts_i8, w.offsets, E + 1, H, F,
+                                     w.hq_r, w.hs_r, P, w.out_r, H, a.status, st)) ||
+        (e = launch_q8_tc_grouped_f32(maps + 2 * E * mb, E, w.counts_f32, w.offsets, max_tiles, H,
+                                      F, w.hp_r, w.hr_r, P, w.out_r, H, a.status, st)))
+      return e;
+  }
+  if (a.skip_shared) return cudaSuccess;
+  if (T == 1) {
+    if ((e = launch_q8_tc_single_i8(a.shared.gate, w.xq, w.xs, T, w.h_s, FS, a.status, st)) ||
+        (e = launch_q8_tc_single_i8(a.shared.up, w.xq, w.xs, T, w.u_s, FS, a.status, st)))
+      return e;
+    launch_swiglu_quantize(w.h_s, w.u_s, T, FS, w.hq_s, w.hs_s, a.status, sms, st);
+    return launch_q8_tc_single_i8(a.shared.down, w.hq_s, w.hs_s, T, a.y, H, a.status, st);
+  }
+  launch_split_rows(a.x, H, nullptr, T, H, w.xp_s, w.xr_s, sms, st);
+  if ((e = launch_q8_tc_single_f32(a.shared.gate, w.xp_s, w.xr_s, T, w.h_s, FS, a.status, st)) ||
+      (e = launch_q8_tc_single_f32(a.shared.up, w.xp_s, w.xr_s, T, w.u_s, FS, a.status, st)))
+    return e;
+  launch_swiglu_split(w.h_s, w.u_s, T, FS, w.hp_s, w.hr_s, sms, st);
+  return launch_q8_tc_single_f32(a.shared.down, w.hp_s, w.hr_s, T, a.y, H, a.status, st);
+}
+
 cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaStream_t st) {
   if (a.n_experts > kMaxGroupExperts || a.top_k > 8) return cudaErrorInvalidValue;
   if (a.skip_shared && a.skip_routed) return cudaErrorInvalidValue;
@@ -527,8 +594,9 @@ cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaS
   }
   if (mode != 0) launch_quantize_rows(a.x, a.hidden, T, a.hidden, w.xq, w.xs, a.status, sms, st);
   if (path != Path::CudaCore) {
-    const cudaError_t e =
-        path == Path::TcInt8 ? prefill_tc(a, w, sms, st) : prefill_tc_f32(a, w, sms, st);
+    const cudaError_t e = path == Path::TcInt8   ? prefill_tc(a, w, sms, st)
+                          : path == Path::TcFp32 ? prefill_tc_f32(a, w, sms, st)
+                                                 : prefill_tc_mixed(a, w, sms, st);
     if (e != cudaSuccess) return e;
   } else {
     GroupSet g{};

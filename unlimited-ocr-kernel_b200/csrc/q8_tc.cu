@@ -110,6 +110,12 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+// Orders this thread's generic-proxy shared-memory accesses before later
+// async-proxy ones (tensor-core reads, bulk copies into the same bytes).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // D[tmem] = A[smem] x B[smem]^T (accumulate = 0: overwrite), kind::i8, s32.
 __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                        uint32_t idesc) {
@@ -188,14 +194,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * kBN;
   const int nbk = a.K >> 5, kstages = a.K / kBK;
-  // this CTA's 64-row tile: blockIdx.y counts tiles over the groups in order
+  // this CTA's 64-row tile: blockIdx.y counts tiles over the groups in order.
+  // The group counts are copied to shared memory by all threads first (one
+  // thread walking them in global memory pays an L2 round trip per group).
+  int* scount = reinterpret_cast<int*>(smem);  // the ring, before any copy lands there
+  if (a.counts)
+    for (int g = threadIdx.x; g < a.groups; g += blockDim.x) scount[g] = a.counts[g];
+  __syncthreads();
   if (threadIdx.x == 0) {
     int g = 0, r0 = blockIdx.y * kBM, rows = a.M - blockIdx.y * kBM;
     if (a.counts) {
       int t = blockIdx.y;
       rows = 0;
       for (g = 0; g < a.groups; ++g) {
-        const int c = a.counts[g], tiles = (c + kBM - 1) / kBM;
+        const int c = scount[g], tiles = (c + kBM - 1) / kBM;
         if (t < tiles) {
           r0 = a.offsets[g] + t * kBM;
           rows = c - t * kBM;
@@ -208,6 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tile[1] = r0;
     tile[2] = rows > kBM ? kBM : rows;
   }
+  fence_proxy_async_smem();  // the scratch reads come before the copies that overwrite it
   __syncthreads();
   const int group = tile[0], row0 = tile[1], rows = tile[2];
   if (rows <= 0) return;  // past the last tile (the grid is an upper bound)
@@ -375,15 +388,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 // FP32 operations only (the int -> float conversion instructions have a
 // quarter of their throughput and made the conversion the bottleneck).
 constexpr int kFK = 64;
-constexpr int kFStages = 4;
 constexpr int kFConvWarps = 4;
-constexpr int kFThreads = 64 + 32 * (kFConvWarps + kEpiWarps);  // 704
-constexpr int kFWbf = kBN * kFK * 2;                            // 16 KB bf16 weights
-constexpr int kFXp = kBM * kFK * 2;                             // 8 KB per activation piece
+constexpr int kFThreads = 96 + 32 * (kFConvWarps + kEpiWarps);  // 736
 constexpr int kFWi8 = kBN * kFK;                                // 8 KB int8 weights
-constexpr int kFStageBytes = kFWbf + 3 * kFXp + kFWi8;          // 48 KB
-constexpr int kFSmemBytes = kFStages * kFStageBytes + 1024 + 512;
-static_assert(kFStageBytes % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+constexpr int kFW8Slots = 8;                                    // int8 weight ring: 64 KB
+constexpr int kFWbf = kBN * kFK * 2;                            // 16 KB bf16 weights
+constexpr int kFSRing = 160 * 1024;                             // MMA-stage ring
+constexpr int kFMaxS = 8;
+constexpr int kFSmemBytes = kFW8Slots * kFWi8 + kFSRing + 1024 + 512;
 
 // kind::f16 with bf16 A and B, f32 D, both K-major, M = 128 (N is added at run time).
 constexpr uint32_t kIdescBf16 = (1u << 4)              // D format: f32
@@ -413,11 +425,6 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint6
       : "memory");
 }
 
-// Orders this thread's generic-proxy shared-memory writes before later
-// async-proxy (tensor core) reads.
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 
 // Four int8 (one word, lowest byte first) -> four bf16, exact.  Each byte,
 // offset to u = v + 128, is placed under the exponent of 2^23 (the float
@@ -442,24 +449,32 @@ __global__ void __launch_bounds__(kFThreads, 1)
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kFStages * kFStageBytes);
-  uint64_t* conv = full + kFStages;
-  uint64_t* empty = conv + kFStages;
-  uint64_t* tfull = empty + kFStages;
-  uint64_t* tempty = tfull + kAccBufs;
+  unsigned char* w8ring = smem;                        // [kFW8Slots][128][64] int8
+  unsigned char* sring = smem + kFW8Slots * kFWi8;     // [nS][bf16 weights | pieces]
+  uint64_t* full8 = reinterpret_cast<uint64_t*>(sring + kFSRing);
+  uint64_t* empty8 = full8 + kFW8Slots;
+  uint64_t* fullx = empty8 + kFW8Slots;
+  uint64_t* conv = fullx + kFMaxS;
+  uint64_t* empty = conv + kFMaxS;
+  uint64_t* tempty = empty + kFMaxS;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + kAccBufs);
   int* tile = reinterpret_cast<int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * kBN;
   const int nbk = a.K >> 5, kstages = a.K / kFK;
+  // the tile lookup, over group counts staged in shared memory (as in the int8 kernel)
+  int* scount = reinterpret_cast<int*>(sring);
+  if (a.counts)
+    for (int g = threadIdx.x; g < a.groups; g += blockDim.x) scount[g] = a.counts[g];
+  __syncthreads();
   if (threadIdx.x == 0) {
     int g = 0, r0 = blockIdx.y * kBM, rows = a.M - blockIdx.y * kBM;
     if (a.counts) {
       int t = blockIdx.y;
       rows = 0;
       for (g = 0; g < a.groups; ++g) {
-        const int c = a.counts[g], tiles = (c + kBM - 1) / kBM;
+        const int c = scount[g], tiles = (c + kBM - 1) / kBM;
         if (t < tiles) {
           r0 = a.offsets[g] + t * kBM;
           rows = c - t * kBM;
@@ -472,6 +487,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
     tile[1] = r0;
     tile[2] = rows > kBM ? kBM : rows;
   }
+  fence_proxy_async_smem();  // the scratch reads come before the copies that overwrite it
   __syncthreads();
   const int group = tile[0], row0 = tile[1], rows = tile[2];
   if (rows <= 0) return;
@@ -483,17 +499,22 @@ __global__ void __launch_bounds__(kFThreads, 1)
   const int box = rows <= 16 ? 16 : rows <= 32 ? 32 : 64;
   const int bufcols = 3 * box;
   const int nbuf = kTmemCols / bufcols < kAccBufs ? kTmemCols / bufcols : kAccBufs;  // 8, 5 or 2
+  // MMA-stage slots: bf16 weights then the pieces; 7, 5 or 4 of them
+  const int sbytes = kFWbf + 3 * box * 128;
+  const int ns_raw = kFSRing / sbytes;
+  const int nS = ns_raw < kFMaxS ? ns_raw : kFMaxS;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kFStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&conv[s], kFConvWarps);
-      mbar_init(&empty[s], 1);
+    for (int i = 0; i < kFW8Slots; ++i) {
+      mbar_init(&full8[i], 1);
+      mbar_init(&empty8[i], kFConvWarps);
     }
-    for (int b = 0; b < kAccBufs; ++b) {
-      mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], kEpiWarps);
+    for (int i = 0; i < kFMaxS; ++i) {
+      mbar_init(&fullx[i], 1);
+      mbar_init(&conv[i], kFConvWarps);
+      mbar_init(&empty[i], 1);
     }
+    for (int b = 0; b < kAccBufs; ++b) mbar_init(&tempty[b], kEpiWarps);
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(tmem_holder, kTmemCols);
@@ -503,41 +524,56 @@ __global__ void __launch_bounds__(kFThreads, 1)
   const uint32_t tmem = *tmem_holder;
 
   if (warp == 0) {
-    // ---- TMA producer
+    // ---- int8 weights: a deep ring whose slots free as soon as they are converted
     if (lane == 0) {
       const CUtensorMap* wmap = a.counts ? &a.maps[group].w_rows64 : &tmap_w;
-      const CUtensorMap* xmap = box == 16 ? &tmap_xp16 : box == 32 ? &tmap_xp32 : &tmap_xp;
-      const uint32_t tx = kFWi8 + 3 * box * 128;
       for (int ks = 0; ks < kstages; ++ks) {
-        const int s = ks % kFStages;
-        if (ks >= kFStages && !mbar_wait_spin(&empty[s], ((ks / kFStages) - 1) & 1, a.status)) break;
-        unsigned char* st = smem + s * kFStageBytes;
-        mbar_arrive_expect_tx(&full[s], tx);
-        tma_load_2d(st + kFWbf + 3 * kFXp, wmap, ks * kFK, n0, &full[s]);
+        const int w = ks % kFW8Slots;
+        if (ks >= kFW8Slots &&
+            !mbar_wait_spin(&empty8[w], ((ks / kFW8Slots) - 1) & 1, a.status))
+          break;
+        mbar_arrive_expect_tx(&full8[w], kFWi8);
+        tma_load_2d(w8ring + w * kFWi8, wmap, ks * kFK, n0, &full8[w]);
+      }
+    }
+  } else if (warp == 2) {
+    // ---- activation pieces into the MMA-stage slots
+    if (lane == 0) {
+      const CUtensorMap* xmap = box == 16 ? &tmap_xp16 : box == 32 ? &tmap_xp32 : &tmap_xp;
+      const uint32_t tx = 3 * box * 128;
+      int sl = 0, lap = 0;
+      for (int ks = 0; ks < kstages; ++ks) {
+        if (lap > 0 && !mbar_wait_spin(&empty[sl], (lap - 1) & 1, a.status)) break;
+        unsigned char* st = sring + sl * sbytes;
+        mbar_arrive_expect_tx(&fullx[sl], tx);
 #pragma unroll
         for (int p = 0; p < 3; ++p)
-          tma_load_2d(st + kFWbf + p * box * 128, xmap, ks * kFK, p * a.piece_rows + row0, &full[s]);
+          tma_load_2d(st + kFWbf + p * box * 128, xmap, ks * kFK, p * a.piece_rows + row0,
+                      &fullx[sl]);
+        if (++sl == nS) {
+          sl = 0;
+          ++lap;
+        }
       }
     }
   } else if (warp == 1) {
     // ---- MMA issuer: per q8 block, one MMA per 16 elements of K into the
-    // block's buffer (N = 3 * box: all pieces at once)
+    // block's buffer (N = 3 * box: all pieces at once); one commit per stage.
+    // Buffer and slot indices are kept incrementally (a division by a
+    // run-time count costs the issuing thread more than an MMA).
     if (lane == 0) {
       const uint32_t idesc = kIdescBf16 | (static_cast<uint32_t>(bufcols >> 3) << 17);
-      // buffer index and lap count kept incrementally: a division by the
-      // run-time nbuf costs the issuing thread more than an MMA
-      int buf = 0, lap = 0;
+      int buf = 0, blap = 0, sl = 0, lap = 0;
       bool ok = true;
       for (int ks = 0; ks < kstages && ok; ++ks) {
-        const int s = ks % kFStages;
-        ok = mbar_wait_spin(&full[s], (ks / kFStages) & 1, a.status) &&
-             mbar_wait_spin(&conv[s], (ks / kFStages) & 1, a.status);
+        ok = mbar_wait_spin(&fullx[sl], lap & 1, a.status) &&
+             mbar_wait_spin(&conv[sl], lap & 1, a.status);
         if (!ok) break;
         tc_fence_after();
-        const unsigned char* st = smem + s * kFStageBytes;
+        const unsigned char* st = sring + sl * sbytes;
         for (int j = 0; j < kFK / 32; ++j) {
-          if (lap > 0) {
-            ok = mbar_wait_spin(&tempty[buf], (lap - 1) & 1, a.status);
+          if (blap > 0) {
+            ok = mbar_wait_spin(&tempty[buf], (blap - 1) & 1, a.status);
             if (!ok) break;
             tc_fence_after();
           }
@@ -548,24 +584,30 @@ __global__ void __launch_bounds__(kFThreads, 1)
                      static_cast<uint32_t>(h));
           if (++buf == nbuf) {
             buf = 0;
-            ++lap;
+            ++blap;
           }
         }
-        // one commit per stage: it frees the slot and publishes both blocks
-        // (a commit costs the issuing thread far more than an MMA)
-        mma_commit(&empty[s]);
+        // frees the slot and publishes both blocks (commits cost more than MMAs)
+        mma_commit(&empty[sl]);
+        if (++sl == nS) {
+          sl = 0;
+          ++lap;
+        }
       }
     }
-  } else if (warp < 2 + kFConvWarps) {
-    // ---- int8 -> bf16 weights: thread ct converts 16-byte chunks ct, ct + 128, ...
-    // (row c / 4, elements 16 * (c % 4) ..) into the swizzled layout: row r's
-    // 16-byte unit j sits at (r / 8) * 1024 + (r % 8) * 128 + ((j ^ (r % 8)) * 16).
-    const int ct = threadIdx.x - 64;
+  } else if (warp < 3 + kFConvWarps) {
+    // ---- int8 -> bf16 weights, from the int8 ring into the stage slot: thread
+    // ct converts 16-byte chunks ct, ct + 32 * kFConvWarps, ... (row c / 4,
+    // elements 16 * (c % 4) ..) into the swizzled layout: row r's 16-byte unit
+    // j sits at (r / 8) * 1024 + (r % 8) * 128 + ((j ^ (r % 8)) * 16).
+    const int ct = threadIdx.x - 96;
+    int sl = 0, lap = 0;
     for (int ks = 0; ks < kstages; ++ks) {
-      const int s = ks % kFStages;
-      if (!mbar_wait_spin(&full[s], (ks / kFStages) & 1, a.status)) break;
-      unsigned char* st = smem + s * kFStageBytes;
-      const unsigned char* wi8 = st + kFWbf + 3 * kFXp;
+      const int w = ks % kFW8Slots;
+      if (!mbar_wait_spin(&full8[w], (ks / kFW8Slots) & 1, a.status)) break;
+      if (lap > 0 && !mbar_wait_spin(&empty[sl], (lap - 1) & 1, a.status)) break;
+      unsigned char* st = sring + sl * sbytes;
+      const unsigned char* wi8 = w8ring + w * kFWi8;
 #pragma unroll
       for (int i = 0; i < (kBN * kFK / 16) / (32 * kFConvWarps); ++i) {
         const int c = ct + 32 * kFConvWarps * i, r = c >> 2, q = c & 3;
@@ -578,12 +620,19 @@ __global__ void __launch_bounds__(kFThreads, 1)
       }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&conv[s]);
+      if (lane == 0) {
+        mbar_arrive(&empty8[w]);  // the int8 slot is read
+        mbar_arrive(&conv[sl]);
+      }
+      if (++sl == nS) {
+        sl = 0;
+        ++lap;
+      }
     }
   } else {
     // ---- epilogue: one weight row and 16 activation rows per thread; per
     // block, the three pieces' sums (smallest first) times the block scale
-    const int ew = warp - 2 - kFConvWarps;
+    const int ew = warp - 3 - kFConvWarps;
     const int q = warp & 3, part = ew / 4;
     const int rl = 32 * q + lane, n = n0 + rl, c0 = kEpiCols * part;
     const bool active = c0 < rows;  // warp-uniform
@@ -593,14 +642,13 @@ __global__ void __launch_bounds__(kFThreads, 1)
 #pragma unroll
     for (int i = 0; i < kEpiCols; ++i) acc[i] = 0.0f;
     bool ok = true;
-    int buf = 0;
+    int buf = 0, sl = 0, lap = 0;
     for (int b = 0; b < nbk; ++b) {
       const float sc = __ldg(srow + b);  // its latency hides behind the wait
-      // the stage's commit (its slot's `empty` phase): the MMA cannot run
-      // kFStages stages ahead of this warp (it waits for the TMEM buffers),
-      // so the phase waited for is the latest one
-      const int ks = b >> 1;
-      if (ok) ok = mbar_wait_try(&empty[ks % kFStages], (ks / kFStages) & 1, a.status);
+      // the stage's commit (its slot's `empty` phase): the MMA cannot
+      // complete this slot's next stage before this warp has released the
+      // stage's TMEM buffers, so the phase waited for is the latest one
+      if (ok) ok = mbar_wait_try(&empty[sl], lap & 1, a.status);
       tc_fence_after();
       // the two small pieces' sums first, then the leading piece's (two
       // rounds of loads keep the epilogue within the register budget)
@@ -626,6 +674,12 @@ __global__ void __launch_bounds__(kFThreads, 1)
           acc[c] = fmaf(__fadd_rn(__uint_as_float(ra[c]), __uint_as_float(rb[c])), sc, acc[c]);
       }
       if (++buf == nbuf) buf = 0;
+      if (b & 1) {
+        if (++sl == nS) {
+          sl = 0;
+          ++lap;
+        }
+      }
     }
     if (active) {
 #pragma unroll
