@@ -120,7 +120,8 @@ def cpu_rank(rank, world, port, case):
 def gpu_rank(rank, world, port, case):
     """NCCL rank: ExpertParallelMoe over the CUDA library, each rank on its own
     GPU.  Its output must equal the single-GPU layer's (uocr_moe_forward over
-    all experts on this rank's tokens) bit for bit, and the oracle's within
+    all experts on this rank's tokens) bit for bit with int8 activations and
+    within the FP32 tolerance with FP32 activations, and the oracle's within
     the MoE layer tolerances of the single-GPU tests."""
     import torch
     import torch.distributed as dist
@@ -151,7 +152,14 @@ def gpu_rank(rank, world, port, case):
             torch.cuda.synchronize()
             ctx.sync()
             y, ids, wts, y1 = y.cpu().numpy(), ids.cpu().numpy(), wts.cpu().numpy(), y1.cpu().numpy()
-            assert bits_equal(y, y1), (rank, mode)
+            if mode == 0:
+                # FP32 activations: an expert's kernel depends on its group's
+                # size, which differs between the owner's groups (rows of all
+                # ranks) and the single-GPU ones, so the FP32 order may too
+                scale0 = float(np.max(np.abs(y1)))
+                assert float(np.max(np.abs(y.astype(np.float64) - y1))) <= 1e-4 * scale0, rank
+            else:
+                assert bits_equal(y, y1), (rank, mode)
             ry, rids, rw = oracle.experts(shared, experts, logits, x, k, mode, norm, scale)
             assert np.array_equal(ids, rids), (rank, mode)
             d = np.abs(wts.view(np.int32).astype(np.int64) - rw.view(np.int32).astype(np.int64))

@@ -42,3 +42,13 @@ def random_q8(rng, rows, cols, lo=1e-4, hi=1e-2):
     w = rng.integers(-127, 128, size=(rows, cols), dtype=np.int8)
     s = rng.uniform(lo, hi, size=(rows, (cols + BLOCK - 1) // BLOCK)).astype(np.float32)
     return w, s
+
+
+def exact_linear(w, s, x):
+    """The exact product of x with the fp32-dequantized weights (w * s rounded
+    to fp32, as Int8Matrix::dequantize), computed in float64 and rounded once
+    to fp32 (a result below fp32's range is 0, as any fp32 evaluation gives)."""
+    w = np.asarray(w)
+    wd = (w.astype(np.float32) * np.repeat(np.asarray(s, np.float32), BLOCK, axis=1)[:, :w.shape[1]]
+          ).astype(np.float64)
+    return (np.asarray(x, np.float64).reshape(-1, w.shape[1]) @ wd.T).astype(np.float32)

@@ -277,7 +277,8 @@ def _parts_forward(ctx, layer, x_t, lg_t, mode, top_k, per_source=None):
 @pytest.mark.parametrize("shape", [(128, 64, 128, 8, 3), (256, 128, 256, 8, 2)])
 def test_parts_equal_forward(ctx, mode, shape):
     """route + expert_rows + shared_rows + combine == uocr_moe_forward, bit for
-    bit (both CUDA-core and tensor-core grouped projections)."""
+    bit in one call; split over three calls (as a multi-GPU dispatch), bit for
+    bit with int8 activations and within the FP32 tolerance otherwise."""
     import torch
     H, F, FS, E, k = shape
     rng = np.random.default_rng(300 + mode + H)
@@ -286,8 +287,14 @@ def test_parts_equal_forward(ctx, mode, shape):
     lg = torch.from_numpy(rng.standard_normal((41, E)).astype(np.float32)).cuda()
     y1 = layer.forward_device(x, lg, mode)
     y2, _, _ = _parts_forward(ctx, layer, x, lg, mode, k, per_source=3)
+    y3, _, _ = _parts_forward(ctx, layer, x, lg, mode, k)
     ctx.sync()
-    assert bits_equal(y1.cpu().numpy(), y2.cpu().numpy())
+    y1, y2, y3 = y1.cpu().numpy(), y2.cpu().numpy(), y3.cpu().numpy()
+    assert bits_equal(y1, y3)
+    if mode == 2:
+        assert bits_equal(y1, y2)
+    else:  # the split changes group sizes, hence kernels and FP32 order
+        assert float(np.max(np.abs(y1.astype(np.float64) - y2))) <= 1e-4 * float(np.max(np.abs(y1)))
 
 
 def test_parts_dynamic_groups_per_source(ctx):

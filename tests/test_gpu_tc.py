@@ -1,4 +1,5 @@
-"""Tensor-core paths of Int8Matrix for many rows (csrc/q8_tc.cu).
+"""Tensor-core paths of Int8Matrix for several rows (csrc/q8_tc.cu for more
+than 16 rows, csrc/q8_small.cu for 2..16).
 
 int8 activations: the reference applies Int8Matrix::linear_dynamic_int8
 (src/cpu/quantized.rs:155-236) row by row; the tensor-core kernel must
@@ -19,18 +20,10 @@ import numpy as np
 import pytest
 
 import oracle
-from helpers import bits_equal, random_q8, rel_err, terms_abs
+from helpers import bits_equal, exact_linear, random_q8, rel_err, terms_abs
 
 FP32_REL_TOL = 1e-4      # vs the exact product
 FP32_ORACLE_TOL = 2e-4   # vs the oracle's sequential FP32 sum
-
-
-def exact_linear(w, s, x):
-    """The exact product of x with the fp32-dequantized weights (w * s rounded
-    to fp32, as Int8Matrix::dequantize), computed in float64 and rounded once
-    to fp32 (a result below fp32's range is 0, as any fp32 evaluation gives)."""
-    wd = (w.astype(np.float32) * np.repeat(s, 32, axis=1)[:, :w.shape[1]]).astype(np.float64)
-    return (np.asarray(x, np.float64) @ wd.T).astype(np.float32)
 
 pytestmark = pytest.mark.gpu
 
@@ -45,9 +38,10 @@ def run_device(ctx, w, s, x):
     return y.cpu().numpy()
 
 
-@pytest.mark.parametrize("batch", [2, 16, 63, 64, 65, 128, 200])
-@pytest.mark.parametrize("rows,cols", [(128, 128), (896, 1280), (256, 896)])
+@pytest.mark.parametrize("batch", [2, 3, 7, 9, 16, 17, 63, 64, 65, 128, 200])
+@pytest.mark.parametrize("rows,cols", [(128, 128), (896, 1280), (256, 896), (1792, 1280), (1280, 1792)])
 def test_tc_dynamic_bit_exact(ctx, rows, cols, batch):
+    """2..16 rows: the warp-level kernel (s8 MMA per block); more: tcgen05."""
     rng = np.random.default_rng(rows * 7 + cols + batch)
     w, s = random_q8(rng, rows, cols)
     x = (rng.standard_normal((batch, cols)) * rng.uniform(0.1, 10, (batch, 1))).astype(np.float32)
@@ -89,8 +83,8 @@ def run_device_f32(ctx, w, s, x):
     return y.cpu().numpy(), m
 
 
-@pytest.mark.parametrize("batch", [8, 16, 63, 64, 65, 130, 512])
-@pytest.mark.parametrize("rows,cols", [(128, 128), (896, 1280), (1280, 896), (3840, 1280)])
+@pytest.mark.parametrize("batch", [2, 5, 8, 16, 17, 63, 64, 65, 130, 512])
+@pytest.mark.parametrize("rows,cols", [(128, 128), (896, 1280), (1280, 896), (3840, 1280), (1280, 1792)])
 def test_tc_fp32_linear_tolerance(ctx, rows, cols, batch):
     rng = np.random.default_rng(rows * 5 + cols + batch)
     w, s = random_q8(rng, rows, cols)
@@ -109,6 +103,7 @@ def test_tc_fp32_extremes(ctx):
     and subnormal scales."""
     rows, cols, batch = 256, 1280, 40
     rng = np.random.default_rng(77)
+    # (the same inputs through the warp-level kernel: see test_small_fp32_extremes)
     i = np.arange(rows * cols).reshape(rows, cols)
     w = ((i * 53) % 255 - 127).astype(np.int8)
     s = rng.uniform(1e-4, 1e-2, (rows, cols // 32)).astype(np.float32)
@@ -121,5 +116,23 @@ def test_tc_fp32_extremes(ctx):
     y, _ = run_device_f32(ctx, w, s, x)
     # magnitudes 10^-20 .. 10^20 within a row cancel: the oracle's sequential
     # sum is itself ~1e-2 from the exact product here, so only that is checked
+    assert rel_err(y, exact_linear(w, s, x), terms_abs(w, s, x)) <= FP32_REL_TOL
+    assert np.all(y[3] == 0)
+
+
+def test_small_fp32_extremes(ctx):
+    """The extremes of test_tc_fp32_extremes through the 2..16-row kernel."""
+    rows, cols, batch = 256, 1280, 12
+    rng = np.random.default_rng(78)
+    i = np.arange(rows * cols).reshape(rows, cols)
+    w = ((i * 53) % 255 - 127).astype(np.int8)
+    s = rng.uniform(1e-4, 1e-2, (rows, cols // 32)).astype(np.float32)
+    s[::5] = 1e-38
+    s[1::7] = 3e3
+    x = (rng.standard_normal((batch, cols)) * 10.0 ** rng.integers(-20, 20, (batch, cols))).astype(np.float32)
+    x[3] = 0.0
+    x[4] = np.float32(1e-41)
+    x[5, ::2] = 1e25
+    y, _ = run_device_f32(ctx, w, s, x)
     assert rel_err(y, exact_linear(w, s, x), terms_abs(w, s, x)) <= FP32_REL_TOL
     assert np.all(y[3] == 0)

@@ -452,25 +452,32 @@ static int dynamic_checks(const uocr_ctx* ctx, const uocr_q8* m) {
   return check_elements(ctx, m->cols * 2 + m->rows + nblocks(m->cols));
 }
 
-// Which kernel a linear of `batch` rows runs on: the GEMV kernels, or one of
-// the tensor-core GEMMs (every row int8-quantized, bit-exact; or FP32
-// activations as exact bf16 pieces, FP32 tolerance) when the shape allows.
-enum class LinearPath { Gemv, TcInt8, TcFp32 };
-constexpr size_t kTcFp32MinBatch = 8;
+// Which kernel a linear of `batch` rows runs on: the GEMV kernels for one
+// row; for 2..kSmallRowsMax rows the warp-level kernel that streams the
+// weights once; beyond that the tensor-core GEMMs.  int8 activations are
+// bit-exact on every path; FP32 activations go to the warp-level and
+// tensor-core kernels as exact bf16 pieces (FP32 tolerance).
+enum class LinearPath { Gemv, SmallInt8, SmallFp32, TcInt8, TcFp32 };
 
 static LinearPath linear_path(const uocr_q8* m, int mode, size_t batch) {
-  const bool tc = q8_tc_supported(static_cast<int>(m->rows), static_cast<int>(m->cols)) &&
-                  reinterpret_cast<uintptr_t>(m->w) % 16 == 0 &&
-                  reinterpret_cast<uintptr_t>(m->s) % 16 == 0;
-  if (mode == MODE_INT8) return batch > 1 && tc ? LinearPath::TcInt8 : LinearPath::Gemv;
-  return batch >= kTcFp32MinBatch && tc ? LinearPath::TcFp32 : LinearPath::Gemv;
+  const bool aligned = reinterpret_cast<uintptr_t>(m->w) % 16 == 0 &&
+                       reinterpret_cast<uintptr_t>(m->s) % 16 == 0;
+  const int rows = static_cast<int>(m->rows), cols = static_cast<int>(m->cols);
+  if (batch < 2 || !aligned) return LinearPath::Gemv;
+  if (batch <= static_cast<size_t>(kSmallRowsMax)) {
+    if (!small_rows_supported(rows, cols)) return LinearPath::Gemv;
+    return mode == MODE_INT8 ? LinearPath::SmallInt8 : LinearPath::SmallFp32;
+  }
+  if (!q8_tc_supported(rows, cols)) return LinearPath::Gemv;
+  return mode == MODE_INT8 ? LinearPath::TcInt8 : LinearPath::TcFp32;
 }
 
 static size_t al256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
 
 // Device scratch of a linear: quantized rows and their scales, or the pieces.
 static size_t linear_scratch_bytes(const uocr_q8* m, int mode, size_t batch) {
-  if (linear_path(m, mode, batch) == LinearPath::TcFp32)
+  const LinearPath path = linear_path(m, mode, batch);
+  if (path == LinearPath::TcFp32 || path == LinearPath::SmallFp32)
     return al256(3 * batch * m->cols * 2) + al256(batch * 4);
   if (mode == MODE_INT8) return al256(batch * m->cols) + al256(batch * nblocks(m->cols) * 4);
   return 0;
@@ -483,16 +490,22 @@ static int linear_launch(uocr_ctx* ctx, const uocr_q8* m, int mode, const float*
   const int b = static_cast<int>(batch);
   LinearPath path = linear_path(m, mode, batch);
   // the pieces are read as float4 rows
-  if (path == LinearPath::TcFp32 && reinterpret_cast<uintptr_t>(x_dev) % 16 != 0)
+  if ((path == LinearPath::TcFp32 || path == LinearPath::SmallFp32) &&
+      reinterpret_cast<uintptr_t>(x_dev) % 16 != 0)
     path = LinearPath::Gemv;
-  if (path == LinearPath::TcFp32) {
+  const Q8View v = view(m);
+  if (path == LinearPath::TcFp32 || path == LinearPath::SmallFp32) {
     uint16_t* pieces = reinterpret_cast<uint16_t*>(scratch);
     float* rinv = reinterpret_cast<float*>(scratch + al256(3 * batch * m->cols * 2));
     launch_split_rows(x_dev, static_cast<long long>(m->cols), nullptr, b, static_cast<int>(m->cols),
                       pieces, rinv, ctx->sms, ctx->stream);
-    const cudaError_t e = launch_q8_tc_single_f32(view(m), pieces, rinv, b, y_dev,
-                                                  static_cast<long long>(m->rows), ctx->status_dev,
-                                                  ctx->stream);
+    const cudaError_t e =
+        path == LinearPath::TcFp32
+            ? launch_q8_tc_single_f32(v, pieces, rinv, b, y_dev, static_cast<long long>(m->rows),
+                                      ctx->status_dev, ctx->stream)
+            : launch_small_rows(false, nullptr, &v, 0, nullptr, nullptr, 1, 1, b, v.rows, v.cols,
+                                pieces, b, rinv, nullptr, nullptr, y_dev,
+                                static_cast<long long>(m->rows), ctx->stream);
     if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "tensor-core linear: %s", cudaGetErrorString(e));
     return check_launch();
   }
@@ -502,17 +515,21 @@ static int linear_launch(uocr_ctx* ctx, const uocr_q8* m, int mode, const float*
     xq = reinterpret_cast<int8_t*>(scratch);
     xs = reinterpret_cast<float*>(scratch + al256(batch * m->cols));
   }
-  if (path == LinearPath::TcInt8) {
-    // many rows: quantize them, then the tensor-core GEMM (bit-exact)
+  if (path == LinearPath::TcInt8 || path == LinearPath::SmallInt8) {
+    // several rows: quantize them, then a tensor-core kernel (bit-exact)
     launch_quantize_rows(x_dev, static_cast<long long>(m->cols), b, static_cast<int>(m->cols), xq,
                          xs, ctx->status_dev, ctx->sms, ctx->stream);
-    const cudaError_t e = launch_q8_tc_single_i8(view(m), xq, xs, b, y_dev,
-                                                 static_cast<long long>(m->rows), ctx->status_dev,
-                                                 ctx->stream);
+    const cudaError_t e =
+        path == LinearPath::TcInt8
+            ? launch_q8_tc_single_i8(v, xq, xs, b, y_dev, static_cast<long long>(m->rows),
+                                     ctx->status_dev, ctx->stream)
+            : launch_small_rows(true, nullptr, &v, 0, nullptr, nullptr, 1, 1, b, v.rows, v.cols,
+                                nullptr, 0, nullptr, xq, xs, y_dev,
+                                static_cast<long long>(m->rows), ctx->stream);
     if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "tensor-core linear: %s", cudaGetErrorString(e));
     return check_launch();
   }
-  launch_gemv(mode, view(m), x_dev, static_cast<long long>(m->cols), b, y_dev,
+  launch_gemv(mode, v, x_dev, static_cast<long long>(m->cols), b, y_dev,
               static_cast<long long>(m->rows), xq, xs, ctx->status_dev, ctx->sms, ctx->stream);
   return check_launch();
 }

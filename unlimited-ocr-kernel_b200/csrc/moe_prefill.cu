@@ -381,8 +381,7 @@ struct PrefillWs {
   float* hr_r;
   float* xr_s;
   float* hr_s;
-  int* counts_i8;   // DynamicActivations: single-row groups (int8) and the rest (FP32)
-  int* counts_f32;
+  int* counts_big;  // tensor-core paths: groups of more than kSmallRowsMax rows
   size_t bytes;
 };
 
@@ -435,10 +434,8 @@ static PrefillWs carve(const MoePrefillArgs& a, void* base, Path path) {
     w.xq_p = reinterpret_cast<int8_t*>(take(P * H));
     w.xs_p = reinterpret_cast<float*>(take(sizeof(float) * P * blocks_of(a.hidden)));
   }
-  if (path == Path::TcMixed) {
-    w.counts_i8 = reinterpret_cast<int*>(take(sizeof(int) * (a.n_experts + 1)));
-    w.counts_f32 = reinterpret_cast<int*>(take(sizeof(int) * (a.n_experts + 1)));
-  }
+  if (path != Path::CudaCore)
+    w.counts_big = reinterpret_cast<int*>(take(sizeof(int) * (a.n_experts + 1)));
   if (path == Path::TcFp32 || path == Path::TcMixed) {
     w.xp_r = reinterpret_cast<uint16_t*>(take(2 * 3 * P * H));
     w.hp_r = reinterpret_cast<uint16_t*>(take(2 * 3 * P * F));
@@ -457,6 +454,36 @@ size_t moe_prefill_workspace(const MoePrefillArgs& a, int mode) {
   return carve(a, nullptr, prefill_path(a, mode)).bytes;
 }
 
+// counts_big[g] = counts[g] when it exceeds kSmallRowsMax, else 0 (the
+// tensor-core GEMMs take the big groups, the warp-level kernel the others).
+__global__ void big_counts_kernel(const int* __restrict__ counts, int groups,
+                                  int* __restrict__ counts_big) {
+  for (int g = threadIdx.x; g < groups; g += blockDim.x) {
+    const int c = counts[g];
+    counts_big[g] = c > kSmallRowsMax ? c : 0;
+  }
+}
+
+static void launch_big_counts(const int* counts, int groups, int* counts_big, cudaStream_t st) {
+  big_counts_kernel<<<1, 256, 0, st>>>(counts, groups, counts_big);
+}
+
+// The shared expert over T <= kSmallRowsMax tokens with FP32 activations (the
+// tokens' pieces are in w.xp_s / w.xr_s); its down projection writes y.
+static cudaError_t shared_small_f32(const MoePrefillArgs& a, const PrefillWs& w, int sms,
+                                    cudaStream_t st) {
+  const int T = a.tokens, H = a.hidden, FS = a.shared_width;
+  cudaError_t e;
+  if ((e = launch_small_rows(false, nullptr, &a.shared.gate, 0, nullptr, nullptr, 1, 1, T, FS, H,
+                             w.xp_s, T, w.xr_s, nullptr, nullptr, w.h_s, FS, st)) ||
+      (e = launch_small_rows(false, nullptr, &a.shared.up, 1, nullptr, nullptr, 1, 1, T, FS, H,
+                             w.xp_s, T, w.xr_s, nullptr, nullptr, w.u_s, FS, st)))
+    return e;
+  launch_swiglu_split(w.h_s, w.u_s, T, FS, w.hp_s, w.hr_s, sms, st);
+  return launch_small_rows(false, nullptr, &a.shared.down, 2, nullptr, nullptr, 1, 1, T, H, FS,
+                           w.hp_s, T, w.hr_s, nullptr, nullptr, a.y, H, st);
+}
+
 // FP32 activations, all projections on the tensor cores (exact bf16 pieces).
 static cudaError_t prefill_tc_f32(const MoePrefillArgs& a, const PrefillWs& w, int sms,
                                   cudaStream_t st) {
@@ -466,20 +493,28 @@ static cudaError_t prefill_tc_f32(const MoePrefillArgs& a, const PrefillWs& w, i
   const unsigned char* maps = static_cast<const unsigned char*>(a.tc_maps);
   const size_t mb = q8_tc_maps_bytes();
   cudaError_t e;
+  const int R = kSmallRowsMax;
   if (!a.skip_routed) {
+    launch_big_counts(w.counts, E, w.counts_big, st);
     launch_split_rows(a.x, H, w.pair_token, P, H, w.xp_r, w.xr_r, sms, st);
-    if ((e = launch_q8_tc_grouped_f32(maps, E, w.counts, w.offsets, max_tiles, F, H, w.xp_r,
-                                      w.xr_r, P, w.h_r, F, a.status, st)) ||
-        (e = launch_q8_tc_grouped_f32(maps + E * mb, E, w.counts, w.offsets, max_tiles, F, H,
-                                      w.xp_r, w.xr_r, P, w.u_r, F, a.status, st)))
-      return e;
+    for (int j = 0; j < 2; ++j) {  // gate, up
+      float* out = j == 0 ? w.h_r : w.u_r;
+      if ((e = launch_small_rows(false, a.experts, nullptr, j, w.counts, w.offsets, E, 1, R, F, H,
+                                 w.xp_r, P, w.xr_r, nullptr, nullptr, out, F, st)) ||
+          (e = launch_q8_tc_grouped_f32(maps + j * E * mb, E, w.counts_big, w.offsets, max_tiles,
+                                        F, H, w.xp_r, w.xr_r, P, out, F, a.status, st)))
+        return e;
+    }
     launch_swiglu_split(w.h_r, w.u_r, P, F, w.hp_r, w.hr_r, sms, st);
-    if ((e = launch_q8_tc_grouped_f32(maps + 2 * E * mb, E, w.counts, w.offsets, max_tiles, H, F,
-                                      w.hp_r, w.hr_r, P, w.out_r, H, a.status, st)))
+    if ((e = launch_small_rows(false, a.experts, nullptr, 2, w.counts, w.offsets, E, 1, R, H, F,
+                               w.hp_r, P, w.hr_r, nullptr, nullptr, w.out_r, H, st)) ||
+        (e = launch_q8_tc_grouped_f32(maps + 2 * E * mb, E, w.counts_big, w.offsets, max_tiles, H,
+                                      F, w.hp_r, w.hr_r, P, w.out_r, H, a.status, st)))
       return e;
   }
   if (a.skip_shared) return cudaSuccess;
   launch_split_rows(a.x, H, nullptr, T, H, w.xp_s, w.xr_s, sms, st);
+  if (T <= R) return shared_small_f32(a, w, sms, st);
   if ((e = launch_q8_tc_single_f32(a.shared.gate, w.xp_s, w.xr_s, T, w.h_s, FS, a.status, st)) ||
       (e = launch_q8_tc_single_f32(a.shared.up, w.xp_s, w.xr_s, T, w.u_s, FS, a.status, st)))
     return e;
@@ -495,21 +530,39 @@ static cudaError_t prefill_tc(const MoePrefillArgs& a, const PrefillWs& w, int s
   const unsigned char* maps = static_cast<const unsigned char*>(a.tc_maps);
   const size_t mb = q8_tc_maps_bytes();  // per matrix
   cudaError_t e;
+  const int R = kSmallRowsMax;
   if (!a.skip_routed) {
-    // routed experts: rows gathered per expert, gate and up, SwiGLU + quantize, down
+    // routed experts: rows gathered per expert; groups of <= R rows on the
+    // warp-level kernel, larger ones on the tensor-core GEMM
+    launch_big_counts(w.counts, E, w.counts_big, st);
     launch_gather_rows(w.xq, w.xs, w.pair_token, P, H, w.xq_p, w.xs_p, sms, st);
-    if ((e = launch_q8_tc_grouped_i8(maps, E, w.counts, w.offsets, max_tiles, F, H, w.xq_p,
-                                     w.xs_p, P, w.h_r, F, a.status, st)) ||
-        (e = launch_q8_tc_grouped_i8(maps + E * mb, E, w.counts, w.offsets, max_tiles, F, H,
-                                     w.xq_p, w.xs_p, P, w.u_r, F, a.status, st)))
-      return e;
+    for (int j = 0; j < 2; ++j) {  // gate, up
+      float* out = j == 0 ? w.h_r : w.u_r;
+      if ((e = launch_small_rows(true, a.experts, nullptr, j, w.counts, w.offsets, E, 1, R, F, H,
+                                 nullptr, 0, nullptr, w.xq_p, w.xs_p, out, F, st)) ||
+          (e = launch_q8_tc_grouped_i8(maps + j * E * mb, E, w.counts_big, w.offsets, max_tiles,
+                                       F, H, w.xq_p, w.xs_p, P, out, F, a.status, st)))
+        return e;
+    }
     launch_swiglu_quantize(w.h_r, w.u_r, P, F, w.hq_r, w.hs_r, a.status, sms, st);
-    if ((e = launch_q8_tc_grouped_i8(maps + 2 * E * mb, E, w.counts, w.offsets, max_tiles, H, F,
-                                     w.hq_r, w.hs_r, P, w.out_r, H, a.status, st)))
+    if ((e = launch_small_rows(true, a.experts, nullptr, 2, w.counts, w.offsets, E, 1, R, H, F,
+                               nullptr, 0, nullptr, w.hq_r, w.hs_r, w.out_r, H, st)) ||
+        (e = launch_q8_tc_grouped_i8(maps + 2 * E * mb, E, w.counts_big, w.offsets, max_tiles, H,
+                                     F, w.hq_r, w.hs_r, P, w.out_r, H, a.status, st)))
       return e;
   }
   if (a.skip_shared) return cudaSuccess;
   // shared expert over every token; its down projection writes y
+  if (T <= R) {
+    if ((e = launch_small_rows(true, nullptr, &a.shared.gate, 0, nullptr, nullptr, 1, 1, T, FS, H,
+                               nullptr, 0, nullptr, w.xq, w.xs, w.h_s, FS, st)) ||
+        (e = launch_small_rows(true, nullptr, &a.shared.up, 1, nullptr, nullptr, 1, 1, T, FS, H,
+                               nullptr, 0, nullptr, w.xq, w.xs, w.u_s, FS, st)))
+      return e;
+    launch_swiglu_quantize(w.h_s, w.u_s, T, FS, w.hq_s, w.hs_s, a.status, sms, st);
+    return launch_small_rows(true, nullptr, &a.shared.down, 2, nullptr, nullptr, 1, 1, T, H, FS,
+                             nullptr, 0, nullptr, w.hq_s, w.hs_s, a.y, H, st);
+  }
   if ((e = launch_q8_tc_single_i8(a.shared.gate, w.xq, w.xs, T, w.h_s, FS, a.status, st)) ||
       (e = launch_q8_tc_single_i8(a.shared.up, w.xq, w.xs, T, w.u_s, FS, a.status, st)))
     return e;
@@ -517,21 +570,12 @@ static cudaError_t prefill_tc(const MoePrefillArgs& a, const PrefillWs& w, int s
   return launch_q8_tc_single_i8(a.shared.down, w.hq_s, w.hs_s, T, a.y, H, a.status, st);
 }
 
-// counts_i8[g] = counts[g] if it is 1 else 0; counts_f32[g] = the others.
-__global__ void split_counts_kernel(const int* __restrict__ counts, int groups,
-                                    int* __restrict__ counts_i8, int* __restrict__ counts_f32) {
-  for (int g = threadIdx.x; g < groups; g += blockDim.x) {
-    const int c = counts[g];
-    counts_i8[g] = c == 1 ? 1 : 0;
-    counts_f32[g] = c == 1 ? 0 : c;
-  }
-}
-
 // QuantizationMode::DynamicActivations on the tensor cores: a group of one
-// row (src/decoder/mod.rs:103-106: projection of a single-row input) runs the
-// bit-exact int8 kernel, every other group the FP32 kernel; the two write
-// disjoint rows.  Both SwiGLU forms run over all rows (each down kernel reads
-// its own).  The shared expert sees every token: int8 for one token, else FP32.
+// row (src/decoder/mod.rs:103-106: projection of a single-row input) takes the
+// bit-exact int8 arithmetic, every other group FP32: groups of 2..R rows on
+// the warp-level kernel, larger ones on the FP32 GEMM; the launches write
+// disjoint rows.  Both SwiGLU forms run over all rows (each down projection
+// reads its own).  The shared expert sees every token: int8 for one token.
 static cudaError_t prefill_tc_mixed(const MoePrefillArgs& a, const PrefillWs& w, int sms,
                                     cudaStream_t st) {
   const int T = a.tokens, k = a.top_k, E = a.n_experts, P = T * k;
@@ -539,36 +583,45 @@ static cudaError_t prefill_tc_mixed(const MoePrefillArgs& a, const PrefillWs& w,
   const int max_tiles = P / 64 + E + 1;
   const unsigned char* maps = static_cast<const unsigned char*>(a.tc_maps);
   const size_t mb = q8_tc_maps_bytes();
+  const int R = kSmallRowsMax;
   cudaError_t e;
   if (!a.skip_routed) {
-    split_counts_kernel<<<1, 256, 0, st>>>(w.counts, E, w.counts_i8, w.counts_f32);
+    launch_big_counts(w.counts, E, w.counts_big, st);
     launch_gather_rows(w.xq, w.xs, w.pair_token, P, H, w.xq_p, w.xs_p, sms, st);
     launch_split_rows(a.x, H, w.pair_token, P, H, w.xp_r, w.xr_r, sms, st);
     for (int j = 0; j < 2; ++j) {  // gate, up
       float* out = j == 0 ? w.h_r : w.u_r;
-      if ((e = launch_q8_tc_grouped_i8(maps + j * E * mb, E, w.counts_i8, w.offsets, E + 1, F, H,
-                                       w.xq_p, w.xs_p, P, out, F, a.status, st)) ||
-          (e = launch_q8_tc_grouped_f32(maps + j * E * mb, E, w.counts_f32, w.offsets, max_tiles,
+      if ((e = launch_small_rows(true, a.experts, nullptr, j, w.counts, w.offsets, E, 1, 1, F, H,
+                                 nullptr, 0, nullptr, w.xq_p, w.xs_p, out, F, st)) ||
+          (e = launch_small_rows(false, a.experts, nullptr, j, w.counts, w.offsets, E, 2, R, F, H,
+                                 w.xp_r, P, w.xr_r, nullptr, nullptr, out, F, st)) ||
+          (e = launch_q8_tc_grouped_f32(maps + j * E * mb, E, w.counts_big, w.offsets, max_tiles,
                                         F, H, w.xp_r, w.xr_r, P, out, F, a.status, st)))
         return e;
     }
     launch_swiglu_quantize(w.h_r, w.u_r, P, F, w.hq_r, w.hs_r, a.status, sms, st);
     launch_swiglu_split(w.h_r, w.u_r, P, F, w.hp_r, w.hr_r, sms, st);
-    if ((e = launch_q8_tc_grouped_i8(maps + 2 * E * mb, E, w.counts_i8, w.offsets, E + 1, H, F,
-                                     w.hq_r, w.hs_r, P, w.out_r, H, a.status, st)) ||
-        (e = launch_q8_tc_grouped_f32(maps + 2 * E * mb, E, w.counts_f32, w.offsets, max_tiles, H,
+    if ((e = launch_small_rows(true, a.experts, nullptr, 2, w.counts, w.offsets, E, 1, 1, H, F,
+                               nullptr, 0, nullptr, w.hq_r, w.hs_r, w.out_r, H, st)) ||
+        (e = launch_small_rows(false, a.experts, nullptr, 2, w.counts, w.offsets, E, 2, R, H, F,
+                               w.hp_r, P, w.hr_r, nullptr, nullptr, w.out_r, H, st)) ||
+        (e = launch_q8_tc_grouped_f32(maps + 2 * E * mb, E, w.counts_big, w.offsets, max_tiles, H,
                                       F, w.hp_r, w.hr_r, P, w.out_r, H, a.status, st)))
       return e;
   }
   if (a.skip_shared) return cudaSuccess;
   if (T == 1) {
-    if ((e = launch_q8_tc_single_i8(a.shared.gate, w.xq, w.xs, T, w.h_s, FS, a.status, st)) ||
-        (e = launch_q8_tc_single_i8(a.shared.up, w.xq, w.xs, T, w.u_s, FS, a.status, st)))
+    if ((e = launch_small_rows(true, nullptr, &a.shared.gate, 0, nullptr, nullptr, 1, 1, 1, FS, H,
+                               nullptr, 0, nullptr, w.xq, w.xs, w.h_s, FS, st)) ||
+        (e = launch_small_rows(true, nullptr, &a.shared.up, 1, nullptr, nullptr, 1, 1, 1, FS, H,
+                               nullptr, 0, nullptr, w.xq, w.xs, w.u_s, FS, st)))
       return e;
     launch_swiglu_quantize(w.h_s, w.u_s, T, FS, w.hq_s, w.hs_s, a.status, sms, st);
-    return launch_q8_tc_single_i8(a.shared.down, w.hq_s, w.hs_s, T, a.y, H, a.status, st);
+    return launch_small_rows(true, nullptr, &a.shared.down, 2, nullptr, nullptr, 1, 1, 1, H, FS,
+                             nullptr, 0, nullptr, w.hq_s, w.hs_s, a.y, H, st);
   }
   launch_split_rows(a.x, H, nullptr, T, H, w.xp_s, w.xr_s, sms, st);
+  if (T <= R) return shared_small_f32(a, w, sms, st);
   if ((e = launch_q8_tc_single_f32(a.shared.gate, w.xp_s, w.xr_s, T, w.h_s, FS, a.status, st)) ||
       (e = launch_q8_tc_single_f32(a.shared.up, w.xp_s, w.xr_s, T, w.u_s, FS, a.status, st)))
     return e;

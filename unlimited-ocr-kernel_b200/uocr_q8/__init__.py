@@ -71,14 +71,27 @@ def _tptr(t) -> int:
 
 
 class GpuContext:
-    """Device, scratch limit and stream of a sequence of calls."""
+    """Device, scratch limit and stream of a sequence of calls.
 
-    def __init__(self, device: int = 0, scratch_limit: int = 1 << 34):
+    The device-tensor methods take torch tensors, so by default the context
+    runs on torch's current stream of its device (torch's caching allocator
+    may reuse a freed tensor's memory for work on that stream at once); pass
+    ``torch_stream=False`` to keep the library's own stream, then order it
+    against torch's with events or ``sync()``."""
+
+    def __init__(self, device: int = 0, scratch_limit: int = 1 << 34, torch_stream: bool = True):
         h = ctypes.c_void_p()
         _check(lib().uocr_ctx_create(int(device), int(scratch_limit), ctypes.byref(h)))
         self._h = h
         self.device = int(device)
         self.scratch_limit = int(scratch_limit)
+        if torch_stream:
+            try:
+                import torch
+                if torch.cuda.is_available():
+                    self.set_stream(torch.cuda.current_stream(self.device))
+            except ImportError:
+                pass
 
     @property
     def handle(self):
