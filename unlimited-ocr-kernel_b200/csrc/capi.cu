@@ -503,9 +503,9 @@ static int linear_launch(uocr_ctx* ctx, const uocr_q8* m, int mode, const float*
         path == LinearPath::TcFp32
             ? launch_q8_tc_single_f32(v, pieces, rinv, b, y_dev, static_cast<long long>(m->rows),
                                       ctx->status_dev, ctx->stream)
-            : launch_small_rows(false, nullptr, &v, 0, nullptr, nullptr, 1, 1, b, v.rows, v.cols,
-                                pieces, b, rinv, nullptr, nullptr, y_dev,
-                                static_cast<long long>(m->rows), ctx->stream);
+            : launch_small_rows(false, nullptr, &v, nullptr, nullptr, 1, 1, kSmallRowsMax, b,
+                                v.rows, v.cols, pieces, b, rinv, nullptr, nullptr, b, y_dev,
+                                static_cast<long long>(m->rows), ctx->status_dev, ctx->stream);
     if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "tensor-core linear: %s", cudaGetErrorString(e));
     return check_launch();
   }
@@ -523,9 +523,9 @@ static int linear_launch(uocr_ctx* ctx, const uocr_q8* m, int mode, const float*
         path == LinearPath::TcInt8
             ? launch_q8_tc_single_i8(v, xq, xs, b, y_dev, static_cast<long long>(m->rows),
                                      ctx->status_dev, ctx->stream)
-            : launch_small_rows(true, nullptr, &v, 0, nullptr, nullptr, 1, 1, b, v.rows, v.cols,
-                                nullptr, 0, nullptr, xq, xs, y_dev,
-                                static_cast<long long>(m->rows), ctx->stream);
+            : launch_small_rows(true, nullptr, &v, nullptr, nullptr, 1, 1, kSmallRowsMax, b,
+                                v.rows, v.cols, nullptr, 0, nullptr, xq, xs, b, y_dev,
+                                static_cast<long long>(m->rows), ctx->status_dev, ctx->stream);
     if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "tensor-core linear: %s", cudaGetErrorString(e));
     return check_launch();
   }

@@ -86,18 +86,19 @@ void launch_swiglu_quantize(const float* g, const float* u, int rows, int cols, 
                             float* hs, unsigned* status, int sms, cudaStream_t st);
 
 // q8_small.cu — grouped projections for groups of lo..hi rows (hi <=
-// kSmallRowsMax), weights streamed once per group, warp-level MMAs over the
-// group's rows.  int8: xq/xs rows (bit-exact linear_dynamic_int8); FP32:
-// pieces [3][piece_rows][K] + rinv (FP32 tolerance).  Grouped: matrix `proj`
-// (0 gate, 1 up, 2 down) of ffns[g], rows [offsets[g], + counts[g]); single
-// (ffns and counts null): *single over rows [0, hi).  N % 8 == 0, K % 128 == 0.
+// kSmallRowsMax), weights streamed once per group (TMA ring), warp-level MMAs
+// over the group's rows.  int8: xq/xs rows (bit-exact linear_dynamic_int8);
+// FP32: pieces [3][piece_rows][K] + rinv (FP32 tolerance).  Grouped: maps =
+// the groups' q8_tc_weight_maps, rows [offsets[g], + counts[g]); single
+// (counts null): *single over rows [0, total_rows) in groups of 16.  x_rows:
+// rows of the int8 activation tensors.  N % 128 == 0, K % 128 == 0.
 constexpr int kSmallRowsMax = 16;
 bool small_rows_supported(int N, int K);
-cudaError_t launch_small_rows(bool int8, const FfnView* ffns, const Q8View* single, int proj,
-                              const int* counts, const int* offsets, int groups, int lo, int hi,
-                              int N, int K, const uint16_t* pieces, long long piece_rows,
-                              const float* rinv, const int8_t* xq, const float* xs, float* y,
-                              long long ldy, cudaStream_t st);
+cudaError_t launch_small_rows(bool int8, const void* maps, const Q8View* single, const int* counts,
+                              const int* offsets, int groups, int lo, int hi, int total_rows, int N,
+                              int K, const uint16_t* pieces, int piece_rows, const float* rinv,
+                              const int8_t* xq, const float* xs, int x_rows, float* y,
+                              long long ldy, unsigned* status, cudaStream_t st);
 
 // moe_route.cu — moe::route for `tokens` rows of logits.  ids/weights are
 // tokens*top_k in the reference's order (probability desc, id asc).

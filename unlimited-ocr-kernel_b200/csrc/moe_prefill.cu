@@ -454,6 +454,10 @@ size_t moe_prefill_workspace(const MoePrefillArgs& a, int mode) {
   return carve(a, nullptr, prefill_path(a, mode)).bytes;
 }
 
+// Token counts up to which the shared expert (one matrix, every token) runs on
+// the warp-level kernel: its tcgen05 tiles would occupy only N / 128 SMs.
+constexpr int kSmallShared = 64;
+
 // counts_big[g] = counts[g] when it exceeds kSmallRowsMax, else 0 (the
 // tensor-core GEMMs take the big groups, the warp-level kernel the others).
 __global__ void big_counts_kernel(const int* __restrict__ counts, int groups,
@@ -468,20 +472,24 @@ static void launch_big_counts(const int* counts, int groups, int* counts_big, cu
   big_counts_kernel<<<1, 256, 0, st>>>(counts, groups, counts_big);
 }
 
-// The shared expert over T <= kSmallRowsMax tokens with FP32 activations (the
-// tokens' pieces are in w.xp_s / w.xr_s); its down projection writes y.
+// The shared expert over T <= kSmallShared tokens with FP32 activations, as
+// groups of 16 rows on the warp-level kernel (the tokens' pieces are in
+// w.xp_s / w.xr_s); its down projection writes y.
 static cudaError_t shared_small_f32(const MoePrefillArgs& a, const PrefillWs& w, int sms,
                                     cudaStream_t st) {
   const int T = a.tokens, H = a.hidden, FS = a.shared_width;
   cudaError_t e;
-  if ((e = launch_small_rows(false, nullptr, &a.shared.gate, 0, nullptr, nullptr, 1, 1, T, FS, H,
-                             w.xp_s, T, w.xr_s, nullptr, nullptr, w.h_s, FS, st)) ||
-      (e = launch_small_rows(false, nullptr, &a.shared.up, 1, nullptr, nullptr, 1, 1, T, FS, H,
-                             w.xp_s, T, w.xr_s, nullptr, nullptr, w.u_s, FS, st)))
+  if ((e = launch_small_rows(false, nullptr, &a.shared.gate, nullptr, nullptr, 1, 1, kSmallRowsMax, T, FS,
+                             H, w.xp_s, T, w.xr_s, nullptr, nullptr, T, w.h_s, FS,
+                             a.status, st)) ||
+      (e = launch_small_rows(false, nullptr, &a.shared.up, nullptr, nullptr, 1, 1, kSmallRowsMax, T, FS,
+                             H, w.xp_s, T, w.xr_s, nullptr, nullptr, T, w.u_s, FS,
+                             a.status, st)))
     return e;
   launch_swiglu_split(w.h_s, w.u_s, T, FS, w.hp_s, w.hr_s, sms, st);
-  return launch_small_rows(false, nullptr, &a.shared.down, 2, nullptr, nullptr, 1, 1, T, H, FS,
-                           w.hp_s, T, w.hr_s, nullptr, nullptr, a.y, H, st);
+  return launch_small_rows(false, nullptr, &a.shared.down, nullptr, nullptr, 1, 1, kSmallRowsMax, T, H,
+                             FS, w.hp_s, T, w.hr_s, nullptr, nullptr, T, a.y, H,
+                             a.status, st);
 }
 
 // FP32 activations, all projections on the tensor cores (exact bf16 pieces).
@@ -499,22 +507,24 @@ static cudaError_t prefill_tc_f32(const MoePrefillArgs& a, const PrefillWs& w, i
     launch_split_rows(a.x, H, w.pair_token, P, H, w.xp_r, w.xr_r, sms, st);
     for (int j = 0; j < 2; ++j) {  // gate, up
       float* out = j == 0 ? w.h_r : w.u_r;
-      if ((e = launch_small_rows(false, a.experts, nullptr, j, w.counts, w.offsets, E, 1, R, F, H,
-                                 w.xp_r, P, w.xr_r, nullptr, nullptr, out, F, st)) ||
+      if ((e = launch_small_rows(false, maps + j * E * mb, nullptr, w.counts, w.offsets, E, 1, R, 0, F,
+                                 H, w.xp_r, P, w.xr_r, nullptr, nullptr, P, out, F,
+                                 a.status, st)) ||
           (e = launch_q8_tc_grouped_f32(maps + j * E * mb, E, w.counts_big, w.offsets, max_tiles,
                                         F, H, w.xp_r, w.xr_r, P, out, F, a.status, st)))
         return e;
     }
     launch_swiglu_split(w.h_r, w.u_r, P, F, w.hp_r, w.hr_r, sms, st);
-    if ((e = launch_small_rows(false, a.experts, nullptr, 2, w.counts, w.offsets, E, 1, R, H, F,
-                               w.hp_r, P, w.hr_r, nullptr, nullptr, w.out_r, H, st)) ||
+    if ((e = launch_small_rows(false, maps + 2 * E * mb, nullptr, w.counts, w.offsets, E, 1, R, 0, H,
+                                 F, w.hp_r, P, w.hr_r, nullptr, nullptr, P, w.out_r, H,
+                                 a.status, st)) ||
         (e = launch_q8_tc_grouped_f32(maps + 2 * E * mb, E, w.counts_big, w.offsets, max_tiles, H,
                                       F, w.hp_r, w.hr_r, P, w.out_r, H, a.status, st)))
       return e;
   }
   if (a.skip_shared) return cudaSuccess;
   launch_split_rows(a.x, H, nullptr, T, H, w.xp_s, w.xr_s, sms, st);
-  if (T <= R) return shared_small_f32(a, w, sms, st);
+  if (T <= kSmallShared) return shared_small_f32(a, w, sms, st);
   if ((e = launch_q8_tc_single_f32(a.shared.gate, w.xp_s, w.xr_s, T, w.h_s, FS, a.status, st)) ||
       (e = launch_q8_tc_single_f32(a.shared.up, w.xp_s, w.xr_s, T, w.u_s, FS, a.status, st)))
     return e;
@@ -538,30 +548,35 @@ static cudaError_t prefill_tc(const MoePrefillArgs& a, const PrefillWs& w, int s
     launch_gather_rows(w.xq, w.xs, w.pair_token, P, H, w.xq_p, w.xs_p, sms, st);
     for (int j = 0; j < 2; ++j) {  // gate, up
       float* out = j == 0 ? w.h_r : w.u_r;
-      if ((e = launch_small_rows(true, a.experts, nullptr, j, w.counts, w.offsets, E, 1, R, F, H,
-                                 nullptr, 0, nullptr, w.xq_p, w.xs_p, out, F, st)) ||
+      if ((e = launch_small_rows(true, maps + j * E * mb, nullptr, w.counts, w.offsets, E, 1, R, 0, F,
+                                 H, nullptr, 0, nullptr, w.xq_p, w.xs_p, P, out, F,
+                                 a.status, st)) ||
           (e = launch_q8_tc_grouped_i8(maps + j * E * mb, E, w.counts_big, w.offsets, max_tiles,
                                        F, H, w.xq_p, w.xs_p, P, out, F, a.status, st)))
         return e;
     }
     launch_swiglu_quantize(w.h_r, w.u_r, P, F, w.hq_r, w.hs_r, a.status, sms, st);
-    if ((e = launch_small_rows(true, a.experts, nullptr, 2, w.counts, w.offsets, E, 1, R, H, F,
-                               nullptr, 0, nullptr, w.hq_r, w.hs_r, w.out_r, H, st)) ||
+    if ((e = launch_small_rows(true, maps + 2 * E * mb, nullptr, w.counts, w.offsets, E, 1, R, 0, H,
+                                 F, nullptr, 0, nullptr, w.hq_r, w.hs_r, P, w.out_r, H,
+                                 a.status, st)) ||
         (e = launch_q8_tc_grouped_i8(maps + 2 * E * mb, E, w.counts_big, w.offsets, max_tiles, H,
                                      F, w.hq_r, w.hs_r, P, w.out_r, H, a.status, st)))
       return e;
   }
   if (a.skip_shared) return cudaSuccess;
   // shared expert over every token; its down projection writes y
-  if (T <= R) {
-    if ((e = launch_small_rows(true, nullptr, &a.shared.gate, 0, nullptr, nullptr, 1, 1, T, FS, H,
-                               nullptr, 0, nullptr, w.xq, w.xs, w.h_s, FS, st)) ||
-        (e = launch_small_rows(true, nullptr, &a.shared.up, 1, nullptr, nullptr, 1, 1, T, FS, H,
-                               nullptr, 0, nullptr, w.xq, w.xs, w.u_s, FS, st)))
+  if (T <= kSmallShared) {
+    if ((e = launch_small_rows(true, nullptr, &a.shared.gate, nullptr, nullptr, 1, 1, kSmallRowsMax, T, FS,
+                             H, nullptr, 0, nullptr, w.xq, w.xs, T, w.h_s, FS,
+                             a.status, st)) ||
+        (e = launch_small_rows(true, nullptr, &a.shared.up, nullptr, nullptr, 1, 1, kSmallRowsMax, T, FS,
+                             H, nullptr, 0, nullptr, w.xq, w.xs, T, w.u_s, FS,
+                             a.status, st)))
       return e;
     launch_swiglu_quantize(w.h_s, w.u_s, T, FS, w.hq_s, w.hs_s, a.status, sms, st);
-    return launch_small_rows(true, nullptr, &a.shared.down, 2, nullptr, nullptr, 1, 1, T, H, FS,
-                             nullptr, 0, nullptr, w.hq_s, w.hs_s, a.y, H, st);
+    return launch_small_rows(true, nullptr, &a.shared.down, nullptr, nullptr, 1, 1, kSmallRowsMax, T, H,
+                             FS, nullptr, 0, nullptr, w.hq_s, w.hs_s, T, a.y, H,
+                             a.status, st);
   }
   if ((e = launch_q8_tc_single_i8(a.shared.gate, w.xq, w.xs, T, w.h_s, FS, a.status, st)) ||
       (e = launch_q8_tc_single_i8(a.shared.up, w.xq, w.xs, T, w.u_s, FS, a.status, st)))
@@ -591,37 +606,44 @@ static cudaError_t prefill_tc_mixed(const MoePrefillArgs& a, const PrefillWs& w,
     launch_split_rows(a.x, H, w.pair_token, P, H, w.xp_r, w.xr_r, sms, st);
     for (int j = 0; j < 2; ++j) {  // gate, up
       float* out = j == 0 ? w.h_r : w.u_r;
-      if ((e = launch_small_rows(true, a.experts, nullptr, j, w.counts, w.offsets, E, 1, 1, F, H,
-                                 nullptr, 0, nullptr, w.xq_p, w.xs_p, out, F, st)) ||
-          (e = launch_small_rows(false, a.experts, nullptr, j, w.counts, w.offsets, E, 2, R, F, H,
-                                 w.xp_r, P, w.xr_r, nullptr, nullptr, out, F, st)) ||
+      if ((e = launch_small_rows(true, maps + j * E * mb, nullptr, w.counts, w.offsets, E, 1, 1, 0, F,
+                                 H, nullptr, 0, nullptr, w.xq_p, w.xs_p, P, out, F,
+                                 a.status, st)) ||
+          (e = launch_small_rows(false, maps + j * E * mb, nullptr, w.counts, w.offsets, E, 2, R, 0, F,
+                                 H, w.xp_r, P, w.xr_r, nullptr, nullptr, P, out, F,
+                                 a.status, st)) ||
           (e = launch_q8_tc_grouped_f32(maps + j * E * mb, E, w.counts_big, w.offsets, max_tiles,
                                         F, H, w.xp_r, w.xr_r, P, out, F, a.status, st)))
         return e;
     }
     launch_swiglu_quantize(w.h_r, w.u_r, P, F, w.hq_r, w.hs_r, a.status, sms, st);
     launch_swiglu_split(w.h_r, w.u_r, P, F, w.hp_r, w.hr_r, sms, st);
-    if ((e = launch_small_rows(true, a.experts, nullptr, 2, w.counts, w.offsets, E, 1, 1, H, F,
-                               nullptr, 0, nullptr, w.hq_r, w.hs_r, w.out_r, H, st)) ||
-        (e = launch_small_rows(false, a.experts, nullptr, 2, w.counts, w.offsets, E, 2, R, H, F,
-                               w.hp_r, P, w.hr_r, nullptr, nullptr, w.out_r, H, st)) ||
+    if ((e = launch_small_rows(true, maps + 2 * E * mb, nullptr, w.counts, w.offsets, E, 1, 1, 0, H,
+                                 F, nullptr, 0, nullptr, w.hq_r, w.hs_r, P, w.out_r, H,
+                                 a.status, st)) ||
+        (e = launch_small_rows(false, maps + 2 * E * mb, nullptr, w.counts, w.offsets, E, 2, R, 0, H,
+                                 F, w.hp_r, P, w.hr_r, nullptr, nullptr, P, w.out_r, H,
+                                 a.status, st)) ||
         (e = launch_q8_tc_grouped_f32(maps + 2 * E * mb, E, w.counts_big, w.offsets, max_tiles, H,
                                       F, w.hp_r, w.hr_r, P, w.out_r, H, a.status, st)))
       return e;
   }
   if (a.skip_shared) return cudaSuccess;
   if (T == 1) {
-    if ((e = launch_small_rows(true, nullptr, &a.shared.gate, 0, nullptr, nullptr, 1, 1, 1, FS, H,
-                               nullptr, 0, nullptr, w.xq, w.xs, w.h_s, FS, st)) ||
-        (e = launch_small_rows(true, nullptr, &a.shared.up, 1, nullptr, nullptr, 1, 1, 1, FS, H,
-                               nullptr, 0, nullptr, w.xq, w.xs, w.u_s, FS, st)))
+    if ((e = launch_small_rows(true, nullptr, &a.shared.gate, nullptr, nullptr, 1, 1, 1, 1, FS,
+                             H, nullptr, 0, nullptr, w.xq, w.xs, T, w.h_s, FS,
+                             a.status, st)) ||
+        (e = launch_small_rows(true, nullptr, &a.shared.up, nullptr, nullptr, 1, 1, 1, 1, FS,
+                             H, nullptr, 0, nullptr, w.xq, w.xs, T, w.u_s, FS,
+                             a.status, st)))
       return e;
     launch_swiglu_quantize(w.h_s, w.u_s, T, FS, w.hq_s, w.hs_s, a.status, sms, st);
-    return launch_small_rows(true, nullptr, &a.shared.down, 2, nullptr, nullptr, 1, 1, 1, H, FS,
-                             nullptr, 0, nullptr, w.hq_s, w.hs_s, a.y, H, st);
+    return launch_small_rows(true, nullptr, &a.shared.down, nullptr, nullptr, 1, 1, 1, 1, H,
+                             FS, nullptr, 0, nullptr, w.hq_s, w.hs_s, T, a.y, H,
+                             a.status, st);
   }
   launch_split_rows(a.x, H, nullptr, T, H, w.xp_s, w.xr_s, sms, st);
-  if (T <= R) return shared_small_f32(a, w, sms, st);
+  if (T <= kSmallShared) return shared_small_f32(a, w, sms, st);
   if ((e = launch_q8_tc_single_f32(a.shared.gate, w.xp_s, w.xr_s, T, w.h_s, FS, a.status, st)) ||
       (e = launch_q8_tc_single_f32(a.shared.up, w.xp_s, w.xr_s, T, w.u_s, FS, a.status, st)))
     return e;

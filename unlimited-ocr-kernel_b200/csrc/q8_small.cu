@@ -9,11 +9,19 @@
 // its own warp-level MMAs over the group's rows, so the instruction cost is
 // spread over the SM and the weights stream at memory speed.
 //
-// Layout: a CTA of 4 warps owns 128 weight rows of one group's matrix; a warp
-// owns 32 of them as four n8 tiles; the group's rows (<= 16, the MMA's M) are
-// the A operand.  Within each 32-wide q8 block K is permuted consistently for
-// A and B (a product over K does not depend on the order) so that lane
-// (g = lane / 4, q = lane % 4) needs only bytes [8q, 8q + 8) of its rows:
+// A CTA owns 128 weight rows of one group's matrix.  Its producer lane moves
+// each 128-wide slice of K into a ring of shared-memory stages with TMA: the
+// weights' int8 tile [128][128] (128-byte swizzle), their block scales
+// [128][4], and the group's 16 activation rows (the three bf16 pieces
+// [16][128] each, or int8 rows [16][128] and their scales [16][4]); rows past
+// the group read as other rows or as zeros and are never stored.  Four warps
+// compute: a warp owns 32 weight rows as four n8 tiles (eight warps of two
+// tiles measured slower: the activation fragments, shared by every warp, are
+// read from shared memory once per warp); the group's rows (the MMA's M) are
+// the A operand.  Within each 32-wide q8 block K is permuted
+// consistently for A and B (a product over K does not depend on the order) so
+// that lane (g = lane / 4, q = lane % 4) needs only elements [8q, 8q + 8) of
+// the block in its rows:
 //   bf16 m16n8k16, step j in {0, 1}: logical k in {2q, 2q+1} <- physical
 //     8q + 4j + {0, 1}; {2q+8, 2q+9} <- 8q + 4j + {2, 3};
 //   s8 m16n8k32 (one step): logical 4q + i <- physical 8q + i, 4q + 16 + i <-
@@ -26,32 +34,44 @@
 // int8 activations (linear_dynamic_int8, bit-exact): the s8 MMA gives the
 // exact int32 block sum S; then acc = acc + ((float)S * ws) * xs block by
 // block from -0.0, one IEEE rounding per operation, as the reference.
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.h"
+#include "tc_maps.cuh"
 
 namespace uocr {
 
 namespace {
 
-constexpr int kSmallWarps = 4;
-constexpr int kSmallCtaRows = 32 * kSmallWarps;  // weight rows per CTA
+constexpr int kSmWarps = 4;                         // consumer warps
+constexpr int kSmTiles = 4;                         // n8 tiles of weight rows per warp
+constexpr int kSmThreads = 32 * (kSmWarps + 1);     // + the producer warp
+constexpr int kSmRows = 8 * kSmTiles * kSmWarps;    // weight rows per CTA (128)
+constexpr int kSmK = 128;                           // K per stage (4 q8 blocks)
+constexpr int kSmStages = 6;
+constexpr int kSmW = kSmRows * kSmK;                // 16 KB int8 weights
+constexpr int kSmWs = kSmRows * 4 * 4;              // 2 KB weight scales
+constexpr int kSmXp = 16 * kSmK * 2;                // 4 KB per bf16 piece tile
+constexpr int kSmXq = 16 * kSmK;                    // 2 KB int8 rows
+constexpr int kSmXs = 16 * 4 * 4;                   // 256 B activation scales
+constexpr int kSmStageF = kSmW + kSmWs + 3 * kSmXp;          // 30 KB
+constexpr int kSmStageI = 21 * 1024;                         // 16 + 2 + 2 + 0.25 KB, padded
+constexpr int kSmSmemF = kSmStages * kSmStageF + 1024 + 256;
+constexpr int kSmSmemI = kSmStages * kSmStageI + 1024 + 256;
+static_assert(kSmStageF % 1024 == 0 && kSmStageI % 1024 == 0, "swizzled tiles: 1024-byte stages");
+static_assert(kSmW + kSmWs + kSmXq + kSmXs <= kSmStageI, "int8 stage layout");
 
 struct SmallArgs {
-  const FfnView* ffns;  // grouped: device [groups]; nullptr: `single`
-  Q8View single;
-  int proj;  // 0 gate, 1 up, 2 down
-  const int* counts;
+  const TcMatrixMaps* maps;  // grouped: device [groups]; nullptr: the single maps
+  const int* counts;         // grouped: rows per group; nullptr: total_rows in groups of 16
   const int* offsets;
-  int groups;
-  int lo, hi;  // groups with lo <= count <= hi
-  int N, K;
-  const uint16_t* pieces;  // FP32 mode: [3][piece_rows][K] bf16
-  long long piece_elems;
+  int groups, lo, hi, total_rows;
+  int N, K, piece_rows;
   const float* rinv;
-  const int8_t* xq;  // int8 mode: [rows][K], scales [rows][K / 32]
-  const float* xs;
   float* y;
   long long ldy;
+  unsigned* status;
 };
 
 __device__ __forceinline__ void mma_bf16_m16n8k16(float (&d)[4], uint32_t a0, uint32_t a1,
@@ -73,7 +93,9 @@ __device__ __forceinline__ void mma_s8_m16n8k32(int (&d)[4], uint32_t a0, uint32
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Four int8 (one word) -> four bf16 (two words), exact (see q8_tc.cu).
+// Four int8 (one word) -> four bf16 (two words), exact: each byte, offset to
+// u = v + 128, is placed under the exponent of 2^23; subtracting 2^23 + 128
+// leaves v, whose bf16 is the float's high half.
 __device__ __forceinline__ uint2 i8x4_bf16(uint32_t w) {
   const uint32_t u = w ^ 0x80808080u;
   const float magic = 8388736.0f;  // 2^23 + 128
@@ -85,165 +107,253 @@ __device__ __forceinline__ uint2 i8x4_bf16(uint32_t w) {
                     __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632));
 }
 
-__device__ __forceinline__ const Q8View& small_matrix(const SmallArgs& a, int g) {
-  if (!a.ffns) return a.single;
-  const FfnView& f = a.ffns[g];
-  return a.proj == 0 ? f.gate : a.proj == 1 ? f.up : f.down;
-}
-
 template <bool INT8>
-__global__ void __launch_bounds__(32 * kSmallWarps) small_rows_kernel(const __grid_constant__ SmallArgs a) {
-  const int g = blockIdx.y;
-  const int count = a.counts ? a.counts[g] : a.hi;
-  if (count < a.lo || count > a.hi || count < 1) return;
-  const int off = a.counts ? a.offsets[g] : 0;
-  const Q8View m = small_matrix(a, g);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int gq = lane >> 2, q = lane & 3;
-  const int n0 = blockIdx.x * kSmallCtaRows + 32 * warp;
-  if (n0 >= a.N) return;
-  const int K = a.K, nb = K >> 5;
-  // this lane's weight rows (B columns) for the four n8 tiles, clamped for loads
-  const int8_t* wrow[4];
-#pragma unroll
-  for (int t = 0; t < 4; ++t) {
-    const int r = n0 + 8 * t + gq;
-    wrow[t] = m.w + static_cast<long long>(r < a.N ? r : a.N - 1) * K + 8 * q;
-  }
-  // this lane's scale rows: output columns 2q, 2q + 1 of each tile (offsets
-  // from m.s; tile t adds 8 * t rows)
-  const int sr0 = n0 + 2 * q;
-  // this lane's activation rows (A rows gq and gq + 8), clamped into the group
-  const int i0 = gq < count ? gq : 0, i1 = gq + 8 < count ? gq + 8 : 0;
-  const long long row0 = off + i0, row1 = off + i1;
+__global__ void __launch_bounds__(kSmThreads, 1)
+    small_rows_kernel(const __grid_constant__ CUtensorMap tw,   // single: weights
+                      const __grid_constant__ CUtensorMap tws,  // single: weight scales
+                      const __grid_constant__ CUtensorMap tx,   // pieces, or int8 rows
+                      const __grid_constant__ CUtensorMap txs,  // int8 row scales
+                      const SmallArgs a) {
+  constexpr int kStage = INT8 ? kSmStageI : kSmStageF;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kSmStages * kStage);
+  uint64_t* empty = full + kSmStages;
 
-  float acc[4][4];
+  const int g = blockIdx.y;
+  int count, off;
+  if (a.counts) {
+    count = a.counts[g];
+    off = a.offsets[g];
+  } else {
+    off = 16 * g;
+    count = a.total_rows - off < 16 ? a.total_rows - off : 16;
+  }
+  if (count < a.lo || count > a.hi || count < 1) return;
+  const int n0 = blockIdx.x * kSmRows;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kstages = a.K / kSmK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSmStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kSmWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ---- producer
+    if (lane == 0) {
+      const CUtensorMap* wmap = a.maps ? &a.maps[g].w_sw128 : &tw;
+      const CUtensorMap* smap = a.maps ? &a.maps[g].ws : &tws;
+      const uint32_t tx_bytes = INT8 ? kSmW + kSmWs + kSmXq + kSmXs : kSmW + kSmWs + 3 * kSmXp;
+      for (int ks = 0; ks < kstages; ++ks) {
+        const int s = ks % kSmStages;
+        if (ks >= kSmStages && !mbar_wait_spin(&empty[s], ((ks / kSmStages) - 1) & 1, a.status))
+          break;
+        unsigned char* st = smem + s * kStage;
+        mbar_arrive_expect_tx(&full[s], tx_bytes);
+        tma_load_2d(st, wmap, ks * kSmK, n0, &full[s]);
+        tma_load_2d(st + kSmW, smap, ks * 4, n0, &full[s]);
+        if (INT8) {
+          tma_load_2d(st + kSmW + kSmWs, &tx, ks * kSmK, off, &full[s]);
+          tma_load_2d(st + kSmW + kSmWs + kSmXq, &txs, ks * 4, off, &full[s]);
+        } else {
 #pragma unroll
-  for (int t = 0; t < 4; ++t)
+          for (int p = 0; p < 3; ++p)
+            tma_load_2d(st + kSmW + kSmWs + p * kSmXp, &tx, ks * kSmK, p * a.piece_rows + off,
+                        &full[s]);
+        }
+      }
+    }
+    return;
+  }
+
+  // ---- consumers: warp cw owns weight rows wr0 .. wr0 + 8 kSmTiles - 1 of the tile
+  const int cw = warp - 1, gq = lane >> 2, q = lane & 3;
+  const int wr0 = 8 * kSmTiles * cw;
+  const int i0 = gq, i1 = gq + 8;  // A rows (the group's rows gq, gq + 8)
+  float acc[kSmTiles][4];
+#pragma unroll
+  for (int t = 0; t < kSmTiles; ++t)
 #pragma unroll
     for (int c = 0; c < 4; ++c) acc[t][c] = INT8 ? -0.0f : 0.0f;
-
-  for (int b = 0; b < nb; ++b) {
-    // the block's weight scales (rows past N clamp to the last row; their
-    // outputs are not stored)
-    float wsv[4][2];
+  bool ok = true;
+  for (int ks = 0; ks < kstages; ++ks) {
+    const int s = ks % kSmStages;
+    if (ok) ok = mbar_wait_spin(&full[s], (ks / kSmStages) & 1, a.status);
+    const unsigned char* st = smem + s * kStage;
+    const float* wsm = reinterpret_cast<const float*>(st + kSmW);  // [128][4]
+    // this lane's weight scales for the stage's four blocks: rows wr0 + 8t + 2q + h
+    float4 ws4[kSmTiles][2];
 #pragma unroll
-    for (int t = 0; t < 4; ++t)
+    for (int t = 0; t < kSmTiles; ++t)
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int r = sr0 + 8 * t + h;
-        wsv[t][h] = __ldg(m.s + static_cast<long long>(r < a.N ? r : a.N - 1) * nb + b);
-      }
-    uint2 wv[4];
-#pragma unroll
-    for (int t = 0; t < 4; ++t) wv[t] = __ldg(reinterpret_cast<const uint2*>(wrow[t] + 32 * b));
+      for (int h = 0; h < 2; ++h)
+        ws4[t][h] = *reinterpret_cast<const float4*>(wsm + 4 * (wr0 + 8 * t + 2 * q + h));
+    float4 xs4[2];
     if (INT8) {
-      const uint2 x0 = __ldg(reinterpret_cast<const uint2*>(a.xq + row0 * K + 32 * b + 8 * q));
-      const uint2 x1 = __ldg(reinterpret_cast<const uint2*>(a.xq + row1 * K + 32 * b + 8 * q));
-      const float xs0 = __ldg(a.xs + row0 * nb + b), xs1 = __ldg(a.xs + row1 * nb + b);
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        int d[4] = {0, 0, 0, 0};
-        mma_s8_m16n8k32(d, x0.x, x1.x, x0.y, x1.y, wv[t].x, wv[t].y);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const float wsb = wsv[t][h];
-          // ((float)S * ws) * xs, then the running sum: |S| < 2^24, so the
-          // conversion is exact; every operation rounded on its own
-          acc[t][h] = __fadd_rn(acc[t][h], __fmul_rn(__fmul_rn(static_cast<float>(d[h]), wsb), xs0));
-          acc[t][2 + h] =
-              __fadd_rn(acc[t][2 + h], __fmul_rn(__fmul_rn(static_cast<float>(d[2 + h]), wsb), xs1));
-        }
-      }
-    } else {
-      float d[4][4];
-#pragma unroll
-      for (int t = 0; t < 4; ++t)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) d[t][c] = 0.0f;
-      uint2 bw[4][2];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        bw[t][0] = i8x4_bf16(wv[t].x);  // step 0: physical 8q + 0..3
-        bw[t][1] = i8x4_bf16(wv[t].y);  // step 1: physical 8q + 4..7
-      }
-#pragma unroll
-      for (int p = 0; p < 3; ++p) {
-        const uint16_t* base = a.pieces + p * a.piece_elems + 32 * b + 8 * q;
-        const uint4 r0 = __ldg(reinterpret_cast<const uint4*>(base + row0 * K));
-        const uint4 r1 = __ldg(reinterpret_cast<const uint4*>(base + row1 * K));
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          mma_bf16_m16n8k16(d[t], r0.x, r1.x, r0.y, r1.y, bw[t][0].x, bw[t][0].y);
-          mma_bf16_m16n8k16(d[t], r0.z, r1.z, r0.w, r1.w, bw[t][1].x, bw[t][1].y);
-        }
-      }
-#pragma unroll
-      for (int t = 0; t < 4; ++t)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          acc[t][h] = fmaf(d[t][h], wsv[t][h], acc[t][h]);
-          acc[t][2 + h] = fmaf(d[t][2 + h], wsv[t][h], acc[t][2 + h]);
-        }
+      const float* xsm = reinterpret_cast<const float*>(st + kSmW + kSmWs + kSmXq);  // [16][4]
+      xs4[0] = *reinterpret_cast<const float4*>(xsm + 4 * i0);
+      xs4[1] = *reinterpret_cast<const float4*>(xsm + 4 * i1);
     }
+#pragma unroll
+    for (int jb = 0; jb < 4; ++jb) {
+      // weights: row r = 32 cw + 8 t + gq, bytes [32 jb + 8q, + 8) of the
+      // 128-byte row; 16-byte unit (2 jb + q / 2) sits at unit ^ (r % 8)
+      uint2 wv[kSmTiles];
+#pragma unroll
+      for (int t = 0; t < kSmTiles; ++t) {
+        const int r = wr0 + 8 * t + gq;
+        const int unit = (2 * jb + (q >> 1)) ^ gq;
+        wv[t] = *reinterpret_cast<const uint2*>(st + r * 128 + (unit << 4) + ((q & 1) << 3));
+      }
+      if (INT8) {
+        const unsigned char* xq = st + kSmW + kSmWs;  // [16][128]
+        const uint2 x0 = *reinterpret_cast<const uint2*>(xq + i0 * 128 + 32 * jb + 8 * q);
+        const uint2 x1 = *reinterpret_cast<const uint2*>(xq + i1 * 128 + 32 * jb + 8 * q);
+        const float xs0 = jb == 0 ? xs4[0].x : jb == 1 ? xs4[0].y : jb == 2 ? xs4[0].z : xs4[0].w;
+        const float xs1 = jb == 0 ? xs4[1].x : jb == 1 ? xs4[1].y : jb == 2 ? xs4[1].z : xs4[1].w;
+#pragma unroll
+        for (int t = 0; t < kSmTiles; ++t) {
+          int d[4] = {0, 0, 0, 0};
+          mma_s8_m16n8k32(d, x0.x, x1.x, x0.y, x1.y, wv[t].x, wv[t].y);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const float4 w4 = ws4[t][h];
+            const float wsb = jb == 0 ? w4.x : jb == 1 ? w4.y : jb == 2 ? w4.z : w4.w;
+            // ((float)S * ws) * xs, then the running sum: |S| < 2^24, so the
+            // conversion is exact; every operation rounded on its own
+            acc[t][h] =
+                __fadd_rn(acc[t][h], __fmul_rn(__fmul_rn(static_cast<float>(d[h]), wsb), xs0));
+            acc[t][2 + h] = __fadd_rn(acc[t][2 + h],
+                                      __fmul_rn(__fmul_rn(static_cast<float>(d[2 + h]), wsb), xs1));
+          }
+        }
+      } else {
+        float d[kSmTiles][4];
+#pragma unroll
+        for (int t = 0; t < kSmTiles; ++t)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) d[t][c] = 0.0f;
+        uint2 bw[kSmTiles][2];
+#pragma unroll
+        for (int t = 0; t < kSmTiles; ++t) {
+          bw[t][0] = i8x4_bf16(wv[t].x);  // step 0: physical 8q + 0..3
+          bw[t][1] = i8x4_bf16(wv[t].y);  // step 1: physical 8q + 4..7
+        }
+#pragma unroll
+        for (int p = 0; p < 3; ++p) {
+          const unsigned char* xp = st + kSmW + kSmWs + p * kSmXp;  // [16][128] bf16
+          const uint4 r0 = *reinterpret_cast<const uint4*>(xp + i0 * 256 + 2 * (32 * jb + 8 * q));
+          const uint4 r1 = *reinterpret_cast<const uint4*>(xp + i1 * 256 + 2 * (32 * jb + 8 * q));
+#pragma unroll
+          for (int t = 0; t < kSmTiles; ++t) {
+            mma_bf16_m16n8k16(d[t], r0.x, r1.x, r0.y, r1.y, bw[t][0].x, bw[t][0].y);
+            mma_bf16_m16n8k16(d[t], r0.z, r1.z, r0.w, r1.w, bw[t][1].x, bw[t][1].y);
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < kSmTiles; ++t)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const float4 w4 = ws4[t][h];
+            const float wsb = jb == 0 ? w4.x : jb == 1 ? w4.y : jb == 2 ? w4.z : w4.w;
+            acc[t][h] = fmaf(d[t][h], wsb, acc[t][h]);
+            acc[t][2 + h] = fmaf(d[t][2 + h], wsb, acc[t][2 + h]);
+          }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
   }
   // C layout: c0, c1 -> row gq, columns 2q, 2q + 1; c2, c3 -> row gq + 8
-  const float sc0 = INT8 ? 1.0f : __ldg(a.rinv + off + i0);
-  const float sc1 = INT8 ? 1.0f : __ldg(a.rinv + off + i1);
 #pragma unroll
-  for (int t = 0; t < 4; ++t) {
-    const int col = n0 + 8 * t + 2 * q;
-    if (col >= a.N) continue;
+  for (int hr = 0; hr < 2; ++hr) {
+    const int i = gq + 8 * hr;
+    if (i >= count) continue;
+    const float sc = INT8 ? 1.0f : __ldg(a.rinv + off + i);
 #pragma unroll
-    for (int hr = 0; hr < 2; ++hr) {
-      const int i = gq + 8 * hr;
-      if (i >= count) continue;
+    for (int t = 0; t < kSmTiles; ++t) {
+      const int col = n0 + wr0 + 8 * t + 2 * q;
       float v0 = acc[t][2 * hr], v1 = acc[t][2 * hr + 1];
       if (!INT8) {
-        const float sc = hr ? sc1 : sc0;
         v0 = __fmul_rn(v0, sc);
         v1 = __fmul_rn(v1, sc);
       }
-      float* yr = a.y + (off + i) * a.ldy + col;
-      yr[0] = v0;
-      if (col + 1 < a.N) yr[1] = v1;
+      *reinterpret_cast<float2*>(a.y + (off + i) * a.ldy + col) = make_float2(v0, v1);
     }
+  }
+}
+
+void configure_small() {
+  static std::mutex mu;
+  static unsigned long long done = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 64 && !(done & (1ull << dev))) {
+    cudaFuncSetAttribute(small_rows_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         kSmSmemF);
+    cudaFuncSetAttribute(small_rows_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         kSmSmemI);
+    done |= 1ull << dev;
   }
 }
 
 }  // namespace
 
-bool small_rows_supported(int N, int K) { return N > 0 && N % 8 == 0 && K > 0 && K % 128 == 0; }
+bool small_rows_supported(int N, int K) {
+  return N > 0 && N % kSmRows == 0 && K > 0 && K % kSmK == 0 && tma_encode_fn() != nullptr;
+}
 
-cudaError_t launch_small_rows(bool int8, const FfnView* ffns, const Q8View* single, int proj,
-                              const int* counts, const int* offsets, int groups, int lo, int hi,
-                              int N, int K, const uint16_t* pieces, long long piece_rows,
-                              const float* rinv, const int8_t* xq, const float* xs, float* y,
-                              long long ldy, cudaStream_t st) {
-  if (!small_rows_supported(N, K) || hi > kSmallRowsMax || groups < 1) return cudaErrorInvalidValue;
+cudaError_t launch_small_rows(bool int8, const void* maps, const Q8View* single, const int* counts,
+                              const int* offsets, int groups, int lo, int hi, int total_rows, int N,
+                              int K, const uint16_t* pieces, int piece_rows, const float* rinv,
+                              const int8_t* xq, const float* xs, int x_rows, float* y,
+                              long long ldy, unsigned* status, cudaStream_t st) {
+  if (!small_rows_supported(N, K) || hi > kSmallRowsMax || lo < 1) return cudaErrorInvalidValue;
+  if (!maps && !single) return cudaErrorInvalidValue;
+  if (!counts) groups = (total_rows + 15) / 16;
+  if (groups < 1 || reinterpret_cast<uintptr_t>(y) % 8 || ldy % 2) return cudaErrorInvalidValue;
+  CUtensorMap tw{}, tws{}, tx{}, txs{};
+  if (single) {
+    TcMatrixMaps mm;
+    if (!q8_tc_weight_maps(&mm, *single)) return cudaErrorInvalidValue;
+    tw = mm.w_sw128;
+    tws = mm.ws;
+  }
+  if (int8) {
+    if (!make_map_i8_plain(&tx, xq, x_rows, K, 16) || !make_map_f32(&txs, xs, x_rows, K / 32, 16))
+      return cudaErrorInvalidValue;
+  } else if (!make_map_pieces_plain(&tx, pieces, piece_rows, K, 16)) {
+    return cudaErrorInvalidValue;
+  }
+  configure_small();
   SmallArgs a{};
-  a.ffns = ffns;
-  if (single) a.single = *single;
-  a.proj = proj;
+  a.maps = static_cast<const TcMatrixMaps*>(maps);
+  if (single) a.maps = nullptr;
   a.counts = counts;
   a.offsets = offsets;
   a.groups = groups;
   a.lo = lo;
   a.hi = hi;
+  a.total_rows = total_rows;
   a.N = N;
   a.K = K;
-  a.pieces = pieces;
-  a.piece_elems = piece_rows * K;
+  a.piece_rows = piece_rows;
   a.rinv = rinv;
-  a.xq = xq;
-  a.xs = xs;
   a.y = y;
   a.ldy = ldy;
-  const dim3 grid((N + kSmallCtaRows - 1) / kSmallCtaRows, groups);
+  a.status = status;
+  const dim3 grid(N / kSmRows, groups);
   if (int8)
-    small_rows_kernel<true><<<grid, 32 * kSmallWarps, 0, st>>>(a);
+    small_rows_kernel<true><<<grid, kSmThreads, kSmSmemI, st>>>(tw, tws, tx, txs, a);
   else
-    small_rows_kernel<false><<<grid, 32 * kSmallWarps, 0, st>>>(a);
+    small_rows_kernel<false><<<grid, kSmThreads, kSmSmemF, st>>>(tw, tws, tx, txs, a);
   return cudaGetLastError();
 }
 

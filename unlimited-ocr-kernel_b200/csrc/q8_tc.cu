@@ -29,14 +29,13 @@
 // A "group" launch serves the MoE prefill: group g owns activation rows
 // [offsets[g], offsets[g] + counts[g]) and multiplies them by its own
 // weights; the grid's y dimension enumerates 64-row tiles over the groups.
-#include <cuda.h>  // CUtensorMap and its enums (types only)
 #include <cuda_bf16.h>
-#include <cudaTypedefs.h>
 
 #include <mutex>
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tc_maps.cuh"
 
 namespace uocr {
 
@@ -59,16 +58,6 @@ constexpr int kStageBytes = kABytes + kBBytes + kWsBytes + kXsBytes;  // 27 KB (
 constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*alignment*/ + 512 /*barriers*/;
 static_assert(kStageBytes % 1024 == 0, "swizzled tiles need 1024-byte alignment");
 
-// Everything the tensor-core kernels need of one weight matrix, built once
-// per matrix on the host (q8_tc_weight_maps) and read by the kernels from
-// device memory in grouped launches.
-struct alignas(64) TcMatrixMaps {
-  CUtensorMap w_sw128;   // int8 weights, 128-byte K boxes x 128 rows, 128-byte swizzle
-  CUtensorMap ws;        // weight scales, 4-block boxes x 128 rows
-  CUtensorMap w_rows64;  // int8 weights, 64-byte K boxes x 128 rows, unswizzled
-  const float* s;        // weight scales [rows][nb] (FP32-activation epilogue)
-  int nb;                // scale blocks per row
-};
 
 struct TcArgs {
   const TcMatrixMaps* maps;  // grouped: [groups]
@@ -81,14 +70,6 @@ struct TcArgs {
 };
 
 // ---- PTX wrappers ----------------------------------------------------------
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
-      : "memory");
-}
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* holder, uint32_t cols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -837,76 +818,6 @@ int grid_for(long long work, int sms) {
 }
 
 // ---- host: tensor maps ------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
-// 2-D int8 tensor [rows][cols] (cols contiguous), box = box_rows x 128 bytes,
-// 128-byte swizzle (the UMMA K-major layout).
-bool make_map_i8(CUtensorMap* map, const void* base, long long rows, long long cols, int box_rows) {
-  auto fn = encode_fn();
-  if (!fn) return false;
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols)};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
-  const cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
-            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-// 2-D float tensor [rows][nb] of block scales, box = box_rows x 4 blocks.
-bool make_map_f32(CUtensorMap* map, const float* base, long long rows, long long nb, int box_rows) {
-  auto fn = encode_fn();
-  if (!fn) return false;
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(nb), static_cast<cuuint64_t>(rows)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(nb * 4)};
-  const cuuint32_t box[2] = {4, static_cast<cuuint32_t>(box_rows)};
-  const cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
-            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-// int8 weights [rows][cols] for the FP32-activation kernel: 64-byte K boxes
-// x 128 rows, unswizzled (the conversion warps read them).
-bool make_map_w_rows64(CUtensorMap* map, const void* base, long long rows, long long cols) {
-  auto fn = encode_fn();
-  if (!fn) return false;
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols)};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kFK), static_cast<cuuint32_t>(kBN)};
-  const cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
-            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-// bf16 activation pieces [3 * piece_rows][cols]: 64-element K boxes x box_rows
-// rows, 128-byte swizzle (the UMMA K-major layout).
-bool make_map_pieces(CUtensorMap* map, const uint16_t* base, long long piece_rows, long long cols,
-                     int box_rows) {
-  auto fn = encode_fn();
-  if (!fn) return false;
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(3 * piece_rows)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 2)};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kFK), static_cast<cuuint32_t>(box_rows)};
-  const cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(base), dims, strides,
-            box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 // The dynamic shared-memory opt-in, once per device.
 void configure() {
   static std::mutex mu;
@@ -928,7 +839,7 @@ bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0;
 }  // namespace
 
 bool q8_tc_supported(int rows, int cols) {
-  return rows > 0 && cols > 0 && rows % kBN == 0 && cols % kBK == 0 && encode_fn() != nullptr;
+  return rows > 0 && cols > 0 && rows % kBN == 0 && cols % kBK == 0 && tma_encode_fn() != nullptr;
 }
 
 size_t q8_tc_maps_bytes() { return sizeof(TcMatrixMaps); }
