@@ -46,7 +46,7 @@ METRIC = "q8-block32 expert GEMV GB/s (MoE decode layer, config 1)"
 # ncu captures summarised in profiles/moe_decode_kernel_config1.md and
 # profiles/gemv_tma_kernel_config0.md (16 matrices per GEMV launch).
 DECODE_TRAFFIC = 31_045_632
-GEMV_TRAFFIC = 20_668_928
+GEMV_TRAFFIC = 4 * 20_668_928  # the 16-matrix capture scaled to a 64-matrix launch
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_HBM = 6650.0
 
@@ -269,12 +269,13 @@ def run_ours(args):
 
 
 GEMV_BYTES = MAT_BYTES(F, H) + H * 4 + F * 4  # config 0: 1,298,944 B
+GEMV_PER_LAUNCH = 64  # matrices per multi-GEMV launch (82.6 MB of weights)
 
 
 def run_gemv(args):
     """Config 0 (secondary workload): single [896x1280] GEMV, FP32 or int8
     activations, measured as a batched stream over a pool of distinct matrices
-    (16 per launch) so the weights come from HBM."""
+    (64 per launch) so the weights come from HBM."""
     import torch
 
     import uocr_q8
@@ -295,13 +296,15 @@ def run_gemv(args):
     ys = [torch.empty(F, device=dev) for _ in range(pool)]
     mode = 1 if args.gemv_int8 else 0
     with torch.cuda.stream(stream):
-        for i in range(0, pool, 16):
-            uocr_q8.linear_multi_device(ctx, mats[i:i + 16], x, ys[i:i + 16], mode)
+        for i in range(0, pool, GEMV_PER_LAUNCH):
+            uocr_q8.linear_multi_device(ctx, mats[i:i + GEMV_PER_LAUNCH], x,
+                                        ys[i:i + GEMV_PER_LAUNCH], mode)
     ctx.sync()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
-        for i in range(0, pool, 16):
-            uocr_q8.linear_multi_device(ctx, mats[i:i + 16], x, ys[i:i + 16], mode)
+        for i in range(0, pool, GEMV_PER_LAUNCH):
+            uocr_q8.linear_multi_device(ctx, mats[i:i + GEMV_PER_LAUNCH], x,
+                                        ys[i:i + GEMV_PER_LAUNCH], mode)
     reps = max(1, args.steps // pool)
     for _ in range(max(args.warmup, 3)):
         graph.replay()
@@ -337,13 +340,13 @@ def run_gemv(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8-act" if mode else "fp32", "data": "synthetic (seeded)",
             "config": {"workload": "config0_gemv_896x1280", "pool": pool,
-                       "matrices_per_launch": 16, "bytes_per_step": GEMV_BYTES},
+                       "matrices_per_launch": GEMV_PER_LAUNCH, "bytes_per_step": GEMV_BYTES},
             "single_call_us": round(single_us, 3),
             "roofline": {"bound": "hbm", "kernel": "gemv_tma_kernel", "achieved": round(gbs, 2),
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(gbs / peak, 4),
                          "traffic": args.traffic if args.traffic is not None else GEMV_TRAFFIC},
-            "gpu_launches": steps // 16, "clocks": clocks.summary()}
+            "gpu_launches": steps // GEMV_PER_LAUNCH, "clocks": clocks.summary()}
 
 
 def make_cpu_layer(seed):

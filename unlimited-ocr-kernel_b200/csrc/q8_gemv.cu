@@ -86,7 +86,7 @@ constexpr int kGemvWarpsPerGroup = 4;
 constexpr int kGemvConsumerWarps = kGemvGroups * kGemvWarpsPerGroup;
 constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;
 constexpr int kGemvStages = 8;
-constexpr int kGemvMaxMats = 16;
+constexpr int kGemvMaxMats = 64;
 constexpr int kGemvStageBudget = 24 * 1024;  // bytes of one stage (weights + scales)
 
 struct GemvTmaParams {
@@ -96,6 +96,7 @@ struct GemvTmaParams {
   int tile_begin[kGemvMaxMats + 1];  // prefix of tiles per matrix
   int rows[kGemvMaxMats];
   int n_mats, cols, tile_rows, total_tiles;
+  int uniform_tiles;  // tiles per matrix when every matrix has the same rows, else 0
   const float* x;
   unsigned* status;
 };
@@ -189,7 +190,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const __grid_
         if (it >= kGemvStages) ok = mbar_wait(&empty[stage], ((it / kGemvStages) - 1) & 1, p.status);
         if (!ok) break;
         int mi = 0;
-        while (tile >= p.tile_begin[mi + 1]) ++mi;
+        if (p.uniform_tiles)
+          mi = tile / p.uniform_tiles;
+        else
+          while (tile >= p.tile_begin[mi + 1]) ++mi;
         const int r0 = (tile - p.tile_begin[mi]) * TR;
         const int nr = min(TR, p.rows[mi] - r0);
         unsigned char* dst = ring + stage * stage_bytes;
@@ -212,7 +216,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const __grid_
     const int stage = it % kGemvStages;
     if (!mbar_wait(&full[stage], (it / kGemvStages) & 1, p.status)) break;
     int mi = 0;
-    while (tile >= p.tile_begin[mi + 1]) ++mi;
+    if (p.uniform_tiles)
+      mi = tile / p.uniform_tiles;
+    else
+      while (tile >= p.tile_begin[mi + 1]) ++mi;
     const int r0 = (tile - p.tile_begin[mi]) * TR;
     const int nr = min(TR, p.rows[mi] - r0);
     const int8_t* wt = reinterpret_cast<const int8_t*>(ring + stage * stage_bytes);
@@ -280,6 +287,9 @@ static void launch_gemv_tma(const Q8View* mats, int n, const float* x, float* co
   }
   for (int i = n; i <= kGemvMaxMats; ++i) p.tile_begin[i] = tiles;
   p.total_tiles = tiles;
+  p.uniform_tiles = (mats[0].rows + tr - 1) / tr;
+  for (int i = 1; i < n; ++i)
+    if (mats[i].rows != mats[0].rows) p.uniform_tiles = 0;
   const size_t smem = gemv_tma_smem(cols, tr);
   static unsigned configured = 0;  // one bit per device ordinal
   int dev = 0;
