@@ -667,7 +667,9 @@ def run_ep(args):
             experts = [[mat(base + 10 * (e + 1) + i, *rc)
                         for i, rc in enumerate(((F, H), (F, H), (H, F)))] for e in mine]
             layer = uocr_q8.MoeLayer(ctx, shared, experts, top_k=1)
-            eps.append(ExpertParallelMoe(LibraryBackend(ctx, layer, E, TOPK), E, TOPK, H))
+            # fixed-capacity exchange: no counts on the host, so steps are captured in a graph
+            eps.append(ExpertParallelMoe(LibraryBackend(ctx, layer, E, TOPK), E, TOPK, H,
+                                         capacity=(EP_TOKENS // world) * TOPK))
     torch.cuda.synchronize()
     T = EP_TOKENS // world
     gen = torch.Generator(device=dev)
@@ -681,18 +683,36 @@ def run_ep(args):
         return eps[i % n_layers].forward(x, l, mode)[0]
 
     with torch.cuda.stream(stream):
-        for i in range(max(args.warmup, 3)):
+        for i in range(max(args.warmup, 3) + n_layers):  # also sizes every layer's workspace
             step(i, xs[i % n_in], lg[i % n_in])
     torch.cuda.synchronize()
-    steps = max(1, args.steps)
+    # one graph of n_layers consecutive steps (distinct layers and tokens)
+    graph = torch.cuda.CUDAGraph()
+    graphed = True
+    try:
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(n_layers):
+                step(i, xs[i % n_in], lg[i % n_in])
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize()
+    except Exception as exc:  # capture not available: time eager steps
+        graphed = False
+        print(f"ep_decode: graph capture failed ({exc}); timing eager steps", file=sys.stderr)
+    reps = max(1, args.steps // n_layers)
+    steps = reps * n_layers
     dist.barrier()
     torch.cuda.synchronize()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         with torch.cuda.stream(stream):
             start.record(stream)
-            for i in range(steps):
-                step(i, xs[i % n_in], lg[i % n_in])
+            for r in range(reps):
+                if graphed:
+                    graph.replay()
+                else:
+                    for i in range(n_layers):
+                        step(i, xs[i % n_in], lg[i % n_in])
             stop.record(stream)
         stop.synchronize()
     torch.cuda.synchronize()
@@ -744,7 +764,8 @@ def run_ep(args):
             "config": {"workload": "config4_moe_layer_ep_decode", "global_batch": EP_TOKENS,
                        "tokens_per_rank": T, "hidden": H, "experts": E, "top_k": TOPK,
                        "experts_per_rank": len(mine), "expert_width": F, "shared_width": FS,
-                       "mode": mode, "parallelism": f"ep{world} (NCCL all_to_all)",
+                       "mode": mode, "parallelism": f"ep{world} (NCCL all_to_all, fixed capacity)",
+                       "cuda_graph": graphed,
                        "l2": f"rotating pool of {n_layers} layers x "
                              f"{per_rank_bytes / 1e6:.1f} MB per rank (> 126 MB L2)"},
             "e2e": {"value": round(e2e, 1), "unit": "tok/s", "steps": e2e_steps,
@@ -752,12 +773,16 @@ def run_ep(args):
             "roofline": {"bound": "hbm", "kernel": "whole EP step (per-rank weight bytes)",
                          "achieved": round(achieved, 2), "peak": peak, "peak_kind": peak_kind,
                          "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None},
-            "gpu_launches": steps * 8 if mode == 0 else None,
+            # route, dispatch (plan + rows), expert rows (grouping, split or quantize,
+            # 3 warp-level + 3 tensor-core projections, SwiGLU, un-permute), shared
+            # expert (split or quantize, 3 projections, SwiGLU), combine
+            "gpu_launches": steps * {0: 20, 2: 21}.get(mode) if mode in (0, 2) else None,
             "clocks": clocks.summary(),
         }
         if cpu:
             result["cpu_baseline"] = cpu
     dist.barrier()
+    del graph  # a graph holding NCCL calls goes before the process group
     dist.destroy_process_group()
     return result
 

@@ -196,13 +196,33 @@ int uocr_moe_forward_host(uocr_ctx *ctx, const uocr_moe *layer, int mode, const 
  * arguments are not used by them.  All asynchronous on the context stream. */
 /* out_dev[i] = FFN_{expert_ids_dev[i]}(x_dev[i]): x_dev/out_dev rows*hidden.
  * Rows of one expert form one group, as the tokens an expert receives in
- * Decoder::experts.  An id outside [0, n_experts) is Shape at the next
- * synchronising call. */
+ * Decoder::experts.  A negative id marks an unused row (a padding slot of
+ * uocr_moe_dispatch): it is skipped and its output row left unchanged.  An
+ * id >= n_experts is Shape at the next synchronising call. */
 int uocr_moe_expert_rows(uocr_ctx *ctx, const uocr_moe *layer, int mode, const float *x_dev,
                          const int32_t *expert_ids_dev, size_t rows, float *out_dev);
 /* y_dev = shared FFN(x_dev), rows*hidden each. */
 int uocr_moe_shared_rows(uocr_ctx *ctx, const uocr_moe *layer, int mode, const float *x_dev,
                          size_t rows, float *y_dev);
+/* Fixed-capacity dispatch, so that the exchange needs no counts on the host
+ * (and a whole expert-parallel step can be captured in a CUDA graph): pair
+ * (t, j) goes to the rank r with rank_bounds[r] <= ids[t,j] <
+ * rank_bounds[r+1] (rank_bounds: host array of world + 1 increasing expert
+ * indices from 0), in slot s = the number of earlier pairs for r;
+ * send_x[r][s] = x[t], send_ids[r][s] = ids[t,j] - rank_bounds[r] (-1 in
+ * unused slots), pair_rows[t*top_k + j] = r * capacity + s.  send_x is
+ * world*capacity*hidden floats, send_ids world*capacity.  More than
+ * `capacity` pairs for one rank is Resource at the next synchronising call
+ * (tokens * top_k always suffices).  world <= 64, top_k <= 8, hidden % 4 == 0. */
+int uocr_moe_dispatch(uocr_ctx *ctx, const float *x_dev, size_t tokens, size_t hidden,
+                      const int32_t *ids_dev, size_t top_k, const int32_t *rank_bounds,
+                      size_t world, size_t capacity, float *send_x_dev, int32_t *send_ids_dev,
+                      int32_t *pair_rows_dev);
+/* uocr_moe_combine with the expert outputs read at rows_dev[pair_rows[t*top_k
+ * + j]] (the returned fixed-capacity buffer of uocr_moe_dispatch). */
+int uocr_moe_combine_rows(uocr_ctx *ctx, const int32_t *ids_dev, const float *weights_dev,
+                          const float *rows_dev, const int32_t *pair_rows_dev, size_t tokens,
+                          size_t top_k, size_t hidden, float *y_dev);
 /* For each token t: y[t] += weights[t,j] * pair_out[t*top_k + j] over its
  * top_k pairs in ascending ids[t,j], one rounding per operation (the combine
  * of src/decoder/mod.rs:208-217; y holds the shared output).  top_k <= 8. */

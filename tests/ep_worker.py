@@ -62,7 +62,7 @@ class OracleBackend:
     def expert_rows(self, x, local_ids, mode, out):
         import torch
         xn, ids = x.numpy(), local_ids.numpy()
-        for e in np.unique(ids):
+        for e in np.unique(ids[ids >= 0]):  # negative: unused slot
             rows = np.nonzero(ids == e)[0]
             out[torch.from_numpy(rows)] = torch.from_numpy(
                 oracle.feed_forward(self.local[int(e)], xn[rows], mode))
@@ -79,6 +79,30 @@ class OracleBackend:
         for t in range(idn.shape[0]):
             for j in np.argsort(idn[t], kind="stable"):
                 yn[t] = yn[t] + np.float32(wn[t, j]) * po[t * k + j]
+
+    def dispatch(self, x, ids, bounds, capacity):
+        """uocr_moe_dispatch restated: slot = earlier pairs for the same rank."""
+        import torch
+        world = len(bounds) - 1
+        xn, idn = x.numpy(), ids.numpy().reshape(-1)
+        k = ids.shape[1]
+        send_x = np.zeros((world * capacity, xn.shape[1]), np.float32)
+        send_ids = np.full((world * capacity,), -1, np.int32)
+        pair_rows = np.empty((idn.size,), np.int32)
+        used = [0] * world
+        for i, e in enumerate(idn):
+            r = next(r for r in range(world) if bounds[r] <= e < bounds[r + 1])
+            slot = used[r]
+            used[r] += 1
+            assert slot < capacity
+            send_x[r * capacity + slot] = xn[i // k]
+            send_ids[r * capacity + slot] = e - bounds[r]
+            pair_rows[i] = r * capacity + slot
+        return torch.from_numpy(send_x), torch.from_numpy(send_ids), torch.from_numpy(pair_rows)
+
+    def combine_rows(self, ids, wts, rows, pair_rows, y):
+        import torch
+        self.combine(ids, wts, rows[torch.from_numpy(pair_rows.numpy().astype(np.int64))], y)
 
 
 def _init(rank, world, port, backend):
@@ -100,7 +124,8 @@ def cpu_rank(rank, world, port, case):
         shared, experts = make_layer(case["seed"], H, F, FS, E)
         b = expert_bounds(E, world)
         be = OracleBackend(shared, experts[b[rank]:b[rank + 1]], k, case["normalize"], case["scale"])
-        ep = ExpertParallelMoe(be, E, k, H)
+        cap = case.get("capacity")
+        ep = ExpertParallelMoe(be, E, k, H, capacity=cap)
         x, logits = rank_inputs(case["seed"], rank, case["tokens"][rank], H, E)
         for mode in case["modes"]:
             y, ids, wts = ep.forward(torch.from_numpy(x), torch.from_numpy(logits), mode)
@@ -142,7 +167,7 @@ def gpu_rank(rank, world, port, case):
         layer = local_layer(ctx, sh, ex, b, rank)
         full = uocr_q8.MoeLayer(ctx, sh, ex, k, norm, scale)
         be = LibraryBackend(ctx, layer, E, k, norm, scale)
-        ep = ExpertParallelMoe(be, E, k, H)
+        ep = ExpertParallelMoe(be, E, k, H, capacity=case.get("capacity"))
         x, logits = rank_inputs(case["seed"], rank, case["tokens"][rank], H, E)
         xt = torch.from_numpy(x).cuda()
         lt = torch.from_numpy(logits).cuda()

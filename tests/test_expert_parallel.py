@@ -46,6 +46,12 @@ def test_ep_gloo_matches_oracle(tokens):
     spawn(ep_worker.cpu_rank, 2, dict(BASE, tokens=list(tokens)))
 
 
+@pytest.mark.parametrize("tokens", [(5, 7), (0, 6)])
+def test_ep_gloo_fixed_capacity(tokens):
+    """The fixed-capacity exchange (no counts on the host): same results."""
+    spawn(ep_worker.cpu_rank, 2, dict(BASE, seed=6, tokens=list(tokens), capacity=7 * 3))
+
+
 def test_ep_gloo_uneven_blocks_renormalised():
     spawn(ep_worker.cpu_rank, 2, dict(BASE, seed=9, experts=7, top_k=4, normalize=True,
                                       scale=2.5, tokens=[9, 4]))
@@ -56,6 +62,8 @@ def test_ep_gloo_uneven_blocks_renormalised():
     dict(BASE, hidden=256, width=128, shared_width=256, tokens=[37, 20]),
     dict(BASE, seed=4, hidden=1280, width=896, shared_width=1792, experts=64, top_k=6,
          tokens=[64, 64], modes=[1, 2]),
+    dict(BASE, seed=5, hidden=1280, width=896, shared_width=1792, experts=64, top_k=6,
+         tokens=[32, 20], modes=[0, 1, 2], capacity=32 * 6),
 ])
 def test_ep_two_gpus_matches_single_gpu(case):
     import torch

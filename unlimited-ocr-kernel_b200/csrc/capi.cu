@@ -131,6 +131,8 @@ int take_device_status(uocr_ctx* ctx) {
     return fail(UOCR_ERR_NUMERICAL, "nonfinite numerical input: invalid or fully masked softmax row");
   if (st & DEV_RANGE) return fail(UOCR_ERR_FORMAT, "invalid checkpoint: INT8 byte -128");
   if (st & DEV_BAD_ROUTE) return fail(UOCR_ERR_SHAPE, "invalid tensor shape: invalid expert routing");
+  if (st & DEV_CAPACITY)
+    return fail(UOCR_ERR_RESOURCE, "resource limit exceeded: expert dispatch capacity");
   return fail(UOCR_ERR_CUDA, "unknown device status 0x%x", st);
 }
 
@@ -925,6 +927,7 @@ static int moe_part(uocr_ctx* ctx, const uocr_moe* L, int mode, const float* x, 
   if (routed) {
     a.skip_shared = 1;
     a.pair_out = out;
+    a.skip_negative_ids = 1;  // padding rows of a fixed-capacity dispatch
   } else {
     a.skip_routed = 1;
     a.y = out;
@@ -951,6 +954,51 @@ int uocr_moe_expert_rows(uocr_ctx* ctx, const uocr_moe* layer, int mode, const f
 int uocr_moe_shared_rows(uocr_ctx* ctx, const uocr_moe* layer, int mode, const float* x_dev,
                          size_t rows, float* y_dev) {
   return moe_part(ctx, layer, mode, x_dev, rows, nullptr, y_dev, false);
+}
+
+int uocr_moe_dispatch(uocr_ctx* ctx, const float* x_dev, size_t tokens, size_t hidden,
+                      const int32_t* ids_dev, size_t top_k, const int32_t* rank_bounds,
+                      size_t world, size_t capacity, float* send_x_dev, int32_t* send_ids_dev,
+                      int32_t* pair_rows_dev) {
+  if (!ctx || !rank_bounds) return fail(UOCR_ERR_INVALID, "null argument");
+  if (world < 1 || world > static_cast<size_t>(kMaxDispatchRanks))
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: 1 <= world <= %d", kMaxDispatchRanks);
+  if (top_k == 0 || top_k > 8 || hidden == 0 || hidden % 4)
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: top_k <= 8, hidden % 4 == 0");
+  if (capacity == 0 || !fits_int(world * capacity) || !fits_int(tokens * top_k))
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: capacity");
+  int bounds[kMaxDispatchRanks + 1];
+  for (size_t r = 0; r <= world; ++r) {
+    bounds[r] = rank_bounds[r];
+    if (r > 0 && bounds[r] <= bounds[r - 1])
+      return fail(UOCR_ERR_SHAPE, "invalid tensor shape: rank bounds must increase");
+  }
+  if (bounds[0] != 0) return fail(UOCR_ERR_SHAPE, "invalid tensor shape: rank bounds start at 0");
+  if (!send_ids_dev || (tokens && (!x_dev || !ids_dev || !send_x_dev || !pair_rows_dev)))
+    return fail(UOCR_ERR_INVALID, "null argument");
+  DeviceGuard g(ctx->device);
+  const cudaError_t e = launch_moe_dispatch(
+      x_dev, static_cast<int>(tokens), static_cast<int>(hidden), ids_dev, static_cast<int>(top_k),
+      bounds[world], bounds, static_cast<int>(world), static_cast<int>(capacity), send_x_dev,
+      send_ids_dev, pair_rows_dev, ctx->status_dev, ctx->stream);
+  if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "dispatch launch: %s", cudaGetErrorString(e));
+  return check_launch();
+}
+
+int uocr_moe_combine_rows(uocr_ctx* ctx, const int32_t* ids_dev, const float* weights_dev,
+                          const float* rows_dev, const int32_t* pair_rows_dev, size_t tokens,
+                          size_t top_k, size_t hidden, float* y_dev) {
+  if (!ctx) return fail(UOCR_ERR_INVALID, "null argument");
+  if (top_k == 0 || top_k > 8) return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: top_k <= 8");
+  if (tokens == 0 || hidden == 0) return ok();
+  if (!ids_dev || !weights_dev || !rows_dev || !pair_rows_dev || !y_dev)
+    return fail(UOCR_ERR_INVALID, "null argument");
+  if (!fits_int(tokens * top_k) || !fits_int(hidden))
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: tokens");
+  DeviceGuard g(ctx->device);
+  launch_moe_combine_rows(ids_dev, weights_dev, rows_dev, pair_rows_dev, static_cast<int>(tokens),
+                          static_cast<int>(top_k), static_cast<int>(hidden), y_dev, ctx->stream);
+  return check_launch();
 }
 
 int uocr_moe_combine(uocr_ctx* ctx, const int32_t* ids_dev, const float* weights_dev,

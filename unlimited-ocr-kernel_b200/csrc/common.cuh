@@ -29,6 +29,7 @@ enum DevStatus : unsigned {
   DEV_SOFTMAX = 1u << 4,        // router row with NaN/+inf or no finite max
   DEV_TIMEOUT = 1u << 5,        // a bounded wait expired
   DEV_BAD_ROUTE = 1u << 6,      // expert id outside the layer
+  DEV_CAPACITY = 1u << 7,       // more pairs for one rank than the dispatch capacity
 };
 
 __device__ __forceinline__ void flag(unsigned* status, unsigned bits) {

@@ -151,9 +151,23 @@ struct MoePrefillArgs {
   // combining into y.
   int route_given, skip_shared, skip_routed;
   float* pair_out;
+  int skip_negative_ids;  // route_given: a negative id marks an unused row
 };
 size_t moe_prefill_workspace(const MoePrefillArgs& a, int mode);
 cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaStream_t st);
+// Fixed-capacity dispatch for expert parallelism (see moe_prefill.cu).
+constexpr int kMaxDispatchRanks = 64;
+struct DispatchBounds {
+  int world;
+  int b[kMaxDispatchRanks + 1];
+};
+cudaError_t launch_moe_dispatch(const float* x, int tokens, int hidden, const int32_t* ids,
+                                int top_k, int n_experts, const int* bounds, int world,
+                                int capacity, float* send_x, int32_t* send_ids,
+                                int32_t* pair_rows, unsigned* status, cudaStream_t st);
+void launch_moe_combine_rows(const int32_t* ids, const float* weights, const float* rows,
+                             const int32_t* pair_rows, int tokens, int top_k, int hidden, float* y,
+                             cudaStream_t st);
 // y[t] += p * out for token t's pairs in ascending expert id (y holds the
 // shared expert's output): the combine of Decoder::experts on outputs given
 // in pair order (row t*top_k + j).

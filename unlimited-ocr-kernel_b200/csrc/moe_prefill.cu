@@ -27,10 +27,12 @@ constexpr int kMaxGroupExperts = 256;
 
 // Stable counting sort of the tokens*top_k (token, expert) pairs by expert.
 // Pair i = t*top_k + j is visited in increasing i, i.e. increasing token, so
-// each expert's slice lists its tokens in ascending order.
+// each expert's slice lists its tokens in ascending order.  With
+// skip_negative, a negative id marks an unused pair (a padding row of a
+// fixed-capacity dispatch): it joins no group and its token_pos is -1.
 __global__ void __launch_bounds__(kGroupThreads) group_pairs_kernel(
     const int32_t* __restrict__ ids, const float* __restrict__ wts, int tokens, int top_k,
-    int n_experts, int* __restrict__ counts, int* __restrict__ offsets,
+    int n_experts, int skip_negative, int* __restrict__ counts, int* __restrict__ offsets,
     int* __restrict__ pair_token, float* __restrict__ pair_weight, int* __restrict__ token_pos,
     unsigned* status) {
   __shared__ int cnt[kGroupThreads / 32][kMaxGroupExperts];
@@ -45,6 +47,7 @@ __global__ void __launch_bounds__(kGroupThreads) group_pairs_kernel(
   // pass 1: histogram
   for (int i = tid; i < npairs; i += blockDim.x) {
     int e = ids[i];
+    if (e < 0 && skip_negative) continue;
     if (e < 0 || e >= n_experts) {
       flag(status, DEV_BAD_ROUTE);
       e = 0;
@@ -68,8 +71,9 @@ __global__ void __launch_bounds__(kGroupThreads) group_pairs_kernel(
   // pass 2: stable positions, chunk by chunk
   for (int c0 = 0; c0 < npairs; c0 += blockDim.x) {
     const int i = c0 + tid;
-    const bool valid = i < npairs;
-    int e = valid ? ids[i] : -1;
+    int e = i < npairs ? ids[i] : -1;
+    if (i < npairs && e < 0 && skip_negative) token_pos[i] = -1;
+    const bool valid = i < npairs && !(e < 0 && skip_negative);
     if (valid && (e < 0 || e >= n_experts)) e = 0;
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     const int rank = __popc(peers & ((1u << lane) - 1));
@@ -95,6 +99,13 @@ __global__ void __launch_bounds__(kGroupThreads) group_pairs_kernel(
     for (int x = tid; x < (kGroupThreads / 32) * n_experts; x += blockDim.x)
       cnt[x / n_experts][x % n_experts] = 0;
     __syncthreads();
+  }
+  // positions past the grouped pairs (unused pairs were skipped): the gathers
+  // that walk every position (split_rows, gather_rows) read row 0 there, a
+  // valid row that no group consumes
+  for (int i = off[n_experts] + tid; i < npairs; i += blockDim.x) {
+    pair_token[i] = 0;
+    pair_weight[i] = 0.0f;
   }
 }
 
@@ -154,11 +165,12 @@ __global__ void combine_pairs_kernel(const int32_t* __restrict__ ids,
   }
 }
 
-// pair_out[i] = out_r[token_pos[i]]: routed outputs back in pair order.
+// pair_out[i] = out_r[token_pos[i]]: routed outputs back in pair order
+// (unused pairs, token_pos -1, are left as they are).
 __global__ void unpermute_kernel(const int* __restrict__ token_pos, const float* __restrict__ out_r,
                                  int pairs, int hidden, float* __restrict__ pair_out) {
   const int i = blockIdx.x;
-  if (i >= pairs) return;
+  if (i >= pairs || token_pos[i] < 0) return;
   const float* src = out_r + static_cast<long long>(token_pos[i]) * hidden;
   float* dst = pair_out + static_cast<long long>(i) * hidden;
   for (int c = threadIdx.x; c < hidden; c += blockDim.x) dst[c] = src[c];
@@ -168,6 +180,134 @@ void launch_moe_combine_pairs(const int32_t* ids, const float* weights, const fl
                               int tokens, int top_k, int hidden, float* y, cudaStream_t st) {
   if (tokens > 0)
     combine_pairs_kernel<<<tokens, 256, 0, st>>>(ids, weights, pair_out, tokens, top_k, hidden, y);
+}
+
+// ---------------------------------------------------------------------------
+// Fixed-capacity dispatch for expert parallelism.  Pair i = t*top_k + j goes
+// to the rank r that owns its expert (bounds[r] <= e < bounds[r+1]), slot =
+// the number of earlier pairs (in pair order) for r: send_ids[r][slot] = e -
+// bounds[r] (-1 marks an unused slot), pair_rows[i] = r * capacity + slot.
+__global__ void __launch_bounds__(kGroupThreads) dispatch_plan_kernel(
+    const int32_t* __restrict__ ids, int pairs, int n_experts, DispatchBounds bd, int capacity,
+    int32_t* __restrict__ send_ids, int32_t* __restrict__ pair_rows, unsigned* status) {
+  __shared__ int cnt[kGroupThreads / 32][kMaxDispatchRanks];
+  __shared__ int base[kMaxDispatchRanks];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, world = bd.world;
+  for (int i = tid; i < world * capacity; i += blockDim.x) send_ids[i] = -1;
+  for (int r = tid; r < world; r += blockDim.x) base[r] = 0;
+  for (int i = tid; i < (kGroupThreads / 32) * kMaxDispatchRanks; i += blockDim.x)
+    (&cnt[0][0])[i] = 0;
+  __syncthreads();
+  for (int c0 = 0; c0 < pairs; c0 += blockDim.x) {
+    const int i = c0 + tid;
+    int e = i < pairs ? ids[i] : -1, r = -1;
+    if (i < pairs) {
+      if (e < 0 || e >= n_experts) {
+        flag(status, DEV_BAD_ROUTE);
+        e = 0;
+      }
+      r = 0;
+      while (r + 1 < world && e >= bd.b[r + 1]) ++r;
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, r);
+    const int rank_in_warp = __popc(peers & ((1u << lane) - 1));
+    if (r >= 0 && rank_in_warp == 0) cnt[warp][r] = __popc(peers);
+    __syncthreads();
+    for (int x = tid; x < world; x += blockDim.x) {
+      int run = base[x];
+      for (int w = 0; w < kGroupThreads / 32; ++w) {
+        const int v = cnt[w][x];
+        cnt[w][x] = run;
+        run += v;
+      }
+      base[x] = run;
+    }
+    __syncthreads();
+    if (r >= 0) {
+      const int slot = cnt[warp][r] + rank_in_warp;
+      if (slot < capacity) {
+        send_ids[r * capacity + slot] = e - bd.b[r];
+        pair_rows[i] = r * capacity + slot;
+      } else {
+        flag(status, DEV_CAPACITY);
+        pair_rows[i] = -1;
+      }
+    }
+    __syncthreads();
+    for (int x = tid; x < (kGroupThreads / 32) * world; x += blockDim.x)
+      cnt[x / world][x % world] = 0;
+    __syncthreads();
+  }
+}
+
+// send_x[pair_rows[i]] = x[i / top_k], one CTA per pair.
+__global__ void dispatch_rows_kernel(const float* __restrict__ x, int hidden, int top_k,
+                                     const int32_t* __restrict__ pair_rows, int pairs,
+                                     float* __restrict__ send_x) {
+  const int i = blockIdx.x;
+  if (i >= pairs) return;
+  const int row = pair_rows[i];
+  if (row < 0) return;
+  const float4* src = reinterpret_cast<const float4*>(x + static_cast<long long>(i / top_k) * hidden);
+  float4* dst = reinterpret_cast<float4*>(send_x + static_cast<long long>(row) * hidden);
+  for (int c = threadIdx.x; c < hidden / 4; c += blockDim.x) dst[c] = src[c];
+}
+
+// y[t] += w * rows[pair_rows[t*top_k + j]] over t's pairs in ascending expert
+// id (y holds the shared expert's output), one rounding per operation.
+__global__ void combine_rows_kernel(const int32_t* __restrict__ ids,
+                                    const float* __restrict__ weights,
+                                    const float* __restrict__ rows,
+                                    const int32_t* __restrict__ pair_rows, int tokens, int top_k,
+                                    int hidden, float* __restrict__ y) {
+  const int t = blockIdx.x;
+  if (t >= tokens) return;
+  int e[8], j[8];
+  for (int i = 0; i < top_k; ++i) {
+    e[i] = ids[t * top_k + i];
+    j[i] = i;
+  }
+  for (int i = 1; i < top_k; ++i)
+    for (int m = i; m > 0 && e[m - 1] > e[m]; --m) {
+      int te = e[m]; e[m] = e[m - 1]; e[m - 1] = te;
+      int tj = j[m]; j[m] = j[m - 1]; j[m - 1] = tj;
+    }
+  for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
+    float acc = y[static_cast<long long>(t) * hidden + c];
+    for (int i = 0; i < top_k; ++i) {
+      const int p = t * top_k + j[i];
+      const int row = pair_rows[p];
+      if (row < 0) continue;  // over capacity: reported through the status word
+      acc = __fadd_rn(acc, __fmul_rn(weights[p], rows[static_cast<long long>(row) * hidden + c]));
+    }
+    y[static_cast<long long>(t) * hidden + c] = acc;
+  }
+}
+
+cudaError_t launch_moe_dispatch(const float* x, int tokens, int hidden, const int32_t* ids,
+                                int top_k, int n_experts, const int* bounds, int world,
+                                int capacity, float* send_x, int32_t* send_ids,
+                                int32_t* pair_rows, unsigned* status, cudaStream_t st) {
+  if (world < 1 || world > kMaxDispatchRanks || capacity < 1 || hidden % 4) return cudaErrorInvalidValue;
+  DispatchBounds bd{};
+  bd.world = world;
+  for (int r = 0; r <= world; ++r) bd.b[r] = bounds[r];
+  const int pairs = tokens * top_k;
+  // unused slots travel as zero rows (quantizing them raises nothing)
+  cudaMemsetAsync(send_x, 0, sizeof(float) * static_cast<size_t>(world) * capacity * hidden, st);
+  dispatch_plan_kernel<<<1, kGroupThreads, 0, st>>>(ids, pairs, n_experts, bd, capacity, send_ids,
+                                                    pair_rows, status);
+  if (pairs > 0)
+    dispatch_rows_kernel<<<pairs, 128, 0, st>>>(x, hidden, top_k, pair_rows, pairs, send_x);
+  return cudaGetLastError();
+}
+
+void launch_moe_combine_rows(const int32_t* ids, const float* weights, const float* rows,
+                             const int32_t* pair_rows, int tokens, int top_k, int hidden, float* y,
+                             cudaStream_t st) {
+  if (tokens > 0)
+    combine_rows_kernel<<<tokens, 256, 0, st>>>(ids, weights, rows, pair_rows, tokens, top_k,
+                                                hidden, y);
 }
 
 // ---------------------------------------------------------------------------
@@ -664,10 +804,18 @@ cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaS
       launch_route(a.logits, T, E, k, a.normalize, a.scale, a.route_ids, a.route_weights,
                    a.status, sms, st);
     group_pairs_kernel<<<1, kGroupThreads, 0, st>>>(a.route_ids, a.route_weights, T, k, E,
-                                                   w.counts, w.offsets, w.pair_token,
-                                                   w.pair_weight, w.token_pos, a.status);
+                                                   a.skip_negative_ids, w.counts, w.offsets,
+                                                   w.pair_token, w.pair_weight, w.token_pos,
+                                                   a.status);
   }
   if (mode != 0) launch_quantize_rows(a.x, a.hidden, T, a.hidden, w.xq, w.xs, a.status, sms, st);
+  if (a.skip_negative_ids && !a.skip_routed) {
+    // unused rows belong to no group and are never written by the projections:
+    // zero them so that the SwiGLU and quantization passes over all rows see 0
+    const size_t hb = sizeof(float) * static_cast<size_t>(T) * k * a.width;
+    cudaMemsetAsync(w.h_r, 0, hb, st);
+    if (w.u_r) cudaMemsetAsync(w.u_r, 0, hb, st);
+  }
   if (path != Path::CudaCore) {
     const cudaError_t e = path == Path::TcInt8   ? prefill_tc(a, w, sms, st)
                           : path == Path::TcFp32 ? prefill_tc_f32(a, w, sms, st)

@@ -290,6 +290,43 @@ def combine_device(ctx: GpuContext, ids_t, wts_t, pair_out_t, y_t):
     return y_t
 
 
+def dispatch_device(ctx: GpuContext, x_t, ids_t, rank_bounds: Sequence[int], capacity: int,
+                    send_x_t=None, send_ids_t=None, pair_rows_t=None):
+    """Fixed-capacity dispatch of (token, expert) pairs to the ranks owning
+    the experts (uocr_moe_dispatch).  Returns (send_x [world * capacity,
+    hidden], send_ids [world * capacity], pair_rows [tokens * top_k])."""
+    import torch
+    tokens, hidden = x_t.shape
+    top_k = ids_t.shape[1]
+    world = len(rank_bounds) - 1
+    dev = x_t.device
+    if send_x_t is None:
+        send_x_t = torch.empty((world * capacity, hidden), dtype=torch.float32, device=dev)
+    if send_ids_t is None:
+        send_ids_t = torch.empty((world * capacity,), dtype=torch.int32, device=dev)
+    if pair_rows_t is None:
+        pair_rows_t = torch.empty((tokens * top_k,), dtype=torch.int32, device=dev)
+    bounds = (ctypes.c_int32 * (world + 1))(*rank_bounds)
+    _check(lib().uocr_moe_dispatch(ctx.handle, ctypes.c_void_p(_tptr(x_t)), tokens, hidden,
+                                   ctypes.c_void_p(_tptr(ids_t)), top_k, bounds, world, capacity,
+                                   ctypes.c_void_p(_tptr(send_x_t)),
+                                   ctypes.c_void_p(_tptr(send_ids_t)),
+                                   ctypes.c_void_p(_tptr(pair_rows_t))))
+    return send_x_t, send_ids_t, pair_rows_t
+
+
+def combine_rows_device(ctx: GpuContext, ids_t, wts_t, rows_t, pair_rows_t, y_t):
+    """uocr_moe_combine_rows: y[t] += w * rows[pair_rows[t * top_k + j]] in
+    ascending expert id.  Asynchronous."""
+    tokens, top_k = ids_t.shape
+    _check(lib().uocr_moe_combine_rows(ctx.handle, ctypes.c_void_p(_tptr(ids_t)),
+                                       ctypes.c_void_p(_tptr(wts_t)),
+                                       ctypes.c_void_p(_tptr(rows_t)),
+                                       ctypes.c_void_p(_tptr(pair_rows_t)), tokens, top_k,
+                                       y_t.shape[1], ctypes.c_void_p(_tptr(y_t))))
+    return y_t
+
+
 class MoeLayer:
     """Decoder::experts over device-resident q8 FFNs (src/decoder/mod.rs:124-220)."""
 
@@ -387,5 +424,5 @@ class MoeLayer:
 
 __all__ = ["BLOCK", "OcrError", "QuantizationMode", "GpuContext", "Int8Matrix", "MoeLayer",
            "route_device", "quantize_rows_device", "linear_multi_device", "default_context",
-           "combine_device",
+           "combine_device", "dispatch_device", "combine_rows_device",
            "LibraryMissing"]

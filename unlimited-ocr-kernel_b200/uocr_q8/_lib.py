@@ -58,6 +58,8 @@ SIGNATURES = {
     "uocr_moe_expert_rows": (I, [P, P, I, P, P, S, P]),
     "uocr_moe_shared_rows": (I, [P, P, I, P, S, P]),
     "uocr_moe_combine": (I, [P, P, P, P, S, S, S, P]),
+    "uocr_moe_dispatch": (I, [P, P, S, S, P, S, P, S, S, P, P, P]),
+    "uocr_moe_combine_rows": (I, [P, P, P, P, P, S, S, S, P]),
 }
 
 _lib = None

@@ -24,12 +24,22 @@ group's row count (src/decoder/mod.rs:103-106: int8 for a single row); in the
 other modes every row's result is independent of its group, so one call
 covers all received rows.
 
+Two forms of the exchange.  With counts (``capacity=None``) the per-rank
+counts are exchanged first and the rows travel in variable-size chunks, which
+needs the counts on the host.  With a fixed ``capacity`` (rows per rank pair,
+``tokens * top_k`` always suffices) every rank sends ``capacity`` rows to every
+rank, unused slots marked by expert id -1 and skipped by the experts: no
+host synchronisation, so a whole step can be captured in a CUDA graph; the
+dispatch (slot assignment and row gather) and the combine (reading the
+returned rows by slot) run on the device.
+
 The collectives are torch.distributed's all_to_all_single: NCCL over NVLink on
-GPUs, gloo on the CPU.  The compute is a backend with four methods
-(``route``, ``expert_rows``, ``shared_rows``, ``combine``); on GPUs it is
-``LibraryBackend``, the CUDA library's C ABI (uocr_moe_route,
-uocr_moe_expert_rows, uocr_moe_shared_rows, uocr_moe_combine), which runs on
-the torch stream current at construction so that collectives and kernels are
+GPUs, gloo on the CPU.  The compute is a backend with the methods ``route``,
+``expert_rows``, ``shared_rows``, ``combine`` (counts form) and ``dispatch``,
+``combine_rows`` (fixed form); on GPUs it is ``LibraryBackend``, the CUDA
+library's C ABI (uocr_moe_route, uocr_moe_expert_rows, uocr_moe_shared_rows,
+uocr_moe_combine, uocr_moe_dispatch, uocr_moe_combine_rows), which runs on the
+torch stream current at construction so that collectives and kernels are
 ordered on one stream.
 """
 from __future__ import annotations
@@ -56,8 +66,10 @@ def expert_bounds(n_experts: int, world: int) -> List[int]:
 class ExpertParallelMoe:
     """One MoE layer whose routed experts are spread over a process group."""
 
-    def __init__(self, backend, n_experts: int, top_k: int, hidden: int, group=None):
+    def __init__(self, backend, n_experts: int, top_k: int, hidden: int, group=None,
+                 capacity=None):
         self.backend = backend
+        self.capacity = capacity
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -96,6 +108,8 @@ class ExpertParallelMoe:
     def forward(self, x, logits, mode: int):
         """(y, ids, weights) for this rank's tokens x [T, hidden] with router
         logits [T, n_experts]."""
+        if self.capacity is not None:
+            return self._forward_fixed(x, logits, mode)
         k, H = self.top_k, self.hidden
         T = x.shape[0]
         ids, wts = self.backend.route(logits)
@@ -128,6 +142,29 @@ class ExpertParallelMoe:
         self.backend.combine(ids, wts, pair_out, y)
         return y, ids, wts
 
+    def _forward_fixed(self, x, logits, mode: int):
+        C, W = self.capacity, self.world
+        if x.shape[0] * self.top_k > C:
+            raise ValueError(f"{x.shape[0]} tokens x top-{self.top_k} exceed capacity {C}")
+        ids, wts = self.backend.route(logits)
+        send_x, send_ids, pair_rows = self.backend.dispatch(x, ids, self.bounds, C)
+        recv_x = torch.empty_like(send_x)
+        recv_ids = torch.empty_like(send_ids)
+        dist.all_to_all_single(recv_x, send_x, group=self.group)
+        dist.all_to_all_single(recv_ids, send_ids, group=self.group)
+        out = torch.empty_like(recv_x)
+        if mode == DYNAMIC_ACTIVATIONS:
+            for r in range(W):
+                seg = slice(r * C, (r + 1) * C)
+                self.backend.expert_rows(recv_x[seg], recv_ids[seg], mode, out[seg])
+        else:
+            self.backend.expert_rows(recv_x, recv_ids, mode, out)
+        back = torch.empty_like(out)
+        dist.all_to_all_single(back, out, group=self.group)
+        y = self.backend.shared_rows(x, mode)
+        self.backend.combine_rows(ids, wts, back, pair_rows, y)
+        return y, ids, wts
+
 
 class LibraryBackend:
     """The CUDA library behind ExpertParallelMoe on one GPU.
@@ -158,6 +195,12 @@ class LibraryBackend:
 
     def combine(self, ids, wts, pair_out, y):
         self._q8.combine_device(self.ctx, ids, wts, pair_out, y)
+
+    def dispatch(self, x, ids, bounds, capacity):
+        return self._q8.dispatch_device(self.ctx, x, ids, bounds, capacity)
+
+    def combine_rows(self, ids, wts, rows, pair_rows, y):
+        self._q8.combine_rows_device(self.ctx, ids, wts, rows, pair_rows, y)
 
 
 def local_layer(ctx, shared: Sequence, experts: Sequence[Sequence], bounds: Sequence[int],
