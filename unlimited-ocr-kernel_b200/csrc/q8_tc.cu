@@ -768,6 +768,55 @@ __global__ void swiglu_split_kernel(const float* __restrict__ g, const float* __
   }
 }
 
+// The same two splits with one CTA per row and the row held in registers: one
+// pass over memory and a CTA-wide maximum (a warp per row walks the row twice
+// with one warp's worth of loads in flight, which made these passes
+// latency-bound when the rows are few).
+constexpr int kSplitThreads = 256;
+constexpr int kSplitMaxV = 8;  // float4 per thread: cols <= 8192
+
+template <bool SWIGLU>
+__global__ void __launch_bounds__(kSplitThreads) split_rows_cta_kernel(
+    const float* __restrict__ x, long long ld_x, const int* __restrict__ src,
+    const float* __restrict__ u, int rows, int cols, uint16_t* __restrict__ pieces,
+    float* __restrict__ rinv, long long piece_elems) {
+  __shared__ float wmax[kSplitThreads / 32];
+  const int r = blockIdx.x;
+  if (r >= rows) return;
+  const int c4 = cols / 4, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float4* xr = reinterpret_cast<const float4*>(
+      SWIGLU ? x + static_cast<long long>(r) * cols : x + (src ? src[r] : r) * ld_x);
+  const float4* ur = reinterpret_cast<const float4*>(u + static_cast<long long>(r) * cols);
+  float4 v[kSplitMaxV];
+  float mx = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kSplitMaxV; ++i) {
+    const int c = threadIdx.x + i * kSplitThreads;
+    if (c < c4) {
+      v[i] = SWIGLU ? swiglu4(xr[c], ur[c]) : xr[c];
+      mx = fmaxf(mx, max_abs4(v[i]));
+    }
+  }
+  mx = warp_max(mx);
+  if (lane == 0) wmax[warp] = mx;
+  __syncthreads();
+  if (warp == 0) {
+    mx = lane < kSplitThreads / 32 ? wmax[lane] : 0.0f;
+    mx = warp_max(mx);
+    if (lane == 0) wmax[0] = mx;
+  }
+  __syncthreads();
+  const int e = row_norm_exp(wmax[0]);
+#pragma unroll
+  for (int i = 0; i < kSplitMaxV; ++i) {
+    const int c = threadIdx.x + i * kSplitThreads;
+    if (c < c4)
+      store_split4(scale_pow2(v[i], e), pieces, static_cast<long long>(r) * cols + 4 * c,
+                   piece_elems);
+  }
+  if (threadIdx.x == 0) rinv[r] = ldexpf(1.0f, -e);
+}
+
 // ---- prefill helpers ---------------------------------------------------------
 // Rows of the block-quantized activations gathered in pair order:
 // xq_p[p] = xq[src[p]], xs_p[p] = xs[src[p]].
@@ -969,14 +1018,24 @@ cudaError_t launch_q8_tc_grouped_f32(const void* maps, int groups, const int* co
 
 void launch_split_rows(const float* x, long long ld_x, const int* src, int rows, int cols,
                        uint16_t* pieces, float* rinv, int sms, cudaStream_t st) {
-  split_rows_kernel<<<grid_for(static_cast<long long>(rows) * 32, sms), 256, 0, st>>>(
-      x, ld_x, src, rows, cols, pieces, rinv, static_cast<long long>(rows) * cols);
+  if (rows <= 0) return;
+  if (cols <= 4 * kSplitThreads * kSplitMaxV)
+    split_rows_cta_kernel<false><<<rows, kSplitThreads, 0, st>>>(
+        x, ld_x, src, nullptr, rows, cols, pieces, rinv, static_cast<long long>(rows) * cols);
+  else
+    split_rows_kernel<<<grid_for(static_cast<long long>(rows) * 32, sms), 256, 0, st>>>(
+        x, ld_x, src, rows, cols, pieces, rinv, static_cast<long long>(rows) * cols);
 }
 
 void launch_swiglu_split(const float* g, const float* u, int rows, int cols, uint16_t* pieces,
                          float* rinv, int sms, cudaStream_t st) {
-  swiglu_split_kernel<<<grid_for(static_cast<long long>(rows) * 32, sms), 256, 0, st>>>(
-      g, u, rows, cols, pieces, rinv, static_cast<long long>(rows) * cols);
+  if (rows <= 0) return;
+  if (cols <= 4 * kSplitThreads * kSplitMaxV)
+    split_rows_cta_kernel<true><<<rows, kSplitThreads, 0, st>>>(
+        g, cols, nullptr, u, rows, cols, pieces, rinv, static_cast<long long>(rows) * cols);
+  else
+    swiglu_split_kernel<<<grid_for(static_cast<long long>(rows) * 32, sms), 256, 0, st>>>(
+        g, u, rows, cols, pieces, rinv, static_cast<long long>(rows) * cols);
 }
 
 void launch_gather_rows(const int8_t* xq, const float* xs, const int* src, int rows, int cols,
