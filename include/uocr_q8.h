@@ -248,6 +248,46 @@ int uocr_moe_combine(uocr_ctx *ctx, const int32_t *ids_dev, const float *weights
 int uocr_moe_forward_decode_noalloc(uocr_ctx *ctx, const uocr_moe *layer, int mode,
                                     const float *x_dev, const float *logits_dev, float *y_dev);
 
+/* ---- INT8 overlay (QuantizedWeights) --------------------------------------
+ * The "uocr-q8-block32-v1" overlay: a safetensors file holding, for every
+ * projection matrix of the source checkpoint, "<name>" (I8 [rows, cols]) and
+ * "<name>.q8_scales" (F32 [rows, ceil(cols/32)]), next to a JSON manifest at
+ * the overlay path with its extension replaced by ".json".
+ *
+ * uocr_overlay_load replaces QuantizedWeights::load(path, &source)
+ * (src/cpu/quantized.rs:304-362): overlay_path is `path`, source_path the
+ * file behind `source` (Checkpoint::open, src/checkpoint.rs:101-166, whose
+ * checks it also applies).  Every check of the reference runs on the host in
+ * the reference's order with its error variant: manifest (Io, Json),
+ * safetensors layout (Format, Json), version and metadata, SHA-256 of the
+ * source and of the overlay, the set of eligible matrices, per matrix dtype /
+ * shape / no byte -128 (Format), then Int8Matrix::from_parts (Shape,
+ * Numerical).  A valid overlay is uploaded into one device allocation on the
+ * context's device (each array 256-byte aligned); nothing is allocated for
+ * an invalid one.  Synchronous.
+ *
+ * uocr_overlay_check: the same validation without a device (no upload);
+ * optional outputs: the matrix count and the device bytes a load takes.
+ *
+ * uocr_overlay_get replaces QuantizedWeights::get (quantized.rs:363-365):
+ * *out = the matrix named `name`, or NULL when the overlay has none (returns
+ * UOCR_OK either way).  The handle belongs to the overlay: do not free it;
+ * it is valid until uocr_overlay_free.  Names enumerate in byte order.
+ *
+ * uocr_sha256_file: lowercase hex SHA-256 of a file (65 bytes with the NUL),
+ * the digest the manifest records (tools/fetch_model.py sha256). */
+typedef struct uocr_overlay uocr_overlay;
+int uocr_overlay_check(const char *overlay_path, const char *source_path, size_t *matrix_count,
+                       size_t *device_bytes);
+int uocr_overlay_load(uocr_ctx *ctx, const char *overlay_path, const char *source_path,
+                      uocr_overlay **out);
+int uocr_overlay_get(const uocr_overlay *overlay, const char *name, const uocr_q8 **out);
+size_t uocr_overlay_count(const uocr_overlay *overlay);
+const char *uocr_overlay_name(const uocr_overlay *overlay, size_t index);
+size_t uocr_overlay_device_bytes(const uocr_overlay *overlay);
+int uocr_overlay_free(uocr_overlay *overlay);
+int uocr_sha256_file(const char *path, char *hex_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -134,10 +134,11 @@ def default_context(device: int = 0) -> GpuContext:
 class Int8Matrix:
     """Device-resident q8-block32 matrix (src/cpu/quantized.rs:11-16)."""
 
-    def __init__(self, handle, ctx: GpuContext, keepalive=None):
+    def __init__(self, handle, ctx: GpuContext, keepalive=None, owned: bool = True):
         self._h = handle
         self.ctx = ctx
         self._keep = keepalive
+        self._owned = owned  # False: a view owned by a QuantizedWeights overlay
         r, c = ctypes.c_size_t(), ctypes.c_size_t()
         _check(lib().uocr_q8_shape(self._h, ctypes.byref(r), ctypes.byref(c)))
         self.rows, self.cols = r.value, c.value
@@ -236,7 +237,8 @@ class Int8Matrix:
 
     def free(self) -> None:
         if getattr(self, "_h", None):
-            lib().uocr_q8_free(self._h)
+            if getattr(self, "_owned", True):
+                lib().uocr_q8_free(self._h)
             self._h = None
 
     def __del__(self):
@@ -425,4 +427,12 @@ class MoeLayer:
 __all__ = ["BLOCK", "OcrError", "QuantizationMode", "GpuContext", "Int8Matrix", "MoeLayer",
            "route_device", "quantize_rows_device", "linear_multi_device", "default_context",
            "combine_device", "dispatch_device", "combine_rows_device",
-           "LibraryMissing"]
+           "LibraryMissing", "QuantizedWeights"]
+
+
+def __getattr__(name):
+    # QuantizedWeights lives in uocr_q8.overlay (imported on first use)
+    if name == "QuantizedWeights":
+        from .overlay import QuantizedWeights
+        return QuantizedWeights
+    raise AttributeError(name)

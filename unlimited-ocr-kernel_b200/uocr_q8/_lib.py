@@ -60,6 +60,15 @@ SIGNATURES = {
     "uocr_moe_combine": (I, [P, P, P, P, S, S, S, P]),
     "uocr_moe_dispatch": (I, [P, P, S, S, P, S, P, S, S, P, P, P]),
     "uocr_moe_combine_rows": (I, [P, P, P, P, P, S, S, S, P]),
+    "uocr_overlay_check": (I, [ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(S),
+                               ctypes.POINTER(S)]),
+    "uocr_overlay_load": (I, [P, ctypes.c_char_p, ctypes.c_char_p, PP]),
+    "uocr_overlay_get": (I, [P, ctypes.c_char_p, PP]),
+    "uocr_overlay_count": (S, [P]),
+    "uocr_overlay_name": (ctypes.c_char_p, [P, S]),
+    "uocr_overlay_device_bytes": (S, [P]),
+    "uocr_overlay_free": (I, [P]),
+    "uocr_sha256_file": (I, [ctypes.c_char_p, ctypes.c_char_p]),
 }
 
 _lib = None
