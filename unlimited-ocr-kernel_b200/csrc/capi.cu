@@ -1027,13 +1027,12 @@ int uocr_moe_forward_host(uocr_ctx* ctx, const uocr_moe* layer, int mode, const 
   int st = moe_checks(ctx, layer, tokens);
   if (st) return st;
   DeviceGuard g(ctx->device);
-  if ((st = take_device_status(ctx))) return st;
   const size_t H = layer->hidden, E = layer->n_experts, k = layer->top_k;
   auto al = [](size_t b) { return (b + 255) & ~static_cast<size_t>(255); };
   const size_t xb = al(tokens * H * 4), lb = al(tokens * E * 4), yb = al(tokens * H * 4),
                rb = al(tokens * k * 4);
-  // Device staging has its own allocation so the layer's workspace (ctx->ws)
-  // can grow independently.
+  // Device staging [x | logits | y | ids | weights] has its own allocation so
+  // the layer's workspace (ctx->ws) can grow independently.
   const size_t need = xb + lb + yb + 2 * rb;
   if (ctx->io_bytes < need) {
     CUDA_TRY(cudaStreamSynchronize(ctx->stream));
@@ -1049,8 +1048,15 @@ int uocr_moe_forward_host(uocr_ctx* ctx, const uocr_moe* layer, int mode, const 
   float* yd = reinterpret_cast<float*>(d + xb + lb);
   int32_t* id = reinterpret_cast<int32_t*>(d + xb + lb + yb);
   float* wd = reinterpret_cast<float*>(d + xb + lb + yb + rb);
-  const bool pin = is_pinned(x) && is_pinned(logits) && is_pinned(y) && (!ids || is_pinned(ids)) &&
-                   (!weights || is_pinned(weights));
+  // Small calls (decode) go through a pinned mirror of the device staging:
+  // one host-to-device copy of [x | logits], one device-to-host copy of the
+  // outputs, one synchronisation (with the status word).  Errors of earlier
+  // asynchronous calls on this context surface at that synchronisation.
+  // Large calls copy straight from/to the caller's buffers when those are
+  // pinned, avoiding two host copies of megabytes.
+  const bool packed = need <= (size_t(1) << 20);
+  const bool pin = !packed && is_pinned(x) && is_pinned(logits) && is_pinned(y) &&
+                   (!ids || is_pinned(ids)) && (!weights || is_pinned(weights));
   char* hp = nullptr;
   if (!pin) {
     if ((st = ensure_pinned(ctx, need))) return st;
@@ -1058,19 +1064,28 @@ int uocr_moe_forward_host(uocr_ctx* ctx, const uocr_moe* layer, int mode, const 
     std::memcpy(hp, x, tokens * H * 4);
     std::memcpy(hp + xb, logits, tokens * E * 4);
   }
-  CUDA_TRY(cudaMemcpyAsync(xd, pin ? x : reinterpret_cast<float*>(hp), tokens * H * 4,
-                           cudaMemcpyHostToDevice, ctx->stream));
-  CUDA_TRY(cudaMemcpyAsync(ld, pin ? logits : reinterpret_cast<float*>(hp + xb), tokens * E * 4,
-                           cudaMemcpyHostToDevice, ctx->stream));
+  if (packed) {
+    CUDA_TRY(cudaMemcpyAsync(xd, hp, xb + tokens * E * 4, cudaMemcpyHostToDevice, ctx->stream));
+  } else {
+    CUDA_TRY(cudaMemcpyAsync(xd, pin ? x : reinterpret_cast<float*>(hp), tokens * H * 4,
+                             cudaMemcpyHostToDevice, ctx->stream));
+    CUDA_TRY(cudaMemcpyAsync(ld, pin ? logits : reinterpret_cast<float*>(hp + xb),
+                             tokens * E * 4, cudaMemcpyHostToDevice, ctx->stream));
+  }
   if ((st = moe_run(ctx, layer, mode, xd, ld, tokens, yd, id, wd))) return st;
-  CUDA_TRY(cudaMemcpyAsync(pin ? y : reinterpret_cast<float*>(hp + xb + lb), yd, tokens * H * 4,
-                           cudaMemcpyDeviceToHost, ctx->stream));
-  if (ids)
-    CUDA_TRY(cudaMemcpyAsync(pin ? ids : reinterpret_cast<int32_t*>(hp + xb + lb + yb), id,
-                             tokens * k * 4, cudaMemcpyDeviceToHost, ctx->stream));
-  if (weights)
-    CUDA_TRY(cudaMemcpyAsync(pin ? weights : reinterpret_cast<float*>(hp + xb + lb + yb + rb), wd,
-                             tokens * k * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  if (packed) {
+    const size_t out = weights ? yb + rb + tokens * k * 4 : ids ? yb + tokens * k * 4 : tokens * H * 4;
+    CUDA_TRY(cudaMemcpyAsync(hp + xb + lb, yd, out, cudaMemcpyDeviceToHost, ctx->stream));
+  } else {
+    CUDA_TRY(cudaMemcpyAsync(pin ? y : reinterpret_cast<float*>(hp + xb + lb), yd, tokens * H * 4,
+                             cudaMemcpyDeviceToHost, ctx->stream));
+    if (ids)
+      CUDA_TRY(cudaMemcpyAsync(pin ? ids : reinterpret_cast<int32_t*>(hp + xb + lb + yb), id,
+                               tokens * k * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    if (weights)
+      CUDA_TRY(cudaMemcpyAsync(pin ? weights : reinterpret_cast<float*>(hp + xb + lb + yb + rb), wd,
+                               tokens * k * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  }
   if ((st = take_device_status(ctx))) return st;
   if (!pin) {
     std::memcpy(y, hp + xb + lb, tokens * H * 4);

@@ -133,6 +133,11 @@ __device__ __forceinline__ float chunk16_dot(uint4 w, const float4 (&x)[4]) {
   return s.x + s.y;
 }
 
+// Barrier among `threads` threads (whole warps) of the CTA, id 1..15.
+__device__ __forceinline__ void named_barrier(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // x staged in shared memory in "chunk-transposed" order: float4 q (q = 0..3)
 // of 16-float chunk c is stored at index q*C + c (C = n/16 chunks), so when
 // lane l reads part q of chunk l, consecutive lanes read consecutive 16-byte

@@ -126,10 +126,10 @@ __device__ __forceinline__ float row_dot_int8(const int8_t* wrow, const float* s
 
 // Block-quantize the CTA's copy of x (cols floats, smem) into xq/xs (smem),
 // the activation step of linear_dynamic_int8 (src/cpu/quantized.rs:169).
-// One warp per 32-column block.  Uses all threads of the CTA.
+// One warp per 32-column block, over warps [0, nw) of the CTA.
 __device__ __forceinline__ void quantize_x_smem(const float* xsm, int cols, int8_t* xq, float* xs,
-                                               unsigned* status) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+                                               int nw, unsigned* status) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nb = blocks_of(cols);
   for (int b = warp; b < nb; b += nw) {
     const int k = b * kBlock + lane;
@@ -170,15 +170,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const __grid_
     }
     fence_mbar_init();
   }
-  if (MODE == MODE_FP32) {
-    stage_x_transposed(xsm, p.x, cols, threadIdx.x, blockDim.x);
-    __syncthreads();
-  } else {
-    for (int k = threadIdx.x; k < cols; k += blockDim.x) xsm[k] = p.x[k];
-    __syncthreads();
-    quantize_x_smem(xsm, cols, xq, xs, p.status);
-    __syncthreads();
-  }
+  __syncthreads();
 
   if (warp == kGemvConsumerWarps) {
     // producer
@@ -209,7 +201,18 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const __grid_
     return;
   }
 
-  // consumers: group g takes this CTA's tiles g, g+4, g+8, ...
+  // consumers: x staged (and quantized) while the producer's first copies
+  // are in flight, then group g takes this CTA's tiles g, g+4, g+8, ...
+  constexpr int kConsumerThreads = kGemvConsumerWarps * 32;
+  if (MODE == MODE_FP32) {
+    stage_x_transposed(xsm, p.x, cols, threadIdx.x, kConsumerThreads);
+    named_barrier(1, kConsumerThreads);
+  } else {
+    for (int k = threadIdx.x; k < cols; k += kConsumerThreads) xsm[k] = p.x[k];
+    named_barrier(1, kConsumerThreads);
+    quantize_x_smem(xsm, cols, xq, xs, kGemvConsumerWarps, p.status);
+    named_barrier(1, kConsumerThreads);
+  }
   const int group = warp / kGemvWarpsPerGroup, wg = warp % kGemvWarpsPerGroup;
   for (int it = group, tile = blockIdx.x + group * gridDim.x; tile < p.total_tiles;
        it += kGemvGroups, tile += kGemvGroups * gridDim.x) {
