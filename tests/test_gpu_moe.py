@@ -139,6 +139,46 @@ def test_decode_device_repeatable(ctx, config1):
     assert torch.equal(a, b)
 
 
+def test_decode_host_calls_replay_graphs(ctx, config1):
+    """The host-buffer decode call runs eagerly for the first call of a
+    (layer, mode) and from a captured graph afterwards: every call equals
+    the device-pointer call bit for bit, across two layers and both modes
+    interleaved, and an error raised inside a replayed graph is reported and
+    cleared."""
+    import torch
+    from uocr_q8 import _ptr, lib, _check
+    layer_a = config1[0]
+    rng = np.random.default_rng(9)
+    layer_b = make_layer(ctx, rng, 1280, 896, 1792, 64, 6)[0]
+    for call in range(6):
+        for layer in (layer_a, layer_b):
+            for mode in (0, 1):
+                x = rng.standard_normal((1, 1280)).astype(np.float32)
+                lg = rng.standard_normal((1, 64)).astype(np.float32)
+                y, ids, wts = layer.forward(x, lg, mode)
+                yd = layer.forward_device(torch.from_numpy(x).cuda(), torch.from_numpy(lg).cuda(),
+                                          mode)
+                ctx.sync()
+                assert bits_equal(y, yd.cpu().numpy()), (call, mode)
+                # y only (no routing outputs): the same graph family, other key
+                y2 = np.empty_like(x)
+                _check(lib().uocr_moe_forward_host(ctx.handle, layer._h, mode, _ptr(x), _ptr(lg),
+                                                   1, _ptr(y2), None, None))
+                assert bits_equal(y2, y)
+    bad = np.zeros((1, 64), np.float32)
+    bad[0, 5] = np.nan
+    with pytest.raises(q8().OcrError) as e:
+        layer_a.forward(np.zeros((1, 1280), np.float32), bad, 0)
+    assert e.value.kind == "Numerical"
+    x = rng.standard_normal((1, 1280)).astype(np.float32)
+    lg = rng.standard_normal((1, 64)).astype(np.float32)
+    y, _, _ = layer_a.forward(x, lg, 0)  # the status was cleared
+    yd = layer_a.forward_device(torch.from_numpy(x).cuda(), torch.from_numpy(lg).cuda(), 0)
+    ctx.sync()
+    assert bits_equal(y, yd.cpu().numpy())
+    layer_b.free()
+
+
 def test_decode_rejects_bad_logits(ctx, config1):
     layer = config1[0]
     x = np.zeros((1, 1280), np.float32)

@@ -7,6 +7,7 @@
 // reference's Tensor-in / Tensor-out methods.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -111,12 +112,9 @@ bool is_pinned(const void* p) {
   return a.type == cudaMemoryTypeHost;
 }
 
-// Maps the device status word to the reference's error variants.
-int take_device_status(uocr_ctx* ctx) {
-  CUDA_TRY(cudaMemcpyAsync(ctx->status_host, ctx->status_dev, sizeof(unsigned),
-                           cudaMemcpyDeviceToHost, ctx->stream));
-  CUDA_TRY(cudaStreamSynchronize(ctx->stream));
-  const unsigned st = *ctx->status_host;
+// Maps a device status word to the reference's error variants (clearing the
+// context's word when it is set).
+int status_result(uocr_ctx* ctx, unsigned st) {
   if (!st) return ok();
   CUDA_TRY(cudaMemsetAsync(ctx->status_dev, 0, sizeof(unsigned), ctx->stream));
   CUDA_TRY(cudaStreamSynchronize(ctx->stream));
@@ -134,6 +132,14 @@ int take_device_status(uocr_ctx* ctx) {
   if (st & DEV_CAPACITY)
     return fail(UOCR_ERR_RESOURCE, "resource limit exceeded: expert dispatch capacity");
   return fail(UOCR_ERR_CUDA, "unknown device status 0x%x", st);
+}
+
+// Reads (synchronously) and maps the context's device status word.
+int take_device_status(uocr_ctx* ctx) {
+  CUDA_TRY(cudaMemcpyAsync(ctx->status_host, ctx->status_dev, sizeof(unsigned),
+                           cudaMemcpyDeviceToHost, ctx->stream));
+  CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  return status_result(ctx, *ctx->status_host);
 }
 
 int check_launch() {
@@ -230,6 +236,9 @@ int uocr_ctx_destroy(uocr_ctx* ctx) {
   if (!ctx) return ok();
   DeviceGuard g(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  for (auto& hg : ctx->host_graphs)
+    if (hg.exec) cudaGraphExecDestroy(hg.exec);
+  if (ctx->capture_stream) cudaStreamDestroy(ctx->capture_stream);
   if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->io) cudaFree(ctx->io);
   if (ctx->pinned) cudaFreeHost(ctx->pinned);
@@ -739,7 +748,9 @@ int uocr_moe_create(uocr_ctx* ctx, const uocr_q8* shared_gate, const uocr_q8* sh
   }
   aligned = aligned && al(shared_gate) && al(shared_up) && al(shared_down);
   DeviceGuard g(ctx->device);
+  static std::atomic<uint64_t> next_serial{1};
   auto* L = new uocr_moe();
+  L->serial = next_serial.fetch_add(1);
   L->device = ctx->device;
   L->n_experts = n_experts;
   L->top_k = top_k;
@@ -804,40 +815,59 @@ static int moe_checks(const uocr_ctx* ctx, const uocr_moe* L, size_t tokens) {
   return ok();
 }
 
+// Arguments of the one-token decode kernel, and whether the layer and x
+// qualify for it.  Its workspace: h, plus the routing when the caller does
+// not want it back.
+static bool decode_args(const uocr_ctx* ctx, const uocr_moe* L, const float* x, MoeDecodeArgs* a) {
+  *a = MoeDecodeArgs{};
+  a->experts = L->experts_dev;
+  a->shared = L->shared;
+  a->n_experts = static_cast<int>(L->n_experts);
+  a->top_k = static_cast<int>(L->top_k);
+  a->normalize = L->normalize;
+  a->scale = L->scale;
+  a->hidden = L->hidden;
+  a->width = L->width;
+  a->shared_width = L->shared_width;
+  return L->aligned && moe_decode_supported(*a, ctx->sms) &&
+         reinterpret_cast<uintptr_t>(x) % 16 == 0;
+}
+
+static size_t decode_h_bytes(int shared_width, int top_k, int width) {
+  const size_t hn = static_cast<size_t>(shared_width) + static_cast<size_t>(top_k) * width;
+  return (hn * 4 + 255) & ~static_cast<size_t>(255);
+}
+
+// Launches the decode kernel with `a` from decode_args (workspace present).
+static int decode_launch(uocr_ctx* ctx, int mode, MoeDecodeArgs& a, const float* x,
+                         const float* logits, float* y, int32_t* ids, float* wts, bool pdl) {
+  const size_t hb = decode_h_bytes(a.shared_width, a.top_k, a.width);
+  const bool own_route = !ids || !wts;
+  a.x = x;
+  a.logits = logits;
+  a.h = static_cast<float*>(ctx->ws);
+  a.route_ids = own_route ? reinterpret_cast<int32_t*>(static_cast<char*>(ctx->ws) + hb) : ids;
+  a.route_weights = own_route ? reinterpret_cast<float*>(static_cast<char*>(ctx->ws) + hb + 256)
+                              : wts;
+  a.y = y;
+  a.status = ctx->status_dev;
+  a.grid_sync = ctx->status_dev + 16;  // zeroed at context creation, decode-only
+  cudaError_t e = launch_moe_decode(mode == UOCR_WEIGHTS_ONLY ? MODE_FP32 : MODE_INT8, a, ctx->sms,
+                                    ctx->stream, pdl);
+  if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "moe decode launch: %s", cudaGetErrorString(e));
+  return check_launch();
+}
+
 static int moe_run(uocr_ctx* ctx, const uocr_moe* L, int mode, const float* x, const float* logits,
                    size_t tokens, float* y, int32_t* ids, float* wts) {
   const int k = static_cast<int>(L->top_k);
   // decode fast path: one token, every projection single-row
   if (tokens == 1) {
-    MoeDecodeArgs a{};
-    a.experts = L->experts_dev;
-    a.shared = L->shared;
-    a.n_experts = static_cast<int>(L->n_experts);
-    a.top_k = k;
-    a.normalize = L->normalize;
-    a.scale = L->scale;
-    a.hidden = L->hidden;
-    a.width = L->width;
-    a.shared_width = L->shared_width;
-    if (L->aligned && moe_decode_supported(a, ctx->sms) && reinterpret_cast<uintptr_t>(x) % 16 == 0) {
-      const size_t hn = L->shared_width + static_cast<size_t>(k) * L->width;
-      const size_t hb = (hn * 4 + 255) & ~static_cast<size_t>(255);
-      const bool own_route = !ids || !wts;
-      int st = ensure_ws(ctx, hb + (own_route ? 512 : 0));
+    MoeDecodeArgs a;
+    if (decode_args(ctx, L, x, &a)) {
+      int st = ensure_ws(ctx, decode_h_bytes(a.shared_width, a.top_k, a.width) + 512);
       if (st) return st;
-      a.x = x;
-      a.logits = logits;
-      a.h = static_cast<float*>(ctx->ws);
-      a.route_ids = own_route ? reinterpret_cast<int32_t*>(static_cast<char*>(ctx->ws) + hb) : ids;
-      a.route_weights = own_route ? reinterpret_cast<float*>(static_cast<char*>(ctx->ws) + hb + 256)
-                                  : wts;
-      a.y = y;
-      a.status = ctx->status_dev;
-      a.grid_sync = ctx->status_dev + 16;  // zeroed at context creation, decode-only
-      cudaError_t e = launch_moe_decode(mode == UOCR_WEIGHTS_ONLY ? MODE_FP32 : MODE_INT8, a,
-                                        ctx->sms, ctx->stream);
-      if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "moe decode launch: %s", cudaGetErrorString(e));
-      return check_launch();
+      return decode_launch(ctx, mode, a, x, logits, y, ids, wts, true);
     }
   }
   MoePrefillArgs a{};
@@ -1016,6 +1046,98 @@ int uocr_moe_combine(uocr_ctx* ctx, const int32_t* ids_dev, const float* weights
   return check_launch();
 }
 
+// The host-buffer decode call as one captured graph per (layer, mode,
+// buffers): copy [x | logits] in, the decode kernel, copy y (and the routing)
+// and the status word out.  One launch and one synchronisation per call
+// instead of four enqueues.  *done
+// is false when the layer does not take the decode kernel or capture is not
+// available; the caller then runs the eager path.
+constexpr size_t kMaxHostGraphs = 8;
+
+static int host_decode_graph(uocr_ctx* ctx, const uocr_moe* L, int mode, size_t xb, size_t lb,
+                             size_t yb, size_t rb, bool outs, bool* done) {
+  *done = false;
+  HostDecodeGraph* g = nullptr;
+  for (auto& e : ctx->host_graphs)
+    if (e.layer == L && e.serial == L->serial && e.mode == mode && e.outs == outs &&
+        e.io == ctx->io && e.ws == ctx->ws && e.pinned == ctx->pinned) {
+      g = &e;
+      break;
+    }
+  if (!g || !g->exec) {
+    // the first call for a key runs eagerly (sizing the workspace, configuring
+    // the kernel); the second captures the graph
+    if (!g) {
+      if (ctx->host_graphs.size() >= kMaxHostGraphs) {
+        if (ctx->host_graphs.front().exec) cudaGraphExecDestroy(ctx->host_graphs.front().exec);
+        ctx->host_graphs.erase(ctx->host_graphs.begin());
+      }
+      HostDecodeGraph seen;
+      seen.layer = L;
+      seen.serial = L->serial;
+      seen.mode = mode;
+      seen.outs = outs;
+      seen.io = ctx->io;
+      seen.ws = ctx->ws;
+      seen.pinned = ctx->pinned;
+      ctx->host_graphs.push_back(seen);
+      return ok();
+    }
+    char* d = static_cast<char*>(ctx->io);
+    const float* xd = reinterpret_cast<const float*>(d);
+    MoeDecodeArgs a;
+    if (!decode_args(ctx, L, xd, &a)) return ok();
+    int st = ensure_ws(ctx, decode_h_bytes(a.shared_width, a.top_k, a.width) + 512);
+    if (st) return st;
+    char* hp = static_cast<char*>(ctx->pinned);
+    if (!ctx->capture_stream)
+      CUDA_TRY(cudaStreamCreateWithFlags(&ctx->capture_stream, cudaStreamNonBlocking));
+    cudaStream_t saved = ctx->stream;
+    ctx->stream = ctx->capture_stream;
+    cudaGraph_t graph = nullptr;
+    int lst = UOCR_OK;
+    cudaError_t e = cudaStreamBeginCapture(ctx->capture_stream, cudaStreamCaptureModeThreadLocal);
+    if (e == cudaSuccess) {
+      e = cudaMemcpyAsync(d, hp, xb + L->n_experts * 4, cudaMemcpyHostToDevice,
+                          ctx->capture_stream);
+      if (e == cudaSuccess)
+        lst = decode_launch(ctx, mode, a, xd, reinterpret_cast<const float*>(d + xb),
+                            reinterpret_cast<float*>(d + xb + lb),
+                            outs ? reinterpret_cast<int32_t*>(d + xb + lb + yb) : nullptr,
+                            outs ? reinterpret_cast<float*>(d + xb + lb + yb + rb) : nullptr,
+                            false);
+      // outputs back by one copy node (a measured 4 us faster than the kernel
+      // storing them into pinned memory itself)
+      if (e == cudaSuccess && !lst)
+        e = cudaMemcpyAsync(hp + xb + lb, d + xb + lb,
+                            outs ? yb + rb + L->top_k * 4 : static_cast<size_t>(L->hidden) * 4,
+                            cudaMemcpyDeviceToHost, ctx->capture_stream);
+      if (e == cudaSuccess && !lst)
+        e = cudaMemcpyAsync(ctx->status_host, ctx->status_dev, sizeof(unsigned),
+                            cudaMemcpyDeviceToHost, ctx->capture_stream);
+      const cudaError_t e2 = cudaStreamEndCapture(ctx->capture_stream, &graph);
+      if (e == cudaSuccess) e = e2;
+    }
+    ctx->stream = saved;
+    cudaGraphExec_t exec = nullptr;
+    if (e == cudaSuccess && !lst && graph) e = cudaGraphInstantiate(&exec, graph, 0);
+    if (graph) cudaGraphDestroy(graph);
+    if (e != cudaSuccess || lst || !exec) {
+      cudaGetLastError();
+      if (exec) cudaGraphExecDestroy(exec);
+      return ok();
+    }
+    g->ws = ctx->ws;  // ensure_ws above may have grown it
+    g->exec = exec;
+  }
+  CUDA_TRY(cudaGraphLaunch(g->exec, ctx->stream));
+  CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  int st = status_result(ctx, *ctx->status_host);
+  if (st) return st;
+  *done = true;
+  return ok();
+}
+
 int uocr_moe_forward_host(uocr_ctx* ctx, const uocr_moe* layer, int mode, const float* x,
                           const float* logits, size_t tokens, float* y, int32_t* ids,
                           float* weights) {
@@ -1063,6 +1185,18 @@ int uocr_moe_forward_host(uocr_ctx* ctx, const uocr_moe* layer, int mode, const 
     hp = static_cast<char*>(ctx->pinned);
     std::memcpy(hp, x, tokens * H * 4);
     std::memcpy(hp + xb, logits, tokens * E * 4);
+  }
+  // one token, routing returned in full or not at all: the captured graph
+  if (packed && tokens == 1 && (!ids) == (!weights)) {
+    bool done = false;
+    if ((st = host_decode_graph(ctx, layer, mode, xb, lb, yb, rb, ids != nullptr, &done)))
+      return st;
+    if (done) {
+      std::memcpy(y, hp + xb + lb, H * 4);
+      if (ids) std::memcpy(ids, hp + xb + lb + yb, k * 4);
+      if (weights) std::memcpy(weights, hp + xb + lb + yb + rb, k * 4);
+      return ok();
+    }
   }
   if (packed) {
     CUDA_TRY(cudaMemcpyAsync(xd, hp, xb + tokens * E * 4, cudaMemcpyHostToDevice, ctx->stream));

@@ -5,7 +5,24 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <vector>
+
 #include "kernels.h"
+
+struct uocr_moe;
+
+// One instantiated graph of the host-buffer decode call (copy in, decode
+// kernel writing into pinned memory, status copy out), valid while the
+// buffers it captured are the context's current ones.
+struct HostDecodeGraph {
+  const uocr_moe* layer = nullptr;
+  uint64_t serial = 0;
+  int mode = 0, outs = 0;
+  const void* io = nullptr;
+  const void* ws = nullptr;
+  const void* pinned = nullptr;
+  cudaGraphExec_t exec = nullptr;
+};
 
 struct uocr_ctx {
   int device = 0;
@@ -21,6 +38,8 @@ struct uocr_ctx {
   size_t pinned_bytes = 0;
   void* io = nullptr;  // device staging of the *_host MoE entry point
   size_t io_bytes = 0;
+  std::vector<HostDecodeGraph> host_graphs;  // at most kMaxHostGraphs, oldest replaced
+  cudaStream_t capture_stream = nullptr;
 };
 
 struct uocr_q8 {
@@ -33,6 +52,7 @@ struct uocr_q8 {
 
 struct uocr_moe {
   int device = 0;
+  uint64_t serial = 0;  // unique per created layer (graph cache key)
   size_t n_experts = 0, top_k = 0;
   int normalize = 0;
   float scale = 1.0f;

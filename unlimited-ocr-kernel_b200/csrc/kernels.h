@@ -123,7 +123,10 @@ struct MoeDecodeArgs {
   unsigned* grid_sync;  // 4 words, zero before first use, owned by this stream
 };
 bool moe_decode_supported(const MoeDecodeArgs& a, int sms);
-cudaError_t launch_moe_decode(int mode, const MoeDecodeArgs& a, int sms, cudaStream_t st);
+// pdl: allow programmatic dependent launch of the next kernel (off for
+// launches captured after a copy node).
+cudaError_t launch_moe_decode(int mode, const MoeDecodeArgs& a, int sms, cudaStream_t st,
+                              bool pdl = true);
 
 // moe_prefill.cu — many tokens: route, group by expert, grouped projections,
 // ordered combine.

@@ -630,7 +630,7 @@ bool moe_decode_supported(const MoeDecodeArgs& a, int sms) {
          L.part_off + part_bytes(a, L.rows_max) <= L.slots * L.stage_bytes;
 }
 
-cudaError_t launch_moe_decode(int mode, const MoeDecodeArgs& a, int sms, cudaStream_t st) {
+cudaError_t launch_moe_decode(int mode, const MoeDecodeArgs& a, int sms, cudaStream_t st, bool pdl) {
   if (!moe_decode_supported(a, sms) || !a.grid_sync) return cudaErrorInvalidValue;
   const int grid = a.hidden < sms ? a.hidden : sms;
   const DecodeLayout L = decode_layout(a, grid);
@@ -670,9 +670,9 @@ cudaError_t launch_moe_decode(int mode, const MoeDecodeArgs& a, int sms, cudaStr
   cfg.dynamicSmemBytes = L.total;
   cfg.stream = st;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = pdl ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, fn, a, L);
-  if (e != cudaSuccess) {
+  if (e != cudaSuccess && pdl) {
     cudaGetLastError();
     cfg.numAttrs = 1;  // cooperative only
     e = cudaLaunchKernelEx(&cfg, fn, a, L);
