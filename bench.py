@@ -804,6 +804,78 @@ def ep_cpu_baseline(args):
             "kind": "port", "sample": f"{n} batches of 64 tokens through one MoE layer in {dt:.1f} s"}
 
 
+ATTN_BATCH, ATTN_HEADS, ATTN_DIM, ATTN_PREFIX, ATTN_WINDOW = 64, 10, 128, 2048, 128
+ATTN_TOKENS = ATTN_PREFIX + ATTN_WINDOW
+# keys + values read per layer step: every token of every sequence, 4 B each
+ATTN_BYTES = ATTN_BATCH * ATTN_TOKENS * ATTN_HEADS * ATTN_DIM * 4 * 2
+
+
+def run_attn(args):
+    """Config 4's attention (secondary workload): one decode step of
+    ops::attention_decode for 64 sequences (10 heads x 128) over a KV cache
+    of a 2048-token prefix plus a full 128-token ring, through
+    uocr_kv_attention; value = KV bytes read / device time."""
+    import torch
+
+    import uocr_q8
+    from uocr_q8.attention import KvCache
+    torch.cuda.set_device(0)
+    dev = "cuda:0"
+    ctx = uocr_q8.GpuContext(0)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream)
+    W = ATTN_HEADS * ATTN_DIM
+    n_layers = 2  # 2 x 1.43 GB caches rotated (> L2)
+    caches = []
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    with torch.cuda.stream(stream):
+        for _ in range(n_layers):
+            kv = KvCache(ctx, ATTN_BATCH, ATTN_HEADS, ATTN_DIM, ATTN_WINDOW, ATTN_PREFIX)
+            for b in range(ATTN_BATCH):
+                k = torch.randn((ATTN_PREFIX, W), device=dev, generator=g)
+                kv.prefill(b, k, k.mul(0.5))
+            for _ in range(ATTN_WINDOW):  # fill the ring
+                r = torch.randn((ATTN_BATCH, W), device=dev, generator=g)
+                kv.push(r, r)
+            caches.append(kv)
+        q = torch.randn((ATTN_BATCH, W), device=dev, generator=g) * 0.05
+        out = torch.empty_like(q)
+    ctx.sync()
+    steps = max(4, min(args.steps, 400))
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            caches[i % n_layers].attention(q, out)
+    ctx.sync()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for i in range(steps):
+                caches[i % n_layers].attention(q, out)
+            stop.record(stream)
+        stop.synchronize()
+    ctx.sync()
+    ms = start.elapsed_time(stop) / steps
+    gbs = ATTN_BYTES / (ms * 1e-3) / 1e9
+    peak, peak_kind = peak_hbm()
+    res = {"metric": "decode attention KV GB/s (config 4 attention, batch 64)",
+           "value": round(gbs, 2), "unit": "GB/s", "n_gpus": 1, "steps": steps,
+           "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded)",
+           "config": {"workload": "config4_attention_decode", "batch": ATTN_BATCH,
+                      "heads": ATTN_HEADS, "head_dim": ATTN_DIM, "prefix": ATTN_PREFIX,
+                      "window": ATTN_WINDOW, "bytes_per_step": ATTN_BYTES,
+                      "l2": "2 caches x 1.43 GB rotated (> 126 MB L2)"},
+           "roofline": {"bound": "hbm", "kernel": "attn_decode_kernel", "achieved": round(gbs, 2),
+                        "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                        "frac": round(gbs / peak, 4), "traffic": args.traffic},
+           "gpu_launches": steps, "clocks": clocks.summary()}
+    for kv in caches:
+        kv.free()
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -820,7 +892,8 @@ def main():
                     help="dram bytes per launch from an ncu capture (roofline.traffic); "
                          "defaults to the committed capture of the workload's kernel")
     ap.add_argument("--workload",
-                    choices=["moe_decode", "gemv", "prefill", "int8suite", "ep_decode"],
+                    choices=["moe_decode", "gemv", "prefill", "int8suite", "ep_decode",
+                             "attn_decode"],
                     default="moe_decode")
     ap.add_argument("--gemv-int8", action="store_true")
     ap.add_argument("--prefill-mode", type=int, choices=[0, 2], default=0)
@@ -836,6 +909,9 @@ def main():
         res = run_ep(args)
         if res is not None:
             print(json.dumps(res), flush=True)
+        return
+    if args.workload == "attn_decode" and args.impl == "ours":
+        print(json.dumps(run_attn(args)), flush=True)
         return
     if args.workload == "int8suite" and args.impl == "ours":
         print(json.dumps(run_int8suite(args)), flush=True)

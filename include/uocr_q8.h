@@ -248,6 +248,68 @@ int uocr_moe_combine(uocr_ctx *ctx, const int32_t *ids_dev, const float *weights
 int uocr_moe_forward_decode_noalloc(uocr_ctx *ctx, const uocr_moe *layer, int mode,
                                     const float *x_dev, const float *logits_dev, float *y_dev);
 
+/* ---- decoder attention at decode --------------------------------------------
+ * The attention half of Decoder::layer (src/decoder/mod.rs:241-341) for one
+ * new token per sequence, on device pointers, asynchronous on the context's
+ * stream.  Arithmetic follows the reference's order (sequential sums, one
+ * rounding per operation); results equal the reference's bit for bit
+ * except where exp rounds differently (rarely one ulp of a softmax weight).
+ * Input errors found on the device (nonfinite norm input, a position past the
+ * rotary table, a cache used before its prefill) are reported at the next
+ * synchronising call, as for the other entry points. */
+typedef struct uocr_rope uocr_rope;
+typedef struct uocr_kv uocr_kv;
+
+/* ops::rms_norm (src/cpu/ops.rs:362-414,419-421): rows x width, weight of
+ * width floats; out may equal x.  Shape for width 0 or eps not finite and
+ * positive; Numerical ("normalization") for a nonfinite input or weight. */
+int uocr_rms_norm(uocr_ctx *ctx, const float *x_dev, size_t rows, size_t width,
+                  const float *weight_dev, float eps, float *out_dev);
+
+/* ops::rope (src/cpu/ops.rs:423-437): a table of cos/sin for positions
+ * [0, max_positions), built on the host with the reference's single-precision
+ * operations; uocr_rope_apply rotates q (and k unless NULL) in place, rows x
+ * width in heads of head_dim, row r at positions_dev[r] (int32).  A position
+ * outside the table is Resource ("maximum context exceeded"). */
+int uocr_rope_create(uocr_ctx *ctx, size_t head_dim, float theta, size_t max_positions,
+                     uocr_rope **out);
+int uocr_rope_free(uocr_rope *rope);
+int uocr_rope_apply(uocr_ctx *ctx, const uocr_rope *rope, float *q_dev, float *k_dev, size_t rows,
+                    size_t width, const int32_t *positions_dev);
+
+/* ops::attention_decode (src/cpu/ops.rs:515-606): one query q [1 x width]
+ * over token-major keys/values (keys_len = values_len = tokens * width),
+ * heads of width/heads; out [width].  Same layout and scratch checks. */
+int uocr_attention_decode(uocr_ctx *ctx, const float *q_dev, const float *keys_dev,
+                          size_t keys_len, const float *values_dev, size_t values_len,
+                          size_t width, size_t heads, float *out_dev);
+
+/* LayerCache (src/decoder/cache.rs) for `batch` sequences on the device:
+ * token-major keys/values, an immutable prefix of up to max_prefix tokens
+ * followed by a ring of `window` tokens (slot of a new token: prefix +
+ * generated % window).  The per-sequence counters live in device memory, so
+ * push, rope and attention can be captured in CUDA graphs.
+ *   uocr_kv_prefill: LayerCache::prefill of sequence seq (device rows);
+ *   uocr_kv_push:    LayerCache::push of row b of k/v ([batch x width]) into
+ *                    every sequence b;
+ *   uocr_kv_rope:    ops::rope of q and k rows at each sequence's position
+ *                    (before this token's push);
+ *   uocr_kv_attention: ops::attention_decode of q row b over sequence b;
+ *   uocr_kv_state:   LayerCache::tokens and ::position (synchronous).
+ * push / rope / attention before every sequence is prefilled: Shape. */
+int uocr_kv_create(uocr_ctx *ctx, size_t batch, size_t heads, size_t head_dim, size_t window,
+                   size_t max_prefix, uocr_kv **out);
+int uocr_kv_free(uocr_kv *kv);
+int uocr_kv_prefill(uocr_ctx *ctx, uocr_kv *kv, size_t seq, const float *keys_dev,
+                    const float *values_dev, size_t tokens);
+int uocr_kv_push(uocr_ctx *ctx, uocr_kv *kv, const float *k_dev, const float *v_dev);
+int uocr_kv_rope(uocr_ctx *ctx, const uocr_kv *kv, const uocr_rope *rope, float *q_dev,
+                 float *k_dev);
+int uocr_kv_attention(uocr_ctx *ctx, const uocr_kv *kv, const float *q_dev, float *out_dev);
+int uocr_kv_state(uocr_ctx *ctx, const uocr_kv *kv, size_t seq, size_t *tokens, size_t *position);
+int uocr_kv_buffers(const uocr_kv *kv, const float **keys_dev, const float **values_dev,
+                    size_t *cap);
+
 /* ---- INT8 overlay (QuantizedWeights) --------------------------------------
  * The "uocr-q8-block32-v1" overlay: a safetensors file holding, for every
  * projection matrix of the source checkpoint, "<name>" (I8 [rows, cols]) and

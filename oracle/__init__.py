@@ -79,6 +79,9 @@ def _declare(L):
         "q8o_linear_bf16": (I, [P, S, S, P, S, P]),
         "q8o_feed_forward": (I, [P, P, S, I, P]),
         "q8o_experts": (I, [P, P, S, P, P, S, S, S, I, F, I, P, P, P]),
+        "q8o_rms_norm": (I, [P, S, S, P, F, P]),
+        "q8o_rope": (I, [P, S, S, S, F]),
+        "q8o_attention_decode": (I, [P, S, P, S, P, S, S, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -236,3 +239,80 @@ def experts(shared: Ffn, routed: list, logits, x, top_k: int, mode: int = WEIGHT
                              hidden, top_k, int(bool(normalize)), float(scale), mode, _ptr(out),
                              _ptr(ids), _ptr(wts)))
     return out, ids, wts
+
+
+def rms_norm(x, weight, eps: float = 1e-6) -> np.ndarray:
+    """ops::rms_norm over the last dimension."""
+    x = _contig(x, np.float32)
+    w = _contig(weight, np.float32)
+    width = x.shape[-1] if x.ndim else 0
+    out = np.empty_like(x)
+    rows = x.size // width if width else 0
+    _check(lib().q8o_rms_norm(_ptr(x), rows, width, _ptr(w), float(eps), _ptr(out)))
+    return out
+
+
+def rope(values, head_dim: int, position: int, theta: float = 10000.0) -> np.ndarray:
+    """ops::rope of one row (every head) at one position; returns a copy."""
+    v = np.array(values, dtype=np.float32, copy=True)
+    _check(lib().q8o_rope(_ptr(v), v.size, head_dim, position, float(theta)))
+    return v
+
+
+def attention_decode(q, keys, values, heads: int) -> np.ndarray:
+    """ops::attention_decode: q [width] over token-major keys/values."""
+    q = _contig(q, np.float32).reshape(-1)
+    k = _contig(keys, np.float32).reshape(-1)
+    v = _contig(values, np.float32).reshape(-1)
+    out = np.empty_like(q)
+    _check(lib().q8o_attention_decode(_ptr(q), q.size, _ptr(k), k.size, _ptr(v), v.size, heads,
+                                      _ptr(out)))
+    return out
+
+
+class LayerCache:
+    """LayerCache (src/decoder/cache.rs:3-95): token-major keys/values, an
+    immutable prefix followed by a ring of `window` tokens."""
+
+    def __init__(self, heads: int, head_dim: int, window: int):
+        if heads * head_dim <= 0:
+            raise OracleError(4)
+        if window == 0:
+            raise OracleError(4)
+        self.width, self.window = heads * head_dim, window
+        self.prefix = None
+        self.generated = 0
+        self.keys = np.zeros((0, self.width), np.float32)
+        self.values = np.zeros((0, self.width), np.float32)
+
+    def prefill(self, keys, values, tokens: int) -> None:
+        keys = _contig(keys, np.float32).reshape(-1)
+        values = _contig(values, np.float32).reshape(-1)
+        if self.prefix is not None or tokens == 0 or tokens * self.width != keys.size or \
+                keys.size != values.size:
+            raise OracleError(4)
+        self.keys = keys.reshape(tokens, self.width).copy()
+        self.values = values.reshape(tokens, self.width).copy()
+        self.prefix = tokens
+
+    def push(self, key, value) -> None:
+        if self.prefix is None:
+            raise OracleError(4)
+        key = _contig(key, np.float32).reshape(-1)
+        value = _contig(value, np.float32).reshape(-1)
+        if key.size != self.width or value.size != self.width:
+            raise OracleError(4)
+        if self.generated < self.window:
+            self.keys = np.vstack([self.keys, key[None]])
+            self.values = np.vstack([self.values, value[None]])
+        else:
+            slot = self.prefix + self.generated % self.window
+            self.keys[slot] = key
+            self.values[slot] = value
+        self.generated += 1
+
+    def tokens(self) -> int:
+        return self.keys.shape[0]
+
+    def position(self) -> int:
+        return (self.prefix or 0) + self.generated

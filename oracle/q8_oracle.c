@@ -413,3 +413,78 @@ int q8o_experts(const q8o_ffn *shared, const q8o_ffn *experts, size_t n_experts,
   free(result);
   return st;
 }
+
+/* src/cpu/ops.rs:362-414 with center = false (rms_norm, :419-421): shape
+ * checks, nonfinite input or weight -> Numerical, then per row the squares
+ * summed left to right from -0.0, divided by the width, sqrt, reciprocal,
+ * and (x - 0) * scale * w + 0 per element. */
+int q8o_rms_norm(const float *x, size_t rows, size_t width, const float *weight, float eps,
+                 float *out) {
+  if (width == 0 || !isfinite(eps) || eps <= 0.0f) return Q8O_SHAPE;
+  for (size_t i = 0; i < rows * width; ++i)
+    if (!isfinite(x[i])) return Q8O_NUMERICAL;
+  for (size_t i = 0; i < width; ++i)
+    if (!isfinite(weight[i])) return Q8O_NUMERICAL;
+  for (size_t r = 0; r < rows; ++r) {
+    const float *in = x + r * width;
+    float *o = out + r * width;
+    const float mean = 0.0f;
+    float variance = -0.0f;
+    for (size_t i = 0; i < width; ++i) variance += (in[i] - mean) * (in[i] - mean);
+    variance /= (float)width;
+    const float scale = 1.0f / sqrtf(variance + eps);
+    for (size_t i = 0; i < width; ++i) o[i] = (in[i] - mean) * scale * weight[i] + 0.0f;
+  }
+  return Q8O_OK;
+}
+
+/* src/cpu/ops.rs:423-437 */
+int q8o_rope(float *values, size_t n, size_t head_dim, size_t position, float theta) {
+  if (head_dim == 0 || head_dim % 2 || n % head_dim || !isfinite(theta) || theta <= 0.0f)
+    return Q8O_SHAPE;
+  const size_t half = head_dim / 2;
+  for (size_t h = 0; h < n; h += head_dim) {
+    float *head = values + h;
+    for (size_t i = 0; i < half; ++i) {
+      const float angle = (float)position / powf(theta, 2.0f * (float)i / (float)head_dim);
+      const float s = sinf(angle), c = cosf(angle);
+      const float a = head[i], b = head[i + half];
+      head[i] = a * c - b * s;
+      head[i + half] = b * c + a * s;
+    }
+  }
+  return Q8O_OK;
+}
+
+/* src/cpu/ops.rs:515-606, scalar branch (one head after another): per head
+ * the token scores (left-to-right dot from -0.0, times 1/sqrt(dim)), the
+ * softmax, then out[d] += score * value over the tokens in order. */
+int q8o_attention_decode(const float *q, size_t width, const float *keys, size_t keys_len,
+                         const float *values, size_t values_len, size_t heads, float *out) {
+  if (heads == 0 || width == 0 || width % heads || keys_len == 0 || keys_len % width ||
+      keys_len != values_len)
+    return Q8O_SHAPE;
+  const size_t tokens = keys_len / width, dim = width / heads;
+  const float scale = 1.0f / sqrtf((float)dim);
+  float *scores = (float *)malloc(tokens * sizeof(float));
+  if (!scores) return Q8O_RESOURCE;
+  for (size_t i = 0; i < width; ++i) out[i] = 0.0f;
+  for (size_t h = 0; h < heads; ++h) {
+    const size_t off = h * dim;
+    for (size_t t = 0; t < tokens; ++t) {
+      float acc = -0.0f;
+      for (size_t d = 0; d < dim; ++d) acc += q[off + d] * keys[t * width + off + d];
+      scores[t] = acc;
+    }
+    for (size_t t = 0; t < tokens; ++t) scores[t] *= scale;
+    int st = q8o_softmax(scores, tokens);
+    if (st) {
+      free(scores);
+      return st;
+    }
+    for (size_t t = 0; t < tokens; ++t)
+      for (size_t d = 0; d < dim; ++d) out[off + d] += scores[t] * values[t * width + off + d];
+  }
+  free(scores);
+  return Q8O_OK;
+}

@@ -120,6 +120,19 @@ int q8o_experts(const q8o_ffn *shared, const q8o_ffn *experts, size_t n_experts,
                 int normalize, float scale, int mode, float *out, int32_t *sel_ids,
                 float *sel_weights);
 
+/* ops::rms_norm (src/cpu/ops.rs:362-414, 419-421): rows x width. */
+int q8o_rms_norm(const float *x, size_t rows, size_t width, const float *weight, float eps,
+                 float *out);
+
+/* ops::rope (src/cpu/ops.rs:423-437): every head of `values` (n floats) at
+ * one position, in place. */
+int q8o_rope(float *values, size_t n, size_t head_dim, size_t position, float theta);
+
+/* ops::attention_decode (src/cpu/ops.rs:515-606), scalar branch: q of width
+ * floats over token-major keys/values of keys_len floats each. */
+int q8o_attention_decode(const float *q, size_t width, const float *keys, size_t keys_len,
+                         const float *values, size_t values_len, size_t heads, float *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,302 @@
+"""GPU parity of the decode-attention ops (RMSNorm, rope, decode attention,
+KV cache, the attention half of a decoder layer) against the CPU oracle,
+through the C ABI.
+
+Bit-exact: RMSNorm, rope and the cache contents.  Attention follows the
+reference's order, so it is bit-identical wherever every exp rounds the same
+(checked exactly with uniform scores, where exp is exact); otherwise the
+device's exp (double, rounded once) and the C library's expf (within 0.502
+ulp) can differ by one ulp in a few of thousands of softmax terms, which
+moves a head's sum and so the last bits of that head's outputs.  Those cases
+are held to the reference's own bound: 2e-6 against its f64 oracle
+(tests/decode_attention.rs:44), and 1e-5 relative against the oracle.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from helpers import bits_equal
+from test_attention_oracle import f64_attention, reference_case
+
+pytestmark = pytest.mark.gpu
+
+
+def A():
+    import uocr_q8.attention as attention
+    return attention
+
+
+def dev(a, dtype=None):
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    return t.cuda() if dtype is None else t.to(dtype).cuda()
+
+
+def host(t):
+    return t.detach().cpu().numpy()
+
+
+# ---------------------------------------------------------------- RMSNorm
+@pytest.mark.parametrize("rows,width", [(1, 2), (3, 7), (64, 1280), (2, 4096), (5, 33)])
+def test_rms_norm_bit_exact(ctx, rows, width):
+    rng = np.random.default_rng(rows * 1000 + width)
+    x = (rng.standard_normal((rows, width)) * rng.uniform(0.01, 30, (rows, 1))).astype(np.float32)
+    w = rng.uniform(-2, 2, width).astype(np.float32)
+    y = A().rms_norm_device(ctx, dev(x), dev(w), 1e-6)
+    ctx.sync()
+    assert bits_equal(host(y), oracle.rms_norm(x, w, 1e-6))
+
+
+def test_rms_norm_known_answer_and_in_place(ctx):
+    x = dev(np.array([[1.0, 3.0]], np.float32))
+    A().rms_norm_device(ctx, x, dev(np.ones(2, np.float32)), 1e-6, out_t=x)
+    ctx.sync()
+    y = host(x)
+    assert abs(float(y[0, 0]) - 0.44721355) < 1e-6 and abs(float(y[0, 1]) - 1.3416406) < 1e-6
+
+
+def test_rms_norm_errors(ctx):
+    import uocr_q8
+    x = np.ones((2, 8), np.float32)
+    x[1, 3] = np.nan
+    A().rms_norm_device(ctx, dev(x), dev(np.ones(8, np.float32)))
+    with pytest.raises(uocr_q8.OcrError) as e:
+        ctx.sync()
+    assert e.value.kind == "Numerical"
+    with pytest.raises(uocr_q8.OcrError) as e:
+        A().rms_norm_device(ctx, dev(np.ones((1, 8), np.float32)), dev(np.ones(8, np.float32)), 0.0)
+    assert e.value.kind == "Shape"
+
+
+# ---------------------------------------------------------------- rope
+def test_rope_known_answer(ctx):
+    r = A().Rope(ctx, 4, 10000.0, 16)
+    q = dev(np.array([[1.0, 2.0, 3.0, 4.0], [1.0, 2.0, 3.0, 4.0]], np.float32))
+    r.apply(q, None, dev(np.array([0, 1], np.int32)))
+    ctx.sync()
+    y = host(q)
+    assert y[0].tolist() == [1.0, 2.0, 3.0, 4.0]
+    assert np.max(np.abs(y[1] - np.array([-1.9841106, 1.9599007, 2.462378, 4.0197997]))) < 1e-5
+    r.free()
+
+
+def test_rope_bit_exact(ctx):
+    rng = np.random.default_rng(4)
+    heads, dim, rows = 10, 128, 12
+    pos = np.array([0, 1, 2, 3, 127, 128, 2047, 2048, 2175, 5000, 32766, 32767], np.int32)
+    q = rng.standard_normal((rows, heads * dim)).astype(np.float32)
+    k = rng.standard_normal((rows, heads * dim)).astype(np.float32)
+    r = A().Rope(ctx, dim, 10000.0, 32768)
+    qt, kt = dev(q), dev(k)
+    r.apply(qt, kt, dev(pos))
+    ctx.sync()
+    for i in range(rows):
+        assert bits_equal(host(qt)[i], oracle.rope(q[i], dim, int(pos[i]))), i
+        assert bits_equal(host(kt)[i], oracle.rope(k[i], dim, int(pos[i]))), i
+    r.free()
+
+
+def test_rope_position_past_table(ctx):
+    import uocr_q8
+    r = A().Rope(ctx, 4, 10000.0, 8)
+    r.apply(dev(np.ones((1, 4), np.float32)), None, dev(np.array([8], np.int32)))
+    with pytest.raises(uocr_q8.OcrError) as e:
+        ctx.sync()
+    assert e.value.kind == "Resource"
+    with pytest.raises(uocr_q8.OcrError) as e:
+        A().Rope(ctx, 3, 10000.0, 8)
+    assert e.value.kind == "Shape"
+    r.free()
+
+
+# ---------------------------------------------------------------- attention
+@pytest.mark.parametrize("tokens", [1, 7, 139, 1641])
+def test_attention_reference_cases(ctx, tokens):
+    """tests/decode_attention.rs:6-47 (3 heads of 5: the scalar-load path)."""
+    q, k, v = reference_case(tokens)
+    out = host(A().attention_decode_device(ctx, dev(q), dev(k), dev(v), 3))
+    ctx.sync()
+    assert np.max(np.abs(out.astype(np.float64) - f64_attention(q, k, v, 3))) < 2e-6
+    ref = oracle.attention_decode(q, k, v, 3)
+    assert np.max(np.abs(out - ref)) <= 1e-5 * max(1.0, float(np.max(np.abs(ref))))
+
+
+@pytest.mark.parametrize("tokens", [129, 1641, 2176])
+def test_attention_decoder_shape(ctx, tokens):
+    """10 heads of 128 (tests/decode_attention.rs:66-96 shapes): vector path."""
+    heads, dim = 10, 128
+    width = heads * dim
+    q = np.sin(np.arange(width, dtype=np.float32) * np.float32(0.17)).astype(np.float32)
+    i = np.arange(tokens * width, dtype=np.float32)
+    k = np.cos(i * np.float32(0.013)).astype(np.float32)
+    v = np.sin(i * np.float32(0.031)).astype(np.float32)
+    out = host(A().attention_decode_device(ctx, dev(q), dev(k), dev(v), heads))
+    ctx.sync()
+    ref = oracle.attention_decode(q, k, v, heads)
+    assert np.max(np.abs(out - ref)) <= 1e-5 * max(1.0, float(np.max(np.abs(ref))))
+    assert np.max(np.abs(out.astype(np.float64) - f64_attention(q, k, v, heads))) < 2e-6
+
+
+@pytest.mark.parametrize("heads,dim,tokens", [(10, 128, 2176), (3, 5, 1641), (2, 64, 33)])
+def test_attention_order_bit_exact_with_exact_exp(ctx, heads, dim, tokens):
+    """Keys equal within each head make every score equal, so every exp is
+    exp(0) = 1 exactly and the softmax is 1/T on both sides: the outputs are
+    then the left-to-right value sums of the reference, bit for bit."""
+    rng = np.random.default_rng(tokens)
+    width = heads * dim
+    q = rng.standard_normal(width).astype(np.float32)
+    k = np.tile(rng.standard_normal(width).astype(np.float32), (tokens, 1))
+    v = (rng.standard_normal((tokens, width)) * rng.uniform(0.1, 10, (tokens, 1))).astype(np.float32)
+    out = host(A().attention_decode_device(ctx, dev(q), dev(k), dev(v), heads))
+    ctx.sync()
+    assert bits_equal(out, oracle.attention_decode(q, k, v, heads))
+
+
+def test_attention_layout_errors(ctx):
+    import torch
+    import uocr_q8
+    q = torch.zeros(6, device="cuda")
+    for keys, values, heads in ((7, 7, 2), (6, 5, 2), (6, 6, 4), (6, 6, 0)):
+        with pytest.raises(uocr_q8.OcrError) as e:
+            A().attention_decode_device(ctx, q, torch.zeros(keys, device="cuda"),
+                                        torch.zeros(values, device="cuda"), heads)
+        assert e.value.kind == "Shape"
+    bad = torch.zeros(6, device="cuda")
+    bad[0] = float("nan")
+    A().attention_decode_device(ctx, bad, torch.ones(12, device="cuda"), torch.ones(12, device="cuda"), 2)
+    with pytest.raises(uocr_q8.OcrError) as e:
+        ctx.sync()
+    assert e.value.kind == "Numerical"
+
+
+# ---------------------------------------------------------------- KV cache
+def test_cache_ring_matches_layer_cache(ctx):
+    """Prefill + pushes across ring wraps (tests/cache.rs shapes scaled up):
+    the device cache holds the reference's physical token order, and the
+    attention over it equals the oracle's over LayerCache contents."""
+    rng = np.random.default_rng(11)
+    batch, heads, dim, window = 3, 2, 8, 5
+    width = heads * dim
+    prefixes = [4, 1, 7]
+    kv = A().KvCache(ctx, batch, heads, dim, window, max_prefix=8)
+    refs = [oracle.LayerCache(heads, dim, window) for _ in range(batch)]
+    for b in range(batch):
+        k = rng.standard_normal((prefixes[b], width)).astype(np.float32)
+        v = rng.standard_normal((prefixes[b], width)).astype(np.float32)
+        kv.prefill(b, dev(k), dev(v))
+        refs[b].prefill(k, v, prefixes[b])
+    for step in range(13):
+        k = rng.standard_normal((batch, width)).astype(np.float32)
+        v = rng.standard_normal((batch, width)).astype(np.float32)
+        q = rng.standard_normal((batch, width)).astype(np.float32)
+        kv.push(dev(k), dev(v))
+        for b in range(batch):
+            refs[b].push(k[b], v[b])
+        out = host(kv.attention(dev(q)))
+        ctx.sync()
+        keys, values = (host(t) for t in kv.buffers())
+        for b in range(batch):
+            n = refs[b].tokens()
+            assert kv.state(b) == (n, refs[b].position())
+            assert bits_equal(keys[b, :n], refs[b].keys) and bits_equal(values[b, :n], refs[b].values)
+            ref = oracle.attention_decode(q[b], refs[b].keys, refs[b].values, heads)
+            assert np.max(np.abs(out[b] - ref)) <= 1e-5 * max(1.0, float(np.max(np.abs(ref))))
+    kv.free()
+
+
+def test_cache_rope_uses_positions(ctx):
+    rng = np.random.default_rng(12)
+    batch, heads, dim, window = 2, 2, 4, 3
+    width = heads * dim
+    kv = A().KvCache(ctx, batch, heads, dim, window, max_prefix=6)
+    r = A().Rope(ctx, dim, 10000.0, 64)
+    for b, n in enumerate((6, 2)):
+        z = np.zeros((n, width), np.float32)
+        kv.prefill(b, dev(z), dev(z))
+    pos = [6, 2]
+    for step in range(5):
+        q = rng.standard_normal((batch, width)).astype(np.float32)
+        k = rng.standard_normal((batch, width)).astype(np.float32)
+        qt, kt = dev(q), dev(k)
+        kv.rope(r, qt, kt)
+        kv.push(kt, kt)
+        ctx.sync()
+        for b in range(batch):
+            assert bits_equal(host(qt)[b], oracle.rope(q[b], dim, pos[b]))
+            assert bits_equal(host(kt)[b], oracle.rope(k[b], dim, pos[b]))
+            pos[b] += 1
+    kv.free()
+    r.free()
+
+
+def test_cache_errors(ctx):
+    import torch
+    import uocr_q8
+    kv = A().KvCache(ctx, 2, 2, 2, 4, max_prefix=3)
+    z = torch.zeros((3, 4), device="cuda")
+    with pytest.raises(uocr_q8.OcrError) as e:
+        kv.push(z[:2], z[:2])
+    assert e.value.kind == "Shape"  # not prefilled
+    kv.prefill(0, z, z)
+    with pytest.raises(uocr_q8.OcrError) as e:
+        kv.prefill(0, z, z)
+    assert e.value.kind == "Shape"  # twice
+    with pytest.raises(uocr_q8.OcrError) as e:
+        kv.attention(z[:2])
+    assert e.value.kind == "Shape"  # sequence 1 not prefilled
+    with pytest.raises(uocr_q8.OcrError) as e:
+        kv.prefill(1, torch.zeros((4, 4), device="cuda"), torch.zeros((4, 4), device="cuda"))
+    assert e.value.kind == "Resource"  # longer than max_prefix
+    for args in ((1, 0, 2, 4, 3), (1, 2, 2, 0, 3)):
+        with pytest.raises(uocr_q8.OcrError) as e:
+            A().KvCache(ctx, *args)
+        assert e.value.kind == "Shape"
+    kv.free()
+
+
+# ---------------------------------------------------------------- attention block
+@pytest.mark.parametrize("mode", [0, 1])
+def test_attention_block_matches_oracle(ctx, mode):
+    """The attention half of Decoder::layer (src/decoder/mod.rs:241-341) for a
+    batch of sequences at decode, three steps, vs the oracle composition."""
+    import torch
+    import uocr_q8
+    from helpers import random_q8
+    rng = np.random.default_rng(20 + mode)
+    batch, heads, dim, window, prefix = 4, 10, 128, 4, 37
+    H = heads * dim
+    mats = [oracle.Matrix(*random_q8(rng, H, H, 1e-3, 2e-3)) for _ in range(4)]
+    dmats = [uocr_q8.Int8Matrix.from_parts(H, H, m.w, m.s, ctx) for m in mats]
+    norm = rng.uniform(0.5, 1.5, H).astype(np.float32)
+    kv = A().KvCache(ctx, batch, heads, dim, window, max_prefix=prefix)
+    rope = A().Rope(ctx, dim, 10000.0, 4096)
+    refs = []
+    for b in range(batch):
+        k = rng.standard_normal((prefix, H)).astype(np.float32)
+        v = rng.standard_normal((prefix, H)).astype(np.float32)
+        kv.prefill(b, dev(k), dev(v))
+        c = oracle.LayerCache(heads, dim, window)
+        c.prefill(k, v, prefix)
+        refs.append(c)
+    block = A().AttentionBlock(ctx, dev(norm), *dmats, kv, rope)
+    lin = oracle.linear_dynamic_int8 if mode == 1 else oracle.linear
+    for step in range(3):
+        x = rng.standard_normal((batch, H)).astype(np.float32)
+        y = host(block.forward_device(dev(x), mode))
+        ctx.sync()
+        for b in range(batch):
+            c = refs[b]
+            n = oracle.rms_norm(x[b:b + 1], norm)
+            q, k, v = (lin(m, n)[0] for m in mats[:3])
+            pos = c.position()
+            q, k = oracle.rope(q, dim, pos), oracle.rope(k, dim, pos)
+            c.push(k, v)
+            a = oracle.attention_decode(q, c.keys, c.values, heads)
+            ref = lin(mats[3], a[None])[0] + x[b]
+            err = np.max(np.abs(y[b].astype(np.float64) - ref))
+            # int8 mode: a one-ulp attention difference can move one activation
+            # quantization step of the o projection (the MoE layer tolerance)
+            tol = 1e-3 if mode == 1 else 1e-4
+            assert err <= tol * float(np.max(np.abs(ref))), (step, b, err)
+    kv.free()
+    rope.free()

@@ -1,0 +1,332 @@
+// attention.cu — the attention half of a decoder layer at decode, on the
+// device: RMSNorm (ops::rms_norm, src/cpu/ops.rs:362-414), the rotary
+// embedding (ops::rope, :420-437), the token-major KV cache with an
+// immutable prefix and a bounded ring (LayerCache, src/decoder/cache.rs:3-95)
+// and single-query attention over it (ops::attention_decode, :515-606).
+//
+// Arithmetic follows the reference's order so that results are bit-identical
+// to it except where exp rounds differently (exp_f32_via_f64, rarely one ulp):
+//  * RMSNorm: squares in parallel, one thread sums them left to right from
+//    -0.0, IEEE division by the width, sqrt then reciprocal, then
+//    ((x * scale) * w) + 0.0 per element;
+//  * rope: cos/sin from a table the host builds with the same single-precision
+//    operations as the reference (powf, division, sinf/cosf), then
+//    a*cos - b*sin and b*cos + a*sin with one rounding per operation;
+//  * attention: per head, each token's score is a left-to-right sum over the
+//    head dimension (one thread per token, -0.0 start), times the scale;
+//    softmax as the reference's (max, subtract, exp, left-to-right sum by one
+//    thread, divide); each output element is a left-to-right sum over the
+//    tokens in physical cache order (one thread per element, +0.0 start).
+//
+// Layout: keys/values [batch][cap][width] floats, row (b, slot) = one token;
+// per-sequence state {prefix, generated} in device memory, so pushes and
+// attention can run inside captured graphs.  Slot of the next token:
+// prefix + generated % window; tokens present: prefix + min(generated, window).
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace uocr {
+
+// ---- RMSNorm -----------------------------------------------------------------
+constexpr int kNormThreads = 256;
+
+__global__ void __launch_bounds__(kNormThreads)
+    rms_norm_kernel(const float* __restrict__ x, long long ld_x, int width,
+                    const float* __restrict__ w, float eps, float* out, long long ld_out,
+                    unsigned* status) {
+  extern __shared__ float sq[];  // width squares
+  __shared__ float s_scale;
+  const long long row = blockIdx.x;
+  const float* xr = x + row * ld_x;
+  bool bad = false;
+  for (int i = threadIdx.x; i < width; i += blockDim.x) {
+    const float v = xr[i];
+    bad |= !isfinite(v) || !isfinite(w[i]);
+    sq[i] = __fmul_rn(v, v);
+  }
+  if (__syncthreads_or(bad)) {
+    if (threadIdx.x == 0) flag(status, DEV_NORM);
+    return;
+  }
+  if (threadIdx.x == 0) {
+    float acc = -0.0f;
+    int i = 0;
+    for (; i + 8 <= width; i += 8) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = sq[i + j];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, v[j]);
+    }
+    for (; i < width; ++i) acc = __fadd_rn(acc, sq[i]);
+    const float var = __fdiv_rn(acc, static_cast<float>(width));
+    s_scale = __frcp_rn(__fsqrt_rn(__fadd_rn(var, eps)));
+  }
+  __syncthreads();
+  const float scale = s_scale;
+  float* o = out + row * ld_out;
+  for (int i = threadIdx.x; i < width; i += blockDim.x)
+    o[i] = __fadd_rn(__fmul_rn(__fmul_rn(xr[i], scale), w[i]), 0.0f);
+}
+
+void launch_rms_norm(const float* x, long long ld_x, int rows, int width, const float* w, float eps,
+                     float* out, long long ld_out, unsigned* status, cudaStream_t st) {
+  if (rows <= 0) return;
+  const size_t smem = static_cast<size_t>(width) * 4;
+  static unsigned configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured & (1u << (dev & 31)))) {
+    cudaFuncSetAttribute(rms_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    configured |= 1u << (dev & 31);
+  }
+  rms_norm_kernel<<<rows, kNormThreads, smem, st>>>(x, ld_x, width, w, eps, out, ld_out, status);
+}
+
+// ---- rotary embedding ---------------------------------------------------------
+// Pairs (i, i + dim/2) of every head of `rows` rows of a (and of b when
+// given, the keys beside the queries).  Position of row r: positions[r], or
+// from the cache state (prefix + generated) when positions is null.
+__global__ void rope_kernel(float* a, float* b, long long ld, int rows, int heads, int dim,
+                            const int* __restrict__ positions, const int* __restrict__ state,
+                            const float2* __restrict__ table, int max_pos, unsigned* status) {
+  const int half = dim >> 1;
+  const long long per_row = static_cast<long long>(heads) * half;
+  const long long n = rows * per_row;
+  for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < n;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(idx / per_row);
+    const int rem = static_cast<int>(idx % per_row);
+    const int head = rem / half, i = rem % half;
+    const int pos = positions ? positions[row] : state[2 * row] + state[2 * row + 1];
+    if (pos < 0 || pos >= max_pos) {
+      flag(status, DEV_POSITION);
+      continue;
+    }
+    const float2 cs = table[static_cast<long long>(pos) * half + i];
+    float* ptrs[2] = {a, b};
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      if (!ptrs[k]) continue;
+      float* h = ptrs[k] + row * ld + static_cast<long long>(head) * dim;
+      const float x0 = h[i], x1 = h[i + half];
+      h[i] = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+      h[i + half] = __fadd_rn(__fmul_rn(x1, cs.x), __fmul_rn(x0, cs.y));
+    }
+  }
+}
+
+void launch_rope(float* a, float* b, long long ld, int rows, int heads, int dim,
+                 const int* positions, const int* state, const float2* table, int max_pos,
+                 unsigned* status, int sms, cudaStream_t st) {
+  const long long n = static_cast<long long>(rows) * heads * (dim / 2);
+  if (n <= 0) return;
+  long long blocks = (n + 255) / 256;
+  if (blocks > 8LL * sms) blocks = 8LL * sms;
+  rope_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(a, b, ld, rows, heads, dim, positions,
+                                                         state, table, max_pos, status);
+}
+
+// ---- KV cache ------------------------------------------------------------------
+__global__ void kv_set_prefix_kernel(int* state, int seq, int tokens) {
+  state[2 * seq] = tokens;
+  state[2 * seq + 1] = 0;
+}
+
+void launch_kv_set_prefix(int* state, int seq, int tokens, cudaStream_t st) {
+  kv_set_prefix_kernel<<<1, 1, 0, st>>>(state, seq, tokens);
+}
+
+// LayerCache::push for every sequence: row b of k/v into its next slot.
+__global__ void kv_push_kernel(float* keys, float* values, int* state, int width, int window,
+                               long long cap, const float* __restrict__ k,
+                               const float* __restrict__ v, long long ld, unsigned* status) {
+  const int b = blockIdx.x;
+  const int prefix = state[2 * b], gen = state[2 * b + 1];
+  if (prefix <= 0) {
+    if (threadIdx.x == 0) flag(status, DEV_CACHE);
+    return;
+  }
+  const long long slot = prefix + gen % window;
+  float* kd = keys + (b * cap + slot) * width;
+  float* vd = values + (b * cap + slot) * width;
+  const float* ks = k + b * ld;
+  const float* vs = v + b * ld;
+  for (int i = threadIdx.x; i < width; i += blockDim.x) {
+    kd[i] = ks[i];
+    vd[i] = vs[i];
+  }
+  __syncthreads();  // every thread has read `gen`
+  if (threadIdx.x == 0) state[2 * b + 1] = gen + 1;
+}
+
+void launch_kv_push(float* keys, float* values, int* state, int batch, int width, int window,
+                    long long cap, const float* k, const float* v, long long ld, unsigned* status,
+                    cudaStream_t st) {
+  if (batch <= 0) return;
+  kv_push_kernel<<<batch, 256, 0, st>>>(keys, values, state, width, window, cap, k, v, ld, status);
+}
+
+// ---- single-query attention ---------------------------------------------------------
+constexpr int kAttnThreads = 256;
+
+// Score of one token: left-to-right over the head dimension from -0.0.
+template <bool VEC>
+__device__ __forceinline__ float token_score(const float* __restrict__ kr, const float* qs, int dim) {
+  float acc = -0.0f;
+  if (VEC) {
+    const float4* q4 = reinterpret_cast<const float4*>(qs);
+    const float4* k4 = reinterpret_cast<const float4*>(kr);
+#pragma unroll 8
+    for (int d = 0; d < dim / 4; ++d) {
+      const float4 kv = __ldg(k4 + d);
+      const float4 qv = q4[d];
+      acc = __fadd_rn(acc, __fmul_rn(qv.x, kv.x));
+      acc = __fadd_rn(acc, __fmul_rn(qv.y, kv.y));
+      acc = __fadd_rn(acc, __fmul_rn(qv.z, kv.z));
+      acc = __fadd_rn(acc, __fmul_rn(qv.w, kv.w));
+    }
+  } else {
+    for (int d = 0; d < dim; ++d) acc = __fadd_rn(acc, __fmul_rn(qs[d], __ldg(kr + d)));
+  }
+  return acc;
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a) {
+  extern __shared__ __align__(16) float smem_f[];
+  __shared__ float red[kAttnThreads / 32];
+  __shared__ int red_bad[kAttnThreads / 32];
+  __shared__ float s_max, s_sum;
+  __shared__ int s_bad;
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int dim = a.dim, width = a.width;
+  float* qs = smem_f;                              // dim floats
+  float* sc = smem_f + ((dim + 3) & ~3);           // tokens floats
+  int T = a.tokens;
+  if (a.state) {
+    const int prefix = a.state[2 * b], gen = a.state[2 * b + 1];
+    if (prefix <= 0) {
+      if (tid == 0) flag(a.status, DEV_CACHE);
+      return;
+    }
+    T = prefix + (gen < a.window ? gen : a.window);
+  }
+  const float* kb = a.keys + static_cast<long long>(b) * a.cap * width + static_cast<long long>(h) * dim;
+  const float* vb = a.values + static_cast<long long>(b) * a.cap * width + static_cast<long long>(h) * dim;
+  for (int d = tid; d < dim; d += kAttnThreads) qs[d] = a.q[b * a.ld_q + static_cast<long long>(h) * dim + d];
+  __syncthreads();
+
+  // scores: one thread per token, two tokens in flight per thread
+  for (int t = tid; t < T; t += 2 * kAttnThreads) {
+    const int t2 = t + kAttnThreads;
+    const float s1 = token_score<VEC>(kb + static_cast<long long>(t) * width, qs, dim);
+    if (t2 < T) {
+      const float s2 = token_score<VEC>(kb + static_cast<long long>(t2) * width, qs, dim);
+      sc[t2] = __fmul_rn(s2, a.scale);
+    }
+    sc[t] = __fmul_rn(s1, a.scale);
+  }
+  __syncthreads();
+
+  // softmax_backend (src/cpu/ops.rs:139-187)
+  float mx = -INFINITY;
+  int bad = 0;
+  for (int t = tid; t < T; t += kAttnThreads) {
+    const float v = sc[t];
+    bad |= isnan(v) || v == INFINITY;
+    mx = fmaxf(mx, v);
+  }
+  mx = warp_max(mx);
+  bad = __any_sync(0xffffffffu, bad);
+  if (lane == 0) {
+    red[warp] = mx;
+    red_bad[warp] = bad;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float m = red[0];
+    int bd = red_bad[0];
+    for (int w = 1; w < kAttnThreads / 32; ++w) {
+      m = fmaxf(m, red[w]);
+      bd |= red_bad[w];
+    }
+    s_max = m;
+    s_bad = bd || !isfinite(m);
+  }
+  __syncthreads();
+  if (s_bad) {
+    if (tid == 0) flag(a.status, DEV_SOFTMAX);
+    return;
+  }
+  mx = s_max;
+  for (int t = tid; t < T; t += kAttnThreads) sc[t] = exp_f32_via_f64(__fsub_rn(sc[t], mx));
+  __syncthreads();
+  if (tid == 0) {
+    float acc = -0.0f;
+    int t = 0;
+    for (; t + 8 <= T; t += 8) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = sc[t + j];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, v[j]);
+    }
+    for (; t < T; ++t) acc = __fadd_rn(acc, sc[t]);
+    s_sum = acc;
+  }
+  __syncthreads();
+  const float sum = s_sum;
+  for (int t = tid; t < T; t += kAttnThreads) sc[t] = __fdiv_rn(sc[t], sum);
+  __syncthreads();
+
+  // output: one thread per element, tokens in order from +0.0
+  float* ob = a.out + b * a.ld_out + static_cast<long long>(h) * dim;
+  for (int d = tid; d < dim; d += kAttnThreads) {
+    const float* vc = vb + d;
+    float acc = 0.0f;
+    int t = 0;
+    for (; t + 16 <= T; t += 16) {
+      float v[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = __ldg(vc + static_cast<long long>(t + j) * width);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc = __fadd_rn(acc, __fmul_rn(sc[t + j], v[j]));
+    }
+    for (; t < T; ++t) acc = __fadd_rn(acc, __fmul_rn(sc[t], __ldg(vc + static_cast<long long>(t) * width)));
+    ob[d] = acc;
+  }
+}
+
+size_t attention_smem_bytes(int dim, int max_tokens) {
+  return static_cast<size_t>((dim + 3) & ~3) * 4 + static_cast<size_t>(max_tokens) * 4;
+}
+
+cudaError_t launch_attention_decode(const AttnArgs& a, int batch, int max_tokens, cudaStream_t st) {
+  const size_t smem = attention_smem_bytes(a.dim, max_tokens);
+  if (smem > kAttnMaxSmem || batch <= 0 || a.heads <= 0) return cudaErrorInvalidValue;
+  // 16-byte key loads: every row (width floats) and head (dim floats) start aligned
+  const bool vec = a.dim % 4 == 0 && a.width % 4 == 0 &&
+                   reinterpret_cast<uintptr_t>(a.keys) % 16 == 0;
+  static unsigned configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured & (1u << (dev & 31)))) {
+    cudaFuncSetAttribute(attn_decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(kAttnMaxSmem));
+    cudaFuncSetAttribute(attn_decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(kAttnMaxSmem));
+    configured |= 1u << (dev & 31);
+  }
+  const dim3 grid(a.heads, batch);
+  if (vec)
+    attn_decode_kernel<true><<<grid, kAttnThreads, smem, st>>>(a);
+  else
+    attn_decode_kernel<false><<<grid, kAttnThreads, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace uocr

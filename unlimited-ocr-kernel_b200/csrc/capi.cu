@@ -131,6 +131,9 @@ int status_result(uocr_ctx* ctx, unsigned st) {
   if (st & DEV_BAD_ROUTE) return fail(UOCR_ERR_SHAPE, "invalid tensor shape: invalid expert routing");
   if (st & DEV_CAPACITY)
     return fail(UOCR_ERR_RESOURCE, "resource limit exceeded: expert dispatch capacity");
+  if (st & DEV_NORM) return fail(UOCR_ERR_NUMERICAL, "nonfinite numerical input: normalization");
+  if (st & DEV_POSITION) return fail(UOCR_ERR_RESOURCE, "resource limit: maximum context exceeded");
+  if (st & DEV_CACHE) return fail(UOCR_ERR_SHAPE, "invalid tensor shape: cache must be prefilled");
   return fail(UOCR_ERR_CUDA, "unknown device status 0x%x", st);
 }
 
@@ -1226,6 +1229,282 @@ int uocr_moe_forward_host(uocr_ctx* ctx, const uocr_moe* layer, int mode, const 
     if (ids) std::memcpy(ids, hp + xb + lb + yb, tokens * k * 4);
     if (weights) std::memcpy(weights, hp + xb + lb + yb + rb, tokens * k * 4);
   }
+  return ok();
+}
+
+
+// ---- decoder attention at decode --------------------------------------------
+// ops::rms_norm (src/cpu/ops.rs:362-414, 419-421)
+int uocr_rms_norm(uocr_ctx* ctx, const float* x_dev, size_t rows, size_t width,
+                  const float* weight_dev, float eps, float* out_dev) {
+  if (!ctx) return fail(UOCR_ERR_INVALID, "null context");
+  if (width == 0 || !std::isfinite(eps) || eps <= 0.0f)
+    return fail(UOCR_ERR_SHAPE, "invalid tensor shape: invalid normalization parameters");
+  if (rows == 0) return ok();
+  if (!x_dev || !weight_dev || !out_dev) return fail(UOCR_ERR_INVALID, "null argument");
+  if (!fits_int(rows) || width > 50000)
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: normalization extent");
+  DeviceGuard g(ctx->device);
+  launch_rms_norm(x_dev, static_cast<long long>(width), static_cast<int>(rows),
+                  static_cast<int>(width), weight_dev, eps, out_dev, static_cast<long long>(width),
+                  ctx->status_dev, ctx->stream);
+  return check_launch();
+}
+
+// ops::rope (src/cpu/ops.rs:423-437): the (cos, sin) table of positions
+// [0, max_positions) for one head dimension and base.
+int uocr_rope_create(uocr_ctx* ctx, size_t head_dim, float theta, size_t max_positions,
+                     uocr_rope** out) {
+  if (!ctx || !out) return fail(UOCR_ERR_INVALID, "null argument");
+  *out = nullptr;
+  if (head_dim == 0 || head_dim % 2 || !std::isfinite(theta) || theta <= 0.0f)
+    return fail(UOCR_ERR_SHAPE, "invalid tensor shape: invalid rotary dimensions or base");
+  size_t n;
+  if (max_positions == 0 || !mul_ok(max_positions, head_dim, &n) || !fits_int(max_positions) ||
+      n > (size_t(1) << 31))
+    return fail(UOCR_ERR_RESOURCE, "resource limit: rotary table");
+  std::vector<float> host(n);  // [max_pos][head_dim/2][2]
+  build_rope_table(static_cast<int>(head_dim), theta, static_cast<int>(max_positions), host.data());
+  DeviceGuard g(ctx->device);
+  auto* r = new uocr_rope();
+  r->device = ctx->device;
+  r->head_dim = static_cast<int>(head_dim);
+  r->max_pos = static_cast<int>(max_positions);
+  r->theta = theta;
+  cudaError_t e = cudaMalloc(&r->table, n * sizeof(float));
+  if (e == cudaSuccess) e = cudaMemcpy(r->table, host.data(), n * sizeof(float), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    uocr_rope_free(r);
+    return fail(UOCR_ERR_CUDA, "rope table: %s", cudaGetErrorString(e));
+  }
+  *out = r;
+  return ok();
+}
+
+int uocr_rope_free(uocr_rope* rope) {
+  if (!rope) return ok();
+  DeviceGuard g(rope->device);
+  if (rope->table) cudaFree(rope->table);
+  delete rope;
+  return ok();
+}
+
+// Rotates q (and k when given) in place: rows x width, heads of head_dim,
+// row r at positions_dev[r].  A position outside the table is Resource
+// ("maximum context exceeded", src/decoder/mod.rs:259-264) at the next sync.
+int uocr_rope_apply(uocr_ctx* ctx, const uocr_rope* rope, float* q_dev, float* k_dev, size_t rows,
+                    size_t width, const int32_t* positions_dev) {
+  if (!ctx || !rope) return fail(UOCR_ERR_INVALID, "null argument");
+  if (width == 0 || width % rope->head_dim)
+    return fail(UOCR_ERR_SHAPE, "invalid tensor shape: invalid rotary dimensions or base");
+  if (rows == 0) return ok();
+  if (!q_dev || !positions_dev) return fail(UOCR_ERR_INVALID, "null argument");
+  if (!fits_int(rows)) return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: rows");
+  DeviceGuard g(ctx->device);
+  launch_rope(q_dev, k_dev, static_cast<long long>(width), static_cast<int>(rows),
+              static_cast<int>(width / rope->head_dim), rope->head_dim, positions_dev, nullptr,
+              rope->table, rope->max_pos, ctx->status_dev, ctx->sms, ctx->stream);
+  return check_launch();
+}
+
+// ops::attention_decode (src/cpu/ops.rs:515-606): one query [1 x width] over
+// token-major keys/values [tokens x width].
+int uocr_attention_decode(uocr_ctx* ctx, const float* q_dev, const float* keys_dev,
+                          size_t keys_len, const float* values_dev, size_t values_len,
+                          size_t width, size_t heads, float* out_dev) {
+  if (!ctx) return fail(UOCR_ERR_INVALID, "null context");
+  if (heads == 0 || width == 0 || width % heads || keys_len == 0 || keys_len % width ||
+      keys_len != values_len)
+    return fail(UOCR_ERR_SHAPE, "invalid tensor shape: decode attention layout");
+  const size_t tokens = keys_len / width;
+  int st = check_elements(ctx, tokens + width);
+  if (st) return st;
+  if (!q_dev || !keys_dev || !values_dev || !out_dev) return fail(UOCR_ERR_INVALID, "null argument");
+  const size_t dim = width / heads;
+  if (!fits_int(width) || !fits_int(tokens) ||
+      attention_smem_bytes(static_cast<int>(dim), static_cast<int>(tokens)) > kAttnMaxSmem)
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: decode attention over %zu tokens",
+                tokens);
+  DeviceGuard g(ctx->device);
+  AttnArgs a{};
+  a.q = q_dev;
+  a.ld_q = static_cast<long long>(width);
+  a.keys = keys_dev;
+  a.values = values_dev;
+  a.cap = static_cast<long long>(tokens);
+  a.width = static_cast<int>(width);
+  a.heads = static_cast<int>(heads);
+  a.dim = static_cast<int>(dim);
+  a.tokens = static_cast<int>(tokens);
+  a.scale = 1.0f / std::sqrt(static_cast<float>(dim));  // (dim as f32).sqrt().recip()
+  a.out = out_dev;
+  a.ld_out = static_cast<long long>(width);
+  a.status = ctx->status_dev;
+  cudaError_t e = launch_attention_decode(a, 1, static_cast<int>(tokens), ctx->stream);
+  if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
+  return ok();
+}
+
+// LayerCache::new (src/decoder/cache.rs:14-31) for `batch` sequences, with
+// room for a prefix of up to max_prefix tokens.
+int uocr_kv_create(uocr_ctx* ctx, size_t batch, size_t heads, size_t head_dim, size_t window,
+                   size_t max_prefix, uocr_kv** out) {
+  if (!ctx || !out) return fail(UOCR_ERR_INVALID, "null argument");
+  *out = nullptr;
+  size_t width;
+  if (!mul_ok(heads, head_dim, &width) || width == 0)
+    return fail(UOCR_ERR_SHAPE, "invalid tensor shape: cache head dimensions");
+  if (window == 0) return fail(UOCR_ERR_SHAPE, "invalid tensor shape: empty cache window");
+  if (batch == 0 || max_prefix == 0)
+    return fail(UOCR_ERR_SHAPE, "invalid tensor shape: empty cache batch or prefix");
+  size_t cap, rows, n, bytes;
+  if (max_prefix > (size_t(1) << 30) || window > (size_t(1) << 30) || !fits_int(width) ||
+      !fits_int(batch) || (cap = max_prefix + window) > (size_t(1) << 30) ||
+      !mul_ok(batch, cap, &rows) || !mul_ok(rows, width, &n) || !mul_ok(n, 4, &bytes))
+    return fail(UOCR_ERR_RESOURCE, "resource limit: cache capacity overflow");
+  DeviceGuard g(ctx->device);
+  auto* kv = new uocr_kv();
+  kv->device = ctx->device;
+  kv->batch = static_cast<int>(batch);
+  kv->heads = static_cast<int>(heads);
+  kv->head_dim = static_cast<int>(head_dim);
+  kv->width = static_cast<int>(width);
+  kv->window = static_cast<int>(window);
+  kv->max_prefix = static_cast<int>(max_prefix);
+  kv->cap = static_cast<long long>(cap);
+  kv->prefix.assign(batch, 0);
+  cudaError_t e = cudaMalloc(&kv->keys, bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&kv->values, bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&kv->state, batch * 2 * sizeof(int));
+  if (e == cudaSuccess) e = cudaMemsetAsync(kv->state, 0, batch * 2 * sizeof(int), ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) {
+    uocr_kv_free(kv);
+    cudaGetLastError();
+    return fail(e == cudaErrorMemoryAllocation ? UOCR_ERR_RESOURCE : UOCR_ERR_CUDA,
+                "cache allocation: %s", cudaGetErrorString(e));
+  }
+  *out = kv;
+  return ok();
+}
+
+int uocr_kv_free(uocr_kv* kv) {
+  if (!kv) return ok();
+  DeviceGuard g(kv->device);
+  if (kv->keys) cudaFree(kv->keys);
+  if (kv->values) cudaFree(kv->values);
+  if (kv->state) cudaFree(kv->state);
+  delete kv;
+  return ok();
+}
+
+// LayerCache::prefill (src/decoder/cache.rs:33-57) of sequence `seq`:
+// tokens rows of width floats (device).
+int uocr_kv_prefill(uocr_ctx* ctx, uocr_kv* kv, size_t seq, const float* keys_dev,
+                    const float* values_dev, size_t tokens) {
+  if (!ctx || !kv) return fail(UOCR_ERR_INVALID, "null argument");
+  if (seq >= static_cast<size_t>(kv->batch)) return fail(UOCR_ERR_SHAPE, "invalid tensor shape: cache sequence");
+  if (kv->prefix[seq] || tokens == 0)
+    return fail(UOCR_ERR_SHAPE, "invalid tensor shape: invalid cache prefill");
+  if (tokens > static_cast<size_t>(kv->max_prefix))
+    return fail(UOCR_ERR_RESOURCE, "resource limit: cache capacity overflow");
+  if (!keys_dev || !values_dev) return fail(UOCR_ERR_INVALID, "null argument");
+  DeviceGuard g(ctx->device);
+  const size_t off = seq * static_cast<size_t>(kv->cap) * kv->width, n = tokens * kv->width * 4;
+  CUDA_TRY(cudaMemcpyAsync(kv->keys + off, keys_dev, n, cudaMemcpyDeviceToDevice, ctx->stream));
+  CUDA_TRY(cudaMemcpyAsync(kv->values + off, values_dev, n, cudaMemcpyDeviceToDevice, ctx->stream));
+  launch_kv_set_prefix(kv->state, static_cast<int>(seq), static_cast<int>(tokens), ctx->stream);
+  int st = check_launch();
+  if (st) return st;
+  kv->prefix[seq] = static_cast<int>(tokens);
+  return ok();
+}
+
+static int kv_ready(const uocr_kv* kv) {
+  for (int p : kv->prefix)
+    if (!p) return fail(UOCR_ERR_SHAPE, "invalid tensor shape: cache must be prefilled");
+  return ok();
+}
+
+// LayerCache::push (src/decoder/cache.rs:59-80) for every sequence: row b of
+// k_dev / v_dev ([batch x width]) into sequence b.
+int uocr_kv_push(uocr_ctx* ctx, uocr_kv* kv, const float* k_dev, const float* v_dev) {
+  if (!ctx || !kv) return fail(UOCR_ERR_INVALID, "null argument");
+  int st = kv_ready(kv);
+  if (st) return st;
+  if (!k_dev || !v_dev) return fail(UOCR_ERR_INVALID, "null argument");
+  DeviceGuard g(ctx->device);
+  launch_kv_push(kv->keys, kv->values, kv->state, kv->batch, kv->width, kv->window, kv->cap, k_dev,
+                 v_dev, kv->width, ctx->status_dev, ctx->stream);
+  return check_launch();
+}
+
+// ops::rope of q and k ([batch x width]) at each sequence's position
+// (LayerCache::position before this token's push).
+int uocr_kv_rope(uocr_ctx* ctx, const uocr_kv* kv, const uocr_rope* rope, float* q_dev, float* k_dev) {
+  if (!ctx || !kv || !rope) return fail(UOCR_ERR_INVALID, "null argument");
+  if (rope->head_dim != kv->head_dim)
+    return fail(UOCR_ERR_SHAPE, "invalid tensor shape: invalid rotary dimensions or base");
+  int st = kv_ready(kv);
+  if (st) return st;
+  if (!q_dev) return fail(UOCR_ERR_INVALID, "null argument");
+  DeviceGuard g(ctx->device);
+  launch_rope(q_dev, k_dev, kv->width, kv->batch, kv->heads, kv->head_dim, nullptr, kv->state,
+              rope->table, rope->max_pos, ctx->status_dev, ctx->sms, ctx->stream);
+  return check_launch();
+}
+
+// ops::attention_decode of q row b over sequence b's cache, for every b.
+int uocr_kv_attention(uocr_ctx* ctx, const uocr_kv* kv, const float* q_dev, float* out_dev) {
+  if (!ctx || !kv) return fail(UOCR_ERR_INVALID, "null argument");
+  int st = kv_ready(kv);
+  if (st) return st;
+  if (!q_dev || !out_dev) return fail(UOCR_ERR_INVALID, "null argument");
+  if ((st = check_elements(ctx, static_cast<size_t>(kv->cap) + kv->width))) return st;
+  if (attention_smem_bytes(kv->head_dim, static_cast<int>(kv->cap)) > kAttnMaxSmem)
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: decode attention over %lld tokens",
+                kv->cap);
+  DeviceGuard g(ctx->device);
+  AttnArgs a{};
+  a.q = q_dev;
+  a.ld_q = kv->width;
+  a.keys = kv->keys;
+  a.values = kv->values;
+  a.cap = kv->cap;
+  a.width = kv->width;
+  a.heads = kv->heads;
+  a.dim = kv->head_dim;
+  a.state = kv->state;
+  a.window = kv->window;
+  a.scale = 1.0f / std::sqrt(static_cast<float>(kv->head_dim));
+  a.out = out_dev;
+  a.ld_out = kv->width;
+  a.status = ctx->status_dev;
+  cudaError_t e = launch_attention_decode(a, kv->batch, static_cast<int>(kv->cap), ctx->stream);
+  if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
+  return ok();
+}
+
+// LayerCache::tokens / position of sequence `seq` (synchronous read).
+int uocr_kv_state(uocr_ctx* ctx, const uocr_kv* kv, size_t seq, size_t* tokens, size_t* position) {
+  if (!ctx || !kv) return fail(UOCR_ERR_INVALID, "null argument");
+  if (seq >= static_cast<size_t>(kv->batch)) return fail(UOCR_ERR_SHAPE, "invalid tensor shape: cache sequence");
+  DeviceGuard g(ctx->device);
+  int h[2];
+  CUDA_TRY(cudaMemcpyAsync(h, kv->state + 2 * seq, sizeof h, cudaMemcpyDeviceToHost, ctx->stream));
+  CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  const size_t gen = static_cast<size_t>(h[1]), win = static_cast<size_t>(kv->window);
+  if (tokens) *tokens = static_cast<size_t>(h[0]) + (gen < win ? gen : win);
+  if (position) *position = static_cast<size_t>(h[0]) + gen;
+  return take_device_status(ctx);
+}
+
+// The cache's device arrays ([batch][cap][width] each) and cap.
+int uocr_kv_buffers(const uocr_kv* kv, const float** keys_dev, const float** values_dev, size_t* cap) {
+  if (!kv) return fail(UOCR_ERR_INVALID, "null cache");
+  if (keys_dev) *keys_dev = kv->keys;
+  if (values_dev) *values_dev = kv->values;
+  if (cap) *cap = static_cast<size_t>(kv->cap);
   return ok();
 }
 

@@ -30,6 +30,9 @@ enum DevStatus : unsigned {
   DEV_TIMEOUT = 1u << 5,        // a bounded wait expired
   DEV_BAD_ROUTE = 1u << 6,      // expert id outside the layer
   DEV_CAPACITY = 1u << 7,       // more pairs for one rank than the dispatch capacity
+  DEV_NORM = 1u << 8,           // normalization row or weight held NaN or Inf
+  DEV_POSITION = 1u << 9,       // rotary position outside the table (context exceeded)
+  DEV_CACHE = 1u << 10,         // KV cache used before its prefill
 };
 
 __device__ __forceinline__ void flag(unsigned* status, unsigned bits) {

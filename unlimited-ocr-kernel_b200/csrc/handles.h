@@ -65,3 +65,24 @@ struct uocr_moe {
   // qualify.
   void* tc_maps = nullptr;
 };
+
+// Rotary table: (cos, sin) of every (position, pair), built on the host.
+struct uocr_rope {
+  int device = 0;
+  int head_dim = 0, max_pos = 0;
+  float theta = 0.0f;
+  float2* table = nullptr;  // device [max_pos][head_dim/2]
+};
+
+// KV cache of `batch` sequences (LayerCache each): keys/values
+// [batch][cap][width], cap = max_prefix + window, device state {prefix,
+// generated} per sequence; the host mirrors which sequences are prefilled.
+struct uocr_kv {
+  int device = 0;
+  int batch = 0, heads = 0, head_dim = 0, width = 0, window = 0, max_prefix = 0;
+  long long cap = 0;
+  float* keys = nullptr;
+  float* values = nullptr;
+  int* state = nullptr;
+  std::vector<int> prefix;  // host mirror (0: not prefilled)
+};

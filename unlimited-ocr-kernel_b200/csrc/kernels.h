@@ -177,4 +177,38 @@ void launch_moe_combine_rows(const int32_t* ids, const float* weights, const flo
 void launch_moe_combine_pairs(const int32_t* ids, const float* weights, const float* pair_out,
                               int tokens, int top_k, int hidden, float* y, cudaStream_t st);
 
+// attention.cu — decode-side attention ops (RMSNorm, rope, KV cache,
+// single-query attention), in the reference's arithmetic order.
+void launch_rms_norm(const float* x, long long ld_x, int rows, int width, const float* w, float eps,
+                     float* out, long long ld_out, unsigned* status, cudaStream_t st);
+// table: [max_pos][dim/2] (cos, sin); positions (device, per row) or, when
+// null, the cache state {prefix, generated} per row.  b may be null.
+void launch_rope(float* a, float* b, long long ld, int rows, int heads, int dim,
+                 const int* positions, const int* state, const float2* table, int max_pos,
+                 unsigned* status, int sms, cudaStream_t st);
+void launch_kv_set_prefix(int* state, int seq, int tokens, cudaStream_t st);
+void launch_kv_push(float* keys, float* values, int* state, int batch, int width, int window,
+                    long long cap, const float* k, const float* v, long long ld, unsigned* status,
+                    cudaStream_t st);
+struct AttnArgs {
+  const float* q;  // [batch][ld_q], head h at h * dim
+  long long ld_q;
+  const float* keys;    // [batch][cap][width]
+  const float* values;  // [batch][cap][width]
+  long long cap;
+  int width, heads, dim;
+  int tokens;          // tokens per sequence when state is null
+  const int* state;    // {prefix, generated} per sequence, or null
+  int window;
+  float scale;         // 1 / sqrt(dim), as the reference rounds it
+  float* out;          // [batch][ld_out]
+  long long ld_out;
+  unsigned* status;
+};
+constexpr size_t kAttnMaxSmem = 200 * 1024;
+size_t attention_smem_bytes(int dim, int max_tokens);
+cudaError_t launch_attention_decode(const AttnArgs& a, int batch, int max_tokens, cudaStream_t st);
+// rope_table.cpp — host: the reference's cos/sin of every (position, pair).
+void build_rope_table(int dim, float theta, int max_pos, float* cos_sin /* [max_pos][dim/2][2] */);
+
 }  // namespace uocr

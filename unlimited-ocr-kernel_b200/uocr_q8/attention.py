@@ -1,0 +1,176 @@
+"""Decode-side attention ops of a decoder layer on the GPU.
+
+Mirrors the reference's operators on device tensors (torch CUDA tensors,
+asynchronous on the context's stream):
+
+* ``rms_norm_device`` — ops::rms_norm (src/cpu/ops.rs:362-414, 419-421);
+* ``Rope`` — ops::rope (src/cpu/ops.rs:423-437) with a host-built cos/sin table;
+* ``attention_decode_device`` — ops::attention_decode (src/cpu/ops.rs:515-606);
+* ``KvCache`` — LayerCache (src/decoder/cache.rs) for a batch of sequences,
+  with ``push``, ``rope`` (at each sequence's position) and ``attention``;
+* ``AttentionBlock`` — the attention half of Decoder::layer
+  (src/decoder/mod.rs:241-341) at decode: norm, q/k/v projections (q8
+  overlay matrices), rope, cache push, attention, o projection, residual.
+
+Every call goes to the CUDA library (libuocr_q8.so).
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+from . import GpuContext, Int8Matrix, QuantizationMode, _check, _tptr, lib
+
+
+def _p(t) -> ctypes.c_void_p:
+    return ctypes.c_void_p(_tptr(t)) if t is not None else None
+
+
+def rms_norm_device(ctx: GpuContext, x_t, weight_t, eps: float = 1e-6, out_t=None):
+    import torch
+    width = x_t.shape[-1]
+    out_t = out_t if out_t is not None else torch.empty_like(x_t)
+    _check(lib().uocr_rms_norm(ctx.handle, _p(x_t), x_t.numel() // max(width, 1), width,
+                               _p(weight_t), float(eps), _p(out_t)))
+    return out_t
+
+
+def attention_decode_device(ctx: GpuContext, q_t, keys_t, values_t, heads: int, out_t=None):
+    """One query [width] over token-major keys/values [tokens x width]."""
+    import torch
+    out_t = out_t if out_t is not None else torch.empty_like(q_t)
+    _check(lib().uocr_attention_decode(ctx.handle, _p(q_t), _p(keys_t), keys_t.numel(),
+                                       _p(values_t), values_t.numel(), q_t.numel(), heads,
+                                       _p(out_t)))
+    return out_t
+
+
+class Rope:
+    """cos/sin table of positions [0, max_positions) (device)."""
+
+    def __init__(self, ctx: GpuContext, head_dim: int, theta: float = 10000.0,
+                 max_positions: int = 32768):
+        self.ctx = ctx
+        self.head_dim = head_dim
+        h = ctypes.c_void_p()
+        _check(lib().uocr_rope_create(ctx.handle, head_dim, float(theta), max_positions,
+                                      ctypes.byref(h)))
+        self._h = h
+
+    def apply(self, q_t, k_t, positions_t):
+        """Rotate q (and k) rows [rows x width] at positions (int32, device)."""
+        width = q_t.shape[-1]
+        _check(lib().uocr_rope_apply(self.ctx.handle, self._h, _p(q_t), _p(k_t),
+                                     q_t.numel() // width, width, _p(positions_t)))
+
+    def free(self):
+        if getattr(self, "_h", None):
+            lib().uocr_rope_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class KvCache:
+    """LayerCache for `batch` sequences (device)."""
+
+    def __init__(self, ctx: GpuContext, batch: int, heads: int, head_dim: int, window: int,
+                 max_prefix: int):
+        self.ctx = ctx
+        self.batch, self.heads, self.head_dim = batch, heads, head_dim
+        self.width = heads * head_dim
+        h = ctypes.c_void_p()
+        _check(lib().uocr_kv_create(ctx.handle, batch, heads, head_dim, window, max_prefix,
+                                    ctypes.byref(h)))
+        self._h = h
+
+    def prefill(self, seq: int, keys_t, values_t):
+        tokens = keys_t.numel() // self.width
+        _check(lib().uocr_kv_prefill(self.ctx.handle, self._h, seq, _p(keys_t), _p(values_t),
+                                     tokens))
+
+    def push(self, k_t, v_t):
+        _check(lib().uocr_kv_push(self.ctx.handle, self._h, _p(k_t), _p(v_t)))
+
+    def rope(self, rope: Rope, q_t, k_t):
+        _check(lib().uocr_kv_rope(self.ctx.handle, self._h, rope._h, _p(q_t), _p(k_t)))
+
+    def attention(self, q_t, out_t=None):
+        import torch
+        out_t = out_t if out_t is not None else torch.empty_like(q_t)
+        _check(lib().uocr_kv_attention(self.ctx.handle, self._h, _p(q_t), _p(out_t)))
+        return out_t
+
+    def state(self, seq: int):
+        """(tokens, position) of sequence seq (synchronous)."""
+        t, p = ctypes.c_size_t(), ctypes.c_size_t()
+        _check(lib().uocr_kv_state(self.ctx.handle, self._h, seq, ctypes.byref(t), ctypes.byref(p)))
+        return t.value, p.value
+
+    def buffers(self):
+        """(keys, values) device arrays as [batch, cap, width] torch views."""
+        import torch
+        k, v, cap = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_size_t()
+        _check(lib().uocr_kv_buffers(self._h, ctypes.byref(k), ctypes.byref(v), ctypes.byref(cap)))
+        n = self.batch * cap.value * self.width
+
+        def view(ptr):
+            return _wrap_device(ptr.value, n, self.ctx.device).view(self.batch, cap.value,
+                                                                    self.width)
+        return view(k), view(v)
+
+    def free(self):
+        if getattr(self, "_h", None):
+            lib().uocr_kv_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def _wrap_device(ptr: int, n: int, device: int):
+    """A float32 torch tensor over n floats of device memory owned elsewhere."""
+    import torch
+
+    class _Arr:
+        __cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False),
+                                    "version": 3, "strides": None}
+    return torch.as_tensor(_Arr(), device=f"cuda:{device}")
+
+
+class AttentionBlock:
+    """The attention half of Decoder::layer at decode for a batch of
+    sequences (src/decoder/mod.rs:241-341): residual = x + o_proj(attn(rope(
+    q_proj(n)), rope(k_proj(n)), v_proj(n))) with n = rms_norm(x), k/v pushed
+    into the cache first.  Projections are q8 matrices under the given
+    QuantizationMode (Decoder::projection, src/decoder/mod.rs:99-112)."""
+
+    def __init__(self, ctx: GpuContext, norm_t, q: Int8Matrix, k: Int8Matrix, v: Int8Matrix,
+                 o: Int8Matrix, cache: KvCache, rope: Rope, eps: float = 1e-6):
+        self.ctx, self.norm, self.q, self.k, self.v, self.o = ctx, norm_t, q, k, v, o
+        self.cache, self.rope_table, self.eps = cache, rope, eps
+
+    def forward_device(self, x_t, mode: int = QuantizationMode.WEIGHTS_ONLY, out_t=None):
+        import torch
+        dyn = mode == QuantizationMode.DYNAMIC_ACTIVATIONS
+        n = rms_norm_device(self.ctx, x_t, self.norm, self.eps)
+        q = self.q.linear_device(n, dynamic=dyn)
+        k = self.k.linear_device(n, dynamic=dyn)
+        v = self.v.linear_device(n, dynamic=dyn)
+        self.cache.rope(self.rope_table, q, k)
+        self.cache.push(k, v)
+        a = self.cache.attention(q)
+        out_t = out_t if out_t is not None else torch.empty_like(x_t)
+        self.o.linear_device(a, out_t, dynamic=dyn)
+        out_t += x_t
+        return out_t
+
+
+__all__ = ["rms_norm_device", "attention_decode_device", "Rope", "KvCache", "AttentionBlock"]
