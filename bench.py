@@ -867,7 +867,7 @@ def run_attn(args):
                       "heads": ATTN_HEADS, "head_dim": ATTN_DIM, "prefix": ATTN_PREFIX,
                       "window": ATTN_WINDOW, "bytes_per_step": ATTN_BYTES,
                       "l2": "2 caches x 1.43 GB rotated (> 126 MB L2)"},
-           "roofline": {"bound": "hbm", "kernel": "attn_decode_kernel", "achieved": round(gbs, 2),
+           "roofline": {"bound": "hbm", "kernel": "attn_decode_tma_kernel", "achieved": round(gbs, 2),
                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                         "frac": round(gbs / peak, 4), "traffic": args.traffic},
            "gpu_launches": steps, "clocks": clocks.summary()}

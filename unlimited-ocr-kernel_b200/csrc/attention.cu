@@ -26,6 +26,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tc_maps.cuh"
 
 namespace uocr {
 
@@ -326,6 +327,224 @@ cudaError_t launch_attention_decode(const AttnArgs& a, int batch, int max_tokens
     attn_decode_kernel<true><<<grid, kAttnThreads, smem, st>>>(a);
   else
     attn_decode_kernel<false><<<grid, kAttnThreads, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+
+// ---- single-query attention, TMA pipeline ----------------------------------------
+// For head_dim % 32 == 0 (<= 256) and 16-byte-aligned rows: one CTA per
+// (head, sequence) of two warps.  The producer warp streams the head's key
+// rows, then its value rows, as 32-token tiles of head_dim/32 boxes of
+// 32 x 32 floats (128-byte swizzle) through a two-stage ring; the consumer
+// warp computes from shared memory with the same arithmetic as
+// attn_decode_kernel: lane = token for the scores (a swizzled row is read
+// conflict-free by eight lanes at a time), one warp for the softmax, lane =
+// four output elements for the value sums.  The ring keeps two tiles in
+// flight per CTA while five CTAs share an SM, and the value tiles stream in
+// while the softmax runs.
+constexpr int kTmaTile = 32;
+constexpr int kTmaStages = 2;
+constexpr int kTmaBoxBytes = 32 * 32 * 4;
+
+__host__ __device__ inline size_t attn_tma_smem(int dim, long long max_tokens) {
+  const size_t stage = static_cast<size_t>(dim / 32) * kTmaBoxBytes;
+  return 1024 + kTmaStages * stage + static_cast<size_t>(dim) * 4 +
+         ((static_cast<size_t>(max_tokens) * 4 + 15) & ~static_cast<size_t>(15)) + 64;
+}
+
+__global__ void __launch_bounds__(64)
+    attn_decode_tma_kernel(const __grid_constant__ CUtensorMap kmap,
+                           const __grid_constant__ CUtensorMap vmap, const AttnArgs a) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int dim = a.dim, nb = dim / 32;
+  const int stage_bytes = nb * kTmaBoxBytes;
+  float* qs = reinterpret_cast<float*>(base + kTmaStages * stage_bytes);
+  float* sc = qs + dim;
+  uint64_t* full = reinterpret_cast<uint64_t*>(
+      (reinterpret_cast<uintptr_t>(sc + a.cap) + 15) & ~static_cast<uintptr_t>(15));
+  uint64_t* empty = full + kTmaStages;
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int T = a.tokens;
+  if (a.state) {
+    const int prefix = a.state[2 * b], gen = a.state[2 * b + 1];
+    if (prefix <= 0) {
+      if (threadIdx.x == 0) flag(a.status, DEV_CACHE);
+      return;
+    }
+    T = prefix + (gen < a.window ? gen : a.window);
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kTmaStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 0)
+    for (int d = lane; d < dim; d += 32) qs[d] = a.q[b * a.ld_q + static_cast<long long>(h) * dim + d];
+  __syncthreads();
+  const int ntiles = (T + kTmaTile - 1) / kTmaTile;
+  if (warp == 1) {
+    // ---- producer
+    if (lane == 0) {
+      const int y0 = static_cast<int>(static_cast<long long>(b) * a.cap);
+      const int x0 = h * dim;
+      int it = 0;
+      for (; it < 2 * ntiles; ++it) {
+        const int st = it & 1;
+        if (it >= kTmaStages && !mbar_wait(&empty[st], ((it >> 1) - 1) & 1, a.status)) break;
+        const bool keys = it < ntiles;
+        const int tile = keys ? it : it - ntiles;
+        unsigned char* dst = base + st * stage_bytes;
+        mbar_arrive_expect_tx(&full[st], stage_bytes);
+        for (int j = 0; j < nb; ++j)
+          tma_load_2d(dst + j * kTmaBoxBytes, keys ? &kmap : &vmap, x0 + 32 * j,
+                      y0 + tile * kTmaTile, &full[st]);
+      }
+      for (int j = it - kTmaStages; j < it; ++j)  // every issued copy lands before exit
+        if (j >= 0) mbar_wait(&full[j & 1], (j >> 1) & 1, a.status);
+    }
+    return;
+  }
+  // ---- consumer: scores
+  const float4* q4 = reinterpret_cast<const float4*>(qs);
+  for (int i = 0; i < ntiles; ++i) {
+    const int st = i & 1;
+    mbar_wait(&full[st], (i >> 1) & 1, a.status);
+    const int t = i * kTmaTile + lane;
+    if (t < T) {
+      const unsigned char* row = base + st * stage_bytes + lane * 128;
+      float acc = -0.0f;
+      for (int j = 0; j < nb; ++j) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float4 kv =
+              *reinterpret_cast<const float4*>(row + j * kTmaBoxBytes + ((c ^ (lane & 7)) << 4));
+          const float4 qv = q4[j * 8 + c];
+          acc = __fadd_rn(acc, __fmul_rn(qv.x, kv.x));
+          acc = __fadd_rn(acc, __fmul_rn(qv.y, kv.y));
+          acc = __fadd_rn(acc, __fmul_rn(qv.z, kv.z));
+          acc = __fadd_rn(acc, __fmul_rn(qv.w, kv.w));
+        }
+      }
+      sc[t] = __fmul_rn(acc, a.scale);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+  }
+  __syncwarp();
+  // ---- softmax_backend (src/cpu/ops.rs:139-187)
+  float mx = -INFINITY;
+  int bad = 0;
+  for (int t = lane; t < T; t += 32) {
+    const float v = sc[t];
+    bad |= isnan(v) || v == INFINITY;
+    mx = fmaxf(mx, v);
+  }
+  mx = warp_max(mx);
+  bad = __any_sync(0xffffffffu, bad) || !isfinite(mx);
+  if (!bad) {
+    for (int t = lane; t < T; t += 32) sc[t] = exp_f32_via_f64(__fsub_rn(sc[t], mx));
+    __syncwarp();
+    float sum = -0.0f;
+    if (lane == 0) {
+      int t = 0;
+      for (; t + 8 <= T; t += 8) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = sc[t + j];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) sum = __fadd_rn(sum, v[j]);
+      }
+      for (; t < T; ++t) sum = __fadd_rn(sum, sc[t]);
+    }
+    sum = __shfl_sync(0xffffffffu, sum, 0);
+    for (int t = lane; t < T; t += 32) sc[t] = __fdiv_rn(sc[t], sum);
+    __syncwarp();
+  } else if (lane == 0) {
+    flag(a.status, DEV_SOFTMAX);
+  }
+  // ---- values: lane owns 16-byte chunks g = lane, lane + 32 of the head row
+  const int chunks = dim / 4;
+  float4 acc0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), acc1 = acc0;
+  const int g0 = lane, g1 = lane + 32;
+  for (int i = 0; i < ntiles; ++i) {
+    const int it = ntiles + i, st = it & 1;
+    mbar_wait(&full[st], (it >> 1) & 1, a.status);
+    if (!bad) {
+      const unsigned char* tile = base + st * stage_bytes;
+      const int rows = T - i * kTmaTile < kTmaTile ? T - i * kTmaTile : kTmaTile;
+      for (int r = 0; r < rows; ++r) {
+        const float p = sc[i * kTmaTile + r];
+        const unsigned char* row = tile + r * 128;
+        if (g0 < chunks) {
+          const float4 v = *reinterpret_cast<const float4*>(
+              row + (g0 >> 3) * kTmaBoxBytes + (((g0 & 7) ^ (r & 7)) << 4));
+          acc0.x = __fadd_rn(acc0.x, __fmul_rn(p, v.x));
+          acc0.y = __fadd_rn(acc0.y, __fmul_rn(p, v.y));
+          acc0.z = __fadd_rn(acc0.z, __fmul_rn(p, v.z));
+          acc0.w = __fadd_rn(acc0.w, __fmul_rn(p, v.w));
+        }
+        if (g1 < chunks) {
+          const float4 v = *reinterpret_cast<const float4*>(
+              row + (g1 >> 3) * kTmaBoxBytes + (((g1 & 7) ^ (r & 7)) << 4));
+          acc1.x = __fadd_rn(acc1.x, __fmul_rn(p, v.x));
+          acc1.y = __fadd_rn(acc1.y, __fmul_rn(p, v.y));
+          acc1.z = __fadd_rn(acc1.z, __fmul_rn(p, v.z));
+          acc1.w = __fadd_rn(acc1.w, __fmul_rn(p, v.w));
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+  }
+  if (bad) return;
+  float* ob = a.out + b * a.ld_out + static_cast<long long>(h) * dim;
+  if (g0 < chunks) {
+    ob[4 * g0] = acc0.x;
+    ob[4 * g0 + 1] = acc0.y;
+    ob[4 * g0 + 2] = acc0.z;
+    ob[4 * g0 + 3] = acc0.w;
+  }
+  if (g1 < chunks) {
+    ob[4 * g1] = acc1.x;
+    ob[4 * g1 + 1] = acc1.y;
+    ob[4 * g1 + 2] = acc1.z;
+    ob[4 * g1 + 3] = acc1.w;
+  }
+}
+
+bool attention_tma_ok(const float* keys, const float* values, long long rows, int width, int dim,
+                      long long cap) {
+  return dim % 32 == 0 && dim <= 256 && width % 4 == 0 && rows < (1LL << 31) &&
+         reinterpret_cast<uintptr_t>(keys) % 16 == 0 &&
+         reinterpret_cast<uintptr_t>(values) % 16 == 0 && attn_tma_smem(dim, cap) <= kAttnMaxSmem;
+}
+
+bool attention_tma_maps(AttnMaps* m, const float* keys, const float* values, long long rows,
+                        int width) {
+  return make_map_f32_sw128(reinterpret_cast<CUtensorMap*>(m->k), keys, rows, width) &&
+         make_map_f32_sw128(reinterpret_cast<CUtensorMap*>(m->v), values, rows, width);
+}
+
+cudaError_t launch_attention_decode_tma(const AttnMaps& m, const AttnArgs& a, int batch,
+                                        cudaStream_t st) {
+  const size_t smem = attn_tma_smem(a.dim, a.cap);
+  if (smem > kAttnMaxSmem || batch <= 0 || a.heads <= 0) return cudaErrorInvalidValue;
+  static unsigned configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured & (1u << (dev & 31)))) {
+    cudaFuncSetAttribute(attn_decode_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(kAttnMaxSmem));
+    configured |= 1u << (dev & 31);
+  }
+  const CUtensorMap* km = reinterpret_cast<const CUtensorMap*>(m.k);
+  const CUtensorMap* vm = reinterpret_cast<const CUtensorMap*>(m.v);
+  attn_decode_tma_kernel<<<dim3(a.heads, batch), 64, smem, st>>>(*km, *vm, a);
   return cudaGetLastError();
 }
 

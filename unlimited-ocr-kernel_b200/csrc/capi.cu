@@ -1340,7 +1340,13 @@ int uocr_attention_decode(uocr_ctx* ctx, const float* q_dev, const float* keys_d
   a.out = out_dev;
   a.ld_out = static_cast<long long>(width);
   a.status = ctx->status_dev;
-  cudaError_t e = launch_attention_decode(a, 1, static_cast<int>(tokens), ctx->stream);
+  AttnMaps maps;
+  const bool tma = attention_tma_ok(keys_dev, values_dev, static_cast<long long>(tokens),
+                                    a.width, a.dim, a.cap) &&
+                   attention_tma_maps(&maps, keys_dev, values_dev, static_cast<long long>(tokens),
+                                      a.width);
+  cudaError_t e = tma ? launch_attention_decode_tma(maps, a, 1, ctx->stream)
+                      : launch_attention_decode(a, 1, static_cast<int>(tokens), ctx->stream);
   if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
   return ok();
 }
@@ -1384,6 +1390,10 @@ int uocr_kv_create(uocr_ctx* ctx, size_t batch, size_t heads, size_t head_dim, s
     return fail(e == cudaErrorMemoryAllocation ? UOCR_ERR_RESOURCE : UOCR_ERR_CUDA,
                 "cache allocation: %s", cudaGetErrorString(e));
   }
+  kv->tma = attention_tma_ok(kv->keys, kv->values, static_cast<long long>(rows), kv->width,
+                             kv->head_dim, kv->cap) &&
+            attention_tma_maps(&kv->maps, kv->keys, kv->values, static_cast<long long>(rows),
+                               kv->width);
   *out = kv;
   return ok();
 }
@@ -1480,7 +1490,9 @@ int uocr_kv_attention(uocr_ctx* ctx, const uocr_kv* kv, const float* q_dev, floa
   a.out = out_dev;
   a.ld_out = kv->width;
   a.status = ctx->status_dev;
-  cudaError_t e = launch_attention_decode(a, kv->batch, static_cast<int>(kv->cap), ctx->stream);
+  cudaError_t e = kv->tma ? launch_attention_decode_tma(kv->maps, a, kv->batch, ctx->stream)
+                          : launch_attention_decode(a, kv->batch, static_cast<int>(kv->cap),
+                                                    ctx->stream);
   if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
   return ok();
 }

@@ -85,4 +85,6 @@ struct uocr_kv {
   float* values = nullptr;
   int* state = nullptr;
   std::vector<int> prefix;  // host mirror (0: not prefilled)
+  bool tma = false;         // maps valid: the TMA attention kernel applies
+  uocr::AttnMaps maps{};
 };

@@ -208,6 +208,18 @@ struct AttnArgs {
 constexpr size_t kAttnMaxSmem = 200 * 1024;
 size_t attention_smem_bytes(int dim, int max_tokens);
 cudaError_t launch_attention_decode(const AttnArgs& a, int batch, int max_tokens, cudaStream_t st);
+// TMA form (head_dim % 32 == 0, <= 256; rows 16-byte aligned): the key and
+// value tensor maps of [rows][width] arrays (opaque 128-byte CUtensorMaps).
+struct alignas(64) AttnMaps {
+  unsigned char k[128];
+  unsigned char v[128];
+};
+bool attention_tma_ok(const float* keys, const float* values, long long rows, int width, int dim,
+                      long long cap);
+bool attention_tma_maps(AttnMaps* m, const float* keys, const float* values, long long rows,
+                        int width);
+cudaError_t launch_attention_decode_tma(const AttnMaps& m, const AttnArgs& a, int batch,
+                                        cudaStream_t st);
 // rope_table.cpp — host: the reference's cos/sin of every (position, pair).
 void build_rope_table(int dim, float theta, int max_pos, float* cos_sin /* [max_pos][dim/2][2] */);
 
