@@ -248,6 +248,16 @@ int uocr_moe_combine(uocr_ctx *ctx, const int32_t *ids_dev, const float *weights
 int uocr_moe_forward_decode_noalloc(uocr_ctx *ctx, const uocr_moe *layer, int mode,
                                     const float *x_dev, const float *logits_dev, float *y_dev);
 
+/* Decoder::feed_forward (src/decoder/mod.rs:114-122): y = down(silu(gate x) *
+ * (up x)) for `rows` rows of x_dev (device, gate->cols floats each; y_dev rows
+ * of down->rows floats).  Each projection's arithmetic follows
+ * Decoder::projection (:99-112): int8 activations for a one-row input in
+ * UOCR_DYNAMIC_ACTIVATIONS, for every row in UOCR_DYNAMIC_ROWWISE (rows of
+ * independent sequences at decode), FP32 activations otherwise.  Shape when
+ * gate/up/down disagree; asynchronous on the context's stream. */
+int uocr_feed_forward(uocr_ctx *ctx, const uocr_q8 *gate, const uocr_q8 *up, const uocr_q8 *down,
+                      int mode, const float *x_dev, size_t rows, float *y_dev);
+
 /* ---- decoder attention at decode --------------------------------------------
  * The attention half of Decoder::layer (src/decoder/mod.rs:241-341) for one
  * new token per sequence, on device pointers, asynchronous on the context's
@@ -284,10 +294,14 @@ int uocr_attention_decode(uocr_ctx *ctx, const float *q_dev, const float *keys_d
                           size_t keys_len, const float *values_dev, size_t values_len,
                           size_t width, size_t heads, float *out_dev);
 
-/* LayerCache (src/decoder/cache.rs) for `batch` sequences on the device:
- * token-major keys/values, an immutable prefix of up to max_prefix tokens
- * followed by a ring of `window` tokens (slot of a new token: prefix +
- * generated % window).  The per-sequence counters live in device memory, so
+/* LayerCache (src/decoder/cache.rs) for `batch` sequences on the device: an
+ * immutable prefix of up to max_prefix tokens followed by a ring of `window`
+ * tokens (slot of a new token: prefix + generated % window).  Stored per
+ * (sequence, head) so that a head's tokens stream contiguously (for head_dim
+ * a multiple of 32, in 32-slot tiles that are one contiguous 16 KB-class
+ * block each); a head's slot order is the reference's physical token order.
+ * Inputs (prefill rows, pushed k/v) and uocr_kv_export's output are
+ * token-major rows of heads * head_dim floats, as in the reference.  The per-sequence counters live in device memory, so
  * push, rope and attention can be captured in CUDA graphs.
  *   uocr_kv_prefill: LayerCache::prefill of sequence seq (device rows);
  *   uocr_kv_push:    LayerCache::push of row b of k/v ([batch x width]) into
@@ -295,7 +309,9 @@ int uocr_attention_decode(uocr_ctx *ctx, const float *q_dev, const float *keys_d
  *   uocr_kv_rope:    ops::rope of q and k rows at each sequence's position
  *                    (before this token's push);
  *   uocr_kv_attention: ops::attention_decode of q row b over sequence b;
- *   uocr_kv_state:   LayerCache::tokens and ::position (synchronous).
+ *   uocr_kv_state:   LayerCache::tokens and ::position (synchronous);
+ *   uocr_kv_export:  LayerCache::keys / ::values of sequence seq as
+ *                    token-major rows (device; NULL outputs: *tokens only).
  * push / rope / attention before every sequence is prefilled: Shape. */
 int uocr_kv_create(uocr_ctx *ctx, size_t batch, size_t heads, size_t head_dim, size_t window,
                    size_t max_prefix, uocr_kv **out);
@@ -307,8 +323,8 @@ int uocr_kv_rope(uocr_ctx *ctx, const uocr_kv *kv, const uocr_rope *rope, float 
                  float *k_dev);
 int uocr_kv_attention(uocr_ctx *ctx, const uocr_kv *kv, const float *q_dev, float *out_dev);
 int uocr_kv_state(uocr_ctx *ctx, const uocr_kv *kv, size_t seq, size_t *tokens, size_t *position);
-int uocr_kv_buffers(const uocr_kv *kv, const float **keys_dev, const float **values_dev,
-                    size_t *cap);
+int uocr_kv_export(uocr_ctx *ctx, const uocr_kv *kv, size_t seq, float *keys_out,
+                   float *values_out, size_t *tokens);
 
 /* ---- INT8 overlay (QuantizedWeights) --------------------------------------
  * The "uocr-q8-block32-v1" overlay: a safetensors file holding, for every

@@ -170,12 +170,14 @@ def test_attention_layout_errors(ctx):
 
 
 # ---------------------------------------------------------------- KV cache
-def test_cache_ring_matches_layer_cache(ctx):
+@pytest.mark.parametrize("heads,dim", [(2, 8), (2, 64), (3, 128)])
+def test_cache_ring_matches_layer_cache(ctx, heads, dim):
     """Prefill + pushes across ring wraps (tests/cache.rs shapes scaled up):
-    the device cache holds the reference's physical token order, and the
-    attention over it equals the oracle's over LayerCache contents."""
-    rng = np.random.default_rng(11)
-    batch, heads, dim, window = 3, 2, 8, 5
+    the device cache holds the reference's physical token order (plain layout
+    for head_dim 8, 32-slot tiles for 64 and 128), and the attention over it
+    equals the oracle's over LayerCache contents."""
+    rng = np.random.default_rng(11 + dim)
+    batch, window = 3, 5
     width = heads * dim
     prefixes = [4, 1, 7]
     kv = A().KvCache(ctx, batch, heads, dim, window, max_prefix=8)
@@ -194,11 +196,11 @@ def test_cache_ring_matches_layer_cache(ctx):
             refs[b].push(k[b], v[b])
         out = host(kv.attention(dev(q)))
         ctx.sync()
-        keys, values = (host(t) for t in kv.buffers())
         for b in range(batch):
             n = refs[b].tokens()
             assert kv.state(b) == (n, refs[b].position())
-            assert bits_equal(keys[b, :n], refs[b].keys) and bits_equal(values[b, :n], refs[b].values)
+            keys, values = (host(t) for t in kv.export(b))
+            assert bits_equal(keys, refs[b].keys) and bits_equal(values, refs[b].values)
             ref = oracle.attention_decode(q[b], refs[b].keys, refs[b].values, heads)
             assert np.max(np.abs(out[b] - ref)) <= 1e-5 * max(1.0, float(np.max(np.abs(ref))))
     kv.free()

@@ -18,10 +18,14 @@
 //    thread, divide); each output element is a left-to-right sum over the
 //    tokens in physical cache order (one thread per element, +0.0 start).
 //
-// Layout: keys/values [batch][cap][width] floats, row (b, slot) = one token;
-// per-sequence state {prefix, generated} in device memory, so pushes and
-// attention can run inside captured graphs.  Slot of the next token:
-// prefix + generated % window; tokens present: prefix + min(generated, window).
+// Cache layout: head-major keys/values [batch][heads][cap][dim], so that one
+// head's tokens are one contiguous stream (the reference stores token-major
+// rows; the physical token order per head is the same, so sums run in the
+// same order); per-sequence state {prefix, generated} in device memory, so
+// pushes and attention can run inside captured graphs.  Slot of the next
+// token: prefix + generated % window; tokens present: prefix +
+// min(generated, window).  The single-query entry point takes the
+// reference's token-major buffers.
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -140,9 +144,18 @@ void launch_kv_set_prefix(int* state, int seq, int tokens, cudaStream_t st) {
   kv_set_prefix_kernel<<<1, 1, 0, st>>>(state, seq, tokens);
 }
 
+__device__ __forceinline__ long long kv_index(const KvLayout& L, int b, int h, long long slot,
+                                              int d) {
+  const long long base = (static_cast<long long>(b) * L.heads + h) * L.cap * L.dim;
+  if (!L.tiled) return base + slot * L.dim + d;
+  const long long tile = slot >> 5;
+  const int t = static_cast<int>(slot & 31), j = d >> 5, f = d & 31;
+  return base + ((tile * (L.dim >> 5) + j) * 32 + t) * 32 + f;
+}
+
 // LayerCache::push for every sequence: row b of k/v into its next slot.
-__global__ void kv_push_kernel(float* keys, float* values, int* state, int width, int window,
-                               long long cap, const float* __restrict__ k,
+__global__ void kv_push_kernel(float* keys, float* values, int* state, const KvLayout L,
+                               int window, const float* __restrict__ k,
                                const float* __restrict__ v, long long ld, unsigned* status) {
   const int b = blockIdx.x;
   const int prefix = state[2 * b], gen = state[2 * b + 1];
@@ -151,23 +164,60 @@ __global__ void kv_push_kernel(float* keys, float* values, int* state, int width
     return;
   }
   const long long slot = prefix + gen % window;
-  float* kd = keys + (b * cap + slot) * width;
-  float* vd = values + (b * cap + slot) * width;
   const float* ks = k + b * ld;
   const float* vs = v + b * ld;
-  for (int i = threadIdx.x; i < width; i += blockDim.x) {
-    kd[i] = ks[i];
-    vd[i] = vs[i];
+  for (int i = threadIdx.x; i < L.heads * L.dim; i += blockDim.x) {
+    const int h = i / L.dim, d = i - h * L.dim;
+    const long long o = kv_index(L, b, h, slot, d);
+    keys[o] = ks[i];
+    values[o] = vs[i];
   }
   __syncthreads();  // every thread has read `gen`
   if (threadIdx.x == 0) state[2 * b + 1] = gen + 1;
 }
 
-void launch_kv_push(float* keys, float* values, int* state, int batch, int width, int window,
-                    long long cap, const float* k, const float* v, long long ld, unsigned* status,
+void launch_kv_push(float* keys, float* values, int* state, int batch, const KvLayout& L,
+                    int window, const float* k, const float* v, long long ld, unsigned* status,
                     cudaStream_t st) {
   if (batch <= 0) return;
-  kv_push_kernel<<<batch, 256, 0, st>>>(keys, values, state, width, window, cap, k, v, ld, status);
+  kv_push_kernel<<<batch, 256, 0, st>>>(keys, values, state, L, window, k, v, ld, status);
+}
+
+// One block per token row: token-major [tokens][heads*dim] into the layout.
+__global__ void kv_prefill_kernel(float* keys, float* values, const KvLayout L, int seq,
+                                  const float* __restrict__ k, const float* __restrict__ v) {
+  const long long t = blockIdx.x;
+  const int width = L.heads * L.dim;
+  for (int i = threadIdx.x; i < width; i += blockDim.x) {
+    const int h = i / L.dim, d = i - h * L.dim;
+    const long long o = kv_index(L, seq, h, t, d);
+    keys[o] = k[t * width + i];
+    values[o] = v[t * width + i];
+  }
+}
+
+void launch_kv_prefill(float* keys, float* values, const KvLayout& L, int seq, const float* k,
+                       const float* v, int tokens, cudaStream_t st) {
+  if (tokens <= 0) return;
+  kv_prefill_kernel<<<tokens, 256, 0, st>>>(keys, values, L, seq, k, v);
+}
+
+__global__ void kv_export_kernel(const float* __restrict__ keys, const float* __restrict__ values,
+                                 const KvLayout L, int seq, float* k, float* v) {
+  const long long t = blockIdx.x;
+  const int width = L.heads * L.dim;
+  for (int i = threadIdx.x; i < width; i += blockDim.x) {
+    const int h = i / L.dim, d = i - h * L.dim;
+    const long long o = kv_index(L, seq, h, t, d);
+    k[t * width + i] = keys[o];
+    v[t * width + i] = values[o];
+  }
+}
+
+void launch_kv_export(const float* keys, const float* values, const KvLayout& L, int seq,
+                      int tokens, float* k_out, float* v_out, cudaStream_t st) {
+  if (tokens <= 0) return;
+  kv_export_kernel<<<tokens, 256, 0, st>>>(keys, values, L, seq, k_out, v_out);
 }
 
 // ---- single-query attention ---------------------------------------------------------
@@ -204,7 +254,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   __shared__ int s_bad;
   const int h = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int dim = a.dim, width = a.width;
+  const int dim = a.dim;
   float* qs = smem_f;                              // dim floats
   float* sc = smem_f + ((dim + 3) & ~3);           // tokens floats
   int T = a.tokens;
@@ -216,17 +266,18 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     }
     T = prefix + (gen < a.window ? gen : a.window);
   }
-  const float* kb = a.keys + static_cast<long long>(b) * a.cap * width + static_cast<long long>(h) * dim;
-  const float* vb = a.values + static_cast<long long>(b) * a.cap * width + static_cast<long long>(h) * dim;
+  const long long off = b * a.seq_stride + h * a.head_stride, rs = a.row_stride;
+  const float* kb = a.keys + off;
+  const float* vb = a.values + off;
   for (int d = tid; d < dim; d += kAttnThreads) qs[d] = a.q[b * a.ld_q + static_cast<long long>(h) * dim + d];
   __syncthreads();
 
   // scores: one thread per token, two tokens in flight per thread
   for (int t = tid; t < T; t += 2 * kAttnThreads) {
     const int t2 = t + kAttnThreads;
-    const float s1 = token_score<VEC>(kb + static_cast<long long>(t) * width, qs, dim);
+    const float s1 = token_score<VEC>(kb + t * rs, qs, dim);
     if (t2 < T) {
-      const float s2 = token_score<VEC>(kb + static_cast<long long>(t2) * width, qs, dim);
+      const float s2 = token_score<VEC>(kb + t2 * rs, qs, dim);
       sc[t2] = __fmul_rn(s2, a.scale);
     }
     sc[t] = __fmul_rn(s1, a.scale);
@@ -293,11 +344,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     for (; t + 16 <= T; t += 16) {
       float v[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = __ldg(vc + static_cast<long long>(t + j) * width);
+      for (int j = 0; j < 16; ++j) v[j] = __ldg(vc + (t + j) * rs);
 #pragma unroll
       for (int j = 0; j < 16; ++j) acc = __fadd_rn(acc, __fmul_rn(sc[t + j], v[j]));
     }
-    for (; t < T; ++t) acc = __fadd_rn(acc, __fmul_rn(sc[t], __ldg(vc + static_cast<long long>(t) * width)));
+    for (; t < T; ++t) acc = __fadd_rn(acc, __fmul_rn(sc[t], __ldg(vc + t * rs)));
     ob[d] = acc;
   }
 }
@@ -309,9 +360,9 @@ size_t attention_smem_bytes(int dim, int max_tokens) {
 cudaError_t launch_attention_decode(const AttnArgs& a, int batch, int max_tokens, cudaStream_t st) {
   const size_t smem = attention_smem_bytes(a.dim, max_tokens);
   if (smem > kAttnMaxSmem || batch <= 0 || a.heads <= 0) return cudaErrorInvalidValue;
-  // 16-byte key loads: every row (width floats) and head (dim floats) start aligned
-  const bool vec = a.dim % 4 == 0 && a.width % 4 == 0 &&
-                   reinterpret_cast<uintptr_t>(a.keys) % 16 == 0;
+  // 16-byte key loads: every row and head start aligned
+  const bool vec = a.dim % 4 == 0 && a.row_stride % 4 == 0 && a.head_stride % 4 == 0 &&
+                   a.seq_stride % 4 == 0 && reinterpret_cast<uintptr_t>(a.keys) % 16 == 0;
   static unsigned configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -390,6 +441,10 @@ __global__ void __launch_bounds__(64)
   if (warp == 1) {
     // ---- producer
     if (lane == 0) {
+      // tiled cache: the map's rows are 128-byte rows of the cache, a tile is
+      // one box of 32 * nb of them; token-major buffers ([rows][width]): a
+      // tile is nb boxes of 32 rows at x = h*dim + 32j
+      const long long tiled_y0 = (static_cast<long long>(b) * a.heads + h) * a.cap * nb;
       const int y0 = static_cast<int>(static_cast<long long>(b) * a.cap);
       const int x0 = h * dim;
       int it = 0;
@@ -400,9 +455,15 @@ __global__ void __launch_bounds__(64)
         const int tile = keys ? it : it - ntiles;
         unsigned char* dst = base + st * stage_bytes;
         mbar_arrive_expect_tx(&full[st], stage_bytes);
-        for (int j = 0; j < nb; ++j)
-          tma_load_2d(dst + j * kTmaBoxBytes, keys ? &kmap : &vmap, x0 + 32 * j,
-                      y0 + tile * kTmaTile, &full[st]);
+        if (a.tiled) {
+          tma_load_2d(dst, keys ? &kmap : &vmap, 0,
+                      static_cast<int>(tiled_y0 + static_cast<long long>(tile) * kTmaTile * nb),
+                      &full[st]);
+        } else {
+          for (int j = 0; j < nb; ++j)
+            tma_load_2d(dst + j * kTmaBoxBytes, keys ? &kmap : &vmap, x0 + 32 * j,
+                        y0 + tile * kTmaTile, &full[st]);
+        }
       }
       for (int j = it - kTmaStages; j < it; ++j)  // every issued copy lands before exit
         if (j >= 0) mbar_wait(&full[j & 1], (j >> 1) & 1, a.status);
@@ -517,17 +578,24 @@ __global__ void __launch_bounds__(64)
   }
 }
 
-bool attention_tma_ok(const float* keys, const float* values, long long rows, int width, int dim,
+bool attention_tma_ok(const float* keys, const float* values, long long rows, int cols, int dim,
                       long long cap) {
-  return dim % 32 == 0 && dim <= 256 && width % 4 == 0 && rows < (1LL << 31) &&
+  return dim % 32 == 0 && dim <= 256 && cols % 4 == 0 && rows < (1LL << 31) &&
          reinterpret_cast<uintptr_t>(keys) % 16 == 0 &&
          reinterpret_cast<uintptr_t>(values) % 16 == 0 && attn_tma_smem(dim, cap) <= kAttnMaxSmem;
 }
 
 bool attention_tma_maps(AttnMaps* m, const float* keys, const float* values, long long rows,
-                        int width) {
-  return make_map_f32_sw128(reinterpret_cast<CUtensorMap*>(m->k), keys, rows, width) &&
-         make_map_f32_sw128(reinterpret_cast<CUtensorMap*>(m->v), values, rows, width);
+                        int cols) {
+  return make_map_f32_sw128(reinterpret_cast<CUtensorMap*>(m->k), keys, rows, cols) &&
+         make_map_f32_sw128(reinterpret_cast<CUtensorMap*>(m->v), values, rows, cols);
+}
+
+bool attention_tma_maps_tiled(AttnMaps* m, const float* keys, const float* values,
+                              long long elements, int dim) {
+  const long long rows = elements / 32;  // 128-byte rows
+  return make_map_f32_sw128(reinterpret_cast<CUtensorMap*>(m->k), keys, rows, 32, dim) &&
+         make_map_f32_sw128(reinterpret_cast<CUtensorMap*>(m->v), values, rows, 32, dim);
 }
 
 cudaError_t launch_attention_decode_tma(const AttnMaps& m, const AttnArgs& a, int batch,

@@ -1233,6 +1233,44 @@ int uocr_moe_forward_host(uocr_ctx* ctx, const uocr_moe* layer, int mode, const 
 }
 
 
+// Decoder::feed_forward (src/decoder/mod.rs:114-122): y = down(silu(gate x) *
+// up x) for `rows` rows of x (device), each projection as
+// Decoder::projection (:99-112) makes it: int8 activations for a one-row
+// input in DynamicActivations mode, for every row in the row-wise mode.
+int uocr_feed_forward(uocr_ctx* ctx, const uocr_q8* gate, const uocr_q8* up, const uocr_q8* down,
+                      int mode, const float* x_dev, size_t rows, float* y_dev) {
+  if (!ctx || !gate || !up || !down) return fail(UOCR_ERR_INVALID, "null argument");
+  if (mode != UOCR_WEIGHTS_ONLY && mode != UOCR_DYNAMIC_ACTIVATIONS && mode != UOCR_DYNAMIC_ROWWISE)
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: mode %d", mode);
+  if (gate->rows != up->rows || gate->cols != up->cols || down->cols != gate->rows)
+    return fail(UOCR_ERR_SHAPE, "invalid tensor shape: feed-forward projections");
+  if (rows == 0) return ok();
+  if (!x_dev || !y_dev) return fail(UOCR_ERR_INVALID, "null argument");
+  if (!fits_int(rows)) return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: rows");
+  int st;
+  if ((st = linear_checks(ctx, gate, rows)) || (st = linear_checks(ctx, down, rows))) return st;
+  const int lm = mode == UOCR_DYNAMIC_ROWWISE || (mode == UOCR_DYNAMIC_ACTIVATIONS && rows == 1)
+                     ? MODE_INT8
+                     : MODE_FP32;
+  const size_t F = gate->rows;
+  const size_t gb = al256(rows * F * 4);
+  size_t sb = linear_scratch_bytes(gate, lm, rows);
+  const size_t sd = linear_scratch_bytes(down, lm, rows);
+  if (sd > sb) sb = sd;
+  DeviceGuard g(ctx->device);
+  if ((st = ensure_ws(ctx, 2 * gb + sb))) return st;
+  char* base = static_cast<char*>(ctx->ws);
+  float* gd = reinterpret_cast<float*>(base);
+  float* ud = reinterpret_cast<float*>(base + gb);
+  char* scratch = base + 2 * gb;
+  if ((st = linear_launch(ctx, gate, lm, x_dev, rows, gd, scratch)) ||
+      (st = linear_launch(ctx, up, lm, x_dev, rows, ud, scratch)))
+    return st;
+  launch_swiglu(gd, ud, static_cast<long long>(rows * F), gd, ctx->sms, ctx->stream);
+  if ((st = check_launch())) return st;
+  return linear_launch(ctx, down, lm, gd, rows, y_dev, scratch);
+}
+
 // ---- decoder attention at decode --------------------------------------------
 // ops::rms_norm (src/cpu/ops.rs:362-414, 419-421)
 int uocr_rms_norm(uocr_ctx* ctx, const float* x_dev, size_t rows, size_t width,
@@ -1331,6 +1369,9 @@ int uocr_attention_decode(uocr_ctx* ctx, const float* q_dev, const float* keys_d
   a.ld_q = static_cast<long long>(width);
   a.keys = keys_dev;
   a.values = values_dev;
+  a.seq_stride = static_cast<long long>(tokens * width);
+  a.head_stride = static_cast<long long>(dim);
+  a.row_stride = static_cast<long long>(width);
   a.cap = static_cast<long long>(tokens);
   a.width = static_cast<int>(width);
   a.heads = static_cast<int>(heads);
@@ -1365,8 +1406,15 @@ int uocr_kv_create(uocr_ctx* ctx, size_t batch, size_t heads, size_t head_dim, s
     return fail(UOCR_ERR_SHAPE, "invalid tensor shape: empty cache batch or prefix");
   size_t cap, rows, n, bytes;
   if (max_prefix > (size_t(1) << 30) || window > (size_t(1) << 30) || !fits_int(width) ||
-      !fits_int(batch) || (cap = max_prefix + window) > (size_t(1) << 30) ||
-      !mul_ok(batch, cap, &rows) || !mul_ok(rows, width, &n) || !mul_ok(n, 4, &bytes))
+      !fits_int(batch) || (cap = max_prefix + window) > (size_t(1) << 30))
+    return fail(UOCR_ERR_RESOURCE, "resource limit: cache capacity overflow");
+  // tiled layout (one TMA box per 32-slot tile) when the TMA attention kernel applies
+  const size_t cap_tiled = (cap + 31) & ~static_cast<size_t>(31);
+  const bool tiled = attention_tma_ok(nullptr, nullptr, 0, 32, static_cast<int>(head_dim),
+                                      static_cast<long long>(cap_tiled));
+  if (tiled) cap = cap_tiled;
+  if (!mul_ok(batch, cap, &rows) || !mul_ok(rows, width, &n) || !mul_ok(n, 4, &bytes) ||
+      n / 32 >= (size_t(1) << 31))
     return fail(UOCR_ERR_RESOURCE, "resource limit: cache capacity overflow");
   DeviceGuard g(ctx->device);
   auto* kv = new uocr_kv();
@@ -1378,6 +1426,7 @@ int uocr_kv_create(uocr_ctx* ctx, size_t batch, size_t heads, size_t head_dim, s
   kv->window = static_cast<int>(window);
   kv->max_prefix = static_cast<int>(max_prefix);
   kv->cap = static_cast<long long>(cap);
+  kv->layout = KvLayout{kv->heads, kv->head_dim, kv->cap, tiled ? 1 : 0};
   kv->prefix.assign(batch, 0);
   cudaError_t e = cudaMalloc(&kv->keys, bytes);
   if (e == cudaSuccess) e = cudaMalloc(&kv->values, bytes);
@@ -1390,10 +1439,12 @@ int uocr_kv_create(uocr_ctx* ctx, size_t batch, size_t heads, size_t head_dim, s
     return fail(e == cudaErrorMemoryAllocation ? UOCR_ERR_RESOURCE : UOCR_ERR_CUDA,
                 "cache allocation: %s", cudaGetErrorString(e));
   }
-  kv->tma = attention_tma_ok(kv->keys, kv->values, static_cast<long long>(rows), kv->width,
-                             kv->head_dim, kv->cap) &&
-            attention_tma_maps(&kv->maps, kv->keys, kv->values, static_cast<long long>(rows),
-                               kv->width);
+  kv->tma = tiled && attention_tma_maps_tiled(&kv->maps, kv->keys, kv->values,
+                                              static_cast<long long>(n), kv->head_dim);
+  if (tiled && !kv->tma) {
+    uocr_kv_free(kv);
+    return fail(UOCR_ERR_CUDA, "cache tensor maps could not be built");
+  }
   *out = kv;
   return ok();
 }
@@ -1420,9 +1471,8 @@ int uocr_kv_prefill(uocr_ctx* ctx, uocr_kv* kv, size_t seq, const float* keys_de
     return fail(UOCR_ERR_RESOURCE, "resource limit: cache capacity overflow");
   if (!keys_dev || !values_dev) return fail(UOCR_ERR_INVALID, "null argument");
   DeviceGuard g(ctx->device);
-  const size_t off = seq * static_cast<size_t>(kv->cap) * kv->width, n = tokens * kv->width * 4;
-  CUDA_TRY(cudaMemcpyAsync(kv->keys + off, keys_dev, n, cudaMemcpyDeviceToDevice, ctx->stream));
-  CUDA_TRY(cudaMemcpyAsync(kv->values + off, values_dev, n, cudaMemcpyDeviceToDevice, ctx->stream));
+  launch_kv_prefill(kv->keys, kv->values, kv->layout, static_cast<int>(seq), keys_dev, values_dev,
+                    static_cast<int>(tokens), ctx->stream);
   launch_kv_set_prefix(kv->state, static_cast<int>(seq), static_cast<int>(tokens), ctx->stream);
   int st = check_launch();
   if (st) return st;
@@ -1444,8 +1494,8 @@ int uocr_kv_push(uocr_ctx* ctx, uocr_kv* kv, const float* k_dev, const float* v_
   if (st) return st;
   if (!k_dev || !v_dev) return fail(UOCR_ERR_INVALID, "null argument");
   DeviceGuard g(ctx->device);
-  launch_kv_push(kv->keys, kv->values, kv->state, kv->batch, kv->width, kv->window, kv->cap, k_dev,
-                 v_dev, kv->width, ctx->status_dev, ctx->stream);
+  launch_kv_push(kv->keys, kv->values, kv->state, kv->batch, kv->layout, kv->window, k_dev, v_dev,
+                 kv->width, ctx->status_dev, ctx->stream);
   return check_launch();
 }
 
@@ -1480,7 +1530,11 @@ int uocr_kv_attention(uocr_ctx* ctx, const uocr_kv* kv, const float* q_dev, floa
   a.ld_q = kv->width;
   a.keys = kv->keys;
   a.values = kv->values;
+  a.head_stride = kv->cap * kv->head_dim;
+  a.seq_stride = a.head_stride * kv->heads;
+  a.row_stride = kv->head_dim;
   a.cap = kv->cap;
+  a.tiled = kv->layout.tiled;
   a.width = kv->width;
   a.heads = kv->heads;
   a.dim = kv->head_dim;
@@ -1511,13 +1565,20 @@ int uocr_kv_state(uocr_ctx* ctx, const uocr_kv* kv, size_t seq, size_t* tokens, 
   return take_device_status(ctx);
 }
 
-// The cache's device arrays ([batch][cap][width] each) and cap.
-int uocr_kv_buffers(const uocr_kv* kv, const float** keys_dev, const float** values_dev, size_t* cap) {
-  if (!kv) return fail(UOCR_ERR_INVALID, "null cache");
-  if (keys_dev) *keys_dev = kv->keys;
-  if (values_dev) *values_dev = kv->values;
-  if (cap) *cap = static_cast<size_t>(kv->cap);
-  return ok();
+// Slots [0, tokens) of sequence seq, where tokens = LayerCache::tokens, as
+// token-major rows (keys_out / values_out: tokens * width floats each, device).
+int uocr_kv_export(uocr_ctx* ctx, const uocr_kv* kv, size_t seq, float* keys_out,
+                   float* values_out, size_t* tokens) {
+  if (!ctx || !kv || !tokens) return fail(UOCR_ERR_INVALID, "null argument");
+  size_t n = 0;
+  int st = uocr_kv_state(ctx, kv, seq, &n, nullptr);
+  if (st) return st;
+  *tokens = n;
+  if (!keys_out || !values_out) return ok();  // size query
+  DeviceGuard g(ctx->device);
+  launch_kv_export(kv->keys, kv->values, kv->layout, static_cast<int>(seq), static_cast<int>(n),
+                   keys_out, values_out, ctx->stream);
+  return check_launch();
 }
 
 }  // extern "C"

@@ -74,13 +74,14 @@ struct uocr_rope {
   float2* table = nullptr;  // device [max_pos][head_dim/2]
 };
 
-// KV cache of `batch` sequences (LayerCache each): keys/values
-// [batch][cap][width], cap = max_prefix + window, device state {prefix,
-// generated} per sequence; the host mirrors which sequences are prefilled.
+// KV cache of `batch` sequences (LayerCache each): keys/values per (sequence,
+// head) in the layout of uocr::KvLayout, device state {prefix, generated} per
+// sequence; the host mirrors which sequences are prefilled.
 struct uocr_kv {
   int device = 0;
   int batch = 0, heads = 0, head_dim = 0, width = 0, window = 0, max_prefix = 0;
-  long long cap = 0;
+  long long cap = 0;          // slots per sequence (max_prefix + window, rounded up when tiled)
+  uocr::KvLayout layout{};
   float* keys = nullptr;
   float* values = nullptr;
   int* state = nullptr;

@@ -81,6 +81,8 @@ void launch_swiglu_split(const float* g, const float* u, int rows, int cols, uin
 // xq_p[p] = xq[src[p]], xs_p[p] = xs[src[p]]
 void launch_gather_rows(const int8_t* xq, const float* xs, const int* src, int rows, int cols,
                         int8_t* xq_p, float* xs_p, int sms, cudaStream_t st);
+// h = silu(g) * u elementwise (n floats; h may alias g)
+void launch_swiglu(const float* g, const float* u, long long n, float* h, int sms, cudaStream_t st);
 // hq/hs = block-quantized silu(g) * u
 void launch_swiglu_quantize(const float* g, const float* u, int rows, int cols, int8_t* hq,
                             float* hs, unsigned* status, int sms, cudaStream_t st);
@@ -187,15 +189,41 @@ void launch_rope(float* a, float* b, long long ld, int rows, int heads, int dim,
                  const int* positions, const int* state, const float2* table, int max_pos,
                  unsigned* status, int sms, cudaStream_t st);
 void launch_kv_set_prefix(int* state, int seq, int tokens, cudaStream_t st);
-void launch_kv_push(float* keys, float* values, int* state, int batch, int width, int window,
-                    long long cap, const float* k, const float* v, long long ld, unsigned* status,
+// Device KV cache layouts, per (sequence b, head h) a region of cap x dim
+// floats at ((b * heads + h) * cap) * dim:
+//   plain: slot-major rows of dim floats;
+//   tiled (dim % 32 == 0, cap % 32 == 0): 32-slot tiles of dim/32 blocks of
+//     [32 slots][32 floats], so that one tile is one contiguous TMA box of
+//     32 x (dim) rows of 128 bytes.
+struct KvLayout {
+  int heads, dim;
+  long long cap;
+  int tiled;
+};
+// LayerCache::push: head h of row b of k/v (token-major, ld floats apart)
+// into slot prefix + generated % window of sequence b.
+void launch_kv_push(float* keys, float* values, int* state, int batch, const KvLayout& L,
+                    int window, const float* k, const float* v, long long ld, unsigned* status,
                     cudaStream_t st);
+// LayerCache::prefill of sequence seq: token-major rows [tokens][heads*dim].
+void launch_kv_prefill(float* keys, float* values, const KvLayout& L, int seq, const float* k,
+                       const float* v, int tokens, cudaStream_t st);
+// Slots [0, tokens) of sequence seq back as token-major rows.
+void launch_kv_export(const float* keys, const float* values, const KvLayout& L, int seq,
+                      int tokens, float* k_out, float* v_out, cudaStream_t st);
 struct AttnArgs {
   const float* q;  // [batch][ld_q], head h at h * dim
   long long ld_q;
-  const float* keys;    // [batch][cap][width]
-  const float* values;  // [batch][cap][width]
-  long long cap;
+  // Row of token t of head h of sequence b: keys + b * seq_stride +
+  // h * head_stride + t * row_stride (same for values).  Token-major
+  // ([batch][cap][width], the reference's layout): cap * width, dim, width.
+  // Head-major ([batch][heads][cap][dim], the device cache): heads * cap * dim,
+  // cap * dim, dim.
+  const float* keys;
+  const float* values;
+  long long seq_stride, head_stride, row_stride;
+  long long cap;  // token capacity of a sequence (scores scratch)
+  int tiled;      // tiled cache layout (TMA kernel: one box per 32-token tile)
   int width, heads, dim;
   int tokens;          // tokens per sequence when state is null
   const int* state;    // {prefix, generated} per sequence, or null
@@ -214,10 +242,15 @@ struct alignas(64) AttnMaps {
   unsigned char k[128];
   unsigned char v[128];
 };
-bool attention_tma_ok(const float* keys, const float* values, long long rows, int width, int dim,
+// rows x cols: the 2-D view the maps cover ([batch*cap][width] token-major,
+// [batch*heads*cap][dim] head-major).
+bool attention_tma_ok(const float* keys, const float* values, long long rows, int cols, int dim,
                       long long cap);
 bool attention_tma_maps(AttnMaps* m, const float* keys, const float* values, long long rows,
-                        int width);
+                        int cols);
+// Maps of a tiled cache (elements floats per array): box = one 32-slot tile.
+bool attention_tma_maps_tiled(AttnMaps* m, const float* keys, const float* values,
+                              long long elements, int dim);
 cudaError_t launch_attention_decode_tma(const AttnMaps& m, const AttnArgs& a, int batch,
                                         cudaStream_t st);
 // rope_table.cpp — host: the reference's cos/sin of every (position, pair).

@@ -134,3 +134,23 @@ void launch_validate_q8(const int8_t* w, long long n_w, const float* s, long lon
 }
 
 }  // namespace uocr
+
+namespace uocr {
+
+// h = silu(g) * u (Decoder::feed_forward, src/decoder/mod.rs:114-122): the
+// reference's silu rounding sequence, then one product.
+__global__ void swiglu_kernel(const float* __restrict__ g, const float* __restrict__ u, long long n,
+                              float* h) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    h[i] = __fmul_rn(silu_ref(g[i]), u[i]);
+}
+
+void launch_swiglu(const float* g, const float* u, long long n, float* h, int sms, cudaStream_t st) {
+  if (n <= 0) return;
+  long long blocks = (n + 255) / 256;
+  if (blocks > 8LL * sms) blocks = 8LL * sms;
+  swiglu_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(g, u, n, h);
+}
+
+}  // namespace uocr

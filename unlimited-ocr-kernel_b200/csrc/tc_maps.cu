@@ -48,12 +48,13 @@ bool make_map_f32(CUtensorMap* map, const float* base, long long rows, long long
             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-bool make_map_f32_sw128(CUtensorMap* map, const float* base, long long rows, long long cols) {
+bool make_map_f32_sw128(CUtensorMap* map, const float* base, long long rows, long long cols,
+                        int box_rows) {
   auto fn = tma_encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 4)};
-  const cuuint32_t box[2] = {32u, 32u};
+  const cuuint32_t box[2] = {32u, static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t estr[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

@@ -43,7 +43,8 @@ bool make_map_i8_plain(CUtensorMap* map, const void* base, long long rows, long 
 bool make_map_f32(CUtensorMap* map, const float* base, long long rows, long long nb, int box_rows);
 // float [rows][cols], box 32 floats (128 bytes) x 32 rows, 128-byte swizzle
 // (token-major KV rows for the decode attention kernel).
-bool make_map_f32_sw128(CUtensorMap* map, const float* base, long long rows, long long cols);
+bool make_map_f32_sw128(CUtensorMap* map, const float* base, long long rows, long long cols,
+                        int box_rows = 32);
 // int8 weights [rows][cols], box 64 bytes x 128 rows, unswizzled.
 bool make_map_w_rows64(CUtensorMap* map, const void* base, long long rows, long long cols);
 // bf16 pieces [3 * piece_rows][cols], box 64 elements x box_rows, 128-byte swizzle.

@@ -60,6 +60,7 @@ SIGNATURES = {
     "uocr_moe_combine": (I, [P, P, P, P, S, S, S, P]),
     "uocr_moe_dispatch": (I, [P, P, S, S, P, S, P, S, S, P, P, P]),
     "uocr_moe_combine_rows": (I, [P, P, P, P, P, S, S, S, P]),
+    "uocr_feed_forward": (I, [P, P, P, P, I, P, S, P]),
     "uocr_rms_norm": (I, [P, P, S, S, P, F, P]),
     "uocr_rope_create": (I, [P, S, F, S, PP]),
     "uocr_rope_free": (I, [P]),
@@ -72,7 +73,7 @@ SIGNATURES = {
     "uocr_kv_rope": (I, [P, P, P, P, P]),
     "uocr_kv_attention": (I, [P, P, P, P]),
     "uocr_kv_state": (I, [P, P, S, ctypes.POINTER(S), ctypes.POINTER(S)]),
-    "uocr_kv_buffers": (I, [P, PP, PP, ctypes.POINTER(S)]),
+    "uocr_kv_export": (I, [P, P, S, P, P, ctypes.POINTER(S)]),
     "uocr_overlay_check": (I, [ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(S),
                                ctypes.POINTER(S)]),
     "uocr_overlay_load": (I, [P, ctypes.c_char_p, ctypes.c_char_p, PP]),

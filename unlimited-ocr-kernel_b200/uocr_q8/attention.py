@@ -111,17 +111,16 @@ class KvCache:
         _check(lib().uocr_kv_state(self.ctx.handle, self._h, seq, ctypes.byref(t), ctypes.byref(p)))
         return t.value, p.value
 
-    def buffers(self):
-        """(keys, values) device arrays as [batch, cap, width] torch views."""
+    def export(self, seq: int):
+        """LayerCache::keys / ::values of sequence seq: token-major [tokens,
+        width] device tensors (a copy)."""
         import torch
-        k, v, cap = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_size_t()
-        _check(lib().uocr_kv_buffers(self._h, ctypes.byref(k), ctypes.byref(v), ctypes.byref(cap)))
-        n = self.batch * cap.value * self.width
-
-        def view(ptr):
-            return _wrap_device(ptr.value, n, self.ctx.device).view(self.batch, cap.value,
-                                                                    self.width)
-        return view(k), view(v)
+        n = ctypes.c_size_t()
+        _check(lib().uocr_kv_export(self.ctx.handle, self._h, seq, None, None, ctypes.byref(n)))
+        k = torch.empty((n.value, self.width), device=f"cuda:{self.ctx.device}")
+        v = torch.empty_like(k)
+        _check(lib().uocr_kv_export(self.ctx.handle, self._h, seq, _p(k), _p(v), ctypes.byref(n)))
+        return k, v
 
     def free(self):
         if getattr(self, "_h", None):
@@ -133,16 +132,6 @@ class KvCache:
             self.free()
         except Exception:
             pass
-
-
-def _wrap_device(ptr: int, n: int, device: int):
-    """A float32 torch tensor over n floats of device memory owned elsewhere."""
-    import torch
-
-    class _Arr:
-        __cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False),
-                                    "version": 3, "strides": None}
-    return torch.as_tensor(_Arr(), device=f"cuda:{device}")
 
 
 class AttentionBlock:
