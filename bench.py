@@ -876,6 +876,114 @@ def run_attn(args):
     return res
 
 
+DEC_BATCH, DEC_PREFIX = 64, 2048
+
+
+def decode_step_bytes(cfg, tokens_per_seq):
+    """Algorithmic HBM bytes of one batched decode step: every layer's KV
+    (keys + values of every present token of every sequence), every weight
+    the step reads (attention projections, the dense FFN, the shared expert,
+    the routed experts the batch selects — all of them at batch 64 — and
+    lm_head), the router and the embedding rows."""
+    H = cfg.hidden
+    kv = cfg.layers * DEC_BATCH * tokens_per_seq * H * 4 * 2
+    q8 = lambda r, c: r * c + r * ((c + 31) // 32) * 4
+    attn = cfg.layers * 4 * q8(H, H)
+    dense = cfg.first_dense * (2 * q8(cfg.dense_width, H) + q8(H, cfg.dense_width))
+    moe_layers = cfg.layers - cfg.first_dense
+    moe = moe_layers * ((cfg.experts * (2 * q8(cfg.expert_width, H) + q8(H, cfg.expert_width)))
+                        + 2 * q8(cfg.shared_width, H) + q8(H, cfg.shared_width)
+                        + cfg.experts * H * 2)
+    head = q8(cfg.vocab, H)
+    return kv + attn + dense + moe + head + DEC_BATCH * H * 2
+
+
+def run_decode(args):
+    """Config 4 on one GPU: a batched decode step of the 12-layer decoder
+    (64 sequences, 2048-token prefixes, 128-token ring) with random-init q8
+    weights, replayed from a CUDA graph; value = tokens/s."""
+    import torch
+
+    import uocr_q8
+    from uocr_q8.decoder import DecodeState, Decoder, DecoderConfig, decode_step
+    torch.cuda.set_device(0)
+    dev = "cuda:0"
+    ctx = uocr_q8.GpuContext(0)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream)
+    cfg = DecoderConfig()
+    mode = args.decode_mode
+    with torch.cuda.stream(stream):
+        dec = Decoder.random(ctx, cfg, seed=11, lm_head=args.lm_head)
+        state = DecodeState(dec, DEC_BATCH, DEC_PREFIX)
+        g = torch.Generator(device=dev)
+        g.manual_seed(12)
+        for cache in state.caches:
+            for b in range(DEC_BATCH):
+                k = torch.randn((DEC_PREFIX, cfg.hidden), device=dev, generator=g)
+                cache.prefill(b, k, k.mul(0.5))
+        tokens = torch.randint(0, cfg.vocab, (DEC_BATCH,), device=dev, generator=g)
+        logits = torch.empty((DEC_BATCH, cfg.vocab), device=dev)
+        for _ in range(max(args.warmup, 3)):  # eager: sizes every workspace
+            decode_step(dec, state, tokens, mode, logits)
+    ctx.sync()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        decode_step(dec, state, tokens, mode, logits)
+        tokens.copy_(torch.argmax(logits, dim=1))
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    steps = max(4, min(args.steps, 200))
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(steps):
+                graph.replay()
+            stop.record(stream)
+        stop.synchronize()
+    ms = start.elapsed_time(stop) / steps
+    tok_s = DEC_BATCH / (ms * 1e-3)
+    # ---- end to end: token ids in from pinned host memory, next ids out
+    e2e_steps = max(4, min(steps, 50))
+    h_in = torch.randint(0, cfg.vocab, (DEC_BATCH,), dtype=torch.int64).pin_memory()
+    h_out = torch.empty((DEC_BATCH,), dtype=torch.int64).pin_memory()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        for _ in range(e2e_steps):
+            tokens.copy_(h_in, non_blocking=True)
+            graph.replay()
+            h_out.copy_(tokens, non_blocking=True)
+            stream.synchronize()
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    tokens_now = state.caches[0].state(0)[0]
+    step_bytes = decode_step_bytes(cfg, tokens_now)
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+    peak, peak_kind = peak_hbm()
+    res = {"metric": "decode tok/s (config 4: 12-layer MoE decoder, batch 64, KV 2048)",
+           "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": 1, "steps": steps,
+           "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None,
+           "dtype": "int8-act" if mode else "fp32", "data": "synthetic (seeded; random-init weights)",
+           "config": {"workload": "config4_decode_step", "batch": DEC_BATCH, "prefix": DEC_PREFIX,
+                      "window": cfg.window, "layers": cfg.layers, "hidden": cfg.hidden,
+                      "experts": cfg.experts, "top_k": cfg.top_k, "vocab": cfg.vocab,
+                      "lm_head": args.lm_head, "mode": mode, "cuda_graph": True,
+                      "tokens_per_sequence": tokens_now, "bytes_per_step": step_bytes,
+                      "l2": "17 GB of KV per step (> 126 MB L2)"},
+           "e2e": {"value": round(DEC_BATCH / e2e_s, 1), "unit": "tok/s", "steps": e2e_steps,
+                   "ms_per_step": round(e2e_s * 1e3, 4), "h2d_bytes_per_step": DEC_BATCH * 8,
+                   "d2h_bytes_per_step": DEC_BATCH * 8},
+           "roofline": {"bound": "hbm", "kernel": "whole step (attention, MoE, projections)",
+                        "achieved": round(gbs, 2), "peak": peak, "peak_kind": peak_kind,
+                        "unit": "GB/s", "frac": round(gbs / peak, 4), "traffic": None},
+           "gpu_launches": None, "clocks": clocks.summary()}
+    state.free()
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -893,11 +1001,13 @@ def main():
                          "defaults to the committed capture of the workload's kernel")
     ap.add_argument("--workload",
                     choices=["moe_decode", "gemv", "prefill", "int8suite", "ep_decode",
-                             "attn_decode"],
+                             "attn_decode", "decode_step"],
                     default="moe_decode")
     ap.add_argument("--gemv-int8", action="store_true")
     ap.add_argument("--prefill-mode", type=int, choices=[0, 2], default=0)
     ap.add_argument("--ep-mode", type=int, choices=[0, 1, 2], default=0)
+    ap.add_argument("--decode-mode", type=int, choices=[0, 2], default=0)
+    ap.add_argument("--lm-head", choices=["q8", "bf16"], default="q8")
     args = ap.parse_args()
     if args.workload == "gemv" and args.impl == "ours":
         print(json.dumps(run_gemv(args)), flush=True)
@@ -909,6 +1019,9 @@ def main():
         res = run_ep(args)
         if res is not None:
             print(json.dumps(res), flush=True)
+        return
+    if args.workload == "decode_step" and args.impl == "ours":
+        print(json.dumps(run_decode(args)), flush=True)
         return
     if args.workload == "attn_decode" and args.impl == "ours":
         print(json.dumps(run_attn(args)), flush=True)

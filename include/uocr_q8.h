@@ -258,6 +258,14 @@ int uocr_moe_forward_decode_noalloc(uocr_ctx *ctx, const uocr_moe *layer, int mo
 int uocr_feed_forward(uocr_ctx *ctx, const uocr_q8 *gate, const uocr_q8 *up, const uocr_q8 *down,
                       int mode, const float *x_dev, size_t rows, float *y_dev);
 
+/* ops::linear_weight, BF16 branch (src/cpu/ops.rs:62-133): y [batch x n] = x
+ * [batch x k] (device floats) times a BF16 weight [n x k] (device bit
+ * patterns), each output a left-to-right float sum as in the reference (bit
+ * for bit): the router logits of Decoder::experts ("mlp.gate.weight" is not
+ * in the INT8 overlay).  Sized for router-like n; asynchronous. */
+int uocr_linear_bf16(uocr_ctx *ctx, const uint16_t *w_dev, size_t n, size_t k, const float *x_dev,
+                     size_t batch, float *y_dev);
+
 /* ---- decoder attention at decode --------------------------------------------
  * The attention half of Decoder::layer (src/decoder/mod.rs:241-341) for one
  * new token per sequence, on device pointers, asynchronous on the context's

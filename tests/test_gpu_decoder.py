@@ -1,0 +1,148 @@
+"""GPU parity of a batched decode step (Decoder::step, src/decoder/mod.rs:
+241-420) against the oracle's composition of the same reference operations,
+on a small decoder with a dense layer and an MoE layer, across ring wraps of
+the KV cache; and the pieces the step adds: Decoder::feed_forward and the
+BF16 router linear."""
+import numpy as np
+import pytest
+
+import oracle
+from helpers import bits_equal, random_q8
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    return t.detach().cpu().numpy()
+
+
+def test_linear_bf16_bit_exact(ctx):
+    from uocr_q8.decoder import linear_bf16_device
+    rng = np.random.default_rng(1)
+    for n, k, rows in ((64, 1280, 64), (7, 33, 3), (130, 256, 1)):
+        # bf16 bit patterns of N(0, 1) * 2^[-20, 20] weights (tail bits kept)
+        wf = (rng.standard_normal((n, k)) * 2.0 ** rng.integers(-20, 21, (n, k))).astype(np.float32)
+        w = (wf.view(np.uint32) >> 16).astype(np.uint16)
+        x = rng.standard_normal((rows, k)).astype(np.float32)
+        y = host(linear_bf16_device(ctx, dev(w.view(np.int16)), dev(x)))
+        ctx.sync()
+        assert bits_equal(y, oracle.linear_bf16(w, x)), (n, k, rows)
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+@pytest.mark.parametrize("rows", [1, 5, 40])
+def test_feed_forward_matches_oracle(ctx, mode, rows):
+    import uocr_q8
+    from uocr_q8.decoder import feed_forward_device
+    rng = np.random.default_rng(10 * mode + rows)
+    H, F = 256, 384
+    g, u, d = (oracle.Matrix(*random_q8(rng, *shape)) for shape in ((F, H), (F, H), (H, F)))
+    dm = [uocr_q8.Int8Matrix.from_parts(m.rows, m.cols, m.w, m.s, ctx) for m in (g, u, d)]
+    x = rng.standard_normal((rows, H)).astype(np.float32)
+    y = host(feed_forward_device(ctx, *dm, dev(x), mode))
+    ctx.sync()
+    ref = oracle.feed_forward(oracle.Ffn(g, u, d), x, mode)
+    if mode == 2 or (mode == 1 and rows == 1):
+        # int8 projections are bit-exact; silu's exp may differ by an ulp
+        assert float(np.mean(y.view(np.uint32) == ref.view(np.uint32))) >= 0.99
+        assert np.max(np.abs(y - ref)) <= 1e-3 * float(np.max(np.abs(ref)))
+    else:
+        assert np.max(np.abs(y.astype(np.float64) - ref)) <= 1e-4 * float(np.max(np.abs(ref)))
+
+
+def small_config():
+    from uocr_q8.decoder import DecoderConfig
+    return DecoderConfig(hidden=256, heads=2, layers=2, first_dense=1, experts=8, top_k=2,
+                         expert_width=128, shared_width=256, dense_width=384, vocab=384, window=4)
+
+
+def host_decoder(dec):
+    """The device weights as oracle objects."""
+    import torch
+
+    def m(x):
+        w, s = x.download()
+        return oracle.Matrix(w, s)
+
+    layers = []
+    for L in dec.layers:
+        d = {"in": host(L.input_norm), "post": host(L.post_norm),
+             "q": m(L.q), "k": m(L.k), "v": m(L.v), "o": m(L.o)}
+        if L.moe is not None:
+            shared, experts = L.moe._keep
+            d["shared"] = oracle.Ffn(*[m(x) for x in shared])
+            d["experts"] = [oracle.Ffn(*[m(x) for x in e]) for e in experts]
+            d["router"] = host(L.router.view(torch.int16)).view(np.uint16)
+        else:
+            d["dense"] = oracle.Ffn(*[m(x) for x in L.dense])
+        layers.append(d)
+    emb = (host(dec.embedding.view(torch.int16)).view(np.uint16).astype(np.uint32) << 16).view(
+        np.float32)
+    return layers, emb, host(dec.final_norm), m(dec.lm_head)
+
+
+def oracle_step(cfg, layers, emb, final_norm, head, caches, token, mode):
+    """Decoder::step for one sequence with the oracle's operations."""
+    int8 = mode != 0
+    proj = (lambda mat, v: oracle.linear_dynamic_int8(mat, v)) if int8 else \
+        (lambda mat, v: oracle.linear(mat, v))
+    x = emb[token][None]
+    for L, c in zip(layers, caches):
+        n = oracle.rms_norm(x, L["in"], cfg.eps)
+        q, k, v = (proj(L[key], n)[0] for key in ("q", "k", "v"))
+        pos = c.position()
+        q, k = oracle.rope(q, cfg.head_dim, pos, cfg.theta), oracle.rope(k, cfg.head_dim, pos, cfg.theta)
+        c.push(k, v)
+        a = oracle.attention_decode(q, c.keys, c.values, cfg.heads)
+        r = proj(L["o"], a[None])[0] + x[0]
+        n2 = oracle.rms_norm(r[None], L["post"], cfg.eps)
+        if "dense" in L:
+            y = oracle.feed_forward(L["dense"], n2, 1 if int8 else 0)
+        else:
+            logits = oracle.linear_bf16(L["router"], n2)
+            y, _, _ = oracle.experts(L["shared"], L["experts"], logits, n2, cfg.top_k, 1 if int8 else 0)
+        x = (r + y[0])[None]
+    h = oracle.rms_norm(x, final_norm, cfg.eps)
+    return proj(head, h)[0]
+
+
+@pytest.mark.parametrize("mode", [0, 2])
+def test_decode_step_matches_oracle(ctx, mode):
+    import torch
+    from uocr_q8.decoder import DecodeState, Decoder, decode_step
+    cfg = small_config()
+    dec = Decoder.random(ctx, cfg, seed=5 + mode)
+    layers, emb, final_norm, head = host_decoder(dec)
+    batch, prefix = 3, 6
+    state = DecodeState(dec, batch, prefix)
+    rng = np.random.default_rng(7)
+    caches = []
+    for b in range(batch):
+        seq = []
+        for li, cache in enumerate(state.caches):
+            k = rng.standard_normal((prefix - b, cfg.hidden)).astype(np.float32)
+            v = rng.standard_normal((prefix - b, cfg.hidden)).astype(np.float32)
+            cache.prefill(b, dev(k), dev(v))
+            c = oracle.LayerCache(cfg.heads, cfg.head_dim, cfg.window)
+            c.prefill(k, v, prefix - b)
+            seq.append(c)
+        caches.append(seq)
+    for step in range(6):  # the 4-token ring wraps
+        tokens = rng.integers(0, cfg.vocab, batch)
+        logits = host(decode_step(dec, state, dev(tokens.astype(np.int64)), mode))
+        ctx.sync()
+        for b in range(batch):
+            ref = oracle_step(cfg, layers, emb, final_norm, head, caches[b], int(tokens[b]), mode)
+            scale = float(np.max(np.abs(ref)))
+            err = float(np.max(np.abs(logits[b].astype(np.float64) - ref)))
+            assert err <= (1e-3 if mode == 0 else 1e-2) * scale, (step, b, err, scale)
+            assert int(np.argmax(logits[b])) == int(np.argmax(ref)) or \
+                np.sort(ref)[-1] - np.sort(ref)[-2] < 2 * err
+    for b in range(batch):
+        assert state.caches[0].state(b) == (caches[b][0].tokens(), caches[b][0].position())
+    state.free()

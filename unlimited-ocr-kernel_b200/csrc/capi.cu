@@ -1271,6 +1271,27 @@ int uocr_feed_forward(uocr_ctx* ctx, const uocr_q8* gate, const uocr_q8* up, con
   return linear_launch(ctx, down, lm, gd, rows, y_dev, scratch);
 }
 
+// ops::linear_weight, BF16 branch (src/cpu/ops.rs:62-133): y [batch x n] =
+// x [batch x k] times the BF16 weight [n x k] (device bit patterns), each
+// output a left-to-right sum; the router logits of Decoder::experts
+// (projection of "mlp.gate.weight", src/decoder/mod.rs:126-130).
+int uocr_linear_bf16(uocr_ctx* ctx, const uint16_t* w_dev, size_t n, size_t k, const float* x_dev,
+                     size_t batch, float* y_dev) {
+  if (!ctx) return fail(UOCR_ERR_INVALID, "null context");
+  if (n == 0 || k == 0) return fail(UOCR_ERR_SHAPE, "invalid tensor shape: linear weight");
+  if (batch == 0) return ok();
+  if (!w_dev || !x_dev || !y_dev) return fail(UOCR_ERR_INVALID, "null argument");
+  if (!fits_int(n) || !fits_int(batch) || k > 50000)
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: BF16 linear extent");
+  int st = check_elements(ctx, batch * n);
+  if (st) return st;
+  DeviceGuard g(ctx->device);
+  cudaError_t e = launch_linear_bf16(w_dev, static_cast<int>(n), static_cast<int>(k), x_dev,
+                                     static_cast<int>(batch), y_dev, ctx->stream);
+  if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "BF16 linear: %s", cudaGetErrorString(e));
+  return ok();
+}
+
 // ---- decoder attention at decode --------------------------------------------
 // ops::rms_norm (src/cpu/ops.rs:362-414, 419-421)
 int uocr_rms_norm(uocr_ctx* ctx, const float* x_dev, size_t rows, size_t width,

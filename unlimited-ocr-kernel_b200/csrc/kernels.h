@@ -81,6 +81,10 @@ void launch_swiglu_split(const float* g, const float* u, int rows, int cols, uin
 // xq_p[p] = xq[src[p]], xs_p[p] = xs[src[p]]
 void launch_gather_rows(const int8_t* xq, const float* xs, const int* src, int rows, int cols,
                         int8_t* xq_p, float* xs_p, int sms, cudaStream_t st);
+// BF16 weights [n][k] (bit patterns) times `batch` float rows of k: the
+// reference's sequential BF16 linear (router logits).
+cudaError_t launch_linear_bf16(const uint16_t* w, int n, int k, const float* x, int batch, float* y,
+                               cudaStream_t st);
 // h = silu(g) * u elementwise (n floats; h may alias g)
 void launch_swiglu(const float* g, const float* u, long long n, float* h, int sms, cudaStream_t st);
 // hq/hs = block-quantized silu(g) * u

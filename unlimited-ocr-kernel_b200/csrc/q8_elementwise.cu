@@ -154,3 +154,54 @@ void launch_swiglu(const float* g, const float* u, long long n, float* h, int sm
 }
 
 }  // namespace uocr
+
+namespace uocr {
+
+// ops::linear_weight, BF16 branch (src/cpu/ops.rs:62-133) as the router uses
+// it: y[b][r] = sum over c of bf16(w[r][c]) * x[b][c], left to right from
+// -0.0, one rounding per operation.  One thread per (b, r); the CTA's rows
+// of x are staged in shared memory.  Meant for small n (the router's 64
+// outputs): every thread streams its own weight row.
+constexpr int kBf16Threads = 128;
+
+__global__ void __launch_bounds__(kBf16Threads)
+    linear_bf16_kernel(const uint16_t* __restrict__ w, int n, int k, const float* __restrict__ x,
+                       int batch, float* y) {
+  extern __shared__ float xs[];  // k floats: row b of x
+  const int b = blockIdx.y;
+  for (int c = threadIdx.x; c < k; c += blockDim.x) xs[c] = x[static_cast<long long>(b) * k + c];
+  __syncthreads();
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  const uint16_t* wr = w + static_cast<long long>(r) * k;
+  float acc = -0.0f;
+  int c = 0;
+  for (; c + 8 <= k; c += 8) {
+    float wv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) wv[j] = __uint_as_float(static_cast<uint32_t>(__ldg(wr + c + j)) << 16);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, __fmul_rn(wv[j], xs[c + j]));
+  }
+  for (; c < k; ++c) acc = __fadd_rn(acc, __fmul_rn(__uint_as_float(static_cast<uint32_t>(wr[c]) << 16), xs[c]));
+  y[static_cast<long long>(b) * n + r] = acc;
+}
+
+cudaError_t launch_linear_bf16(const uint16_t* w, int n, int k, const float* x, int batch, float* y,
+                               cudaStream_t st) {
+  if (n <= 0 || batch <= 0) return cudaSuccess;
+  const size_t smem = static_cast<size_t>(k) * 4;
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  static unsigned configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured & (1u << (dev & 31)))) {
+    cudaFuncSetAttribute(linear_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    configured |= 1u << (dev & 31);
+  }
+  linear_bf16_kernel<<<dim3((n + kBf16Threads - 1) / kBf16Threads, batch), kBf16Threads, smem, st>>>(
+      w, n, k, x, batch, y);
+  return cudaGetLastError();
+}
+
+}  // namespace uocr

@@ -61,6 +61,7 @@ SIGNATURES = {
     "uocr_moe_dispatch": (I, [P, P, S, S, P, S, P, S, S, P, P, P]),
     "uocr_moe_combine_rows": (I, [P, P, P, P, P, S, S, S, P]),
     "uocr_feed_forward": (I, [P, P, P, P, I, P, S, P]),
+    "uocr_linear_bf16": (I, [P, P, S, S, P, S, P]),
     "uocr_rms_norm": (I, [P, P, S, S, P, F, P]),
     "uocr_rope_create": (I, [P, S, F, S, PP]),
     "uocr_rope_free": (I, [P]),

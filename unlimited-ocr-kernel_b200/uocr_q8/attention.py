@@ -147,8 +147,10 @@ class AttentionBlock:
         self.cache, self.rope_table, self.eps = cache, rope, eps
 
     def forward_device(self, x_t, mode: int = QuantizationMode.WEIGHTS_ONLY, out_t=None):
+        """Rows of x_t are independent sequences (one token each), so both
+        int8 modes quantize every row's activations, as one-row calls would."""
         import torch
-        dyn = mode == QuantizationMode.DYNAMIC_ACTIVATIONS
+        dyn = mode in (QuantizationMode.DYNAMIC_ACTIVATIONS, QuantizationMode.DYNAMIC_ROWWISE)
         n = rms_norm_device(self.ctx, x_t, self.norm, self.eps)
         q = self.q.linear_device(n, dynamic=dyn)
         k = self.k.linear_device(n, dynamic=dyn)
