@@ -56,9 +56,11 @@ def test_feed_forward_matches_oracle(ctx, mode, rows):
 
 
 def small_config():
+    """Two layers: a dense FFN of width 352 (padded to 384 on the device) and
+    an MoE layer of 8 experts."""
     from uocr_q8.decoder import DecoderConfig
     return DecoderConfig(hidden=256, heads=2, layers=2, first_dense=1, experts=8, top_k=2,
-                         expert_width=128, shared_width=256, dense_width=384, vocab=384, window=4)
+                         expert_width=128, shared_width=256, dense_width=352, vocab=384, window=4)
 
 
 def host_decoder(dec):
@@ -71,15 +73,23 @@ def host_decoder(dec):
 
     layers = []
     for L in dec.layers:
-        d = {"in": host(L.input_norm), "post": host(L.post_norm),
-             "q": m(L.q), "k": m(L.k), "v": m(L.v), "o": m(L.o)}
+        w, s = L.qkv.download()
+        H = w.shape[1]
+        d = {"in": host(L.input_norm), "post": host(L.post_norm), "o": m(L.o)}
+        for i, key in enumerate(("q", "k", "v")):
+            d[key] = oracle.Matrix(w[i * H:(i + 1) * H].copy(), s[i * H:(i + 1) * H].copy())
         if L.moe is not None:
             shared, experts = L.moe._keep
             d["shared"] = oracle.Ffn(*[m(x) for x in shared])
             d["experts"] = [oracle.Ffn(*[m(x) for x in e]) for e in experts]
             d["router"] = host(L.router.view(torch.int16)).view(np.uint16)
         else:
-            d["dense"] = oracle.Ffn(*[m(x) for x in L.dense])
+            # the unpadded FFN (the device one is zero-padded to a multiple of 128)
+            F = L.dense_width
+            (gw, gs), (uw, us), (dw, ds) = (x.download() for x in L.dense)
+            d["dense"] = oracle.Ffn(oracle.Matrix(gw[:F].copy(), gs[:F].copy()),
+                                    oracle.Matrix(uw[:F].copy(), us[:F].copy()),
+                                    oracle.Matrix(dw[:, :F].copy(), ds[:, :F // 32].copy()))
         layers.append(d)
     emb = (host(dec.embedding.view(torch.int16)).view(np.uint16).astype(np.uint32) << 16).view(
         np.float32)

@@ -478,9 +478,13 @@ static LinearPath linear_path(const uocr_q8* m, int mode, size_t batch) {
                        reinterpret_cast<uintptr_t>(m->s) % 16 == 0;
   const int rows = static_cast<int>(m->rows), cols = static_cast<int>(m->cols);
   if (batch < 2 || !aligned) return LinearPath::Gemv;
-  if (batch <= static_cast<size_t>(kSmallRowsMax)) {
-    if (!small_rows_supported(rows, cols)) return LinearPath::Gemv;
-    return mode == MODE_INT8 ? LinearPath::SmallInt8 : LinearPath::SmallFp32;
+  // up to 16 rows, or up to 64 rows of a matrix small enough that its
+  // re-reads by the 16-row groups come from L2: the warp-level kernel
+  const bool small_matrix = static_cast<size_t>(rows) * cols <= (size_t(16) << 20);
+  if (batch <= static_cast<size_t>(kSmallRowsMax) || (batch <= 64 && small_matrix)) {
+    if (small_rows_supported(rows, cols))
+      return mode == MODE_INT8 ? LinearPath::SmallInt8 : LinearPath::SmallFp32;
+    if (batch <= static_cast<size_t>(kSmallRowsMax)) return LinearPath::Gemv;
   }
   if (!q8_tc_supported(rows, cols)) return LinearPath::Gemv;
   return mode == MODE_INT8 ? LinearPath::TcInt8 : LinearPath::TcFp32;
@@ -1281,7 +1285,7 @@ int uocr_linear_bf16(uocr_ctx* ctx, const uint16_t* w_dev, size_t n, size_t k, c
   if (n == 0 || k == 0) return fail(UOCR_ERR_SHAPE, "invalid tensor shape: linear weight");
   if (batch == 0) return ok();
   if (!w_dev || !x_dev || !y_dev) return fail(UOCR_ERR_INVALID, "null argument");
-  if (!fits_int(n) || !fits_int(batch) || k > 50000)
+  if (!fits_int(n) || !fits_int(batch) || k > 12000)
     return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: BF16 linear extent");
   int st = check_elements(ctx, batch * n);
   if (st) return st;

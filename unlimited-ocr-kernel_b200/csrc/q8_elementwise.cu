@@ -159,38 +159,41 @@ namespace uocr {
 
 // ops::linear_weight, BF16 branch (src/cpu/ops.rs:62-133) as the router uses
 // it: y[b][r] = sum over c of bf16(w[r][c]) * x[b][c], left to right from
-// -0.0, one rounding per operation.  One thread per (b, r); the CTA's rows
-// of x are staged in shared memory.  Meant for small n (the router's 64
-// outputs): every thread streams its own weight row.
-constexpr int kBf16Threads = 128;
+// -0.0, one rounding per operation.  A thread owns output r for kBf16Rows
+// rows of x (independent chains sharing each weight it loads); the CTA's
+// rows of x are staged in shared memory.  Meant for small n (the router's
+// 64 outputs).
+constexpr int kBf16Threads = 64;
+constexpr int kBf16Rows = 4;
 
 __global__ void __launch_bounds__(kBf16Threads)
     linear_bf16_kernel(const uint16_t* __restrict__ w, int n, int k, const float* __restrict__ x,
                        int batch, float* y) {
-  extern __shared__ float xs[];  // k floats: row b of x
-  const int b = blockIdx.y;
-  for (int c = threadIdx.x; c < k; c += blockDim.x) xs[c] = x[static_cast<long long>(b) * k + c];
+  extern __shared__ float xs[];  // [kBf16Rows][k]
+  const int b0 = blockIdx.y * kBf16Rows;
+  const int nb = batch - b0 < kBf16Rows ? batch - b0 : kBf16Rows;
+  for (int i = threadIdx.x; i < nb * k; i += blockDim.x)
+    xs[i] = x[static_cast<long long>(b0) * k + i];
   __syncthreads();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= n) return;
   const uint16_t* wr = w + static_cast<long long>(r) * k;
-  float acc = -0.0f;
-  int c = 0;
-  for (; c + 8 <= k; c += 8) {
-    float wv[8];
+  float acc[kBf16Rows];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) wv[j] = __uint_as_float(static_cast<uint32_t>(__ldg(wr + c + j)) << 16);
+  for (int j = 0; j < kBf16Rows; ++j) acc[j] = -0.0f;
+  for (int c = 0; c < k; ++c) {
+    const float wv = __uint_as_float(static_cast<uint32_t>(__ldg(wr + c)) << 16);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, __fmul_rn(wv[j], xs[c + j]));
+    for (int j = 0; j < kBf16Rows; ++j)
+      if (j < nb) acc[j] = __fadd_rn(acc[j], __fmul_rn(wv, xs[j * k + c]));
   }
-  for (; c < k; ++c) acc = __fadd_rn(acc, __fmul_rn(__uint_as_float(static_cast<uint32_t>(wr[c]) << 16), xs[c]));
-  y[static_cast<long long>(b) * n + r] = acc;
+  for (int j = 0; j < nb; ++j) y[static_cast<long long>(b0 + j) * n + r] = acc[j];
 }
 
 cudaError_t launch_linear_bf16(const uint16_t* w, int n, int k, const float* x, int batch, float* y,
                                cudaStream_t st) {
   if (n <= 0 || batch <= 0) return cudaSuccess;
-  const size_t smem = static_cast<size_t>(k) * 4;
+  const size_t smem = static_cast<size_t>(k) * 4 * kBf16Rows;
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
   static unsigned configured = 0;
   int dev = 0;
@@ -199,8 +202,9 @@ cudaError_t launch_linear_bf16(const uint16_t* w, int n, int k, const float* x, 
     cudaFuncSetAttribute(linear_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     configured |= 1u << (dev & 31);
   }
-  linear_bf16_kernel<<<dim3((n + kBf16Threads - 1) / kBf16Threads, batch), kBf16Threads, smem, st>>>(
-      w, n, k, x, batch, y);
+  linear_bf16_kernel<<<dim3((n + kBf16Threads - 1) / kBf16Threads,
+                            (batch + kBf16Rows - 1) / kBf16Rows),
+                       kBf16Threads, smem, st>>>(w, n, k, x, batch, y);
   return cudaGetLastError();
 }
 

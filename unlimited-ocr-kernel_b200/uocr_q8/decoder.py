@@ -27,7 +27,7 @@ from dataclasses import dataclass
 from typing import List, Optional
 
 from . import (GpuContext, Int8Matrix, MoeLayer, QuantizationMode, _check, _tptr, lib)
-from .attention import AttentionBlock, KvCache, Rope, rms_norm_device
+from .attention import KvCache, Rope, rms_norm_device
 
 
 @dataclass
@@ -83,13 +83,20 @@ def feed_forward_device(ctx: GpuContext, gate: Int8Matrix, up: Int8Matrix, down:
 
 
 class DecoderLayer:
-    """Weights of one decoder layer on the device."""
+    """Weights of one decoder layer on the device.  ``qkv`` is the q, k and v
+    projections stacked into one [3*hidden x hidden] matrix (one launch for
+    the three; each output row is the same dot as in its own matrix).
+    ``dense`` holds the dense FFN with its width zero-padded to a multiple of
+    128 (zero weights and scales in the extra rows of gate/up and columns of
+    down, which leaves every output unchanged); ``dense_width`` is the
+    unpadded width."""
 
-    def __init__(self, input_norm_t, q, k, v, o, post_norm_t, dense=None, router_t=None,
-                 moe: Optional[MoeLayer] = None):
-        self.input_norm, self.q, self.k, self.v, self.o = input_norm_t, q, k, v, o
+    def __init__(self, input_norm_t, qkv: Int8Matrix, o: Int8Matrix, post_norm_t, dense=None,
+                 dense_width: int = 0, router_t=None, moe: Optional[MoeLayer] = None):
+        self.input_norm, self.qkv, self.o = input_norm_t, qkv, o
         self.post_norm = post_norm_t
         self.dense = dense      # (gate, up, down) Int8Matrix
+        self.dense_width = dense_width
         self.router = router_t  # BF16 [experts x hidden]
         self.moe = moe
 
@@ -124,12 +131,31 @@ class Decoder:
         def norm():
             return (torch.rand(H, device=dev, generator=g) * 0.5 + 0.75).contiguous()
 
+        def padded_ffn(F):
+            # rows F.. of gate/up and columns F.. of down are zero (weights and
+            # scales): the padded FFN computes exactly the unpadded one
+            Fp = (F + 127) // 128 * 128
+            gw = torch.zeros((Fp, H), dtype=torch.int8, device=dev)
+            uw = torch.zeros((Fp, H), dtype=torch.int8, device=dev)
+            gs = torch.zeros((Fp, H // 32), device=dev)
+            us = torch.zeros((Fp, H // 32), device=dev)
+            dw = torch.zeros((H, Fp), dtype=torch.int8, device=dev)
+            ds = torch.zeros((H, Fp // 32), device=dev)
+            for w_, s_ in ((gw, gs), (uw, us)):
+                w_[:F] = torch.randint(-127, 128, (F, H), dtype=torch.int8, device=dev, generator=g)
+                s_[:F] = torch.rand((F, H // 32), device=dev, generator=g) * (1e-2 - 1e-4) + 1e-4
+            dw[:, :F] = torch.randint(-127, 128, (H, F), dtype=torch.int8, device=dev, generator=g)
+            ds[:, :F // 32] = torch.rand((H, F // 32), device=dev, generator=g) * (1e-2 - 1e-4) + 1e-4
+            return (Int8Matrix.from_device(Fp, H, gw, gs, ctx),
+                    Int8Matrix.from_device(Fp, H, uw, us, ctx),
+                    Int8Matrix.from_device(H, Fp, dw, ds, ctx))
+
         layers = []
         for i in range(cfg.layers):
-            att = [mat(H, H, 1e-4, 1e-3) for _ in range(4)]
+            qkv, o = mat(3 * H, H, 1e-4, 1e-3), mat(H, H, 1e-4, 1e-3)
             if i < cfg.first_dense:
-                dense = (mat(cfg.dense_width, H), mat(cfg.dense_width, H), mat(H, cfg.dense_width))
-                layers.append(DecoderLayer(norm(), *att, norm(), dense=dense))
+                layers.append(DecoderLayer(norm(), qkv, o, norm(), dense=padded_ffn(cfg.dense_width),
+                                           dense_width=cfg.dense_width))
             else:
                 shared = [mat(cfg.shared_width, H), mat(cfg.shared_width, H),
                           mat(H, cfg.shared_width)]
@@ -138,7 +164,7 @@ class Decoder:
                 moe = MoeLayer(ctx, shared, experts, cfg.top_k, cfg.normalize, cfg.routed_scale)
                 router = (torch.randn((cfg.experts, H), device=dev, generator=g) * 0.03).to(
                     torch.bfloat16)
-                layers.append(DecoderLayer(norm(), *att, norm(), router_t=router, moe=moe))
+                layers.append(DecoderLayer(norm(), qkv, o, norm(), router_t=router, moe=moe))
         emb = torch.randn((cfg.vocab, H), device=dev, generator=g).to(torch.bfloat16)
         if lm_head == "q8":
             head = mat(cfg.vocab, H, 1e-4, 1e-3)
@@ -171,11 +197,18 @@ def decode_step(decoder: Decoder, state: DecodeState, tokens_t, mode: int = 0, l
     ctx, cfg = decoder.ctx, decoder.cfg
     rowwise = mode in (QuantizationMode.DYNAMIC_ACTIVATIONS, QuantizationMode.DYNAMIC_ROWWISE)
     lin_mode = QuantizationMode.DYNAMIC_ROWWISE if rowwise else QuantizationMode.WEIGHTS_ONLY
+    H = cfg.hidden
     x = decoder.embedding.index_select(0, tokens_t).float()
     for layer, cache in zip(decoder.layers, state.caches):
-        block = AttentionBlock(ctx, layer.input_norm, layer.q, layer.k, layer.v, layer.o, cache,
-                               state.rope, cfg.eps)
-        r = block.forward_device(x, lin_mode)
+        # attention half of Decoder::layer (src/decoder/mod.rs:266-347)
+        n = rms_norm_device(ctx, x, layer.input_norm, cfg.eps)
+        qkv = layer.qkv.linear_device(n, dynamic=rowwise)
+        q, k, v = (qkv[:, i * H:(i + 1) * H].contiguous() for i in range(3))
+        cache.rope(state.rope, q, k)
+        cache.push(k, v)
+        a = cache.attention(q)
+        r = layer.o.linear_device(a, dynamic=rowwise)
+        r += x
         n = rms_norm_device(ctx, r, layer.post_norm, cfg.eps)
         if layer.moe is not None:
             logits = linear_bf16_device(ctx, layer.router, n)
