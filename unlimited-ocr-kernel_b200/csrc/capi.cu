@@ -1285,13 +1285,13 @@ int uocr_linear_bf16(uocr_ctx* ctx, const uint16_t* w_dev, size_t n, size_t k, c
   if (n == 0 || k == 0) return fail(UOCR_ERR_SHAPE, "invalid tensor shape: linear weight");
   if (batch == 0) return ok();
   if (!w_dev || !x_dev || !y_dev) return fail(UOCR_ERR_INVALID, "null argument");
-  if (!fits_int(n) || !fits_int(batch) || k > 12000)
+  if (!fits_int(n) || !fits_int(batch) || k > 2400)
     return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: BF16 linear extent");
   int st = check_elements(ctx, batch * n);
   if (st) return st;
   DeviceGuard g(ctx->device);
   cudaError_t e = launch_linear_bf16(w_dev, static_cast<int>(n), static_cast<int>(k), x_dev,
-                                     static_cast<int>(batch), y_dev, ctx->stream);
+                                     static_cast<int>(batch), y_dev, ctx->status_dev, ctx->stream);
   if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "BF16 linear: %s", cudaGetErrorString(e));
   return ok();
 }

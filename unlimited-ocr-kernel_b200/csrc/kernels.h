@@ -84,7 +84,7 @@ void launch_gather_rows(const int8_t* xq, const float* xs, const int* src, int r
 // BF16 weights [n][k] (bit patterns) times `batch` float rows of k: the
 // reference's sequential BF16 linear (router logits).
 cudaError_t launch_linear_bf16(const uint16_t* w, int n, int k, const float* x, int batch, float* y,
-                               cudaStream_t st);
+                               unsigned* status, cudaStream_t st);
 // h = silu(g) * u elementwise (n floats; h may alias g)
 void launch_swiglu(const float* g, const float* u, long long n, float* h, int sms, cudaStream_t st);
 // hq/hs = block-quantized silu(g) * u
@@ -92,13 +92,16 @@ void launch_swiglu_quantize(const float* g, const float* u, int rows, int cols, 
                             float* hs, unsigned* status, int sms, cudaStream_t st);
 
 // q8_small.cu — grouped projections for groups of lo..hi rows (hi <=
-// kSmallRowsMax), weights streamed once per group (TMA ring), warp-level MMAs
-// over the group's rows.  int8: xq/xs rows (bit-exact linear_dynamic_int8);
+// kSmallChunkedMax; a group of more than 16 rows runs as 16-row chunks),
+// weights streamed once per chunk (TMA ring), warp-level MMAs over the rows.  int8: xq/xs rows (bit-exact linear_dynamic_int8);
 // FP32: pieces [3][piece_rows][K] + rinv (FP32 tolerance).  Grouped: maps =
 // the groups' q8_tc_weight_maps, rows [offsets[g], + counts[g]); single
 // (counts null): *single over rows [0, total_rows) in groups of 16.  x_rows:
 // rows of the int8 activation tensors.  N % 128 == 0, K % 128 == 0.
 constexpr int kSmallRowsMax = 16;
+// Grouped launches may take groups of up to this many rows, as 16-row chunks
+// (one CTA each, the group's weights re-read from L2).
+constexpr int kSmallChunkedMax = 64;
 bool small_rows_supported(int N, int K);
 cudaError_t launch_small_rows(bool int8, const void* maps, const Q8View* single, const int* counts,
                               const int* offsets, int groups, int lo, int hi, int total_rows, int N,

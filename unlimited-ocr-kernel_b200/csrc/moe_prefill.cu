@@ -641,25 +641,30 @@ static cudaError_t prefill_tc_f32(const MoePrefillArgs& a, const PrefillWs& w, i
   const unsigned char* maps = static_cast<const unsigned char*>(a.tc_maps);
   const size_t mb = q8_tc_maps_bytes();
   cudaError_t e;
-  const int R = kSmallRowsMax;
+  // no group exceeds T rows: up to kSmallChunkedMax tokens every group runs on
+  // the warp-level kernel and the tensor-core launches are skipped
+  const bool tc = T > kSmallChunkedMax;
+  const int R = tc ? kSmallRowsMax : (T > 1 ? T : 1);
   if (!a.skip_routed) {
-    launch_big_counts(w.counts, E, w.counts_big, st);
+    if (tc) launch_big_counts(w.counts, E, w.counts_big, st);
     launch_split_rows(a.x, H, w.pair_token, P, H, w.xp_r, w.xr_r, sms, st);
     for (int j = 0; j < 2; ++j) {  // gate, up
       float* out = j == 0 ? w.h_r : w.u_r;
       if ((e = launch_small_rows(false, maps + j * E * mb, nullptr, w.counts, w.offsets, E, 1, R, 0, F,
                                  H, w.xp_r, P, w.xr_r, nullptr, nullptr, P, out, F,
                                  a.status, st)) ||
-          (e = launch_q8_tc_grouped_f32(maps + j * E * mb, E, w.counts_big, w.offsets, max_tiles,
-                                        F, H, w.xp_r, w.xr_r, P, out, F, a.status, st)))
+          (tc && (e = launch_q8_tc_grouped_f32(maps + j * E * mb, E, w.counts_big, w.offsets,
+                                               max_tiles, F, H, w.xp_r, w.xr_r, P, out, F,
+                                               a.status, st))))
         return e;
     }
     launch_swiglu_split(w.h_r, w.u_r, P, F, w.hp_r, w.hr_r, sms, st);
     if ((e = launch_small_rows(false, maps + 2 * E * mb, nullptr, w.counts, w.offsets, E, 1, R, 0, H,
                                  F, w.hp_r, P, w.hr_r, nullptr, nullptr, P, w.out_r, H,
                                  a.status, st)) ||
-        (e = launch_q8_tc_grouped_f32(maps + 2 * E * mb, E, w.counts_big, w.offsets, max_tiles, H,
-                                      F, w.hp_r, w.hr_r, P, w.out_r, H, a.status, st)))
+        (tc && (e = launch_q8_tc_grouped_f32(maps + 2 * E * mb, E, w.counts_big, w.offsets,
+                                             max_tiles, H, F, w.hp_r, w.hr_r, P, w.out_r, H,
+                                             a.status, st))))
       return e;
   }
   if (a.skip_shared) return cudaSuccess;
@@ -680,27 +685,30 @@ static cudaError_t prefill_tc(const MoePrefillArgs& a, const PrefillWs& w, int s
   const unsigned char* maps = static_cast<const unsigned char*>(a.tc_maps);
   const size_t mb = q8_tc_maps_bytes();  // per matrix
   cudaError_t e;
-  const int R = kSmallRowsMax;
+  const bool tc = T > kSmallChunkedMax;
+  const int R = tc ? kSmallRowsMax : (T > 1 ? T : 1);
   if (!a.skip_routed) {
     // routed experts: rows gathered per expert; groups of <= R rows on the
     // warp-level kernel, larger ones on the tensor-core GEMM
-    launch_big_counts(w.counts, E, w.counts_big, st);
+    if (tc) launch_big_counts(w.counts, E, w.counts_big, st);
     launch_gather_rows(w.xq, w.xs, w.pair_token, P, H, w.xq_p, w.xs_p, sms, st);
     for (int j = 0; j < 2; ++j) {  // gate, up
       float* out = j == 0 ? w.h_r : w.u_r;
       if ((e = launch_small_rows(true, maps + j * E * mb, nullptr, w.counts, w.offsets, E, 1, R, 0, F,
                                  H, nullptr, 0, nullptr, w.xq_p, w.xs_p, P, out, F,
                                  a.status, st)) ||
-          (e = launch_q8_tc_grouped_i8(maps + j * E * mb, E, w.counts_big, w.offsets, max_tiles,
-                                       F, H, w.xq_p, w.xs_p, P, out, F, a.status, st)))
+          (tc && (e = launch_q8_tc_grouped_i8(maps + j * E * mb, E, w.counts_big, w.offsets,
+                                              max_tiles, F, H, w.xq_p, w.xs_p, P, out, F,
+                                              a.status, st))))
         return e;
     }
     launch_swiglu_quantize(w.h_r, w.u_r, P, F, w.hq_r, w.hs_r, a.status, sms, st);
     if ((e = launch_small_rows(true, maps + 2 * E * mb, nullptr, w.counts, w.offsets, E, 1, R, 0, H,
                                  F, nullptr, 0, nullptr, w.hq_r, w.hs_r, P, w.out_r, H,
                                  a.status, st)) ||
-        (e = launch_q8_tc_grouped_i8(maps + 2 * E * mb, E, w.counts_big, w.offsets, max_tiles, H,
-                                     F, w.hq_r, w.hs_r, P, w.out_r, H, a.status, st)))
+        (tc && (e = launch_q8_tc_grouped_i8(maps + 2 * E * mb, E, w.counts_big, w.offsets,
+                                            max_tiles, H, F, w.hq_r, w.hs_r, P, w.out_r, H,
+                                            a.status, st))))
       return e;
   }
   if (a.skip_shared) return cudaSuccess;
@@ -738,10 +746,11 @@ static cudaError_t prefill_tc_mixed(const MoePrefillArgs& a, const PrefillWs& w,
   const int max_tiles = P / 64 + E + 1;
   const unsigned char* maps = static_cast<const unsigned char*>(a.tc_maps);
   const size_t mb = q8_tc_maps_bytes();
-  const int R = kSmallRowsMax;
+  const bool tc = T > kSmallChunkedMax;
+  const int R = tc ? kSmallRowsMax : (T > 2 ? T : 2);
   cudaError_t e;
   if (!a.skip_routed) {
-    launch_big_counts(w.counts, E, w.counts_big, st);
+    if (tc) launch_big_counts(w.counts, E, w.counts_big, st);
     launch_gather_rows(w.xq, w.xs, w.pair_token, P, H, w.xq_p, w.xs_p, sms, st);
     launch_split_rows(a.x, H, w.pair_token, P, H, w.xp_r, w.xr_r, sms, st);
     for (int j = 0; j < 2; ++j) {  // gate, up
@@ -752,8 +761,9 @@ static cudaError_t prefill_tc_mixed(const MoePrefillArgs& a, const PrefillWs& w,
           (e = launch_small_rows(false, maps + j * E * mb, nullptr, w.counts, w.offsets, E, 2, R, 0, F,
                                  H, w.xp_r, P, w.xr_r, nullptr, nullptr, P, out, F,
                                  a.status, st)) ||
-          (e = launch_q8_tc_grouped_f32(maps + j * E * mb, E, w.counts_big, w.offsets, max_tiles,
-                                        F, H, w.xp_r, w.xr_r, P, out, F, a.status, st)))
+          (tc && (e = launch_q8_tc_grouped_f32(maps + j * E * mb, E, w.counts_big, w.offsets,
+                                               max_tiles, F, H, w.xp_r, w.xr_r, P, out, F,
+                                               a.status, st))))
         return e;
     }
     launch_swiglu_quantize(w.h_r, w.u_r, P, F, w.hq_r, w.hs_r, a.status, sms, st);
@@ -764,8 +774,9 @@ static cudaError_t prefill_tc_mixed(const MoePrefillArgs& a, const PrefillWs& w,
         (e = launch_small_rows(false, maps + 2 * E * mb, nullptr, w.counts, w.offsets, E, 2, R, 0, H,
                                  F, w.hp_r, P, w.hr_r, nullptr, nullptr, P, w.out_r, H,
                                  a.status, st)) ||
-        (e = launch_q8_tc_grouped_f32(maps + 2 * E * mb, E, w.counts_big, w.offsets, max_tiles, H,
-                                      F, w.hp_r, w.hr_r, P, w.out_r, H, a.status, st)))
+        (tc && (e = launch_q8_tc_grouped_f32(maps + 2 * E * mb, E, w.counts_big, w.offsets,
+                                             max_tiles, H, F, w.hp_r, w.hr_r, P, w.out_r, H,
+                                             a.status, st))))
       return e;
   }
   if (a.skip_shared) return cudaSuccess;

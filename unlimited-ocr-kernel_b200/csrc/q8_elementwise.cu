@@ -159,42 +159,84 @@ namespace uocr {
 
 // ops::linear_weight, BF16 branch (src/cpu/ops.rs:62-133) as the router uses
 // it: y[b][r] = sum over c of bf16(w[r][c]) * x[b][c], left to right from
-// -0.0, one rounding per operation.  A thread owns output r for kBf16Rows
-// rows of x (independent chains sharing each weight it loads); the CTA's
-// rows of x are staged in shared memory.  Meant for small n (the router's
-// 64 outputs).
-constexpr int kBf16Threads = 64;
-constexpr int kBf16Rows = 4;
+// -0.0, one rounding per operation.  A CTA computes kBf16Out outputs for
+// kBf16Rows rows of x: both tiles are staged in shared memory (one bulk
+// async copy per row when rows are 16-byte multiples, else plain loads),
+// rows padded so that a warp's eight weight rows and four x rows fall in
+// distinct banks; then every thread runs one output's sequential sum for
+// one row.
+constexpr int kBf16Out = 8;
+constexpr int kBf16Rows = 16;
+constexpr int kBf16Threads = kBf16Out * kBf16Rows;
+
+__host__ __device__ inline int bf16_w_stride(int k) { return k + 8; }  // bf16 elements
+__host__ __device__ inline int bf16_x_stride(int k) { return k + 4; }  // floats
 
 __global__ void __launch_bounds__(kBf16Threads)
     linear_bf16_kernel(const uint16_t* __restrict__ w, int n, int k, const float* __restrict__ x,
-                       int batch, float* y) {
-  extern __shared__ float xs[];  // [kBf16Rows][k]
-  const int b0 = blockIdx.y * kBf16Rows;
+                       int batch, float* y, int bulk, unsigned* status) {
+  extern __shared__ __align__(16) unsigned char smem_b[];
+  __shared__ __align__(8) uint64_t bar;
+  const int kw = bf16_w_stride(k), kx = bf16_x_stride(k);
+  uint16_t* ws = reinterpret_cast<uint16_t*>(smem_b);
+  float* xs = reinterpret_cast<float*>(smem_b + static_cast<size_t>(kBf16Out) * kw * 2);
+  const int r0 = blockIdx.x * kBf16Out, b0 = blockIdx.y * kBf16Rows;
+  const int nr = n - r0 < kBf16Out ? n - r0 : kBf16Out;
   const int nb = batch - b0 < kBf16Rows ? batch - b0 : kBf16Rows;
-  for (int i = threadIdx.x; i < nb * k; i += blockDim.x)
-    xs[i] = x[static_cast<long long>(b0) * k + i];
-  __syncthreads();
-  const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= n) return;
-  const uint16_t* wr = w + static_cast<long long>(r) * k;
-  float acc[kBf16Rows];
-#pragma unroll
-  for (int j = 0; j < kBf16Rows; ++j) acc[j] = -0.0f;
-  for (int c = 0; c < k; ++c) {
-    const float wv = __uint_as_float(static_cast<uint32_t>(__ldg(wr + c)) << 16);
-#pragma unroll
-    for (int j = 0; j < kBf16Rows; ++j)
-      if (j < nb) acc[j] = __fadd_rn(acc[j], __fmul_rn(wv, xs[j * k + c]));
+  if (bulk) {
+    if (threadIdx.x == 0) {
+      mbar_init(&bar, 1);
+      fence_mbar_init();
+      mbar_arrive_expect_tx(&bar, nr * k * 2 + nb * k * 4);
+      for (int r = 0; r < nr; ++r)
+        bulk_g2s(ws + r * kw, w + static_cast<long long>(r0 + r) * k, k * 2, &bar);
+      for (int b = 0; b < nb; ++b)
+        bulk_g2s(xs + b * kx, x + static_cast<long long>(b0 + b) * k, k * 4, &bar);
+    }
+    __syncthreads();  // the barrier is initialised before anyone waits on it
+    mbar_wait(&bar, 0, status);
+  } else {
+    for (int r = 0; r < nr; ++r)
+      for (int c = threadIdx.x; c < k; c += blockDim.x)
+        ws[r * kw + c] = w[static_cast<long long>(r0 + r) * k + c];
+    for (int b = 0; b < nb; ++b)
+      for (int c = threadIdx.x; c < k; c += blockDim.x)
+        xs[b * kx + c] = x[static_cast<long long>(b0 + b) * k + c];
+    __syncthreads();
   }
-  for (int j = 0; j < nb; ++j) y[static_cast<long long>(b0 + j) * n + r] = acc[j];
+  const int r = threadIdx.x % kBf16Out, b = threadIdx.x / kBf16Out;
+  if (r >= nr || b >= nb) return;
+  const uint16_t* wr = ws + r * kw;
+  const float* xr = xs + b * kx;
+  float acc = -0.0f;
+  int c = 0;
+  for (; c + 8 <= k; c += 8) {
+    float wv[8], xv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      wv[j] = __uint_as_float(static_cast<uint32_t>(wr[c + j]) << 16);
+      xv[j] = xr[c + j];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, __fmul_rn(wv[j], xv[j]));
+  }
+  for (; c < k; ++c) acc = __fadd_rn(acc, __fmul_rn(__uint_as_float(static_cast<uint32_t>(wr[c]) << 16), xr[c]));
+  y[static_cast<long long>(b0 + b) * n + r0 + r] = acc;
+}
+
+static size_t linear_bf16_smem(int k) {
+  return static_cast<size_t>(kBf16Out) * bf16_w_stride(k) * 2 +
+         static_cast<size_t>(kBf16Rows) * bf16_x_stride(k) * 4;
 }
 
 cudaError_t launch_linear_bf16(const uint16_t* w, int n, int k, const float* x, int batch, float* y,
-                               cudaStream_t st) {
+                               unsigned* status, cudaStream_t st) {
   if (n <= 0 || batch <= 0) return cudaSuccess;
-  const size_t smem = static_cast<size_t>(k) * 4 * kBf16Rows;
+  const size_t smem = linear_bf16_smem(k);
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  // bulk copies: 16-byte aligned rows of 16-byte multiples (k % 8 == 0)
+  const int bulk = k % 8 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(x) % 16 == 0;
   static unsigned configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -202,9 +244,8 @@ cudaError_t launch_linear_bf16(const uint16_t* w, int n, int k, const float* x, 
     cudaFuncSetAttribute(linear_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     configured |= 1u << (dev & 31);
   }
-  linear_bf16_kernel<<<dim3((n + kBf16Threads - 1) / kBf16Threads,
-                            (batch + kBf16Rows - 1) / kBf16Rows),
-                       kBf16Threads, smem, st>>>(w, n, k, x, batch, y);
+  linear_bf16_kernel<<<dim3((n + kBf16Out - 1) / kBf16Out, (batch + kBf16Rows - 1) / kBf16Rows),
+                       kBf16Threads, smem, st>>>(w, n, k, x, batch, y, bulk, status);
   return cudaGetLastError();
 }
 

@@ -67,6 +67,7 @@ struct SmallArgs {
   const int* counts;         // grouped: rows per group; nullptr: total_rows in groups of 16
   const int* offsets;
   int groups, lo, hi, total_rows;
+  int chunks;                // grouped: 16-row chunks per group (grid.y = groups * chunks)
   int N, K, piece_rows;
   const float* rinv;
   float* y;
@@ -121,16 +122,22 @@ __global__ void __launch_bounds__(kSmThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kSmStages * kStage);
   uint64_t* empty = full + kSmStages;
 
-  const int g = blockIdx.y;
+  int g = blockIdx.y;
   int count, off;
   if (a.counts) {
-    count = a.counts[g];
-    off = a.offsets[g];
+    // group g's rows [16c, 16c + 16) of chunk c; the group qualifies by its
+    // whole row count
+    const int c = g % a.chunks;
+    g /= a.chunks;
+    const int total = a.counts[g];
+    if (total < a.lo || total > a.hi) return;
+    off = a.offsets[g] + 16 * c;
+    count = total - 16 * c < 16 ? total - 16 * c : 16;
   } else {
     off = 16 * g;
     count = a.total_rows - off < 16 ? a.total_rows - off : 16;
   }
-  if (count < a.lo || count > a.hi || count < 1) return;
+  if (count < 1) return;
   const int n0 = blockIdx.x * kSmRows;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kstages = a.K / kSmK;
@@ -315,8 +322,9 @@ cudaError_t launch_small_rows(bool int8, const void* maps, const Q8View* single,
                               int K, const uint16_t* pieces, int piece_rows, const float* rinv,
                               const int8_t* xq, const float* xs, int x_rows, float* y,
                               long long ldy, unsigned* status, cudaStream_t st) {
-  if (!small_rows_supported(N, K) || hi > kSmallRowsMax || lo < 1) return cudaErrorInvalidValue;
+  if (!small_rows_supported(N, K) || hi > kSmallChunkedMax || lo < 1) return cudaErrorInvalidValue;
   if (!maps && !single) return cudaErrorInvalidValue;
+  const int chunks = counts ? (hi + 15) / 16 : 1;
   if (!counts) groups = (total_rows + 15) / 16;
   if (groups < 1 || reinterpret_cast<uintptr_t>(y) % 8 || ldy % 2) return cudaErrorInvalidValue;
   CUtensorMap tw{}, tws{}, tx{}, txs{};
@@ -339,6 +347,7 @@ cudaError_t launch_small_rows(bool int8, const void* maps, const Q8View* single,
   a.counts = counts;
   a.offsets = offsets;
   a.groups = groups;
+  a.chunks = chunks;
   a.lo = lo;
   a.hi = hi;
   a.total_rows = total_rows;
@@ -349,7 +358,7 @@ cudaError_t launch_small_rows(bool int8, const void* maps, const Q8View* single,
   a.y = y;
   a.ldy = ldy;
   a.status = status;
-  const dim3 grid(N / kSmRows, groups);
+  const dim3 grid(N / kSmRows, groups * chunks);
   if (int8)
     small_rows_kernel<true><<<grid, kSmThreads, kSmSmemI, st>>>(tw, tws, tx, txs, a);
   else
