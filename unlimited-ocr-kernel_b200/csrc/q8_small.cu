@@ -49,7 +49,10 @@ constexpr int kSmTiles = 4;                         // n8 tiles of weight rows p
 constexpr int kSmThreads = 32 * (kSmWarps + 1);     // + the producer warp
 constexpr int kSmRows = 8 * kSmTiles * kSmWarps;    // weight rows per CTA (128)
 constexpr int kSmK = 128;                           // K per stage (4 q8 blocks)
-constexpr int kSmStages = 6;
+// Ring depth: three stages, so that two FP32 CTAs (or three int8 CTAs) share
+// an SM and one computes while the other waits for its tiles.
+constexpr int kSmStagesF = 3;
+constexpr int kSmStagesI = 3;
 constexpr int kSmW = kSmRows * kSmK;                // 16 KB int8 weights
 constexpr int kSmWs = kSmRows * 4 * 4;              // 2 KB weight scales
 constexpr int kSmXp = 16 * kSmK * 2;                // 4 KB per bf16 piece tile
@@ -57,8 +60,8 @@ constexpr int kSmXq = 16 * kSmK;                    // 2 KB int8 rows
 constexpr int kSmXs = 16 * 4 * 4;                   // 256 B activation scales
 constexpr int kSmStageF = kSmW + kSmWs + 3 * kSmXp;          // 30 KB
 constexpr int kSmStageI = 21 * 1024;                         // 16 + 2 + 2 + 0.25 KB, padded
-constexpr int kSmSmemF = kSmStages * kSmStageF + 1024 + 256;
-constexpr int kSmSmemI = kSmStages * kSmStageI + 1024 + 256;
+constexpr int kSmSmemF = kSmStagesF * kSmStageF + 1024 + 256;
+constexpr int kSmSmemI = kSmStagesI * kSmStageI + 1024 + 256;
 static_assert(kSmStageF % 1024 == 0 && kSmStageI % 1024 == 0, "swizzled tiles: 1024-byte stages");
 static_assert(kSmW + kSmWs + kSmXq + kSmXs <= kSmStageI, "int8 stage layout");
 
@@ -109,7 +112,7 @@ __device__ __forceinline__ uint2 i8x4_bf16(uint32_t w) {
 }
 
 template <bool INT8>
-__global__ void __launch_bounds__(kSmThreads, 1)
+__global__ void __launch_bounds__(kSmThreads, 2)
     small_rows_kernel(const __grid_constant__ CUtensorMap tw,   // single: weights
                       const __grid_constant__ CUtensorMap tws,  // single: weight scales
                       const __grid_constant__ CUtensorMap tx,   // pieces, or int8 rows
@@ -119,6 +122,7 @@ __global__ void __launch_bounds__(kSmThreads, 1)
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  constexpr int kSmStages = INT8 ? kSmStagesI : kSmStagesF;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kSmStages * kStage);
   uint64_t* empty = full + kSmStages;
 
@@ -307,6 +311,11 @@ void configure_small() {
                          kSmSmemF);
     cudaFuncSetAttribute(small_rows_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          kSmSmemI);
+    // all of the unified L1 as shared memory, so that two CTAs fit on an SM
+    cudaFuncSetAttribute(small_rows_kernel<false>,
+                         cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(small_rows_kernel<true>,
+                         cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     done |= 1ull << dev;
   }
 }
