@@ -871,6 +871,8 @@ def run_attn(args):
                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                         "frac": round(gbs / peak, 4), "traffic": args.traffic},
            "gpu_launches": steps, "clocks": clocks.summary()}
+    if not args.no_cpu:
+        res["cpu_baseline"] = attn_cpu_baseline(min(args.cpu_seconds, 8.0))
     for kv in caches:
         kv.free()
     return res
@@ -896,6 +898,91 @@ def decode_step_bytes(cfg, tokens_per_seq):
                         + cfg.experts * H * 2)
     head = q8(cfg.vocab, H)
     return kv + attn + dense + moe + head + DEC_BATCH * H * 2
+
+
+def attn_cpu_baseline(seconds):
+    """The oracle's ops::attention_decode (scalar port of the reference) for
+    one sequence over 2176 tokens of 10 heads x 128, timed on the host for a
+    bounded number of seconds; GB/s of keys + values read."""
+    import oracle
+    rng = np.random.default_rng(5)
+    W = ATTN_HEADS * ATTN_DIM
+    k = rng.standard_normal((ATTN_TOKENS, W)).astype(np.float32)
+    v = (k * 0.5).astype(np.float32)
+    q = (rng.standard_normal(W) * 0.05).astype(np.float32)
+    oracle.attention_decode(q, k, v, ATTN_HEADS)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        oracle.attention_decode(q, k, v, ATTN_HEADS)
+        n += 1
+    dt = time.perf_counter() - t0
+    per_seq = ATTN_TOKENS * W * 4 * 2
+    return {"value": round(per_seq * n / dt / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{n} single-sequence attention_decode calls (2176 tokens) in {dt:.1f} s"}
+
+
+def decode_cpu_baseline(seconds):
+    """One sequence's decode step through the oracle (the reference's scalar
+    operations): attention block (norm, q/k/v/o, rope, cache push, attention
+    over 2176 tokens), BF16 router and MoE layer (64 experts, top 6, shared
+    1792), timed for a bounded number of seconds over MoE layers, plus one
+    dense layer and lm_head timed once; tokens/s of a 12-layer step (1 dense
+    + 11 MoE layers) for one sequence."""
+    import oracle
+    rng = np.random.default_rng(6)
+    H, heads, dim = 1280, ATTN_HEADS, ATTN_DIM
+
+    def m(r, c):
+        return oracle.Matrix(rng.integers(-127, 128, size=(r, c), dtype=np.int8),
+                             rng.uniform(1e-4, 1e-2, size=(r, (c + 31) // 32)).astype(np.float32))
+
+    qkvo = [m(H, H) for _ in range(4)]
+    norm = np.ones(H, np.float32)
+    cache = oracle.LayerCache(heads, dim, 128)
+    kp = rng.standard_normal((DEC_PREFIX, H)).astype(np.float32)
+    cache.prefill(kp, kp * 0.5, DEC_PREFIX)
+    for _ in range(127):
+        r = rng.standard_normal(H).astype(np.float32)
+        cache.push(r, r)
+    shared = oracle.Ffn(m(FS, H), m(FS, H), m(H, FS))
+    experts = [oracle.Ffn(m(F, H), m(F, H), m(H, F)) for _ in range(E)]
+    router = (rng.standard_normal((E, H)).astype(np.float32) * 0.03).view(np.uint32) >> 16
+    router = router.astype(np.uint16)
+
+    def attention_block(x):
+        n = oracle.rms_norm(x, norm)
+        q, k, v = (oracle.linear(mm, n)[0] for mm in qkvo[:3])
+        pos = cache.position()
+        q, k = oracle.rope(q, dim, pos), oracle.rope(k, dim, pos)
+        cache.push(k, v)
+        a = oracle.attention_decode(q, cache.keys, cache.values, heads)
+        return oracle.linear(qkvo[3], a[None])[0] + x[0]
+
+    def moe_layer(x):
+        r = attention_block(x)
+        n = oracle.rms_norm(r[None], norm)
+        lg = oracle.linear_bf16(router, n)
+        y, _, _ = oracle.experts(shared, experts, lg, n, TOPK, 0)
+        return (r + y[0])[None]
+
+    x = rng.standard_normal((1, H)).astype(np.float32)
+    moe_layer(x)
+    n_layers, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        x = moe_layer(x)
+        n_layers += 1
+    moe_s = (time.perf_counter() - t0) / n_layers
+    dense = oracle.Ffn(m(6848, H), m(6848, H), m(H, 6848))
+    t1 = time.perf_counter()
+    r = attention_block(x)
+    oracle.feed_forward(dense, oracle.rms_norm(r[None], norm), 0)
+    dense_s = time.perf_counter() - t1
+    step_s = 11 * moe_s + dense_s
+    return {"value": round(1.0 / step_s, 3), "unit": "tok/s", "cores": oracle.get_threads(),
+            "kind": "port",
+            "sample": f"{n_layers} MoE layers ({moe_s * 1e3:.1f} ms each) and one dense layer "
+                      f"({dense_s * 1e3:.1f} ms) of one sequence; a 12-layer step = 11 MoE + 1 dense "
+                      "(lm_head not included)"}
 
 
 def run_decode(args):
@@ -981,6 +1068,8 @@ def run_decode(args):
                         "unit": "GB/s", "frac": round(gbs / peak, 4), "traffic": None},
            "gpu_launches": None, "clocks": clocks.summary()}
     state.free()
+    if not args.no_cpu:
+        res["cpu_baseline"] = decode_cpu_baseline(min(args.cpu_seconds, 10.0))
     return res
 
 
