@@ -330,6 +330,12 @@ int uocr_kv_push(uocr_ctx *ctx, uocr_kv *kv, const float *k_dev, const float *v_
 int uocr_kv_rope(uocr_ctx *ctx, const uocr_kv *kv, const uocr_rope *rope, float *q_dev,
                  float *k_dev);
 int uocr_kv_attention(uocr_ctx *ctx, const uocr_kv *kv, const float *q_dev, float *out_dev);
+/* uocr_kv_rope then uocr_kv_push in one launch, reading the fused q/k/v
+ * projection rows [q | k | v] (batch x 3*heads*head_dim, device): q is rotated
+ * into q_out_dev (batch x heads*head_dim), k rotated and v copied into the
+ * cache.  Same results as the two calls. */
+int uocr_kv_rope_push_qkv(uocr_ctx *ctx, uocr_kv *kv, const uocr_rope *rope, const float *qkv_dev,
+                          float *q_out_dev);
 int uocr_kv_state(uocr_ctx *ctx, const uocr_kv *kv, size_t seq, size_t *tokens, size_t *position);
 int uocr_kv_export(uocr_ctx *ctx, const uocr_kv *kv, size_t seq, float *keys_out,
                    float *values_out, size_t *tokens);

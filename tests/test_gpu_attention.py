@@ -302,3 +302,36 @@ def test_attention_block_matches_oracle(ctx, mode):
             assert err <= tol * float(np.max(np.abs(ref))), (step, b, err)
     kv.free()
     rope.free()
+
+
+@pytest.mark.parametrize("heads,dim", [(2, 8), (10, 128)])
+def test_rope_push_qkv_equals_rope_then_push(ctx, heads, dim):
+    """uocr_kv_rope_push_qkv on fused [q | k | v] rows equals uocr_kv_rope
+    followed by uocr_kv_push on the separate rows, bit for bit (q and the
+    cache contents), across ring wraps, for the plain and tiled layouts."""
+    import torch
+    rng = np.random.default_rng(31 + dim)
+    batch, window, prefix = 3, 4, 5
+    width = heads * dim
+    a = A().KvCache(ctx, batch, heads, dim, window, prefix)
+    b = A().KvCache(ctx, batch, heads, dim, window, prefix)
+    rope = A().Rope(ctx, dim, 10000.0, 64)
+    for s in range(batch):
+        k = dev(rng.standard_normal((prefix - s, width)).astype(np.float32))
+        a.prefill(s, k, k)
+        b.prefill(s, k, k)
+    for step in range(6):
+        qkv = dev(rng.standard_normal((batch, 3 * width)).astype(np.float32))
+        q1 = a.rope_push_qkv(rope, qkv)
+        q2, k2, v2 = (qkv[:, i * width:(i + 1) * width].contiguous() for i in range(3))
+        b.rope(rope, q2, k2)
+        b.push(k2, v2)
+        ctx.sync()
+        assert bits_equal(host(q1), host(q2)), step
+        for s in range(batch):
+            assert a.state(s) == b.state(s)
+            for x, y in zip(a.export(s), b.export(s)):
+                assert bits_equal(host(x), host(y)), (step, s)
+    a.free()
+    b.free()
+    rope.free()

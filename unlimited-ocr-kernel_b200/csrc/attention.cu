@@ -183,6 +183,64 @@ void launch_kv_push(float* keys, float* values, int* state, int batch, const KvL
   kv_push_kernel<<<batch, 256, 0, st>>>(keys, values, state, L, window, k, v, ld, status);
 }
 
+// ops::rope of q and k and LayerCache::push of k and v for every sequence,
+// straight from the fused projection output: row b of qkv is [q | k | v]
+// (3 * heads * dim floats).  q is rotated into q_out (row b), k rotated and v
+// copied into sequence b's next slot, then the sequence's counter advances —
+// the same results as uocr_kv_rope followed by uocr_kv_push.
+__global__ void kv_rope_push_kernel(float* keys, float* values, int* state, const KvLayout L,
+                                    int window, const float* __restrict__ qkv, float* q_out,
+                                    const float2* __restrict__ table, int max_pos,
+                                    unsigned* status) {
+  const int b = blockIdx.x;
+  const int prefix = state[2 * b], gen = state[2 * b + 1];
+  if (prefix <= 0) {
+    if (threadIdx.x == 0) flag(status, DEV_CACHE);
+    return;
+  }
+  const int width = L.heads * L.dim, half = L.dim >> 1;
+  const int pos = prefix + gen;
+  const long long slot = prefix + gen % window;
+  const float* q = qkv + static_cast<long long>(b) * 3 * width;
+  const float* k = q + width;
+  const float* v = k + width;
+  float* qo = q_out + static_cast<long long>(b) * width;
+  const bool in_table = pos >= 0 && pos < max_pos;
+  if (!in_table && threadIdx.x == 0) flag(status, DEV_POSITION);
+  for (int p = threadIdx.x; p < L.heads * half; p += blockDim.x) {
+    const int h = p / half, i = p - h * half;
+    const int d0 = h * L.dim + i, d1 = d0 + half;
+    float q0 = q[d0], q1 = q[d1], k0 = k[d0], k1 = k[d1];
+    if (in_table) {
+      const float2 cs = table[static_cast<long long>(pos) * half + i];
+      const float rq0 = __fsub_rn(__fmul_rn(q0, cs.x), __fmul_rn(q1, cs.y));
+      const float rq1 = __fadd_rn(__fmul_rn(q1, cs.x), __fmul_rn(q0, cs.y));
+      const float rk0 = __fsub_rn(__fmul_rn(k0, cs.x), __fmul_rn(k1, cs.y));
+      const float rk1 = __fadd_rn(__fmul_rn(k1, cs.x), __fmul_rn(k0, cs.y));
+      q0 = rq0;
+      q1 = rq1;
+      k0 = rk0;
+      k1 = rk1;
+    }
+    qo[d0] = q0;
+    qo[d1] = q1;
+    keys[kv_index(L, b, h, slot, i)] = k0;
+    keys[kv_index(L, b, h, slot, i + half)] = k1;
+    values[kv_index(L, b, h, slot, i)] = v[d0];
+    values[kv_index(L, b, h, slot, i + half)] = v[d1];
+  }
+  __syncthreads();  // every thread has read `gen`
+  if (threadIdx.x == 0) state[2 * b + 1] = gen + 1;
+}
+
+void launch_kv_rope_push(float* keys, float* values, int* state, int batch, const KvLayout& L,
+                         int window, const float* qkv, float* q_out, const float2* table,
+                         int max_pos, unsigned* status, cudaStream_t st) {
+  if (batch <= 0) return;
+  kv_rope_push_kernel<<<batch, 256, 0, st>>>(keys, values, state, L, window, qkv, q_out, table,
+                                             max_pos, status);
+}
+
 // One block per token row: token-major [tokens][heads*dim] into the layout.
 __global__ void kv_prefill_kernel(float* keys, float* values, const KvLayout L, int seq,
                                   const float* __restrict__ k, const float* __restrict__ v) {

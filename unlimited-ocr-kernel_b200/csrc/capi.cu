@@ -1539,6 +1539,24 @@ int uocr_kv_rope(uocr_ctx* ctx, const uocr_kv* kv, const uocr_rope* rope, float*
   return check_launch();
 }
 
+// ops::rope of q and k at each sequence's position and LayerCache::push of
+// k and v, from the fused projection rows [q | k | v] (batch x 3*width,
+// device): q rotated into q_out (batch x width).  One launch for what
+// uocr_kv_rope then uocr_kv_push do, with the same results.
+int uocr_kv_rope_push_qkv(uocr_ctx* ctx, uocr_kv* kv, const uocr_rope* rope, const float* qkv_dev,
+                          float* q_out_dev) {
+  if (!ctx || !kv || !rope) return fail(UOCR_ERR_INVALID, "null argument");
+  if (rope->head_dim != kv->head_dim)
+    return fail(UOCR_ERR_SHAPE, "invalid tensor shape: invalid rotary dimensions or base");
+  int st = kv_ready(kv);
+  if (st) return st;
+  if (!qkv_dev || !q_out_dev) return fail(UOCR_ERR_INVALID, "null argument");
+  DeviceGuard g(ctx->device);
+  launch_kv_rope_push(kv->keys, kv->values, kv->state, kv->batch, kv->layout, kv->window, qkv_dev,
+                      q_out_dev, rope->table, rope->max_pos, ctx->status_dev, ctx->stream);
+  return check_launch();
+}
+
 // ops::attention_decode of q row b over sequence b's cache, for every b.
 int uocr_kv_attention(uocr_ctx* ctx, const uocr_kv* kv, const float* q_dev, float* out_dev) {
   if (!ctx || !kv) return fail(UOCR_ERR_INVALID, "null argument");

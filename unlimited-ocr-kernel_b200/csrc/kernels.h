@@ -212,6 +212,10 @@ struct KvLayout {
 void launch_kv_push(float* keys, float* values, int* state, int batch, const KvLayout& L,
                     int window, const float* k, const float* v, long long ld, unsigned* status,
                     cudaStream_t st);
+// Rope of q and k plus the push of k and v, from fused rows [q | k | v].
+void launch_kv_rope_push(float* keys, float* values, int* state, int batch, const KvLayout& L,
+                         int window, const float* qkv, float* q_out, const float2* table,
+                         int max_pos, unsigned* status, cudaStream_t st);
 // LayerCache::prefill of sequence seq: token-major rows [tokens][heads*dim].
 void launch_kv_prefill(float* keys, float* values, const KvLayout& L, int seq, const float* k,
                        const float* v, int tokens, cudaStream_t st);

@@ -73,6 +73,7 @@ SIGNATURES = {
     "uocr_kv_push": (I, [P, P, P, P]),
     "uocr_kv_rope": (I, [P, P, P, P, P]),
     "uocr_kv_attention": (I, [P, P, P, P]),
+    "uocr_kv_rope_push_qkv": (I, [P, P, P, P, P]),
     "uocr_kv_state": (I, [P, P, S, ctypes.POINTER(S), ctypes.POINTER(S)]),
     "uocr_kv_export": (I, [P, P, S, P, P, ctypes.POINTER(S)]),
     "uocr_overlay_check": (I, [ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(S),

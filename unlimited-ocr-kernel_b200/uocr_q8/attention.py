@@ -99,6 +99,16 @@ class KvCache:
     def rope(self, rope: Rope, q_t, k_t):
         _check(lib().uocr_kv_rope(self.ctx.handle, self._h, rope._h, _p(q_t), _p(k_t)))
 
+    def rope_push_qkv(self, rope: Rope, qkv_t, q_out_t=None):
+        """rope + push from fused projection rows [q | k | v]; returns the
+        rotated q rows (uocr_kv_rope_push_qkv)."""
+        import torch
+        q_out_t = q_out_t if q_out_t is not None else torch.empty(
+            (self.batch, self.width), device=qkv_t.device)
+        _check(lib().uocr_kv_rope_push_qkv(self.ctx.handle, self._h, rope._h, _p(qkv_t),
+                                           _p(q_out_t)))
+        return q_out_t
+
     def attention(self, q_t, out_t=None):
         import torch
         out_t = out_t if out_t is not None else torch.empty_like(q_t)

@@ -203,9 +203,7 @@ def decode_step(decoder: Decoder, state: DecodeState, tokens_t, mode: int = 0, l
         # attention half of Decoder::layer (src/decoder/mod.rs:266-347)
         n = rms_norm_device(ctx, x, layer.input_norm, cfg.eps)
         qkv = layer.qkv.linear_device(n, dynamic=rowwise)
-        q, k, v = (qkv[:, i * H:(i + 1) * H].contiguous() for i in range(3))
-        cache.rope(state.rope, q, k)
-        cache.push(k, v)
+        q = cache.rope_push_qkv(state.rope, qkv)  # rope of q, k; push of k, v
         a = cache.attention(q)
         r = layer.o.linear_device(a, dynamic=rowwise)
         r += x
