@@ -26,6 +26,8 @@ import ctypes
 from dataclasses import dataclass
 from typing import List, Optional
 
+import numpy as np
+
 from . import (GpuContext, Int8Matrix, MoeLayer, QuantizationMode, _check, _tptr, lib)
 from .attention import KvCache, Rope, rms_norm_device
 
@@ -224,5 +226,230 @@ def decode_step(decoder: Decoder, state: DecodeState, tokens_t, mode: int = 0, l
     return out
 
 
+# ---- loading a checkpoint with its INT8 overlay -------------------------------
+
+_CONFIG_REQUIRED = ("model_type", "hidden_size", "intermediate_size", "moe_intermediate_size",
+                    "num_hidden_layers", "num_attention_heads", "num_key_value_heads",
+                    "n_routed_experts", "n_shared_experts", "num_experts_per_tok",
+                    "first_k_dense_replace", "use_mla", "vocab_size")
+
+
+def config_from_json(text: str) -> DecoderConfig:
+    """ModelConfig::from_json (src/model/config.rs:69-117): the same required
+    fields, defaults and checks (Unsupported for an attention or routing
+    variant the decoder does not implement, Shape for invalid dimensions)."""
+    import json
+
+    from . import OcrError
+    try:
+        c = json.loads(text)
+    except ValueError as e:
+        raise OcrError(2, f"JSON: {e}") from None
+    if not isinstance(c, dict):
+        raise OcrError(2, "JSON: invalid type, expected struct ModelConfig")
+    for key in _CONFIG_REQUIRED:
+        if key not in c:
+            raise OcrError(2, f"JSON: missing field `{key}`")
+    g = lambda k, d: c.get(k, d)  # noqa: E731
+    if (c["model_type"] != "unlimited-ocr" or c["use_mla"] or g("attention_bias", False)
+            or g("rope_scaling", None) is not None or g("topk_method", "greedy") != "greedy"
+            or g("scoring_func", "softmax") != "softmax" or g("moe_layer_freq", 1) != 1):
+        raise OcrError(5, "unsupported configuration: model attention or routing configuration")
+    hidden, heads = c["hidden_size"], c["num_attention_heads"]
+    eps, theta = g("rms_norm_eps", 1e-6), g("rope_theta", 10000.0)
+    scale = g("routed_scaling_factor", 1.0)
+    bad = (hidden == 0 or heads == 0 or hidden % heads or (hidden // heads) % 2
+           or heads != c["num_key_value_heads"] or c["num_hidden_layers"] == 0
+           or c["vocab_size"] == 0 or c["intermediate_size"] == 0
+           or c["moe_intermediate_size"] == 0 or c["n_shared_experts"] == 0
+           or c["num_experts_per_tok"] == 0
+           or c["num_experts_per_tok"] > c["n_routed_experts"]
+           or c["first_k_dense_replace"] > c["num_hidden_layers"]
+           or g("sliding_window", 128) == 0 or g("max_position_embeddings", 32768) == 0
+           or not (eps > 0 and eps != float("inf")) or not (theta > 0 and theta != float("inf"))
+           or not (scale > 0 and scale != float("inf")))
+    if bad:
+        raise OcrError(4, "invalid tensor shape: invalid decoder configuration")
+    return DecoderConfig(hidden=hidden, heads=heads, layers=c["num_hidden_layers"],
+                         first_dense=c["first_k_dense_replace"], experts=c["n_routed_experts"],
+                         top_k=c["num_experts_per_tok"],
+                         expert_width=c["moe_intermediate_size"],
+                         shared_width=c["moe_intermediate_size"] * c["n_shared_experts"],
+                         dense_width=c["intermediate_size"], vocab=c["vocab_size"],
+                         window=g("sliding_window", 128), eps=float(eps), theta=float(theta),
+                         max_positions=g("max_position_embeddings", 32768),
+                         normalize=bool(g("norm_topk_prob", False)), routed_scale=float(scale))
+
+
+class _Checkpoint:
+    """Read-only view of a safetensors file's tensors (host, memory-mapped);
+    layout validation is the library's (the overlay loader checks the source
+    with the reference's rules before this reads it)."""
+
+    def __init__(self, path):
+        import json
+        import struct
+        with open(path, "rb") as f:
+            n = struct.unpack("<Q", f.read(8))[0]
+            header = json.loads(f.read(n))
+        header.pop("__metadata__", None)
+        self.header, self.start = header, 8 + n
+        self.mm = np.memmap(path, dtype=np.uint8, mode="r")
+
+    def raw(self, name):
+        from . import OcrError
+        d = self.header.get(name)
+        if d is None:
+            raise OcrError(3, f"invalid checkpoint: missing tensor: {name}")
+        b = self.mm[self.start + d["data_offsets"][0]:self.start + d["data_offsets"][1]]
+        return d["dtype"], list(d["shape"]), b
+
+    def f32(self, name, shape):
+        """WeightView::to_f32 (src/checkpoint.rs:75-107) of a tensor whose
+        shape must be `shape` (Decoder::new's check, src/decoder/mod.rs:34-43)."""
+        from . import OcrError
+        dt, sh, b = self.raw(name)
+        if sh != list(shape):
+            raise OcrError(4, f"invalid tensor shape: {name}: expected {list(shape)}, got {sh}")
+        if dt == "F32":
+            v = b.view("<f4")
+        elif dt == "BF16":
+            v = (b.view("<u2").astype(np.uint32) << 16).view(np.float32)
+        elif dt == "F16":
+            v = b.view("<f2").astype(np.float32)
+        elif dt == "I8":
+            v = b.view(np.int8).astype(np.float32)
+        elif dt == "I64":
+            v = b.view("<i8").astype(np.float32)
+        else:
+            raise OcrError(5, f"unsupported configuration: dtype {dt} of {name}")
+        return np.array(v.reshape(shape), dtype=np.float32)  # a writable copy
+
+
+def _device_view(ptr: int, n: int, typestr: str, device: int):
+    """A torch tensor over n elements of device memory owned elsewhere."""
+    import torch
+
+    class _Arr:
+        __cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, False),
+                                    "version": 3, "strides": None}
+    return torch.as_tensor(_Arr(), device=f"cuda:{device}")
+
+
+def _matrix_tensors(m: Int8Matrix):
+    """(weights int8 [rows, cols], scales float [rows, blocks]) device views."""
+    w, s = m.device_ptrs()
+    nb = (m.cols + 31) // 32
+    return (_device_view(w, m.rows * m.cols, "|i1", m.ctx.device).view(m.rows, m.cols),
+            _device_view(s, m.rows * nb, "<f4", m.ctx.device).view(m.rows, nb))
+
+
+def load_decoder(ctx: GpuContext, directory, overlay_path,
+                 mode: int = QuantizationMode.WEIGHTS_ONLY, source_path=None) -> "Decoder":
+    """Model::load_with_quantization (src/model/mod.rs:81-105) for the decoder:
+    config.json and the checkpoint of ``directory``, the INT8 overlay validated
+    and uploaded by QuantizedWeights::load (uocr_overlay_load, every check of
+    the reference), the checkpoint's shapes checked as Decoder::new does
+    (src/decoder/mod.rs:32-83).  Norms, the router (BF16) and the embedding
+    come from the checkpoint; every projection and lm_head from the overlay.
+    On the device the q/k/v projections are stacked into one matrix and the
+    dense FFN is zero-padded to a multiple of 128 rows (exactly the same
+    outputs); the routed and shared experts are the overlay's own matrices."""
+    import os
+
+    import torch
+
+    from . import OcrError
+    from .overlay import QuantizedWeights
+    if overlay_path is None:
+        if mode == QuantizationMode.DYNAMIC_ACTIVATIONS:
+            raise OcrError(3, "dynamic INT8 requires a quantized weight overlay")
+        raise OcrError(5, "unsupported configuration: the device decoder runs the INT8 overlay "
+                          "(BF16 projections are outside it)")
+    source_path = source_path or os.path.join(directory, "model-00001-of-000001.safetensors")
+    with open(os.path.join(directory, "config.json")) as f:
+        cfg = config_from_json(f.read())
+    ov = QuantizedWeights.load(overlay_path, source_path, ctx)
+    ck = _Checkpoint(source_path)
+    H, dev = cfg.hidden, f"cuda:{ctx.device}"
+
+    def q8(name, rows, cols):
+        m = ov.get(name)
+        if m is None:
+            raise OcrError(3, f"invalid checkpoint: missing tensor: {name}")
+        if (m.rows, m.cols) != (rows, cols):
+            raise OcrError(4, f"invalid tensor shape: {name}: expected {[rows, cols]}, "
+                              f"got {[m.rows, m.cols]}")
+        return m
+
+    def vec(name):
+        return torch.from_numpy(ck.f32(name, [H])).to(dev)
+
+    def padded_ffn(prefix, F):
+        g, u, d = (q8(f"{prefix}.{p}_proj.weight", *shape) for p, shape in
+                   (("gate", (F, H)), ("up", (F, H)), ("down", (H, F))))
+        Fp = (F + 127) // 128 * 128
+        if Fp == F:
+            return (g, u, d), []
+        nbH, nbF, nbP = (H + 31) // 32, (F + 31) // 32, Fp // 32
+        if F % 32:
+            raise OcrError(5, "unsupported configuration: dense FFN width not a multiple of 32")
+        out, keep = [], []
+        for m in (g, u):
+            w, s = _matrix_tensors(m)
+            wp = torch.zeros((Fp, H), dtype=torch.int8, device=dev)
+            sp = torch.zeros((Fp, nbH), device=dev)
+            wp[:F], sp[:F] = w, s
+            out.append(Int8Matrix.from_device(Fp, H, wp, sp, ctx))
+        w, s = _matrix_tensors(d)
+        wp = torch.zeros((H, Fp), dtype=torch.int8, device=dev)
+        sp = torch.zeros((H, nbP), device=dev)
+        wp[:, :F], sp[:, :nbF] = w, s
+        out.append(Int8Matrix.from_device(H, Fp, wp, sp, ctx))
+        return tuple(out), keep
+
+    layers = []
+    for i in range(cfg.layers):
+        pre = f"model.layers.{i}"
+        parts = [_matrix_tensors(q8(f"{pre}.self_attn.{p}_proj.weight", H, H)) for p in "qkv"]
+        qkv = Int8Matrix.from_device(3 * H, H, torch.cat([w for w, _ in parts]).contiguous(),
+                                     torch.cat([s for _, s in parts]).contiguous(), ctx)
+        o = q8(f"{pre}.self_attn.o_proj.weight", H, H)
+        in_norm, post_norm = vec(f"{pre}.input_layernorm.weight"), \
+            vec(f"{pre}.post_attention_layernorm.weight")
+        if i < cfg.first_dense:
+            dense, _ = padded_ffn(f"{pre}.mlp", cfg.dense_width)
+            layers.append(DecoderLayer(in_norm, qkv, o, post_norm, dense=dense,
+                                       dense_width=cfg.dense_width))
+            continue
+        dt, sh, b = ck.raw(f"{pre}.mlp.gate.weight")
+        if sh != [cfg.experts, H]:
+            raise OcrError(4, f"invalid tensor shape: {pre}.mlp.gate.weight: expected "
+                              f"{[cfg.experts, H]}, got {sh}")
+        if dt != "BF16":
+            raise OcrError(5, f"unsupported configuration: router dtype {dt} (BF16 only)")
+        router = torch.from_numpy(np.array(b.view("<i2")).reshape(cfg.experts, H)).to(dev)
+        ffn = lambda name, F: [q8(f"{name}.{p}_proj.weight", *shape) for p, shape in  # noqa: E731
+                               (("gate", (F, H)), ("up", (F, H)), ("down", (H, F)))]
+        shared = ffn(f"{pre}.mlp.shared_experts", cfg.shared_width)
+        experts = [ffn(f"{pre}.mlp.experts.{e}", cfg.expert_width) for e in range(cfg.experts)]
+        moe = MoeLayer(ctx, shared, experts, cfg.top_k, cfg.normalize, cfg.routed_scale)
+        layers.append(DecoderLayer(in_norm, qkv, o, post_norm, router_t=router, moe=moe))
+    dt, sh, b = ck.raw("model.embed_tokens.weight")
+    if sh != [cfg.vocab, H]:
+        raise OcrError(4, f"invalid tensor shape: model.embed_tokens.weight: expected "
+                          f"{[cfg.vocab, H]}, got {sh}")
+    if dt == "BF16":
+        emb = torch.from_numpy(np.array(b.view("<i2")).reshape(cfg.vocab, H)).to(dev).view(
+            torch.bfloat16)
+    else:
+        emb = torch.from_numpy(ck.f32("model.embed_tokens.weight", [cfg.vocab, H])).to(dev)
+    head = q8("lm_head.weight", cfg.vocab, H)
+    dec = Decoder(ctx, cfg, layers, emb, vec("model.norm.weight"), head)
+    dec.mode = int(mode)
+    dec.overlay = ov  # the overlay owns the matrices the layers borrow
+    return dec
+
+
 __all__ = ["DecoderConfig", "Decoder", "DecoderLayer", "DecodeState", "decode_step",
-           "linear_bf16_device", "feed_forward_device"]
+           "linear_bf16_device", "feed_forward_device", "config_from_json", "load_decoder"]
