@@ -12,13 +12,17 @@
 // A CTA owns 128 weight rows of one group's matrix.  Its producer lane moves
 // each 128-wide slice of K into a ring of shared-memory stages with TMA: the
 // weights' int8 tile [128][128] (128-byte swizzle), their block scales
-// [128][4], and the group's 16 activation rows (the three bf16 pieces
-// [16][128] each, or int8 rows [16][128] and their scales [16][4]); rows past
-// the group read as other rows or as zeros and are never stored.  Four warps
-// compute: a warp owns 32 weight rows as four n8 tiles (eight warps of two
-// tiles measured slower: the activation fragments, shared by every warp, are
-// read from shared memory once per warp); the group's rows (the MMA's M) are
-// the A operand.  Within each 32-wide q8 block K is permuted
+// [128][4], and 8 of the group's rows (the three bf16 pieces [8][128] each,
+// or int8 rows [8][128] and their scales [8][4]); a group of more than 8
+// rows takes one CTA per 8-row chunk (the weight tiles of its other chunks
+// mostly come from L2), and rows past the group read as other rows or as
+// zeros and are never stored.  Four warps compute: a warp owns 32 weight rows
+// as two m16 tiles, the MMA's A operand, and the chunk's rows are the n8 N
+// operand.  (With the group's rows as M every MMA covers 16 rows however few
+// the group has; at about 6 rows per expert the weights as M halve the MMAs
+// and the int8 per-block epilogue, and the 8-row stages fit three CTAs on an
+// SM.)
+// Within each 32-wide q8 block K is permuted
 // consistently for A and B (a product over K does not depend on the order) so
 // that lane (g = lane / 4, q = lane % 4) needs only elements [8q, 8q + 8) of
 // the block in its rows:
@@ -49,17 +53,19 @@ constexpr int kSmTiles = 4;                         // n8 tiles of weight rows p
 constexpr int kSmThreads = 32 * (kSmWarps + 1);     // + the producer warp
 constexpr int kSmRows = 8 * kSmTiles * kSmWarps;    // weight rows per CTA (128)
 constexpr int kSmK = 128;                           // K per stage (4 q8 blocks)
-// Ring depth: three stages, so that two FP32 CTAs (or three int8 CTAs) share
-// an SM and one computes while the other waits for its tiles.
+constexpr int kSmChunk = 8;                         // group rows per CTA (the MMA's N)
+// Ring depth: three stages, and three CTAs share an SM (registers <= 136 and
+// <= 75 KB of shared memory each), so that one computes while the others wait
+// for their tiles.
 constexpr int kSmStagesF = 3;
 constexpr int kSmStagesI = 3;
 constexpr int kSmW = kSmRows * kSmK;                // 16 KB int8 weights
 constexpr int kSmWs = kSmRows * 4 * 4;              // 2 KB weight scales
-constexpr int kSmXp = 16 * kSmK * 2;                // 4 KB per bf16 piece tile
-constexpr int kSmXq = 16 * kSmK;                    // 2 KB int8 rows
-constexpr int kSmXs = 16 * 4 * 4;                   // 256 B activation scales
-constexpr int kSmStageF = kSmW + kSmWs + 3 * kSmXp;          // 30 KB
-constexpr int kSmStageI = 21 * 1024;                         // 16 + 2 + 2 + 0.25 KB, padded
+constexpr int kSmXp = kSmChunk * kSmK * 2;          // 2 KB per bf16 piece tile
+constexpr int kSmXq = kSmChunk * kSmK;              // 1 KB int8 rows
+constexpr int kSmXs = kSmChunk * 4 * 4;             // 128 B activation scales
+constexpr int kSmStageF = kSmW + kSmWs + 3 * kSmXp;          // 24 KB
+constexpr int kSmStageI = 20 * 1024;                         // 16 + 2 + 1 + 0.125 KB, padded
 constexpr int kSmSmemF = kSmStagesF * kSmStageF + 1024 + 256;
 constexpr int kSmSmemI = kSmStagesI * kSmStageI + 1024 + 256;
 static_assert(kSmStageF % 1024 == 0 && kSmStageI % 1024 == 0, "swizzled tiles: 1024-byte stages");
@@ -67,10 +73,10 @@ static_assert(kSmW + kSmWs + kSmXq + kSmXs <= kSmStageI, "int8 stage layout");
 
 struct SmallArgs {
   const TcMatrixMaps* maps;  // grouped: device [groups]; nullptr: the single maps
-  const int* counts;         // grouped: rows per group; nullptr: total_rows in groups of 16
+  const int* counts;         // grouped: rows per group; nullptr: total_rows in chunks of 8
   const int* offsets;
   int groups, lo, hi, total_rows;
-  int chunks;                // grouped: 16-row chunks per group (grid.y = groups * chunks)
+  int chunks;                // grouped: 8-row chunks per group (grid.y = chunks * groups)
   int N, K, piece_rows;
   const float* rinv;
   float* y;
@@ -112,7 +118,7 @@ __device__ __forceinline__ uint2 i8x4_bf16(uint32_t w) {
 }
 
 template <bool INT8>
-__global__ void __launch_bounds__(kSmThreads, 2)
+__global__ void __launch_bounds__(kSmThreads, 3)
     small_rows_kernel(const __grid_constant__ CUtensorMap tw,   // single: weights
                       const __grid_constant__ CUtensorMap tws,  // single: weight scales
                       const __grid_constant__ CUtensorMap tx,   // pieces, or int8 rows
@@ -129,17 +135,18 @@ __global__ void __launch_bounds__(kSmThreads, 2)
   int g = blockIdx.y;
   int count, off;
   if (a.counts) {
-    // group g's rows [16c, 16c + 16) of chunk c; the group qualifies by its
-    // whole row count
-    const int c = g % a.chunks;
-    g /= a.chunks;
+    // group g's rows [8c, 8c + 8) of chunk c; the group qualifies by its whole
+    // row count.  Chunk-major order: every group's first chunk is dispatched
+    // before the (mostly empty) later ones.
+    const int c = g / a.groups;
+    g -= c * a.groups;
     const int total = a.counts[g];
     if (total < a.lo || total > a.hi) return;
-    off = a.offsets[g] + 16 * c;
-    count = total - 16 * c < 16 ? total - 16 * c : 16;
+    off = a.offsets[g] + kSmChunk * c;
+    count = total - kSmChunk * c < kSmChunk ? total - kSmChunk * c : kSmChunk;
   } else {
-    off = 16 * g;
-    count = a.total_rows - off < 16 ? a.total_rows - off : 16;
+    off = kSmChunk * g;
+    count = a.total_rows - off < kSmChunk ? a.total_rows - off : kSmChunk;
   }
   if (count < 1) return;
   const int n0 = blockIdx.x * kSmRows;
@@ -183,120 +190,122 @@ __global__ void __launch_bounds__(kSmThreads, 2)
     return;
   }
 
-  // ---- consumers: warp cw owns weight rows wr0 .. wr0 + 8 kSmTiles - 1 of the tile
+  // ---- consumers: warp cw owns weight rows wr0 .. wr0 + 31 of the tile as two
+  // m16 tiles (the MMA's A operand); the chunk's (up to 8) rows are the N
+  // operand.  Lane (gq, q) holds the outputs of weight rows wr0 + 16 m + 8 h +
+  // gq (h = 0, 1) for chunk rows 2 q and 2 q + 1.
   const int cw = warp - 1, gq = lane >> 2, q = lane & 3;
   const int wr0 = 8 * kSmTiles * cw;
-  const int i0 = gq, i1 = gq + 8;  // A rows (the group's rows gq, gq + 8)
-  float acc[kSmTiles][4];
+  float acc[2][4];
 #pragma unroll
-  for (int t = 0; t < kSmTiles; ++t)
+  for (int m = 0; m < 2; ++m)
 #pragma unroll
-    for (int c = 0; c < 4; ++c) acc[t][c] = INT8 ? -0.0f : 0.0f;
+    for (int c = 0; c < 4; ++c) acc[m][c] = INT8 ? -0.0f : 0.0f;
   bool ok = true;
   for (int ks = 0; ks < kstages; ++ks) {
     const int s = ks % kSmStages;
     if (ok) ok = mbar_wait_spin(&full[s], (ks / kSmStages) & 1, a.status);
     const unsigned char* st = smem + s * kStage;
     const float* wsm = reinterpret_cast<const float*>(st + kSmW);  // [128][4]
-    // this lane's weight scales for the stage's four blocks: rows wr0 + 8t + 2q + h
-    float4 ws4[kSmTiles][2];
+    // this lane's weight scales for the stage's four blocks
+    float4 ws4[2][2];
 #pragma unroll
-    for (int t = 0; t < kSmTiles; ++t)
+    for (int m = 0; m < 2; ++m)
 #pragma unroll
       for (int h = 0; h < 2; ++h)
-        ws4[t][h] = *reinterpret_cast<const float4*>(wsm + 4 * (wr0 + 8 * t + 2 * q + h));
+        ws4[m][h] = *reinterpret_cast<const float4*>(wsm + 4 * (wr0 + 16 * m + 8 * h + gq));
     float4 xs4[2];
     if (INT8) {
-      const float* xsm = reinterpret_cast<const float*>(st + kSmW + kSmWs + kSmXq);  // [16][4]
-      xs4[0] = *reinterpret_cast<const float4*>(xsm + 4 * i0);
-      xs4[1] = *reinterpret_cast<const float4*>(xsm + 4 * i1);
+      const float* xsm = reinterpret_cast<const float*>(st + kSmW + kSmWs + kSmXq);  // [8][4]
+#pragma unroll
+      for (int e = 0; e < 2; ++e) xs4[e] = *reinterpret_cast<const float4*>(xsm + 4 * (2 * q + e));
     }
 #pragma unroll
     for (int jb = 0; jb < 4; ++jb) {
-      // weights: row r = 32 cw + 8 t + gq, bytes [32 jb + 8q, + 8) of the
-      // 128-byte row; 16-byte unit (2 jb + q / 2) sits at unit ^ (r % 8)
-      uint2 wv[kSmTiles];
+      // weights: row r = wr0 + 16 m + 8 h + gq, bytes [32 jb + 8q, + 8) of
+      // the 128-byte row; 16-byte unit (2 jb + q / 2) sits at unit ^ (r % 8)
+      uint2 wv[2][2];
+      const int unit = (2 * jb + (q >> 1)) ^ gq;
 #pragma unroll
-      for (int t = 0; t < kSmTiles; ++t) {
-        const int r = wr0 + 8 * t + gq;
-        const int unit = (2 * jb + (q >> 1)) ^ gq;
-        wv[t] = *reinterpret_cast<const uint2*>(st + r * 128 + (unit << 4) + ((q & 1) << 3));
-      }
+      for (int m = 0; m < 2; ++m)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int r = wr0 + 16 * m + 8 * h + gq;
+          wv[m][h] = *reinterpret_cast<const uint2*>(st + r * 128 + (unit << 4) + ((q & 1) << 3));
+        }
       if (INT8) {
-        const unsigned char* xq = st + kSmW + kSmWs;  // [16][128]
-        const uint2 x0 = *reinterpret_cast<const uint2*>(xq + i0 * 128 + 32 * jb + 8 * q);
-        const uint2 x1 = *reinterpret_cast<const uint2*>(xq + i1 * 128 + 32 * jb + 8 * q);
-        const float xs0 = jb == 0 ? xs4[0].x : jb == 1 ? xs4[0].y : jb == 2 ? xs4[0].z : xs4[0].w;
-        const float xs1 = jb == 0 ? xs4[1].x : jb == 1 ? xs4[1].y : jb == 2 ? xs4[1].z : xs4[1].w;
+        const unsigned char* xq = st + kSmW + kSmWs;  // [8][128]
+        const uint2 xv = *reinterpret_cast<const uint2*>(xq + gq * 128 + 32 * jb + 8 * q);
 #pragma unroll
-        for (int t = 0; t < kSmTiles; ++t) {
+        for (int m = 0; m < 2; ++m) {
           int d[4] = {0, 0, 0, 0};
-          mma_s8_m16n8k32(d, x0.x, x1.x, x0.y, x1.y, wv[t].x, wv[t].y);
+          mma_s8_m16n8k32(d, wv[m][0].x, wv[m][1].x, wv[m][0].y, wv[m][1].y, xv.x, xv.y);
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const float4 w4 = ws4[t][h];
+          for (int c = 0; c < 4; ++c) {
+            const float4 w4 = ws4[m][c >> 1];
+            const float4 x4 = xs4[c & 1];
             const float wsb = jb == 0 ? w4.x : jb == 1 ? w4.y : jb == 2 ? w4.z : w4.w;
+            const float xsb = jb == 0 ? x4.x : jb == 1 ? x4.y : jb == 2 ? x4.z : x4.w;
             // ((float)S * ws) * xs, then the running sum: |S| < 2^24, so the
             // conversion is exact; every operation rounded on its own
-            acc[t][h] =
-                __fadd_rn(acc[t][h], __fmul_rn(__fmul_rn(static_cast<float>(d[h]), wsb), xs0));
-            acc[t][2 + h] = __fadd_rn(acc[t][2 + h],
-                                      __fmul_rn(__fmul_rn(static_cast<float>(d[2 + h]), wsb), xs1));
+            acc[m][c] = __fadd_rn(acc[m][c],
+                                  __fmul_rn(__fmul_rn(static_cast<float>(d[c]), wsb), xsb));
           }
         }
       } else {
-        float d[kSmTiles][4];
+        float d[2][4];
 #pragma unroll
-        for (int t = 0; t < kSmTiles; ++t)
+        for (int m = 0; m < 2; ++m)
 #pragma unroll
-          for (int c = 0; c < 4; ++c) d[t][c] = 0.0f;
-        uint2 bw[kSmTiles][2];
+          for (int c = 0; c < 4; ++c) d[m][c] = 0.0f;
+        uint2 bw[2][2][2];  // [m][h][step]
 #pragma unroll
-        for (int t = 0; t < kSmTiles; ++t) {
-          bw[t][0] = i8x4_bf16(wv[t].x);  // step 0: physical 8q + 0..3
-          bw[t][1] = i8x4_bf16(wv[t].y);  // step 1: physical 8q + 4..7
-        }
+        for (int m = 0; m < 2; ++m)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            bw[m][h][0] = i8x4_bf16(wv[m][h].x);  // step 0: physical 8q + 0..3
+            bw[m][h][1] = i8x4_bf16(wv[m][h].y);  // step 1: physical 8q + 4..7
+          }
 #pragma unroll
         for (int p = 0; p < 3; ++p) {
-          const unsigned char* xp = st + kSmW + kSmWs + p * kSmXp;  // [16][128] bf16
-          const uint4 r0 = *reinterpret_cast<const uint4*>(xp + i0 * 256 + 2 * (32 * jb + 8 * q));
-          const uint4 r1 = *reinterpret_cast<const uint4*>(xp + i1 * 256 + 2 * (32 * jb + 8 * q));
+          const unsigned char* xp = st + kSmW + kSmWs + p * kSmXp;  // [8][128] bf16
+          const uint4 rb = *reinterpret_cast<const uint4*>(xp + gq * 256 + 2 * (32 * jb + 8 * q));
 #pragma unroll
-          for (int t = 0; t < kSmTiles; ++t) {
-            mma_bf16_m16n8k16(d[t], r0.x, r1.x, r0.y, r1.y, bw[t][0].x, bw[t][0].y);
-            mma_bf16_m16n8k16(d[t], r0.z, r1.z, r0.w, r1.w, bw[t][1].x, bw[t][1].y);
+          for (int m = 0; m < 2; ++m) {
+            mma_bf16_m16n8k16(d[m], bw[m][0][0].x, bw[m][1][0].x, bw[m][0][0].y, bw[m][1][0].y,
+                              rb.x, rb.y);
+            mma_bf16_m16n8k16(d[m], bw[m][0][1].x, bw[m][1][1].x, bw[m][0][1].y, bw[m][1][1].y,
+                              rb.z, rb.w);
           }
         }
 #pragma unroll
-        for (int t = 0; t < kSmTiles; ++t)
+        for (int m = 0; m < 2; ++m)
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const float4 w4 = ws4[t][h];
+          for (int c = 0; c < 4; ++c) {
+            const float4 w4 = ws4[m][c >> 1];
             const float wsb = jb == 0 ? w4.x : jb == 1 ? w4.y : jb == 2 ? w4.z : w4.w;
-            acc[t][h] = fmaf(d[t][h], wsb, acc[t][h]);
-            acc[t][2 + h] = fmaf(d[t][2 + h], wsb, acc[t][2 + h]);
+            acc[m][c] = fmaf(d[m][c], wsb, acc[m][c]);
           }
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
-  // C layout: c0, c1 -> row gq, columns 2q, 2q + 1; c2, c3 -> row gq + 8
+  // C layout: c0, c1 -> weight row gq, chunk rows 2q, 2q + 1; c2, c3 -> weight row gq + 8
 #pragma unroll
-  for (int hr = 0; hr < 2; ++hr) {
-    const int i = gq + 8 * hr;
+  for (int e = 0; e < 2; ++e) {
+    const int i = 2 * q + e;
     if (i >= count) continue;
     const float sc = INT8 ? 1.0f : __ldg(a.rinv + off + i);
+    float* yr = a.y + (off + i) * a.ldy + n0 + wr0 + gq;
 #pragma unroll
-    for (int t = 0; t < kSmTiles; ++t) {
-      const int col = n0 + wr0 + 8 * t + 2 * q;
-      float v0 = acc[t][2 * hr], v1 = acc[t][2 * hr + 1];
-      if (!INT8) {
-        v0 = __fmul_rn(v0, sc);
-        v1 = __fmul_rn(v1, sc);
+    for (int m = 0; m < 2; ++m)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float v = acc[m][2 * h + e];
+        if (!INT8) v = __fmul_rn(v, sc);
+        yr[16 * m + 8 * h] = v;
       }
-      *reinterpret_cast<float2*>(a.y + (off + i) * a.ldy + col) = make_float2(v0, v1);
-    }
   }
 }
 
@@ -333,8 +342,8 @@ cudaError_t launch_small_rows(bool int8, const void* maps, const Q8View* single,
                               long long ldy, unsigned* status, cudaStream_t st) {
   if (!small_rows_supported(N, K) || hi > kSmallChunkedMax || lo < 1) return cudaErrorInvalidValue;
   if (!maps && !single) return cudaErrorInvalidValue;
-  const int chunks = counts ? (hi + 15) / 16 : 1;
-  if (!counts) groups = (total_rows + 15) / 16;
+  const int chunks = counts ? (hi + kSmChunk - 1) / kSmChunk : 1;
+  if (!counts) groups = (total_rows + kSmChunk - 1) / kSmChunk;
   if (groups < 1 || reinterpret_cast<uintptr_t>(y) % 8 || ldy % 2) return cudaErrorInvalidValue;
   CUtensorMap tw{}, tws{}, tx{}, txs{};
   if (single) {
@@ -344,9 +353,10 @@ cudaError_t launch_small_rows(bool int8, const void* maps, const Q8View* single,
     tws = mm.ws;
   }
   if (int8) {
-    if (!make_map_i8_plain(&tx, xq, x_rows, K, 16) || !make_map_f32(&txs, xs, x_rows, K / 32, 16))
+    if (!make_map_i8_plain(&tx, xq, x_rows, K, kSmChunk) ||
+        !make_map_f32(&txs, xs, x_rows, K / 32, kSmChunk))
       return cudaErrorInvalidValue;
-  } else if (!make_map_pieces_plain(&tx, pieces, piece_rows, K, 16)) {
+  } else if (!make_map_pieces_plain(&tx, pieces, piece_rows, K, kSmChunk)) {
     return cudaErrorInvalidValue;
   }
   configure_small();
@@ -367,7 +377,7 @@ cudaError_t launch_small_rows(bool int8, const void* maps, const Q8View* single,
   a.y = y;
   a.ldy = ldy;
   a.status = status;
-  const dim3 grid(N / kSmRows, groups * chunks);
+  const dim3 grid(N / kSmRows, chunks * groups);
   if (int8)
     small_rows_kernel<true><<<grid, kSmThreads, kSmSmemI, st>>>(tw, tws, tx, txs, a);
   else
