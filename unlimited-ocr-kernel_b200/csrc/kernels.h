@@ -99,15 +99,19 @@ void launch_swiglu_quantize(const float* g, const float* u, int rows, int cols, 
 // (counts null): *single over rows [0, total_rows) in groups of 16.  x_rows:
 // rows of the int8 activation tensors.  N % 128 == 0, K % 128 == 0.
 constexpr int kSmallRowsMax = 16;
-// Grouped launches may take groups of up to this many rows, as 16-row chunks
+// Grouped launches may take groups of up to this many rows, as 8-row chunks
 // (one CTA each, the group's weights re-read from L2).
 constexpr int kSmallChunkedMax = 64;
+// Upper bound on the 8-row chunks of `pairs` rows in `groups` groups (the
+// length of the chunk list group_pairs_kernel writes, without its count).
+inline int small_chunk_items(int pairs, int groups) { return (pairs + 7 * groups) / 8 + 1; }
 bool small_rows_supported(int N, int K);
 cudaError_t launch_small_rows(bool int8, const void* maps, const Q8View* single, const int* counts,
                               const int* offsets, int groups, int lo, int hi, int total_rows, int N,
                               int K, const uint16_t* pieces, int piece_rows, const float* rinv,
                               const int8_t* xq, const float* xs, int x_rows, float* y,
-                              long long ldy, unsigned* status, cudaStream_t st);
+                              long long ldy, unsigned* status, cudaStream_t st,
+                              const int* items = nullptr, int max_items = 0);
 
 // moe_route.cu — moe::route for `tokens` rows of logits.  ids/weights are
 // tokens*top_k in the reference's order (probability desc, id asc).

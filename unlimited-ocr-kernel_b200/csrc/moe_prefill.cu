@@ -34,10 +34,11 @@ __global__ void __launch_bounds__(kGroupThreads) group_pairs_kernel(
     const int32_t* __restrict__ ids, const float* __restrict__ wts, int tokens, int top_k,
     int n_experts, int skip_negative, int* __restrict__ counts, int* __restrict__ offsets,
     int* __restrict__ pair_token, float* __restrict__ pair_weight, int* __restrict__ token_pos,
-    unsigned* status) {
+    int* __restrict__ items, unsigned* status) {
   __shared__ int cnt[kGroupThreads / 32][kMaxGroupExperts];
   __shared__ int base[kMaxGroupExperts];
   __shared__ int off[kMaxGroupExperts + 1];
+  __shared__ int first[kMaxGroupExperts + 1];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int npairs = tokens * top_k;
   for (int e = tid; e < n_experts; e += blockDim.x) base[e] = 0;
@@ -66,8 +67,20 @@ __global__ void __launch_bounds__(kGroupThreads) group_pairs_kernel(
     }
     off[n_experts] = run;
     offsets[n_experts] = run;
+    int chunks = 0;  // first list position of each group's 8-row chunks
+    for (int e = 0; e < n_experts; ++e) {
+      first[e] = chunks;
+      chunks += (off[e + 1] - off[e] + 7) / 8;
+    }
+    first[n_experts] = chunks;
   }
   __syncthreads();
+  if (items) {
+    // the list of 8-row chunks of every group (small_rows_kernel's work)
+    if (tid == 0) items[0] = first[n_experts];
+    for (int e = warp; e < n_experts; e += kGroupThreads / 32)
+      for (int c = lane; c < first[e + 1] - first[e]; c += 32) items[1 + first[e] + c] = c << 8 | e;
+  }
   // pass 2: stable positions, chunk by chunk
   for (int c0 = 0; c0 < npairs; c0 += blockDim.x) {
     const int i = c0 + tid;
@@ -522,6 +535,8 @@ struct PrefillWs {
   float* xr_s;
   float* hr_s;
   int* counts_big;  // tensor-core paths: groups of more than kSmallRowsMax rows
+  int* items;       // 8-row chunks of the groups (count first)
+  int max_items;
   size_t bytes;
 };
 
@@ -555,6 +570,8 @@ static PrefillWs carve(const MoePrefillArgs& a, void* base, Path path) {
   w.pair_token = reinterpret_cast<int*>(take(sizeof(int) * P));
   w.pair_weight = reinterpret_cast<float*>(take(sizeof(float) * P));
   w.token_pos = reinterpret_cast<int*>(take(sizeof(int) * P));
+  w.max_items = small_chunk_items(static_cast<int>(P), a.n_experts);
+  w.items = reinterpret_cast<int*>(take(sizeof(int) * (w.max_items + 1)));
   w.h_r = reinterpret_cast<float*>(take(sizeof(float) * P * F));
   w.h_s = reinterpret_cast<float*>(take(sizeof(float) * T * FS));
   w.out_r = reinterpret_cast<float*>(take(sizeof(float) * P * H));
@@ -652,7 +669,8 @@ static cudaError_t prefill_tc_f32(const MoePrefillArgs& a, const PrefillWs& w, i
       float* out = j == 0 ? w.h_r : w.u_r;
       if ((e = launch_small_rows(false, maps + j * E * mb, nullptr, w.counts, w.offsets, E, 1, R, 0, F,
                                  H, w.xp_r, P, w.xr_r, nullptr, nullptr, P, out, F,
-                                 a.status, st)) ||
+                                 a.status, st,
+                                 tc ? nullptr : w.items, w.max_items)) ||
           (tc && (e = launch_q8_tc_grouped_f32(maps + j * E * mb, E, w.counts_big, w.offsets,
                                                max_tiles, F, H, w.xp_r, w.xr_r, P, out, F,
                                                a.status, st))))
@@ -661,7 +679,8 @@ static cudaError_t prefill_tc_f32(const MoePrefillArgs& a, const PrefillWs& w, i
     launch_swiglu_split(w.h_r, w.u_r, P, F, w.hp_r, w.hr_r, sms, st);
     if ((e = launch_small_rows(false, maps + 2 * E * mb, nullptr, w.counts, w.offsets, E, 1, R, 0, H,
                                  F, w.hp_r, P, w.hr_r, nullptr, nullptr, P, w.out_r, H,
-                                 a.status, st)) ||
+                                 a.status, st,
+                                 tc ? nullptr : w.items, w.max_items)) ||
         (tc && (e = launch_q8_tc_grouped_f32(maps + 2 * E * mb, E, w.counts_big, w.offsets,
                                              max_tiles, H, F, w.hp_r, w.hr_r, P, w.out_r, H,
                                              a.status, st))))
@@ -696,7 +715,8 @@ static cudaError_t prefill_tc(const MoePrefillArgs& a, const PrefillWs& w, int s
       float* out = j == 0 ? w.h_r : w.u_r;
       if ((e = launch_small_rows(true, maps + j * E * mb, nullptr, w.counts, w.offsets, E, 1, R, 0, F,
                                  H, nullptr, 0, nullptr, w.xq_p, w.xs_p, P, out, F,
-                                 a.status, st)) ||
+                                 a.status, st,
+                                 tc ? nullptr : w.items, w.max_items)) ||
           (tc && (e = launch_q8_tc_grouped_i8(maps + j * E * mb, E, w.counts_big, w.offsets,
                                               max_tiles, F, H, w.xq_p, w.xs_p, P, out, F,
                                               a.status, st))))
@@ -705,7 +725,8 @@ static cudaError_t prefill_tc(const MoePrefillArgs& a, const PrefillWs& w, int s
     launch_swiglu_quantize(w.h_r, w.u_r, P, F, w.hq_r, w.hs_r, a.status, sms, st);
     if ((e = launch_small_rows(true, maps + 2 * E * mb, nullptr, w.counts, w.offsets, E, 1, R, 0, H,
                                  F, nullptr, 0, nullptr, w.hq_r, w.hs_r, P, w.out_r, H,
-                                 a.status, st)) ||
+                                 a.status, st,
+                                 tc ? nullptr : w.items, w.max_items)) ||
         (tc && (e = launch_q8_tc_grouped_i8(maps + 2 * E * mb, E, w.counts_big, w.offsets,
                                             max_tiles, H, F, w.hq_r, w.hs_r, P, w.out_r, H,
                                             a.status, st))))
@@ -757,10 +778,12 @@ static cudaError_t prefill_tc_mixed(const MoePrefillArgs& a, const PrefillWs& w,
       float* out = j == 0 ? w.h_r : w.u_r;
       if ((e = launch_small_rows(true, maps + j * E * mb, nullptr, w.counts, w.offsets, E, 1, 1, 0, F,
                                  H, nullptr, 0, nullptr, w.xq_p, w.xs_p, P, out, F,
-                                 a.status, st)) ||
+                                 a.status, st,
+                                 tc ? nullptr : w.items, w.max_items)) ||
           (e = launch_small_rows(false, maps + j * E * mb, nullptr, w.counts, w.offsets, E, 2, R, 0, F,
                                  H, w.xp_r, P, w.xr_r, nullptr, nullptr, P, out, F,
-                                 a.status, st)) ||
+                                 a.status, st,
+                                 tc ? nullptr : w.items, w.max_items)) ||
           (tc && (e = launch_q8_tc_grouped_f32(maps + j * E * mb, E, w.counts_big, w.offsets,
                                                max_tiles, F, H, w.xp_r, w.xr_r, P, out, F,
                                                a.status, st))))
@@ -770,10 +793,12 @@ static cudaError_t prefill_tc_mixed(const MoePrefillArgs& a, const PrefillWs& w,
     launch_swiglu_split(w.h_r, w.u_r, P, F, w.hp_r, w.hr_r, sms, st);
     if ((e = launch_small_rows(true, maps + 2 * E * mb, nullptr, w.counts, w.offsets, E, 1, 1, 0, H,
                                  F, nullptr, 0, nullptr, w.hq_r, w.hs_r, P, w.out_r, H,
-                                 a.status, st)) ||
+                                 a.status, st,
+                                 tc ? nullptr : w.items, w.max_items)) ||
         (e = launch_small_rows(false, maps + 2 * E * mb, nullptr, w.counts, w.offsets, E, 2, R, 0, H,
                                  F, w.hp_r, P, w.hr_r, nullptr, nullptr, P, w.out_r, H,
-                                 a.status, st)) ||
+                                 a.status, st,
+                                 tc ? nullptr : w.items, w.max_items)) ||
         (tc && (e = launch_q8_tc_grouped_f32(maps + 2 * E * mb, E, w.counts_big, w.offsets,
                                              max_tiles, H, F, w.hp_r, w.hr_r, P, w.out_r, H,
                                              a.status, st))))
@@ -817,6 +842,7 @@ cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaS
     group_pairs_kernel<<<1, kGroupThreads, 0, st>>>(a.route_ids, a.route_weights, T, k, E,
                                                    a.skip_negative_ids, w.counts, w.offsets,
                                                    w.pair_token, w.pair_weight, w.token_pos,
+                                                   T <= kSmallChunkedMax ? w.items : nullptr,
                                                    a.status);
   }
   if (mode != 0) launch_quantize_rows(a.x, a.hidden, T, a.hidden, w.xq, w.xs, a.status, sms, st);

@@ -77,6 +77,7 @@ struct SmallArgs {
   const int* offsets;
   int groups, lo, hi, total_rows;
   int chunks;                // grouped: 8-row chunks per group (grid.y = chunks * groups)
+  const int* items;          // grouped, optional: [0] = n, [1 + i] = chunk << 8 | group
   int N, K, piece_rows;
   const float* rinv;
   float* y;
@@ -136,10 +137,19 @@ __global__ void __launch_bounds__(kSmThreads, 3)
   int count, off;
   if (a.counts) {
     // group g's rows [8c, 8c + 8) of chunk c; the group qualifies by its whole
-    // row count.  Chunk-major order: every group's first chunk is dispatched
-    // before the (mostly empty) later ones.
-    const int c = g / a.groups;
-    g -= c * a.groups;
+    // row count.  From the chunk list when there is one; otherwise
+    // chunk-major, so that every group's first chunk is dispatched before the
+    // (mostly empty) later ones.
+    int c;
+    if (a.items) {
+      if (g >= a.items[0]) return;
+      const int packed = a.items[1 + g];
+      c = packed >> 8;
+      g = packed & 255;
+    } else {
+      c = g / a.groups;
+      g -= c * a.groups;
+    }
     const int total = a.counts[g];
     if (total < a.lo || total > a.hi) return;
     off = a.offsets[g] + kSmChunk * c;
@@ -339,8 +349,10 @@ cudaError_t launch_small_rows(bool int8, const void* maps, const Q8View* single,
                               const int* offsets, int groups, int lo, int hi, int total_rows, int N,
                               int K, const uint16_t* pieces, int piece_rows, const float* rinv,
                               const int8_t* xq, const float* xs, int x_rows, float* y,
-                              long long ldy, unsigned* status, cudaStream_t st) {
+                              long long ldy, unsigned* status, cudaStream_t st,
+                              const int* items, int max_items) {
   if (!small_rows_supported(N, K) || hi > kSmallChunkedMax || lo < 1) return cudaErrorInvalidValue;
+  if (items && (!counts || max_items < 1 || groups > 256)) return cudaErrorInvalidValue;
   if (!maps && !single) return cudaErrorInvalidValue;
   const int chunks = counts ? (hi + kSmChunk - 1) / kSmChunk : 1;
   if (!counts) groups = (total_rows + kSmChunk - 1) / kSmChunk;
@@ -367,6 +379,7 @@ cudaError_t launch_small_rows(bool int8, const void* maps, const Q8View* single,
   a.offsets = offsets;
   a.groups = groups;
   a.chunks = chunks;
+  a.items = items;
   a.lo = lo;
   a.hi = hi;
   a.total_rows = total_rows;
@@ -377,7 +390,7 @@ cudaError_t launch_small_rows(bool int8, const void* maps, const Q8View* single,
   a.y = y;
   a.ldy = ldy;
   a.status = status;
-  const dim3 grid(N / kSmRows, chunks * groups);
+  const dim3 grid(N / kSmRows, items ? max_items : chunks * groups);
   if (int8)
     small_rows_kernel<true><<<grid, kSmThreads, kSmSmemI, st>>>(tw, tws, tx, txs, a);
   else
