@@ -111,7 +111,9 @@ cudaError_t launch_small_rows(bool int8, const void* maps, const Q8View* single,
                               int K, const uint16_t* pieces, int piece_rows, const float* rinv,
                               const int8_t* xq, const float* xs, int x_rows, float* y,
                               long long ldy, unsigned* status, cudaStream_t st,
-                              const int* items = nullptr, int max_items = 0);
+                              const int* items = nullptr, int max_items = 0,
+                              const void* maps2 = nullptr, const Q8View* single2 = nullptr,
+                              float* y2 = nullptr);
 
 // moe_route.cu — moe::route for `tokens` rows of logits.  ids/weights are
 // tokens*top_k in the reference's order (probability desc, id asc).

@@ -630,18 +630,16 @@ static void launch_big_counts(const int* counts, int groups, int* counts_big, cu
 }
 
 // The shared expert over T <= kSmallShared tokens with FP32 activations, as
-// groups of 16 rows on the warp-level kernel (the tokens' pieces are in
+// chunks of 8 rows on the warp-level kernel (the tokens' pieces are in
 // w.xp_s / w.xr_s); its down projection writes y.
 static cudaError_t shared_small_f32(const MoePrefillArgs& a, const PrefillWs& w, int sms,
                                     cudaStream_t st) {
   const int T = a.tokens, H = a.hidden, FS = a.shared_width;
   cudaError_t e;
+  // gate and up in one launch
   if ((e = launch_small_rows(false, nullptr, &a.shared.gate, nullptr, nullptr, 1, 1, kSmallRowsMax, T, FS,
                              H, w.xp_s, T, w.xr_s, nullptr, nullptr, T, w.h_s, FS,
-                             a.status, st)) ||
-      (e = launch_small_rows(false, nullptr, &a.shared.up, nullptr, nullptr, 1, 1, kSmallRowsMax, T, FS,
-                             H, w.xp_s, T, w.xr_s, nullptr, nullptr, T, w.u_s, FS,
-                             a.status, st)))
+                             a.status, st, nullptr, 0, nullptr, &a.shared.up, w.u_s)))
     return e;
   launch_swiglu_split(w.h_s, w.u_s, T, FS, w.hp_s, w.hr_s, sms, st);
   return launch_small_rows(false, nullptr, &a.shared.down, nullptr, nullptr, 1, 1, kSmallRowsMax, T, H,
@@ -665,17 +663,17 @@ static cudaError_t prefill_tc_f32(const MoePrefillArgs& a, const PrefillWs& w, i
   if (!a.skip_routed) {
     if (tc) launch_big_counts(w.counts, E, w.counts_big, st);
     launch_split_rows(a.x, H, w.pair_token, P, H, w.xp_r, w.xr_r, sms, st);
-    for (int j = 0; j < 2; ++j) {  // gate, up
-      float* out = j == 0 ? w.h_r : w.u_r;
-      if ((e = launch_small_rows(false, maps + j * E * mb, nullptr, w.counts, w.offsets, E, 1, R, 0, F,
-                                 H, w.xp_r, P, w.xr_r, nullptr, nullptr, P, out, F,
-                                 a.status, st,
-                                 tc ? nullptr : w.items, w.max_items)) ||
-          (tc && (e = launch_q8_tc_grouped_f32(maps + j * E * mb, E, w.counts_big, w.offsets,
-                                               max_tiles, F, H, w.xp_r, w.xr_r, P, out, F,
-                                               a.status, st))))
+    // gate and up of the small groups in one launch
+    if ((e = launch_small_rows(false, maps, nullptr, w.counts, w.offsets, E, 1, R, 0, F, H, w.xp_r,
+                               P, w.xr_r, nullptr, nullptr, P, w.h_r, F, a.status, st,
+                               tc ? nullptr : w.items, w.max_items, maps + E * mb, nullptr,
+                               w.u_r)))
+      return e;
+    for (int j = 0; tc && j < 2; ++j)  // gate, up of the larger groups
+      if ((e = launch_q8_tc_grouped_f32(maps + j * E * mb, E, w.counts_big, w.offsets, max_tiles,
+                                        F, H, w.xp_r, w.xr_r, P, j == 0 ? w.h_r : w.u_r, F,
+                                        a.status, st)))
         return e;
-    }
     launch_swiglu_split(w.h_r, w.u_r, P, F, w.hp_r, w.hr_r, sms, st);
     if ((e = launch_small_rows(false, maps + 2 * E * mb, nullptr, w.counts, w.offsets, E, 1, R, 0, H,
                                  F, w.hp_r, P, w.hr_r, nullptr, nullptr, P, w.out_r, H,
@@ -711,17 +709,17 @@ static cudaError_t prefill_tc(const MoePrefillArgs& a, const PrefillWs& w, int s
     // warp-level kernel, larger ones on the tensor-core GEMM
     if (tc) launch_big_counts(w.counts, E, w.counts_big, st);
     launch_gather_rows(w.xq, w.xs, w.pair_token, P, H, w.xq_p, w.xs_p, sms, st);
-    for (int j = 0; j < 2; ++j) {  // gate, up
-      float* out = j == 0 ? w.h_r : w.u_r;
-      if ((e = launch_small_rows(true, maps + j * E * mb, nullptr, w.counts, w.offsets, E, 1, R, 0, F,
-                                 H, nullptr, 0, nullptr, w.xq_p, w.xs_p, P, out, F,
-                                 a.status, st,
-                                 tc ? nullptr : w.items, w.max_items)) ||
-          (tc && (e = launch_q8_tc_grouped_i8(maps + j * E * mb, E, w.counts_big, w.offsets,
-                                              max_tiles, F, H, w.xq_p, w.xs_p, P, out, F,
-                                              a.status, st))))
+    // gate and up of the small groups in one launch
+    if ((e = launch_small_rows(true, maps, nullptr, w.counts, w.offsets, E, 1, R, 0, F, H, nullptr,
+                               0, nullptr, w.xq_p, w.xs_p, P, w.h_r, F, a.status, st,
+                               tc ? nullptr : w.items, w.max_items, maps + E * mb, nullptr,
+                               w.u_r)))
+      return e;
+    for (int j = 0; tc && j < 2; ++j)  // gate, up of the larger groups
+      if ((e = launch_q8_tc_grouped_i8(maps + j * E * mb, E, w.counts_big, w.offsets, max_tiles,
+                                       F, H, w.xq_p, w.xs_p, P, j == 0 ? w.h_r : w.u_r, F,
+                                       a.status, st)))
         return e;
-    }
     launch_swiglu_quantize(w.h_r, w.u_r, P, F, w.hq_r, w.hs_r, a.status, sms, st);
     if ((e = launch_small_rows(true, maps + 2 * E * mb, nullptr, w.counts, w.offsets, E, 1, R, 0, H,
                                  F, nullptr, 0, nullptr, w.hq_r, w.hs_r, P, w.out_r, H,
@@ -737,10 +735,7 @@ static cudaError_t prefill_tc(const MoePrefillArgs& a, const PrefillWs& w, int s
   if (T <= kSmallShared) {
     if ((e = launch_small_rows(true, nullptr, &a.shared.gate, nullptr, nullptr, 1, 1, kSmallRowsMax, T, FS,
                              H, nullptr, 0, nullptr, w.xq, w.xs, T, w.h_s, FS,
-                             a.status, st)) ||
-        (e = launch_small_rows(true, nullptr, &a.shared.up, nullptr, nullptr, 1, 1, kSmallRowsMax, T, FS,
-                             H, nullptr, 0, nullptr, w.xq, w.xs, T, w.u_s, FS,
-                             a.status, st)))
+                             a.status, st, nullptr, 0, nullptr, &a.shared.up, w.u_s)))
       return e;
     launch_swiglu_quantize(w.h_s, w.u_s, T, FS, w.hq_s, w.hs_s, a.status, sms, st);
     return launch_small_rows(true, nullptr, &a.shared.down, nullptr, nullptr, 1, 1, kSmallRowsMax, T, H,
@@ -774,21 +769,21 @@ static cudaError_t prefill_tc_mixed(const MoePrefillArgs& a, const PrefillWs& w,
     if (tc) launch_big_counts(w.counts, E, w.counts_big, st);
     launch_gather_rows(w.xq, w.xs, w.pair_token, P, H, w.xq_p, w.xs_p, sms, st);
     launch_split_rows(a.x, H, w.pair_token, P, H, w.xp_r, w.xr_r, sms, st);
-    for (int j = 0; j < 2; ++j) {  // gate, up
-      float* out = j == 0 ? w.h_r : w.u_r;
-      if ((e = launch_small_rows(true, maps + j * E * mb, nullptr, w.counts, w.offsets, E, 1, 1, 0, F,
-                                 H, nullptr, 0, nullptr, w.xq_p, w.xs_p, P, out, F,
-                                 a.status, st,
-                                 tc ? nullptr : w.items, w.max_items)) ||
-          (e = launch_small_rows(false, maps + j * E * mb, nullptr, w.counts, w.offsets, E, 2, R, 0, F,
-                                 H, w.xp_r, P, w.xr_r, nullptr, nullptr, P, out, F,
-                                 a.status, st,
-                                 tc ? nullptr : w.items, w.max_items)) ||
-          (tc && (e = launch_q8_tc_grouped_f32(maps + j * E * mb, E, w.counts_big, w.offsets,
-                                               max_tiles, F, H, w.xp_r, w.xr_r, P, out, F,
-                                               a.status, st))))
+    // gate and up together: one-row groups int8, 2..R rows FP32, larger on the GEMM
+    if ((e = launch_small_rows(true, maps, nullptr, w.counts, w.offsets, E, 1, 1, 0, F, H, nullptr,
+                               0, nullptr, w.xq_p, w.xs_p, P, w.h_r, F, a.status, st,
+                               tc ? nullptr : w.items, w.max_items, maps + E * mb, nullptr,
+                               w.u_r)) ||
+        (e = launch_small_rows(false, maps, nullptr, w.counts, w.offsets, E, 2, R, 0, F, H, w.xp_r,
+                               P, w.xr_r, nullptr, nullptr, P, w.h_r, F, a.status, st,
+                               tc ? nullptr : w.items, w.max_items, maps + E * mb, nullptr,
+                               w.u_r)))
+      return e;
+    for (int j = 0; tc && j < 2; ++j)
+      if ((e = launch_q8_tc_grouped_f32(maps + j * E * mb, E, w.counts_big, w.offsets, max_tiles,
+                                        F, H, w.xp_r, w.xr_r, P, j == 0 ? w.h_r : w.u_r, F,
+                                        a.status, st)))
         return e;
-    }
     launch_swiglu_quantize(w.h_r, w.u_r, P, F, w.hq_r, w.hs_r, a.status, sms, st);
     launch_swiglu_split(w.h_r, w.u_r, P, F, w.hp_r, w.hr_r, sms, st);
     if ((e = launch_small_rows(true, maps + 2 * E * mb, nullptr, w.counts, w.offsets, E, 1, 1, 0, H,
@@ -808,10 +803,7 @@ static cudaError_t prefill_tc_mixed(const MoePrefillArgs& a, const PrefillWs& w,
   if (T == 1) {
     if ((e = launch_small_rows(true, nullptr, &a.shared.gate, nullptr, nullptr, 1, 1, 1, 1, FS,
                              H, nullptr, 0, nullptr, w.xq, w.xs, T, w.h_s, FS,
-                             a.status, st)) ||
-        (e = launch_small_rows(true, nullptr, &a.shared.up, nullptr, nullptr, 1, 1, 1, 1, FS,
-                             H, nullptr, 0, nullptr, w.xq, w.xs, T, w.u_s, FS,
-                             a.status, st)))
+                             a.status, st, nullptr, 0, nullptr, &a.shared.up, w.u_s)))
       return e;
     launch_swiglu_quantize(w.h_s, w.u_s, T, FS, w.hq_s, w.hs_s, a.status, sms, st);
     return launch_small_rows(true, nullptr, &a.shared.down, nullptr, nullptr, 1, 1, 1, 1, H,

@@ -78,6 +78,9 @@ struct SmallArgs {
   int groups, lo, hi, total_rows;
   int chunks;                // grouped: 8-row chunks per group (grid.y = chunks * groups)
   const int* items;          // grouped, optional: [0] = n, [1 + i] = chunk << 8 | group
+  const TcMatrixMaps* maps2;  // optional second matrix of the same shape (gate and up in one
+  float* y2;                  // launch): CTAs x >= tiles compute it into y2
+  int tiles;                  // N / kSmRows
   int N, K, piece_rows;
   const float* rinv;
   float* y;
@@ -124,6 +127,8 @@ __global__ void __launch_bounds__(kSmThreads, 3)
                       const __grid_constant__ CUtensorMap tws,  // single: weight scales
                       const __grid_constant__ CUtensorMap tx,   // pieces, or int8 rows
                       const __grid_constant__ CUtensorMap txs,  // int8 row scales
+                      const __grid_constant__ CUtensorMap tw2,  // single: second matrix
+                      const __grid_constant__ CUtensorMap tws2,
                       const SmallArgs a) {
   constexpr int kStage = INT8 ? kSmStageI : kSmStageF;
   extern __shared__ unsigned char smem_raw[];
@@ -159,7 +164,9 @@ __global__ void __launch_bounds__(kSmThreads, 3)
     count = a.total_rows - off < kSmChunk ? a.total_rows - off : kSmChunk;
   }
   if (count < 1) return;
-  const int n0 = blockIdx.x * kSmRows;
+  const bool second = static_cast<int>(blockIdx.x) >= a.tiles;  // only with y2
+  const int n0 = (second ? blockIdx.x - a.tiles : blockIdx.x) * kSmRows;
+  float* const y = second ? a.y2 : a.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kstages = a.K / kSmK;
 
@@ -175,8 +182,9 @@ __global__ void __launch_bounds__(kSmThreads, 3)
   if (warp == 0) {
     // ---- producer
     if (lane == 0) {
-      const CUtensorMap* wmap = a.maps ? &a.maps[g].w_sw128 : &tw;
-      const CUtensorMap* smap = a.maps ? &a.maps[g].ws : &tws;
+      const TcMatrixMaps* gm = second ? a.maps2 : a.maps;
+      const CUtensorMap* wmap = gm ? &gm[g].w_sw128 : second ? &tw2 : &tw;
+      const CUtensorMap* smap = gm ? &gm[g].ws : second ? &tws2 : &tws;
       const uint32_t tx_bytes = INT8 ? kSmW + kSmWs + kSmXq + kSmXs : kSmW + kSmWs + 3 * kSmXp;
       for (int ks = 0; ks < kstages; ++ks) {
         const int s = ks % kSmStages;
@@ -307,7 +315,7 @@ __global__ void __launch_bounds__(kSmThreads, 3)
     const int i = 2 * q + e;
     if (i >= count) continue;
     const float sc = INT8 ? 1.0f : __ldg(a.rinv + off + i);
-    float* yr = a.y + (off + i) * a.ldy + n0 + wr0 + gq;
+    float* yr = y + (off + i) * a.ldy + n0 + wr0 + gq;
 #pragma unroll
     for (int m = 0; m < 2; ++m)
 #pragma unroll
@@ -350,19 +358,29 @@ cudaError_t launch_small_rows(bool int8, const void* maps, const Q8View* single,
                               int K, const uint16_t* pieces, int piece_rows, const float* rinv,
                               const int8_t* xq, const float* xs, int x_rows, float* y,
                               long long ldy, unsigned* status, cudaStream_t st,
-                              const int* items, int max_items) {
+                              const int* items, int max_items, const void* maps2,
+                              const Q8View* single2, float* y2) {
   if (!small_rows_supported(N, K) || hi > kSmallChunkedMax || lo < 1) return cudaErrorInvalidValue;
   if (items && (!counts || max_items < 1 || groups > 256)) return cudaErrorInvalidValue;
   if (!maps && !single) return cudaErrorInvalidValue;
+  if (y2 && (single ? !single2 : !maps2)) return cudaErrorInvalidValue;
+  if (y2 && reinterpret_cast<uintptr_t>(y2) % 8) return cudaErrorInvalidValue;
   const int chunks = counts ? (hi + kSmChunk - 1) / kSmChunk : 1;
   if (!counts) groups = (total_rows + kSmChunk - 1) / kSmChunk;
   if (groups < 1 || reinterpret_cast<uintptr_t>(y) % 8 || ldy % 2) return cudaErrorInvalidValue;
-  CUtensorMap tw{}, tws{}, tx{}, txs{};
+  CUtensorMap tw{}, tws{}, tx{}, txs{}, tw2{}, tws2{};
   if (single) {
     TcMatrixMaps mm;
     if (!q8_tc_weight_maps(&mm, *single)) return cudaErrorInvalidValue;
     tw = mm.w_sw128;
     tws = mm.ws;
+    if (y2) {
+      if (single2->rows != single->rows || single2->cols != single->cols ||
+          !q8_tc_weight_maps(&mm, *single2))
+        return cudaErrorInvalidValue;
+      tw2 = mm.w_sw128;
+      tws2 = mm.ws;
+    }
   }
   if (int8) {
     if (!make_map_i8_plain(&tx, xq, x_rows, K, kSmChunk) ||
@@ -380,6 +398,9 @@ cudaError_t launch_small_rows(bool int8, const void* maps, const Q8View* single,
   a.groups = groups;
   a.chunks = chunks;
   a.items = items;
+  a.tiles = y2 ? N / kSmRows : 1 << 30;
+  a.y2 = y2;
+  a.maps2 = single ? nullptr : static_cast<const TcMatrixMaps*>(maps2);
   a.lo = lo;
   a.hi = hi;
   a.total_rows = total_rows;
@@ -390,11 +411,11 @@ cudaError_t launch_small_rows(bool int8, const void* maps, const Q8View* single,
   a.y = y;
   a.ldy = ldy;
   a.status = status;
-  const dim3 grid(N / kSmRows, items ? max_items : chunks * groups);
+  const dim3 grid((N / kSmRows) * (y2 ? 2 : 1), items ? max_items : chunks * groups);
   if (int8)
-    small_rows_kernel<true><<<grid, kSmThreads, kSmSmemI, st>>>(tw, tws, tx, txs, a);
+    small_rows_kernel<true><<<grid, kSmThreads, kSmSmemI, st>>>(tw, tws, tx, txs, tw2, tws2, a);
   else
-    small_rows_kernel<false><<<grid, kSmThreads, kSmSmemF, st>>>(tw, tws, tx, txs, a);
+    small_rows_kernel<false><<<grid, kSmThreads, kSmSmemF, st>>>(tw, tws, tx, txs, tw2, tws2, a);
   return cudaGetLastError();
 }
 
