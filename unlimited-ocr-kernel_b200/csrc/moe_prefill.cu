@@ -124,29 +124,60 @@ __global__ void __launch_bounds__(kGroupThreads) group_pairs_kernel(
 
 // y[t] = shared_out[t] (already in y); then for t's experts in ascending id:
 // y[t] += p * out[pos] — src/decoder/mod.rs:208-217, one rounding per op.
-__global__ void combine_kernel(const int32_t* __restrict__ ids, const int* __restrict__ token_pos,
-                               const float* __restrict__ pair_weight,
-                               const float* __restrict__ out_routed, int tokens, int top_k,
-                               int hidden, float* __restrict__ y) {
+// Grid (tokens, column blocks); the top_k (<= 8) pairs sit in fixed-size
+// register arrays (unused slots sort last), a thread's loads of all pairs
+// are issued before its ordered sums.
+template <bool VEC4>
+__global__ void __launch_bounds__(128) combine_kernel(
+    const int32_t* __restrict__ ids, const int* __restrict__ token_pos,
+    const float* __restrict__ pair_weight, const float* __restrict__ out_routed, int tokens,
+    int top_k, int hidden, float* __restrict__ y) {
   const int t = blockIdx.x;
   if (t >= tokens) return;
   int e[8], pos[8];
   float w[8];
-  for (int j = 0; j < top_k; ++j) {
-    e[j] = ids[t * top_k + j];
-    pos[j] = token_pos[t * top_k + j];
-    w[j] = pair_weight[pos[j]];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const bool used = j < top_k;
+    e[j] = used ? ids[t * top_k + j] : 0x7fffffff;
+    pos[j] = used ? token_pos[t * top_k + j] : 0;
+    w[j] = used ? pair_weight[pos[j]] : 0.0f;
   }
-  for (int i = 1; i < top_k; ++i)
-    for (int j = i; j > 0 && e[j - 1] > e[j]; --j) {
-      int te = e[j]; e[j] = e[j - 1]; e[j - 1] = te;
-      int tp = pos[j]; pos[j] = pos[j - 1]; pos[j - 1] = tp;
-      float tw = w[j]; w[j] = w[j - 1]; w[j - 1] = tw;
-    }
-  for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
+#pragma unroll
+  for (int i = 1; i < 8; ++i)
+#pragma unroll
+    for (int j = i; j > 0; --j)
+      if (e[j - 1] > e[j]) {
+        const int te = e[j]; e[j] = e[j - 1]; e[j - 1] = te;
+        const int tp = pos[j]; pos[j] = pos[j - 1]; pos[j - 1] = tp;
+        const float tw = w[j]; w[j] = w[j - 1]; w[j - 1] = tw;
+      }
+  const int c = blockIdx.y * blockDim.x + threadIdx.x;
+  if (VEC4) {
+    if (4 * c >= hidden) return;
+    float4* yr = reinterpret_cast<float4*>(y + static_cast<long long>(t) * hidden) + c;
+    float4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j < top_k)
+        v[j] = reinterpret_cast<const float4*>(out_routed + static_cast<long long>(pos[j]) * hidden)[c];
+    float4 acc = *yr;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j < top_k) {
+        acc.x = __fadd_rn(acc.x, __fmul_rn(w[j], v[j].x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(w[j], v[j].y));
+        acc.z = __fadd_rn(acc.z, __fmul_rn(w[j], v[j].z));
+        acc.w = __fadd_rn(acc.w, __fmul_rn(w[j], v[j].w));
+      }
+    *yr = acc;
+  } else {
+    if (c >= hidden) return;
     float acc = y[static_cast<long long>(t) * hidden + c];
-    for (int j = 0; j < top_k; ++j)
-      acc = __fadd_rn(acc, __fmul_rn(w[j], out_routed[static_cast<long long>(pos[j]) * hidden + c]));
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j < top_k)
+        acc = __fadd_rn(acc, __fmul_rn(w[j], out_routed[static_cast<long long>(pos[j]) * hidden + c]));
     y[static_cast<long long>(t) * hidden + c] = acc;
   }
 }
@@ -893,8 +924,18 @@ cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaS
     if (a.pair_out)
       unpermute_kernel<<<T * k, 256, 0, st>>>(w.token_pos, w.out_r, T * k, a.hidden, a.pair_out);
     else
-      combine_kernel<<<T, 256, 0, st>>>(a.route_ids, w.token_pos, w.pair_weight, w.out_r, T, k,
-                                        a.hidden, a.y);
+    {
+      // float4 columns when rows stay 16-byte aligned
+      const bool v4 = a.hidden % 4 == 0 && reinterpret_cast<uintptr_t>(a.y) % 16 == 0;
+      const int cols = v4 ? a.hidden / 4 : a.hidden;
+      const dim3 grid(T, (cols + 127) / 128);
+      if (v4)
+        combine_kernel<true><<<grid, 128, 0, st>>>(a.route_ids, w.token_pos, w.pair_weight,
+                                                   w.out_r, T, k, a.hidden, a.y);
+      else
+        combine_kernel<false><<<grid, 128, 0, st>>>(a.route_ids, w.token_pos, w.pair_weight,
+                                                    w.out_r, T, k, a.hidden, a.y);
+    }
   }
   return cudaGetLastError();
 }
