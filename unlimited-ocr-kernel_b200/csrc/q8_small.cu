@@ -108,17 +108,19 @@ __device__ __forceinline__ void mma_s8_m16n8k32(int (&d)[4], uint32_t a0, uint32
 }
 
 // Four int8 (one word) -> four bf16 (two words), exact: each byte, offset to
-// u = v + 128, is placed under the exponent of 2^23; subtracting 2^23 + 128
-// leaves v, whose bf16 is the float's high half.
+// u = v + 128, is placed under the exponent of 2^23; adding -(2^23 + 128)
+// (two lanes per packed add) leaves v, whose bf16 is the float's high half.
 __device__ __forceinline__ uint2 i8x4_bf16(uint32_t w) {
   const uint32_t u = w ^ 0x80808080u;
-  const float magic = 8388736.0f;  // 2^23 + 128
-  const float f0 = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440)), magic);
-  const float f1 = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441)), magic);
-  const float f2 = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442)), magic);
-  const float f3 = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443)), magic);
-  return make_uint2(__byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632),
-                    __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632));
+  const float2 magic = make_float2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
+  const float2 a = f2_add(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440)),
+                                      __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441))),
+                          magic);
+  const float2 b = f2_add(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442)),
+                                      __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443))),
+                          magic);
+  return make_uint2(__byte_perm(__float_as_uint(a.x), __float_as_uint(a.y), 0x7632),
+                    __byte_perm(__float_as_uint(b.x), __float_as_uint(b.y), 0x7632));
 }
 
 template <bool INT8>
