@@ -461,7 +461,12 @@ __host__ __device__ inline size_t attn_tma_smem(int dim, long long max_tokens) {
          ((static_cast<size_t>(max_tokens) * 4 + 15) & ~static_cast<size_t>(15)) + 64;
 }
 
-__global__ void __launch_bounds__(64)
+// D128 (head dim 128): the consumer copies its part of a tile (its token's
+// key row, or its four output columns of the tile's 32 value rows: 128 floats
+// either way) into registers and frees the stage before computing on it, so
+// that both stages are in flight while it computes.
+template <bool D128>
+__global__ void __launch_bounds__(64, 5)
     attn_decode_tma_kernel(const __grid_constant__ CUtensorMap kmap,
                            const __grid_constant__ CUtensorMap vmap, const AttnArgs a) {
   extern __shared__ unsigned char smem_raw[];
@@ -530,7 +535,36 @@ __global__ void __launch_bounds__(64)
   }
   // ---- consumer: scores
   const float4* q4 = reinterpret_cast<const float4*>(qs);
-  for (int i = 0; i < ntiles; ++i) {
+  if (D128) {
+    for (int i = 0; i < ntiles; ++i) {
+      const int st = i & 1;
+      mbar_wait(&full[st], (i >> 1) & 1, a.status);
+      const unsigned char* row = base + st * stage_bytes + lane * 128;
+      float4 kr[32];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          kr[j * 8 + c] =
+              *reinterpret_cast<const float4*>(row + j * kTmaBoxBytes + ((c ^ (lane & 7)) << 4));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+      const int t = i * kTmaTile + lane;
+      if (t < T) {
+        float acc = -0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float4 qv = q4[j];
+          acc = __fadd_rn(acc, __fmul_rn(qv.x, kr[j].x));
+          acc = __fadd_rn(acc, __fmul_rn(qv.y, kr[j].y));
+          acc = __fadd_rn(acc, __fmul_rn(qv.z, kr[j].z));
+          acc = __fadd_rn(acc, __fmul_rn(qv.w, kr[j].w));
+        }
+        sc[t] = __fmul_rn(acc, a.scale);
+      }
+    }
+  }
+  for (int i = 0; !D128 && i < ntiles; ++i) {
     const int st = i & 1;
     mbar_wait(&full[st], (i >> 1) & 1, a.status);
     const int t = i * kTmaTile + lane;
@@ -590,7 +624,33 @@ __global__ void __launch_bounds__(64)
   const int chunks = dim / 4;
   float4 acc0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), acc1 = acc0;
   const int g0 = lane, g1 = lane + 32;
-  for (int i = 0; i < ntiles; ++i) {
+  if (D128) {
+    // chunks == 32: lane owns chunk g0 = lane, in box lane / 8
+    for (int i = 0; i < ntiles; ++i) {
+      const int it = ntiles + i, st = it & 1;
+      mbar_wait(&full[st], (it >> 1) & 1, a.status);
+      const unsigned char* tile = base + st * stage_bytes + (lane >> 3) * kTmaBoxBytes;
+      float4 vr[32];
+#pragma unroll
+      for (int r = 0; r < 32; ++r)
+        vr[r] = *reinterpret_cast<const float4*>(tile + r * 128 + (((lane & 7) ^ (r & 7)) << 4));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+      if (!bad) {
+        const int rows = T - i * kTmaTile < kTmaTile ? T - i * kTmaTile : kTmaTile;
+#pragma unroll
+        for (int r = 0; r < 32; ++r)
+          if (r < rows) {
+            const float p = sc[i * kTmaTile + r];
+            acc0.x = __fadd_rn(acc0.x, __fmul_rn(p, vr[r].x));
+            acc0.y = __fadd_rn(acc0.y, __fmul_rn(p, vr[r].y));
+            acc0.z = __fadd_rn(acc0.z, __fmul_rn(p, vr[r].z));
+            acc0.w = __fadd_rn(acc0.w, __fmul_rn(p, vr[r].w));
+          }
+      }
+    }
+  }
+  for (int i = 0; !D128 && i < ntiles; ++i) {
     const int it = ntiles + i, st = it & 1;
     mbar_wait(&full[st], (it >> 1) & 1, a.status);
     if (!bad) {
@@ -664,13 +724,18 @@ cudaError_t launch_attention_decode_tma(const AttnMaps& m, const AttnArgs& a, in
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(configured & (1u << (dev & 31)))) {
-    cudaFuncSetAttribute(attn_decode_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(kAttnMaxSmem));
+    cudaFuncSetAttribute(attn_decode_tma_kernel<false>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kAttnMaxSmem));
+    cudaFuncSetAttribute(attn_decode_tma_kernel<true>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kAttnMaxSmem));
     configured |= 1u << (dev & 31);
   }
   const CUtensorMap* km = reinterpret_cast<const CUtensorMap*>(m.k);
   const CUtensorMap* vm = reinterpret_cast<const CUtensorMap*>(m.v);
-  attn_decode_tma_kernel<<<dim3(a.heads, batch), 64, smem, st>>>(*km, *vm, a);
+  if (a.dim == 128)
+    attn_decode_tma_kernel<true><<<dim3(a.heads, batch), 64, smem, st>>>(*km, *vm, a);
+  else
+    attn_decode_tma_kernel<false><<<dim3(a.heads, batch), 64, smem, st>>>(*km, *vm, a);
   return cudaGetLastError();
 }
 
