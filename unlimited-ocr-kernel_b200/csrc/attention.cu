@@ -34,6 +34,25 @@
 
 namespace uocr {
 
+// Left-to-right sum from -0.0 of n floats in shared memory (16-byte aligned),
+// one thread: 16-byte loads, unrolled so that they run ahead of the chain of
+// dependent adds (the order, and so the result, is the sequential one).
+__device__ __forceinline__ float serial_sum_smem(const float* v, int n) {
+  float acc = -0.0f;
+  const float4* v4 = reinterpret_cast<const float4*>(v);
+  const int n4 = n >> 2;
+#pragma unroll 8
+  for (int i = 0; i < n4; ++i) {
+    const float4 c = v4[i];
+    acc = __fadd_rn(acc, c.x);
+    acc = __fadd_rn(acc, c.y);
+    acc = __fadd_rn(acc, c.z);
+    acc = __fadd_rn(acc, c.w);
+  }
+  for (int i = n4 << 2; i < n; ++i) acc = __fadd_rn(acc, v[i]);
+  return acc;
+}
+
 // ---- RMSNorm -----------------------------------------------------------------
 constexpr int kNormThreads = 256;
 
@@ -41,7 +60,7 @@ __global__ void __launch_bounds__(kNormThreads)
     rms_norm_kernel(const float* __restrict__ x, long long ld_x, int width,
                     const float* __restrict__ w, float eps, float* out, long long ld_out,
                     unsigned* status) {
-  extern __shared__ float sq[];  // width squares
+  extern __shared__ __align__(16) float sq[];  // width squares
   __shared__ float s_scale;
   const long long row = blockIdx.x;
   const float* xr = x + row * ld_x;
@@ -56,16 +75,7 @@ __global__ void __launch_bounds__(kNormThreads)
     return;
   }
   if (threadIdx.x == 0) {
-    float acc = -0.0f;
-    int i = 0;
-    for (; i + 8 <= width; i += 8) {
-      float v[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = sq[i + j];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, v[j]);
-    }
-    for (; i < width; ++i) acc = __fadd_rn(acc, sq[i]);
+    const float acc = serial_sum_smem(sq, width);
     const float var = __fdiv_rn(acc, static_cast<float>(width));
     s_scale = __frcp_rn(__fsqrt_rn(__fadd_rn(var, eps)));
   }
@@ -603,17 +613,7 @@ __global__ void __launch_bounds__(64, 5)
     for (int t = lane; t < T; t += 32) sc[t] = exp_f32_via_f64(__fsub_rn(sc[t], mx));
     __syncwarp();
     float sum = -0.0f;
-    if (lane == 0) {
-      int t = 0;
-      for (; t + 8 <= T; t += 8) {
-        float v[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = sc[t + j];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) sum = __fadd_rn(sum, v[j]);
-      }
-      for (; t < T; ++t) sum = __fadd_rn(sum, sc[t]);
-    }
+    if (lane == 0) sum = serial_sum_smem(sc, T);
     sum = __shfl_sync(0xffffffffu, sum, 0);
     for (int t = lane; t < T; t += 32) sc[t] = __fdiv_rn(sc[t], sum);
     __syncwarp();
