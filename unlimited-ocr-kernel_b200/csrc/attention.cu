@@ -385,19 +385,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   mx = s_max;
   for (int t = tid; t < T; t += kAttnThreads) sc[t] = exp_f32_via_f64(__fsub_rn(sc[t], mx));
   __syncthreads();
-  if (tid == 0) {
-    float acc = -0.0f;
-    int t = 0;
-    for (; t + 8 <= T; t += 8) {
-      float v[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = sc[t + j];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, v[j]);
-    }
-    for (; t < T; ++t) acc = __fadd_rn(acc, sc[t]);
-    s_sum = acc;
-  }
+  if (tid == 0) s_sum = serial_sum_smem(sc, T);
   __syncthreads();
   const float sum = s_sum;
   for (int t = tid; t < T; t += kAttnThreads) sc[t] = __fdiv_rn(sc[t], sum);
