@@ -261,6 +261,25 @@ def test_prefill_dynamic_single_row_groups_are_int8(ctx):
     assert bits_equal(out1.cpu().numpy(), out2.cpu().numpy())
 
 
+@pytest.mark.parametrize("mode", [0, 1, 2])
+@pytest.mark.parametrize("T,skew", [(24, False), (64, False), (64, True)])
+def test_decode_batch_groups(ctx, mode, T, skew):
+    """Up to 64 tokens every routed group runs on the warp-level kernel as
+    8-row chunks listed by the pair grouping, gate and up in one launch: groups
+    of several chunks, single-row groups and empty experts; with `skew` every
+    token picks expert 3 (one 64-row group of eight chunks)."""
+    rng = np.random.default_rng(1100 + 10 * T + mode + (5 if skew else 0))
+    layer, sh, ex = make_layer(ctx, rng, 256, 128, 256, 8, 2)
+    x = rng.standard_normal((T, 256)).astype(np.float32)
+    logits = rng.standard_normal((T, 8)).astype(np.float32)
+    logits[:, 6] -= 6.0  # expert 6 nearly empty
+    if skew:
+        logits[:, 3] += 8.0
+    y, ids, wts = layer.forward(x, logits, mode)
+    ref, ids_ref, wts_ref = oracle.experts(sh, ex, logits, x, 2, mode)
+    _check_layer(y, ref, ids, ids_ref, wts, wts_ref, mode == 2)
+
+
 @pytest.mark.parametrize("T", [2, 65, 150])
 def test_prefill_tensor_core_int8(ctx, T):
     """Int8 activations for every row on shapes the tensor-core path takes
