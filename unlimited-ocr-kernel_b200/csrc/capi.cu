@@ -479,7 +479,7 @@ static LinearPath linear_path(const uocr_q8* m, int mode, size_t batch) {
   const int rows = static_cast<int>(m->rows), cols = static_cast<int>(m->cols);
   if (batch < 2 || !aligned) return LinearPath::Gemv;
   // up to 16 rows, or up to 64 rows of a matrix small enough that its
-  // re-reads by the 16-row groups come from L2: the warp-level kernel
+  // re-reads by the 8-row chunks come from L2: the warp-level kernel
   const bool small_matrix = static_cast<size_t>(rows) * cols <= (size_t(16) << 20);
   if (batch <= static_cast<size_t>(kSmallRowsMax) || (batch <= 64 && small_matrix)) {
     if (small_rows_supported(rows, cols))

@@ -92,12 +92,16 @@ void launch_swiglu_quantize(const float* g, const float* u, int rows, int cols, 
                             float* hs, unsigned* status, int sms, cudaStream_t st);
 
 // q8_small.cu — grouped projections for groups of lo..hi rows (hi <=
-// kSmallChunkedMax; a group of more than 16 rows runs as 16-row chunks),
-// weights streamed once per chunk (TMA ring), warp-level MMAs over the rows.  int8: xq/xs rows (bit-exact linear_dynamic_int8);
-// FP32: pieces [3][piece_rows][K] + rinv (FP32 tolerance).  Grouped: maps =
-// the groups' q8_tc_weight_maps, rows [offsets[g], + counts[g]); single
-// (counts null): *single over rows [0, total_rows) in groups of 16.  x_rows:
-// rows of the int8 activation tensors.  N % 128 == 0, K % 128 == 0.
+// kSmallChunkedMax), as 8-row chunks, weights streamed once per chunk (TMA
+// ring), warp-level MMAs over the rows.  int8: xq/xs rows (bit-exact
+// linear_dynamic_int8); FP32: pieces [3][piece_rows][K] + rinv (FP32
+// tolerance).  Grouped: maps = the groups' q8_tc_weight_maps, rows
+// [offsets[g], + counts[g]); `items` (optional) lists the chunks to run
+// (group_pairs_kernel writes it; grid.y = max_items).  Single (counts null):
+// *single over rows [0, total_rows) in chunks of 8.  maps2 / single2 / y2
+// (optional): a second matrix of the same shape over the same rows (gate and
+// up in one launch).  x_rows: rows of the int8 activation tensors.
+// N % 128 == 0, K % 128 == 0.
 constexpr int kSmallRowsMax = 16;
 // Grouped launches may take groups of up to this many rows, as 8-row chunks
 // (one CTA each, the group's weights re-read from L2).

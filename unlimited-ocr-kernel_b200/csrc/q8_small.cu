@@ -1,4 +1,4 @@
-// q8_small.cu — grouped projections for groups of at most 16 rows.
+// q8_small.cu — grouped projections for groups of a few rows (up to 64).
 //
 // A MoE layer at decode batch sizes gives each expert a handful of rows
 // (config 4: 64 tokens x top-6 over 64 experts, about 6 rows per expert).
