@@ -226,6 +226,9 @@ int uocr_ctx_create(int device, size_t scratch_limit, uocr_ctx** out) {
   if (e == cudaSuccess) e = cudaMalloc(&c->status_dev, 256);
   if (e == cudaSuccess) e = cudaMemset(c->status_dev, 0, 256);
   if (e == cudaSuccess) e = cudaMallocHost(&c->status_host, sizeof(unsigned) * 4);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->side_stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming);
   if (e != cudaSuccess) {
     uocr_ctx_destroy(c);
     return fail(UOCR_ERR_CUDA, "context: %s", cudaGetErrorString(e));
@@ -242,6 +245,12 @@ int uocr_ctx_destroy(uocr_ctx* ctx) {
   for (auto& hg : ctx->host_graphs)
     if (hg.exec) cudaGraphExecDestroy(hg.exec);
   if (ctx->capture_stream) cudaStreamDestroy(ctx->capture_stream);
+  if (ctx->side_stream) {
+    cudaStreamSynchronize(ctx->side_stream);
+    cudaStreamDestroy(ctx->side_stream);
+  }
+  if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);
+  if (ctx->ev_join) cudaEventDestroy(ctx->ev_join);
   if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->io) cudaFree(ctx->io);
   if (ctx->pinned) cudaFreeHost(ctx->pinned);
@@ -909,6 +918,9 @@ static int moe_run(uocr_ctx* ctx, const uocr_moe* L, int mode, const float* x, c
   }
   a.workspace = base;
   a.workspace_bytes = ctx->ws_bytes - (base - static_cast<char*>(ctx->ws));
+  a.side = ctx->side_stream;
+  a.ev_fork = ctx->ev_fork;
+  a.ev_join = ctx->ev_join;
   cudaError_t e = launch_moe_prefill(mode, a, ctx->sms, ctx->stream);
   if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "moe prefill launch: %s", cudaGetErrorString(e));
   return check_launch();

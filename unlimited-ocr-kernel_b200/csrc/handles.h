@@ -40,6 +40,10 @@ struct uocr_ctx {
   size_t io_bytes = 0;
   std::vector<HostDecodeGraph> host_graphs;  // at most kMaxHostGraphs, oldest replaced
   cudaStream_t capture_stream = nullptr;
+  // a second stream for independent work inside one call (the shared expert
+  // next to the routed ones), forked and joined through the two events
+  cudaStream_t side_stream = nullptr;
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
 };
 
 struct uocr_q8 {

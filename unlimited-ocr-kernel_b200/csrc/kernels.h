@@ -174,6 +174,12 @@ struct MoePrefillArgs {
   int route_given, skip_shared, skip_routed;
   float* pair_out;
   int skip_negative_ids;  // route_given: a negative id marks an unused row
+  // optional: a second stream and two events; up to kSmallChunkedMax tokens
+  // the shared expert then runs on `side` next to the routing and the routed
+  // experts (forked after the activations are quantized, joined before the
+  // combine)
+  cudaStream_t side;
+  cudaEvent_t ev_fork, ev_join;
 };
 size_t moe_prefill_workspace(const MoePrefillArgs& a, int mode);
 cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaStream_t st);

@@ -858,6 +858,30 @@ cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaS
   PrefillWs w = carve(a, a.workspace, path);
   if (w.bytes > a.workspace_bytes) return cudaErrorInvalidValue;
   const int T = a.tokens, k = a.top_k, E = a.n_experts;
+  if (mode != 0) launch_quantize_rows(a.x, a.hidden, T, a.hidden, w.xq, w.xs, a.status, sms, st);
+  // the shared expert needs only x: on the side stream, next to the routing
+  // and the routed experts, when both parts run on the warp-level kernel
+  const bool fork = a.side && a.ev_fork && a.ev_join && !a.skip_shared && !a.skip_routed &&
+                    !a.pair_out && path != Path::CudaCore && T <= kSmallShared &&
+                    T <= kSmallChunkedMax;
+  auto run_path = [&](const MoePrefillArgs& pa, cudaStream_t s) {
+    return path == Path::TcInt8   ? prefill_tc(pa, w, sms, s)
+           : path == Path::TcFp32 ? prefill_tc_f32(pa, w, sms, s)
+                                  : prefill_tc_mixed(pa, w, sms, s);
+  };
+  if (fork) {
+    MoePrefillArgs shared_only = a;
+    shared_only.skip_routed = 1;
+    cudaError_t e = cudaEventRecord(a.ev_fork, st);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(a.side, a.ev_fork, 0);
+    if (e != cudaSuccess) return e;
+    e = run_path(shared_only, a.side);
+    const cudaError_t ej = cudaEventRecord(a.ev_join, a.side);
+    if (e != cudaSuccess || ej != cudaSuccess) {
+      cudaStreamWaitEvent(st, a.ev_join, 0);
+      return e != cudaSuccess ? e : ej;
+    }
+  }
   if (!a.skip_routed) {
     if (!a.route_given)
       launch_route(a.logits, T, E, k, a.normalize, a.scale, a.route_ids, a.route_weights,
@@ -868,7 +892,6 @@ cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaS
                                                    T <= kSmallChunkedMax ? w.items : nullptr,
                                                    a.status);
   }
-  if (mode != 0) launch_quantize_rows(a.x, a.hidden, T, a.hidden, w.xq, w.xs, a.status, sms, st);
   if (a.skip_negative_ids && !a.skip_routed) {
     // unused rows belong to no group and are never written by the projections:
     // zero them so that the SwiGLU and quantization passes over all rows see 0
@@ -876,7 +899,14 @@ cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaS
     cudaMemsetAsync(w.h_r, 0, hb, st);
     if (w.u_r) cudaMemsetAsync(w.u_r, 0, hb, st);
   }
-  if (path != Path::CudaCore) {
+  if (fork) {
+    MoePrefillArgs routed_only = a;
+    routed_only.skip_shared = 1;
+    const cudaError_t e = run_path(routed_only, st);
+    const cudaError_t ej = cudaStreamWaitEvent(st, a.ev_join, 0);  // y holds the shared part
+    if (e != cudaSuccess) return e;
+    if (ej != cudaSuccess) return ej;
+  } else if (path != Path::CudaCore) {
     const cudaError_t e = path == Path::TcInt8   ? prefill_tc(a, w, sms, st)
                           : path == Path::TcFp32 ? prefill_tc_f32(a, w, sms, st)
                                                  : prefill_tc_mixed(a, w, sms, st);
