@@ -660,6 +660,16 @@ static void launch_big_counts(const int* counts, int groups, int* counts_big, cu
   big_counts_kernel<<<1, 256, 0, st>>>(counts, groups, counts_big);
 }
 
+// Upper bound on the 64-row tiles of the groups the tensor-core GEMMs take
+// (more than kSmallRowsMax rows each, so at most P / (kSmallRowsMax + 1) of
+// them): sum over those groups of ceil(count / 64) <= P / 64 + their number.
+// The grid has a slot per possible tile; a tight bound keeps the slots that
+// find no tile (every one, at decode batch sizes) few.
+static int big_group_tiles(int P, int E) {
+  const int groups = P / (kSmallRowsMax + 1) < E ? P / (kSmallRowsMax + 1) : E;
+  return P / 64 + groups + 1;
+}
+
 // The shared expert over T <= kSmallShared tokens with FP32 activations, as
 // chunks of 8 rows on the warp-level kernel (the tokens' pieces are in
 // w.xp_s / w.xr_s); its down projection writes y.
@@ -683,7 +693,7 @@ static cudaError_t prefill_tc_f32(const MoePrefillArgs& a, const PrefillWs& w, i
                                   cudaStream_t st) {
   const int T = a.tokens, k = a.top_k, E = a.n_experts, P = T * k;
   const int H = a.hidden, F = a.width, FS = a.shared_width;
-  const int max_tiles = P / 64 + E + 1;
+  const int max_tiles = big_group_tiles(P, E);
   const unsigned char* maps = static_cast<const unsigned char*>(a.tc_maps);
   const size_t mb = q8_tc_maps_bytes();
   cudaError_t e;
@@ -729,7 +739,7 @@ static cudaError_t prefill_tc_f32(const MoePrefillArgs& a, const PrefillWs& w, i
 static cudaError_t prefill_tc(const MoePrefillArgs& a, const PrefillWs& w, int sms, cudaStream_t st) {
   const int T = a.tokens, k = a.top_k, E = a.n_experts, P = T * k;
   const int H = a.hidden, F = a.width, FS = a.shared_width;
-  const int max_tiles = P / 64 + E + 1;  // sum over experts of ceil(count / 64)
+  const int max_tiles = big_group_tiles(P, E);
   const unsigned char* maps = static_cast<const unsigned char*>(a.tc_maps);
   const size_t mb = q8_tc_maps_bytes();  // per matrix
   cudaError_t e;
@@ -790,7 +800,7 @@ static cudaError_t prefill_tc_mixed(const MoePrefillArgs& a, const PrefillWs& w,
                                     cudaStream_t st) {
   const int T = a.tokens, k = a.top_k, E = a.n_experts, P = T * k;
   const int H = a.hidden, F = a.width, FS = a.shared_width;
-  const int max_tiles = P / 64 + E + 1;
+  const int max_tiles = big_group_tiles(P, E);
   const unsigned char* maps = static_cast<const unsigned char*>(a.tc_maps);
   const size_t mb = q8_tc_maps_bytes();
   const bool tc = T > kSmallChunkedMax;
