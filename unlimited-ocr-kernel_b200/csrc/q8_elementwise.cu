@@ -210,6 +210,27 @@ __global__ void __launch_bounds__(kBf16Threads)
   const float* xr = xs + b * kx;
   float acc = -0.0f;
   int c = 0;
+  if (bulk) {
+    // k % 8 == 0 and 16-byte aligned rows: one 16-byte load of eight weights
+    // and two of x per eight products (the padded strides keep a warp's rows
+    // on distinct banks); the products and sums in the same order
+    const uint4* w4 = reinterpret_cast<const uint4*>(wr);
+    const float4* x4 = reinterpret_cast<const float4*>(xr);
+#pragma unroll 4
+    for (int c8 = 0; c8 < (k >> 3); ++c8) {
+      const uint4 wv = w4[c8];
+      const float4 xa = x4[2 * c8], xb = x4[2 * c8 + 1];
+      acc = __fadd_rn(acc, __fmul_rn(__uint_as_float(wv.x << 16), xa.x));
+      acc = __fadd_rn(acc, __fmul_rn(__uint_as_float(wv.x & 0xffff0000u), xa.y));
+      acc = __fadd_rn(acc, __fmul_rn(__uint_as_float(wv.y << 16), xa.z));
+      acc = __fadd_rn(acc, __fmul_rn(__uint_as_float(wv.y & 0xffff0000u), xa.w));
+      acc = __fadd_rn(acc, __fmul_rn(__uint_as_float(wv.z << 16), xb.x));
+      acc = __fadd_rn(acc, __fmul_rn(__uint_as_float(wv.z & 0xffff0000u), xb.y));
+      acc = __fadd_rn(acc, __fmul_rn(__uint_as_float(wv.w << 16), xb.z));
+      acc = __fadd_rn(acc, __fmul_rn(__uint_as_float(wv.w & 0xffff0000u), xb.w));
+    }
+    c = k;
+  }
   for (; c + 8 <= k; c += 8) {
     float wv[8], xv[8];
 #pragma unroll
