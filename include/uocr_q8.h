@@ -171,10 +171,11 @@ int uocr_moe_free(uocr_moe *layer);
 /* One MoE FFN over `tokens` rows: x_dev tokens*hidden, router logits
  * tokens*n_experts, y_dev tokens*hidden.  ids/weights (optional, may be
  * NULL) receive each token's routing.  mode: uocr_mode.  Asynchronous.
- * Between 2 and 64 tokens the shared expert runs on a second stream owned by
- * the context, forked from and joined back into the context's stream within
- * the call (events), so the call stays ordered on that stream and can be
- * captured in a CUDA graph. */
+ * Between 2 and 64 tokens the routing and the routed experts run on a second,
+ * high-priority stream owned by the context while the shared expert runs on
+ * the context's stream; the second stream is forked from and joined back into
+ * the context's stream within the call (events), so the call stays ordered on
+ * that stream and can be captured in a CUDA graph. */
 int uocr_moe_forward(uocr_ctx *ctx, const uocr_moe *layer, int mode, const float *x_dev,
                      const float *logits_dev, size_t tokens, float *y_dev, int32_t *ids_dev,
                      float *weights_dev);

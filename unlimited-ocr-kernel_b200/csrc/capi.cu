@@ -226,7 +226,10 @@ int uocr_ctx_create(int device, size_t scratch_limit, uocr_ctx** out) {
   if (e == cudaSuccess) e = cudaMalloc(&c->status_dev, 256);
   if (e == cudaSuccess) e = cudaMemset(c->status_dev, 0, 256);
   if (e == cudaSuccess) e = cudaMallocHost(&c->status_host, sizeof(unsigned) * 4);
-  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->side_stream, cudaStreamNonBlocking);
+  int least_priority = 0, greatest_priority = 0;
+  if (e == cudaSuccess) e = cudaDeviceGetStreamPriorityRange(&least_priority, &greatest_priority);
+  if (e == cudaSuccess)
+    e = cudaStreamCreateWithPriority(&c->side_stream, cudaStreamNonBlocking, greatest_priority);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming);
   if (e != cudaSuccess) {

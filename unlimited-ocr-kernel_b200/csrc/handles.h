@@ -40,8 +40,9 @@ struct uocr_ctx {
   size_t io_bytes = 0;
   std::vector<HostDecodeGraph> host_graphs;  // at most kMaxHostGraphs, oldest replaced
   cudaStream_t capture_stream = nullptr;
-  // a second stream for independent work inside one call (the shared expert
-  // next to the routed ones), forked and joined through the two events
+  // a second stream, of the highest priority, for the critical chain of a call
+  // that forks (the routing and the routed experts, while the shared expert
+  // runs on `stream`), forked and joined through the two events
   cudaStream_t side_stream = nullptr;
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
 };

@@ -174,10 +174,10 @@ struct MoePrefillArgs {
   int route_given, skip_shared, skip_routed;
   float* pair_out;
   int skip_negative_ids;  // route_given: a negative id marks an unused row
-  // optional: a second stream and two events; up to kSmallChunkedMax tokens
-  // the shared expert then runs on `side` next to the routing and the routed
-  // experts (forked after the activations are quantized, joined before the
-  // combine)
+  // optional: a second stream (of high priority) and two events; up to
+  // kSmallChunkedMax tokens the routing and the routed experts then run on
+  // `side` while the shared expert runs on the call's stream (forked after the
+  // activations are quantized, joined before the combine)
   cudaStream_t side;
   cudaEvent_t ev_fork, ev_join;
 };

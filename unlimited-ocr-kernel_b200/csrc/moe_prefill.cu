@@ -869,34 +869,28 @@ cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaS
   if (w.bytes > a.workspace_bytes) return cudaErrorInvalidValue;
   const int T = a.tokens, k = a.top_k, E = a.n_experts;
   if (mode != 0) launch_quantize_rows(a.x, a.hidden, T, a.hidden, w.xq, w.xs, a.status, sms, st);
-  // the shared expert needs only x: on the side stream, next to the routing
-  // and the routed experts, when both parts run on the warp-level kernel
+  // the shared expert needs only x: it runs on the call's stream while the
+  // routing and the routed experts (the longer chain) run on the high-priority
+  // side stream, when both parts run on the warp-level kernel
   const bool fork = a.side && a.ev_fork && a.ev_join && !a.skip_shared && !a.skip_routed &&
-                    !a.pair_out && path != Path::CudaCore && T <= kSmallShared &&
-                    T <= kSmallChunkedMax;
+                    !a.pair_out && !a.skip_negative_ids && path != Path::CudaCore &&
+                    T <= kSmallShared && T <= kSmallChunkedMax;
   auto run_path = [&](const MoePrefillArgs& pa, cudaStream_t s) {
     return path == Path::TcInt8   ? prefill_tc(pa, w, sms, s)
            : path == Path::TcFp32 ? prefill_tc_f32(pa, w, sms, s)
                                   : prefill_tc_mixed(pa, w, sms, s);
   };
+  const cudaStream_t rs = fork ? a.side : st;  // the routed chain's stream
   if (fork) {
-    MoePrefillArgs shared_only = a;
-    shared_only.skip_routed = 1;
     cudaError_t e = cudaEventRecord(a.ev_fork, st);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(a.side, a.ev_fork, 0);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(rs, a.ev_fork, 0);
     if (e != cudaSuccess) return e;
-    e = run_path(shared_only, a.side);
-    const cudaError_t ej = cudaEventRecord(a.ev_join, a.side);
-    if (e != cudaSuccess || ej != cudaSuccess) {
-      cudaStreamWaitEvent(st, a.ev_join, 0);
-      return e != cudaSuccess ? e : ej;
-    }
   }
   if (!a.skip_routed) {
     if (!a.route_given)
       launch_route(a.logits, T, E, k, a.normalize, a.scale, a.route_ids, a.route_weights,
-                   a.status, sms, st);
-    group_pairs_kernel<<<1, kGroupThreads, 0, st>>>(a.route_ids, a.route_weights, T, k, E,
+                   a.status, sms, rs);
+    group_pairs_kernel<<<1, kGroupThreads, 0, rs>>>(a.route_ids, a.route_weights, T, k, E,
                                                    a.skip_negative_ids, w.counts, w.offsets,
                                                    w.pair_token, w.pair_weight, w.token_pos,
                                                    T <= kSmallChunkedMax ? w.items : nullptr,
@@ -910,12 +904,15 @@ cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaS
     if (w.u_r) cudaMemsetAsync(w.u_r, 0, hb, st);
   }
   if (fork) {
-    MoePrefillArgs routed_only = a;
+    MoePrefillArgs routed_only = a, shared_only = a;
     routed_only.skip_shared = 1;
-    const cudaError_t e = run_path(routed_only, st);
-    const cudaError_t ej = cudaStreamWaitEvent(st, a.ev_join, 0);  // y holds the shared part
+    shared_only.skip_routed = 1;
+    cudaError_t e = run_path(routed_only, rs);
+    const cudaError_t ej = cudaEventRecord(a.ev_join, rs);
+    const cudaError_t es = e == cudaSuccess ? run_path(shared_only, st) : cudaSuccess;
+    const cudaError_t ew = cudaStreamWaitEvent(st, a.ev_join, 0);  // the routed outputs
+    if (e == cudaSuccess) e = ej != cudaSuccess ? ej : es != cudaSuccess ? es : ew;
     if (e != cudaSuccess) return e;
-    if (ej != cudaSuccess) return ej;
   } else if (path != Path::CudaCore) {
     const cudaError_t e = path == Path::TcInt8   ? prefill_tc(a, w, sms, st)
                           : path == Path::TcFp32 ? prefill_tc_f32(a, w, sms, st)
