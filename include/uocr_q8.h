@@ -288,6 +288,15 @@ typedef struct uocr_kv uocr_kv;
  * positive; Numerical ("normalization") for a nonfinite input or weight. */
 int uocr_rms_norm(uocr_ctx *ctx, const float *x_dev, size_t rows, size_t width,
                   const float *weight_dev, float eps, float *out_dev);
+/* The residual add of Decoder::layer (src/decoder/mod.rs:348-349, 361-362)
+ * fused with the RMSNorm that follows it (:355, or the next layer's input
+ * norm): sum = x + res elementwise (one rounding each; sum may equal x or
+ * res), out = rms_norm(sum), bit-identical to the add followed by
+ * uocr_rms_norm.  No reference entry point of its own; errors as
+ * uocr_rms_norm. */
+int uocr_add_rms_norm(uocr_ctx *ctx, const float *x_dev, const float *res_dev, size_t rows,
+                      size_t width, const float *weight_dev, float eps, float *sum_dev,
+                      float *out_dev);
 
 /* ops::rope (src/cpu/ops.rs:423-437): a table of cos/sin for positions
  * [0, max_positions), built on the host with the reference's single-precision

@@ -68,6 +68,35 @@ def test_rms_norm_errors(ctx):
     assert e.value.kind == "Shape"
 
 
+@pytest.mark.parametrize("alias", ["none", "x", "res"])
+@pytest.mark.parametrize("rows,width", [(64, 1280), (3, 7)])
+def test_add_rms_norm_equals_add_then_norm(ctx, alias, rows, width):
+    """uocr_add_rms_norm: the residual sum bit for bit as x + res (one
+    rounding), the output as rms_norm of it (the oracle's), with the sum
+    written to a separate buffer or over either input."""
+    rng = np.random.default_rng(rows + width + len(alias))
+    x = (rng.standard_normal((rows, width)) * 3).astype(np.float32)
+    r = (rng.standard_normal((rows, width)) * 2).astype(np.float32)
+    w = rng.uniform(-2, 2, width).astype(np.float32)
+    xt, rt = dev(x), dev(r)
+    st = {"none": None, "x": xt, "res": rt}[alias]
+    out = A().add_rms_norm_device(ctx, xt, rt, dev(w), 1e-6, sum_t=st)
+    ctx.sync()
+    s_ref = (x + r).astype(np.float32)
+    if st is not None:
+        assert bits_equal(host(st), s_ref)
+    assert bits_equal(host(out), oracle.rms_norm(s_ref, w, 1e-6))
+
+
+def test_add_rms_norm_errors(ctx):
+    import uocr_q8
+    x = np.full((2, 8), 3e38, np.float32)  # the sum overflows: a nonfinite norm input
+    A().add_rms_norm_device(ctx, dev(x), dev(x), dev(np.ones(8, np.float32)))
+    with pytest.raises(uocr_q8.OcrError) as e:
+        ctx.sync()
+    assert e.value.kind == "Numerical"
+
+
 # ---------------------------------------------------------------- rope
 def test_rope_known_answer(ctx):
     r = A().Rope(ctx, 4, 10000.0, 16)

@@ -57,16 +57,25 @@ __device__ __forceinline__ float serial_sum_smem(const float* v, int n) {
 constexpr int kNormThreads = 256;
 
 __global__ void __launch_bounds__(kNormThreads)
-    rms_norm_kernel(const float* __restrict__ x, long long ld_x, int width,
-                    const float* __restrict__ w, float eps, float* out, long long ld_out,
+    rms_norm_kernel(const float* x, long long ld_x, int width, const float* __restrict__ w,
+                    float eps, float* out, long long ld_out, const float* res, float* sum,
                     unsigned* status) {
   extern __shared__ __align__(16) float sq[];  // width squares
   __shared__ float s_scale;
   const long long row = blockIdx.x;
   const float* xr = x + row * ld_x;
+  // with a residual: the row normalised is sum = x + res (one rounding),
+  // written to `sum` (which may alias x or res: each element is read and
+  // written by the same thread)
+  const float* rr = res ? res + row * ld_x : nullptr;
+  float* sr = res ? sum + row * ld_x : nullptr;
   bool bad = false;
   for (int i = threadIdx.x; i < width; i += blockDim.x) {
-    const float v = xr[i];
+    float v = xr[i];
+    if (rr) {
+      v = __fadd_rn(v, rr[i]);
+      sr[i] = v;
+    }
     bad |= !isfinite(v) || !isfinite(w[i]);
     sq[i] = __fmul_rn(v, v);
   }
@@ -82,12 +91,14 @@ __global__ void __launch_bounds__(kNormThreads)
   __syncthreads();
   const float scale = s_scale;
   float* o = out + row * ld_out;
+  const float* src = sr ? sr : xr;  // this thread's own writes of `sum`
   for (int i = threadIdx.x; i < width; i += blockDim.x)
-    o[i] = __fadd_rn(__fmul_rn(__fmul_rn(xr[i], scale), w[i]), 0.0f);
+    o[i] = __fadd_rn(__fmul_rn(__fmul_rn(src[i], scale), w[i]), 0.0f);
 }
 
 void launch_rms_norm(const float* x, long long ld_x, int rows, int width, const float* w, float eps,
-                     float* out, long long ld_out, unsigned* status, cudaStream_t st) {
+                     float* out, long long ld_out, unsigned* status, cudaStream_t st,
+                     const float* res, float* sum) {
   if (rows <= 0) return;
   const size_t smem = static_cast<size_t>(width) * 4;
   static unsigned configured = 0;
@@ -97,7 +108,8 @@ void launch_rms_norm(const float* x, long long ld_x, int rows, int width, const 
     cudaFuncSetAttribute(rms_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     configured |= 1u << (dev & 31);
   }
-  rms_norm_kernel<<<rows, kNormThreads, smem, st>>>(x, ld_x, width, w, eps, out, ld_out, status);
+  rms_norm_kernel<<<rows, kNormThreads, smem, st>>>(x, ld_x, width, w, eps, out, ld_out, res, sum,
+                                                    status);
 }
 
 // ---- rotary embedding ---------------------------------------------------------

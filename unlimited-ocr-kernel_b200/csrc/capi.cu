@@ -1329,6 +1329,29 @@ int uocr_rms_norm(uocr_ctx* ctx, const float* x_dev, size_t rows, size_t width,
   return check_launch();
 }
 
+// The residual adds of Decoder::layer (src/decoder/mod.rs:348-349, attention
+// output + x; :361-362, + the FFN output) and the RMSNorm of the result that
+// follows (:355, or the next layer's input norm) in one launch:
+// sum = x + res (one rounding per element; sum may alias x or res), then
+// out = rms_norm(sum), each bit-identical to the two separate operations.
+int uocr_add_rms_norm(uocr_ctx* ctx, const float* x_dev, const float* res_dev, size_t rows,
+                      size_t width, const float* weight_dev, float eps, float* sum_dev,
+                      float* out_dev) {
+  if (!ctx) return fail(UOCR_ERR_INVALID, "null context");
+  if (width == 0 || !std::isfinite(eps) || eps <= 0.0f)
+    return fail(UOCR_ERR_SHAPE, "invalid tensor shape: invalid normalization parameters");
+  if (rows == 0) return ok();
+  if (!x_dev || !res_dev || !weight_dev || !sum_dev || !out_dev)
+    return fail(UOCR_ERR_INVALID, "null argument");
+  if (!fits_int(rows) || width > 50000)
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: normalization extent");
+  DeviceGuard g(ctx->device);
+  launch_rms_norm(x_dev, static_cast<long long>(width), static_cast<int>(rows),
+                  static_cast<int>(width), weight_dev, eps, out_dev, static_cast<long long>(width),
+                  ctx->status_dev, ctx->stream, res_dev, sum_dev);
+  return check_launch();
+}
+
 // ops::rope (src/cpu/ops.rs:423-437): the (cos, sin) table of positions
 // [0, max_positions) for one head dimension and base.
 int uocr_rope_create(uocr_ctx* ctx, size_t head_dim, float theta, size_t max_positions,

@@ -204,8 +204,11 @@ void launch_moe_combine_pairs(const int32_t* ids, const float* weights, const fl
 
 // attention.cu — decode-side attention ops (RMSNorm, rope, KV cache,
 // single-query attention), in the reference's arithmetic order.
+// res (optional): normalise sum = x + res instead, written to `sum` (rows of
+// ld_x; sum may alias x or res).
 void launch_rms_norm(const float* x, long long ld_x, int rows, int width, const float* w, float eps,
-                     float* out, long long ld_out, unsigned* status, cudaStream_t st);
+                     float* out, long long ld_out, unsigned* status, cudaStream_t st,
+                     const float* res = nullptr, float* sum = nullptr);
 // table: [max_pos][dim/2] (cos, sin); positions (device, per row) or, when
 // null, the cache state {prefix, generated} per row.  b may be null.
 void launch_rope(float* a, float* b, long long ld, int rows, int heads, int dim,

@@ -63,6 +63,7 @@ SIGNATURES = {
     "uocr_feed_forward": (I, [P, P, P, P, I, P, S, P]),
     "uocr_linear_bf16": (I, [P, P, S, S, P, S, P]),
     "uocr_rms_norm": (I, [P, P, S, S, P, F, P]),
+    "uocr_add_rms_norm": (I, [P, P, P, S, S, P, F, P, P]),
     "uocr_rope_create": (I, [P, S, F, S, PP]),
     "uocr_rope_free": (I, [P]),
     "uocr_rope_apply": (I, [P, P, P, P, S, S, P]),

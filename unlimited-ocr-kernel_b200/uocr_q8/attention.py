@@ -35,6 +35,19 @@ def rms_norm_device(ctx: GpuContext, x_t, weight_t, eps: float = 1e-6, out_t=Non
     return out_t
 
 
+def add_rms_norm_device(ctx: GpuContext, x_t, res_t, weight_t, eps: float = 1e-6, sum_t=None,
+                        out_t=None):
+    """sum = x + res (into sum_t, which may be x_t or res_t), then the RMSNorm
+    of sum into out_t, in one launch (uocr_add_rms_norm).  Returns out_t."""
+    import torch
+    width = x_t.shape[-1]
+    sum_t = sum_t if sum_t is not None else torch.empty_like(x_t)
+    out_t = out_t if out_t is not None else torch.empty_like(x_t)
+    _check(lib().uocr_add_rms_norm(ctx.handle, _p(x_t), _p(res_t), x_t.numel() // max(width, 1),
+                                   width, _p(weight_t), float(eps), _p(sum_t), _p(out_t)))
+    return out_t
+
+
 def attention_decode_device(ctx: GpuContext, q_t, keys_t, values_t, heads: int, out_t=None):
     """One query [width] over token-major keys/values [tokens x width]."""
     import torch
@@ -174,4 +187,5 @@ class AttentionBlock:
         return out_t
 
 
-__all__ = ["rms_norm_device", "attention_decode_device", "Rope", "KvCache", "AttentionBlock"]
+__all__ = ["rms_norm_device", "add_rms_norm_device", "attention_decode_device", "Rope", "KvCache",
+           "AttentionBlock"]

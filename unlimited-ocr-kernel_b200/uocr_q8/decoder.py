@@ -29,7 +29,7 @@ from typing import List, Optional
 import numpy as np
 
 from . import (GpuContext, Int8Matrix, MoeLayer, QuantizationMode, _check, _tptr, lib)
-from .attention import KvCache, Rope, rms_norm_device
+from .attention import KvCache, Rope, add_rms_norm_device, rms_norm_device
 
 
 @dataclass
@@ -201,22 +201,26 @@ def decode_step(decoder: Decoder, state: DecodeState, tokens_t, mode: int = 0, l
     lin_mode = QuantizationMode.DYNAMIC_ROWWISE if rowwise else QuantizationMode.WEIGHTS_ONLY
     H = cfg.hidden
     x = decoder.embedding.index_select(0, tokens_t).float()
+    y = None  # the previous layer's FFN output, added to x before the next norm
     for layer, cache in zip(decoder.layers, state.caches):
-        # attention half of Decoder::layer (src/decoder/mod.rs:266-347)
-        n = rms_norm_device(ctx, x, layer.input_norm, cfg.eps)
+        # attention half of Decoder::layer (src/decoder/mod.rs:266-347); each
+        # residual add runs fused with the RMSNorm of its sum
+        if y is None:
+            n = rms_norm_device(ctx, x, layer.input_norm, cfg.eps)
+        else:
+            n = add_rms_norm_device(ctx, x, y, layer.input_norm, cfg.eps, sum_t=x)
         qkv = layer.qkv.linear_device(n, dynamic=rowwise)
         q = cache.rope_push_qkv(state.rope, qkv)  # rope of q, k; push of k, v
         a = cache.attention(q)
         r = layer.o.linear_device(a, dynamic=rowwise)
-        r += x
-        n = rms_norm_device(ctx, r, layer.post_norm, cfg.eps)
+        n = add_rms_norm_device(ctx, r, x, layer.post_norm, cfg.eps, sum_t=r)  # r += x
         if layer.moe is not None:
             logits = linear_bf16_device(ctx, layer.router, n)
             y = layer.moe.forward_device(n, logits, lin_mode)
         else:
             y = feed_forward_device(ctx, *layer.dense, n, lin_mode)
-        x = r.add_(y)
-    h = rms_norm_device(ctx, x, decoder.final_norm, cfg.eps)
+        x = r  # x + y is formed by the next norm
+    h = add_rms_norm_device(ctx, x, y, decoder.final_norm, cfg.eps, sum_t=x)
     if isinstance(decoder.lm_head, Int8Matrix):
         return decoder.lm_head.linear_device(h, logits_t, dynamic=rowwise)
     out = torch.matmul(h, decoder.lm_head.t())  # BF16 head: a library GEMM over its f32 copy
