@@ -135,9 +135,12 @@ def test_linear_reference_tolerance(ctx, cols):
 
 
 @pytest.mark.parametrize("rows,cols", [(896, 1280), (1280, 896), (1792, 1280), (1280, 1792),
-                                       (129, 1280), (6, 128), (37, 513), (1000, 6848)])
+                                       (129, 1280), (6, 128), (37, 513), (1000, 6848),
+                                       (64, 6144), (32, 8192)])
 @pytest.mark.parametrize("batch", [1, 4])
 def test_linear_vs_oracle(ctx, rows, cols, batch):
+    """(64, 6144) and (32, 8192): rows too wide for the streaming kernel's ring
+    in shared memory take the generic kernel at batch 1."""
     rng = np.random.default_rng(rows * 7 + cols + batch)
     w, s = random_q8(rng, rows, cols)
     x = rng.standard_normal((batch, cols)).astype(np.float32)
@@ -201,7 +204,7 @@ def test_dynamic_reference_tolerance_and_bits(ctx, cols):
 
 
 @pytest.mark.parametrize("rows,cols", [(896, 1280), (1280, 896), (3840, 1280), (1280, 1792),
-                                       (64, 6848), (33, 100), (4, 32)])
+                                       (64, 6848), (33, 100), (4, 32), (64, 6144), (32, 8192)])
 def test_dynamic_bit_exact(ctx, rows, cols):
     rng = np.random.default_rng(rows + 3 * cols)
     w, s = random_q8(rng, rows, cols)

@@ -250,10 +250,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const __grid_
   }
 }
 
-bool gemv_fast_path_ok(const Q8View& m) {
-  return m.cols % 128 == 0 && m.cols <= 8192 && reinterpret_cast<uintptr_t>(m.w) % 16 == 0 &&
-         reinterpret_cast<uintptr_t>(m.s) % 16 == 0;
-}
 
 static int gemv_tile_rows(int cols) {
   int tr = kGemvStageBudget / (cols + cols / 8);
@@ -266,6 +262,17 @@ static size_t gemv_tma_smem(int cols, int tile_rows) {
   const int nb = cols / 32;
   const size_t stage = static_cast<size_t>(tile_rows) * cols + static_cast<size_t>(tile_rows) * nb * 4;
   return kGemvStages * stage + cols * 4 + cols + nb * 4 + 16 + 2 * kGemvStages * 8 + 16;
+}
+
+constexpr size_t kGemvSmemLimit = 220 * 1024;  // the kernels' dynamic shared-memory opt-in
+
+// The streaming kernel takes a matrix whose ring of kGemvStages tiles (at
+// least four rows each) and staged x fit the opt-in; wider rows (above about
+// 5000 columns) go to the generic kernel.
+bool gemv_fast_path_ok(const Q8View& m) {
+  return m.cols % 128 == 0 && m.cols <= 8192 && reinterpret_cast<uintptr_t>(m.w) % 16 == 0 &&
+         reinterpret_cast<uintptr_t>(m.s) % 16 == 0 &&
+         gemv_tma_smem(m.cols, gemv_tile_rows(m.cols)) <= kGemvSmemLimit;
 }
 
 template <int MODE>
@@ -299,7 +306,7 @@ static void launch_gemv_tma(const Q8View* mats, int n, const float* x, float* co
   cudaGetDevice(&dev);
   if (!(configured & (1u << (dev & 31)))) {
     cudaFuncSetAttribute(gemv_tma_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         220 * 1024);
+                         static_cast<int>(kGemvSmemLimit));
     configured |= 1u << (dev & 31);
   }
   const int grid = tiles < sms ? tiles : sms;
