@@ -124,6 +124,37 @@ __device__ __forceinline__ float row_dot_int8(const int8_t* wrow, const float* s
   return acc;
 }
 
+// row_dot_int8 for four rows at once (their own chains, interleaved so that
+// the shuffle reductions and ordered sums of the four overlap); each row's
+// result is bit-identical to row_dot_int8 of that row.
+__device__ __forceinline__ void rows4_dot_int8(const int8_t* const (&wr)[4],
+                                               const float* const (&sr)[4], const int8_t* xq,
+                                               const float* xs, int cols, int lane,
+                                               float (&out)[4]) {
+  float acc[4] = {-0.0f, -0.0f, -0.0f, -0.0f};
+  for (int k0 = lane * 4; k0 < cols; k0 += 128) {
+    const int b = k0 >> 5;
+    const int xv = *reinterpret_cast<const int*>(xq + k0);
+    const float xsb = xs[b];
+    int p[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) p[r] = __dp4a(*reinterpret_cast<const int*>(wr[r] + k0), xv, 0);
+#pragma unroll
+    for (int m = 1; m <= 4; m <<= 1)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) p[r] += __shfl_xor_sync(0xffffffffu, p[r], m);
+    float t[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) t[r] = __fmul_rn(__fmul_rn(static_cast<float>(p[r]), sr[r][b]), xsb);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[r] = __fadd_rn(acc[r], __shfl_sync(0xffffffffu, t[r], 8 * q));
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) out[r] = acc[r];
+}
+
 // Block-quantize the CTA's copy of x (cols floats, smem) into xq/xs (smem),
 // the activation step of linear_dynamic_int8 (src/cpu/quantized.rs:169).
 // One warp per 32-column block, over warps [0, nw) of the CTA.
@@ -237,12 +268,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const __grid_
         const int j = ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);
         if ((lane & 7) == 0 && r + j < nr) y[r + j] = v;
       } else {
-        const int rr[4] = {r, q1, q2, q3};
+        const int8_t* const wr[4] = {wt + r * cols, wt + q1 * cols, wt + q2 * cols,
+                                     wt + q3 * cols};
+        const float* const sr[4] = {st + r * nb, st + q1 * nb, st + q2 * nb, st + q3 * nb};
+        float v[4];
+        rows4_dot_int8(wr, sr, xq, xs, cols, lane, v);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float v = row_dot_int8(wt + rr[j] * cols, st + rr[j] * nb, xq, xs, cols, lane);
-          if (lane == 0 && r + j < nr) y[r + j] = v;
-        }
+        for (int j = 0; j < 4; ++j)
+          if (lane == 0 && r + j < nr) y[r + j] = v[j];
       }
     }
     __syncwarp();
