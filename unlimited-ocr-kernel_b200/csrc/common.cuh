@@ -207,6 +207,41 @@ __device__ __forceinline__ float rows4_dot_xsmem(const int8_t* r0, const int8_t*
   return k;
 }
 
+// linear_dynamic_int8's ordered row dot (src/cpu/quantized.rs:155-236) for
+// four rows at once, one warp: lane l owns bytes [4l, 4l + 4) of every
+// 128-byte window (block = window * 4 + l / 8); per window and row the exact
+// int32 block sums S (dp4a, then a reduction over the block's 8 lanes), then
+// acc = acc + ((float)S * ws) * xs block by block from -0.0.  The four rows'
+// chains are interleaved so that their shuffles and ordered sums overlap;
+// each row's result is that of the row on its own.
+__device__ __forceinline__ void rows4_dot_int8(const int8_t* const (&wr)[4],
+                                               const float* const (&sr)[4], const int8_t* xq,
+                                               const float* xs, int cols, int lane,
+                                               float (&out)[4]) {
+  float acc[4] = {-0.0f, -0.0f, -0.0f, -0.0f};
+  for (int k0 = lane * 4; k0 < cols; k0 += 128) {
+    const int b = k0 >> 5;
+    const int xv = *reinterpret_cast<const int*>(xq + k0);
+    const float xsb = xs[b];
+    int p[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) p[r] = __dp4a(*reinterpret_cast<const int*>(wr[r] + k0), xv, 0);
+#pragma unroll
+    for (int m = 1; m <= 4; m <<= 1)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) p[r] += __shfl_xor_sync(0xffffffffu, p[r], m);
+    float t[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) t[r] = __fmul_rn(__fmul_rn(static_cast<float>(p[r]), sr[r][b]), xsb);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[r] = __fadd_rn(acc[r], __shfl_sync(0xffffffffu, t[r], 8 * q));
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) out[r] = acc[r];
+}
+
 // ---- mbarrier / bulk-copy PTX wrappers --------------------------------------
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -132,27 +132,6 @@ __device__ __forceinline__ bool grid_barrier(unsigned* sync, unsigned gen, unsig
   return true;
 }
 
-// Ordered int8-mode dot (bit-exact linear_dynamic_int8 row).
-__device__ __forceinline__ float dot_int8_ordered(const int8_t* wrow, const float* srow,
-                                                  const int8_t* xq, const float* xs, int cols,
-                                                  int lane) {
-  float acc = -0.0f;
-  for (int k0 = lane * 4; k0 < cols; k0 += 128) {
-    const int b = k0 >> 5;
-    int p = __dp4a(*reinterpret_cast<const int*>(wrow + k0),
-                   *reinterpret_cast<const int*>(xq + k0), 0);
-    p += __shfl_xor_sync(0xffffffffu, p, 1);
-    p += __shfl_xor_sync(0xffffffffu, p, 2);
-    p += __shfl_xor_sync(0xffffffffu, p, 4);
-    const float t = __fmul_rn(__fmul_rn(static_cast<float>(p), srow[b]), xs[b]);
-    acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, t, 0));
-    acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, t, 8));
-    acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, t, 16));
-    acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, t, 24));
-  }
-  return acc;
-}
-
 // Block quantization of a float vector in shared memory by `nw` warps
 // starting at warp `warp` (the activation step of linear_dynamic_int8).
 __device__ __forceinline__ void quantize_vec_smem(const float* v, int n, int8_t* q, float* s,
@@ -471,13 +450,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const __grid_co
           if (lane == 0) h[r] = __fmul_rn(silu_ref(v), u);
           if (lane == 16 && r1 != r) h[r1] = __fmul_rn(silu_ref(v), u);
         } else {
-          const int rr[2] = {r, r1};
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            if (j == 1 && r1 == r) break;
-            const float g = dot_int8_ordered(gw + rr[j] * H, gs + rr[j] * nbH, xq, xs, H, lane);
-            const float u = dot_int8_ordered(uw + rr[j] * H, us + rr[j] * nbH, xq, xs, H, lane);
-            if (lane == 0) h[rr[j]] = __fmul_rn(silu_ref(g), u);
+          // gate r, up r, gate r1, up r1 as four interleaved ordered chains
+          const int8_t* const wr[4] = {gw + r * H, uw + r * H, gw + r1 * H, uw + r1 * H};
+          const float* const sr[4] = {gs + r * nbH, us + r * nbH, gs + r1 * nbH, us + r1 * nbH};
+          float v[4];
+          rows4_dot_int8(wr, sr, xq, xs, H, lane, v);
+          if (lane == 0) {
+            h[r] = __fmul_rn(silu_ref(v[0]), v[1]);
+            if (r1 != r) h[r1] = __fmul_rn(silu_ref(v[2]), v[3]);
           }
         }
       }

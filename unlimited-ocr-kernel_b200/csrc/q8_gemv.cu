@@ -102,59 +102,6 @@ struct GemvTmaParams {
 };
 
 
-// Per-warp ordered dot of one smem row (int8 mode).  xq: cols int8 in smem,
-// xs: nb floats in smem.  Every lane returns the same value.
-__device__ __forceinline__ float row_dot_int8(const int8_t* wrow, const float* srow,
-                                              const int8_t* xq, const float* xs, int cols,
-                                              int lane) {
-  float acc = -0.0f;
-  for (int k0 = lane * 4; k0 < cols; k0 += 128) {
-    const int b = k0 >> 5;
-    int p = __dp4a(*reinterpret_cast<const int*>(wrow + k0), *reinterpret_cast<const int*>(xq + k0),
-                   0);
-    p += __shfl_xor_sync(0xffffffffu, p, 1);
-    p += __shfl_xor_sync(0xffffffffu, p, 2);
-    p += __shfl_xor_sync(0xffffffffu, p, 4);
-    const float t = __fmul_rn(__fmul_rn(static_cast<float>(p), srow[b]), xs[b]);
-    acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, t, 0));
-    acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, t, 8));
-    acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, t, 16));
-    acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, t, 24));
-  }
-  return acc;
-}
-
-// row_dot_int8 for four rows at once (their own chains, interleaved so that
-// the shuffle reductions and ordered sums of the four overlap); each row's
-// result is bit-identical to row_dot_int8 of that row.
-__device__ __forceinline__ void rows4_dot_int8(const int8_t* const (&wr)[4],
-                                               const float* const (&sr)[4], const int8_t* xq,
-                                               const float* xs, int cols, int lane,
-                                               float (&out)[4]) {
-  float acc[4] = {-0.0f, -0.0f, -0.0f, -0.0f};
-  for (int k0 = lane * 4; k0 < cols; k0 += 128) {
-    const int b = k0 >> 5;
-    const int xv = *reinterpret_cast<const int*>(xq + k0);
-    const float xsb = xs[b];
-    int p[4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) p[r] = __dp4a(*reinterpret_cast<const int*>(wr[r] + k0), xv, 0);
-#pragma unroll
-    for (int m = 1; m <= 4; m <<= 1)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) p[r] += __shfl_xor_sync(0xffffffffu, p[r], m);
-    float t[4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) t[r] = __fmul_rn(__fmul_rn(static_cast<float>(p[r]), sr[r][b]), xsb);
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) acc[r] = __fadd_rn(acc[r], __shfl_sync(0xffffffffu, t[r], 8 * q));
-  }
-#pragma unroll
-  for (int r = 0; r < 4; ++r) out[r] = acc[r];
-}
-
 // Block-quantize the CTA's copy of x (cols floats, smem) into xq/xs (smem),
 // the activation step of linear_dynamic_int8 (src/cpu/quantized.rs:169).
 // One warp per 32-column block, over warps [0, nw) of the CTA.
