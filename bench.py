@@ -1,25 +1,34 @@
-"""Benchmark of the q8-block32 MoE decode path.
+"""Benchmark of the B200 q8-block32 MoE path.
 
-A step is one token through one MoE FFN layer (Decoder::experts at decode):
-router logits -> top-6 of 64 experts -> six SwiGLU experts (gate/up
-[896x1280], down [1280x896]) plus the fused shared expert (width 1792), all
-q8-block32, FP32 activations -> ordered combine.  Inputs are seeded synthetic
-data with the configuration's distributions (x ~ N(0,1), logits ~ N(0,1),
-int8 weights uniform in [-127,127], scales ~ U(1e-4,1e-2)).
+Default workload (the one the multi-GPU scaling runs measure): the 12-layer
+decoder's MoE FFN layer at decode with its routed experts split over the GPUs
+(expert parallelism).  Every GPU brings a decode batch of 64 tokens (weak
+scaling) and holds 64/N of the 64 routed experts (gate/up [896x1280], down
+[1280x896], q8-block32) plus the fused shared expert (width 1792).  One layer
+forward: router logits -> top-6 (moe::route) -> dispatch of every (token,
+expert) row into the owning GPU's memory (stores over NVLink, the library's
+own kernels) -> the owners' grouped SwiGLU projections -> return of the
+outputs -> ordered combine with the shared expert's output.  FP32
+activations by default (--ep-mode 2: int8 activations for every row).
 
-metric  : q8-block32 expert GEMV GB/s = algorithmic bytes / time, where the
-          algorithmic bytes of a step are the int8 weights + fp32 scales of
-          the 7 FFNs it touches + x + logits + y (30,976,256 B).
-value   : device-resident inputs, K steps replayed from CUDA graphs; each
-          step uses the next of 8 distinct layers (2.0 GB > 126 MB L2), so
-          weights come from HBM.
-e2e     : the same metric through the C ABI's host-buffer entry point
-          (uocr_moe_forward_host): pinned host x/logits copied in and y copied
-          out inside the timed region, one synchronous call per step.
+metric  : decode tok/s = tokens of all GPUs / device time (max over ranks).
+value   : device-resident inputs; a step replays a CUDA graph of R
+          consecutive layer forwards over distinct layers (weights from HBM),
+          R sized so that the K timed steps last >= 0.6 s.
+e2e     : the same metric through uocr_ep_forward_host (pinned host x and
+          logits copied in, y copied out, synchronous per layer forward).
+ep_parity: one step of the sharded layer against the single-GPU layer on rank
+          0's tokens (FP32 activations within the FP32 tolerance, int8
+          activations bit for bit).
+secondary (one GPU only): every other configuration, bounded: the one-token
+          MoE decode layer (GB/s), the GEMV stream (GB/s), grouped prefill at
+          1024 tokens in both modes (TOP/s), the int8 micro-suite, decode
+          attention and the whole 12-layer decode step.
 --impl reference: the reference's scalar CPU path (oracle port, all host
-          threads) on the same workload.
-Multi-GPU (torchrun): every rank runs its own token stream (weak scaling,
-no collective on the data path); time is the max over ranks.
+          threads) on the default workload, rank 0 only.
+Inputs are seeded synthetic data with the configurations' distributions
+(x ~ N(0,1), logits ~ N(0,1), int8 weights uniform in [-127,127], scales ~
+U(1e-4,1e-2)).
 """
 import argparse
 import json
@@ -1073,57 +1082,421 @@ def run_decode(args):
     return res
 
 
+
+# ---------------------------------------------------------------------------
+# Default workload: the 12-layer decoder's MoE layer at decode with its routed
+# experts split over the GPUs (expert parallelism), rows exchanged through
+# NVLink peer memory by the library's own kernels (uocr_ep_*).
+EPP_TOKENS = 64          # decode batch per rank (weak scaling: fixed per GPU)
+EPP_METRIC = "decode tok/s (MoE decoder layer, expert-parallel, 64 tokens per GPU)"
+EPP_MIN_TIMED_S = 0.6    # timed region at least this long (clock samples)
+
+
+def cpu_model():
+    try:
+        out = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+        for line in out.splitlines():
+            if line.startswith("Model name:"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return None
+
+
+def epp_weights(dev, ctx, layer_index, expert_ids):
+    """Deterministic weights of one layer: every matrix seeded by (layer,
+    expert, projection), so that any rank builds the same expert."""
+    import torch
+
+    import uocr_q8
+
+    def mat(seed, r, c):
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        w = torch.randint(-127, 128, (r, c), dtype=torch.int8, device=dev, generator=g)
+        sc = torch.rand((r, (c + 31) // 32), device=dev, generator=g) * (1e-2 - 1e-4) + 1e-4
+        return uocr_q8.Int8Matrix.from_device(r, c, w, sc.float().contiguous(), ctx)
+
+    base = 100000 * (layer_index + 1)
+    shared = [mat(base + i, *rc) for i, rc in enumerate(((FS, H), (FS, H), (H, FS)))]
+    experts = [[mat(base + 10 * (e + 1) + i, *rc) for i, rc in enumerate(((F, H), (F, H), (H, F)))]
+               for e in expert_ids]
+    return shared, experts
+
+
+def epp_cpu_baseline(seconds, mode=0):
+    """The reference's scalar path (oracle port) on a bounded sample: batches
+    of 64 tokens through one MoE layer, on all host threads and on one."""
+    import oracle
+    shared, routed, rng = make_cpu_layer(7)
+    x = rng.standard_normal((EPP_TOKENS, H)).astype(np.float32)
+    lg = rng.standard_normal((EPP_TOKENS, E)).astype(np.float32)
+    out = {}
+    for threads, budget in ((0, seconds), (1, seconds / 2)):
+        oracle.set_threads(threads)
+        n, t0 = 0, time.perf_counter()
+        while n == 0 or time.perf_counter() - t0 < budget:
+            oracle.experts(shared, routed, lg, x, TOPK, mode)
+            n += 1
+        dt = time.perf_counter() - t0
+        out[threads] = (EPP_TOKENS * n / dt, n, dt, oracle.get_threads())
+    oracle.set_threads(0)
+    v, n, dt, cores = out[0]
+    v1, n1, dt1, _ = out[1]
+    return {"value": round(v, 2), "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{n} batches of 64 tokens through one MoE layer in {dt:.1f} s "
+                      "(scalar restatement of the reference's Rust path; the crate cannot be "
+                      "built here)",
+            "single_thread": {"value": round(v1, 2), "unit": "tok/s", "cores": 1,
+                              "sample": f"{n1} batches in {dt1:.1f} s"},
+            "cpu_model": cpu_model(), "nproc": os.cpu_count()}
+
+
+def run_ep_peer(args):
+    """The MoE layer of the 12-layer decoder (64 routed experts of width 896,
+    top-6, shared expert of width 1792, hidden 1280) at decode: every rank
+    brings a batch of 64 tokens (weak scaling) and holds a contiguous block of
+    the routed experts plus the shared expert; one layer forward = route,
+    dispatch of the (token, expert) rows into the owners' memory over NVLink,
+    the owners' grouped SwiGLU experts, return of the outputs, ordered
+    combine.  A bench step replays a CUDA graph of R consecutive layer
+    forwards (distinct layers rotated so that every layer's weights come from
+    HBM), R chosen so that the K timed steps last at least 0.6 s."""
+    import datetime
+    import math
+
+    import torch
+    import torch.distributed as dist
+
+    import uocr_q8
+    from uocr_q8.expert_parallel import expert_bounds, peer_expert_parallel
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    if world > 1 and not dist.is_initialized():
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device(dev))
+    ctx = uocr_q8.GpuContext(local)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream)
+    mode = args.ep_mode
+    bounds = expert_bounds(E, world)
+    mine = list(range(bounds[rank], bounds[rank + 1]))
+    per_rank_weight_bytes = len(mine) * EP_EXPERT_BYTES + EP_SHARED_BYTES
+    n_layers = max(2, math.ceil(3 * 126e6 / per_rank_weight_bytes))  # > L2 between reuses
+    T = EPP_TOKENS
+    layers, eps = [], []
+    with torch.cuda.stream(stream):
+        for li in range(n_layers):
+            shared, experts = epp_weights(dev, ctx, li, mine)
+            layer = uocr_q8.MoeLayer(ctx, shared, experts, top_k=1)
+            layers.append(layer)
+            if world > 1:
+                ep = peer_expert_parallel(ctx, layer, E, TOPK, T)
+            else:
+                ep = uocr_q8.PeerExpertParallel(ctx, layer, E, TOPK, bounds, 0, T)
+                uocr_q8.PeerExpertParallel.connect_local([ep])
+            ep.set_wait_limit(5.0)
+            eps.append(ep)
+    torch.cuda.synchronize()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(555 + rank)
+    n_in = 8
+    xs = torch.randn((n_in, T, H), device=dev, generator=gen)
+    lg = torch.randn((n_in, T, E), device=dev, generator=gen)
+    ys = torch.empty((n_in, T, H), device=dev)
+
+    def step(i):
+        eps[i % n_layers].forward_device(xs[i % n_in], lg[i % n_in], mode, ys[i % n_in])
+
+    if world > 1:
+        dist.barrier()
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3) + n_layers):
+            step(i)
+    ctx.sync()
+
+    # parity of one step of every rank against the single-GPU layer (all 64
+    # experts) on rank 0's tokens: FP32 activations within the FP32 layer
+    # tolerance, int8 activations bit for bit
+    parity = {}
+    for pm in (0, 2):
+        if world > 1:
+            dist.barrier()
+        y_ep = torch.empty((T, H), device=dev)
+        with torch.cuda.stream(stream):
+            eps[0].forward_device(xs[0], lg[0], pm, y_ep)
+        ctx.sync()
+        if rank == 0:
+            with torch.cuda.stream(stream):
+                shared, experts = epp_weights(dev, ctx, 0, range(E))
+                full = uocr_q8.MoeLayer(ctx, shared, experts, TOPK)
+                y_ref = full.forward_device(xs[0], lg[0], pm)
+            ctx.sync()
+            a, b = y_ep.cpu().numpy(), y_ref.cpu().numpy()
+            same = float(np.mean(a.view(np.uint32) == b.view(np.uint32)))
+            rel = float(np.max(np.abs(a.astype(np.float64) - b)) / max(np.max(np.abs(b)), 1e-30))
+            parity[f"mode{pm}"] = {"bit_identical": round(same, 6), "max_rel_diff": rel,
+                                   "ok": bool(same == 1.0 if pm else rel <= 1e-4)}
+            full.free()
+            del shared, experts, full
+    if world > 1:
+        dist.barrier()
+
+    # R layer forwards per bench step, from the measured time of one forward
+    probe = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(probe, stream=stream):
+        for i in range(n_layers):
+            step(i)
+    for _ in range(2):
+        probe.replay()
+    torch.cuda.synchronize()
+    t0e, t1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t0e.record(stream)
+        for _ in range(4):
+            probe.replay()
+        t1e.record(stream)
+    t1e.synchronize()
+    t_layer = t0e.elapsed_time(t1e) * 1e-3 / (4 * n_layers)
+    tl = torch.tensor([t_layer], device=dev)
+    if world > 1:
+        dist.all_reduce(tl, op=dist.ReduceOp.MAX)
+    t_layer = float(tl.item())
+    K = max(1, args.steps)
+    R = n_layers * max(1, math.ceil(EPP_MIN_TIMED_S / (K * t_layer * n_layers)))
+    R = min(R, n_layers * 4096)
+    del probe
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(R):
+            step(i)
+    warm = max(args.warmup, 3)
+    for _ in range(warm):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(K):
+                graph.replay()
+            stop.record(stream)
+        stop.synchronize()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(stop)
+    ctx.sync()
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    forwards = K * R
+    value = world * T * forwards / (ms * 1e-3)
+    us_layer = ms * 1e3 / forwards
+    del graph
+
+    # end to end: pinned host x / logits in, y out, through uocr_ep_forward_host
+    hx = torch.empty((n_in, T, H), pin_memory=True)
+    hl = torch.empty((n_in, T, E), pin_memory=True)
+    hy = torch.empty((n_in, T, H), pin_memory=True)
+    hx.copy_(xs.cpu())
+    hl.copy_(lg.cpu())
+    e2e_steps = max(n_layers, min(args.e2e_steps, int(2.0 / max(t_layer, 1e-6)) // n_layers * n_layers))
+    for i in range(n_layers):
+        eps[i].forward_host_ptrs(hx[0].data_ptr(), hl[0].data_ptr(), T, hy[0].data_ptr(), mode)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        j = i % n_in
+        eps[i % n_layers].forward_host_ptrs(hx[j].data_ptr(), hl[j].data_ptr(), T,
+                                            hy[j].data_ptr(), mode)
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_s = float(te.item())
+    e2e = world * T * e2e_steps / e2e_s
+
+    peak, peak_kind = peak_hbm()
+    step_bytes = per_rank_weight_bytes + T * (H + E + H) * 4
+    achieved = step_bytes / (us_layer * 1e-6) / 1e9
+    result = None
+    if rank == 0:
+        result = {
+            "metric": EPP_METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
+            "steps": K, "warmup": warm, "ms_per_step": round(ms / K, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp32" if mode == 0 else "int8-act",
+            "data": "synthetic (seeded; x ~ N(0,1), router logits ~ N(0,1), int8 weights "
+                    "uniform in [-127,127], scales ~ U(1e-4,1e-2))",
+            "config": {"workload": "moe_layer_ep_decode", "tokens_per_gpu": T,
+                       "global_batch": world * T, "hidden": H, "experts": E, "top_k": TOPK,
+                       "experts_per_gpu": len(mine), "expert_width": F, "shared_width": FS,
+                       "mode": {0: "weights_only (fp32 activations)", 1: "dynamic activations",
+                                2: "dynamic int8 activations, every row"}[mode],
+                       "parallelism": f"ep{world} (routed experts split, rows exchanged by "
+                                      "stores into peer memory over NVLink; no collective)",
+                       "step": f"one CUDA-graph replay of {R} consecutive layer forwards",
+                       "layer_forwards_per_step": R, "us_per_layer_forward": round(us_layer, 3),
+                       "l2": f"rotating pool of {n_layers} layers x "
+                             f"{per_rank_weight_bytes / 1e6:.1f} MB per GPU (> 126 MB L2)"},
+            "e2e": {"value": round(e2e, 1), "unit": "tok/s", "steps": e2e_steps,
+                    "us_per_step": round(e2e_s / e2e_steps * 1e6, 2),
+                    "api": "uocr_ep_forward_host (one layer forward per call)",
+                    "h2d_bytes_per_step": T * (H + E) * 4, "d2h_bytes_per_step": T * H * 4},
+            "roofline": {"bound": "hbm",
+                         "kernel": "one layer forward (all its launches: route, dispatch, "
+                                   "small_rows_kernel gate/up and down, splits, return, "
+                                   "combine); algorithmic bytes = this GPU's expert and "
+                                   "shared weights + x, logits, y",
+                         "achieved": round(achieved, 2), "peak": peak, "peak_kind": peak_kind,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                         "bytes_per_layer_forward": step_bytes},
+            "ep_parity": parity,
+            # route, dispatch, wait, grouping, split, small-rows gate/up (+ tensor-core
+            # gate, up, big-counts when a group can exceed 64 rows), SwiGLU split,
+            # small-rows down (+ tensor-core down), un-permute, return, shared
+            # expert (split, gate/up, SwiGLU split, down), combine
+            "gpu_launches": forwards * (16 if world * T <= 64 else 20),
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu:
+            result["cpu_baseline"] = epp_cpu_baseline(args.cpu_seconds, mode)
+    for ep in eps:
+        ep.free()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def run_secondary(args):
+    """Every other configuration, bounded, on GPU 0 (one GPU runs only)."""
+    import copy
+    out = {}
+
+    def sub(name, fn, **over):
+        a = copy.copy(args)
+        for k, v in over.items():
+            setattr(a, k, v)
+        t0 = time.perf_counter()
+        try:
+            r = fn(a)
+            r["wall_s"] = round(time.perf_counter() - t0, 1)
+            out[name] = r
+        except Exception as exc:  # a secondary never hides the headline line
+            out[name] = {"error": f"{type(exc).__name__}: {exc}"}
+
+    sub("config1_moe_decode_layer", run_ours, steps=4096, e2e_steps=4000,
+        cpu_seconds=min(args.cpu_seconds, 6.0))
+    sub("config0_gemv_fp32", run_gemv, steps=256 * 4096, gemv_int8=False)
+    sub("config0_gemv_int8", run_gemv, steps=256 * 4096, gemv_int8=True)
+    sub("config2_prefill_fp32", run_prefill, steps=40, prefill_mode=0)
+    sub("config2_prefill_int8", run_prefill, steps=40, prefill_mode=2)
+    sub("config3_int8_suite", run_int8suite)
+    sub("config4_attention", run_attn, steps=200, cpu_seconds=min(args.cpu_seconds, 5.0))
+    sub("config4_decode_step", run_decode, steps=60, cpu_seconds=min(args.cpu_seconds, 6.0))
+    return out
+
+
+def run_reference_ep(args):
+    """The reference's scalar CPU path (oracle port, all host threads) on the
+    default workload: each step one batch of 64 tokens through one MoE layer;
+    rank 0 alone runs it."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    import oracle
+    oracle.set_threads(0)
+    shared, routed, rng = make_cpu_layer(7)
+    xs = rng.standard_normal((4, EPP_TOKENS, H)).astype(np.float32)
+    lgs = rng.standard_normal((4, EPP_TOKENS, E)).astype(np.float32)
+    for i in range(max(args.warmup, 3)):
+        oracle.experts(shared, routed, lgs[i % 4], xs[i % 4], TOPK, args.ep_mode)
+    steps = args.steps if args.ref_steps is None else args.ref_steps
+    t0 = time.perf_counter()
+    for i in range(steps):
+        oracle.experts(shared, routed, lgs[i % 4], xs[i % 4], TOPK, args.ep_mode)
+    dt = time.perf_counter() - t0
+    v = EPP_TOKENS * steps / dt
+    cores = oracle.get_threads()
+    return {"impl": "reference", "metric": EPP_METRIC, "value": round(v, 2), "unit": "tok/s",
+            "n_gpus": world, "steps": steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": round(dt / steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp32" if args.ep_mode == 0 else "int8-act",
+            "data": "synthetic (seeded; same distributions as the GPU arm)",
+            "config": {"workload": "moe_layer_ep_decode", "tokens_per_gpu": EPP_TOKENS,
+                       "hidden": H, "experts": E, "top_k": TOPK, "expert_width": F,
+                       "shared_width": FS, "parallelism": "rank 0 only (host CPU)",
+                       "step": "one batch of 64 tokens through one MoE layer"},
+            "cpu_baseline": {"value": round(v, 2), "unit": "tok/s", "cores": cores, "kind": "port",
+                             "sample": f"{steps} batches of 64 tokens through one MoE layer "
+                                       "(scalar restatement of the reference's Rust path; the "
+                                       "Rust crate cannot be built here)",
+                             "cpu_model": cpu_model()},
+            "e2e": {"value": round(v, 2), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=131072)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--graph-steps", type=int, default=256)
     ap.add_argument("--e2e-steps", type=int, default=4000)
-    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-steps", type=int, default=None)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="default workload only (skip the one-GPU secondary configurations)")
     ap.add_argument("--traffic", type=float, default=None,
                     help="dram bytes per launch from an ncu capture (roofline.traffic); "
                          "defaults to the committed capture of the workload's kernel")
     ap.add_argument("--workload",
-                    choices=["moe_decode", "gemv", "prefill", "int8suite", "ep_decode",
+                    choices=["ep_peer", "moe_decode", "gemv", "prefill", "int8suite", "ep_decode",
                              "attn_decode", "decode_step"],
-                    default="moe_decode")
+                    default="ep_peer")
     ap.add_argument("--gemv-int8", action="store_true")
     ap.add_argument("--prefill-mode", type=int, choices=[0, 2], default=0)
     ap.add_argument("--ep-mode", type=int, choices=[0, 1, 2], default=0)
     ap.add_argument("--decode-mode", type=int, choices=[0, 2], default=0)
     ap.add_argument("--lm-head", choices=["q8", "bf16"], default="q8")
     args = ap.parse_args()
-    if args.workload == "gemv" and args.impl == "ours":
-        print(json.dumps(run_gemv(args)), flush=True)
-        return
-    if args.workload == "prefill" and args.impl == "ours":
-        print(json.dumps(run_prefill(args)), flush=True)
-        return
-    if args.workload == "ep_decode" and args.impl == "ours":
-        res = run_ep(args)
+    if args.impl == "reference":
+        if args.workload == "ep_peer":
+            res = run_reference_ep(args)
+        else:
+            if args.ref_steps is None:
+                args.ref_steps = min(args.steps, 1500)
+            res = run_reference(args)
         if res is not None:
             print(json.dumps(res), flush=True)
         return
-    if args.workload == "decode_step" and args.impl == "ours":
-        print(json.dumps(run_decode(args)), flush=True)
+    single = {"gemv": run_gemv, "prefill": run_prefill, "decode_step": run_decode,
+              "attn_decode": run_attn, "int8suite": run_int8suite}
+    if args.workload in single:
+        print(json.dumps(single[args.workload](args)), flush=True)
         return
-    if args.workload == "attn_decode" and args.impl == "ours":
-        print(json.dumps(run_attn(args)), flush=True)
-        return
-    if args.workload == "int8suite" and args.impl == "ours":
-        print(json.dumps(run_int8suite(args)), flush=True)
-        return
-    if args.impl == "reference":
-        if args.ref_steps is None:
-            args.ref_steps = min(args.steps, 1500)
-        res = run_reference(args)
-    else:
+    if args.workload == "ep_decode":
+        res = run_ep(args)
+    elif args.workload == "moe_decode":
         res = run_ours(args)
+    else:
+        res = run_ep_peer(args)
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        if res is not None and world == 1 and not args.no_secondary:
+            res["secondary"] = run_secondary(args)
     if res is not None:
         print(json.dumps(res), flush=True)
 

@@ -235,6 +235,68 @@ int uocr_moe_combine(uocr_ctx *ctx, const int32_t *ids_dev, const float *weights
                      const float *pair_out_dev, size_t tokens, size_t top_k, size_t hidden,
                      float *y_dev);
 
+/* ---- expert parallelism over NVLink peer memory ----------------------------
+ * No counterpart in the reference (Decoder::experts, src/decoder/mod.rs:
+ * 124-220, runs on one device).  A layer whose routed experts are split over
+ * `world` GPUs of one node in contiguous blocks (rank r holds experts
+ * [rank_bounds[r], rank_bounds[r+1]) as `local_layer`, every rank holds the
+ * shared expert and brings its own tokens).  Rows travel as stores into the
+ * other GPUs' memory (CUDA IPC mappings; no collective library, no padding,
+ * no host synchronisation): a step is capturable in a CUDA graph, and its
+ * result on each rank is uocr_moe_forward of that rank's tokens: routing and
+ * int8-activation outputs bit for bit; FP32-activation outputs within the
+ * FP32 tolerance (an owner's group, rows of several ranks, may take another
+ * projection kernel, with another FP32 summation order).
+ *
+ *   uocr_ep_create   this rank's end: device buffers for up to max_tokens
+ *                    tokens per rank and step (the same on every rank).
+ *   uocr_ep_handle   UOCR_EP_HANDLE_BYTES describing this rank's buffers
+ *                    (a CUDA IPC handle); the caller gathers all ranks'
+ *                    handles by any channel (MPI, a TCP store, ...) and
+ *   uocr_ep_connect  opens them (world * UOCR_EP_HANDLE_BYTES, rank order).
+ *                    Ranks in one process (testing several ranks on one GPU)
+ *                    use uocr_ep_connect_local instead.
+ *   uocr_ep_forward  one step of this rank's tokens, asynchronous on the
+ *                    context's stream (the exchange runs on an internal
+ *                    high-priority stream forked from and joined back into
+ *                    it).  Every rank must run the same number of steps, in
+ *                    the same order; a rank with no tokens passes tokens = 0.
+ *   uocr_ep_dispatch / uocr_ep_experts / uocr_ep_combine: the same step in
+ *                    three parts on the context's stream, for one host thread
+ *                    driving several ranks of one process on ONE stream in
+ *                    the order dispatch(all ranks), experts(all ranks),
+ *                    combine(all ranks), so that no wait depends on work
+ *                    queued behind it.
+ * Every device wait is bounded (uocr_ep_set_wait_limit, default 2 s); a wait
+ * that expires returns UOCR_ERR_TIMEOUT at the next synchronising call, after
+ * which the layers of all ranks must be freed and created again.  tokens >
+ * max_tokens is Resource; x_dev and y_dev 16-byte aligned; hidden % 4 == 0;
+ * world <= 64, top_k <= 8, n_experts <= 256. */
+typedef struct uocr_ep uocr_ep;
+#define UOCR_EP_HANDLE_BYTES 128
+int uocr_ep_create(uocr_ctx *ctx, const uocr_moe *local_layer, size_t n_experts, size_t top_k,
+                   int normalize_topk, float routed_scale, const int32_t *rank_bounds,
+                   size_t world, size_t rank, size_t max_tokens, uocr_ep **out);
+int uocr_ep_free(uocr_ep *ep);
+int uocr_ep_handle(const uocr_ep *ep, void *handle_out);
+int uocr_ep_connect(uocr_ep *ep, const void *handles);
+int uocr_ep_connect_local(uocr_ep *const *eps, size_t world);
+int uocr_ep_set_wait_limit(uocr_ep *ep, uint64_t ns);
+int uocr_ep_forward(uocr_ctx *ctx, uocr_ep *ep, int mode, const float *x_dev,
+                    const float *logits_dev, size_t tokens, float *y_dev, int32_t *ids_dev,
+                    float *weights_dev);
+/* Host-buffer form of uocr_ep_forward (x tokens*hidden, logits
+ * tokens*n_experts, y tokens*hidden floats): copies in, one step, copies out,
+ * synchronises and returns the step's device status (pinned buffers are
+ * copied directly, others through a pinned mirror). */
+int uocr_ep_forward_host(uocr_ctx *ctx, uocr_ep *ep, int mode, const float *x,
+                         const float *logits, size_t tokens, float *y);
+int uocr_ep_dispatch(uocr_ctx *ctx, uocr_ep *ep, int mode, const float *x_dev,
+                     const float *logits_dev, size_t tokens, float *y_dev);
+int uocr_ep_experts(uocr_ctx *ctx, uocr_ep *ep);
+int uocr_ep_combine(uocr_ctx *ctx, uocr_ep *ep, float *y_dev, int32_t *ids_dev,
+                    float *weights_dev);
+
 /* ---- allocation-free decode ------------------------------------------------
  * No counterpart in the reference.  For callers that may not allocate device
  * memory while inference runs (a serving loop that reserves everything at

@@ -72,15 +72,20 @@ cudaError_t launch_q8_tc_grouped_f32(const void* maps, int groups, const int* co
                                      const int* offsets, int max_tiles, int N, int K,
                                      const uint16_t* pieces, const float* rinv, int total_rows,
                                      float* y, long long ldy, unsigned* status, cudaStream_t st);
+// The row passes below take an optional device row count `live`: rows at or
+// past *live are skipped (grouped rows of which only the first *live are in
+// use; the pieces keep the stride of `rows`).
 // pieces and rinv of rows x[src ? src[r] : r] (cols % 4 == 0, x rows 16-byte aligned)
 void launch_split_rows(const float* x, long long ld_x, const int* src, int rows, int cols,
-                       uint16_t* pieces, float* rinv, int sms, cudaStream_t st);
+                       uint16_t* pieces, float* rinv, int sms, cudaStream_t st,
+                       const int* live = nullptr);
 // pieces and rinv of silu(g) * u
 void launch_swiglu_split(const float* g, const float* u, int rows, int cols, uint16_t* pieces,
-                         float* rinv, int sms, cudaStream_t st);
+                         float* rinv, int sms, cudaStream_t st, const int* live = nullptr);
 // xq_p[p] = xq[src[p]], xs_p[p] = xs[src[p]]
 void launch_gather_rows(const int8_t* xq, const float* xs, const int* src, int rows, int cols,
-                        int8_t* xq_p, float* xs_p, int sms, cudaStream_t st);
+                        int8_t* xq_p, float* xs_p, int sms, cudaStream_t st,
+                        const int* live = nullptr);
 // BF16 weights [n][k] (bit patterns) times `batch` float rows of k: the
 // reference's sequential BF16 linear (router logits).
 cudaError_t launch_linear_bf16(const uint16_t* w, int n, int k, const float* x, int batch, float* y,
@@ -89,7 +94,8 @@ cudaError_t launch_linear_bf16(const uint16_t* w, int n, int k, const float* x, 
 void launch_swiglu(const float* g, const float* u, long long n, float* h, int sms, cudaStream_t st);
 // hq/hs = block-quantized silu(g) * u
 void launch_swiglu_quantize(const float* g, const float* u, int rows, int cols, int8_t* hq,
-                            float* hs, unsigned* status, int sms, cudaStream_t st);
+                            float* hs, unsigned* status, int sms, cudaStream_t st,
+                            const int* live = nullptr);
 
 // q8_small.cu — grouped projections for groups of lo..hi rows (hi <=
 // kSmallChunkedMax), as 8-row chunks, weights streamed once per chunk (TMA
@@ -174,6 +180,10 @@ struct MoePrefillArgs {
   int route_given, skip_shared, skip_routed;
   float* pair_out;
   int skip_negative_ids;  // route_given: a negative id marks an unused row
+  // optional (0 = tokens): no expert receives more rows than this (a caller
+  // whose rows come from several sources of at most this many tokens each
+  // selects the kernels by it)
+  int max_group_rows;
   // optional: a second stream (of high priority) and two events; up to
   // kSmallChunkedMax tokens the routing and the routed experts then run on
   // `side` while the shared expert runs on the call's stream (forked after the

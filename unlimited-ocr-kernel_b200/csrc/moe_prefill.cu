@@ -670,6 +670,17 @@ static int big_group_tiles(int P, int E) {
   return P / 64 + groups + 1;
 }
 
+// The largest group a call can form: tokens, or the caller's bound.
+static int max_group_rows(const MoePrefillArgs& a) {
+  return a.max_group_rows > 0 && a.max_group_rows < a.tokens ? a.max_group_rows : a.tokens;
+}
+
+// With unused rows (negative ids) the grouped rows in use are the first
+// offsets[n_experts]; the row passes over grouped rows stop there.
+static const int* grouped_live(const MoePrefillArgs& a, const PrefillWs& w) {
+  return a.skip_negative_ids ? w.offsets + a.n_experts : nullptr;
+}
+
 // The shared expert over T <= kSmallShared tokens with FP32 activations, as
 // chunks of 8 rows on the warp-level kernel (the tokens' pieces are in
 // w.xp_s / w.xr_s); its down projection writes y.
@@ -699,11 +710,13 @@ static cudaError_t prefill_tc_f32(const MoePrefillArgs& a, const PrefillWs& w, i
   cudaError_t e;
   // no group exceeds T rows: up to kSmallChunkedMax tokens every group runs on
   // the warp-level kernel and the tensor-core launches are skipped
-  const bool tc = T > kSmallChunkedMax;
-  const int R = tc ? kSmallRowsMax : (T > 1 ? T : 1);
+  const int G = max_group_rows(a);
+  const bool tc = G > kSmallChunkedMax;
+  const int R = tc ? kSmallRowsMax : (G > 1 ? G : 1);
+  const int* live = grouped_live(a, w);
   if (!a.skip_routed) {
     if (tc) launch_big_counts(w.counts, E, w.counts_big, st);
-    launch_split_rows(a.x, H, w.pair_token, P, H, w.xp_r, w.xr_r, sms, st);
+    launch_split_rows(a.x, H, w.pair_token, P, H, w.xp_r, w.xr_r, sms, st, live);
     // gate and up of the small groups in one launch
     if ((e = launch_small_rows(false, maps, nullptr, w.counts, w.offsets, E, 1, R, 0, F, H, w.xp_r,
                                P, w.xr_r, nullptr, nullptr, P, w.h_r, F, a.status, st,
@@ -715,7 +728,7 @@ static cudaError_t prefill_tc_f32(const MoePrefillArgs& a, const PrefillWs& w, i
                                         F, H, w.xp_r, w.xr_r, P, j == 0 ? w.h_r : w.u_r, F,
                                         a.status, st)))
         return e;
-    launch_swiglu_split(w.h_r, w.u_r, P, F, w.hp_r, w.hr_r, sms, st);
+    launch_swiglu_split(w.h_r, w.u_r, P, F, w.hp_r, w.hr_r, sms, st, live);
     if ((e = launch_small_rows(false, maps + 2 * E * mb, nullptr, w.counts, w.offsets, E, 1, R, 0, H,
                                  F, w.hp_r, P, w.hr_r, nullptr, nullptr, P, w.out_r, H,
                                  a.status, st,
@@ -743,13 +756,15 @@ static cudaError_t prefill_tc(const MoePrefillArgs& a, const PrefillWs& w, int s
   const unsigned char* maps = static_cast<const unsigned char*>(a.tc_maps);
   const size_t mb = q8_tc_maps_bytes();  // per matrix
   cudaError_t e;
-  const bool tc = T > kSmallChunkedMax;
-  const int R = tc ? kSmallRowsMax : (T > 1 ? T : 1);
+  const int G = max_group_rows(a);
+  const bool tc = G > kSmallChunkedMax;
+  const int R = tc ? kSmallRowsMax : (G > 1 ? G : 1);
+  const int* live = grouped_live(a, w);
   if (!a.skip_routed) {
     // routed experts: rows gathered per expert; groups of <= R rows on the
     // warp-level kernel, larger ones on the tensor-core GEMM
     if (tc) launch_big_counts(w.counts, E, w.counts_big, st);
-    launch_gather_rows(w.xq, w.xs, w.pair_token, P, H, w.xq_p, w.xs_p, sms, st);
+    launch_gather_rows(w.xq, w.xs, w.pair_token, P, H, w.xq_p, w.xs_p, sms, st, live);
     // gate and up of the small groups in one launch
     if ((e = launch_small_rows(true, maps, nullptr, w.counts, w.offsets, E, 1, R, 0, F, H, nullptr,
                                0, nullptr, w.xq_p, w.xs_p, P, w.h_r, F, a.status, st,
@@ -761,7 +776,7 @@ static cudaError_t prefill_tc(const MoePrefillArgs& a, const PrefillWs& w, int s
                                        F, H, w.xq_p, w.xs_p, P, j == 0 ? w.h_r : w.u_r, F,
                                        a.status, st)))
         return e;
-    launch_swiglu_quantize(w.h_r, w.u_r, P, F, w.hq_r, w.hs_r, a.status, sms, st);
+    launch_swiglu_quantize(w.h_r, w.u_r, P, F, w.hq_r, w.hs_r, a.status, sms, st, live);
     if ((e = launch_small_rows(true, maps + 2 * E * mb, nullptr, w.counts, w.offsets, E, 1, R, 0, H,
                                  F, nullptr, 0, nullptr, w.hq_r, w.hs_r, P, w.out_r, H,
                                  a.status, st,
@@ -803,13 +818,15 @@ static cudaError_t prefill_tc_mixed(const MoePrefillArgs& a, const PrefillWs& w,
   const int max_tiles = big_group_tiles(P, E);
   const unsigned char* maps = static_cast<const unsigned char*>(a.tc_maps);
   const size_t mb = q8_tc_maps_bytes();
-  const bool tc = T > kSmallChunkedMax;
-  const int R = tc ? kSmallRowsMax : (T > 2 ? T : 2);
+  const int G = max_group_rows(a);
+  const bool tc = G > kSmallChunkedMax;
+  const int R = tc ? kSmallRowsMax : (G > 2 ? G : 2);
+  const int* live = grouped_live(a, w);
   cudaError_t e;
   if (!a.skip_routed) {
     if (tc) launch_big_counts(w.counts, E, w.counts_big, st);
-    launch_gather_rows(w.xq, w.xs, w.pair_token, P, H, w.xq_p, w.xs_p, sms, st);
-    launch_split_rows(a.x, H, w.pair_token, P, H, w.xp_r, w.xr_r, sms, st);
+    launch_gather_rows(w.xq, w.xs, w.pair_token, P, H, w.xq_p, w.xs_p, sms, st, live);
+    launch_split_rows(a.x, H, w.pair_token, P, H, w.xp_r, w.xr_r, sms, st, live);
     // gate and up together: one-row groups int8, 2..R rows FP32, larger on the GEMM
     if ((e = launch_small_rows(true, maps, nullptr, w.counts, w.offsets, E, 1, 1, 0, F, H, nullptr,
                                0, nullptr, w.xq_p, w.xs_p, P, w.h_r, F, a.status, st,
@@ -825,8 +842,8 @@ static cudaError_t prefill_tc_mixed(const MoePrefillArgs& a, const PrefillWs& w,
                                         F, H, w.xp_r, w.xr_r, P, j == 0 ? w.h_r : w.u_r, F,
                                         a.status, st)))
         return e;
-    launch_swiglu_quantize(w.h_r, w.u_r, P, F, w.hq_r, w.hs_r, a.status, sms, st);
-    launch_swiglu_split(w.h_r, w.u_r, P, F, w.hp_r, w.hr_r, sms, st);
+    launch_swiglu_quantize(w.h_r, w.u_r, P, F, w.hq_r, w.hs_r, a.status, sms, st, live);
+    launch_swiglu_split(w.h_r, w.u_r, P, F, w.hp_r, w.hr_r, sms, st, live);
     if ((e = launch_small_rows(true, maps + 2 * E * mb, nullptr, w.counts, w.offsets, E, 1, 1, 0, H,
                                  F, nullptr, 0, nullptr, w.hq_r, w.hs_r, P, w.out_r, H,
                                  a.status, st,
@@ -893,12 +910,14 @@ cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaS
     group_pairs_kernel<<<1, kGroupThreads, 0, rs>>>(a.route_ids, a.route_weights, T, k, E,
                                                    a.skip_negative_ids, w.counts, w.offsets,
                                                    w.pair_token, w.pair_weight, w.token_pos,
-                                                   T <= kSmallChunkedMax ? w.items : nullptr,
+                                                   max_group_rows(a) <= kSmallChunkedMax
+                                                       ? w.items : nullptr,
                                                    a.status);
   }
-  if (a.skip_negative_ids && !a.skip_routed) {
+  if (a.skip_negative_ids && !a.skip_routed && path == Path::CudaCore) {
     // unused rows belong to no group and are never written by the projections:
     // zero them so that the SwiGLU and quantization passes over all rows see 0
+    // (the tensor-core paths stop their row passes at the grouped count)
     const size_t hb = sizeof(float) * static_cast<size_t>(T) * k * a.width;
     cudaMemsetAsync(w.h_r, 0, hb, st);
     if (w.u_r) cudaMemsetAsync(w.u_r, 0, hb, st);

@@ -728,8 +728,9 @@ __device__ __forceinline__ void store_split4(float4 v, uint16_t* pieces, long lo
 __global__ void split_rows_kernel(const float* __restrict__ x, long long ld_x,
                                   const int* __restrict__ src, int rows, int cols,
                                   uint16_t* __restrict__ pieces, float* __restrict__ rinv,
-                                  long long piece_elems) {
+                                  long long piece_elems, const int* __restrict__ live) {
   const int lane = threadIdx.x & 31, c4 = cols / 4;
+  if (live) rows = min(rows, *live);
   const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
   for (long long r = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
        r < rows; r += warps) {
@@ -752,8 +753,10 @@ __device__ __forceinline__ float4 swiglu4(float4 g, float4 u) {
 // into pieces as split_rows_kernel does.
 __global__ void swiglu_split_kernel(const float* __restrict__ g, const float* __restrict__ u,
                                     int rows, int cols, uint16_t* __restrict__ pieces,
-                                    float* __restrict__ rinv, long long piece_elems) {
+                                    float* __restrict__ rinv, long long piece_elems,
+                                    const int* __restrict__ live) {
   const int lane = threadIdx.x & 31, c4 = cols / 4;
+  if (live) rows = min(rows, *live);
   const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
   for (long long r = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
        r < rows; r += warps) {
@@ -779,10 +782,10 @@ template <bool SWIGLU>
 __global__ void __launch_bounds__(kSplitThreads) split_rows_cta_kernel(
     const float* __restrict__ x, long long ld_x, const int* __restrict__ src,
     const float* __restrict__ u, int rows, int cols, uint16_t* __restrict__ pieces,
-    float* __restrict__ rinv, long long piece_elems) {
+    float* __restrict__ rinv, long long piece_elems, const int* __restrict__ live) {
   __shared__ float wmax[kSplitThreads / 32];
   const int r = blockIdx.x;
-  if (r >= rows) return;
+  if (r >= rows || (live && r >= *live)) return;
   const int c4 = cols / 4, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float4* xr = reinterpret_cast<const float4*>(
       SWIGLU ? x + static_cast<long long>(r) * cols : x + (src ? src[r] : r) * ld_x);
@@ -822,8 +825,10 @@ __global__ void __launch_bounds__(kSplitThreads) split_rows_cta_kernel(
 // xq_p[p] = xq[src[p]], xs_p[p] = xs[src[p]].
 __global__ void gather_rows_kernel(const int8_t* __restrict__ xq, const float* __restrict__ xs,
                                    const int* __restrict__ src, int rows, int cols,
-                                   int8_t* __restrict__ xq_p, float* __restrict__ xs_p) {
+                                   int8_t* __restrict__ xq_p, float* __restrict__ xs_p,
+                                   const int* __restrict__ live) {
   const int nb = cols / 32, c16 = cols / 16;
+  if (live) rows = min(rows, *live);
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
        i < static_cast<long long>(rows) * c16; i += stride) {
@@ -843,8 +848,10 @@ __global__ void gather_rows_kernel(const int8_t* __restrict__ xq, const float* _
 // (src/cpu/quantized.rs:43-74): one warp per 32-wide block.
 __global__ void swiglu_quantize_kernel(const float* __restrict__ g, const float* __restrict__ u,
                                        int rows, int cols, int8_t* __restrict__ hq,
-                                       float* __restrict__ hs, unsigned* status) {
+                                       float* __restrict__ hs, unsigned* status,
+                                       const int* __restrict__ live) {
   const int lane = threadIdx.x & 31, nb = cols / 32;
+  if (live) rows = min(rows, *live);
   const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
   for (long long w = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
        w < static_cast<long long>(rows) * nb; w += warps) {
@@ -1017,38 +1024,39 @@ cudaError_t launch_q8_tc_grouped_f32(const void* maps, int groups, const int* co
 }
 
 void launch_split_rows(const float* x, long long ld_x, const int* src, int rows, int cols,
-                       uint16_t* pieces, float* rinv, int sms, cudaStream_t st) {
+                       uint16_t* pieces, float* rinv, int sms, cudaStream_t st, const int* live) {
   if (rows <= 0) return;
   if (cols <= 4 * kSplitThreads * kSplitMaxV)
     split_rows_cta_kernel<false><<<rows, kSplitThreads, 0, st>>>(
-        x, ld_x, src, nullptr, rows, cols, pieces, rinv, static_cast<long long>(rows) * cols);
+        x, ld_x, src, nullptr, rows, cols, pieces, rinv, static_cast<long long>(rows) * cols, live);
   else
     split_rows_kernel<<<grid_for(static_cast<long long>(rows) * 32, sms), 256, 0, st>>>(
-        x, ld_x, src, rows, cols, pieces, rinv, static_cast<long long>(rows) * cols);
+        x, ld_x, src, rows, cols, pieces, rinv, static_cast<long long>(rows) * cols, live);
 }
 
 void launch_swiglu_split(const float* g, const float* u, int rows, int cols, uint16_t* pieces,
-                         float* rinv, int sms, cudaStream_t st) {
+                         float* rinv, int sms, cudaStream_t st, const int* live) {
   if (rows <= 0) return;
   if (cols <= 4 * kSplitThreads * kSplitMaxV)
     split_rows_cta_kernel<true><<<rows, kSplitThreads, 0, st>>>(
-        g, cols, nullptr, u, rows, cols, pieces, rinv, static_cast<long long>(rows) * cols);
+        g, cols, nullptr, u, rows, cols, pieces, rinv, static_cast<long long>(rows) * cols, live);
   else
     swiglu_split_kernel<<<grid_for(static_cast<long long>(rows) * 32, sms), 256, 0, st>>>(
-        g, u, rows, cols, pieces, rinv, static_cast<long long>(rows) * cols);
+        g, u, rows, cols, pieces, rinv, static_cast<long long>(rows) * cols, live);
 }
 
 void launch_gather_rows(const int8_t* xq, const float* xs, const int* src, int rows, int cols,
-                        int8_t* xq_p, float* xs_p, int sms, cudaStream_t st) {
+                        int8_t* xq_p, float* xs_p, int sms, cudaStream_t st, const int* live) {
   gather_rows_kernel<<<grid_for(static_cast<long long>(rows) * (cols / 16), sms), 256, 0, st>>>(
-      xq, xs, src, rows, cols, xq_p, xs_p);
+      xq, xs, src, rows, cols, xq_p, xs_p, live);
 }
 
 void launch_swiglu_quantize(const float* g, const float* u, int rows, int cols, int8_t* hq,
-                            float* hs, unsigned* status, int sms, cudaStream_t st) {
+                            float* hs, unsigned* status, int sms, cudaStream_t st,
+                            const int* live) {
   const long long warps = static_cast<long long>(rows) * (cols / 32);
   swiglu_quantize_kernel<<<grid_for(warps * 32, sms), 256, 0, st>>>(g, u, rows, cols, hq, hs,
-                                                                     status);
+                                                                     status, live);
 }
 
 }  // namespace uocr

@@ -349,6 +349,10 @@ class MoeLayer:
         self.n_experts = n
         self.hidden = shared[0].cols
 
+    @property
+    def handle(self):
+        return self._h
+
     def forward(self, x, logits, mode: int = QuantizationMode.WEIGHTS_ONLY):
         """Host tensors in, host tensors out: (y, ids, weights)."""
         x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, self.hidden)
@@ -424,10 +428,123 @@ class MoeLayer:
             pass
 
 
+EP_HANDLE_BYTES = 128
+
+
+class PeerExpertParallel:
+    """This GPU's end of a MoE layer whose routed experts are split over the
+    GPUs of one node, rows moving as stores into peer memory (uocr_ep_*).
+
+    ``local_layer`` holds the shared expert and experts
+    ``[rank_bounds[rank], rank_bounds[rank + 1])`` of an ``n_experts`` layer
+    (ids local to it); ``max_tokens`` bounds the tokens of one step on every
+    rank.  After ``connect`` (the handles of all ranks, in rank order, from
+    ``handle()`` on each) or ``connect_local`` (ranks of this process), every
+    step gives each rank ``Decoder::experts`` of its own tokens."""
+
+    def __init__(self, ctx: GpuContext, local_layer: "MoeLayer", n_experts: int, top_k: int,
+                 rank_bounds: Sequence[int], rank: int, max_tokens: int,
+                 normalize_topk: bool = False, routed_scale: float = 1.0):
+        world = len(rank_bounds) - 1
+        bounds = (ctypes.c_int32 * (world + 1))(*rank_bounds)
+        h = ctypes.c_void_p()
+        _check(lib().uocr_ep_create(ctx.handle, local_layer.handle, n_experts, top_k,
+                                    int(bool(normalize_topk)), float(routed_scale), bounds, world,
+                                    rank, max_tokens, ctypes.byref(h)))
+        self._h = h
+        self.ctx = ctx
+        self.layer = local_layer
+        self.world, self.rank = world, rank
+        self.n_experts, self.top_k, self.max_tokens = n_experts, top_k, max_tokens
+        self.hidden = local_layer.hidden
+
+    @property
+    def handle_ptr(self):
+        return self._h
+
+    def handle(self) -> bytes:
+        buf = ctypes.create_string_buffer(EP_HANDLE_BYTES)
+        _check(lib().uocr_ep_handle(self._h, buf))
+        return buf.raw
+
+    def connect(self, handles: Sequence[bytes]) -> None:
+        blob = b"".join(bytes(h) for h in handles)
+        if len(blob) != EP_HANDLE_BYTES * self.world:
+            raise OcrError(4, f"invalid tensor shape: expected {self.world} handles")
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        _check(lib().uocr_ep_connect(self._h, buf))
+
+    @staticmethod
+    def connect_local(eps: Sequence["PeerExpertParallel"]) -> None:
+        arr = (ctypes.c_void_p * len(eps))(*[e._h.value for e in eps])
+        _check(lib().uocr_ep_connect_local(arr, len(eps)))
+
+    def set_wait_limit(self, seconds: float) -> None:
+        _check(lib().uocr_ep_set_wait_limit(self._h, max(1, int(seconds * 1e9))))
+
+    def forward_device(self, x_t, logits_t, mode: int = QuantizationMode.WEIGHTS_ONLY, y_t=None,
+                       ids_t=None, wts_t=None):
+        """One step of this rank's tokens x [T, hidden] (T may be 0).
+        Asynchronous on the context's stream."""
+        import torch
+        t = x_t.shape[0]
+        y_t = y_t if y_t is not None else torch.empty_like(x_t)
+        ip = ctypes.c_void_p(_tptr(ids_t)) if ids_t is not None else None
+        wp = ctypes.c_void_p(_tptr(wts_t)) if wts_t is not None else None
+        _check(lib().uocr_ep_forward(self.ctx.handle, self._h, int(mode),
+                                     ctypes.c_void_p(_tptr(x_t)) if t else None,
+                                     ctypes.c_void_p(_tptr(logits_t)) if t else None, t,
+                                     ctypes.c_void_p(_tptr(y_t)) if t else None, ip, wp))
+        return y_t
+
+    def forward_host_ptrs(self, x_ptr: int, logits_ptr: int, tokens: int, y_ptr: int,
+                          mode: int = QuantizationMode.WEIGHTS_ONLY) -> None:
+        """Host buffers (raw pointers): copy in, one step, copy out, synchronise."""
+        _check(lib().uocr_ep_forward_host(self.ctx.handle, self._h, int(mode),
+                                          ctypes.c_void_p(x_ptr), ctypes.c_void_p(logits_ptr),
+                                          tokens, ctypes.c_void_p(y_ptr)))
+
+    def forward(self, x, logits, mode: int = QuantizationMode.WEIGHTS_ONLY) -> np.ndarray:
+        """Host tensors in, host tensor out (synchronous)."""
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, self.hidden)
+        logits = np.ascontiguousarray(logits, dtype=np.float32).reshape(x.shape[0], self.n_experts)
+        y = np.empty_like(x)
+        self.forward_host_ptrs(x.ctypes.data, logits.ctypes.data, x.shape[0], y.ctypes.data, mode)
+        return y
+
+    # the step in three parts (several ranks driven from one thread, one stream)
+    def dispatch_device(self, x_t, logits_t, mode: int, y_t) -> None:
+        t = x_t.shape[0]
+        _check(lib().uocr_ep_dispatch(self.ctx.handle, self._h, int(mode),
+                                      ctypes.c_void_p(_tptr(x_t)) if t else None,
+                                      ctypes.c_void_p(_tptr(logits_t)) if t else None, t,
+                                      ctypes.c_void_p(_tptr(y_t)) if t else None))
+
+    def experts_device(self) -> None:
+        _check(lib().uocr_ep_experts(self.ctx.handle, self._h))
+
+    def combine_device(self, y_t, ids_t=None, wts_t=None) -> None:
+        yp = ctypes.c_void_p(_tptr(y_t)) if y_t is not None and y_t.numel() else None
+        ip = ctypes.c_void_p(_tptr(ids_t)) if ids_t is not None and ids_t.numel() else None
+        wp = ctypes.c_void_p(_tptr(wts_t)) if wts_t is not None and wts_t.numel() else None
+        _check(lib().uocr_ep_combine(self.ctx.handle, self._h, yp, ip, wp))
+
+    def free(self) -> None:
+        if getattr(self, "_h", None):
+            lib().uocr_ep_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
 __all__ = ["BLOCK", "OcrError", "QuantizationMode", "GpuContext", "Int8Matrix", "MoeLayer",
            "route_device", "quantize_rows_device", "linear_multi_device", "default_context",
            "combine_device", "dispatch_device", "combine_rows_device",
-           "LibraryMissing", "QuantizedWeights"]
+           "LibraryMissing", "QuantizedWeights", "PeerExpertParallel", "EP_HANDLE_BYTES"]
 
 
 def __getattr__(name):

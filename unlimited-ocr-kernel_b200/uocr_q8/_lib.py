@@ -60,6 +60,17 @@ SIGNATURES = {
     "uocr_moe_combine": (I, [P, P, P, P, S, S, S, P]),
     "uocr_moe_dispatch": (I, [P, P, S, S, P, S, P, S, S, P, P, P]),
     "uocr_moe_combine_rows": (I, [P, P, P, P, P, S, S, S, P]),
+    "uocr_ep_create": (I, [P, P, S, S, I, F, P, S, S, S, PP]),
+    "uocr_ep_free": (I, [P]),
+    "uocr_ep_handle": (I, [P, P]),
+    "uocr_ep_connect": (I, [P, P]),
+    "uocr_ep_connect_local": (I, [P, S]),
+    "uocr_ep_set_wait_limit": (I, [P, ctypes.c_uint64]),
+    "uocr_ep_forward": (I, [P, P, I, P, P, S, P, P, P]),
+    "uocr_ep_forward_host": (I, [P, P, I, P, P, S, P]),
+    "uocr_ep_dispatch": (I, [P, P, I, P, P, S, P]),
+    "uocr_ep_experts": (I, [P, P]),
+    "uocr_ep_combine": (I, [P, P, P, P, P]),
     "uocr_feed_forward": (I, [P, P, P, P, I, P, S, P]),
     "uocr_linear_bf16": (I, [P, P, S, S, P, S, P]),
     "uocr_rms_norm": (I, [P, P, S, S, P, F, P]),

@@ -33,9 +33,13 @@ host synchronisation, so a whole step can be captured in a CUDA graph; the
 dispatch (slot assignment and row gather) and the combine (reading the
 returned rows by slot) run on the device.
 
-The collectives are torch.distributed's all_to_all_single: NCCL over NVLink on
-GPUs, gloo on the CPU.  The compute is a backend with the methods ``route``,
-``expert_rows``, ``shared_rows``, ``combine`` (counts form) and ``dispatch``,
+This module's exchange runs torch.distributed's all_to_all_single: NCCL over
+NVLink on GPUs, gloo on the CPU.  The library's own exchange
+(``uocr_q8.PeerExpertParallel``, uocr_ep_* in the C ABI) moves only the rows
+in use, as stores into the other GPUs' memory, and needs no collective;
+``peer_expert_parallel`` below builds it over a process group.
+
+The compute is a backend with the methods ``route``, ``expert_rows``, ``shared_rows``, ``combine`` (counts form) and ``dispatch``,
 ``combine_rows`` (fixed form); on GPUs it is ``LibraryBackend``, the CUDA
 library's C ABI (uocr_moe_route, uocr_moe_expert_rows, uocr_moe_shared_rows,
 uocr_moe_combine, uocr_moe_dispatch, uocr_moe_combine_rows), which runs on the
@@ -211,3 +215,20 @@ def local_layer(ctx, shared: Sequence, experts: Sequence[Sequence], bounds: Sequ
     mine = list(experts[bounds[rank]:bounds[rank + 1]])
     # top_k and the routing arguments are not used by the per-part calls
     return uocr_q8.MoeLayer(ctx, shared, mine, top_k=1)
+
+
+def peer_expert_parallel(ctx, local_layer, n_experts: int, top_k: int, max_tokens: int,
+                         group=None, normalize: bool = False, scale: float = 1.0):
+    """This rank's uocr_q8.PeerExpertParallel over the ranks of a process
+    group (one GPU each), connected: the handles of all ranks are gathered
+    with all_gather_object (any backend)."""
+    import uocr_q8
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    ep = uocr_q8.PeerExpertParallel(ctx, local_layer, n_experts, top_k,
+                                    expert_bounds(n_experts, world), rank, max_tokens,
+                                    normalize, scale)
+    handles = [None] * world
+    dist.all_gather_object(handles, ep.handle(), group=group)
+    ep.connect(handles)
+    return ep
