@@ -46,7 +46,7 @@
 // another projection kernel than the same rows on one GPU).
 //
 // The buffers are written only by plain stores and read after an acquire at
-// system scope: no multicast and no TMA touches peer memory.
+// system scope; no bulk or tensor-map copy ever reads peer memory.
 #include <cuda_runtime.h>
 
 #include <algorithm>
