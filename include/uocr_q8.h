@@ -91,6 +91,17 @@ int uocr_ctx_set_stream(uocr_ctx *ctx, void *stream);
 /* Wait for the context's stream; return and clear device-detected errors. */
 int uocr_ctx_sync(uocr_ctx *ctx);
 int uocr_ctx_device(const uocr_ctx *ctx, int *device, int *sm_count);
+/* No counterpart in the reference (which has no device waits).  The bounded
+ * device waits of the context's kernels (the one-token decode kernel's grid
+ * barrier) give up after `ns` nanoseconds (0: the default, about 2 s) and
+ * report UOCR_ERR_TIMEOUT at the next synchronising call. */
+int uocr_ctx_set_wait_limit(uocr_ctx *ctx, uint64_t ns);
+/* Failure-detection test hook, host-side (no GPU fault): while `hold` is
+ * nonzero, the one-token decode kernel's grid barrier waits for one arrival
+ * more than its grid makes, so every such launch runs out its wait limit and
+ * the next synchronising call reports UOCR_ERR_TIMEOUT.  The barrier's words
+ * stay valid: after the hold is cleared the next launch is exact again. */
+int uocr_ctx_hold_decode_barrier(uocr_ctx *ctx, int hold);
 
 /* ---- matrices: Int8Matrix (src/cpu/quantized.rs:11-237) -----------------
  * Int8Matrix::from_parts (:18-42): copies host weights/scales to the device.

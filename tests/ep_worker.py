@@ -142,6 +142,39 @@ def cpu_rank(rank, world, port, case):
         dist.destroy_process_group()
 
 
+def cpu_rank_leaves(rank, world, port, case):
+    """gloo ranks: both run one step, then the last rank leaves (returns
+    between steps, none of its collectives in flight); the others' next step
+    must fail with OcrError "Nccl" within the process group's timeout instead
+    of waiting for ever.  Each rank writes its outcome to case["out"]."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from uocr_q8 import OcrError
+    from uocr_q8.expert_parallel import ExpertParallelMoe, expert_bounds
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+    H, F, FS, E, k = case["hidden"], case["width"], case["shared_width"], case["experts"], case["top_k"]
+    shared, experts = make_layer(case["seed"], H, F, FS, E)
+    b = expert_bounds(E, world)
+    be = OracleBackend(shared, experts[b[rank]:b[rank + 1]], k, False, 1.0)
+    ep = ExpertParallelMoe(be, E, k, H, capacity=case.get("capacity"))
+    x, logits = rank_inputs(case["seed"], rank, 4, H, E)
+    ep.forward(torch.from_numpy(x), torch.from_numpy(logits), 0)
+    outcome = "left"
+    if rank != world - 1:
+        try:
+            ep.forward(torch.from_numpy(x), torch.from_numpy(logits), 0)
+            outcome = "no error"
+        except OcrError as exc:
+            outcome = exc.kind
+    with open(os.path.join(case["out"], f"rank{rank}"), "w") as f:
+        f.write(outcome)
+    if rank == world - 1:
+        os._exit(0)  # leave without a goodbye: the others learn it from the transport
+
+
 def gpu_rank(rank, world, port, case):
     """NCCL rank: ExpertParallelMoe over the CUDA library, each rank on its own
     GPU.  Its output must equal the single-GPU layer's (uocr_moe_forward over

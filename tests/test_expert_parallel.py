@@ -57,6 +57,20 @@ def test_ep_gloo_uneven_blocks_renormalised():
                                       scale=2.5, tokens=[9, 4]))
 
 
+@pytest.mark.parametrize("capacity", [None, 4 * 3])
+def test_ep_gloo_rank_leaves_between_steps(tmp_path, capacity):
+    """Failure detection on the host: after one step the last rank exits; the
+    other rank's next exchange raises OcrError "Nccl" (a dropped peer is an
+    error, not a hang), within the 10 s process-group timeout."""
+    import time
+    t0 = time.time()
+    spawn(ep_worker.cpu_rank_leaves, 2, dict(BASE, seed=12, tokens=[4, 4], capacity=capacity,
+                                              out=str(tmp_path)))
+    assert (tmp_path / "rank0").read_text() == "Nccl"
+    assert (tmp_path / "rank1").read_text() == "left"
+    assert time.time() - t0 < 60
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("case", [
     dict(BASE, hidden=256, width=128, shared_width=256, tokens=[37, 20]),

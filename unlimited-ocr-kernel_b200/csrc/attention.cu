@@ -29,6 +29,7 @@
 #include <cuda_runtime.h>
 
 #include "common.cuh"
+#include "device_once.h"
 #include "kernels.h"
 #include "tc_maps.cuh"
 
@@ -101,13 +102,10 @@ void launch_rms_norm(const float* x, long long ld_x, int rows, int width, const 
                      const float* res, float* sum) {
   if (rows <= 0) return;
   const size_t smem = static_cast<size_t>(width) * 4;
-  static unsigned configured = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(configured & (1u << (dev & 31)))) {
+  static PerDeviceOnce configured;
+  configured.run([] {
     cudaFuncSetAttribute(rms_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    configured |= 1u << (dev & 31);
-  }
+  });
   rms_norm_kernel<<<rows, kNormThreads, smem, st>>>(x, ld_x, width, w, eps, out, ld_out, res, sum,
                                                     status);
 }
@@ -431,16 +429,13 @@ cudaError_t launch_attention_decode(const AttnArgs& a, int batch, int max_tokens
   // 16-byte key loads: every row and head start aligned
   const bool vec = a.dim % 4 == 0 && a.row_stride % 4 == 0 && a.head_stride % 4 == 0 &&
                    a.seq_stride % 4 == 0 && reinterpret_cast<uintptr_t>(a.keys) % 16 == 0;
-  static unsigned configured = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(configured & (1u << (dev & 31)))) {
+  static PerDeviceOnce configured;
+  configured.run([] {
     cudaFuncSetAttribute(attn_decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(kAttnMaxSmem));
     cudaFuncSetAttribute(attn_decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(kAttnMaxSmem));
-    configured |= 1u << (dev & 31);
-  }
+  });
   const dim3 grid(a.heads, batch);
   if (vec)
     attn_decode_kernel<true><<<grid, kAttnThreads, smem, st>>>(a);
@@ -720,16 +715,13 @@ cudaError_t launch_attention_decode_tma(const AttnMaps& m, const AttnArgs& a, in
                                         cudaStream_t st) {
   const size_t smem = attn_tma_smem(a.dim, a.cap);
   if (smem > kAttnMaxSmem || batch <= 0 || a.heads <= 0) return cudaErrorInvalidValue;
-  static unsigned configured = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(configured & (1u << (dev & 31)))) {
+  static PerDeviceOnce configured;
+  configured.run([] {
     cudaFuncSetAttribute(attn_decode_tma_kernel<false>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kAttnMaxSmem));
     cudaFuncSetAttribute(attn_decode_tma_kernel<true>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kAttnMaxSmem));
-    configured |= 1u << (dev & 31);
-  }
+  });
   const CUtensorMap* km = reinterpret_cast<const CUtensorMap*>(m.k);
   const CUtensorMap* vm = reinterpret_cast<const CUtensorMap*>(m.v);
   if (a.dim == 128)

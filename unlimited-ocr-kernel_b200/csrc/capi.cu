@@ -281,6 +281,20 @@ int uocr_ctx_sync(uocr_ctx* ctx) {
   return take_device_status(ctx);
 }
 
+int uocr_ctx_set_wait_limit(uocr_ctx* ctx, uint64_t ns) {
+  if (!ctx) return fail(UOCR_ERR_INVALID, "null context");
+  if (ns > (uint64_t{1} << 40))
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: wait limit above 1099 s");
+  ctx->wait_ns = ns;
+  return ok();
+}
+
+int uocr_ctx_hold_decode_barrier(uocr_ctx* ctx, int hold) {
+  if (!ctx) return fail(UOCR_ERR_INVALID, "null context");
+  ctx->hold_barrier = hold ? 1 : 0;
+  return ok();
+}
+
 int uocr_ctx_device(const uocr_ctx* ctx, int* device, int* sm_count) {
   if (!ctx) return fail(UOCR_ERR_INVALID, "null context");
   if (device) *device = ctx->device;
@@ -871,6 +885,10 @@ static int decode_launch(uocr_ctx* ctx, int mode, MoeDecodeArgs& a, const float*
   a.y = y;
   a.status = ctx->status_dev;
   a.grid_sync = ctx->status_dev + 16;  // zeroed at context creation, decode-only
+  // nanoseconds to SM cycles at the 1.965 GHz maximum clock, rounded up (a
+  // lower clock only lengthens the wait)
+  a.wait_cycles = ctx->wait_ns ? static_cast<long long>(ctx->wait_ns * 2) : 0;
+  a.barrier_extra = ctx->hold_barrier ? 1u : 0u;
   cudaError_t e = launch_moe_decode(mode == UOCR_WEIGHTS_ONLY ? MODE_FP32 : MODE_INT8, a, ctx->sms,
                                     ctx->stream, pdl);
   if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "moe decode launch: %s", cudaGetErrorString(e));

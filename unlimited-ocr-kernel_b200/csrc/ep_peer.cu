@@ -117,6 +117,7 @@ struct EpDev {
   int* live;            // [world] rows received from each source this step
   unsigned* status;
   unsigned long long wait_ns;
+  int sys;  // some peer is another GPU: fences at system scope, else GPU scope
 };
 
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
@@ -154,18 +155,40 @@ __device__ __forceinline__ int pair_owner(const EpDev& d, const int32_t* ids, in
   return d.owner_of[e];
 }
 
-// The last CTA of a grid to arrive on counter *c: every thread's prior global
-// stores (peer memory included) are ordered before the caller's following
-// stores by the system-scope fences around the arrival.
-__device__ __forceinline__ bool last_to_arrive(unsigned* c) {
+// cnt[owner] += pairs [0, n) per owner, by the whole CTA: one shared atomic
+// per owner present in each warp's 32 pairs.
+__device__ __forceinline__ void count_owners(const EpDev& d, const int32_t* ids, int n, int* cnt) {
+  const int lane = threadIdx.x & 31;
+  for (int q0 = threadIdx.x & ~31; q0 < n; q0 += blockDim.x) {
+    const int q = q0 + lane;
+    const int o = q < n ? pair_owner(d, ids, q) : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, o);
+    if (o >= 0 && lane == __ffs(peers) - 1) atomicAdd(&cnt[o], __popc(peers));
+  }
+}
+
+__device__ __forceinline__ void fence_for(const EpDev& d) {
+  if (d.sys)
+    __threadfence_system();
+  else
+    __threadfence();
+}
+
+// The last CTA of a grid to arrive on counter *c.  The CTA barrier orders the
+// CTA's stores (peer memory included) before its first thread's system-scope
+// fence and arrival; the last CTA's fence after the arrival orders every
+// CTA's stores before what it stores next (the pattern of a grid barrier,
+// one fence per CTA instead of one per thread).
+__device__ __forceinline__ bool last_to_arrive(const EpDev& d, unsigned* c) {
   __shared__ int last;
-  __threadfence_system();
   __syncthreads();
-  if (threadIdx.x == 0) last = atomicAdd(c, 1u) == gridDim.x - 1u;
+  if (threadIdx.x == 0) {
+    fence_for(d);
+    last = atomicAdd(c, 1u) == gridDim.x - 1u;
+    if (last) fence_for(d);
+  }
   __syncthreads();
-  if (!last) return false;
-  __threadfence_system();
-  return true;
+  return last != 0;
 }
 
 // Dispatch: CTA c moves pairs [8c, 8c + 8), one warp per pair; a pair's slot
@@ -181,7 +204,7 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(
   const int p0 = blockIdx.x * kEpWarps;
   for (int r = tid; r < d.world; r += kEpThreads) cnt[r] = 0;
   __syncthreads();
-  for (int q = tid; q < min(p0, P); q += kEpThreads) atomicAdd(&cnt[pair_owner(d, ids, q)], 1);
+  count_owners(d, ids, min(p0, P), cnt);
   if (tid < kEpWarps) own[tid] = p0 + tid < P ? pair_owner(d, ids, p0 + tid) : -1;
   __syncthreads();
   const int p = p0 + warp;
@@ -202,15 +225,14 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(
       reinterpret_cast<int*>(base + d.L.recv_pair)[row] = p;
     }
   }
-  if (!last_to_arrive(d.ctr + kCtrDispatch)) return;
+  if (!last_to_arrive(d, d.ctr + kCtrDispatch)) return;
   for (int r = tid; r < d.world; r += kEpThreads) cnt[r] = 0;
   __syncthreads();
-  for (int q = tid; q < P; q += kEpThreads) atomicAdd(&cnt[pair_owner(d, ids, q)], 1);
+  count_owners(d, ids, P, cnt);
   __syncthreads();
   for (int r = tid; r < d.world; r += kEpThreads) {
     char* base = d.peers[r];
     reinterpret_cast<volatile int*>(base + d.L.recv_count)[d.rank] = cnt[r];
-    __threadfence_system();
     st_release_sys(reinterpret_cast<unsigned*>(base + d.L.recv_flag) + d.rank, step);
   }
   if (tid == 0) d.ctr[kCtrDispatch] = 0u;
@@ -245,10 +267,13 @@ __global__ void __launch_bounds__(kEpThreads) ep_recv_wait_kernel(const __grid_c
     if (i % d.cap >= cnt[i / d.cap]) rid[i] = -1;
 }
 
-// Return: the output row of every received pair (out_slots, in slot order)
-// into its source's ret_rows at the pair index; one warp per row.
+// Return: the output row of every received pair into its source's ret_rows
+// at the pair index; one warp per row.  The row of slot i is row
+// token_pos[i] of `rows` (the experts' grouped outputs), or row i when
+// token_pos is null (outputs already in slot order).
 __global__ void __launch_bounds__(kEpThreads) ep_return_kernel(const __grid_constant__ EpDev d,
-                                                               const float* __restrict__ out_slots) {
+                                                               const float* __restrict__ rows,
+                                                               const int* __restrict__ token_pos) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const unsigned step = d.ctr[kCtrStep] + 1u;
   const int* pair = reinterpret_cast<const int*>(d.peers[d.rank] + d.L.recv_pair);
@@ -261,11 +286,16 @@ __global__ void __launch_bounds__(kEpThreads) ep_return_kernel(const __grid_cons
       if (lane == 0) flag(d.status, DEV_BAD_ROUTE);
       continue;
     }
+    const int src_row = token_pos ? token_pos[i] : i;
+    if (src_row < 0) {
+      if (lane == 0) flag(d.status, DEV_BAD_ROUTE);
+      continue;
+    }
     float4* dst = reinterpret_cast<float4*>(d.peers[s] + d.L.ret_rows) + static_cast<long long>(p) * h4;
-    const float4* src = reinterpret_cast<const float4*>(out_slots) + static_cast<long long>(i) * h4;
+    const float4* src = reinterpret_cast<const float4*>(rows) + static_cast<long long>(src_row) * h4;
     for (int c = lane; c < h4; c += 32) dst[c] = src[c];
   }
-  if (!last_to_arrive(d.ctr + kCtrReturn)) return;
+  if (!last_to_arrive(d, d.ctr + kCtrReturn)) return;
   for (int r = threadIdx.x; r < d.world; r += kEpThreads)
     st_release_sys(reinterpret_cast<unsigned*>(d.peers[r] + d.L.ret_flag) + d.rank, step);
   if (threadIdx.x == 0) d.ctr[kCtrReturn] = 0u;
@@ -399,6 +429,7 @@ struct uocr_ep {
   char* io = nullptr;
   char* io_host = nullptr;
   size_t io_x = 0, io_l = 0;  // byte offsets of logits and y
+  bool cross_device = false;  // some peer is another GPU (set when connecting)
   // the step begun by uocr_ep_dispatch
   int step_tokens = -1;
   int step_mode = 0;
@@ -422,6 +453,7 @@ EpDev ep_dev(const uocr_ep* ep, const uocr_ctx* ctx) {
   d.live = ep->live;
   d.status = ctx->status_dev;
   d.wait_ns = ep->wait_ns;
+  d.sys = ep->cross_device ? 1 : 0;
   return d;
 }
 
@@ -455,6 +487,10 @@ MoePrefillArgs routed_args(const uocr_ep* ep, const uocr_ctx* ctx, int first, in
   a.skip_negative_ids = 1;
   a.pair_out = ep->out_slots + static_cast<long long>(first) * ep->hidden;
   a.max_group_rows = max_group;
+  // every group on the warp-level kernel, one CTA per 8-row chunk (at decode
+  // batch sizes groups hold tens of rows; a large group re-reads its
+  // weights from L2 once per chunk)
+  a.small_max = max_group;
   a.workspace = ep->ws_routed;
   a.workspace_bytes = ep->ws_routed_bytes;
   return a;
@@ -527,21 +563,28 @@ int enqueue_experts(uocr_ctx* ctx, uocr_ep* ep, int mode, cudaStream_t rs) {
   ep_recv_wait_kernel<<<1, kEpThreads, 0, rs>>>(d);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_err(e, "expert-parallel wait");
+  const float* rows = ep->out_slots;
+  const int* token_pos = nullptr;
   if (mode == UOCR_DYNAMIC_ACTIVATIONS) {
-    // a group's row count selects its arithmetic: one call per source block
+    // a group's row count selects its arithmetic: one call per source block,
+    // outputs into out_slots in slot order
     for (int s = 0; s < ep->world && e == cudaSuccess; ++s)
       e = launch_moe_prefill(mode, routed_args(ep, ctx, s * ep->cap, ep->cap, ep->max_tokens),
                              ctx->sms, rs);
   } else {
-    e = launch_moe_prefill(mode,
-                           routed_args(ep, ctx, 0, ep->world * ep->cap, ep->world * ep->max_tokens),
-                           ctx->sms, rs);
+    // one call over every source block; the return reads the grouped outputs
+    MoePrefillArgs a =
+        routed_args(ep, ctx, 0, ep->world * ep->cap, ep->world * ep->max_tokens);
+    a.pair_out = nullptr;
+    a.keep_grouped = 1;
+    e = launch_moe_prefill(mode, a, ctx->sms, rs);
+    moe_prefill_grouped(a, mode, &token_pos, &rows);
   }
   if (e != cudaSuccess) return cuda_err(e, "expert-parallel experts");
   const int total_warps = ep->world * ep->cap;
   int grid = (total_warps + kEpWarps - 1) / kEpWarps;
   if (grid > 2 * ctx->sms) grid = 2 * ctx->sms;
-  ep_return_kernel<<<grid, kEpThreads, 0, rs>>>(d, ep->out_slots);
+  ep_return_kernel<<<grid, kEpThreads, 0, rs>>>(d, rows, token_pos);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_err(e, "expert-parallel return");
   return UOCR_OK;
@@ -770,6 +813,7 @@ int uocr_ep_connect(uocr_ep* ep, const void* handles) {
     }
     ep->peers[r] = static_cast<char*>(p);
     ep->opened[r] = true;
+    ep->cross_device = true;  // another process: fences at system scope
   }
   return finish_connect(ep);
 }
@@ -792,6 +836,7 @@ int uocr_ep_connect_local(uocr_ep* const* eps, size_t world) {
     for (size_t q = 0; q < world; ++q) {
       ep->peers[q] = eps[q]->region;
       if (eps[q]->device != ep->device) {
+        ep->cross_device = true;
         const cudaError_t e = cudaDeviceEnablePeerAccess(eps[q]->device, 0);
         if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled)
           return cuda_err(e, "cudaDeviceEnablePeerAccess");

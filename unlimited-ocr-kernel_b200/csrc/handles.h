@@ -45,6 +45,10 @@ struct uocr_ctx {
   // runs on `stream`), forked and joined through the two events
   cudaStream_t side_stream = nullptr;
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+  // uocr_ctx_set_wait_limit (0: the kernels' default) and the failure-detection
+  // test hook uocr_ctx_hold_decode_barrier
+  uint64_t wait_ns = 0;
+  int hold_barrier = 0;
 };
 
 struct uocr_q8 {

@@ -109,8 +109,9 @@ void launch_swiglu_quantize(const float* g, const float* u, int rows, int cols, 
 // up in one launch).  x_rows: rows of the int8 activation tensors.
 // N % 128 == 0, K % 128 == 0.
 constexpr int kSmallRowsMax = 16;
-// Grouped launches may take groups of up to this many rows, as 8-row chunks
-// (one CTA each, the group's weights re-read from L2).
+// Grouped launches without a chunk list may take groups of up to this many
+// rows, as 8-row chunks (one CTA each, the group's weights re-read from L2);
+// with a chunk list, groups of any size.
 constexpr int kSmallChunkedMax = 64;
 // Upper bound on the 8-row chunks of `pairs` rows in `groups` groups (the
 // length of the chunk list group_pairs_kernel writes, without its count).
@@ -146,6 +147,11 @@ struct MoeDecodeArgs {
   float* y;             // [hidden]
   unsigned* status;
   unsigned* grid_sync;  // 4 words, zero before first use, owned by this stream
+  // bounded waits: the grid barrier gives up after this many SM cycles (0: the
+  // default, about 2 s); barrier_extra > 0 makes it wait for arrivals that
+  // never come (host-side fault injection for failure-detection tests)
+  long long wait_cycles;
+  unsigned barrier_extra;
 };
 bool moe_decode_supported(const MoeDecodeArgs& a, int sms);
 // pdl: allow programmatic dependent launch of the next kernel (off for
@@ -184,6 +190,13 @@ struct MoePrefillArgs {
   // whose rows come from several sources of at most this many tokens each
   // selects the kernels by it)
   int max_group_rows;
+  // optional (0 = default): groups of up to this many rows run on the
+  // warp-level kernel (one CTA per 8-row chunk) when some group can be
+  // larger, the rest on the tensor-core GEMMs; the default is kSmallRowsMax
+  int small_max;
+  // routed part only: leave the expert outputs grouped (no pair_out); read
+  // them with moe_prefill_grouped
+  int keep_grouped;
   // optional: a second stream (of high priority) and two events; up to
   // kSmallChunkedMax tokens the routing and the routed experts then run on
   // `side` while the shared expert runs on the call's stream (forked after the
@@ -192,6 +205,10 @@ struct MoePrefillArgs {
   cudaEvent_t ev_fork, ev_join;
 };
 size_t moe_prefill_workspace(const MoePrefillArgs& a, int mode);
+// The grouped outputs of a keep_grouped call: the output of pair (row) i is
+// row token_pos[i] of out_rows (token_pos -1: an unused row).
+void moe_prefill_grouped(const MoePrefillArgs& a, int mode, const int** token_pos,
+                         const float** out_rows);
 cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaStream_t st);
 // Fixed-capacity dispatch for expert parallelism (see moe_prefill.cu).
 constexpr int kMaxDispatchRanks = 64;

@@ -35,6 +35,7 @@
 // reference's order: r = shared; r += p_e * out_e for e ascending, one
 // rounding per op.
 #include "common.cuh"
+#include "device_once.h"
 #include "kernels.h"
 #include "route.cuh"
 
@@ -118,12 +119,12 @@ __device__ __forceinline__ void red_release_gpu_add(unsigned* p, unsigned v) {
 // path: the last arrival's one-way trip to L2 and one observed load.  A
 // launch that timed out still leaves the words ready for the next one.
 __device__ __forceinline__ bool grid_barrier(unsigned* sync, unsigned gen, unsigned nblocks,
-                                             unsigned* status) {
+                                             unsigned* status, long long limit) {
   unsigned* cnt = sync + 2 + (gen & 1u);
   red_release_gpu_add(cnt, 1u);
   const long long t0 = clock64();
   while (ld_acquire_gpu(cnt) < nblocks) {
-    if (clock64() - t0 > kWaitLimitCycles) {
+    if (clock64() - t0 > limit) {
       flag(status, DEV_TIMEOUT);
       return false;
     }
@@ -468,7 +469,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const __grid_co
   // ---- every CTA's slice of h is in global memory
   named_barrier(1, kConsumerThreads);
   if (threadIdx.x == 0) {
-    grid_barrier(a.grid_sync, barrier_gen, gridDim.x, a.status);
+    grid_barrier(a.grid_sync, barrier_gen, gridDim.x + a.barrier_extra, a.status,
+                 a.wait_cycles > 0 ? a.wait_cycles : kWaitLimitCycles);
     if (blockIdx.x == 0) a.grid_sync[1] = barrier_gen + 1u;
   }
   named_barrier(1, kConsumerThreads);
@@ -626,16 +628,13 @@ cudaError_t launch_moe_decode(int mode, const MoeDecodeArgs& a, int sms, cudaStr
 
   using Fn = void (*)(MoeDecodeArgs, DecodeLayout);
   Fn fn = mode == MODE_INT8 ? moe_decode_kernel<MODE_INT8> : moe_decode_kernel<MODE_FP32>;
-  static unsigned configured = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(configured & (1u << (dev & 31)))) {
+  static PerDeviceOnce configured;
+  configured.run([] {
     cudaFuncSetAttribute(moe_decode_kernel<MODE_FP32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          kSmemBudget);
     cudaFuncSetAttribute(moe_decode_kernel<MODE_INT8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          kSmemBudget);
-    configured |= 1u << (dev & 31);
-  }
+  });
   // Cooperative: all CTAs co-resident (the grid barrier needs it).  PDL: the
   // next step's kernel may launch early; its CTAs wait in
   // griddepcontrol.wait before reading anything this one writes.

@@ -34,7 +34,7 @@ __global__ void __launch_bounds__(kGroupThreads) group_pairs_kernel(
     const int32_t* __restrict__ ids, const float* __restrict__ wts, int tokens, int top_k,
     int n_experts, int skip_negative, int* __restrict__ counts, int* __restrict__ offsets,
     int* __restrict__ pair_token, float* __restrict__ pair_weight, int* __restrict__ token_pos,
-    int* __restrict__ items, unsigned* status) {
+    int* __restrict__ items, int items_max, unsigned* status) {
   __shared__ int cnt[kGroupThreads / 32][kMaxGroupExperts];
   __shared__ int base[kMaxGroupExperts];
   __shared__ int off[kMaxGroupExperts + 1];
@@ -70,13 +70,15 @@ __global__ void __launch_bounds__(kGroupThreads) group_pairs_kernel(
     int chunks = 0;  // first list position of each group's 8-row chunks
     for (int e = 0; e < n_experts; ++e) {
       first[e] = chunks;
-      chunks += (off[e + 1] - off[e] + 7) / 8;
+      const int c = off[e + 1] - off[e];
+      if (c <= items_max) chunks += (c + 7) / 8;  // larger groups: the tensor-core GEMMs
     }
     first[n_experts] = chunks;
   }
   __syncthreads();
   if (items) {
-    // the list of 8-row chunks of every group (small_rows_kernel's work)
+    // the list of 8-row chunks of every group of at most items_max rows
+    // (small_rows_kernel's work)
     if (tid == 0) items[0] = first[n_experts];
     for (int e = warp; e < n_experts; e += kGroupThreads / 32)
       for (int c = lane; c < first[e + 1] - first[e]; c += 32) items[1 + first[e] + c] = c << 8 | e;
@@ -642,22 +644,30 @@ size_t moe_prefill_workspace(const MoePrefillArgs& a, int mode) {
   return carve(a, nullptr, prefill_path(a, mode)).bytes;
 }
 
+void moe_prefill_grouped(const MoePrefillArgs& a, int mode, const int** token_pos,
+                         const float** out_rows) {
+  const PrefillWs w = carve(a, a.workspace, prefill_path(a, mode));
+  *token_pos = w.token_pos;
+  *out_rows = w.out_r;
+}
+
 // Token counts up to which the shared expert (one matrix, every token) runs on
 // the warp-level kernel: its tcgen05 tiles would occupy only N / 128 SMs.
 constexpr int kSmallShared = 64;
 
-// counts_big[g] = counts[g] when it exceeds kSmallRowsMax, else 0 (the
+// counts_big[g] = counts[g] when it exceeds `small` rows, else 0 (the
 // tensor-core GEMMs take the big groups, the warp-level kernel the others).
-__global__ void big_counts_kernel(const int* __restrict__ counts, int groups,
+__global__ void big_counts_kernel(const int* __restrict__ counts, int groups, int small,
                                   int* __restrict__ counts_big) {
   for (int g = threadIdx.x; g < groups; g += blockDim.x) {
     const int c = counts[g];
-    counts_big[g] = c > kSmallRowsMax ? c : 0;
+    counts_big[g] = c > small ? c : 0;
   }
 }
 
-static void launch_big_counts(const int* counts, int groups, int* counts_big, cudaStream_t st) {
-  big_counts_kernel<<<1, 256, 0, st>>>(counts, groups, counts_big);
+static void launch_big_counts(const int* counts, int groups, int small, int* counts_big,
+                              cudaStream_t st) {
+  big_counts_kernel<<<1, 256, 0, st>>>(counts, groups, small, counts_big);
 }
 
 // Upper bound on the 64-row tiles of the groups the tensor-core GEMMs take
@@ -673,6 +683,24 @@ static int big_group_tiles(int P, int E) {
 // The largest group a call can form: tokens, or the caller's bound.
 static int max_group_rows(const MoePrefillArgs& a) {
   return a.max_group_rows > 0 && a.max_group_rows < a.tokens ? a.max_group_rows : a.tokens;
+}
+
+// Groups of up to this many rows run on the warp-level kernel (from the chunk
+// list, one CTA per 8-row chunk), larger ones on the tensor-core GEMMs: every
+// group when no group can exceed kSmallChunkedMax rows, else the caller's
+// bound or kSmallRowsMax.
+static int small_group_rows(const MoePrefillArgs& a) {
+  const int G = max_group_rows(a);
+  if (G <= kSmallChunkedMax) return G > 1 ? G : 1;
+  if (a.small_max > 0) return a.small_max;
+  return kSmallRowsMax;
+}
+
+// Grid rows of a chunk-list launch: the list holds the chunks of groups of at
+// most R rows, so with larger groups possible (tc) at most n_experts * R/8.
+static int items_bound(const MoePrefillArgs& a, const PrefillWs& w, int R, bool tc) {
+  const int by_groups = a.n_experts * ((R + 7) / 8);
+  return tc && by_groups < w.max_items ? by_groups : w.max_items;
 }
 
 // With unused rows (negative ids) the grouped rows in use are the first
@@ -710,18 +738,17 @@ static cudaError_t prefill_tc_f32(const MoePrefillArgs& a, const PrefillWs& w, i
   cudaError_t e;
   // no group exceeds T rows: up to kSmallChunkedMax tokens every group runs on
   // the warp-level kernel and the tensor-core launches are skipped
-  const int G = max_group_rows(a);
-  const bool tc = G > kSmallChunkedMax;
-  const int R = tc ? kSmallRowsMax : (G > 1 ? G : 1);
+  const int R = small_group_rows(a);
+  const bool tc = max_group_rows(a) > R;
   const int* live = grouped_live(a, w);
+  const int ni = items_bound(a, w, R, tc);
   if (!a.skip_routed) {
-    if (tc) launch_big_counts(w.counts, E, w.counts_big, st);
+    if (tc) launch_big_counts(w.counts, E, R, w.counts_big, st);
     launch_split_rows(a.x, H, w.pair_token, P, H, w.xp_r, w.xr_r, sms, st, live);
     // gate and up of the small groups in one launch
     if ((e = launch_small_rows(false, maps, nullptr, w.counts, w.offsets, E, 1, R, 0, F, H, w.xp_r,
                                P, w.xr_r, nullptr, nullptr, P, w.h_r, F, a.status, st,
-                               tc ? nullptr : w.items, w.max_items, maps + E * mb, nullptr,
-                               w.u_r)))
+                               w.items, ni, maps + E * mb, nullptr, w.u_r)))
       return e;
     for (int j = 0; tc && j < 2; ++j)  // gate, up of the larger groups
       if ((e = launch_q8_tc_grouped_f32(maps + j * E * mb, E, w.counts_big, w.offsets, max_tiles,
@@ -731,8 +758,7 @@ static cudaError_t prefill_tc_f32(const MoePrefillArgs& a, const PrefillWs& w, i
     launch_swiglu_split(w.h_r, w.u_r, P, F, w.hp_r, w.hr_r, sms, st, live);
     if ((e = launch_small_rows(false, maps + 2 * E * mb, nullptr, w.counts, w.offsets, E, 1, R, 0, H,
                                  F, w.hp_r, P, w.hr_r, nullptr, nullptr, P, w.out_r, H,
-                                 a.status, st,
-                                 tc ? nullptr : w.items, w.max_items)) ||
+                                 a.status, st, w.items, ni)) ||
         (tc && (e = launch_q8_tc_grouped_f32(maps + 2 * E * mb, E, w.counts_big, w.offsets,
                                              max_tiles, H, F, w.hp_r, w.hr_r, P, w.out_r, H,
                                              a.status, st))))
@@ -756,20 +782,19 @@ static cudaError_t prefill_tc(const MoePrefillArgs& a, const PrefillWs& w, int s
   const unsigned char* maps = static_cast<const unsigned char*>(a.tc_maps);
   const size_t mb = q8_tc_maps_bytes();  // per matrix
   cudaError_t e;
-  const int G = max_group_rows(a);
-  const bool tc = G > kSmallChunkedMax;
-  const int R = tc ? kSmallRowsMax : (G > 1 ? G : 1);
+  const int R = small_group_rows(a);
+  const bool tc = max_group_rows(a) > R;
   const int* live = grouped_live(a, w);
+  const int ni = items_bound(a, w, R, tc);
   if (!a.skip_routed) {
     // routed experts: rows gathered per expert; groups of <= R rows on the
     // warp-level kernel, larger ones on the tensor-core GEMM
-    if (tc) launch_big_counts(w.counts, E, w.counts_big, st);
+    if (tc) launch_big_counts(w.counts, E, R, w.counts_big, st);
     launch_gather_rows(w.xq, w.xs, w.pair_token, P, H, w.xq_p, w.xs_p, sms, st, live);
     // gate and up of the small groups in one launch
     if ((e = launch_small_rows(true, maps, nullptr, w.counts, w.offsets, E, 1, R, 0, F, H, nullptr,
                                0, nullptr, w.xq_p, w.xs_p, P, w.h_r, F, a.status, st,
-                               tc ? nullptr : w.items, w.max_items, maps + E * mb, nullptr,
-                               w.u_r)))
+                               w.items, ni, maps + E * mb, nullptr, w.u_r)))
       return e;
     for (int j = 0; tc && j < 2; ++j)  // gate, up of the larger groups
       if ((e = launch_q8_tc_grouped_i8(maps + j * E * mb, E, w.counts_big, w.offsets, max_tiles,
@@ -779,8 +804,7 @@ static cudaError_t prefill_tc(const MoePrefillArgs& a, const PrefillWs& w, int s
     launch_swiglu_quantize(w.h_r, w.u_r, P, F, w.hq_r, w.hs_r, a.status, sms, st, live);
     if ((e = launch_small_rows(true, maps + 2 * E * mb, nullptr, w.counts, w.offsets, E, 1, R, 0, H,
                                  F, nullptr, 0, nullptr, w.hq_r, w.hs_r, P, w.out_r, H,
-                                 a.status, st,
-                                 tc ? nullptr : w.items, w.max_items)) ||
+                                 a.status, st, w.items, ni)) ||
         (tc && (e = launch_q8_tc_grouped_i8(maps + 2 * E * mb, E, w.counts_big, w.offsets,
                                             max_tiles, H, F, w.hq_r, w.hs_r, P, w.out_r, H,
                                             a.status, st))))
@@ -818,24 +842,23 @@ static cudaError_t prefill_tc_mixed(const MoePrefillArgs& a, const PrefillWs& w,
   const int max_tiles = big_group_tiles(P, E);
   const unsigned char* maps = static_cast<const unsigned char*>(a.tc_maps);
   const size_t mb = q8_tc_maps_bytes();
-  const int G = max_group_rows(a);
-  const bool tc = G > kSmallChunkedMax;
-  const int R = tc ? kSmallRowsMax : (G > 2 ? G : 2);
+  const int R0 = small_group_rows(a);
+  const int R = R0 > 2 ? R0 : 2;
+  const bool tc = max_group_rows(a) > R0;
   const int* live = grouped_live(a, w);
+  const int ni = items_bound(a, w, R, tc);
   cudaError_t e;
   if (!a.skip_routed) {
-    if (tc) launch_big_counts(w.counts, E, w.counts_big, st);
+    if (tc) launch_big_counts(w.counts, E, R, w.counts_big, st);
     launch_gather_rows(w.xq, w.xs, w.pair_token, P, H, w.xq_p, w.xs_p, sms, st, live);
     launch_split_rows(a.x, H, w.pair_token, P, H, w.xp_r, w.xr_r, sms, st, live);
     // gate and up together: one-row groups int8, 2..R rows FP32, larger on the GEMM
     if ((e = launch_small_rows(true, maps, nullptr, w.counts, w.offsets, E, 1, 1, 0, F, H, nullptr,
                                0, nullptr, w.xq_p, w.xs_p, P, w.h_r, F, a.status, st,
-                               tc ? nullptr : w.items, w.max_items, maps + E * mb, nullptr,
-                               w.u_r)) ||
+                               w.items, ni, maps + E * mb, nullptr, w.u_r)) ||
         (e = launch_small_rows(false, maps, nullptr, w.counts, w.offsets, E, 2, R, 0, F, H, w.xp_r,
                                P, w.xr_r, nullptr, nullptr, P, w.h_r, F, a.status, st,
-                               tc ? nullptr : w.items, w.max_items, maps + E * mb, nullptr,
-                               w.u_r)))
+                               w.items, ni, maps + E * mb, nullptr, w.u_r)))
       return e;
     for (int j = 0; tc && j < 2; ++j)
       if ((e = launch_q8_tc_grouped_f32(maps + j * E * mb, E, w.counts_big, w.offsets, max_tiles,
@@ -846,12 +869,10 @@ static cudaError_t prefill_tc_mixed(const MoePrefillArgs& a, const PrefillWs& w,
     launch_swiglu_split(w.h_r, w.u_r, P, F, w.hp_r, w.hr_r, sms, st, live);
     if ((e = launch_small_rows(true, maps + 2 * E * mb, nullptr, w.counts, w.offsets, E, 1, 1, 0, H,
                                  F, nullptr, 0, nullptr, w.hq_r, w.hs_r, P, w.out_r, H,
-                                 a.status, st,
-                                 tc ? nullptr : w.items, w.max_items)) ||
+                                 a.status, st, w.items, ni)) ||
         (e = launch_small_rows(false, maps + 2 * E * mb, nullptr, w.counts, w.offsets, E, 2, R, 0, H,
                                  F, w.hp_r, P, w.hr_r, nullptr, nullptr, P, w.out_r, H,
-                                 a.status, st,
-                                 tc ? nullptr : w.items, w.max_items)) ||
+                                 a.status, st, w.items, ni)) ||
         (tc && (e = launch_q8_tc_grouped_f32(maps + 2 * E * mb, E, w.counts_big, w.offsets,
                                              max_tiles, H, F, w.hp_r, w.hr_r, P, w.out_r, H,
                                              a.status, st))))
@@ -880,7 +901,8 @@ static cudaError_t prefill_tc_mixed(const MoePrefillArgs& a, const PrefillWs& w,
 cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaStream_t st) {
   if (a.n_experts > kMaxGroupExperts || a.top_k > 8) return cudaErrorInvalidValue;
   if (a.skip_shared && a.skip_routed) return cudaErrorInvalidValue;
-  if (a.skip_shared && !a.skip_routed && !a.pair_out) return cudaErrorInvalidValue;
+  if (a.skip_shared && !a.skip_routed && !a.pair_out && !a.keep_grouped)
+    return cudaErrorInvalidValue;
   const Path path = prefill_path(a, mode);
   PrefillWs w = carve(a, a.workspace, path);
   if (w.bytes > a.workspace_bytes) return cudaErrorInvalidValue;
@@ -910,8 +932,10 @@ cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaS
     group_pairs_kernel<<<1, kGroupThreads, 0, rs>>>(a.route_ids, a.route_weights, T, k, E,
                                                    a.skip_negative_ids, w.counts, w.offsets,
                                                    w.pair_token, w.pair_weight, w.token_pos,
-                                                   max_group_rows(a) <= kSmallChunkedMax
-                                                       ? w.items : nullptr,
+                                                   path == Path::CudaCore ? nullptr : w.items,
+                                                   path == Path::TcMixed
+                                                       ? (small_group_rows(a) > 2 ? small_group_rows(a) : 2)
+                                                       : small_group_rows(a),
                                                    a.status);
   }
   if (a.skip_negative_ids && !a.skip_routed && path == Path::CudaCore) {
@@ -976,7 +1000,7 @@ cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaS
     g.stage = 1;
     grouped_cc_kernel<false><<<dim3(mtiles, (a.hidden + kTN - 1) / kTN), kCCThreads, 0, st>>>(g);
   }
-  if (!a.skip_routed) {
+  if (!a.skip_routed && !a.keep_grouped) {
     if (a.pair_out)
       unpermute_kernel<<<T * k, 256, 0, st>>>(w.token_pos, w.out_r, T * k, a.hidden, a.pair_out);
     else

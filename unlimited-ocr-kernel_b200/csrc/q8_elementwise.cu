@@ -4,6 +4,7 @@
 // pass over the output bytes, no reuse.  Grids are sized in multiples of the
 // SM count by the launchers in capi.cu.
 #include "common.cuh"
+#include "device_once.h"
 #include "kernels.h"
 
 namespace uocr {
@@ -258,13 +259,10 @@ cudaError_t launch_linear_bf16(const uint16_t* w, int n, int k, const float* x, 
   // bulk copies: 16-byte aligned rows of 16-byte multiples (k % 8 == 0)
   const int bulk = k % 8 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0 &&
                    reinterpret_cast<uintptr_t>(x) % 16 == 0;
-  static unsigned configured = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(configured & (1u << (dev & 31)))) {
+  static PerDeviceOnce configured;
+  configured.run([] {
     cudaFuncSetAttribute(linear_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    configured |= 1u << (dev & 31);
-  }
+  });
   linear_bf16_kernel<<<dim3((n + kBf16Out - 1) / kBf16Out, (batch + kBf16Rows - 1) / kBf16Rows),
                        kBf16Threads, smem, st>>>(w, n, k, x, batch, y, bulk, status);
   return cudaGetLastError();

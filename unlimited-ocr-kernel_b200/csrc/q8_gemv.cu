@@ -22,6 +22,7 @@
 //   acc = acc + (float(S_b) * ws_b) * xs_b over b = 0,1,2,... with _rn
 //   intrinsics starting from -0.0: the reference's exact rounding sequence.
 #include "common.cuh"
+#include "device_once.h"
 #include "kernels.h"
 
 namespace uocr {
@@ -281,14 +282,11 @@ static void launch_gemv_tma(const Q8View* mats, int n, const float* x, float* co
   for (int i = 1; i < n; ++i)
     if (mats[i].rows != mats[0].rows) p.uniform_tiles = 0;
   const size_t smem = gemv_tma_smem(cols, tr);
-  static unsigned configured = 0;  // one bit per device ordinal
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(configured & (1u << (dev & 31)))) {
+  static PerDeviceOnce configured;
+  configured.run([] {
     cudaFuncSetAttribute(gemv_tma_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(kGemvSmemLimit));
-    configured |= 1u << (dev & 31);
-  }
+  });
   const int grid = tiles < sms ? tiles : sms;
   gemv_tma_kernel<MODE><<<grid, kGemvThreads, smem, st>>>(p);
 }

@@ -41,6 +41,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "device_once.h"
 #include "kernels.h"
 #include "tc_maps.cuh"
 
@@ -330,12 +331,8 @@ __global__ void __launch_bounds__(kSmThreads, 3)
 }
 
 void configure_small() {
-  static std::mutex mu;
-  static unsigned long long done = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  std::lock_guard<std::mutex> lock(mu);
-  if (dev < 64 && !(done & (1ull << dev))) {
+  static PerDeviceOnce configured;
+  configured.run([] {
     cudaFuncSetAttribute(small_rows_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          kSmSmemF);
     cudaFuncSetAttribute(small_rows_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -345,8 +342,7 @@ void configure_small() {
                          cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     cudaFuncSetAttribute(small_rows_kernel<true>,
                          cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    done |= 1ull << dev;
-  }
+  });
 }
 
 }  // namespace
@@ -362,7 +358,8 @@ cudaError_t launch_small_rows(bool int8, const void* maps, const Q8View* single,
                               long long ldy, unsigned* status, cudaStream_t st,
                               const int* items, int max_items, const void* maps2,
                               const Q8View* single2, float* y2) {
-  if (!small_rows_supported(N, K) || hi > kSmallChunkedMax || lo < 1) return cudaErrorInvalidValue;
+  if (!small_rows_supported(N, K) || (!items && hi > kSmallChunkedMax) || lo < 1)
+    return cudaErrorInvalidValue;
   if (items && (!counts || max_items < 1 || groups > 256)) return cudaErrorInvalidValue;
   if (!maps && !single) return cudaErrorInvalidValue;
   if (y2 && (single ? !single2 : !maps2)) return cudaErrorInvalidValue;

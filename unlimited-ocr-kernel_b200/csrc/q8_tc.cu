@@ -34,6 +34,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "device_once.h"
 #include "kernels.h"
 #include "tc_maps.cuh"
 
@@ -876,18 +877,13 @@ int grid_for(long long work, int sms) {
 // ---- host: tensor maps ------------------------------------------------------
 // The dynamic shared-memory opt-in, once per device.
 void configure() {
-  static std::mutex mu;
-  static unsigned long long done = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  std::lock_guard<std::mutex> lock(mu);
-  if (dev < 64 && !(done & (1ull << dev))) {
+  static PerDeviceOnce configured;
+  configured.run([] {
     cudaFuncSetAttribute(q8_tc_gemm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          kSmemBytes);
     cudaFuncSetAttribute(q8_tc_gemm_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          kFSmemBytes);
-    done |= 1ull << dev;
-  }
+  });
 }
 
 bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }

@@ -105,6 +105,16 @@ class GpuContext:
     def sync(self) -> None:
         _check(lib().uocr_ctx_sync(self._h))
 
+    def set_wait_limit(self, seconds: float) -> None:
+        """Bounded device waits of this context's kernels give up after
+        `seconds` (0: the default, about 2 s) and report Timeout."""
+        _check(lib().uocr_ctx_set_wait_limit(self._h, int(seconds * 1e9)))
+
+    def hold_decode_barrier(self, hold: bool) -> None:
+        """Failure-detection test hook: the one-token decode kernel's grid
+        barrier waits for an arrival that never comes until released."""
+        _check(lib().uocr_ctx_hold_decode_barrier(self._h, int(bool(hold))))
+
     def sm_count(self) -> int:
         d, s = ctypes.c_int(), ctypes.c_int()
         _check(lib().uocr_ctx_device(self._h, ctypes.byref(d), ctypes.byref(s)))

@@ -33,6 +33,8 @@ SIGNATURES = {
     "uocr_ctx_set_stream": (I, [P, P]),
     "uocr_ctx_sync": (I, [P]),
     "uocr_ctx_device": (I, [P, ctypes.POINTER(I), ctypes.POINTER(I)]),
+    "uocr_ctx_set_wait_limit": (I, [P, ctypes.c_uint64]),
+    "uocr_ctx_hold_decode_barrier": (I, [P, I]),
     "uocr_q8_from_parts": (I, [P, S, S, P, S, P, S, PP]),
     "uocr_q8_from_device": (I, [P, S, S, P, P, PP]),
     "uocr_q8_quantize": (I, [P, S, S, P, PP]),

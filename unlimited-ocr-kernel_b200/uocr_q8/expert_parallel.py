@@ -39,12 +39,14 @@ NVLink on GPUs, gloo on the CPU.  The library's own exchange
 in use, as stores into the other GPUs' memory, and needs no collective;
 ``peer_expert_parallel`` below builds it over a process group.
 
-The compute is a backend with the methods ``route``, ``expert_rows``, ``shared_rows``, ``combine`` (counts form) and ``dispatch``,
-``combine_rows`` (fixed form); on GPUs it is ``LibraryBackend``, the CUDA
+The compute is a backend with the methods ``route``, ``expert_rows``,
+``shared_rows``, ``combine`` (counts form) and ``dispatch``, ``combine_rows``
+(fixed form); on GPUs it is ``LibraryBackend``, the CUDA
 library's C ABI (uocr_moe_route, uocr_moe_expert_rows, uocr_moe_shared_rows,
 uocr_moe_combine, uocr_moe_dispatch, uocr_moe_combine_rows), which runs on the
 torch stream current at construction so that collectives and kernels are
-ordered on one stream.
+ordered on one stream.  A failed collective (a rank that left, a
+process-group timeout) raises OcrError "Nccl" instead of hanging.
 """
 from __future__ import annotations
 
@@ -54,6 +56,17 @@ import torch
 import torch.distributed as dist
 
 DYNAMIC_ACTIVATIONS = 1
+EXCHANGE_ERROR = 9  # uocr_status UOCR_ERR_NCCL: the collective exchange failed
+
+
+def _exchange(fn, *args, **kwargs):
+    """One collective of the exchange; a failure (a rank that left, a
+    process-group timeout, a transport error) becomes OcrError "Nccl"."""
+    try:
+        return fn(*args, **kwargs)
+    except Exception as exc:
+        from . import OcrError
+        raise OcrError(EXCHANGE_ERROR, f"expert-parallel exchange failed: {exc}") from exc
 
 
 def expert_bounds(n_experts: int, world: int) -> List[int]:
@@ -119,15 +132,15 @@ class ExpertParallelMoe:
         ids, wts = self.backend.route(logits)
         order, local_ids, send_counts = self.dispatch_plan(ids)
         recv_counts = torch.empty_like(send_counts)
-        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        _exchange(dist.all_to_all_single, recv_counts, send_counts, group=self.group)
         sc = send_counts.tolist()
         rc = recv_counts.tolist()
         n_recv = sum(rc)
         send_x = x.index_select(0, torch.div(order, k, rounding_mode="floor"))
         recv_x = x.new_empty((n_recv, H))
         recv_ids = local_ids.new_empty((n_recv,))
-        dist.all_to_all_single(recv_x, send_x, rc, sc, group=self.group)
-        dist.all_to_all_single(recv_ids, local_ids, rc, sc, group=self.group)
+        _exchange(dist.all_to_all_single, recv_x, send_x, rc, sc, group=self.group)
+        _exchange(dist.all_to_all_single, recv_ids, local_ids, rc, sc, group=self.group)
         out = x.new_empty((n_recv, H))
         if mode == DYNAMIC_ACTIVATIONS:
             pos = 0
@@ -139,7 +152,7 @@ class ExpertParallelMoe:
         elif n_recv:
             self.backend.expert_rows(recv_x, recv_ids, mode, out)
         back = x.new_empty((T * k, H))
-        dist.all_to_all_single(back, out, sc, rc, group=self.group)
+        _exchange(dist.all_to_all_single, back, out, sc, rc, group=self.group)
         pair_out = torch.empty_like(back)
         pair_out.index_copy_(0, order, back)
         y = self.backend.shared_rows(x, mode)
@@ -154,8 +167,8 @@ class ExpertParallelMoe:
         send_x, send_ids, pair_rows = self.backend.dispatch(x, ids, self.bounds, C)
         recv_x = torch.empty_like(send_x)
         recv_ids = torch.empty_like(send_ids)
-        dist.all_to_all_single(recv_x, send_x, group=self.group)
-        dist.all_to_all_single(recv_ids, send_ids, group=self.group)
+        _exchange(dist.all_to_all_single, recv_x, send_x, group=self.group)
+        _exchange(dist.all_to_all_single, recv_ids, send_ids, group=self.group)
         out = torch.empty_like(recv_x)
         if mode == DYNAMIC_ACTIVATIONS:
             for r in range(W):
@@ -164,7 +177,7 @@ class ExpertParallelMoe:
         else:
             self.backend.expert_rows(recv_x, recv_ids, mode, out)
         back = torch.empty_like(out)
-        dist.all_to_all_single(back, out, group=self.group)
+        _exchange(dist.all_to_all_single, back, out, group=self.group)
         y = self.backend.shared_rows(x, mode)
         self.backend.combine_rows(ids, wts, back, pair_rows, y)
         return y, ids, wts
