@@ -50,10 +50,10 @@ H, F, FS, E, TOPK = 1280, 896, 1792, 64, 6
 MAT_BYTES = lambda r, c: r * c + r * ((c + 31) // 32) * 4
 STEP_WEIGHT_BYTES = TOPK * 3 * MAT_BYTES(F, H) + 3 * MAT_BYTES(FS, H)  # 30,965,760
 STEP_BYTES = STEP_WEIGHT_BYTES + H * 4 + E * 4 + H * 4
-METRIC = "q8-block32 expert GEMV GB/s (MoE decode layer, config 1)"
+METRIC = "q8-block32 expert GEMV GB/s (MoE decode layer, one token)"
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch, from the
-# ncu captures summarised in profiles/moe_decode_kernel_config1.md and
-# profiles/gemv_tma_kernel_config0.md (16 matrices per GEMV launch).
+# ncu captures summarised in profiles/moe_decode_kernel_one_token_layer.md and
+# profiles/gemv_tma_kernel_896x1280_stream.md (16 matrices per GEMV launch).
 DECODE_TRAFFIC = 31_045_632
 GEMV_TRAFFIC = 4 * 20_668_928  # the 16-matrix capture scaled to a 64-matrix launch
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -134,7 +134,8 @@ def dist_setup(n_gpus):
 
 
 def build_layers(ctx, n_layers, device, seed):
-    """n_layers MoE layers of config-1 shapes, generated on the device."""
+    """n_layers MoE layers of the upstream decoder's shapes (64 experts of width
+    896, top-6, shared expert 1792, hidden 1280), generated on the device."""
     import torch
 
     import uocr_q8
@@ -249,8 +250,8 @@ def run_ours(args):
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms_step, 6),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
-            "data": "synthetic (seeded; config-1 distributions)",
-            "config": {"workload": "config1_moe_decode_layer", "tokens_per_step": 1,
+            "data": "synthetic (seeded; x, logits ~ N(0,1), int8 weights uniform in [-127,127], scales ~ U(1e-4,1e-2))",
+            "config": {"workload": "moe_decode_layer_1_token", "tokens_per_step": 1,
                        "hidden": H, "experts": E, "top_k": TOPK, "expert_width": F,
                        "shared_width": FS, "mode": "weights_only (fp32 activations)",
                        "l2": f"rotating pool of {n_layers} layers x 255.5 MB (> 126 MB L2)",
@@ -277,7 +278,7 @@ def run_ours(args):
     return result
 
 
-GEMV_BYTES = MAT_BYTES(F, H) + H * 4 + F * 4  # config 0: 1,298,944 B
+GEMV_BYTES = MAT_BYTES(F, H) + H * 4 + F * 4  # one [896x1280] GEMV: 1,298,944 B
 GEMV_PER_LAUNCH = 64  # matrices per multi-GEMV launch (82.6 MB of weights)
 
 
@@ -343,12 +344,12 @@ def run_gemv(args):
     single_us = t0.elapsed_time(t1) * 1e3 / 200
     peak, peak_kind = peak_hbm()
     gbs = GEMV_BYTES * steps / (ms * 1e-3) / 1e9
-    return {"metric": "q8-block32 expert GEMV GB/s (config 0, batched stream)",
+    return {"metric": "q8-block32 expert GEMV GB/s (896x1280 GEMV, batched stream)",
             "value": round(gbs, 2), "unit": "GB/s", "n_gpus": 1, "steps": steps,
             "warmup": max(args.warmup, 3), "ms_per_step": round(ms / steps, 6),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8-act" if mode else "fp32", "data": "synthetic (seeded)",
-            "config": {"workload": "config0_gemv_896x1280", "pool": pool,
+            "config": {"workload": "gemv_896x1280", "pool": pool,
                        "matrices_per_launch": GEMV_PER_LAUNCH, "bytes_per_step": GEMV_BYTES},
             "single_call_us": round(single_us, 3),
             "roofline": {"bound": "hbm", "kernel": "gemv_tma_kernel", "achieved": round(gbs, 2),
@@ -390,7 +391,7 @@ def cpu_baseline(args, seconds=None):
     dt = time.perf_counter() - t0
     return {"value": round(STEP_BYTES * n / dt / 1e9, 3), "unit": "GB/s",
             "cores": oracle.get_threads(), "kind": "port",
-            "sample": f"{n} tokens of config 1 (one MoE decode layer each) in {dt:.1f} s",
+            "sample": f"{n} tokens (one MoE decode layer each) in {dt:.1f} s",
             "ms_per_step": round(dt / n * 1e3, 3)}
 
 
@@ -416,8 +417,8 @@ def run_reference(args):
             "n_gpus": world, "steps": steps, "warmup": max(args.warmup, 3),
             "ms_per_step": round(dt / steps * 1e3, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
-            "data": "synthetic (seeded; config-1 distributions)",
-            "config": {"workload": "config1_moe_decode_layer", "tokens_per_step": 1,
+            "data": "synthetic (seeded; x, logits ~ N(0,1), int8 weights uniform in [-127,127], scales ~ U(1e-4,1e-2))",
+            "config": {"workload": "moe_decode_layer_1_token", "tokens_per_step": 1,
                        "hidden": H, "experts": E, "top_k": TOPK, "expert_width": F,
                        "shared_width": FS, "mode": "weights_only (fp32 activations)",
                        "parallelism": "rank 0 only (host CPU)", "bytes_per_step": STEP_BYTES},
@@ -431,7 +432,7 @@ def run_reference(args):
 
 
 PREFILL_TOKENS = 1024
-# config 2 algorithmic work: 6144 (token, expert) pairs x 3 projections of [896x1280]
+# grouped prefill algorithmic work: 6144 (token, expert) pairs x 3 projections of [896x1280]
 # plus 1024 tokens through the shared expert's 3 projections of [1792x1280]
 PREFILL_OPS = PREFILL_TOKENS * TOPK * 3 * 2 * F * H + PREFILL_TOKENS * 3 * 2 * FS * H
 PREFILL_WEIGHT_BYTES = E * 3 * MAT_BYTES(F, H) + 3 * MAT_BYTES(FS, H)  # 255,467,520
@@ -447,7 +448,7 @@ def peak_tensor():
 
 def zipf_logits(gen, tokens, experts, s=1.1):
     """Router logits with a Zipf(s) popularity bias over a random expert order
-    plus N(0,1) noise (the config-2 stand-in for a real prefill)."""
+    plus N(0,1) noise (the stand-in for a real prefill's routing)."""
     import torch
     order = torch.randperm(experts, generator=gen, device=gen.device)
     bias = torch.empty(experts, device=gen.device)
@@ -506,13 +507,13 @@ def run_prefill(args):
     peak_t, kind_t = peak_tensor()
     hbm, kind_h = peak_hbm()
     attainable = min(peak_t, PREFILL_OPS / PREFILL_WEIGHT_BYTES * hbm / 1e3)  # TFLOP/s
-    return {"metric": "q8-block32 grouped prefill TOP/s (MoE layer, config 2)",
+    return {"metric": "q8-block32 grouped prefill TOP/s (MoE layer, 1024 tokens)",
             "value": round(tops, 3), "unit": "TOP/s", "n_gpus": 1, "steps": steps,
             "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8-act" if mode else "fp32",
             "data": "synthetic (seeded; x ~ N(0,1), Zipf(1.1)-biased router logits)",
-            "config": {"workload": "config2_grouped_prefill", "tokens": T, "experts": E,
+            "config": {"workload": "grouped_prefill_1024_tokens", "tokens": T, "experts": E,
                        "top_k": TOPK, "hidden": H, "expert_width": F, "shared_width": FS,
                        "mode": "weights_only (fp32 activations)" if mode == 0 else
                                "dynamic int8 activations, every row",
@@ -599,19 +600,19 @@ def run_int8suite(args):
             ctx.sync()
     ctx.sync()
     agg = total_ops / total_s / 1e12
-    return {"metric": "q8-block32 linear_dynamic_int8 micro-suite TOP/s (config 3)",
+    return {"metric": "q8-block32 linear_dynamic_int8 micro-suite TOP/s",
             "value": round(agg, 3), "unit": "TOP/s", "n_gpus": 1, "steps": len(cases),
             "warmup": 3, "ms_per_step": round(total_s * 1e3 / len(cases), 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8-act",
             "data": "synthetic (seeded; rows ~ N(0,1) * U(0.1,10))",
-            "config": {"workload": "config3_int8_micro_suite", "K": K,
+            "config": {"workload": "int8_micro_suite", "K": K,
                        "aggregate": "total ops / total time over the 12 cases",
                        "timing": "CUDA graph of one call per pool matrix, replayed; "
                                  "pool > 400 MB so weights come from HBM"},
             "cases": cases, "clocks": clocks.summary()}
 
 
-EP_TOKENS = 64  # config 4: a decode batch of 64 independent sequences
+EP_TOKENS = 64  # a decode batch of 64 independent sequences
 EP_EXPERT_BYTES = 3 * MAT_BYTES(F, H)
 EP_SHARED_BYTES = 3 * MAT_BYTES(FS, H)
 
@@ -764,13 +765,13 @@ def run_ep(args):
     if rank == 0:
         cpu = ep_cpu_baseline(args) if (world == 1 and not args.no_cpu) else None
         result = {
-            "metric": "MoE layer decode tok/s (config-4 layer, batch 64, expert-parallel)",
+            "metric": "MoE layer decode tok/s (batch 64, expert-parallel over NCCL all_to_all)",
             "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": steps,
             "warmup": max(args.warmup, 3), "ms_per_step": round(ms_step, 5),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "fp32" if mode == 0 else "int8-act",
-            "data": "synthetic (seeded; config-1 weight distributions)",
-            "config": {"workload": "config4_moe_layer_ep_decode", "global_batch": EP_TOKENS,
+            "data": "synthetic (seeded; int8 weights uniform in [-127,127], scales ~ U(1e-4,1e-2))",
+            "config": {"workload": "moe_layer_ep_decode_nccl", "global_batch": EP_TOKENS,
                        "tokens_per_rank": T, "hidden": H, "experts": E, "top_k": TOPK,
                        "experts_per_rank": len(mine), "expert_width": F, "shared_width": FS,
                        "mode": mode, "parallelism": f"ep{world} (NCCL all_to_all, fixed capacity)",
@@ -868,11 +869,11 @@ def run_attn(args):
     ms = start.elapsed_time(stop) / steps
     gbs = ATTN_BYTES / (ms * 1e-3) / 1e9
     peak, peak_kind = peak_hbm()
-    res = {"metric": "decode attention KV GB/s (config 4 attention, batch 64)",
+    res = {"metric": "decode attention KV GB/s (batch 64, 10 heads x 128, prefix 2048 + ring 128)",
            "value": round(gbs, 2), "unit": "GB/s", "n_gpus": 1, "steps": steps,
            "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4), "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded)",
-           "config": {"workload": "config4_attention_decode", "batch": ATTN_BATCH,
+           "config": {"workload": "attention_decode_batch64", "batch": ATTN_BATCH,
                       "heads": ATTN_HEADS, "head_dim": ATTN_DIM, "prefix": ATTN_PREFIX,
                       "window": ATTN_WINDOW, "bytes_per_step": ATTN_BYTES,
                       "l2": "2 caches x 1.43 GB rotated (> 126 MB L2)"},
@@ -1058,12 +1059,12 @@ def run_decode(args):
     step_bytes = decode_step_bytes(cfg, tokens_now)
     gbs = step_bytes / (ms * 1e-3) / 1e9
     peak, peak_kind = peak_hbm()
-    res = {"metric": "decode tok/s (config 4: 12-layer MoE decoder, batch 64, KV 2048)",
+    res = {"metric": "decode tok/s (12-layer MoE decoder, batch 64, KV 2048)",
            "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": 1, "steps": steps,
            "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4), "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None,
            "dtype": "int8-act" if mode else "fp32", "data": "synthetic (seeded; random-init weights)",
-           "config": {"workload": "config4_decode_step", "batch": DEC_BATCH, "prefix": DEC_PREFIX,
+           "config": {"workload": "decode_step_12_layers", "batch": DEC_BATCH, "prefix": DEC_PREFIX,
                       "window": cfg.window, "layers": cfg.layers, "hidden": cfg.hidden,
                       "experts": cfg.experts, "top_k": cfg.top_k, "vocab": cfg.vocab,
                       "lm_head": args.lm_head, "mode": mode, "cuda_graph": True,
@@ -1393,15 +1394,15 @@ def run_secondary(args):
         except Exception as exc:  # a secondary never hides the headline line
             out[name] = {"error": f"{type(exc).__name__}: {exc}"}
 
-    sub("config1_moe_decode_layer", run_ours, steps=4096, e2e_steps=4000,
+    sub("moe_decode_layer_1_token", run_ours, steps=4096, e2e_steps=4000,
         cpu_seconds=min(args.cpu_seconds, 6.0))
-    sub("config0_gemv_fp32", run_gemv, steps=256 * 4096, gemv_int8=False)
-    sub("config0_gemv_int8", run_gemv, steps=256 * 4096, gemv_int8=True)
-    sub("config2_prefill_fp32", run_prefill, steps=40, prefill_mode=0)
-    sub("config2_prefill_int8", run_prefill, steps=40, prefill_mode=2)
-    sub("config3_int8_suite", run_int8suite)
-    sub("config4_attention", run_attn, steps=200, cpu_seconds=min(args.cpu_seconds, 5.0))
-    sub("config4_decode_step", run_decode, steps=60, cpu_seconds=min(args.cpu_seconds, 6.0))
+    sub("gemv_stream_fp32", run_gemv, steps=256 * 4096, gemv_int8=False)
+    sub("gemv_stream_int8", run_gemv, steps=256 * 4096, gemv_int8=True)
+    sub("prefill_1024_fp32", run_prefill, steps=40, prefill_mode=0)
+    sub("prefill_1024_int8", run_prefill, steps=40, prefill_mode=2)
+    sub("int8_micro_suite", run_int8suite)
+    sub("attention_decode", run_attn, steps=200, cpu_seconds=min(args.cpu_seconds, 5.0))
+    sub("decode_step_12_layers", run_decode, steps=60, cpu_seconds=min(args.cpu_seconds, 6.0))
     return out
 
 

@@ -320,7 +320,9 @@ int uocr_ep_combine(uocr_ctx *ctx, uocr_ep *ep, float *y_dev, int32_t *ids_dev,
  * decode kernels with UOCR_ERR_UNSUPPORTED.  The first call on a device looks
  * up the array's device address (make it before any stream capture).  All
  * calls on a device share the array: calls that overlap on the GPU race, so
- * serialise them.  x_dev hidden floats (16-byte aligned), logits_dev
+ * serialise them.  The array's address is cached per device for the life of
+ * the process: do not use the library across a cudaDeviceReset of a device it
+ * has served.  x_dev hidden floats (16-byte aligned), logits_dev
  * n_experts floats, y_dev hidden floats; asynchronous on the context stream. */
 #define UOCR_NOALLOC_MAX_H 16384
 int uocr_moe_forward_decode_noalloc(uocr_ctx *ctx, const uocr_moe *layer, int mode,

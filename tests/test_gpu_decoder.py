@@ -156,3 +156,47 @@ def test_decode_step_matches_oracle(ctx, mode):
     for b in range(batch):
         assert state.caches[0].state(b) == (caches[b][0].tokens(), caches[b][0].position())
     state.free()
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("mode", [0, 2])
+def test_decode_step_config4_shapes(ctx, mode):
+    """The decode step at the upstream decoder's shapes: hidden 1280, 10 heads
+    of 128, a dense FFN of width 6848 and an MoE layer of 64 experts (top-6,
+    width 896) plus the 1792-wide shared expert, the q8 lm_head over the full
+    129,280-token vocabulary; 8 sequences with 2048-token prefixes (ragged),
+    five steps.  Two layers (one of each kind) and a 4-token ring, so that the
+    ring wraps within the steps; the 12-layer step repeats these layers."""
+    from uocr_q8.decoder import DecodeState, Decoder, DecoderConfig, decode_step
+    cfg = DecoderConfig(layers=2, window=4)
+    dec = Decoder.random(ctx, cfg, seed=31 + mode)
+    layers, emb, final_norm, head = host_decoder(dec)
+    batch, prefix = 8, 2048
+    state = DecodeState(dec, batch, prefix)
+    rng = np.random.default_rng(17 + mode)
+    caches = []
+    for b in range(batch):
+        seq = []
+        for cache in state.caches:
+            n = prefix - 3 * b
+            k = rng.standard_normal((n, cfg.hidden)).astype(np.float32)
+            v = rng.standard_normal((n, cfg.hidden)).astype(np.float32)
+            cache.prefill(b, dev(k), dev(v))
+            c = oracle.LayerCache(cfg.heads, cfg.head_dim, cfg.window)
+            c.prefill(k, v, n)
+            seq.append(c)
+        caches.append(seq)
+    for step in range(5):
+        tokens = rng.integers(0, cfg.vocab, batch)
+        logits = host(decode_step(dec, state, dev(tokens.astype(np.int64)), mode))
+        ctx.sync()
+        for b in range(batch):
+            ref = oracle_step(cfg, layers, emb, final_norm, head, caches[b], int(tokens[b]), mode)
+            scale = float(np.max(np.abs(ref)))
+            err = float(np.max(np.abs(logits[b].astype(np.float64) - ref)))
+            assert err <= (1e-3 if mode == 0 else 1e-2) * scale, (step, b, err, scale)
+            assert int(np.argmax(logits[b])) == int(np.argmax(ref)) or \
+                np.sort(ref)[-1] - np.sort(ref)[-2] < 2 * err
+    for b in range(batch):
+        assert state.caches[1].state(b) == (caches[b][1].tokens(), caches[b][1].position())
+    state.free()

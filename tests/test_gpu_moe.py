@@ -93,7 +93,8 @@ def test_route_errors(ctx):
 # ---------------------------------------------------------------- decode (1 token)
 @pytest.fixture(scope="module")
 def config1(ctx):
-    """hidden 1280, 64 experts of width 896, top-6, shared 1792."""
+    """The MoE layer of the upstream decoder: hidden 1280, 64 experts of width
+    896, top-6, a fused shared expert of width 1792."""
     rng = np.random.default_rng(1)
     return make_layer(ctx, rng, 1280, 896, 1792, 64, 6)
 
@@ -105,6 +106,7 @@ def _check_layer(y, ref, ids, ids_ref, wts, wts_ref, int8):
     err = float(np.max(np.abs(y.astype(np.float64) - ref)))
     if int8:
         same = float(np.mean(y.view(np.uint32) == ref.view(np.uint32)))
+        print(f"int8 layer outputs bit-identical to the oracle: {same:.5f}")
         assert same >= 0.99, same
         assert err <= LAYER_INT8_TOL * scale
     else:
@@ -307,6 +309,33 @@ def test_prefill_config2_shape(ctx, config1, mode):
     logits = (rng.standard_normal((T, 64)).astype(np.float32) + rng.permutation(bias)).astype(np.float32)
     y, ids, wts = layer.forward(x, logits, mode)
     ref, ids_ref, wts_ref = oracle.experts(sh, ex, logits, x, 6, mode)
+    _check_layer(y, ref, ids, ids_ref, wts, wts_ref, mode != 0)
+
+
+def zipf_logits(rng, tokens, experts, s=1.1):
+    """Router logits of a prefill with skewed expert popularity: N(0, 1) noise
+    plus a Zipf(s) bias, -s * log(rank), over a random order of the experts."""
+    bias = np.empty(experts, np.float32)
+    bias[rng.permutation(experts)] = -s * np.log(np.arange(1, experts + 1, dtype=np.float64))
+    return (rng.standard_normal((tokens, experts)) + bias).astype(np.float32)
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("mode", [0, 2])
+def test_prefill_config2_full(ctx, config1, mode):
+    """The grouped prefill at its full size: 1024 tokens, top-6 of 64 experts
+    with Zipf(1.1)-skewed routing (groups from a few rows to several hundred:
+    warp-level chunks and tensor-core tiles in one layer), FP32 activations
+    and int8 activations for every row."""
+    layer, sh, ex = config1
+    rng = np.random.default_rng(2024)
+    T = 1024
+    x = rng.standard_normal((T, 1280)).astype(np.float32)
+    logits = zipf_logits(rng, T, 64)
+    y, ids, wts = layer.forward(x, logits, mode)
+    ref, ids_ref, wts_ref = oracle.experts(sh, ex, logits, x, 6, mode)
+    sizes = np.bincount(ids_ref.reshape(-1), minlength=64)
+    assert sizes.max() > 256 and sizes.min() < 64, sizes  # both kernels reached
     _check_layer(y, ref, ids, ids_ref, wts, wts_ref, mode != 0)
 
 

@@ -4,7 +4,7 @@ than 16 rows, csrc/q8_small.cu for 2..16).
 int8 activations: the reference applies Int8Matrix::linear_dynamic_int8
 (src/cpu/quantized.rs:155-236) row by row; the tensor-core kernel must
 reproduce it bit for bit: exact int32 block sums, then ((float)S * ws) * xs
-added block by block from -0.0.  Shapes: BASELINE config 3 (M in
+added block by block from -0.0.  Shapes: the int8 micro-suite (M in
 {1,16,128,512}, N in {896,1280,3840}, K = 1280) and ragged edges (M not a
 multiple of the 64-row tile, one 128-row weight tile, K of one stage).
 

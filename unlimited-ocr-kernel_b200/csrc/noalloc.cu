@@ -28,6 +28,10 @@
 //    every element of h and of the routing slots before the second reads
 //    them), but calls that overlap on the GPU — two streams, or two contexts
 //    on the same device running concurrently — race on it.  Serialise them.
+//  * the looked-up addresses are cached for the life of the process: the
+//    library must not be used across a cudaDeviceReset (or a new primary
+//    context) of a device it has served, whose scratch would then be freed
+//    memory.
 #include <cuda_runtime.h>
 
 #include <cmath>

@@ -117,8 +117,8 @@ class Decoder:
     @classmethod
     def random(cls, ctx: GpuContext, cfg: DecoderConfig, seed: int = 0, lm_head: str = "q8"):
         """Random-init weights of the decoder's architecture, generated on the
-        device (q8 weights uniform in [-127, 127], scales U(1e-4, 1e-2) as in
-        BASELINE config 0; norms near 1; BF16 embedding and router N(0, 1))."""
+        device (q8 weights uniform in [-127, 127], scales U(1e-4, 1e-2); norms
+        near 1; BF16 embedding and router N(0, 1))."""
         import torch
         dev = f"cuda:{ctx.device}"
         g = torch.Generator(device=dev)
