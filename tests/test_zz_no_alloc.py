@@ -6,9 +6,10 @@ buffer at start-up because a late cudaMalloc can stall the device, and hosts
 whose own pool allocator must own all device memory.  It keeps its scratch in
 a fixed array inside the library instead of the context's growable workspace.
 
-The test calls it through the C ABI twice in a row on a fresh context (two
-different tokens, so the second call reuses the scratch the first one left
-behind), checks that the device's free memory did not change, and compares
+The test calls it through the C ABI on a fresh context: once for the per-device
+set-up, then twice in a row (two different tokens, so the second call reuses
+the scratch the first one left behind), checks that the device's free memory
+did not change across the two calls, and compares
 each output with the regular entry point, uocr_moe_forward, on the same token
 (on a second context), in all three modes.  The tolerance is the MoE layer
 tolerance of the other parity tests
@@ -58,6 +59,10 @@ def test_noalloc_matches_regular_entry_point(mode):
     # the library runs on the context's own stream: synchronise it before
     # torch touches the outputs on its stream
     torch.cuda.synchronize()
+    # the first call on a device is the set-up: it looks up the scratch
+    # array, which may load the library's device code (and with it the array)
+    layer.forward_decode_noalloc(tokens[0][0], tokens[0][1], mode, y_t=outs[1])
+    ctx.sync()
     free_before = torch.cuda.mem_get_info(0)[0]
     for (x, lg), y in zip(tokens, outs):  # two calls in a row
         layer.forward_decode_noalloc(x, lg, mode, y_t=y)
