@@ -356,7 +356,8 @@ def run_gemv(args):
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(gbs / peak, 4),
                          "traffic": args.traffic if args.traffic is not None else GEMV_TRAFFIC},
-            "gpu_launches": steps // GEMV_PER_LAUNCH, "clocks": clocks.summary()}
+            "gpu_launches": steps // GEMV_PER_LAUNCH, "clocks": clocks.summary(),
+            "cpu_baseline": None if args.no_cpu else gemv_cpu_baseline(mode, 3.0)}
 
 
 def make_cpu_layer(seed):
@@ -429,6 +430,67 @@ def run_reference(args):
                                        "crate cannot be built here)"},
             "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
+
+
+def gemv_cpu_baseline(mode, seconds):
+    """The reference's scalar linear / linear_dynamic_int8 (oracle port, rows
+    split over all host threads) on one [896x1280] matrix, bounded."""
+    import oracle
+    rng = np.random.default_rng(0)
+    m = oracle.Matrix(rng.integers(-127, 128, size=(F, H), dtype=np.int8),
+                      rng.uniform(1e-4, 1e-2, size=(F, H // 32)).astype(np.float32))
+    x = rng.standard_normal((1, H)).astype(np.float32)
+    fn = oracle.linear_dynamic_int8 if mode else oracle.linear
+    oracle.set_threads(0)
+    fn(m, x)
+    n, t0 = 0, time.perf_counter()
+    while n == 0 or time.perf_counter() - t0 < seconds:
+        fn(m, x)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(GEMV_BYTES * n / dt / 1e9, 3), "unit": "GB/s",
+            "cores": oracle.get_threads(), "kind": "port",
+            "sample": f"{n} GEMVs of one [896x1280] matrix in {dt:.1f} s"}
+
+
+def prefill_cpu_baseline(mode, seconds):
+    """The reference's serial grouped experts (oracle port, all host threads)
+    on a sample of 128 tokens with Zipf(1.1) routing; TOP/s of that sample."""
+    import oracle
+    shared, routed, rng = make_cpu_layer(11)
+    T = 128
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    bias = np.empty(E, np.float32)
+    bias[rng.permutation(E)] = -1.1 * np.log(np.arange(1, E + 1, dtype=np.float64))
+    lg = (rng.standard_normal((T, E)) + bias).astype(np.float32)
+    oracle.set_threads(0)
+    ops = T * TOPK * 3 * 2 * F * H + T * 3 * 2 * FS * H
+    n, t0 = 0, time.perf_counter()
+    while n == 0 or time.perf_counter() - t0 < seconds:
+        oracle.experts(shared, routed, lg, x, TOPK, mode)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(ops * n / dt / 1e12, 5), "unit": "TOP/s", "cores": oracle.get_threads(),
+            "kind": "port", "sample": f"{n} prefills of 128 tokens through one MoE layer in {dt:.1f} s"}
+
+
+def int8suite_cpu_baseline(seconds):
+    """The reference's scalar linear_dynamic_int8 (oracle port, all host
+    threads), row by row, for M = 16 rows of an [896x1280] matrix."""
+    import oracle
+    rng = np.random.default_rng(3)
+    m = oracle.Matrix(rng.integers(-127, 128, size=(F, H), dtype=np.int8),
+                      rng.uniform(1e-4, 1e-2, size=(F, H // 32)).astype(np.float32))
+    x = (rng.standard_normal((16, H)) * rng.uniform(0.1, 10, (16, 1))).astype(np.float32)
+    oracle.set_threads(0)
+    n, t0 = 0, time.perf_counter()
+    while n == 0 or time.perf_counter() - t0 < seconds:
+        oracle.linear_dynamic_int8(m, x)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(2.0 * 16 * F * H * n / dt / 1e12, 5), "unit": "TOP/s",
+            "cores": oracle.get_threads(), "kind": "port",
+            "sample": f"{n} calls of 16 rows x [896x1280] in {dt:.1f} s"}
 
 
 PREFILL_TOKENS = 1024
@@ -531,7 +593,8 @@ def run_prefill(args):
                          "unit": "TFLOP/s", "frac": round(tops / attainable, 5), "traffic": None},
             # route, grouping, split or quantize (+ gather), 3 grouped GEMMs, SwiGLU,
             # shared: split/quantize + 3 GEMMs + SwiGLU, combine
-            "gpu_launches": steps * 13, "clocks": clocks.summary()}
+            "gpu_launches": steps * 13, "clocks": clocks.summary(),
+            "cpu_baseline": None if args.no_cpu else prefill_cpu_baseline(mode, 6.0)}
 
 
 def run_int8suite(args):
@@ -551,6 +614,7 @@ def run_int8suite(args):
     K = H
     cases = []
     total_ops = 0.0
+    total_bytes = 0.0
     total_s = 0.0
     with ClockSampler(0) as clocks:
         for N in (896, 1280, 3840):
@@ -595,6 +659,7 @@ def run_int8suite(args):
                               "TOP/s": round(ops / (us * 1e-6) / 1e12, 3),
                               "GB/s": round(byts / (us * 1e-6) / 1e9, 1)})
                 total_ops += ops
+                total_bytes += byts
                 total_s += us * 1e-6
             del mats
             ctx.sync()
@@ -609,7 +674,15 @@ def run_int8suite(args):
                        "aggregate": "total ops / total time over the 12 cases",
                        "timing": "CUDA graph of one call per pool matrix, replayed; "
                                  "pool > 400 MB so weights come from HBM"},
-            "cases": cases, "clocks": clocks.summary()}
+            "cases": cases, "clocks": clocks.summary(),
+            "roofline": {"bound": "hbm (M = 1, 16) / tensor (M >= 128)",
+                         "kernel": "all cases: gemv_tma_kernel (M = 1), small_rows_kernel "
+                                   "(M = 16), q8_tc_gemm_i8_kernel (M >= 128)",
+                         "achieved": round(total_bytes / total_s / 1e9, 2),
+                         "peak": peak_hbm()[0], "peak_kind": peak_hbm()[1], "unit": "GB/s",
+                         "frac": round(total_bytes / total_s / 1e9 / peak_hbm()[0], 4),
+                         "traffic": None},
+            "cpu_baseline": None if args.no_cpu else int8suite_cpu_baseline(3.0)}
 
 
 EP_TOKENS = 64  # a decode batch of 64 independent sequences
