@@ -19,11 +19,12 @@
 //   ret_flag   [world]               step number of each owner's last return
 // with cap = max_tokens * top_k (a source can send all of its pairs to one
 // rank).  One step (stream order, step number e = previous + 1):
-//   dispatch  route this rank's tokens (moe::route); every pair's row of x is
-//             stored into its owner's recv_x block at the next free slot (pair
-//             order), with its local expert id and pair index; the last CTA to
-//             finish stores each owner's count and then, with release
-//             semantics at system scope, the flag = e.
+//   dispatch  route this rank's tokens (moe::route, one warp per token, in
+//             the same kernel); every pair's row of x is stored into its
+//             owner's recv_x block at a slot claimed from a counter per owner,
+//             with its local expert id and pair index; the last CTA to finish
+//             stores each owner's count and then, with release semantics at
+//             system scope, the flag = e.
 //   wait      the owner waits (bounded) until every source's flag is e, reads
 //             the counts and marks the unused slots of each block (id -1).
 //   experts   the owner's grouped SwiGLU projections over all received rows
@@ -61,6 +62,7 @@
 #include "common.cuh"
 #include "handles.h"
 #include "kernels.h"
+#include "route.cuh"
 
 namespace uocr {
 int record_error(int status, const char* message);  // capi.cu
@@ -146,27 +148,6 @@ __device__ bool wait_flag_sys(const unsigned* p, unsigned want, unsigned long lo
   }
 }
 
-__device__ __forceinline__ int pair_owner(const EpDev& d, const int32_t* ids, int q) {
-  int e = ids[q];
-  if (e < 0 || e >= d.n_experts) {
-    flag(d.status, DEV_BAD_ROUTE);
-    e = 0;
-  }
-  return d.owner_of[e];
-}
-
-// cnt[owner] += pairs [0, n) per owner, by the whole CTA: one shared atomic
-// per owner present in each warp's 32 pairs.
-__device__ __forceinline__ void count_owners(const EpDev& d, const int32_t* ids, int n, int* cnt) {
-  const int lane = threadIdx.x & 31;
-  for (int q0 = threadIdx.x & ~31; q0 < n; q0 += blockDim.x) {
-    const int q = q0 + lane;
-    const int o = q < n ? pair_owner(d, ids, q) : -1;
-    const unsigned peers = __match_any_sync(0xffffffffu, o);
-    if (o >= 0 && lane == __ffs(peers) - 1) atomicAdd(&cnt[o], __popc(peers));
-  }
-}
-
 __device__ __forceinline__ void fence_for(const EpDev& d) {
   if (d.sys)
     __threadfence_system();
@@ -191,51 +172,70 @@ __device__ __forceinline__ bool last_to_arrive(const EpDev& d, unsigned* c) {
   return last != 0;
 }
 
-// Dispatch: CTA c moves pairs [8c, 8c + 8), one warp per pair; a pair's slot
-// is the number of earlier pairs (pair order) with the same owner.
-__global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(
-    const __grid_constant__ EpDev d, const float* __restrict__ x, const int32_t* __restrict__ ids,
-    int tokens) {
-  __shared__ int cnt[kEpMaxWorld];
-  __shared__ int own[kEpWarps];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int P = tokens * d.top_k;
+// Route and dispatch: one warp per token runs moe::route (route.cuh), writes
+// the token's routing, claims a slot in each selected expert's owner block
+// (a counter per owner; the slot order within a block does not change any
+// result, every row is computed on its own) and stores the token's row of x
+// there with the expert id local to the owner and the pair index.  The last
+// CTA to finish publishes each owner's count and then, with release
+// semantics at system scope, the step number.
+constexpr int kRdWarps = 4;
+
+__global__ void __launch_bounds__(kRdWarps * 32) ep_route_dispatch_kernel(
+    const __grid_constant__ EpDev d, const float* __restrict__ x, const float* __restrict__ logits,
+    int tokens, int normalize, float scale, int32_t* __restrict__ ids, float* __restrict__ wts,
+    unsigned* __restrict__ send_cnt) {
+  extern __shared__ float rd_smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, k = d.top_k;
+  float* p = rd_smem + warp * (d.n_experts + 2 * k);
+  int* sel = reinterpret_cast<int*>(p + d.n_experts);
+  float* sw = p + d.n_experts + k;
   const unsigned step = d.ctr[kCtrStep] + 1u;
-  const int p0 = blockIdx.x * kEpWarps;
-  for (int r = tid; r < d.world; r += kEpThreads) cnt[r] = 0;
-  __syncthreads();
-  count_owners(d, ids, min(p0, P), cnt);
-  if (tid < kEpWarps) own[tid] = p0 + tid < P ? pair_owner(d, ids, p0 + tid) : -1;
-  __syncthreads();
-  const int p = p0 + warp;
-  if (p < P) {
-    const int o = own[warp];
-    int slot = cnt[o];
-    for (int w = 0; w < warp; ++w) slot += own[w] == o;
-    int e = ids[p];
-    if (e < 0 || e >= d.n_experts) e = 0;  // flagged by pair_owner
-    char* base = d.peers[o];
-    const long long row = static_cast<long long>(d.rank) * d.cap + slot;
-    const int h4 = d.hidden >> 2;
-    float4* dst = reinterpret_cast<float4*>(base + d.L.recv_x) + row * h4;
-    const float4* src = reinterpret_cast<const float4*>(x) + static_cast<long long>(p / d.top_k) * h4;
-    for (int c = lane; c < h4; c += 32) dst[c] = src[c];
-    if (lane == 0) {
-      reinterpret_cast<int*>(base + d.L.recv_ids)[row] = d.local_of[e];
-      reinterpret_cast<int*>(base + d.L.recv_pair)[row] = p;
+  const int h4 = d.hidden >> 2;
+  for (int t = blockIdx.x * kRdWarps + warp; t < tokens; t += gridDim.x * kRdWarps) {
+    const bool ok = route_row_warp(logits + static_cast<long long>(t) * d.n_experts, d.n_experts,
+                                   k, normalize, scale, p, sel, sw, d.status);
+    for (int r = lane; r < k; r += 32) {
+      ids[static_cast<long long>(t) * k + r] = ok ? sel[r] : -1;
+      wts[static_cast<long long>(t) * k + r] = ok ? sw[r] : 0.0f;
     }
+    if (ok) {
+      int e = 0, o = 0, slot = 0;
+      if (lane < k) {
+        e = sel[lane];
+        o = d.owner_of[e];
+        slot = static_cast<int>(atomicAdd(send_cnt + o, 1u));
+      }
+      const float4* src = reinterpret_cast<const float4*>(x) + static_cast<long long>(t) * h4;
+      for (int j = 0; j < k; ++j) {
+        const int oj = __shfl_sync(0xffffffffu, o, j);
+        const int sj = __shfl_sync(0xffffffffu, slot, j);
+        const int ej = __shfl_sync(0xffffffffu, e, j);
+        if (sj >= d.cap) {  // cannot happen while every step completes; never write past a block
+          if (lane == 0) flag(d.status, DEV_CAPACITY);
+          continue;
+        }
+        char* base = d.peers[oj];
+        const long long row = static_cast<long long>(d.rank) * d.cap + sj;
+        float4* dst = reinterpret_cast<float4*>(base + d.L.recv_x) + row * h4;
+        for (int c = lane; c < h4; c += 32) dst[c] = src[c];
+        if (lane == 0) {
+          reinterpret_cast<int*>(base + d.L.recv_ids)[row] = d.local_of[ej];
+          reinterpret_cast<int*>(base + d.L.recv_pair)[row] = t * k + j;
+        }
+      }
+    }
+    __syncwarp();
   }
   if (!last_to_arrive(d, d.ctr + kCtrDispatch)) return;
-  for (int r = tid; r < d.world; r += kEpThreads) cnt[r] = 0;
-  __syncthreads();
-  count_owners(d, ids, P, cnt);
-  __syncthreads();
-  for (int r = tid; r < d.world; r += kEpThreads) {
+  for (int r = threadIdx.x; r < d.world; r += blockDim.x) {
+    const unsigned c = atomicExch(send_cnt + r, 0u);
     char* base = d.peers[r];
-    reinterpret_cast<volatile int*>(base + d.L.recv_count)[d.rank] = cnt[r];
+    reinterpret_cast<volatile int*>(base + d.L.recv_count)[d.rank] =
+        c < static_cast<unsigned>(d.cap) ? static_cast<int>(c) : d.cap;
     st_release_sys(reinterpret_cast<unsigned*>(base + d.L.recv_flag) + d.rank, step);
   }
-  if (tid == 0) d.ctr[kCtrDispatch] = 0u;
+  if (threadIdx.x == 0) d.ctr[kCtrDispatch] = 0u;
 }
 
 // Owner side: wait for every source's dispatch of this step, take the counts,
@@ -325,6 +325,7 @@ __global__ void __launch_bounds__(128) ep_combine_kernel(const __grid_constant__
       e[j] = used ? ids[t * k + j] : 0x7fffffff;
       p[j] = t * k + j;
       w[j] = used ? wts[t * k + j] : 0.0f;
+      if (used && e[j] < 0) e[j] = 0x7ffffffe;  // an invalid router row (flagged): no pair
     }
 #pragma unroll
     for (int i = 1; i < 8; ++i)
@@ -341,12 +342,12 @@ __global__ void __launch_bounds__(128) ep_combine_kernel(const __grid_constant__
       float4 v[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        if (j < k) v[j] = __ldcg(rows + static_cast<long long>(p[j]) * h4 + c);
+        if (j < k && e[j] < 0x7ffffffe) v[j] = __ldcg(rows + static_cast<long long>(p[j]) * h4 + c);
       float4* yr = reinterpret_cast<float4*>(y + static_cast<long long>(t) * d.hidden) + c;
       float4 acc = *yr;
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        if (j < k) {
+        if (j < k && e[j] < 0x7ffffffe) {
           acc.x = __fadd_rn(acc.x, __fmul_rn(w[j], v[j].x));
           acc.y = __fadd_rn(acc.y, __fmul_rn(w[j], v[j].y));
           acc.z = __fadd_rn(acc.z, __fmul_rn(w[j], v[j].z));
@@ -414,6 +415,7 @@ struct uocr_ep {
   int* local_of = nullptr;
   unsigned* ctr = nullptr;
   int* live = nullptr;
+  unsigned* send_cnt = nullptr;  // [world] rows claimed per owner in the step's dispatch
   int32_t* ids = nullptr;
   float* wts = nullptr;
   float* pair_w = nullptr;  // grouping reads a weight per received row; never applied
@@ -542,12 +544,10 @@ int check_scratch(const uocr_ctx* ctx, const uocr_ep* ep, size_t tokens) {
 int enqueue_dispatch(uocr_ctx* ctx, uocr_ep* ep, int mode, const float* x, const float* logits,
                      int tokens, float* y, cudaStream_t rs, cudaStream_t ss) {
   const EpDev d = ep_dev(ep, ctx);
-  if (tokens > 0)
-    launch_route(logits, tokens, ep->n_experts, ep->top_k, ep->normalize, ep->scale, ep->ids,
-                 ep->wts, ctx->status_dev, ctx->sms, rs);
-  const int P = tokens * ep->top_k;
-  const int grid = P > 0 ? (P + kEpWarps - 1) / kEpWarps : 1;
-  ep_dispatch_kernel<<<grid, kEpThreads, 0, rs>>>(d, x, ep->ids, tokens);
+  const int grid = tokens > 0 ? (tokens + kRdWarps - 1) / kRdWarps : 1;
+  const size_t smem = sizeof(float) * kRdWarps * (ep->n_experts + 2 * ep->top_k);
+  ep_route_dispatch_kernel<<<grid, kRdWarps * 32, smem, rs>>>(
+      d, x, logits, tokens, ep->normalize, ep->scale, ep->ids, ep->wts, ep->send_cnt);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_err(e, "expert-parallel dispatch");
   if (tokens > 0) {
@@ -630,6 +630,7 @@ void release(uocr_ep* ep) {
   if (ep->ev_fork) cudaEventDestroy(ep->ev_fork);
   if (ep->ev_join) cudaEventDestroy(ep->ev_join);
   void* bufs[] = {ep->region, ep->peers_dev, ep->owner_of, ep->local_of, ep->ctr, ep->live,
+                  ep->send_cnt,
                   ep->ids, ep->wts, ep->pair_w, ep->out_slots, ep->ws_routed, ep->ws_shared,
                   ep->io};
   for (void* b : bufs)
@@ -721,6 +722,8 @@ int uocr_ep_create(uocr_ctx* ctx, const uocr_moe* local_layer, size_t n_experts,
   if (e == cudaSuccess) e = cudaMemset(ep->ctr, 0, sizeof(unsigned) * kCtrWords);
   if (e == cudaSuccess) e = cudaMalloc(&ep->live, sizeof(int) * world);
   if (e == cudaSuccess) e = cudaMemset(ep->live, 0, sizeof(int) * world);
+  if (e == cudaSuccess) e = cudaMalloc(&ep->send_cnt, sizeof(unsigned) * world);
+  if (e == cudaSuccess) e = cudaMemset(ep->send_cnt, 0, sizeof(unsigned) * world);
   if (e == cudaSuccess) e = cudaMalloc(&ep->ids, sizeof(int32_t) * ep->cap);
   if (e == cudaSuccess) e = cudaMalloc(&ep->wts, sizeof(float) * ep->cap);
   if (e == cudaSuccess) e = cudaMalloc(&ep->pair_w, sizeof(float) * rows);
