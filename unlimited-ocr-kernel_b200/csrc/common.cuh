@@ -105,6 +105,26 @@ __device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
   return d;
 }
 
+// Two IEEE products, each rounded on its own; lane for lane bit-identical to
+// __fmul_rn, subnormals included (checked on ten million pairs of arbitrary
+// bit patterns).  Its result must not feed a packed add (f2_add) where the
+// two roundings matter: the PTX assembler (CUDA 12.9) fuses a mul.rn.f32x2
+// whose result feeds an add.rn.f32x2 into one fused multiply-add despite the
+// rounding modifiers (about 23% of 2 million random pairs differed from the
+// separately rounded operations, every one equal to the fused result, with or
+// without -fmad=false, and in a running sum even with the product moved
+// through another register first).  Add such a product with __fadd_rn per
+// lane: that pairing stays separately rounded (measured over running sums of
+// 40 blocks), and the bit-exact int8 tests hold it.
+__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
+  float2 d;
+  asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+      " mul.rn.f32x2 rd, ra, rb;\n mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
 __device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) {
   float2 d;
   asm("{\n .reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"

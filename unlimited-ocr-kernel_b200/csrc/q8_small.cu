@@ -257,20 +257,28 @@ __global__ void __launch_bounds__(kSmThreads, 3)
       if (INT8) {
         const unsigned char* xq = st + kSmW + kSmWs;  // [8][128]
         const uint2 xv = *reinterpret_cast<const uint2*>(xq + gq * 128 + 32 * jb + 8 * q);
+        const float2 xs2 = make_float2(jb == 0 ? xs4[0].x : jb == 1 ? xs4[0].y : jb == 2 ? xs4[0].z : xs4[0].w,
+                                       jb == 0 ? xs4[1].x : jb == 1 ? xs4[1].y : jb == 2 ? xs4[1].z : xs4[1].w);
+        const float2 magic = make_float2(-12582912.0f, -12582912.0f);
 #pragma unroll
         for (int m = 0; m < 2; ++m) {
           int d[4] = {0, 0, 0, 0};
           mma_s8_m16n8k32(d, wv[m][0].x, wv[m][1].x, wv[m][0].y, wv[m][1].y, xv.x, xv.y);
+          // (c, c + 1) = one weight row and chunk rows 2q, 2q + 1: a packed pair
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const float4 w4 = ws4[m][c >> 1];
-            const float4 x4 = xs4[c & 1];
+          for (int h = 0; h < 2; ++h) {
+            const float4 w4 = ws4[m][h];
             const float wsb = jb == 0 ? w4.x : jb == 1 ? w4.y : jb == 2 ? w4.z : w4.w;
-            const float xsb = jb == 0 ? x4.x : jb == 1 ? x4.y : jb == 2 ? x4.z : x4.w;
-            // ((float)S * ws) * xs, then the running sum: |S| < 2^24, so the
-            // conversion is exact; every operation rounded on its own
-            acc[m][c] = __fadd_rn(acc[m][c],
-                                  __fmul_rn(__fmul_rn(static_cast<float>(d[c]), wsb), xsb));
+            // exact int32 -> float: |S| < 2^22 (32 * 128 * 128), 2^23 + 2^22 + S
+            // minus 2^23 + 2^22
+            const float2 sf = f2_add(make_float2(__int_as_float(0x4B400000 + d[2 * h]),
+                                                 __int_as_float(0x4B400000 + d[2 * h + 1])),
+                                     magic);
+            // ((float)S * ws) * xs (packed: each lane is the scalar IEEE
+            // product), then the running sum, every operation rounded on its own
+            const float2 t = f2_mul(f2_mul(sf, make_float2(wsb, wsb)), xs2);
+            acc[m][2 * h] = __fadd_rn(acc[m][2 * h], t.x);  // scalar adds: see f2_mul
+            acc[m][2 * h + 1] = __fadd_rn(acc[m][2 * h + 1], t.y);
           }
         }
       } else {

@@ -273,9 +273,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int rl = 32 * q + lane, n = n0 + rl, c0 = kEpiCols * part;
     const bool row_ok = n < a.N;
     const uint32_t tlane = tmem + (static_cast<uint32_t>(32 * q) << 16) + c0;
-    float acc[kEpiCols];
+    // running sums of two neighbouring columns per register pair: the
+    // conversion and the two products run as packed f32x2 instructions (each
+    // lane is the scalar IEEE operation), the adds as scalar ones, so each
+    // column keeps the reference's rounding sequence
+    float2 acc[kEpiCols / 2];
 #pragma unroll
-    for (int i = 0; i < kEpiCols; ++i) acc[i] = -0.0f;
+    for (int i = 0; i < kEpiCols / 2; ++i) acc[i] = make_float2(-0.0f, -0.0f);
     bool ok = true;
     // Block b: its S values are in `now`; start loading block b + 1 into
     // `next`, apply block b, then wait for the load.  Called with the two
@@ -296,16 +300,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* ws_s = reinterpret_cast<const float*>(st + kABytes + kBBytes);  // [128][4]
       const float* xs_s = reinterpret_cast<const float*>(st + kABytes + kBBytes + kWsBytes);  // [64][4]
       const float wsb = ws_s[4 * rl + jb];
+      const float2 ws2 = make_float2(wsb, wsb);
+      const float2 magic = make_float2(-12582912.0f, -12582912.0f);
       // columns past the tile's last row are padding: nothing to apply
       // (the warp still takes part in every barrier)
 #pragma unroll
-      for (int c = 0; c < kEpiCols && c0 < rows; ++c) {
-        const float xsc = xs_s[4 * (c0 + c) + jb];
-        // exact int32 -> float: |S| < 2^22 (32 * 127 * 127)
-        const float sf = __int_as_float(0x4B400000 + static_cast<int>(now[c])) - 12582912.0f;
+      for (int c = 0; c < kEpiCols && c0 < rows; c += 2) {
+        const float2 xs2 = make_float2(xs_s[4 * (c0 + c) + jb], xs_s[4 * (c0 + c + 1) + jb]);
+        // exact int32 -> float: |S| < 2^22 (32 * 127 * 127), 2^23 + 2^22 + S
+        // minus 2^23 + 2^22
+        const float2 sf =
+            f2_add(make_float2(__int_as_float(0x4B400000 + static_cast<int>(now[c])),
+                               __int_as_float(0x4B400000 + static_cast<int>(now[c + 1]))),
+                   magic);
         // ((float)S * ws) * xs, then the running sum: each step rounded on
         // its own (the reference never contracts into an fma)
-        acc[c] = __fadd_rn(acc[c], __fmul_rn(__fmul_rn(sf, wsb), xsc));
+        const float2 t = f2_mul(f2_mul(sf, ws2), xs2);
+        acc[c / 2].x = __fadd_rn(acc[c / 2].x, t.x);  // scalar adds: see f2_mul
+        acc[c / 2].y = __fadd_rn(acc[c / 2].y, t.y);
       }
       if (jb == 3) {
         __syncwarp();
@@ -326,7 +338,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (row_ok) {
 #pragma unroll
       for (int i = 0; i < kEpiCols; ++i)
-        if (c0 + i < rows) a.y[static_cast<long long>(row0 + c0 + i) * a.ldy + n] = acc[i];
+        if (c0 + i < rows)
+          a.y[static_cast<long long>(row0 + c0 + i) * a.ldy + n] = (i & 1) ? acc[i / 2].y : acc[i / 2].x;
     }
   }
   tc_fence_before();
