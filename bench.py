@@ -1450,6 +1450,66 @@ def run_ep_peer(args):
     return result
 
 
+def run_ep_emulated(args):
+    """Profiling aid, one GPU: the expert-parallel layer of R ranks emulated on
+    one device (R contexts' worth of buffers, one stream), every step driven
+    through the three-part API in the order dispatch(all ranks),
+    experts(all ranks), combine(all ranks), so that the kernels of all ranks
+    run serialised and no wait depends on work queued behind it.  The time
+    per step is the sum over the ranks (it is not a multi-GPU number)."""
+    import torch
+
+    import uocr_q8
+    from uocr_q8.expert_parallel import expert_bounds
+    W, T, mode = args.emulate_ranks, EPP_TOKENS, args.ep_mode
+    torch.cuda.set_device(0)
+    dev = "cuda:0"
+    ctx = uocr_q8.GpuContext(0)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream)
+    bounds = expert_bounds(E, W)
+    with torch.cuda.stream(stream):
+        shared, experts = epp_weights(dev, ctx, 0, range(E))
+        locs = [uocr_q8.MoeLayer(ctx, shared, experts[bounds[r]:bounds[r + 1]], top_k=1)
+                for r in range(W)]
+        eps = [uocr_q8.PeerExpertParallel(ctx, locs[r], E, TOPK, bounds, r, T) for r in range(W)]
+        uocr_q8.PeerExpertParallel.connect_local(eps)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(77)
+        xs = torch.randn((W, T, H), device=dev, generator=gen)
+        lg = torch.randn((W, T, E), device=dev, generator=gen)
+        ys = torch.empty((W, T, H), device=dev)
+
+    def step():
+        for r in range(W):
+            eps[r].dispatch_device(xs[r], lg[r], mode, ys[r])
+        for r in range(W):
+            eps[r].experts_device()
+        for r in range(W):
+            eps[r].combine_device(ys[r])
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            step()
+    ctx.sync()
+    steps = max(1, args.steps)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for _ in range(steps):
+            step()
+        t1.record(stream)
+    t1.synchronize()
+    ctx.sync()
+    us = t0.elapsed_time(t1) * 1e3 / steps
+    for ep in eps:
+        ep.free()
+    return {"metric": f"emulated expert-parallel MoE layer, {W} ranks on one GPU (profiling aid)",
+            "value": round(us, 2), "unit": "us per step (all ranks, serialised)", "n_gpus": 1,
+            "steps": steps, "higher_is_better": False, "emulated_ranks": W,
+            "us_per_rank_step": round(us / W, 2), "tokens_per_rank": T, "mode": mode}
+
+
 def run_secondary(args):
     """Every other configuration, bounded, on GPU 0 (one GPU runs only)."""
     import copy
@@ -1546,6 +1606,9 @@ def main():
     ap.add_argument("--ep-mode", type=int, choices=[0, 1, 2], default=0)
     ap.add_argument("--decode-mode", type=int, choices=[0, 2], default=0)
     ap.add_argument("--lm-head", choices=["q8", "bf16"], default="q8")
+    ap.add_argument("--emulate-ranks", type=int, default=0,
+                    help="profiling aid: run the expert-parallel layer of this many ranks "
+                         "emulated on GPU 0 (serialised), print its time per step")
     args = ap.parse_args()
     if args.impl == "reference":
         if args.workload == "ep_peer":
@@ -1556,6 +1619,9 @@ def main():
             res = run_reference(args)
         if res is not None:
             print(json.dumps(res), flush=True)
+        return
+    if args.emulate_ranks > 1:
+        print(json.dumps(run_ep_emulated(args)), flush=True)
         return
     single = {"gemv": run_gemv, "prefill": run_prefill, "decode_step": run_decode,
               "attn_decode": run_attn, "int8suite": run_int8suite}
