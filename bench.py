@@ -964,7 +964,7 @@ def run_attn(args):
 DEC_BATCH, DEC_PREFIX = 64, 2048
 
 
-def decode_step_bytes(cfg, tokens_per_seq):
+def decode_step_bytes(cfg, tokens_per_seq, lm_head="q8"):
     """Algorithmic HBM bytes of one batched decode step: every layer's KV
     (keys + values of every present token of every sequence), every weight
     the step reads (attention projections, the dense FFN, the shared expert,
@@ -979,7 +979,7 @@ def decode_step_bytes(cfg, tokens_per_seq):
     moe = moe_layers * ((cfg.experts * (2 * q8(cfg.expert_width, H) + q8(H, cfg.expert_width)))
                         + 2 * q8(cfg.shared_width, H) + q8(H, cfg.shared_width)
                         + cfg.experts * H * 2)
-    head = q8(cfg.vocab, H)
+    head = q8(cfg.vocab, H) if lm_head == "q8" else cfg.vocab * H * 2
     return kv + attn + dense + moe + head + DEC_BATCH * H * 2
 
 
@@ -1129,7 +1129,7 @@ def run_decode(args):
             stream.synchronize()
     e2e_s = (time.perf_counter() - t0) / e2e_steps
     tokens_now = state.caches[0].state(0)[0]
-    step_bytes = decode_step_bytes(cfg, tokens_now)
+    step_bytes = decode_step_bytes(cfg, tokens_now, args.lm_head)
     gbs = step_bytes / (ms * 1e-3) / 1e9
     peak, peak_kind = peak_hbm()
     res = {"metric": "decode tok/s (12-layer MoE decoder, batch 64, KV 2048)",

@@ -345,6 +345,14 @@ int uocr_feed_forward(uocr_ctx *ctx, const uocr_q8 *gate, const uocr_q8 *up, con
  * in the INT8 overlay).  Sized for router-like n; asynchronous. */
 int uocr_linear_bf16(uocr_ctx *ctx, const uint16_t *w_dev, size_t n, size_t k, const float *x_dev,
                      size_t batch, float *y_dev);
+/* The same product for large BF16 weights (the lm_head, n = 129,280): each
+ * row of x is split into three bf16 pieces that sum to it exactly, so every
+ * product on the tensor cores is exact, and the sums accumulate in FP32 in
+ * another order than the reference's (FP32 tolerance, as Int8Matrix::linear
+ * on the tensor cores).  Streams the BF16 weights at HBM rate.  k % 64 == 0;
+ * w_dev and x_dev 16-byte aligned; asynchronous. */
+int uocr_linear_bf16_tc(uocr_ctx *ctx, const uint16_t *w_dev, size_t n, size_t k,
+                        const float *x_dev, size_t batch, float *y_dev);
 
 /* ---- decoder attention at decode --------------------------------------------
  * The attention half of Decoder::layer (src/decoder/mod.rs:241-341) for one

@@ -34,6 +34,57 @@ def test_linear_bf16_bit_exact(ctx):
         assert bits_equal(y, oracle.linear_bf16(w, x)), (n, k, rows)
 
 
+def _bf16_bits(rng, shape, scale):
+    w = (rng.standard_normal(shape) * scale).astype(np.float32)
+    return (w.view(np.uint32) >> 16).astype(np.uint16)
+
+
+def _check_fp32(y, w_bits, x, rows_idx=None):
+    """FP32 tolerance against the reference's left-to-right BF16 sums (oracle):
+    |y - ref| <= 1e-4 * max(|ref|, sum |w x| * 2^-10), on the given weight rows."""
+    idx = np.arange(w_bits.shape[0]) if rows_idx is None else rows_idx
+    ws = w_bits[idx]
+    ref = oracle.linear_bf16(ws, x)
+    wf = (ws.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    terms = np.abs(x.astype(np.float64)) @ np.abs(wf).T
+    got = y[:, idx].astype(np.float64)
+    denom = np.maximum(np.abs(ref), terms * 2.0 ** -10)
+    err = float(np.max(np.abs(got - ref) / np.where(denom == 0, 1, denom)))
+    assert err <= 1e-4, err
+    return err
+
+
+@pytest.mark.parametrize("n,k,rows", [(130, 64, 1), (1000, 256, 17), (300, 128, 65),
+                                      (517, 1280, 64)])
+def test_linear_bf16_tc_matches_oracle(ctx, n, k, rows):
+    """The tensor-core BF16 linear (exact products, FP32 accumulation) against
+    the reference's sequential sums: ragged weight tiles (n not a multiple of
+    128), one row, two row tiles, the lm_head's K."""
+    from uocr_q8.decoder import linear_bf16_tc_device
+    rng = np.random.default_rng(n + k + rows)
+    w = _bf16_bits(rng, (n, k), 0.05)
+    x = (rng.standard_normal((rows, k)) * rng.uniform(0.1, 10, (rows, 1))).astype(np.float32)
+    y = host(linear_bf16_tc_device(ctx, dev(w.view(np.int16)), dev(x)))
+    ctx.sync()
+    _check_fp32(y, w, x)
+
+
+@pytest.mark.slow
+def test_linear_bf16_tc_lm_head_size(ctx):
+    """The BF16 lm_head at its full size, 129,280 x 1280, batch 64: sampled
+    output rows against the oracle (the whole product is 10.6 G sequential
+    multiply-adds on the host)."""
+    from uocr_q8.decoder import linear_bf16_tc_device
+    rng = np.random.default_rng(129280)
+    w = _bf16_bits(rng, (129280, 1280), 0.03)
+    x = rng.standard_normal((64, 1280)).astype(np.float32)
+    y = host(linear_bf16_tc_device(ctx, dev(w.view(np.int16)), dev(x)))
+    ctx.sync()
+    idx = np.concatenate([np.arange(0, 256), rng.choice(129280, 512, replace=False),
+                          np.arange(129280 - 128, 129280)])
+    _check_fp32(y, w, x, idx)
+
+
 @pytest.mark.parametrize("mode", [0, 1, 2])
 @pytest.mark.parametrize("rows", [1, 5, 40])
 def test_feed_forward_matches_oracle(ctx, mode, rows):
@@ -93,7 +144,11 @@ def host_decoder(dec):
         layers.append(d)
     emb = (host(dec.embedding.view(torch.int16)).view(np.uint16).astype(np.uint32) << 16).view(
         np.float32)
-    return layers, emb, host(dec.final_norm), m(dec.lm_head)
+    if isinstance(dec.lm_head, torch.Tensor):  # BF16 head: its bit patterns
+        head = host(dec.lm_head.view(torch.int16)).view(np.uint16)
+    else:
+        head = m(dec.lm_head)
+    return layers, emb, host(dec.final_norm), head
 
 
 def oracle_step(cfg, layers, emb, final_norm, head, caches, token, mode):
@@ -118,15 +173,17 @@ def oracle_step(cfg, layers, emb, final_norm, head, caches, token, mode):
             y, _, _ = oracle.experts(L["shared"], L["experts"], logits, n2, cfg.top_k, 1 if int8 else 0)
         x = (r + y[0])[None]
     h = oracle.rms_norm(x, final_norm, cfg.eps)
+    if isinstance(head, np.ndarray):  # BF16 head (ops::linear_weight)
+        return oracle.linear_bf16(head, h)[0]
     return proj(head, h)[0]
 
 
-@pytest.mark.parametrize("mode", [0, 2])
-def test_decode_step_matches_oracle(ctx, mode):
+@pytest.mark.parametrize("mode,head", [(0, "q8"), (2, "q8"), (0, "bf16")])
+def test_decode_step_matches_oracle(ctx, mode, head):
     import torch
     from uocr_q8.decoder import DecodeState, Decoder, decode_step
     cfg = small_config()
-    dec = Decoder.random(ctx, cfg, seed=5 + mode)
+    dec = Decoder.random(ctx, cfg, seed=5 + mode, lm_head=head)
     layers, emb, final_norm, head = host_decoder(dec)
     batch, prefix = 3, 6
     state = DecodeState(dec, batch, prefix)

@@ -1331,6 +1331,39 @@ int uocr_linear_bf16(uocr_ctx* ctx, const uint16_t* w_dev, size_t n, size_t k, c
 
 // ---- decoder attention at decode --------------------------------------------
 // ops::rms_norm (src/cpu/ops.rs:362-414, 419-421)
+// ops::linear_weight, BF16 branch (src/cpu/ops.rs:62-133), for large BF16
+// weights: exact products on the tensor cores, FP32 accumulation in another
+// order than the reference's left-to-right sum (FP32 tolerance).  The
+// reference's element-count checks: n for one row, weight + output otherwise.
+int uocr_linear_bf16_tc(uocr_ctx* ctx, const uint16_t* w_dev, size_t n, size_t k,
+                        const float* x_dev, size_t batch, float* y_dev) {
+  if (!ctx) return fail(UOCR_ERR_INVALID, "null argument");
+  if (n == 0 || k == 0) return fail(UOCR_ERR_SHAPE, "linear weight must be [out,in]");
+  if (batch == 0) return ok();
+  if (!w_dev || !x_dev || !y_dev) return fail(UOCR_ERR_INVALID, "null argument");
+  if (!fits_int(n) || !fits_int(k) || !fits_int(batch) || !fits_int(batch * k))
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: size");
+  if (!linear_bf16_tc_supported(static_cast<int>(n), static_cast<int>(k)))
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: k must be a multiple of 64");
+  if (reinterpret_cast<uintptr_t>(w_dev) % 16 || reinterpret_cast<uintptr_t>(x_dev) % 16)
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: 16-byte aligned weights and rows");
+  int st = batch == 1 ? check_elements(ctx, n) : check_elements(ctx, n * k + batch * n);
+  if (st) return st;
+  DeviceGuard g(ctx->device);
+  const size_t pb = al256(3 * batch * k * 2);
+  if ((st = ensure_ws(ctx, pb + al256(batch * 4)))) return st;
+  uint16_t* pieces = static_cast<uint16_t*>(ctx->ws);
+  float* rinv = reinterpret_cast<float*>(static_cast<char*>(ctx->ws) + pb);
+  launch_split_rows(x_dev, static_cast<long long>(k), nullptr, static_cast<int>(batch),
+                    static_cast<int>(k), pieces, rinv, ctx->sms, ctx->stream);
+  const cudaError_t e = launch_linear_bf16_tc(w_dev, static_cast<int>(n), static_cast<int>(k), pieces,
+                                              rinv, static_cast<int>(batch), y_dev,
+                                              static_cast<long long>(n), ctx->status_dev, ctx->sms,
+                                              ctx->stream);
+  if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "linear_bf16_tc launch: %s", cudaGetErrorString(e));
+  return check_launch();
+}
+
 int uocr_rms_norm(uocr_ctx* ctx, const float* x_dev, size_t rows, size_t width,
                   const float* weight_dev, float eps, float* out_dev) {
   if (!ctx) return fail(UOCR_ERR_INVALID, "null context");

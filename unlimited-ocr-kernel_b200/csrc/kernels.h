@@ -75,6 +75,14 @@ cudaError_t launch_q8_tc_grouped_f32(const void* maps, int groups, const int* co
 // The row passes below take an optional device row count `live`: rows at or
 // past *live are skipped (grouped rows of which only the first *live are in
 // use; the pieces keep the stride of `rows`).
+// BF16 weights [n][k] (bit patterns) times `batch` FP32 rows given as their
+// exact three-way bf16 pieces [3][batch][k] and row scales (launch_split_rows):
+// y [batch][ldy], FP32 tolerance (exact products, FP32 accumulation on the
+// tensor cores).  k % 64 == 0, weights and pieces 16-byte aligned.
+bool linear_bf16_tc_supported(int n, int k);
+cudaError_t launch_linear_bf16_tc(const uint16_t* w, int n, int k, const uint16_t* pieces,
+                                  const float* rinv, int batch, float* y, long long ldy,
+                                  unsigned* status, int sms, cudaStream_t st);
 // pieces and rinv of rows x[src ? src[r] : r] (cols % 4 == 0, x rows 16-byte aligned)
 void launch_split_rows(const float* x, long long ld_x, const int* src, int rows, int cols,
                        uint16_t* pieces, float* rinv, int sms, cudaStream_t st,

@@ -901,6 +901,169 @@ void configure() {
 
 bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
 
+// ---- BF16 weights, FP32 activations (ops::linear_weight, BF16 branch) ---------
+// y[m][n] = sum_k x[m][k] * w[n][k] for a large BF16 weight (the lm_head,
+// 129,280 x 1280 at a decode batch of 64).  The weights need no conversion:
+// a TMA box of 128 rows x 64 bf16 with the 128-byte swizzle is already the
+// MMA's K-major operand layout.  The activations come as the exact three
+// bf16 pieces of each row scaled by a power of two (launch_split_rows), stacked
+// as one B operand of 3 * box rows, so every product is exact and one TMEM
+// accumulator takes the whole of K (no per-block scale here): the epilogue
+// runs once per tile, adds the three pieces' sums (smallest first) and
+// rescales the row.  Persistent: each CTA takes tiles (128 weight rows x 64
+// activation rows) in turn through one ring of stages, with two TMEM
+// accumulators so that a tile's epilogue overlaps the next tile's MMAs.
+// Warp 0: TMA.  Warp 1: TMEM owner and MMA issuer.  Warps 2-5: epilogue.
+constexpr int kHK = 64;                           // K elements per stage (128 bytes of bf16)
+constexpr int kHStages = 5;
+constexpr int kHWBytes = kBN * kHK * 2;           // 16 KB weight tile
+constexpr int kHStageBytes = kHWBytes + 3 * kBM * kHK * 2;  // + pieces of up to 64 rows: 40 KB
+constexpr int kHEpiWarps = 4;
+constexpr int kHThreads = 64 + 32 * kHEpiWarps;   // 192
+constexpr int kHAccCols = 256;                    // TMEM columns per accumulator (3 * 64 used)
+constexpr int kHTmemCols = 2 * kHAccCols;
+constexpr int kHSmemBytes = kHStages * kHStageBytes + 1024 + 256;
+static_assert(kHStageBytes % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+
+struct HeadArgs {
+  const float* rinv;  // 2^-e of each activation row
+  float* y;           // [batch][ldy]
+  int n, k, batch, ldy;
+  int piece_rows;     // rows of each piece tensor (batch)
+  int box;            // activation rows per tile as loaded: 16, 32 or 64
+  int n_tiles, row_tiles;
+  unsigned* status;
+};
+
+__global__ void __launch_bounds__(kHThreads, 1)
+    bf16_head_kernel(const __grid_constant__ CUtensorMap tmap_w,
+                     const __grid_constant__ CUtensorMap tmap_x, const HeadArgs a) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kHStages * kHStageBytes);
+  uint64_t* empty = full + kHStages;
+  uint64_t* tfull = empty + kHStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int box = a.box, ncols = 3 * box;
+  const int kstages = a.k / kHK;
+  const int total = a.n_tiles * a.row_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kHStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kHEpiWarps);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_holder, kHTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    // ---- TMA: the weight tile and the three piece tiles of each stage
+    if (lane == 0) {
+      const uint32_t tx = kHWBytes + 3 * box * kHK * 2;
+      int g = 0;  // stages issued
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const int n0 = (t % a.n_tiles) * kBN, r0 = (t / a.n_tiles) * kBM;
+        for (int ks = 0; ks < kstages; ++ks, ++g) {
+          const int s = g % kHStages;
+          if (g >= kHStages && !(ok = mbar_wait_spin(&empty[s], ((g / kHStages) - 1) & 1, a.status)))
+            break;
+          unsigned char* st = smem + s * kHStageBytes;
+          mbar_arrive_expect_tx(&full[s], tx);
+          tma_load_2d(st, &tmap_w, ks * kHK, n0, &full[s]);
+#pragma unroll
+          for (int p = 0; p < 3; ++p)
+            tma_load_2d(st + kHWBytes + p * box * kHK * 2, &tmap_x, ks * kHK,
+                        p * a.piece_rows + r0, &full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA: four K = 16 steps per stage into the tile's accumulator
+    if (lane == 0) {
+      const uint32_t idesc = kIdescBf16 | (static_cast<uint32_t>(ncols >> 3) << 17);
+      int g = 0, i = 0;  // stages consumed, tiles begun
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++i) {
+        const int buf = i & 1;
+        if (i >= 2) {
+          if (!(ok = mbar_wait_spin(&tempty[buf], ((i >> 1) - 1) & 1, a.status))) break;
+          tc_fence_after();
+        }
+        const uint32_t d = tmem + buf * kHAccCols;
+        for (int ks = 0; ks < kstages; ++ks, ++g) {
+          const int s = g % kHStages;
+          if (!(ok = mbar_wait_spin(&full[s], (g / kHStages) & 1, a.status))) break;
+          tc_fence_after();
+          const unsigned char* st = smem + s * kHStageBytes;
+#pragma unroll
+          for (int j = 0; j < kHK / 16; ++j)
+            mma_bf16(d, smem_desc_sw128(st + 32 * j), smem_desc_sw128(st + kHWBytes + 32 * j), idesc,
+                     (ks | j) ? 1u : 0u);
+          mma_commit(&empty[s]);  // the slot is free once these MMAs are done
+        }
+        mma_commit(&tfull[buf]);  // the tile's accumulator is complete
+      }
+    }
+  } else {
+    // ---- epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31, one weight
+    // row per thread; for every activation row, (p2 + p1) + p0, times 2^-e
+    const int q = warp & 3;
+    int i = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++i) {
+      const int buf = i & 1;
+      const int n0 = (t % a.n_tiles) * kBN, r0 = (t / a.n_tiles) * kBM;
+      if (ok) ok = mbar_wait_try(&tfull[buf], (i >> 1) & 1, a.status);
+      tc_fence_after();
+      const int n = n0 + 32 * q + lane;
+      const int rows = a.batch - r0 < kBM ? a.batch - r0 : kBM;
+      const uint32_t tl = tmem + (static_cast<uint32_t>(32 * q) << 16) + buf * kHAccCols;
+      for (int c = 0; c < box; c += 16) {
+        uint32_t p0[16], p1[16], p2[16];
+        tmem_ld16(tl + c, p0);
+        tmem_ld16(tl + box + c, p1);
+        tmem_ld16(tl + 2 * box + c, p2);
+        tmem_ld_wait(p0);
+        tmem_ld_wait(p1);
+        tmem_ld_wait(p2);
+        if (ok && n < a.n) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (c + e < rows) {
+              const float v = __fadd_rn(__fadd_rn(__uint_as_float(p2[e]), __uint_as_float(p1[e])),
+                                        __uint_as_float(p0[e]));
+              a.y[static_cast<long long>(r0 + c + e) * a.ldy + n] =
+                  __fmul_rn(v, __ldg(a.rinv + r0 + c + e));
+            }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kHTmemCols);
+  }
+}
+
 }  // namespace
 
 bool q8_tc_supported(int rows, int cols) {
@@ -1066,6 +1229,40 @@ void launch_swiglu_quantize(const float* g, const float* u, int rows, int cols, 
   const long long warps = static_cast<long long>(rows) * (cols / 32);
   swiglu_quantize_kernel<<<grid_for(warps * 32, sms), 256, 0, st>>>(g, u, rows, cols, hq, hs,
                                                                      status, live);
+}
+
+bool linear_bf16_tc_supported(int n, int k) { return n > 0 && k > 0 && k % kHK == 0; }
+
+cudaError_t launch_linear_bf16_tc(const uint16_t* w, int n, int k, const uint16_t* pieces,
+                                  const float* rinv, int batch, float* y, long long ldy,
+                                  unsigned* status, int sms, cudaStream_t st) {
+  if (!linear_bf16_tc_supported(n, k) || batch < 1) return cudaErrorInvalidValue;
+  if (!aligned16(w) || !aligned16(pieces)) return cudaErrorMisalignedAddress;
+  const int box = batch <= 16 ? 16 : batch <= 32 ? 32 : kBM;
+  CUtensorMap tw, tx;
+  if (!make_map_bf16_sw128(&tw, w, n, k) || !make_map_pieces(&tx, pieces, batch, k, box))
+    return cudaErrorInvalidValue;
+  static PerDeviceOnce configured;
+  configured.run([] {
+    cudaFuncSetAttribute(bf16_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         kHSmemBytes);
+  });
+  HeadArgs a{};
+  a.rinv = rinv;
+  a.y = y;
+  a.n = n;
+  a.k = k;
+  a.batch = batch;
+  a.ldy = static_cast<int>(ldy);
+  a.piece_rows = batch;
+  a.box = box;
+  a.n_tiles = (n + kBN - 1) / kBN;
+  a.row_tiles = (batch + kBM - 1) / kBM;
+  a.status = status;
+  const int total = a.n_tiles * a.row_tiles;
+  const int grid = total < sms ? total : sms;
+  bf16_head_kernel<<<grid, kHThreads, kHSmemBytes, st>>>(tw, tx, a);
+  return cudaGetLastError();
 }
 
 }  // namespace uocr

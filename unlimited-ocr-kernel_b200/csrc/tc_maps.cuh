@@ -50,6 +50,8 @@ bool make_map_w_rows64(CUtensorMap* map, const void* base, long long rows, long 
 // bf16 pieces [3 * piece_rows][cols], box 64 elements x box_rows, 128-byte swizzle.
 bool make_map_pieces(CUtensorMap* map, const uint16_t* base, long long piece_rows, long long cols,
                      int box_rows);
+// bf16 weights [rows][cols], box 64 elements x 128 rows, 128-byte swizzle.
+bool make_map_bf16_sw128(CUtensorMap* map, const uint16_t* base, long long rows, long long cols);
 // bf16 pieces [3 * piece_rows][cols], box 128 elements x box_rows, unswizzled.
 bool make_map_pieces_plain(CUtensorMap* map, const uint16_t* base, long long piece_rows,
                            long long cols, int box_rows);

@@ -75,6 +75,7 @@ SIGNATURES = {
     "uocr_ep_combine": (I, [P, P, P, P, P]),
     "uocr_feed_forward": (I, [P, P, P, P, I, P, S, P]),
     "uocr_linear_bf16": (I, [P, P, S, S, P, S, P]),
+    "uocr_linear_bf16_tc": (I, [P, P, S, S, P, S, P]),
     "uocr_rms_norm": (I, [P, P, S, S, P, F, P]),
     "uocr_add_rms_norm": (I, [P, P, P, S, S, P, F, P, P]),
     "uocr_rope_create": (I, [P, S, F, S, PP]),

@@ -73,6 +73,17 @@ def linear_bf16_device(ctx: GpuContext, w_t, x_t, y_t=None):
     return y_t
 
 
+def linear_bf16_tc_device(ctx: GpuContext, w_t, x_t, y_t=None):
+    """ops::linear_weight BF16 branch for a large weight (the lm_head): exact
+    products on the tensor cores, FP32 accumulation (FP32 tolerance)."""
+    import torch
+    n, k = w_t.shape
+    rows = x_t.numel() // k
+    y_t = y_t if y_t is not None else torch.empty((rows, n), device=x_t.device)
+    _check(lib().uocr_linear_bf16_tc(ctx.handle, _p(w_t), n, k, _p(x_t), rows, _p(y_t)))
+    return y_t
+
+
 def feed_forward_device(ctx: GpuContext, gate: Int8Matrix, up: Int8Matrix, down: Int8Matrix,
                         x_t, mode: int, y_t=None):
     """Decoder::feed_forward over rows of x (uocr_feed_forward)."""
@@ -112,7 +123,7 @@ class Decoder:
         self.ctx, self.cfg, self.layers = ctx, cfg, layers
         self.embedding = embedding_t  # torch.bfloat16 [vocab x hidden]
         self.final_norm = final_norm_t
-        self.lm_head = lm_head        # Int8Matrix, or a float32 torch tensor [vocab x hidden]
+        self.lm_head = lm_head        # Int8Matrix, or a bf16 torch tensor [vocab x hidden]
 
     @classmethod
     def random(cls, ctx: GpuContext, cfg: DecoderConfig, seed: int = 0, lm_head: str = "q8"):
@@ -172,7 +183,7 @@ class Decoder:
             head = mat(cfg.vocab, H, 1e-4, 1e-3)
         else:
             head = (torch.randn((cfg.vocab, H), device=dev, generator=g) * 0.03).to(
-                torch.bfloat16).float()
+                torch.bfloat16)
         return cls(ctx, cfg, layers, emb, norm(), head)
 
 
@@ -223,11 +234,8 @@ def decode_step(decoder: Decoder, state: DecodeState, tokens_t, mode: int = 0, l
     h = add_rms_norm_device(ctx, x, y, decoder.final_norm, cfg.eps, sum_t=x)
     if isinstance(decoder.lm_head, Int8Matrix):
         return decoder.lm_head.linear_device(h, logits_t, dynamic=rowwise)
-    out = torch.matmul(h, decoder.lm_head.t())  # BF16 head: a library GEMM over its f32 copy
-    if logits_t is not None:
-        logits_t.copy_(out)
-        return logits_t
-    return out
+    # BF16 head: the tensor-core BF16 linear straight from the bf16 weights
+    return linear_bf16_tc_device(ctx, decoder.lm_head, h, logits_t)
 
 
 # ---- loading a checkpoint with its INT8 overlay -------------------------------
