@@ -1150,6 +1150,27 @@ def run_decode(args):
                         "achieved": round(gbs, 2), "peak": peak, "peak_kind": peak_kind,
                         "unit": "GB/s", "frac": round(gbs / peak, 4), "traffic": None},
            "gpu_launches": None, "clocks": clocks.summary()}
+    if args.lm_head == "bf16":
+        # the BF16 lm_head alone (uocr_linear_bf16_tc, 129,280 x 1280 at batch
+        # 64), weights from HBM (331 MB, more than L2), events on its stream
+        from uocr_q8.decoder import linear_bf16_tc_device
+        hx = torch.randn((DEC_BATCH, cfg.hidden), device=dev)
+        hy = torch.empty((DEC_BATCH, cfg.vocab), device=dev)
+        h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                linear_bf16_tc_device(ctx, dec.lm_head, hx, hy)
+            h0.record(stream)
+            for _ in range(20):
+                linear_bf16_tc_device(ctx, dec.lm_head, hx, hy)
+            h1.record(stream)
+        h1.synchronize()
+        ctx.sync()
+        us = h0.elapsed_time(h1) * 1e3 / 20
+        hb = cfg.vocab * cfg.hidden * 2 + DEC_BATCH * cfg.hidden * 4 + DEC_BATCH * cfg.vocab * 4
+        res["lm_head"] = {"kernel": "bf16_head_kernel (+ the activation split)", "us": round(us, 2),
+                          "bytes": hb, "GB/s": round(hb / (us * 1e-6) / 1e9, 1),
+                          "frac": round(hb / (us * 1e-6) / 1e9 / peak, 4), "peak_kind": peak_kind}
     state.free()
     if not args.no_cpu:
         res["cpu_baseline"] = decode_cpu_baseline(min(args.cpu_seconds, 10.0))
@@ -1535,7 +1556,8 @@ def run_secondary(args):
     sub("prefill_1024_int8", run_prefill, steps=40, prefill_mode=2)
     sub("int8_micro_suite", run_int8suite)
     sub("attention_decode", run_attn, steps=200, cpu_seconds=min(args.cpu_seconds, 5.0))
-    sub("decode_step_12_layers", run_decode, steps=60, cpu_seconds=min(args.cpu_seconds, 6.0))
+    sub("decode_step_12_layers", run_decode, steps=60, cpu_seconds=min(args.cpu_seconds, 6.0),
+        lm_head="bf16")
     return out
 
 
