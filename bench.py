@@ -1004,15 +1004,17 @@ def attn_cpu_baseline(seconds):
             "sample": f"{n} single-sequence attention_decode calls (2176 tokens) in {dt:.1f} s"}
 
 
-def decode_cpu_baseline(seconds):
+def decode_cpu_baseline(seconds, prefix=DEC_PREFIX, mode=0, head=False):
     """One sequence's decode step through the oracle (the reference's scalar
     operations): attention block (norm, q/k/v/o, rope, cache push, attention
-    over 2176 tokens), BF16 router and MoE layer (64 experts, top 6, shared
-    1792), timed for a bounded number of seconds over MoE layers, plus one
-    dense layer and lm_head timed once; tokens/s of a 12-layer step (1 dense
-    + 11 MoE layers) for one sequence."""
+    over prefix + 128 tokens), BF16 router and MoE layer (64 experts, top 6,
+    shared 1792), timed for a bounded number of seconds over MoE layers, plus
+    one dense layer (and, with head, the q8 lm_head) timed once; tokens/s of
+    a 12-layer step (1 dense + 11 MoE layers) for one sequence.  mode 1:
+    DynamicActivations (every one-row projection with int8 activations)."""
     import oracle
     rng = np.random.default_rng(6)
+    lin = oracle.linear_dynamic_int8 if mode else oracle.linear
     H, heads, dim = 1280, ATTN_HEADS, ATTN_DIM
 
     def m(r, c):
@@ -1022,8 +1024,8 @@ def decode_cpu_baseline(seconds):
     qkvo = [m(H, H) for _ in range(4)]
     norm = np.ones(H, np.float32)
     cache = oracle.LayerCache(heads, dim, 128)
-    kp = rng.standard_normal((DEC_PREFIX, H)).astype(np.float32)
-    cache.prefill(kp, kp * 0.5, DEC_PREFIX)
+    kp = rng.standard_normal((prefix, H)).astype(np.float32)
+    cache.prefill(kp, kp * 0.5, prefix)
     for _ in range(127):
         r = rng.standard_normal(H).astype(np.float32)
         cache.push(r, r)
@@ -1034,18 +1036,18 @@ def decode_cpu_baseline(seconds):
 
     def attention_block(x):
         n = oracle.rms_norm(x, norm)
-        q, k, v = (oracle.linear(mm, n)[0] for mm in qkvo[:3])
+        q, k, v = (lin(mm, n)[0] for mm in qkvo[:3])
         pos = cache.position()
         q, k = oracle.rope(q, dim, pos), oracle.rope(k, dim, pos)
         cache.push(k, v)
         a = oracle.attention_decode(q, cache.keys, cache.values, heads)
-        return oracle.linear(qkvo[3], a[None])[0] + x[0]
+        return lin(qkvo[3], a[None])[0] + x[0]
 
     def moe_layer(x):
         r = attention_block(x)
         n = oracle.rms_norm(r[None], norm)
         lg = oracle.linear_bf16(router, n)
-        y, _, _ = oracle.experts(shared, experts, lg, n, TOPK, 0)
+        y, _, _ = oracle.experts(shared, experts, lg, n, TOPK, mode)
         return (r + y[0])[None]
 
     x = rng.standard_normal((1, H)).astype(np.float32)
@@ -1058,14 +1060,21 @@ def decode_cpu_baseline(seconds):
     dense = oracle.Ffn(m(6848, H), m(6848, H), m(H, 6848))
     t1 = time.perf_counter()
     r = attention_block(x)
-    oracle.feed_forward(dense, oracle.rms_norm(r[None], norm), 0)
+    oracle.feed_forward(dense, oracle.rms_norm(r[None], norm), mode)
     dense_s = time.perf_counter() - t1
-    step_s = 11 * moe_s + dense_s
+    head_s = 0.0
+    if head:
+        lm = m(129280, H)
+        t2 = time.perf_counter()
+        lin(lm, oracle.rms_norm(x, norm))
+        head_s = time.perf_counter() - t2
+    step_s = 11 * moe_s + dense_s + head_s
+    what = f"and the q8 lm_head ({head_s * 1e3:.1f} ms)" if head else "(lm_head not included)"
     return {"value": round(1.0 / step_s, 3), "unit": "tok/s", "cores": oracle.get_threads(),
             "kind": "port",
             "sample": f"{n_layers} MoE layers ({moe_s * 1e3:.1f} ms each) and one dense layer "
-                      f"({dense_s * 1e3:.1f} ms) of one sequence; a 12-layer step = 11 MoE + 1 dense "
-                      "(lm_head not included)"}
+                      f"({dense_s * 1e3:.1f} ms) of one sequence over a {prefix}-token prefix, "
+                      f"mode {mode}; a 12-layer step = 11 MoE + 1 dense {what}"}
 
 
 def run_decode(args):
@@ -1176,6 +1185,157 @@ def run_decode(args):
         res["cpu_baseline"] = decode_cpu_baseline(min(args.cpu_seconds, 10.0))
     return res
 
+
+
+# ---------------------------------------------------------------------------
+# The reference's fixed-work decoder benchmark (src/model/benchmark.rs:5-64):
+# a 1517-token prefill, then 512 teacher-forced decode steps of one sequence
+# whose logits are all consumed by a checksum, DynamicActivations, q8 lm_head.
+FW_PREFIX, FW_STEPS, FW_RECORDED = 1517, 512, 250
+FW_METRIC = "fixed-work decode tok/s (1517-token prefill, 512 teacher-forced steps, batch 1)"
+
+
+def fixed_work_step_bytes(cfg, tokens):
+    """Algorithmic HBM bytes of one batch-1 decode step: every weight the
+    step reads (attention projections, dense FFN, shared expert, six routed
+    experts per MoE layer, routers, q8 lm_head) and every layer's KV."""
+    H = cfg.hidden
+    q8 = lambda r, c: r * c + r * ((c + 31) // 32) * 4
+    attn = cfg.layers * 4 * q8(H, H)
+    dense = cfg.first_dense * (2 * q8(cfg.dense_width, H) + q8(H, cfg.dense_width))
+    per_moe = (cfg.top_k * (2 * q8(cfg.expert_width, H) + q8(H, cfg.expert_width))
+               + 2 * q8(cfg.shared_width, H) + q8(H, cfg.shared_width) + cfg.experts * H * 2)
+    kv = cfg.layers * tokens * H * 4 * 2
+    return attn + dense + (cfg.layers - cfg.first_dense) * per_moe + kv + q8(cfg.vocab, H)
+
+
+def run_fixed_work(args):
+    """The fixed-work decoder benchmark on one GPU with random-init weights of
+    the upstream decoder's shapes (12 layers, 64 experts, q8 lm_head over
+    129,280 tokens).  Synthetic stand-ins: the 1517 prefill rows (1513 image
+    features + 4 prompt embeddings in the reference) are N(0, 1) rows, and the
+    250 recorded token ids are seeded random ids, cycled to 512 steps.
+
+    Each repetition: the embeddings (pinned host memory) are copied in, the
+    prefill runs (eager launches; uocr_kv_attention_prefill for its causal
+    attention), then 512 replays of a CUDA graph of one step (the step's token
+    read from the device list, the decode step, the checksum of all 129,280
+    logits), then the 8-byte checksum is read back.  The reference's first
+    repetition is its warm-up; here a whole warm-up repetition precedes the
+    timed ones.  value = 512 / decode seconds (median repetition)."""
+    import torch
+
+    import uocr_q8
+    from uocr_q8.decoder import (DecodeState, Decoder, DecoderConfig, decode_step,
+                                 logits_checksum_device, prefill)
+    torch.cuda.set_device(0)
+    dev = "cuda:0"
+    ctx = uocr_q8.GpuContext(0)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream)
+    cfg = DecoderConfig()
+    mode = uocr_q8.QuantizationMode.DYNAMIC_ACTIVATIONS
+    rng = np.random.default_rng(23)
+    emb_h = torch.from_numpy(
+        rng.standard_normal((FW_PREFIX, cfg.hidden)).astype(np.float32)).pin_memory()
+    recorded = rng.integers(0, cfg.vocab, FW_RECORDED)
+    tok_h = torch.from_numpy(np.resize(recorded, FW_STEPS).astype(np.int64)).pin_memory()
+    acc_h = torch.zeros(1, dtype=torch.int64).pin_memory()
+    with torch.cuda.stream(stream):
+        dec = Decoder.random(ctx, cfg, seed=21, lm_head="q8")
+        state = DecodeState(dec, 1, FW_PREFIX)
+        emb_d = torch.empty((FW_PREFIX, cfg.hidden), device=dev)
+        tok_d = torch.empty(FW_STEPS, dtype=torch.int64, device=dev)
+        ctr = torch.zeros(1, dtype=torch.int64, device=dev)
+        acc = torch.zeros(1, dtype=torch.int64, device=dev)
+        logits = torch.empty((1, cfg.vocab), device=dev)
+
+    def step():
+        decode_step(dec, state, tok_d.index_select(0, ctr), mode, logits)
+        logits_checksum_device(ctx, logits, acc)
+        ctr.add_(1)
+
+    def begin():
+        state.reset(0)
+        emb_d.copy_(emb_h, non_blocking=True)
+        tok_d.copy_(tok_h, non_blocking=True)
+        ctr.zero_()
+        acc.zero_()
+        return prefill(dec, state, emb_d, mode)
+
+    with torch.cuda.stream(stream):  # warm-up: sizes every workspace
+        begin()
+        for _ in range(3):
+            step()
+    ctx.sync()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    with torch.cuda.stream(stream):  # warm-up repetition through the graph
+        begin()
+        for _ in range(FW_STEPS):
+            graph.replay()
+    ctx.sync()
+    torch.cuda.synchronize()
+    reps = max(3, min(args.steps, 5))
+    prefill_s, decode_s, sums = [], [], []
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    with ClockSampler(0) as clocks:
+        for _ in range(reps):
+            with torch.cuda.stream(stream):
+                ev[0].record(stream)
+                begin()
+                ev[1].record(stream)
+                for _ in range(FW_STEPS):
+                    graph.replay()
+                acc_h.copy_(acc, non_blocking=True)
+                ev[2].record(stream)
+            ev[2].synchronize()
+            prefill_s.append(ev[0].elapsed_time(ev[1]) * 1e-3)
+            decode_s.append(ev[1].elapsed_time(ev[2]) * 1e-3)
+            sums.append(int(acc_h.numpy().view(np.uint64)[0]))
+    ctx.sync()
+    med = sorted(range(reps), key=lambda i: decode_s[i])[reps // 2]
+    dsec, psec = decode_s[med], prefill_s[med]
+    # KV present at step g: the prefix plus min(g + 1, window) ring tokens
+    total_bytes = sum(fixed_work_step_bytes(cfg, FW_PREFIX + min(g + 1, cfg.window))
+                      for g in range(FW_STEPS))
+    step_bytes = total_bytes // FW_STEPS
+    gbs = total_bytes / dsec / 1e9
+    peak, peak_kind = peak_hbm()
+    res = {"metric": FW_METRIC, "value": round(FW_STEPS / dsec, 1), "unit": "tok/s", "n_gpus": 1,
+           "steps": reps, "warmup": 1, "ms_per_step": round(dsec / FW_STEPS * 1e3, 4),
+           "higher_is_better": True, "scaling": "none (one sequence)", "vs_baseline": None,
+           "dtype": "int8-act", "data": "synthetic (seeded; random-init weights)",
+           "config": {"workload": "fixed_work_decoder", "prefix_tokens": FW_PREFIX,
+                      "decode_steps": FW_STEPS, "layers": cfg.layers, "hidden": cfg.hidden,
+                      "experts": cfg.experts, "top_k": cfg.top_k, "vocab": cfg.vocab,
+                      "lm_head": "q8", "mode": "DynamicActivations", "cuda_graph": "decode step",
+                      "l2": f"{step_bytes / 1e6:.0f} MB read per step (> 126 MB L2)"},
+           "prefill_seconds": round(psec, 5), "decode_with_checksum_seconds": round(dsec, 5),
+           "prefill_tok_s": round(FW_PREFIX / psec, 1),
+           "repetitions": [{"prefill_s": round(p, 5), "decode_s": round(d, 5)}
+                           for p, d in zip(prefill_s, decode_s)],
+           "logits_checksum": sums[med], "checksums_equal": len(set(sums)) == 1,
+           "e2e": {"value": round(FW_STEPS / dsec, 1), "unit": "tok/s",
+                   "h2d_bytes_per_step": FW_PREFIX * cfg.hidden * 4 + FW_STEPS * 8,
+                   "d2h_bytes_per_step": 8,
+                   "note": "a step is a whole repetition: embeddings and token ids in, "
+                           "checksum out"},
+           "roofline": {"bound": "hbm", "kernel": "whole decode step (attention, MoE, projections, "
+                                                "lm_head)",
+                        "achieved": round(gbs, 2), "peak": peak, "peak_kind": peak_kind,
+                        "unit": "GB/s", "frac": round(gbs / peak, 4), "traffic": None},
+           "gpu_launches": None, "clocks": clocks.summary(),
+           "reference_published": {"decode_with_checksum_seconds": 4.031535, "tok_s": 127.0,
+                                   "hardware": "M4 Pro, 8 threads"}}
+    del graph
+    state.free()
+    if not args.no_cpu:
+        res["cpu_baseline"] = decode_cpu_baseline(min(args.cpu_seconds, 8.0), prefix=FW_PREFIX,
+                                                  mode=1, head=True)
+    return res
 
 
 # ---------------------------------------------------------------------------
@@ -1558,6 +1718,7 @@ def run_secondary(args):
     sub("attention_decode", run_attn, steps=200, cpu_seconds=min(args.cpu_seconds, 5.0))
     sub("decode_step_12_layers", run_decode, steps=60, cpu_seconds=min(args.cpu_seconds, 6.0),
         lm_head="bf16")
+    sub("fixed_work_decoder", run_fixed_work, steps=3, cpu_seconds=min(args.cpu_seconds, 6.0))
     return out
 
 
@@ -1621,7 +1782,7 @@ def main():
                          "defaults to the committed capture of the workload's kernel")
     ap.add_argument("--workload",
                     choices=["ep_peer", "moe_decode", "gemv", "prefill", "int8suite", "ep_decode",
-                             "attn_decode", "decode_step"],
+                             "attn_decode", "decode_step", "fixed_work"],
                     default="ep_peer")
     ap.add_argument("--gemv-int8", action="store_true")
     ap.add_argument("--prefill-mode", type=int, choices=[0, 2], default=0)
@@ -1646,7 +1807,7 @@ def main():
         print(json.dumps(run_ep_emulated(args)), flush=True)
         return
     single = {"gemv": run_gemv, "prefill": run_prefill, "decode_step": run_decode,
-              "attn_decode": run_attn, "int8suite": run_int8suite}
+              "attn_decode": run_attn, "int8suite": run_int8suite, "fixed_work": run_fixed_work}
     if args.workload in single:
         print(json.dumps(single[args.workload](args)), flush=True)
         return

@@ -366,6 +366,12 @@ int uocr_linear_bf16_tc(uocr_ctx *ctx, const uint16_t *w_dev, size_t n, size_t k
 typedef struct uocr_rope uocr_rope;
 typedef struct uocr_kv uocr_kv;
 
+/* The fixed-work decoder benchmark's logits checksum (src/model/benchmark.rs:
+ * 43-47): *acc_dev (device u64) += the bit pattern of each of the n floats
+ * of x_dev, wrapping modulo 2^64, so equal to the reference's sequential
+ * wrapping_add.  Asynchronous on the context's stream. */
+int uocr_bits_checksum(uocr_ctx *ctx, const float *x_dev, size_t n, uint64_t *acc_dev);
+
 /* ops::rms_norm (src/cpu/ops.rs:362-414,419-421): rows x width, weight of
  * width floats; out may equal x.  Shape for width 0 or eps not finite and
  * positive; Numerical ("normalization") for a nonfinite input or weight. */
@@ -399,6 +405,19 @@ int uocr_attention_decode(uocr_ctx *ctx, const float *q_dev, const float *keys_d
                           size_t keys_len, const float *values_dev, size_t values_len,
                           size_t width, size_t heads, float *out_dev);
 
+/* The prefill branch of Decoder::layer (src/decoder/mod.rs:313-338): causal
+ * ops::attention (src/cpu/ops.rs:263-360, its mask in softmax_rows :190-222)
+ * of token-major q, keys, values [tokens x width] in heads of width/heads;
+ * out [tokens x width], row i over tokens 0..i.  The same arithmetic order as
+ * the reference's, so row i equals uocr_attention_decode over tokens 0..i; the
+ * outputs match the reference bit for bit except where exp rounds differently
+ * and in the sign of an output that is zero.  Shape for an empty or uneven
+ * layout; Resource under the reference's scratch rule (dim*tokens +
+ * tokens*width + tokens elements); Unsupported beyond 65535 tokens. */
+int uocr_attention_prefill(uocr_ctx *ctx, const float *q_dev, const float *keys_dev,
+                           const float *values_dev, size_t tokens, size_t width, size_t heads,
+                           float *out_dev);
+
 /* LayerCache (src/decoder/cache.rs) for `batch` sequences on the device: an
  * immutable prefix of up to max_prefix tokens followed by a ring of `window`
  * tokens (slot of a new token: prefix + generated % window).  Stored per
@@ -414,19 +433,29 @@ int uocr_attention_decode(uocr_ctx *ctx, const float *q_dev, const float *keys_d
  *   uocr_kv_rope:    ops::rope of q and k rows at each sequence's position
  *                    (before this token's push);
  *   uocr_kv_attention: ops::attention_decode of q row b over sequence b;
+ *   uocr_kv_attention_prefill: the causal attention of a prefill
+ *                    (uocr_attention_prefill) of q rows [rows x width] of
+ *                    sequence seq over its prefix, right after
+ *                    uocr_kv_prefill of those rows (Shape unless rows equals
+ *                    that prefix);
  *   uocr_kv_state:   LayerCache::tokens and ::position (synchronous);
  *   uocr_kv_export:  LayerCache::keys / ::values of sequence seq as
  *                    token-major rows (device; NULL outputs: *tokens only).
+ *   uocr_kv_reset:   sequence seq empty again (LayerCache::new), to be
+ *                    prefilled anew;
  * push / rope / attention before every sequence is prefilled: Shape. */
 int uocr_kv_create(uocr_ctx *ctx, size_t batch, size_t heads, size_t head_dim, size_t window,
                    size_t max_prefix, uocr_kv **out);
 int uocr_kv_free(uocr_kv *kv);
+int uocr_kv_reset(uocr_ctx *ctx, uocr_kv *kv, size_t seq);
 int uocr_kv_prefill(uocr_ctx *ctx, uocr_kv *kv, size_t seq, const float *keys_dev,
                     const float *values_dev, size_t tokens);
 int uocr_kv_push(uocr_ctx *ctx, uocr_kv *kv, const float *k_dev, const float *v_dev);
 int uocr_kv_rope(uocr_ctx *ctx, const uocr_kv *kv, const uocr_rope *rope, float *q_dev,
                  float *k_dev);
 int uocr_kv_attention(uocr_ctx *ctx, const uocr_kv *kv, const float *q_dev, float *out_dev);
+int uocr_kv_attention_prefill(uocr_ctx *ctx, const uocr_kv *kv, size_t seq, const float *q_dev,
+                              size_t rows, float *out_dev);
 /* uocr_kv_rope then uocr_kv_push in one launch, reading the fused q/k/v
  * projection rows [q | k | v] (batch x 3*heads*head_dim, device): q is rotated
  * into q_out_dev (batch x heads*head_dim), k rotated and v copied into the

@@ -82,6 +82,7 @@ def _declare(L):
         "q8o_rms_norm": (I, [P, S, S, P, F, P]),
         "q8o_rope": (I, [P, S, S, S, F]),
         "q8o_attention_decode": (I, [P, S, P, S, P, S, S, P]),
+        "q8o_attention": (I, [P, S, S, S, P, P, S, I, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -268,6 +269,36 @@ def attention_decode(q, keys, values, heads: int) -> np.ndarray:
     _check(lib().q8o_attention_decode(_ptr(q), q.size, _ptr(k), k.size, _ptr(v), v.size, heads,
                                       _ptr(out)))
     return out
+
+
+def attention(q, k, v, causal: bool = True) -> np.ndarray:
+    """ops::attention: q [heads, nq, dim] over k, v [heads, nk, dim]."""
+    q = _contig(q, np.float32)
+    k = _contig(k, np.float32)
+    v = _contig(v, np.float32)
+    heads, nq, dim = q.shape
+    if k.shape != v.shape or k.ndim != 3 or k.shape[0] != heads or k.shape[2] != dim:
+        raise OracleError(4)
+    out = np.empty_like(q)
+    _check(lib().q8o_attention(_ptr(q), heads, nq, dim, _ptr(k), _ptr(v), k.shape[1],
+                               int(bool(causal)), _ptr(out)))
+    return out
+
+
+def attention_prefill(q, keys, values, heads: int) -> np.ndarray:
+    """The prefill branch of Decoder::layer (src/decoder/mod.rs:313-338):
+    token-major q, keys, values [tokens x width] split into heads, causal
+    ops::attention, joined back to token-major rows."""
+    q = _contig(q, np.float32)
+    tokens, width = q.shape
+    dim = width // heads
+
+    def split(a):
+        return np.ascontiguousarray(
+            _contig(a, np.float32).reshape(-1, heads, dim).transpose(1, 0, 2))
+
+    out = attention(split(q), split(keys), split(values), True)
+    return np.ascontiguousarray(out.transpose(1, 0, 2).reshape(tokens, width))
 
 
 class LayerCache:

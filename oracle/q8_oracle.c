@@ -488,3 +488,46 @@ int q8o_attention_decode(const float *q, size_t width, const float *keys, size_t
   free(scores);
   return Q8O_OK;
 }
+
+/* ops::attention (src/cpu/ops.rs:263-360) with its causal mask
+ * (softmax_rows, :190-222), scalar branch: q [heads][nq][dim] over k, v
+ * [heads][nk][dim].  Per head and query row i: scores over all nk keys
+ * (left-to-right dot from -0.0, times 1/sqrt(dim)); when causal (nq == nk)
+ * the scores after key i become -inf; the softmax; then each output element
+ * is the left-to-right sum from -0.0 over all nk keys of score * value (the
+ * masked keys add products of +0.0).  The reference's query blocks change
+ * only how many rows are held at once, not a row's arithmetic. */
+int q8o_attention(const float *q, size_t heads, size_t nq, size_t dim, const float *k,
+                  const float *v, size_t nk, int causal, float *out) {
+  if (heads == 0 || nq == 0 || nk == 0 || dim == 0 || (causal && nq != nk)) return Q8O_SHAPE;
+  const float scale = 1.0f / sqrtf((float)dim);
+  float *scores = (float *)malloc(nk * sizeof(float));
+  if (!scores) return Q8O_RESOURCE;
+  for (size_t h = 0; h < heads; ++h) {
+    const float *kh = k + h * nk * dim, *vh = v + h * nk * dim;
+    for (size_t i = 0; i < nq; ++i) {
+      const float *qi = q + (h * nq + i) * dim;
+      for (size_t t = 0; t < nk; ++t) {
+        float acc = -0.0f;
+        for (size_t d = 0; d < dim; ++d) acc += qi[d] * kh[t * dim + d];
+        scores[t] = acc;
+      }
+      for (size_t t = 0; t < nk; ++t) scores[t] *= scale;
+      if (causal)
+        for (size_t t = i + 1; t < nk; ++t) scores[t] = -INFINITY;
+      int st = q8o_softmax(scores, nk);
+      if (st) {
+        free(scores);
+        return st;
+      }
+      float *o = out + (h * nq + i) * dim;
+      for (size_t d = 0; d < dim; ++d) {
+        float acc = -0.0f;
+        for (size_t t = 0; t < nk; ++t) acc += scores[t] * vh[t * dim + d];
+        o[d] = acc;
+      }
+    }
+  }
+  free(scores);
+  return Q8O_OK;
+}

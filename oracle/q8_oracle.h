@@ -133,6 +133,12 @@ int q8o_rope(float *values, size_t n, size_t head_dim, size_t position, float th
 int q8o_attention_decode(const float *q, size_t width, const float *keys, size_t keys_len,
                          const float *values, size_t values_len, size_t heads, float *out);
 
+/* ops::attention (src/cpu/ops.rs:263-360), scalar branch: q [heads][nq][dim]
+ * over k, v [heads][nk][dim]; causal (nq == nk) masks the keys after each
+ * query's own position. */
+int q8o_attention(const float *q, size_t heads, size_t nq, size_t dim, const float *k,
+                  const float *v, size_t nk, int causal, float *out);
+
 #ifdef __cplusplus
 }
 #endif

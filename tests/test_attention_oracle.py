@@ -1,7 +1,8 @@
 """CPU checks of the oracle's decode-attention ops against the reference's
 own tests: RMSNorm and rope known answers (tests/ops.rs:33-73), decode
 attention against an f64 restatement (tests/decode_attention.rs:6-47) and its
-layout rejections (:50-64), and the KV cache ring (tests/cache.rs).
+layout rejections (:50-64), causal prefill attention (tests/ops.rs:89-99,
+166-202), and the KV cache ring (tests/cache.rs).
 """
 import numpy as np
 import pytest
@@ -104,6 +105,67 @@ def test_attention_rejects_layouts():
             oracle.attention_decode(q, np.array(keys, np.float32), np.array(values, np.float32),
                                     heads)
         assert e.value.kind == "Shape"
+
+
+def test_causal_attention_excludes_future_values():
+    """tests/ops.rs:89-99."""
+    q = np.zeros((1, 2, 2), np.float32)
+    v = np.array([2.0, 4.0, 6.0, 8.0], np.float32).reshape(1, 2, 2)
+    assert oracle.attention(q, q, v, True).ravel().tolist() == [2.0, 4.0, 4.0, 6.0]
+    assert oracle.attention(q, q, v, False).ravel().tolist() == [4.0, 6.0, 4.0, 6.0]
+
+
+def causal_block_case(heads=2, tokens=129, dim=3):
+    """tests/ops.rs:167-181 inputs: zero queries and keys, values
+    head * 100 + token + channel."""
+    q = np.zeros((heads, tokens, dim), np.float32)
+    i = np.arange(heads * tokens * dim)
+    v = ((i // (tokens * dim)) * 100 + (i // dim) % tokens + i % dim).astype(np.float32)
+    return q, v.reshape(heads, tokens, dim)
+
+
+def test_causal_attention_masks_across_query_block_boundaries():
+    """tests/ops.rs:166-194: uniform weights over the first token + 1 values."""
+    heads, tokens, dim = 2, 129, 3
+    q, v = causal_block_case(heads, tokens, dim)
+    out = oracle.attention(q, q, v, True)
+    h, t, c = np.meshgrid(np.arange(heads), np.arange(tokens), np.arange(dim), indexing="ij")
+    want = (h * 100 + c).astype(np.float32) + t.astype(np.float32) / 2
+    assert np.max(np.abs(out - want)) < 2e-4
+
+
+def test_causal_attention_of_zeros_is_zero():
+    """tests/ops.rs:196-202 (a zero input gives a zero output)."""
+    q = np.zeros((1, 129, 3), np.float32)
+    assert np.array_equal(oracle.attention(q, q, q, True), q)
+
+
+def test_causal_row_equals_decode_over_its_prefix():
+    """Row i of the causal prefill attention is attention_decode over tokens
+    0..i: the masked keys only add +0.0 products after the real ones, so every
+    nonzero output is bit-identical."""
+    rng = np.random.default_rng(5)
+    tokens, heads, dim = 23, 3, 8
+    width = heads * dim
+    q, k, v = (rng.standard_normal((tokens, width)).astype(np.float32) for _ in range(3))
+    out = oracle.attention_prefill(q, k, v, heads)
+    for i in range(tokens):
+        ref = oracle.attention_decode(q[i], k[:i + 1], v[:i + 1], heads)
+        assert np.array_equal(out[i], ref)
+        nz = ref != 0
+        assert np.array_equal(out[i][nz].view(np.uint32), ref[nz].view(np.uint32))
+
+
+def test_causal_attention_rejects_layouts():
+    q = np.zeros((1, 2, 2), np.float32)
+    with pytest.raises(oracle.OracleError) as e:
+        oracle.attention(q, np.zeros((1, 3, 2), np.float32), np.zeros((1, 3, 2), np.float32), True)
+    assert e.value.kind == "Shape"
+    bad = q.copy()
+    bad[0, 0, 0] = np.nan
+    with pytest.raises(oracle.OracleError) as e:
+        oracle.attention(bad, q, q, True)
+    assert e.value.kind == "Numerical"
 
 
 def test_cache_prefix_survives_ring_wraps():

@@ -2,7 +2,9 @@
 KV cache, the attention half of a decoder layer) against the CPU oracle,
 through the C ABI.
 
-Bit-exact: RMSNorm, rope and the cache contents.  Attention follows the
+Bit-exact: RMSNorm, rope and the cache contents.  The causal attention of a
+prefill runs the decode kernels with one query per row, so it is held to the
+same bounds.  Attention follows the
 reference's order, so it is bit-identical wherever every exp rounds the same
 (checked exactly with uniform scores, where exp is exact); otherwise the
 device's exp (double, rounded once) and the C library's expf (within 0.502
@@ -283,6 +285,119 @@ def test_cache_errors(ctx):
             A().KvCache(ctx, *args)
         assert e.value.kind == "Shape"
     kv.free()
+
+
+# ---------------------------------------------------------------- prefill attention
+def _token_major(a):
+    """[heads, tokens, dim] -> token-major [tokens, heads * dim]."""
+    return np.ascontiguousarray(np.transpose(a, (1, 0, 2)).reshape(a.shape[1], -1))
+
+
+def _equal_values(a, b):
+    """Bit-identical except for the sign of zeros (ops::attention sums its
+    masked +0.0 products after the real ones; the device sums only the real
+    ones)."""
+    a, b = np.asarray(a, np.float32), np.asarray(b, np.float32)
+    nz = b != 0
+    return np.array_equal(a, b) and np.array_equal(a[nz].view(np.uint32), b[nz].view(np.uint32))
+
+
+def test_prefill_attention_reference_cases(ctx):
+    """tests/ops.rs:89-99 (future values excluded), :166-194 (masks across
+    the reference's 128-query blocks: uniform weights, so every exp is exact
+    and the outputs are the oracle's bit for bit) and :196-202 (zeros)."""
+    from test_attention_oracle import causal_block_case
+    q = np.zeros((2, 2), np.float32)
+    v = np.array([[2.0, 4.0], [6.0, 8.0]], np.float32)
+    out = host(A().attention_prefill_device(ctx, dev(q), dev(q), dev(v), 1))
+    ctx.sync()
+    assert out.ravel().tolist() == [2.0, 4.0, 4.0, 6.0]
+    heads, tokens, dim = 2, 129, 3
+    qh, vh = causal_block_case(heads, tokens, dim)
+    out = host(A().attention_prefill_device(ctx, dev(_token_major(qh)), dev(_token_major(qh)),
+                                            dev(_token_major(vh)), heads))
+    ctx.sync()
+    ref = _token_major(oracle.attention(qh, qh, vh, True))
+    assert _equal_values(out, ref)
+    h, t, c = np.meshgrid(np.arange(heads), np.arange(tokens), np.arange(dim), indexing="ij")
+    want = _token_major(((h * 100 + c).astype(np.float32) + t.astype(np.float32) / 2))
+    assert np.max(np.abs(out - want)) < 2e-4
+    z = np.zeros((129, 3), np.float32)
+    out = host(A().attention_prefill_device(ctx, dev(z), dev(z), dev(z), 1))
+    ctx.sync()
+    assert np.array_equal(out, z)
+
+
+@pytest.mark.parametrize("heads,dim,tokens", [(3, 5, 37), (2, 64, 300), (10, 128, 257)])
+def test_prefill_attention_matches_oracle(ctx, heads, dim, tokens):
+    """Random inputs (the generic kernel for 3 x 5, the TMA kernel otherwise)
+    against the oracle's causal ops::attention: 1e-5 relative (exp may round
+    differently by one ulp); with keys equal within each head every exp is
+    exact and the outputs are bit-identical up to the sign of zeros."""
+    rng = np.random.default_rng(tokens)
+    width = heads * dim
+    q, k, v = (rng.standard_normal((tokens, width)).astype(np.float32) for _ in range(3))
+    out = host(A().attention_prefill_device(ctx, dev(q), dev(k), dev(v), heads))
+    ctx.sync()
+    ref = oracle.attention_prefill(q, k, v, heads)
+    assert np.max(np.abs(out - ref)) <= 1e-5 * max(1.0, float(np.max(np.abs(ref))))
+    k = np.tile(rng.standard_normal(width).astype(np.float32), (tokens, 1))
+    out = host(A().attention_prefill_device(ctx, dev(q), dev(k), dev(v), heads))
+    ctx.sync()
+    assert _equal_values(out, oracle.attention_prefill(q, k, v, heads))
+
+
+def test_prefill_attention_full_prefix_sampled_rows(ctx):
+    """The benchmark's prefill (1517 tokens, 10 heads of 128): sampled rows
+    against the oracle's attention_decode over each row's prefix, which is the
+    same arithmetic as its causal row."""
+    rng = np.random.default_rng(1517)
+    tokens, heads, dim = 1517, 10, 128
+    width = heads * dim
+    q, k, v = (rng.standard_normal((tokens, width)).astype(np.float32) for _ in range(3))
+    out = host(A().attention_prefill_device(ctx, dev(q), dev(k), dev(v), heads))
+    ctx.sync()
+    for i in (0, 1, 31, 32, 33, 700, 1023, 1024, 1516):
+        ref = oracle.attention_decode(q[i], k[:i + 1], v[:i + 1], heads)
+        assert np.max(np.abs(out[i] - ref)) <= 1e-5 * max(1.0, float(np.max(np.abs(ref)))), i
+
+
+@pytest.mark.parametrize("heads,dim", [(2, 8), (10, 128)])
+def test_kv_prefill_attention_equals_token_major(ctx, heads, dim):
+    """uocr_kv_attention_prefill over the cache (head-major or tiled layout)
+    gives the token-major entry point's outputs bit for bit; rows other than
+    the prefilled ones are Shape."""
+    import uocr_q8
+    rng = np.random.default_rng(dim)
+    width, tokens = heads * dim, 45
+    kv = A().KvCache(ctx, 2, heads, dim, 4, max_prefix=64)
+    q, k, v = (rng.standard_normal((tokens, width)).astype(np.float32) for _ in range(3))
+    kv.prefill(0, dev(rng.standard_normal((7, width)).astype(np.float32)),
+               dev(rng.standard_normal((7, width)).astype(np.float32)))
+    kv.prefill(1, dev(k), dev(v))
+    out = host(kv.attention_prefill(1, dev(q)))
+    ref = host(A().attention_prefill_device(ctx, dev(q), dev(k), dev(v), heads))
+    ctx.sync()
+    assert bits_equal(out, ref)
+    with pytest.raises(uocr_q8.OcrError) as e:
+        kv.attention_prefill(0, dev(q))
+    assert e.value.kind == "Shape"
+    kv.free()
+
+
+def test_prefill_attention_errors(ctx):
+    import torch
+    import uocr_q8
+    z = torch.zeros((4, 6), device="cuda")
+    with pytest.raises(uocr_q8.OcrError) as e:
+        A().attention_prefill_device(ctx, z, z, z, 4)
+    assert e.value.kind == "Shape"
+    bad = z.clone()
+    bad[1, 0] = float("nan")
+    A().attention_prefill_device(ctx, bad, z, z, 2)
+    with pytest.raises(uocr_q8.OcrError) as e:
+        ctx.sync()
+    assert e.value.kind == "Numerical"
 
 
 # ---------------------------------------------------------------- attention block

@@ -224,6 +224,131 @@ def test_decode_step_matches_oracle(ctx, mode, head):
     state.free()
 
 
+def oracle_prefill(cfg, layers, final_norm, head, x, mode):
+    """Decoder::prefill (src/decoder/mod.rs:382-398) of embedding rows x with
+    the oracle's operations; returns the layer caches and the logits."""
+    T = x.shape[0]
+    dyn = mode == 2 or (mode == 1 and T == 1)
+    proj = (lambda mat, v: oracle.linear_dynamic_int8(mat, v)) if dyn else \
+        (lambda mat, v: oracle.linear(mat, v))
+    caches = []
+    for L in layers:
+        n = oracle.rms_norm(x, L["in"], cfg.eps)
+        q, k, v = (proj(L[key], n) for key in ("q", "k", "v"))
+        q = np.stack([oracle.rope(q[i], cfg.head_dim, i, cfg.theta) for i in range(T)])
+        k = np.stack([oracle.rope(k[i], cfg.head_dim, i, cfg.theta) for i in range(T)])
+        c = oracle.LayerCache(cfg.heads, cfg.head_dim, cfg.window)
+        c.prefill(k, v, T)
+        caches.append(c)
+        a = oracle.attention_prefill(q, k, v, cfg.heads)
+        r = proj(L["o"], a) + x
+        n2 = oracle.rms_norm(r, L["post"], cfg.eps)
+        if "dense" in L:
+            y = oracle.feed_forward(L["dense"], n2, mode)
+        else:
+            logits = oracle.linear_bf16(L["router"], n2)
+            y, _, _ = oracle.experts(L["shared"], L["experts"], logits, n2, cfg.top_k, mode)
+        x = r + y
+    h = oracle.rms_norm(x[T - 1:], final_norm, cfg.eps)
+    if isinstance(head, np.ndarray):
+        return caches, oracle.linear_bf16(head, h)[0]
+    lin = oracle.linear_dynamic_int8 if mode != 0 else oracle.linear
+    return caches, lin(head, h)[0]
+
+
+def _close(got, ref, tol):
+    scale = float(np.max(np.abs(ref)))
+    err = float(np.max(np.abs(got.astype(np.float64) - ref)))
+    assert err <= tol * scale, (err, scale)
+    assert int(np.argmax(got)) == int(np.argmax(ref)) or \
+        np.sort(ref)[-1] - np.sort(ref)[-2] < 2 * err
+
+
+@pytest.mark.parametrize("mode,head,tokens", [(0, "q8", 37), (1, "q8", 37), (1, "q8", 1),
+                                              (0, "bf16", 70)])
+def test_prefill_then_decode_matches_oracle(ctx, mode, head, tokens):
+    """Decoder::prefill of one sequence (causal attention over its rows, the
+    MoE over all rows with the reference's per-group arithmetic) and then
+    teacher-forced Decoder::step calls, as in the fixed-work benchmark
+    (src/model/benchmark.rs:37-50), against the oracle: the prefill logits,
+    the caches' contents and every step's logits.  DynamicActivations runs a
+    multi-row prefill with FP32 activations and every decode projection with
+    int8 ones."""
+    import torch
+    from uocr_q8.decoder import DecodeState, Decoder, decode_step, prefill
+    cfg = small_config()
+    dec = Decoder.random(ctx, cfg, seed=40 + mode, lm_head=head)
+    layers, emb, final_norm, head_h = host_decoder(dec)
+    rng = np.random.default_rng(41 + tokens)
+    x = rng.standard_normal((tokens, cfg.hidden)).astype(np.float32)
+    state = DecodeState(dec, 1, tokens)
+    logits = host(prefill(dec, state, dev(x), mode))
+    ctx.sync()
+    caches, ref = oracle_prefill(cfg, layers, final_norm, head_h, x, mode)
+    tol = 1e-3 if mode == 0 else 1e-2
+    _close(logits[0], ref, tol)
+    for cache, c in zip(state.caches, caches):
+        keys, values = (host(t) for t in cache.export(0)[:2])
+        kerr = float(np.max(np.abs(keys - c.keys)))
+        assert kerr <= tol * float(np.max(np.abs(c.keys)))
+        assert float(np.max(np.abs(values - c.values))) <= tol * float(np.max(np.abs(c.values)))
+    # continue from the oracle's own caches: each side follows its own state
+    for step in range(6):  # the 4-token ring wraps
+        token = int(rng.integers(0, cfg.vocab))
+        got = host(decode_step(dec, state, dev(np.array([token], np.int64)), mode))
+        ctx.sync()
+        ref = oracle_step(cfg, layers, emb, final_norm, head_h, caches, token, mode)
+        _close(got[0], ref, tol)
+    assert state.caches[0].state(0) == (caches[0].tokens(), caches[0].position())
+    state.free()
+
+
+def test_logits_checksum_wraps_like_the_reference(ctx):
+    """uocr_bits_checksum: the u64 wrapping sum of the logits' bit patterns
+    (src/model/benchmark.rs:43-47), accumulated over calls."""
+    import torch
+    from uocr_q8.decoder import logits_checksum_device
+    rng = np.random.default_rng(3)
+    acc = torch.zeros(1, dtype=torch.int64, device="cuda")
+    want = 0
+    for n in (1, 129280, 1000003):
+        x = rng.standard_normal(n).astype(np.float32)
+        x[: n // 3] = -x[: n // 3]
+        logits_checksum_device(ctx, dev(x), acc)
+        want = (want + int(x.view(np.uint32).astype(np.uint64).sum())) % (1 << 64)
+    # push the sum across 2^64 to check the wrap
+    big = np.full(1 << 20, np.uint32(0xFFFFFFFF)).view(np.float32)
+    for _ in range(3):
+        logits_checksum_device(ctx, dev(big), acc)
+        want = (want + (1 << 20) * 0xFFFFFFFF) % (1 << 64)
+    ctx.sync()
+    got = int(host(acc).view(np.uint64)[0])
+    assert got == want
+
+
+def test_cache_reset_then_prefill_again(ctx):
+    """uocr_kv_reset empties a sequence: attention before the new prefill is
+    Shape, and the new prefill gives a fresh cache."""
+    import torch
+    import uocr_q8
+    from uocr_q8.attention import KvCache
+    kv = KvCache(ctx, 1, 2, 8, 4, max_prefix=10)
+    a = torch.randn((10, 16), device="cuda")
+    kv.prefill(0, a, a)
+    kv.push(a[:1], a[:1])
+    kv.reset(0)
+    with pytest.raises(uocr_q8.OcrError) as e:
+        kv.attention(a[:1])
+    assert e.value.kind == "Shape"
+    b = torch.randn((6, 16), device="cuda")
+    kv.prefill(0, b, b * 2)
+    k, v, _ = (kv.export(0) + (None,))
+    ctx.sync()
+    assert kv.state(0) == (6, 6)
+    assert torch.equal(k, b) and torch.equal(v, b * 2)
+    kv.free()
+
+
 @pytest.mark.slow
 @pytest.mark.parametrize("mode", [0, 2])
 def test_decode_step_config4_shapes(ctx, mode):

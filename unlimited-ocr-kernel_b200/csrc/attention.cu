@@ -2,7 +2,9 @@
 // device: RMSNorm (ops::rms_norm, src/cpu/ops.rs:362-414), the rotary
 // embedding (ops::rope, :420-437), the token-major KV cache with an
 // immutable prefix and a bounded ring (LayerCache, src/decoder/cache.rs:3-95)
-// and single-query attention over it (ops::attention_decode, :515-606).
+// and single-query attention over it (ops::attention_decode, :515-606); the
+// causal attention of a prefill (ops::attention, :263-360) runs the same
+// kernels with one query per row, row i over tokens 0..i of one sequence.
 //
 // Arithmetic follows the reference's order so that results are bit-identical
 // to it except where exp rounds differently (exp_f32_via_f64, rarely one ulp):
@@ -330,13 +332,17 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   __shared__ int red_bad[kAttnThreads / 32];
   __shared__ float s_max, s_sum;
   __shared__ int s_bad;
-  const int h = blockIdx.x, b = blockIdx.y;
+  const int h = blockIdx.x;
+  // causal: the longest rows first, so that the short ones fill the tail
+  const int b = a.causal ? static_cast<int>(gridDim.y - 1 - blockIdx.y) : static_cast<int>(blockIdx.y);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int dim = a.dim;
   float* qs = smem_f;                              // dim floats
   float* sc = smem_f + ((dim + 3) & ~3);           // tokens floats
   int T = a.tokens;
-  if (a.state) {
+  if (a.causal) {
+    T = b + 1;
+  } else if (a.state) {
     const int prefix = a.state[2 * b], gen = a.state[2 * b + 1];
     if (prefix <= 0) {
       if (tid == 0) flag(a.status, DEV_CACHE);
@@ -344,7 +350,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     }
     T = prefix + (gen < a.window ? gen : a.window);
   }
-  const long long off = b * a.seq_stride + h * a.head_stride, rs = a.row_stride;
+  const long long off = (a.causal ? a.seq : b) * a.seq_stride + h * a.head_stride,
+                  rs = a.row_stride;
   const float* kb = a.keys + off;
   const float* vb = a.values + off;
   for (int d = tid; d < dim; d += kAttnThreads) qs[d] = a.q[b * a.ld_q + static_cast<long long>(h) * dim + d];
@@ -402,10 +409,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   __syncthreads();
 
   // output: one thread per element, tokens in order from +0.0
+  // (ops::attention_decode) or from -0.0 (the Sum of ops::attention)
   float* ob = a.out + b * a.ld_out + static_cast<long long>(h) * dim;
+  const float zero = a.causal ? -0.0f : 0.0f;
   for (int d = tid; d < dim; d += kAttnThreads) {
     const float* vc = vb + d;
-    float acc = 0.0f;
+    float acc = zero;
     int t = 0;
     for (; t + 16 <= T; t += 16) {
       float v[16];
@@ -484,10 +493,14 @@ __global__ void __launch_bounds__(64, 5)
   uint64_t* full = reinterpret_cast<uint64_t*>(
       (reinterpret_cast<uintptr_t>(sc + a.cap) + 15) & ~static_cast<uintptr_t>(15));
   uint64_t* empty = full + kTmaStages;
-  const int h = blockIdx.x, b = blockIdx.y;
+  const int h = blockIdx.x;
+  const int b = a.causal ? static_cast<int>(gridDim.y - 1 - blockIdx.y) : static_cast<int>(blockIdx.y);
+  const int kvs = a.causal ? a.seq : b;  // the sequence whose keys/values are read
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int T = a.tokens;
-  if (a.state) {
+  if (a.causal) {
+    T = b + 1;
+  } else if (a.state) {
     const int prefix = a.state[2 * b], gen = a.state[2 * b + 1];
     if (prefix <= 0) {
       if (threadIdx.x == 0) flag(a.status, DEV_CACHE);
@@ -512,8 +525,8 @@ __global__ void __launch_bounds__(64, 5)
       // tiled cache: the map's rows are 128-byte rows of the cache, a tile is
       // one box of 32 * nb of them; token-major buffers ([rows][width]): a
       // tile is nb boxes of 32 rows at x = h*dim + 32j
-      const long long tiled_y0 = (static_cast<long long>(b) * a.heads + h) * a.cap * nb;
-      const int y0 = static_cast<int>(static_cast<long long>(b) * a.cap);
+      const long long tiled_y0 = (static_cast<long long>(kvs) * a.heads + h) * a.cap * nb;
+      const int y0 = static_cast<int>(static_cast<long long>(kvs) * a.cap);
       const int x0 = h * dim;
       int it = 0;
       for (; it < 2 * ntiles; ++it) {
@@ -617,7 +630,8 @@ __global__ void __launch_bounds__(64, 5)
   }
   // ---- values: lane owns 16-byte chunks g = lane, lane + 32 of the head row
   const int chunks = dim / 4;
-  float4 acc0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), acc1 = acc0;
+  const float zero = a.causal ? -0.0f : 0.0f;  // see attn_decode_kernel
+  float4 acc0 = make_float4(zero, zero, zero, zero), acc1 = acc0;
   const int g0 = lane, g1 = lane + 32;
   if (D128) {
     // chunks == 32: lane owns chunk g0 = lane, in box lane / 8

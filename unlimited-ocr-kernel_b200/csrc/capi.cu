@@ -1364,6 +1364,18 @@ int uocr_linear_bf16_tc(uocr_ctx* ctx, const uint16_t* w_dev, size_t n, size_t k
   return check_launch();
 }
 
+// The fixed-work benchmark's checksum (src/model/benchmark.rs:43-47):
+// *acc_dev += the bit patterns of x_dev[0..n) (u64, wrapping).
+int uocr_bits_checksum(uocr_ctx* ctx, const float* x_dev, size_t n, uint64_t* acc_dev) {
+  if (!ctx) return fail(UOCR_ERR_INVALID, "null context");
+  if (n == 0) return ok();
+  if (!x_dev || !acc_dev) return fail(UOCR_ERR_INVALID, "null argument");
+  DeviceGuard g(ctx->device);
+  launch_bits_checksum(x_dev, static_cast<long long>(n), reinterpret_cast<unsigned long long*>(acc_dev),
+                       ctx->sms, ctx->stream);
+  return check_launch();
+}
+
 int uocr_rms_norm(uocr_ctx* ctx, const float* x_dev, size_t rows, size_t width,
                   const float* weight_dev, float eps, float* out_dev) {
   if (!ctx) return fail(UOCR_ERR_INVALID, "null context");
@@ -1502,6 +1514,55 @@ int uocr_attention_decode(uocr_ctx* ctx, const float* q_dev, const float* keys_d
                                       a.width);
   cudaError_t e = tma ? launch_attention_decode_tma(maps, a, 1, ctx->stream)
                       : launch_attention_decode(a, 1, static_cast<int>(tokens), ctx->stream);
+  if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
+  return ok();
+}
+
+// The prefill branch of Decoder::layer (src/decoder/mod.rs:313-338): causal
+// ops::attention (src/cpu/ops.rs:263-360, mask :190-222) of token-major
+// q/keys/values [tokens x width] split into heads; query i sees tokens 0..i.
+int uocr_attention_prefill(uocr_ctx* ctx, const float* q_dev, const float* keys_dev,
+                           const float* values_dev, size_t tokens, size_t width, size_t heads,
+                           float* out_dev) {
+  if (!ctx) return fail(UOCR_ERR_INVALID, "null context");
+  if (heads == 0 || width == 0 || width % heads || tokens == 0)
+    return fail(UOCR_ERR_SHAPE, "invalid tensor shape: invalid attention layout");
+  const size_t dim = width / heads;
+  // the reference's scratch rule: d * nk + q elements + nk
+  int st = check_elements(ctx, dim * tokens + tokens * width + tokens);
+  if (st) return st;
+  if (!q_dev || !keys_dev || !values_dev || !out_dev) return fail(UOCR_ERR_INVALID, "null argument");
+  if (!fits_int(width) || tokens > 65535 ||
+      attention_smem_bytes(static_cast<int>(dim), static_cast<int>(tokens)) > kAttnMaxSmem)
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: prefill attention over %zu tokens",
+                tokens);
+  DeviceGuard g(ctx->device);
+  AttnArgs a{};
+  a.q = q_dev;
+  a.ld_q = static_cast<long long>(width);
+  a.keys = keys_dev;
+  a.values = values_dev;
+  a.seq_stride = 0;
+  a.head_stride = static_cast<long long>(dim);
+  a.row_stride = static_cast<long long>(width);
+  a.cap = static_cast<long long>(tokens);
+  a.width = static_cast<int>(width);
+  a.heads = static_cast<int>(heads);
+  a.dim = static_cast<int>(dim);
+  a.causal = 1;
+  a.seq = 0;
+  a.scale = 1.0f / std::sqrt(static_cast<float>(dim));
+  a.out = out_dev;
+  a.ld_out = static_cast<long long>(width);
+  a.status = ctx->status_dev;
+  AttnMaps maps;
+  const bool tma = attention_tma_ok(keys_dev, values_dev, static_cast<long long>(tokens),
+                                    a.width, a.dim, a.cap) &&
+                   attention_tma_maps(&maps, keys_dev, values_dev, static_cast<long long>(tokens),
+                                      a.width);
+  const int rows = static_cast<int>(tokens);
+  cudaError_t e = tma ? launch_attention_decode_tma(maps, a, rows, ctx->stream)
+                      : launch_attention_decode(a, rows, rows, ctx->stream);
   if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
   return ok();
 }
@@ -1680,6 +1741,62 @@ int uocr_kv_attention(uocr_ctx* ctx, const uocr_kv* kv, const float* q_dev, floa
                           : launch_attention_decode(a, kv->batch, static_cast<int>(kv->cap),
                                                     ctx->stream);
   if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
+  return ok();
+}
+
+// The prefill branch of Decoder::layer (src/decoder/mod.rs:313-338) on the
+// cache: right after uocr_kv_prefill of `rows` tokens, query row i of q
+// ([rows x width], position i) attends to the sequence's tokens 0..i.
+int uocr_kv_attention_prefill(uocr_ctx* ctx, const uocr_kv* kv, size_t seq, const float* q_dev,
+                              size_t rows, float* out_dev) {
+  if (!ctx || !kv) return fail(UOCR_ERR_INVALID, "null argument");
+  if (seq >= static_cast<size_t>(kv->batch)) return fail(UOCR_ERR_SHAPE, "invalid tensor shape: cache sequence");
+  if (rows == 0 || static_cast<size_t>(kv->prefix[seq]) != rows)
+    return fail(UOCR_ERR_SHAPE, "invalid tensor shape: prefill attention needs the prefilled rows");
+  int st = check_elements(ctx, static_cast<size_t>(kv->head_dim) * rows +
+                                   rows * static_cast<size_t>(kv->width) + rows);
+  if (st) return st;
+  if (!q_dev || !out_dev) return fail(UOCR_ERR_INVALID, "null argument");
+  if (rows > 65535 || attention_smem_bytes(kv->head_dim, static_cast<int>(kv->cap)) > kAttnMaxSmem)
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: prefill attention over %zu tokens",
+                rows);
+  DeviceGuard g(ctx->device);
+  AttnArgs a{};
+  a.q = q_dev;
+  a.ld_q = kv->width;
+  a.keys = kv->keys;
+  a.values = kv->values;
+  a.head_stride = kv->cap * kv->head_dim;
+  a.seq_stride = a.head_stride * kv->heads;
+  a.row_stride = kv->head_dim;
+  a.cap = kv->cap;
+  a.tiled = kv->layout.tiled;
+  a.width = kv->width;
+  a.heads = kv->heads;
+  a.dim = kv->head_dim;
+  a.causal = 1;
+  a.seq = static_cast<int>(seq);
+  a.scale = 1.0f / std::sqrt(static_cast<float>(kv->head_dim));
+  a.out = out_dev;
+  a.ld_out = kv->width;
+  a.status = ctx->status_dev;
+  const int n = static_cast<int>(rows);
+  cudaError_t e = kv->tma ? launch_attention_decode_tma(kv->maps, a, n, ctx->stream)
+                          : launch_attention_decode(a, n, static_cast<int>(kv->cap), ctx->stream);
+  if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
+  return ok();
+}
+
+// LayerCache::new (src/decoder/cache.rs:14-31) again for sequence `seq`:
+// empty, to be prefilled anew (the reference's prefill makes new caches).
+int uocr_kv_reset(uocr_ctx* ctx, uocr_kv* kv, size_t seq) {
+  if (!ctx || !kv) return fail(UOCR_ERR_INVALID, "null argument");
+  if (seq >= static_cast<size_t>(kv->batch)) return fail(UOCR_ERR_SHAPE, "invalid tensor shape: cache sequence");
+  DeviceGuard g(ctx->device);
+  launch_kv_set_prefix(kv->state, static_cast<int>(seq), 0, ctx->stream);
+  int st = check_launch();
+  if (st) return st;
+  kv->prefix[seq] = 0;
   return ok();
 }
 

@@ -100,6 +100,9 @@ cudaError_t launch_linear_bf16(const uint16_t* w, int n, int k, const float* x, 
                                unsigned* status, cudaStream_t st);
 // h = silu(g) * u elementwise (n floats; h may alias g)
 void launch_swiglu(const float* g, const float* u, long long n, float* h, int sms, cudaStream_t st);
+// acc += the bit patterns of x[0..n) as u64 (the benchmark's logits checksum).
+void launch_bits_checksum(const float* x, long long n, unsigned long long* acc, int sms,
+                          cudaStream_t st);
 // hq/hs = block-quantized silu(g) * u
 void launch_swiglu_quantize(const float* g, const float* u, int rows, int cols, int8_t* hq,
                             float* hs, unsigned* status, int sms, cudaStream_t st,
@@ -292,6 +295,10 @@ struct AttnArgs {
   int width, heads, dim;
   int tokens;          // tokens per sequence when state is null
   const int* state;    // {prefix, generated} per sequence, or null
+  // Causal prefill (ops::attention with its mask): the queries are rows
+  // 0..batch-1 of the one sequence `seq`, query b at position b over tokens
+  // 0..b of that sequence (state and tokens unused).
+  int causal, seq;
   int window;
   float scale;         // 1 / sqrt(dim), as the reference rounds it
   float* out;          // [batch][ld_out]

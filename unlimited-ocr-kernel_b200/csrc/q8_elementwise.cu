@@ -268,4 +268,27 @@ cudaError_t launch_linear_bf16(const uint16_t* w, int n, int k, const float* x, 
   return cudaGetLastError();
 }
 
+// ---- logits checksum -----------------------------------------------------------
+// The fixed-work benchmark consumes every logit of every step by adding its
+// bit pattern to a u64 (src/model/benchmark.rs:43-47, wrapping_add): sums
+// modulo 2^64 do not depend on the order, so a parallel reduction is exact.
+__global__ void bits_checksum_kernel(const uint32_t* __restrict__ x, long long n,
+                                     unsigned long long* acc) {
+  unsigned long long s = 0;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n; i += stride)
+    s += x[i];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_down_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0 && s) atomicAdd(acc, s);
+}
+
+void launch_bits_checksum(const float* x, long long n, unsigned long long* acc, int sms,
+                          cudaStream_t st) {
+  if (n <= 0) return;
+  const long long want = (n + 255) / 256;
+  const int grid = static_cast<int>(want < 2LL * sms ? want : 2LL * sms);
+  bits_checksum_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const uint32_t*>(x), n, acc);
+}
+
 }  // namespace uocr

@@ -88,6 +88,10 @@ SIGNATURES = {
     "uocr_kv_push": (I, [P, P, P, P]),
     "uocr_kv_rope": (I, [P, P, P, P, P]),
     "uocr_kv_attention": (I, [P, P, P, P]),
+    "uocr_kv_attention_prefill": (I, [P, P, S, P, S, P]),
+    "uocr_kv_reset": (I, [P, P, S]),
+    "uocr_bits_checksum": (I, [P, P, S, P]),
+    "uocr_attention_prefill": (I, [P, P, P, P, S, S, S, P]),
     "uocr_kv_rope_push_qkv": (I, [P, P, P, P, P]),
     "uocr_kv_state": (I, [P, P, S, ctypes.POINTER(S), ctypes.POINTER(S)]),
     "uocr_kv_export": (I, [P, P, S, P, P, ctypes.POINTER(S)]),

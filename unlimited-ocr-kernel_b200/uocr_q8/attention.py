@@ -58,6 +58,17 @@ def attention_decode_device(ctx: GpuContext, q_t, keys_t, values_t, heads: int, 
     return out_t
 
 
+def attention_prefill_device(ctx: GpuContext, q_t, keys_t, values_t, heads: int, out_t=None):
+    """Causal attention of a prefill: token-major q/keys/values [tokens x
+    width], row i over tokens 0..i (uocr_attention_prefill)."""
+    import torch
+    tokens, width = q_t.shape
+    out_t = out_t if out_t is not None else torch.empty_like(q_t)
+    _check(lib().uocr_attention_prefill(ctx.handle, _p(q_t), _p(keys_t), _p(values_t), tokens,
+                                        width, heads, _p(out_t)))
+    return out_t
+
+
 class Rope:
     """cos/sin table of positions [0, max_positions) (device)."""
 
@@ -126,6 +137,19 @@ class KvCache:
         import torch
         out_t = out_t if out_t is not None else torch.empty_like(q_t)
         _check(lib().uocr_kv_attention(self.ctx.handle, self._h, _p(q_t), _p(out_t)))
+        return out_t
+
+    def reset(self, seq: int):
+        """Sequence seq empty again, to be prefilled anew (uocr_kv_reset)."""
+        _check(lib().uocr_kv_reset(self.ctx.handle, self._h, seq))
+
+    def attention_prefill(self, seq: int, q_t, out_t=None):
+        """Causal attention of the prefill rows of sequence seq, right after
+        their prefill (uocr_kv_attention_prefill)."""
+        import torch
+        out_t = out_t if out_t is not None else torch.empty_like(q_t)
+        _check(lib().uocr_kv_attention_prefill(self.ctx.handle, self._h, seq, _p(q_t),
+                                               q_t.numel() // self.width, _p(out_t)))
         return out_t
 
     def state(self, seq: int):

@@ -1,4 +1,4 @@
-"""A batched decode step of the decoder on one GPU.
+"""The decoder on one GPU: prefill of a sequence and a batched decode step.
 
 Decoder::step (src/decoder/mod.rs:400-420) for `batch` independent sequences
 at once: embedding lookup (BF16 table), then per layer Decoder::layer
@@ -193,9 +193,15 @@ class DecodeState:
     def __init__(self, decoder: Decoder, batch: int, max_prefix: int):
         cfg = decoder.cfg
         self.batch = batch
+        self.max_prefix = max_prefix
         self.caches = [KvCache(decoder.ctx, batch, cfg.heads, cfg.head_dim, cfg.window, max_prefix)
                        for _ in range(cfg.layers)]
         self.rope = Rope(decoder.ctx, cfg.head_dim, cfg.theta, cfg.max_positions)
+
+    def reset(self, seq: int = 0):
+        """Every layer's cache of sequence seq empty again (a new prefill)."""
+        for c in self.caches:
+            c.reset(seq)
 
     def free(self):
         for c in self.caches:
@@ -236,6 +242,62 @@ def decode_step(decoder: Decoder, state: DecodeState, tokens_t, mode: int = 0, l
         return decoder.lm_head.linear_device(h, logits_t, dynamic=rowwise)
     # BF16 head: the tensor-core BF16 linear straight from the bf16 weights
     return linear_bf16_tc_device(ctx, decoder.lm_head, h, logits_t)
+
+
+def prefill(decoder: Decoder, state: DecodeState, embeddings_t, mode: int = 0, seq: int = 0,
+            logits_t=None):
+    """Decoder::prefill (src/decoder/mod.rs:382-398) of sequence `seq` of the
+    state: embeddings_t [tokens x hidden] (FP32, device) through every layer
+    at positions 0..tokens-1 — Decoder::layer with position 0
+    (:241-367): RMSNorm, q/k/v projections, rope of every row at its
+    position, LayerCache::prefill, the causal attention over the prefix, o
+    projection, residual, RMSNorm, the dense FFN or the MoE over all rows,
+    residual — then Decoder::logits (:369-380) of the last row.  Projections
+    follow Decoder::projection: int8 activations only for one-row inputs in
+    DynamicActivations (so a prefill of several rows runs its projections
+    with FP32 activations, and an expert that receives one row runs it with
+    int8 activations), every row in the row-wise mode.  Returns the logits
+    [1 x vocab] (device, asynchronous)."""
+    import torch
+    ctx, cfg = decoder.ctx, decoder.cfg
+    H = cfg.hidden
+    x = embeddings_t.reshape(-1, H).float().clone()
+    T = x.shape[0]
+    if T > state.max_prefix:
+        raise ValueError("prefill longer than the state's prefix capacity")
+    dyn = mode == QuantizationMode.DYNAMIC_ROWWISE or (
+        mode == QuantizationMode.DYNAMIC_ACTIVATIONS and T == 1)
+    positions = torch.arange(T, dtype=torch.int32, device=x.device)
+    y = None
+    for layer, cache in zip(decoder.layers, state.caches):
+        if y is None:
+            n = rms_norm_device(ctx, x, layer.input_norm, cfg.eps)
+        else:
+            n = add_rms_norm_device(ctx, x, y, layer.input_norm, cfg.eps, sum_t=x)
+        qkv = layer.qkv.linear_device(n, dynamic=dyn)
+        q, k, v = (qkv[:, i * H:(i + 1) * H].contiguous() for i in range(3))
+        state.rope.apply(q, k, positions)
+        cache.prefill(seq, k, v)
+        a = cache.attention_prefill(seq, q)
+        r = layer.o.linear_device(a, dynamic=dyn)
+        n = add_rms_norm_device(ctx, r, x, layer.post_norm, cfg.eps, sum_t=r)  # r += x
+        if layer.moe is not None:
+            logits = linear_bf16_device(ctx, layer.router, n)
+            y = layer.moe.forward_device(n, logits, mode)
+        else:
+            y = feed_forward_device(ctx, *layer.dense, n, mode)
+        x = r
+    h = add_rms_norm_device(ctx, x[T - 1:], y[T - 1:], decoder.final_norm, cfg.eps)
+    if isinstance(decoder.lm_head, Int8Matrix):
+        return decoder.lm_head.linear_device(
+            h, logits_t, dynamic=mode != QuantizationMode.WEIGHTS_ONLY)
+    return linear_bf16_tc_device(ctx, decoder.lm_head, h, logits_t)
+
+
+def logits_checksum_device(ctx: GpuContext, logits_t, acc_t):
+    """acc_t (int64 [1], device) += the bit patterns of logits_t as u64,
+    wrapping (the fixed-work benchmark's checksum, uocr_bits_checksum)."""
+    _check(lib().uocr_bits_checksum(ctx.handle, _p(logits_t), logits_t.numel(), _p(acc_t)))
 
 
 # ---- loading a checkpoint with its INT8 overlay -------------------------------
