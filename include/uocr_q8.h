@@ -448,6 +448,12 @@ int uocr_kv_create(uocr_ctx *ctx, size_t batch, size_t heads, size_t head_dim, s
                    size_t max_prefix, uocr_kv **out);
 int uocr_kv_free(uocr_kv *kv);
 int uocr_kv_reset(uocr_ctx *ctx, uocr_kv *kv, size_t seq);
+/* The form uocr_kv_attention runs: 0 (default) chooses by size, 1 one CTA per
+ * (head, sequence), 2 split over tokens (a scores kernel over token chunks,
+ * then per head-dimension slice the softmax and value sums; caches whose
+ * head_dim is a multiple of 32 only, else Unsupported).  Every form gives
+ * the same bits; the choice only moves time. */
+int uocr_kv_set_attention_form(uocr_kv *kv, int form);
 int uocr_kv_prefill(uocr_ctx *ctx, uocr_kv *kv, size_t seq, const float *keys_dev,
                     const float *values_dev, size_t tokens);
 int uocr_kv_push(uocr_ctx *ctx, uocr_kv *kv, const float *k_dev, const float *v_dev);

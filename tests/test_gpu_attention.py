@@ -287,6 +287,53 @@ def test_cache_errors(ctx):
     kv.free()
 
 
+@pytest.mark.parametrize("batch,heads,dim,prefix", [(1, 10, 128, 1517), (3, 2, 64, 100),
+                                                     (2, 1, 256, 33), (5, 10, 128, 300)])
+def test_split_attention_equals_one_cta_per_head(ctx, batch, heads, dim, prefix):
+    """The split form (scores over token chunks, then softmax and value sums
+    per 32-column slice) gives the one-CTA-per-head kernel's bits, across
+    ragged prefixes and ring wraps, and matches the oracle."""
+    import torch
+    rng = np.random.default_rng(prefix + batch)
+    width = heads * dim
+    kv = A().KvCache(ctx, batch, heads, dim, 8, max_prefix=prefix)
+    for b in range(batch):
+        n = prefix - b
+        kv.prefill(b, dev(rng.standard_normal((n, width)).astype(np.float32)),
+                   dev(rng.standard_normal((n, width)).astype(np.float32)))
+    for _ in range(11):  # the 8-token ring wraps
+        kv.push(dev(rng.standard_normal((batch, width)).astype(np.float32)),
+                dev(rng.standard_normal((batch, width)).astype(np.float32)))
+    q = dev((rng.standard_normal((batch, width)) * 0.2).astype(np.float32))
+    kv.set_attention_form(1)
+    one = host(kv.attention(q))
+    kv.set_attention_form(2)
+    split = host(kv.attention(q))
+    kv.set_attention_form(0)
+    auto = host(kv.attention(q))
+    ctx.sync()
+    assert bits_equal(split, one)
+    assert bits_equal(auto, one)
+    for b in range(batch):
+        k, v = (host(t) for t in kv.export(b))
+        ref = oracle.attention_decode(host(q)[b], k, v, heads)
+        assert np.max(np.abs(split[b] - ref)) <= 1e-5 * max(1.0, float(np.max(np.abs(ref))))
+    bad = q.clone()
+    bad[0, 0] = float("nan")
+    kv.set_attention_form(2)
+    kv.attention(bad)
+    import uocr_q8
+    with pytest.raises(uocr_q8.OcrError) as e:
+        ctx.sync()
+    assert e.value.kind == "Numerical"
+    kv.free()
+    small = A().KvCache(ctx, 1, 2, 8, 4, max_prefix=4)  # head_dim 8: no split form
+    with pytest.raises(uocr_q8.OcrError) as e:
+        small.set_attention_form(2)
+    assert e.value.kind == "Unsupported"
+    small.free()
+
+
 # ---------------------------------------------------------------- prefill attention
 def _token_major(a):
     """[heads, tokens, dim] -> token-major [tokens, heads * dim]."""

@@ -745,4 +745,267 @@ cudaError_t launch_attention_decode_tma(const AttnMaps& m, const AttnArgs& a, in
   return cudaGetLastError();
 }
 
+// ---- single-query attention, split over tokens (few sequences) -------------------
+// With one CTA per (head, sequence) a small batch leaves most SMs idle and
+// each CTA is bound by its own latency (one sequential stream of its head's
+// keys and values).  This form splits the work without changing a single
+// rounding:
+//  * scores kernel, grid (chunks of 128 tokens, heads, batch): thread = token,
+//    the left-to-right dot from -0.0 over the head dimension, times the
+//    scale, into scratch [batch][heads][cap];
+//  * values kernel, grid (head_dim / 32 column slices, heads, batch), launched
+//    as a programmatic dependent of the scores kernel: its producer warp
+//    starts streaming the slice's value sub-blocks (32 tokens x 32 floats,
+//    4 KB contiguous in the tiled cache) through a bulk-copy ring at once;
+//    three warps wait for the scores, take the max, the exps, the
+//    left-to-right sum (one thread) and the divisions; then lane c of warp 0
+//    runs column c's left-to-right sum over the tokens from +0.0 out of the
+//    ring.
+constexpr int kSplitChunk = 128;
+constexpr int kSplitStages = 16;
+constexpr int kSplitThreads = 128;  // warps 0-2 softmax (warp 0 the sums), warp 3 producer
+constexpr int kSplitSubBytes = 32 * 32 * 4;
+
+__device__ __forceinline__ int split_tokens(const AttnArgs& a, int b, bool* ok) {
+  *ok = true;
+  if (!a.state) return a.tokens;
+  const int prefix = a.state[2 * b], gen = a.state[2 * b + 1];
+  if (prefix <= 0) {
+    *ok = false;
+    return 0;
+  }
+  return prefix + (gen < a.window ? gen : a.window);
+}
+
+__global__ void __launch_bounds__(kSplitChunk) attn_split_scores_kernel(const AttnArgs a) {
+  __shared__ __align__(16) float qs[256];
+  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  pdl_launch_dependents();  // the values kernel waits for this grid before reading scores
+  bool ok;
+  const int T = split_tokens(a, b, &ok);
+  if (!ok) {
+    if (c == 0 && threadIdx.x == 0) flag(a.status, DEV_CACHE);
+    return;
+  }
+  const int t0 = c * kSplitChunk;
+  if (t0 >= T) return;
+  const int dim = a.dim, nb = dim >> 5;
+  for (int d = threadIdx.x; d < dim; d += kSplitChunk)
+    qs[d] = a.q[b * a.ld_q + static_cast<long long>(h) * dim + d];
+  __syncthreads();
+  const int t = t0 + threadIdx.x;
+  if (t >= T) return;
+  const float* kh = a.keys + b * a.seq_stride + h * a.head_stride;
+  const float4* q4 = reinterpret_cast<const float4*>(qs);
+  float acc = -0.0f;
+  // four 32-float pieces of the key row per round, all loads issued before
+  // the chain of adds that consumes them
+  for (int j0 = 0; j0 < nb; j0 += 4) {
+    float4 kr[32];
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      const int j = j0 + jj;
+      if (j < nb) {
+        const float* row = a.tiled
+                               ? kh + ((static_cast<long long>(t >> 5) * nb + j) * 32 + (t & 31)) * 32
+                               : kh + t * a.row_stride + 32 * j;
+        const float4* k4 = reinterpret_cast<const float4*>(row);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) kr[jj * 8 + i] = __ldg(k4 + i);
+      }
+    }
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      if (j0 + jj < nb) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 kv = kr[jj * 8 + i];
+          const float4 qv = q4[(j0 + jj) * 8 + i];
+          acc = __fadd_rn(acc, __fmul_rn(qv.x, kv.x));
+          acc = __fadd_rn(acc, __fmul_rn(qv.y, kv.y));
+          acc = __fadd_rn(acc, __fmul_rn(qv.z, kv.z));
+          acc = __fadd_rn(acc, __fmul_rn(qv.w, kv.w));
+        }
+      }
+    }
+  }
+  a.scores[(static_cast<long long>(b) * a.heads + h) * a.cap + t] = __fmul_rn(acc, a.scale);
+}
+
+__device__ __forceinline__ void softmax_bar() {  // warps 0-2 only
+  asm volatile("bar.sync 1, 96;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kSplitThreads) attn_split_values_kernel(const AttnArgs a) {
+  extern __shared__ __align__(128) unsigned char split_raw[];
+  float* ring = reinterpret_cast<float*>(split_raw);  // kSplitStages x 32 x 32
+  float* sc = ring + kSplitStages * 1024;              // cap floats
+  uint64_t* full = reinterpret_cast<uint64_t*>(
+      (reinterpret_cast<uintptr_t>(sc + a.cap) + 15) & ~static_cast<uintptr_t>(15));
+  uint64_t* empty = full + kSplitStages;
+  __shared__ float red[3];
+  __shared__ int red_bad[3];
+  __shared__ float s_max, s_sum;
+  __shared__ int s_bad;
+  const int j = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = a.dim >> 5;
+  bool ok;
+  const int T = split_tokens(a, b, &ok);
+  if (!ok) return;  // flagged by the scores kernel
+  const int ntiles = (T + 31) >> 5;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kSplitStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (warp == 3) {
+    // ---- producer: the slice's sub-blocks in token order (written by the
+    // cache kernels before the scores kernel, so readable before its end)
+    if (lane == 0) {
+      const float* vh = a.values + b * a.seq_stride + h * a.head_stride;
+      int it = 0;
+      for (; it < ntiles; ++it) {
+        const int st = it % kSplitStages;
+        if (it >= kSplitStages &&
+            !mbar_wait(&empty[st], ((it / kSplitStages) - 1) & 1, a.status))
+          break;
+        mbar_arrive_expect_tx(&full[st], kSplitSubBytes);
+        bulk_g2s(ring + st * 1024, vh + (static_cast<long long>(it) * nb + j) * 1024,
+                 kSplitSubBytes, &full[st]);
+      }
+      for (int i = it - kSplitStages; i < it; ++i)  // every issued copy lands before exit
+        if (i >= 0) mbar_wait(&full[i % kSplitStages], (i / kSplitStages) & 1, a.status);
+    }
+    return;
+  }
+  // ---- softmax_backend (src/cpu/ops.rs:139-187) over the scores
+  pdl_wait_prior_grids();
+  // the scores row (16-byte aligned: cap is a multiple of 32), four 16-byte
+  // loads in flight per thread
+  const float4* src4 =
+      reinterpret_cast<const float4*>(a.scores + (static_cast<long long>(b) * a.heads + h) * a.cap);
+  float4* sc4 = reinterpret_cast<float4*>(sc);
+  const int n4 = (T + 3) >> 2;
+  float mx = -INFINITY;
+  int bad = 0;
+  for (int g0 = threadIdx.x; g0 < n4; g0 += 4 * 96) {
+    float4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (g0 + u * 96 < n4) v[u] = __ldcg(src4 + g0 + u * 96);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int g = g0 + u * 96;
+      if (g < n4) {
+        sc4[g] = v[u];
+        const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if (4 * g + c < T) {
+            bad |= isnan(e[c]) || e[c] == INFINITY;
+            mx = fmaxf(mx, e[c]);
+          }
+      }
+    }
+  }
+  mx = warp_max(mx);
+  bad = __any_sync(0xffffffffu, bad);
+  if (lane == 0) {
+    red[warp] = mx;
+    red_bad[warp] = bad;
+  }
+  softmax_bar();
+  if (threadIdx.x == 0) {
+    const float m = fmaxf(fmaxf(red[0], red[1]), red[2]);
+    s_max = m;
+    s_bad = red_bad[0] | red_bad[1] | red_bad[2] | !isfinite(m);
+  }
+  softmax_bar();
+  bad = s_bad;
+  if (!bad) {
+    mx = s_max;
+#pragma unroll 4
+    for (int t = threadIdx.x; t < T; t += 96) sc[t] = exp_f32_via_f64(__fsub_rn(sc[t], mx));
+    softmax_bar();
+    if (threadIdx.x == 0) s_sum = serial_sum_smem(sc, T);
+    softmax_bar();
+    const float sum = s_sum;
+#pragma unroll 4
+    for (int t = threadIdx.x; t < T; t += 96) sc[t] = __fdiv_rn(sc[t], sum);
+    softmax_bar();
+  } else if (threadIdx.x == 0 && j == 0) {
+    flag(a.status, DEV_SOFTMAX);
+  }
+  if (warp != 0) return;
+  // ---- column sums: lane = column 32 j + lane, tokens in order from +0.0;
+  // every tile is consumed (and its slot released) even after an error, so
+  // that the producer never waits for a slot that is not coming
+  float acc = 0.0f;
+  for (int i = 0; i < ntiles; ++i) {
+    const int st = i % kSplitStages;
+    mbar_wait(&full[st], (i / kSplitStages) & 1, a.status);
+    if (!bad) {
+      const float* tile = ring + st * 1024 + lane;
+      const float* p = sc + i * 32;
+      const int rows = T - i * 32 < 32 ? T - i * 32 : 32;
+      if (rows == 32) {
+#pragma unroll
+        for (int r = 0; r < 32; ++r) acc = __fadd_rn(acc, __fmul_rn(p[r], tile[r * 32]));
+      } else {
+        for (int r = 0; r < rows; ++r) acc = __fadd_rn(acc, __fmul_rn(p[r], tile[r * 32]));
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+  }
+  if (!bad) a.out[b * a.ld_out + static_cast<long long>(h) * a.dim + 32 * j + lane] = acc;
+}
+
+static size_t split_smem(long long cap) {
+  return static_cast<size_t>(kSplitStages) * kSplitSubBytes +
+         ((static_cast<size_t>(cap) * 4 + 15) & ~static_cast<size_t>(15)) +
+         2 * kSplitStages * sizeof(uint64_t) + 16;
+}
+
+bool attention_split_ok(const AttnArgs& a) {
+  return a.tiled && !a.causal && a.scores && a.dim % 32 == 0 && a.dim <= 256 &&
+         split_smem(a.cap) <= kAttnMaxSmem;
+}
+
+cudaError_t launch_attention_split(const AttnArgs& a, int batch, int max_tokens, cudaStream_t st) {
+  if (!attention_split_ok(a) || batch <= 0 || a.heads <= 0 || max_tokens <= 0 || batch > 65535 ||
+      a.heads > 65535)
+    return cudaErrorInvalidValue;
+  static PerDeviceOnce configured;
+  configured.run([] {
+    cudaFuncSetAttribute(attn_split_values_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(kAttnMaxSmem));
+  });
+  const int chunks = (max_tokens + kSplitChunk - 1) / kSplitChunk;
+  attn_split_scores_kernel<<<dim3(chunks, a.heads, batch), kSplitChunk, 0, st>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(a.dim / 32, a.heads, batch);
+  cfg.blockDim = dim3(kSplitThreads);
+  cfg.dynamicSmemBytes = split_smem(a.cap);
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, attn_split_values_kernel, a);
+  if (e != cudaSuccess) {  // without the early start
+    cudaGetLastError();
+    cfg.numAttrs = 0;
+    e = cudaLaunchKernelEx(&cfg, attn_split_values_kernel, a);
+  }
+  return e;
+}
+
 }  // namespace uocr

@@ -1607,6 +1607,7 @@ int uocr_kv_create(uocr_ctx* ctx, size_t batch, size_t heads, size_t head_dim, s
   if (e == cudaSuccess) e = cudaMalloc(&kv->values, bytes);
   if (e == cudaSuccess) e = cudaMalloc(&kv->state, batch * 2 * sizeof(int));
   if (e == cudaSuccess) e = cudaMemsetAsync(kv->state, 0, batch * 2 * sizeof(int), ctx->stream);
+  if (e == cudaSuccess && tiled) e = cudaMalloc(&kv->scores, rows * heads * sizeof(float));
   if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
   if (e != cudaSuccess) {
     uocr_kv_free(kv);
@@ -1630,7 +1631,18 @@ int uocr_kv_free(uocr_kv* kv) {
   if (kv->keys) cudaFree(kv->keys);
   if (kv->values) cudaFree(kv->values);
   if (kv->state) cudaFree(kv->state);
+  if (kv->scores) cudaFree(kv->scores);
   delete kv;
+  return ok();
+}
+
+// Attention form of uocr_kv_attention: 0 chooses by batch size, 1 one CTA per
+// (head, sequence), 2 split over tokens (tiled caches only).  Same results.
+int uocr_kv_set_attention_form(uocr_kv* kv, int form) {
+  if (!kv) return fail(UOCR_ERR_INVALID, "null argument");
+  if (form < 0 || form > 2 || (form == 2 && !kv->scores))
+    return fail(UOCR_ERR_UNSUPPORTED, "unsupported configuration: attention form");
+  kv->split = form;
   return ok();
 }
 
@@ -1737,9 +1749,16 @@ int uocr_kv_attention(uocr_ctx* ctx, const uocr_kv* kv, const float* q_dev, floa
   a.out = out_dev;
   a.ld_out = kv->width;
   a.status = ctx->status_dev;
-  cudaError_t e = kv->tma ? launch_attention_decode_tma(kv->maps, a, kv->batch, ctx->stream)
-                          : launch_attention_decode(a, kv->batch, static_cast<int>(kv->cap),
-                                                    ctx->stream);
+  a.scores = kv->scores;
+  // few CTAs with one per (head, sequence): each would stream its head alone,
+  // latency-bound; the split form spreads every head over many CTAs
+  const bool split = attention_split_ok(a) &&
+                     (kv->split == 2 ||
+                      (kv->split == 0 && static_cast<long long>(kv->batch) * kv->heads <= ctx->sms));
+  cudaError_t e = split     ? launch_attention_split(a, kv->batch, static_cast<int>(kv->cap), ctx->stream)
+                  : kv->tma ? launch_attention_decode_tma(kv->maps, a, kv->batch, ctx->stream)
+                            : launch_attention_decode(a, kv->batch, static_cast<int>(kv->cap),
+                                                      ctx->stream);
   if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
   return ok();
 }

@@ -97,4 +97,6 @@ struct uocr_kv {
   std::vector<int> prefix;  // host mirror (0: not prefilled)
   bool tma = false;         // maps valid: the TMA attention kernel applies
   uocr::AttnMaps maps{};
+  float* scores = nullptr;  // split attention scratch [batch][heads][cap] (tiled layout)
+  int split = 0;            // attention form: 0 by batch size, 1 one CTA per head, 2 split
 };

@@ -299,6 +299,8 @@ struct AttnArgs {
   // 0..batch-1 of the one sequence `seq`, query b at position b over tokens
   // 0..b of that sequence (state and tokens unused).
   int causal, seq;
+  // Split form (launch_attention_split): scores scratch [batch][heads][cap].
+  float* scores;
   int window;
   float scale;         // 1 / sqrt(dim), as the reference rounds it
   float* out;          // [batch][ld_out]
@@ -323,6 +325,13 @@ bool attention_tma_maps(AttnMaps* m, const float* keys, const float* values, lon
 // Maps of a tiled cache (elements floats per array): box = one 32-slot tile.
 bool attention_tma_maps_tiled(AttnMaps* m, const float* keys, const float* values,
                               long long elements, int dim);
+// Split form for few sequences (decode, tiled cache, dim % 32 == 0): a scores
+// kernel over 128-token chunks, then one kernel per (32-column slice, head,
+// sequence) for the softmax and the value sums; the same arithmetic as the
+// one-CTA-per-head kernels, so the same bits.  max_tokens bounds every
+// sequence's token count (the scratch row length).
+bool attention_split_ok(const AttnArgs& a);
+cudaError_t launch_attention_split(const AttnArgs& a, int batch, int max_tokens, cudaStream_t st);
 cudaError_t launch_attention_decode_tma(const AttnMaps& m, const AttnArgs& a, int batch,
                                         cudaStream_t st);
 // rope_table.cpp — host: the reference's cos/sin of every (position, pair).

@@ -90,6 +90,7 @@ SIGNATURES = {
     "uocr_kv_attention": (I, [P, P, P, P]),
     "uocr_kv_attention_prefill": (I, [P, P, S, P, S, P]),
     "uocr_kv_reset": (I, [P, P, S]),
+    "uocr_kv_set_attention_form": (I, [P, I]),
     "uocr_bits_checksum": (I, [P, P, S, P]),
     "uocr_attention_prefill": (I, [P, P, P, P, S, S, S, P]),
     "uocr_kv_rope_push_qkv": (I, [P, P, P, P, P]),

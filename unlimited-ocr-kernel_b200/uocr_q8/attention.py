@@ -139,6 +139,11 @@ class KvCache:
         _check(lib().uocr_kv_attention(self.ctx.handle, self._h, _p(q_t), _p(out_t)))
         return out_t
 
+    def set_attention_form(self, form: int):
+        """0 by size, 1 one CTA per (head, sequence), 2 split over tokens
+        (uocr_kv_set_attention_form); the same results either way."""
+        _check(lib().uocr_kv_set_attention_form(self._h, int(form)))
+
     def reset(self, seq: int):
         """Sequence seq empty again, to be prefilled anew (uocr_kv_reset)."""
         _check(lib().uocr_kv_reset(self.ctx.handle, self._h, seq))
