@@ -1265,8 +1265,12 @@ def run_fixed_work(args):
 
     with torch.cuda.stream(stream):  # warm-up: sizes every workspace
         begin()
-        for _ in range(3):
+        for i in range(3):
+            if i == 2:  # one eager step in an NVTX range, for a profiler's launch list
+                torch.cuda.nvtx.range_push("fixed_work_step")
             step()
+            if i == 2:
+                torch.cuda.nvtx.range_pop()
     ctx.sync()
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
@@ -1468,9 +1472,14 @@ def run_ep_peer(args):
 
     if world > 1:
         dist.barrier()
+    n_warm = max(args.warmup, 3) + n_layers
     with torch.cuda.stream(stream):
-        for i in range(max(args.warmup, 3) + n_layers):
+        for i in range(n_warm):
+            if i == n_warm - 1:  # one eager forward in an NVTX range, for a profiler's launch list
+                torch.cuda.nvtx.range_push("ep_layer_forward")
             step(i)
+            if i == n_warm - 1:
+                torch.cuda.nvtx.range_pop()
     ctx.sync()
 
     # parity of one step of every rank against the single-GPU layer (all 64

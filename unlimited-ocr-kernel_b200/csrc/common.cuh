@@ -408,4 +408,45 @@ __device__ __forceinline__ int8_t quantize_elem(float v, float scale) {
   return static_cast<int8_t>(q);
 }
 
+// Block quantization of v[0, n) in shared memory (16-byte aligned) into q and
+// s (shared memory), the activation step of linear_dynamic_int8
+// (src/cpu/quantized.rs:43-74 applied at :169), by the `nt` threads
+// tid in [0, nt) of a named barrier `bar`.  Two short steps: one thread per
+// 32-element block takes the block's max |v| (the reference folds from 0
+// with f32::max, which ignores NaN like fmaxf; a max does not depend on the
+// order) and the scale max / 127; then every element is divided by its
+// block's scale on its own.  (One warp per block instead chains a block's
+// shuffles and two dependent divisions, block after block.)  Lane-rotated
+// 16-byte reads keep the per-block scans free of bank conflicts.
+__device__ __forceinline__ void quantize_blocks_smem(const float* v, int n, int8_t* q, float* s,
+                                                     int tid, int nt, int bar, unsigned* status) {
+  const int nb = blocks_of(n);
+  for (int b = tid; b < nb; b += nt) {
+    const int k0 = b * kBlock;
+    float mx = 0.0f;
+    bool bad = false;
+    if (k0 + kBlock <= n) {
+      const float4* v4 = reinterpret_cast<const float4*>(v + k0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 c = v4[(j + b) & 7];
+        bad |= !isfinite(c.x) || !isfinite(c.y) || !isfinite(c.z) || !isfinite(c.w);
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(c.x), fabsf(c.y)), fmaxf(fabsf(c.z), fabsf(c.w))));
+      }
+    } else {
+      for (int k = k0; k < n; ++k) {
+        bad |= !isfinite(v[k]);
+        mx = fmaxf(mx, fabsf(v[k]));
+      }
+    }
+    const float scale = __fdiv_rn(mx, 127.0f);
+    if (bad) flag(status, DEV_NONFINITE);
+    if (mx > 0.0f && scale == 0.0f) flag(status, DEV_UNDERFLOW);
+    s[b] = scale;
+  }
+  named_barrier(bar, nt);
+#pragma unroll 4
+  for (int k = tid; k < n; k += nt) q[k] = quantize_elem(v[k], s[k / kBlock]);
+}
+
 }  // namespace uocr

@@ -133,28 +133,6 @@ __device__ __forceinline__ bool grid_barrier(unsigned* sync, unsigned gen, unsig
   return true;
 }
 
-// Block quantization of a float vector in shared memory by `nw` warps
-// starting at warp `warp` (the activation step of linear_dynamic_int8).
-__device__ __forceinline__ void quantize_vec_smem(const float* v, int n, int8_t* q, float* s,
-                                                 int warp, int nw, unsigned* status) {
-  const int lane = threadIdx.x & 31;
-  const int nb = blocks_of(n);
-  for (int b = warp; b < nb; b += nw) {
-    const int k = b * kBlock + lane;
-    const bool in = k < n;
-    const float x = in ? v[k] : 0.0f;
-    const bool bad = in && !isfinite(x);
-    if (__any_sync(0xffffffffu, bad) && lane == 0) flag(status, DEV_NONFINITE);
-    const float mx = warp_max(in ? fabsf(x) : 0.0f);
-    const float scale = __fdiv_rn(mx, 127.0f);
-    if (lane == 0) {
-      if (mx > 0.0f && scale == 0.0f) flag(status, DEV_UNDERFLOW);
-      s[b] = scale;
-    }
-    if (in) q[k] = quantize_elem(x, scale);
-  }
-}
-
 // Sum of N row partials over the warp, N rows at once (transposed butterfly:
 // N/2 + N/4 + ... + 1 shuffles to split the rows over lane groups, then a
 // plain butterfly inside each group).  Afterwards every lane of group
@@ -422,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const __grid_co
   } else {
     for (int k = threadIdx.x; k < H; k += kConsumerThreads) xsm[k] = a.x[k];
     named_barrier(1, kConsumerThreads);
-    quantize_vec_smem(xsm, H, xq, xs, warp, kConsumerWarps, a.status);
+    quantize_blocks_smem(xsm, H, xq, xs, threadIdx.x, kConsumerThreads, 1, a.status);
     named_barrier(1, kConsumerThreads);
   }
   // ---- phase A: group g consumes this CTA's stages g, g+4, ...
@@ -503,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const __grid_co
   named_barrier(1, kConsumerThreads);
   if (MODE == MODE_INT8) {
     // unit boundaries are multiples of 32, so flat 32-blocks are unit blocks
-    quantize_vec_smem(hsm, hn, hq, hs, warp, kConsumerWarps, a.status);
+    quantize_blocks_smem(hsm, hn, hq, hs, threadIdx.x, kConsumerThreads, 1, a.status);
     named_barrier(1, kConsumerThreads);
   }
   const bool ready = nr > 0 && mbar_wait(down_bar, 0, a.status);

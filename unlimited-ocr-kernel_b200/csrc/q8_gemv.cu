@@ -103,30 +103,6 @@ struct GemvTmaParams {
 };
 
 
-// Block-quantize the CTA's copy of x (cols floats, smem) into xq/xs (smem),
-// the activation step of linear_dynamic_int8 (src/cpu/quantized.rs:169).
-// One warp per 32-column block, over warps [0, nw) of the CTA.
-__device__ __forceinline__ void quantize_x_smem(const float* xsm, int cols, int8_t* xq, float* xs,
-                                               int nw, unsigned* status) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int nb = blocks_of(cols);
-  for (int b = warp; b < nb; b += nw) {
-    const int k = b * kBlock + lane;
-    const bool in = k < cols;
-    const float v = in ? xsm[k] : 0.0f;
-    const bool bad = in && !isfinite(v);
-    if (__any_sync(0xffffffffu, bad) && lane == 0) flag(status, DEV_NONFINITE);
-    const float mx = warp_max(in ? fabsf(v) : 0.0f);
-    const float scale = __fdiv_rn(mx, 127.0f);
-    if (lane == 0) {
-      if (mx > 0.0f && scale == 0.0f) flag(status, DEV_UNDERFLOW);
-      xs[b] = scale;
-    }
-    if (in) xq[k] = quantize_elem(v, scale);
-  }
-}
-
-
 template <int MODE>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const __grid_constant__ GemvTmaParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -189,7 +165,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const __grid_
   } else {
     for (int k = threadIdx.x; k < cols; k += kConsumerThreads) xsm[k] = p.x[k];
     named_barrier(1, kConsumerThreads);
-    quantize_x_smem(xsm, cols, xq, xs, kGemvConsumerWarps, p.status);
+    quantize_blocks_smem(xsm, cols, xq, xs, threadIdx.x, kConsumerThreads, 1, p.status);
     named_barrier(1, kConsumerThreads);
   }
   const int group = warp / kGemvWarpsPerGroup, wg = warp % kGemvWarpsPerGroup;
