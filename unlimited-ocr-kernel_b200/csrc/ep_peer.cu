@@ -190,22 +190,39 @@ __global__ void __launch_bounds__(kRdWarps * 32) ep_route_dispatch_kernel(
   float* p = rd_smem + warp * (d.n_experts + 2 * k);
   int* sel = reinterpret_cast<int*>(p + d.n_experts);
   float* sw = p + d.n_experts + k;
+  __shared__ unsigned cta_cnt[kEpMaxWorld], cta_base[kEpMaxWorld];
   const unsigned step = d.ctr[kCtrStep] + 1u;
   const int h4 = d.hidden >> 2;
-  for (int t = blockIdx.x * kRdWarps + warp; t < tokens; t += gridDim.x * kRdWarps) {
-    const bool ok = route_row_warp(logits + static_cast<long long>(t) * d.n_experts, d.n_experts,
-                                   k, normalize, scale, p, sel, sw, d.status);
+  for (int r = threadIdx.x; r < d.world; r += blockDim.x) cta_cnt[r] = 0u;
+  __syncthreads();
+  // one token per warp (the grid covers the tokens); slots are claimed per
+  // CTA: shared-memory counts per owner, then one global reservation per
+  // (CTA, owner).  One global atomic per pair serialised 384 of them on one
+  // address at one GPU.  A block's slot order carries no meaning: each row's
+  // output depends on that row alone, and the combine orders by expert id.
+  const int t = blockIdx.x * kRdWarps + warp;
+  bool ok = false;
+  int e = 0, o = 0, local = 0;
+  if (t < tokens) {
+    ok = route_row_warp(logits + static_cast<long long>(t) * d.n_experts, d.n_experts, k,
+                        normalize, scale, p, sel, sw, d.status);
     for (int r = lane; r < k; r += 32) {
       ids[static_cast<long long>(t) * k + r] = ok ? sel[r] : -1;
       wts[static_cast<long long>(t) * k + r] = ok ? sw[r] : 0.0f;
     }
+    if (ok && lane < k) {
+      e = sel[lane];
+      o = d.owner_of[e];
+      local = static_cast<int>(atomicAdd(&cta_cnt[o], 1u));
+    }
+  }
+  __syncthreads();
+  for (int r = threadIdx.x; r < d.world; r += blockDim.x)
+    cta_base[r] = cta_cnt[r] ? atomicAdd(send_cnt + r, cta_cnt[r]) : 0u;
+  __syncthreads();
+  if (t < tokens) {
     if (ok) {
-      int e = 0, o = 0, slot = 0;
-      if (lane < k) {
-        e = sel[lane];
-        o = d.owner_of[e];
-        slot = static_cast<int>(atomicAdd(send_cnt + o, 1u));
-      }
+      const int slot = lane < k ? static_cast<int>(cta_base[o]) + local : 0;
       const float4* src = reinterpret_cast<const float4*>(x) + static_cast<long long>(t) * h4;
       for (int j = 0; j < k; ++j) {
         const int oj = __shfl_sync(0xffffffffu, o, j);
