@@ -432,6 +432,31 @@ def test_kv_prefill_attention_equals_token_major(ctx, heads, dim):
     kv.free()
 
 
+@pytest.mark.parametrize("heads,tokens", [(10, 1517), (2, 33), (3, 16), (1, 17)])
+def test_blocked_prefill_attention_equals_row_per_cta(ctx, heads, tokens):
+    """The 16-rows-per-CTA causal prefill (head_dim 128, the default form)
+    gives the one-row-per-CTA form's bits (forced with attention form 1),
+    including the last partial block of rows; sampled rows against the oracle."""
+    rng = np.random.default_rng(tokens + heads)
+    dim = 128
+    width = heads * dim
+    q, k, v = (rng.standard_normal((tokens, width)).astype(np.float32) for _ in range(3))
+    outs = []
+    for form in (0, 1):
+        kv = A().KvCache(ctx, 2, heads, dim, 8, max_prefix=tokens)
+        kv.prefill(0, dev(rng.standard_normal((3, width)).astype(np.float32)),
+                   dev(rng.standard_normal((3, width)).astype(np.float32)))
+        kv.prefill(1, dev(k), dev(v))
+        kv.set_attention_form(form)
+        outs.append(host(kv.attention_prefill(1, dev(q))))
+        ctx.sync()
+        kv.free()
+    assert bits_equal(outs[0], outs[1])
+    for i in sorted({0, 1, 15, 16, tokens // 2, tokens - 1} & set(range(tokens))):
+        ref = oracle.attention_decode(q[i], k[:i + 1], v[:i + 1], heads)
+        assert np.max(np.abs(outs[0][i] - ref)) <= 1e-5 * max(1.0, float(np.max(np.abs(ref)))), i
+
+
 def test_prefill_attention_errors(ctx):
     import torch
     import uocr_q8

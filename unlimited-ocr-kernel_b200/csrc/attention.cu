@@ -1008,4 +1008,184 @@ cudaError_t launch_attention_split(const AttnArgs& a, int batch, int max_tokens,
   return e;
 }
 
+// ---- causal attention of a prefill, 16 query rows per CTA (head_dim 128) ---------
+// ops::attention with its mask (src/cpu/ops.rs:263-360) over the tiled cache:
+// CTA = (head, 16 consecutive query rows), so that each 32-token key or value
+// tile crosses from L2 once per 16 rows instead of once per row.  A producer
+// warp streams the head's key tiles, then its value tiles (tokens 0 .. the
+// block's last row), through a four-slot TMA ring; warp q owns query row
+// i = i0 + q:
+//  * scores: lane = token of the tile, the left-to-right dot from -0.0 over
+//    the head dimension (products in pairs, each rounded on its own, added
+//    one by one), times the scale, for tokens 0..i only;
+//  * softmax over tokens 0..i: max, exps, lane 0's left-to-right sum, the
+//    divisions;
+//  * values: lane = four output columns, tokens 0..i in order from -0.0.
+// The same operations in the same order as the one-query-per-CTA causal form,
+// so the same bits.
+constexpr int kPfRows = 16;
+constexpr int kPfStages = 4;
+constexpr int kPfThreads = (kPfRows + 1) * 32;
+constexpr int kPfTileBytes = 4 * kTmaBoxBytes;  // 32 tokens x 128 floats
+
+__host__ __device__ inline size_t attn_prefill_smem(long long tokens) {
+  const size_t tpad = static_cast<size_t>((tokens + 3) & ~3LL);
+  return 1024 + kPfStages * kPfTileBytes + kPfRows * 128 * 4 + kPfRows * tpad * 4 +
+         2 * kPfStages * 8 + 16;
+}
+
+__global__ void __launch_bounds__(kPfThreads, 1)
+    attn_prefill_kernel(const __grid_constant__ CUtensorMap kmap,
+                        const __grid_constant__ CUtensorMap vmap, const AttnArgs a) {
+  extern __shared__ __align__(1024) unsigned char pf_raw[];
+  // offset from the shared array itself (not through an integer cast), so
+  // that every pointer below stays a shared-memory pointer to the compiler
+  unsigned char* ring = pf_raw + ((1024u - (smem_addr(pf_raw) & 1023u)) & 1023u);
+  const int T = a.tokens, tpad = (T + 3) & ~3;
+  float* qs = reinterpret_cast<float*>(ring + kPfStages * kPfTileBytes);  // [16][128]
+  float* sc_all = qs + kPfRows * 128;                                      // [16][tpad]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sc_all + kPfRows * tpad);
+  uint64_t* empty = full + kPfStages;
+  const int h = blockIdx.y;
+  const int i0 = static_cast<int>(gridDim.x - 1 - blockIdx.x) * kPfRows;  // longest first
+  const int last = min(i0 + kPfRows, T);  // rows [i0, last)
+  const int ntk = (last + 31) >> 5;       // key tiles 0 .. ntk-1 cover tokens 0 .. last-1
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kPfStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kPfRows);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (warp == kPfRows) {
+    // ---- producer: key tiles, then value tiles
+    if (lane == 0) {
+      const long long y0 = (static_cast<long long>(a.seq) * a.heads + h) * a.cap * 4;
+      int it = 0;
+      for (; it < 2 * ntk; ++it) {
+        const int st = it % kPfStages;
+        if (it >= kPfStages && !mbar_wait(&empty[st], ((it / kPfStages) - 1) & 1, a.status)) break;
+        const bool keys = it < ntk;
+        const int tile = keys ? it : it - ntk;
+        mbar_arrive_expect_tx(&full[st], kPfTileBytes);
+        tma_load_2d(ring + st * kPfTileBytes, keys ? &kmap : &vmap, 0,
+                    static_cast<int>(y0 + static_cast<long long>(tile) * 32 * 4), &full[st]);
+      }
+      for (int j = it - kPfStages; j < it; ++j)  // every issued copy lands before exit
+        if (j >= 0) mbar_wait(&full[j % kPfStages], (j / kPfStages) & 1, a.status);
+    }
+    return;
+  }
+  const int i = i0 + warp;
+  const bool valid = i < T;
+  float* qrow = qs + warp * 128;
+  float* sc = sc_all + warp * tpad;
+  {
+    const float4 v = valid ? *reinterpret_cast<const float4*>(a.q + static_cast<long long>(i) * a.ld_q +
+                                                              static_cast<long long>(h) * 128 + 4 * lane)
+                           : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    reinterpret_cast<float4*>(qrow)[lane] = v;
+  }
+  __syncwarp();
+  const float4* q4 = reinterpret_cast<const float4*>(qrow);
+  // ---- scores
+  for (int j = 0; j < ntk; ++j) {
+    const int st = j % kPfStages;
+    mbar_wait(&full[st], (j / kPfStages) & 1, a.status);
+    const int t = 32 * j + lane;
+    if (valid && t <= i) {
+      const unsigned char* row = ring + st * kPfTileBytes + lane * 128;
+      float acc = -0.0f;
+#pragma unroll
+      for (int b = 0; b < 4; ++b)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float4 kv =
+              *reinterpret_cast<const float4*>(row + b * kTmaBoxBytes + ((c ^ (lane & 7)) << 4));
+          const float4 qv = q4[b * 8 + c];
+          const float2 p0 = f2_mul(make_float2(qv.x, qv.y), make_float2(kv.x, kv.y));
+          const float2 p1 = f2_mul(make_float2(qv.z, qv.w), make_float2(kv.z, kv.w));
+          acc = __fadd_rn(acc, p0.x);
+          acc = __fadd_rn(acc, p0.y);
+          acc = __fadd_rn(acc, p1.x);
+          acc = __fadd_rn(acc, p1.y);
+        }
+      sc[t] = __fmul_rn(acc, a.scale);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+  }
+  // ---- softmax_backend (src/cpu/ops.rs:139-187) over tokens 0..i
+  const int L = i + 1;
+  bool bad = false;
+  if (valid) {
+    float mx = -INFINITY;
+    int b = 0;
+    for (int t = lane; t < L; t += 32) {
+      const float v = sc[t];
+      b |= isnan(v) || v == INFINITY;
+      mx = fmaxf(mx, v);
+    }
+    mx = warp_max(mx);
+    bad = __any_sync(0xffffffffu, b) || !isfinite(mx);
+    if (!bad) {
+      for (int t = lane; t < L; t += 32) sc[t] = exp_f32_via_f64(__fsub_rn(sc[t], mx));
+      __syncwarp();
+      float sum = -0.0f;
+      if (lane == 0) sum = serial_sum_smem(sc, L);
+      sum = __shfl_sync(0xffffffffu, sum, 0);
+      for (int t = lane; t < L; t += 32) sc[t] = __fdiv_rn(sc[t], sum);
+      __syncwarp();
+    } else if (lane == 0) {
+      flag(a.status, DEV_SOFTMAX);
+    }
+  }
+  // ---- values: lane owns columns 4 lane .. 4 lane + 3 (box lane / 8)
+  float4 acc = make_float4(-0.0f, -0.0f, -0.0f, -0.0f);
+  for (int j = 0; j < ntk; ++j) {
+    const int it = ntk + j, st = it % kPfStages;
+    mbar_wait(&full[st], (it / kPfStages) & 1, a.status);
+    const int rows = valid && !bad ? min(32, L - 32 * j) : 0;
+    if (rows > 0) {
+      const unsigned char* tile = ring + st * kPfTileBytes + (lane >> 3) * kTmaBoxBytes;
+      const float* p = sc + 32 * j;
+#pragma unroll 8
+      for (int r = 0; r < rows; ++r) {
+        const float4 v = *reinterpret_cast<const float4*>(tile + r * 128 + (((lane & 7) ^ (r & 7)) << 4));
+        const float pr = p[r];
+        acc.x = __fadd_rn(acc.x, __fmul_rn(pr, v.x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(pr, v.y));
+        acc.z = __fadd_rn(acc.z, __fmul_rn(pr, v.z));
+        acc.w = __fadd_rn(acc.w, __fmul_rn(pr, v.w));
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+  }
+  if (valid && !bad)
+    *reinterpret_cast<float4*>(a.out + static_cast<long long>(i) * a.ld_out +
+                               static_cast<long long>(h) * 128 + 4 * lane) = acc;
+}
+
+bool attention_prefill_ok(const AttnArgs& a) {
+  return a.tiled && a.dim == 128 && a.causal && a.tokens > 0 &&
+         attn_prefill_smem(a.tokens) <= 227 * 1024 && a.ld_q % 4 == 0 && a.ld_out % 4 == 0 &&
+         reinterpret_cast<uintptr_t>(a.q) % 16 == 0 && reinterpret_cast<uintptr_t>(a.out) % 16 == 0;
+}
+
+cudaError_t launch_attention_prefill(const AttnMaps& m, const AttnArgs& a, cudaStream_t st) {
+  if (!attention_prefill_ok(a) || a.heads <= 0 || a.heads > 65535) return cudaErrorInvalidValue;
+  static PerDeviceOnce configured;
+  configured.run([] {
+    cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         227 * 1024);
+  });
+  const int blocks = (a.tokens + kPfRows - 1) / kPfRows;
+  attn_prefill_kernel<<<dim3(blocks, a.heads), kPfThreads, attn_prefill_smem(a.tokens), st>>>(
+      *reinterpret_cast<const CUtensorMap*>(m.k), *reinterpret_cast<const CUtensorMap*>(m.v), a);
+  return cudaGetLastError();
+}
+
 }  // namespace uocr

@@ -1795,13 +1795,18 @@ int uocr_kv_attention_prefill(uocr_ctx* ctx, const uocr_kv* kv, size_t seq, cons
   a.dim = kv->head_dim;
   a.causal = 1;
   a.seq = static_cast<int>(seq);
+  a.tokens = static_cast<int>(rows);
   a.scale = 1.0f / std::sqrt(static_cast<float>(kv->head_dim));
   a.out = out_dev;
   a.ld_out = kv->width;
   a.status = ctx->status_dev;
   const int n = static_cast<int>(rows);
-  cudaError_t e = kv->tma ? launch_attention_decode_tma(kv->maps, a, n, ctx->stream)
-                          : launch_attention_decode(a, n, static_cast<int>(kv->cap), ctx->stream);
+  // 16 rows per CTA where it applies (head_dim 128, prefix up to ~2,500
+  // tokens), else one row per CTA; the same bits either way
+  const bool blocked = kv->tma && kv->split != 1 && attention_prefill_ok(a);
+  cudaError_t e = blocked   ? launch_attention_prefill(kv->maps, a, ctx->stream)
+                  : kv->tma ? launch_attention_decode_tma(kv->maps, a, n, ctx->stream)
+                            : launch_attention_decode(a, n, static_cast<int>(kv->cap), ctx->stream);
   if (e != cudaSuccess) return fail(UOCR_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
   return ok();
 }

@@ -331,6 +331,11 @@ bool attention_tma_maps_tiled(AttnMaps* m, const float* keys, const float* value
 // one-CTA-per-head kernels, so the same bits.  max_tokens bounds every
 // sequence's token count (the scratch row length).
 bool attention_split_ok(const AttnArgs& a);
+// Causal prefill over the tiled cache, 16 query rows per CTA (head_dim 128;
+// rows = a.tokens of sequence a.seq; q and out token-major); the same bits as
+// the one-query-per-CTA causal form.
+bool attention_prefill_ok(const AttnArgs& a);
+cudaError_t launch_attention_prefill(const AttnMaps& m, const AttnArgs& a, cudaStream_t st);
 cudaError_t launch_attention_split(const AttnArgs& a, int batch, int max_tokens, cudaStream_t st);
 cudaError_t launch_attention_decode_tma(const AttnMaps& m, const AttnArgs& a, int batch,
                                         cudaStream_t st);
