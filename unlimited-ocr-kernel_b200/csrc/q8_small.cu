@@ -135,8 +135,9 @@ __global__ void __launch_bounds__(kSmThreads, 3)
                       const SmallArgs a) {
   constexpr int kStage = INT8 ? kSmStageI : kSmStageF;
   extern __shared__ unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  // offset from the shared array itself: derived pointers stay shared-memory
+  // pointers to the compiler (an integer-cast alignment makes them generic)
+  unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   constexpr int kSmStages = INT8 ? kSmStagesI : kSmStagesF;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kSmStages * kStage);
   uint64_t* empty = full + kSmStages;

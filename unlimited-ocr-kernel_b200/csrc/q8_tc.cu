@@ -164,8 +164,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                          const __grid_constant__ CUtensorMap tmap_x,
                          const __grid_constant__ CUtensorMap tmap_xs, const TcArgs a) {
   extern __shared__ unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  // offset from the shared array itself: derived pointers stay shared-memory
+  // pointers to the compiler (an integer-cast alignment makes them generic)
+  unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
@@ -442,8 +443,9 @@ __global__ void __launch_bounds__(kFThreads, 1)
                           const __grid_constant__ CUtensorMap tmap_xp16,
                           const __grid_constant__ CUtensorMap tmap_xp32, const TcF32Args a) {
   extern __shared__ unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  // offset from the shared array itself: derived pointers stay shared-memory
+  // pointers to the compiler (an integer-cast alignment makes them generic)
+  unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   unsigned char* w8ring = smem;                        // [kFW8Slots][128][64] int8
   unsigned char* sring = smem + kFW8Slots * kFWi8;     // [nS][bf16 weights | pieces]
   uint64_t* full8 = reinterpret_cast<uint64_t*>(sring + kFSRing);
@@ -939,8 +941,9 @@ __global__ void __launch_bounds__(kHThreads, 1)
     bf16_head_kernel(const __grid_constant__ CUtensorMap tmap_w,
                      const __grid_constant__ CUtensorMap tmap_x, const HeadArgs a) {
   extern __shared__ unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  // offset from the shared array itself: derived pointers stay shared-memory
+  // pointers to the compiler (an integer-cast alignment makes them generic)
+  unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kHStages * kHStageBytes);
   uint64_t* empty = full + kHStages;
   uint64_t* tfull = empty + kHStages;
