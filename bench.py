@@ -60,6 +60,45 @@ PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_HBM = 6650.0
 
 
+def kept_graph():
+    """A CUDA graph whose cudaGraph_t is kept after capture, so that its
+    kernel nodes can be counted (graph_launches); replay instantiates it."""
+    import torch
+    return torch.cuda.CUDAGraph(keep_graph=True)
+
+
+def graph_launches(graph):
+    """Kernel launches of one replay of a kept graph that are this library's
+    own kernels (function names in namespace uocr; torch's copies and index
+    kernels are not counted), read from the graph's nodes; None if the
+    graph cannot be inspected."""
+    try:
+        from cuda.bindings import runtime as rt
+        h = graph.raw_cuda_graph()
+        h = h if isinstance(h, rt.cudaGraph_t) else rt.cudaGraph_t(init_value=int(h))
+        err, _, n = rt.cudaGraphGetNodes(h, 0)
+        if err != rt.cudaError_t.cudaSuccess:
+            return None
+        err, nodes, n = rt.cudaGraphGetNodes(h, n)
+        ours = 0
+        for nd in nodes[:n]:
+            err, t = rt.cudaGraphNodeGetType(nd)
+            if t != rt.cudaGraphNodeType.cudaGraphNodeTypeKernel:
+                continue
+            err, prm = rt.cudaGraphKernelNodeGetParams(nd)
+            err, name = rt.cudaFuncGetName(prm.func)
+            name = name.decode() if isinstance(name, bytes) else str(name)
+            ours += "uocr" in name
+        return ours
+    except Exception as exc:  # an inspection failure leaves the count unknown
+        print(f"graph_launches: {exc}", file=sys.stderr)
+        return None
+
+
+def _launches(per_replay, replays):
+    return None if per_replay is None else per_replay * replays
+
+
 def peak_hbm():
     try:
         with open(PEAKS_PATH) as f:
@@ -184,10 +223,11 @@ def run_ours(args):
             enqueue(i)
     ctx.sync()
     # capture `chunk` consecutive steps (distinct layers and tokens) in a graph
-    graph = torch.cuda.CUDAGraph()
+    graph = kept_graph()
     with torch.cuda.graph(graph, stream=stream):
         for i in range(chunk):
             enqueue(i)
+    per_replay = graph_launches(graph)
     reps = max(1, args.steps // chunk)
     steps = reps * chunk
     for _ in range(max(args.warmup, 3)):
@@ -265,7 +305,7 @@ def run_ours(args):
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(STEP_BYTES / (ms_step * 1e-3) / 1e9 / peak, 4),
                          "traffic": args.traffic if args.traffic is not None else DECODE_TRAFFIC},
-            "gpu_launches": steps,
+            "gpu_launches": _launches(per_replay, reps),
             "clocks": clocks.summary(),
         }
         if cpu:
@@ -310,11 +350,12 @@ def run_gemv(args):
             uocr_q8.linear_multi_device(ctx, mats[i:i + GEMV_PER_LAUNCH], x,
                                         ys[i:i + GEMV_PER_LAUNCH], mode)
     ctx.sync()
-    graph = torch.cuda.CUDAGraph()
+    graph = kept_graph()
     with torch.cuda.graph(graph, stream=stream):
         for i in range(0, pool, GEMV_PER_LAUNCH):
             uocr_q8.linear_multi_device(ctx, mats[i:i + GEMV_PER_LAUNCH], x,
                                         ys[i:i + GEMV_PER_LAUNCH], mode)
+    per_replay = graph_launches(graph)
     reps = max(1, args.steps // pool)
     for _ in range(max(args.warmup, 3)):
         graph.replay()
@@ -356,7 +397,7 @@ def run_gemv(args):
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(gbs / peak, 4),
                          "traffic": args.traffic if args.traffic is not None else GEMV_TRAFFIC},
-            "gpu_launches": steps // GEMV_PER_LAUNCH, "clocks": clocks.summary(),
+            "gpu_launches": _launches(per_replay, reps), "clocks": clocks.summary(),
             "cpu_baseline": None if args.no_cpu else gemv_cpu_baseline(mode, 3.0)}
 
 
@@ -543,6 +584,16 @@ def run_prefill(args):
             layer.forward_device(x, lg, mode, y)
     ctx.sync()
     steps = max(1, args.steps)
+    # launches of one forward, counted from a captured (never replayed) copy
+    try:
+        counted = kept_graph()
+        with torch.cuda.graph(counted, stream=stream):
+            layer.forward_device(x, lg, mode, y)
+        per_forward = graph_launches(counted)
+        del counted
+    except Exception as exc:
+        print(f"prefill: launch count unavailable ({exc})", file=sys.stderr)
+        per_forward = None
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(0) as clocks:
         with torch.cuda.stream(stream):
@@ -591,9 +642,7 @@ def run_prefill(args):
                          "achieved": round(tops, 3), "peak": round(attainable, 1),
                          "peak_kind": f"min(bf16 dense {kind_t}, AI x HBM {kind_h})",
                          "unit": "TFLOP/s", "frac": round(tops / attainable, 5), "traffic": None},
-            # route, grouping, split or quantize (+ gather), 3 grouped GEMMs, SwiGLU,
-            # shared: split/quantize + 3 GEMMs + SwiGLU, combine
-            "gpu_launches": steps * 13, "clocks": clocks.summary(),
+            "gpu_launches": _launches(per_forward, steps), "clocks": clocks.summary(),
             "cpu_baseline": None if args.no_cpu else prefill_cpu_baseline(mode, 6.0)}
 
 
@@ -613,6 +662,7 @@ def run_int8suite(args):
     g.manual_seed(3)
     K = H
     cases = []
+    launches = 0  # this library's kernels in the timed replays
     total_ops = 0.0
     total_bytes = 0.0
     total_s = 0.0
@@ -634,11 +684,13 @@ def run_int8suite(args):
                     for i in range(pool):
                         mats[i].linear_device(x, y, dynamic=True)
                 ctx.sync()
-                graph = torch.cuda.CUDAGraph()
+                graph = kept_graph()
                 with torch.cuda.graph(graph, stream=stream):
                     for i in range(pool):
                         mats[i].linear_device(x, y, dynamic=True)
                 replays = max(1, 2048 // pool)
+                per = graph_launches(graph)
+                launches = None if launches is None or per is None else launches + per * replays
                 for _ in range(3):
                     graph.replay()
                 torch.cuda.synchronize()
@@ -674,7 +726,7 @@ def run_int8suite(args):
                        "aggregate": "total ops / total time over the 12 cases",
                        "timing": "CUDA graph of one call per pool matrix, replayed; "
                                  "pool > 400 MB so weights come from HBM"},
-            "cases": cases, "clocks": clocks.summary(),
+            "cases": cases, "clocks": clocks.summary(), "gpu_launches": launches,
             "roofline": {"bound": "hbm (M = 1, 16) / tensor (M >= 128)",
                          "kernel": "all cases: gemv_tma_kernel (M = 1), small_rows_kernel "
                                    "(M = 16), q8_tc_gemm_i8_kernel (M >= 128)",
@@ -770,12 +822,13 @@ def run_ep(args):
             step(i, xs[i % n_in], lg[i % n_in])
     torch.cuda.synchronize()
     # one graph of n_layers consecutive steps (distinct layers and tokens)
-    graph = torch.cuda.CUDAGraph()
+    graph = kept_graph()
     graphed = True
     try:
         with torch.cuda.graph(graph, stream=stream):
             for i in range(n_layers):
                 step(i, xs[i % n_in], lg[i % n_in])
+        per_replay = graph_launches(graph)
         for _ in range(2):
             graph.replay()
         torch.cuda.synchronize()
@@ -859,7 +912,7 @@ def run_ep(args):
             # route, dispatch (plan + rows), expert rows (grouping, split or quantize,
             # 3 warp-level + 3 tensor-core projections, SwiGLU, un-permute), shared
             # expert (split or quantize, 3 projections, SwiGLU), combine
-            "gpu_launches": steps * {0: 20, 2: 21}.get(mode) if mode in (0, 2) else None,
+            "gpu_launches": _launches(per_replay, reps) if graphed else None,
             "clocks": clocks.summary(),
         }
         if cpu:
@@ -1106,10 +1159,11 @@ def run_decode(args):
         for _ in range(max(args.warmup, 3)):  # eager: sizes every workspace
             decode_step(dec, state, tokens, mode, logits)
     ctx.sync()
-    graph = torch.cuda.CUDAGraph()
+    graph = kept_graph()
     with torch.cuda.graph(graph, stream=stream):
         decode_step(dec, state, tokens, mode, logits)
         tokens.copy_(torch.argmax(logits, dim=1))
+    per_replay = graph_launches(graph)
     for _ in range(3):
         graph.replay()
     torch.cuda.synchronize()
@@ -1158,7 +1212,7 @@ def run_decode(args):
            "roofline": {"bound": "hbm", "kernel": "whole step (attention, MoE, projections)",
                         "achieved": round(gbs, 2), "peak": peak, "peak_kind": peak_kind,
                         "unit": "GB/s", "frac": round(gbs / peak, 4), "traffic": None},
-           "gpu_launches": None, "clocks": clocks.summary()}
+           "gpu_launches": _launches(per_replay, steps), "clocks": clocks.summary()}
     if args.lm_head == "bf16":
         # the BF16 lm_head alone (uocr_linear_bf16_tc, 129,280 x 1280 at batch
         # 64), weights from HBM (331 MB, more than L2), events on its stream
@@ -1273,9 +1327,10 @@ def run_fixed_work(args):
                 torch.cuda.nvtx.range_pop()
     ctx.sync()
     torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
+    graph = kept_graph()
     with torch.cuda.graph(graph, stream=stream):
         step()
+    per_replay = graph_launches(graph)
     with torch.cuda.stream(stream):  # warm-up repetition through the graph
         begin()
         for _ in range(FW_STEPS):
@@ -1331,7 +1386,9 @@ def run_fixed_work(args):
                                                 "lm_head)",
                         "achieved": round(gbs, 2), "peak": peak, "peak_kind": peak_kind,
                         "unit": "GB/s", "frac": round(gbs / peak, 4), "traffic": None},
-           "gpu_launches": None, "clocks": clocks.summary(),
+           # the timed repetitions' decode replays (the eager prefills' launches are
+           # not counted)
+           "gpu_launches": _launches(per_replay, FW_STEPS * reps), "clocks": clocks.summary(),
            "reference_published": {"decode_with_checksum_seconds": 4.031535, "tok_s": 127.0,
                                    "hardware": "M4 Pro, 8 threads"}}
     del graph
@@ -1533,10 +1590,11 @@ def run_ep_peer(args):
     R = n_layers * max(1, math.ceil(EPP_MIN_TIMED_S / (K * t_layer * n_layers)))
     R = min(R, n_layers * 4096)
     del probe
-    graph = torch.cuda.CUDAGraph()
+    graph = kept_graph()
     with torch.cuda.graph(graph, stream=stream):
         for i in range(R):
             step(i)
+    per_replay = graph_launches(graph)
     warm = max(args.warmup, 3)
     for _ in range(warm):
         graph.replay()
@@ -1627,7 +1685,7 @@ def run_ep_peer(args):
             # gate, up, big-counts when a group can exceed 64 rows), SwiGLU split,
             # small-rows down (+ tensor-core down), un-permute, return, shared
             # expert (split, gate/up, SwiGLU split, down), combine
-            "gpu_launches": forwards * (16 if world * T <= 64 else 20),
+            "gpu_launches": _launches(per_replay, K),
             "clocks": clocks.summary(),
         }
         if world == 1 and not args.no_cpu:
