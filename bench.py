@@ -69,24 +69,32 @@ def kept_graph():
 
 def graph_launches(graph):
     """Kernel launches of one replay of a kept graph that are this library's
-    own kernels (function names in namespace uocr; torch's copies and index
-    kernels are not counted), read from the graph's nodes; None if the
-    graph cannot be inspected."""
+    own kernels: the graph's kernel nodes whose function (driver API name,
+    mangled) is in namespace uocr; torch's copies and index kernels are not
+    counted.  None if the graph cannot be inspected."""
     try:
-        from cuda.bindings import runtime as rt
+        from cuda.bindings import driver as drv
         h = graph.raw_cuda_graph()
-        h = h if isinstance(h, rt.cudaGraph_t) else rt.cudaGraph_t(init_value=int(h))
-        err, _, n = rt.cudaGraphGetNodes(h, 0)
-        if err != rt.cudaError_t.cudaSuccess:
+        h = h if isinstance(h, drv.CUgraph) else drv.CUgraph(init_value=int(h))
+        err, _, n = drv.cuGraphGetNodes(h, 0)
+        if err != drv.CUresult.CUDA_SUCCESS:
             return None
-        err, nodes, n = rt.cudaGraphGetNodes(h, n)
+        err, nodes, n = drv.cuGraphGetNodes(h, n)
         ours = 0
         for nd in nodes[:n]:
-            err, t = rt.cudaGraphNodeGetType(nd)
-            if t != rt.cudaGraphNodeType.cudaGraphNodeTypeKernel:
+            err, t = drv.cuGraphNodeGetType(nd)
+            if t != drv.CUgraphNodeType.CU_GRAPH_NODE_TYPE_KERNEL:
                 continue
-            err, prm = rt.cudaGraphKernelNodeGetParams(nd)
-            err, name = rt.cudaFuncGetName(prm.func)
+            err, prm = drv.cuGraphKernelNodeGetParams(nd)
+            if err != drv.CUresult.CUDA_SUCCESS:
+                return None
+            name = None
+            if int(prm.func):
+                err, name = drv.cuFuncGetName(prm.func)
+            elif int(getattr(prm, "kern", 0) or 0):
+                err, name = drv.cuKernelGetName(prm.kern)
+            if name is None or err != drv.CUresult.CUDA_SUCCESS:
+                return None
             name = name.decode() if isinstance(name, bytes) else str(name)
             ours += "uocr" in name
         return ours
