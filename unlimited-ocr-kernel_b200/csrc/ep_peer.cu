@@ -70,6 +70,10 @@ int record_error(int status, const char* message);  // capi.cu
 
 using namespace uocr;
 
+// The exchange's kernels and device helpers live in namespace uocr like every
+// other kernel of the library (a profiler or a graph's node list shows them
+// as uocr::...).
+namespace uocr {
 namespace {
 
 constexpr int kEpThreads = 256;
@@ -414,6 +418,7 @@ int cuda_err(cudaError_t e, const char* what) {
 }
 
 }  // namespace
+}  // namespace uocr
 
 struct uocr_ep {
   int device = 0;
