@@ -184,6 +184,26 @@ __device__ __forceinline__ bool last_to_arrive(const EpDev& d, unsigned* c) {
 // CTA to finish publishes each owner's count and then, with release
 // semantics at system scope, the step number.
 constexpr int kRdWarps = 4;
+// A warp moves a row of up to 32 * kRowRegs float4 through registers: every
+// load issued before the first store (a copy loop `dst[c] = src[c]` waits for
+// each load in turn, since the stores may alias the source).
+constexpr int kRowRegs = 16;
+
+__device__ __forceinline__ void row_to_regs(const float4* src, int h4, int lane, float4 (&v)[kRowRegs]) {
+#pragma unroll
+  for (int u = 0; u < kRowRegs; ++u) {
+    const int c = lane + 32 * u;
+    if (c < h4) v[u] = __ldcg(src + c);
+  }
+}
+
+__device__ __forceinline__ void regs_to_row(float4* dst, int h4, int lane, const float4 (&v)[kRowRegs]) {
+#pragma unroll
+  for (int u = 0; u < kRowRegs; ++u) {
+    const int c = lane + 32 * u;
+    if (c < h4) dst[c] = v[u];
+  }
+}
 
 __global__ void __launch_bounds__(kRdWarps * 32) ep_route_dispatch_kernel(
     const __grid_constant__ EpDev d, const float* __restrict__ x, const float* __restrict__ logits,
@@ -228,6 +248,10 @@ __global__ void __launch_bounds__(kRdWarps * 32) ep_route_dispatch_kernel(
     if (ok) {
       const int slot = lane < k ? static_cast<int>(cta_base[o]) + local : 0;
       const float4* src = reinterpret_cast<const float4*>(x) + static_cast<long long>(t) * h4;
+      // the token's row once into registers, then stored to each owner
+      const bool in_regs = h4 <= 32 * kRowRegs;
+      float4 v[kRowRegs];
+      if (in_regs) row_to_regs(src, h4, lane, v);
       for (int j = 0; j < k; ++j) {
         const int oj = __shfl_sync(0xffffffffu, o, j);
         const int sj = __shfl_sync(0xffffffffu, slot, j);
@@ -239,7 +263,10 @@ __global__ void __launch_bounds__(kRdWarps * 32) ep_route_dispatch_kernel(
         char* base = d.peers[oj];
         const long long row = static_cast<long long>(d.rank) * d.cap + sj;
         float4* dst = reinterpret_cast<float4*>(base + d.L.recv_x) + row * h4;
-        for (int c = lane; c < h4; c += 32) dst[c] = src[c];
+        if (in_regs)
+          regs_to_row(dst, h4, lane, v);
+        else
+          for (int c = lane; c < h4; c += 32) dst[c] = src[c];
         if (lane == 0) {
           reinterpret_cast<int*>(base + d.L.recv_ids)[row] = d.local_of[ej];
           reinterpret_cast<int*>(base + d.L.recv_pair)[row] = t * k + j;
@@ -314,7 +341,13 @@ __global__ void __launch_bounds__(kEpThreads) ep_return_kernel(const __grid_cons
     }
     float4* dst = reinterpret_cast<float4*>(d.peers[s] + d.L.ret_rows) + static_cast<long long>(p) * h4;
     const float4* src = reinterpret_cast<const float4*>(rows) + static_cast<long long>(src_row) * h4;
-    for (int c = lane; c < h4; c += 32) dst[c] = src[c];
+    if (h4 <= 32 * kRowRegs) {
+      float4 v[kRowRegs];
+      row_to_regs(src, h4, lane, v);
+      regs_to_row(dst, h4, lane, v);
+    } else {
+      for (int c = lane; c < h4; c += 32) dst[c] = src[c];
+    }
   }
   if (!last_to_arrive(d, d.ctr + kCtrReturn)) return;
   for (int r = threadIdx.x; r < d.world; r += kEpThreads)
