@@ -53,7 +53,7 @@ constexpr int kMaxStages = 6;  // ring slots: as many as shared memory allows
 // by phase parity, which is only sound while no group can wait more than one
 // phase ahead of a slot's first fill.
 constexpr int kMinStages = 4;
-static_assert(kMinStages >= 4, "one ring slot per consumer group (kGroups) at least");
+static_assert(kMinStages >= kGroups, "one ring slot per consumer group at least");
 constexpr int kSmemBudget = 220 * 1024;
 constexpr int kTileRows = 8;
 constexpr int kMaxTopK = 8;
