@@ -1249,6 +1249,158 @@ def run_decode(args):
 
 
 
+def decode_step_bytes_ep(cfg, tokens_per_seq, world, lm_head="q8"):
+    """decode_step_bytes for one GPU of an expert-parallel step: this GPU's
+    sequences' KV and projections, the shared expert and 1/world of every MoE
+    layer's routed experts."""
+    q8 = lambda r, c: r * c + r * ((c + 31) // 32) * 4
+    routed = (cfg.layers - cfg.first_dense) * cfg.experts * (
+        2 * q8(cfg.expert_width, cfg.hidden) + q8(cfg.hidden, cfg.expert_width))
+    return decode_step_bytes(cfg, tokens_per_seq, lm_head) - routed + routed // world
+
+
+def run_decode_ep(args):
+    """Config 4 on N GPUs: the 12-layer decode step with the sequences split
+    over the GPUs (each GPU: 64 sequences with 2048-token prefixes, their
+    attention, projections, KV cache and lm_head) and every MoE layer's routed
+    experts split over the GPUs (each holds 64/N of them; rows cross NVLink
+    through the library's peer-memory exchange, uocr_ep_*).  Weak scaling:
+    value = all GPUs' tokens / the slowest GPU's step time.  Rank 0 checks the
+    first step against the plain one-GPU step (all experts) on a copy of its
+    state."""
+    import torch
+
+    import uocr_q8
+    from uocr_q8.decoder import DecodeState, Decoder, DecoderConfig, decode_step
+    from uocr_q8.expert_parallel import decoder_peer_experts
+    world, rank, local = dist_setup(args.gpus)
+    if world > 1:
+        import torch.distributed as dist
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    ctx = uocr_q8.GpuContext(local)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream)
+    cfg = DecoderConfig()
+    mode = args.decode_mode
+    with torch.cuda.stream(stream):
+        dec = Decoder.random(ctx, cfg, seed=11, lm_head=args.lm_head)  # the same weights on every GPU
+        states = [DecodeState(dec, DEC_BATCH, DEC_PREFIX) for _ in range(2 if rank == 0 else 1)]
+        g = torch.Generator(device=dev)
+        g.manual_seed(12 + rank)
+        for li in range(cfg.layers):
+            for b in range(DEC_BATCH):
+                k = torch.randn((DEC_PREFIX, cfg.hidden), device=dev, generator=g)
+                for st in states:
+                    st.caches[li].prefill(b, k, k.mul(0.5))
+        tokens = torch.randint(0, cfg.vocab, (DEC_BATCH,), device=dev, generator=g)
+        logits = torch.empty((DEC_BATCH, cfg.vocab), device=dev)
+    ctx.sync()
+    eps = decoder_peer_experts(dec, DEC_BATCH)
+    state = states[0]
+    # parity of the first step (every GPU steps through the exchange together)
+    with torch.cuda.stream(stream):
+        decode_step(dec, state, tokens, mode, logits, experts=eps)
+    ctx.sync()
+    parity = None
+    if rank == 0:
+        with torch.cuda.stream(stream):
+            ref = decode_step(dec, states[1], tokens, mode)
+        ctx.sync()
+        a, b_ = logits.cpu().numpy(), ref.cpu().numpy()
+        same = float(np.mean(a.view(np.uint32) == b_.view(np.uint32)))
+        rel = float(np.max(np.abs(a.astype(np.float64) - b_)) / max(float(np.max(np.abs(b_))), 1e-30))
+        parity = {"bit_identical": round(same, 6), "max_rel_diff": rel,
+                  "ok": same == 1.0 if mode == 2 else rel <= 1e-3}
+        states[1].free()
+        del ref
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3) - 1):  # eager: sizes every workspace
+            decode_step(dec, state, tokens, mode, logits, experts=eps)
+    ctx.sync()
+    if world > 1:
+        dist.barrier()
+    graph = kept_graph()
+    with torch.cuda.graph(graph, stream=stream):
+        decode_step(dec, state, tokens, mode, logits, experts=eps)
+        tokens.copy_(torch.argmax(logits, dim=1))
+    per_replay = graph_launches(graph)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    steps = max(4, min(args.steps, 200))
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(steps):
+                graph.replay()
+            stop.record(stream)
+        stop.synchronize()
+    ms = start.elapsed_time(stop) / steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    # ---- end to end: token ids in from pinned host memory, next ids out
+    e2e_steps = max(4, min(steps, 50))
+    h_in = torch.randint(0, cfg.vocab, (DEC_BATCH,), dtype=torch.int64).pin_memory()
+    h_out = torch.empty((DEC_BATCH,), dtype=torch.int64).pin_memory()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        for _ in range(e2e_steps):
+            tokens.copy_(h_in, non_blocking=True)
+            graph.replay()
+            h_out.copy_(tokens, non_blocking=True)
+            stream.synchronize()
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    tokens_now = state.caches[0].state(0)[0]
+    step_bytes = decode_step_bytes_ep(cfg, tokens_now, world, args.lm_head)
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+    peak, peak_kind = peak_hbm()
+    res = {"metric": "decode tok/s (12-layer MoE decoder, 64 sequences per GPU, KV 2048, "
+                     "experts split over the GPUs)",
+           "value": round(world * DEC_BATCH / (ms * 1e-3), 1), "unit": "tok/s", "n_gpus": world,
+           "steps": steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "int8-act" if mode else "fp32", "data": "synthetic (seeded; random-init weights)",
+           "config": {"workload": "decode_step_12_layers_ep", "batch_per_gpu": DEC_BATCH,
+                      "prefix": DEC_PREFIX, "window": cfg.window, "layers": cfg.layers,
+                      "hidden": cfg.hidden, "experts": cfg.experts, "top_k": cfg.top_k,
+                      "vocab": cfg.vocab, "lm_head": args.lm_head, "mode": mode,
+                      "parallelism": f"sequences split, experts split (ep{world}), peer memory",
+                      "cuda_graph": True, "tokens_per_sequence": tokens_now,
+                      "bytes_per_step_per_gpu": step_bytes,
+                      "l2": "17 GB of KV per step and GPU (> 126 MB L2)"},
+           "ep_parity": parity,
+           "e2e": {"value": round(world * DEC_BATCH / e2e_s, 1), "unit": "tok/s",
+                   "steps": e2e_steps, "ms_per_step": round(e2e_s * 1e3, 4),
+                   "h2d_bytes_per_step": DEC_BATCH * 8, "d2h_bytes_per_step": DEC_BATCH * 8},
+           "roofline": {"bound": "hbm", "kernel": "whole step per GPU (attention, MoE, projections)",
+                        "achieved": round(gbs, 2), "peak": peak, "peak_kind": peak_kind,
+                        "unit": "GB/s", "frac": round(gbs / peak, 4), "traffic": None},
+           "gpu_launches": _launches(per_replay, steps), "clocks": clocks.summary()}
+    del graph  # before the exchange and the process group go
+    for e in eps:
+        if e is not None:
+            e.free()
+    state.free()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return res if rank == 0 else None
+
+
 # ---------------------------------------------------------------------------
 # The reference's fixed-work decoder benchmark (src/model/benchmark.rs:5-64):
 # a 1517-token prefill, then 512 teacher-forced decode steps of one sequence
@@ -1857,7 +2009,7 @@ def main():
                          "defaults to the committed capture of the workload's kernel")
     ap.add_argument("--workload",
                     choices=["ep_peer", "moe_decode", "gemv", "prefill", "int8suite", "ep_decode",
-                             "attn_decode", "decode_step", "fixed_work"],
+                             "attn_decode", "decode_step", "fixed_work", "decode_step_ep"],
                     default="ep_peer")
     ap.add_argument("--gemv-int8", action="store_true")
     ap.add_argument("--prefill-mode", type=int, choices=[0, 2], default=0)
@@ -1888,6 +2040,8 @@ def main():
         return
     if args.workload == "ep_decode":
         res = run_ep(args)
+    elif args.workload == "decode_step_ep":
+        res = run_decode_ep(args)
     elif args.workload == "moe_decode":
         res = run_ours(args)
     else:

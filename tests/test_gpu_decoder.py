@@ -303,6 +303,44 @@ def test_prefill_then_decode_matches_oracle(ctx, mode, head, tokens):
     state.free()
 
 
+@pytest.mark.parametrize("mode", [0, 2])
+def test_decode_step_with_peer_experts_matches_plain(ctx, mode):
+    """The decode step with its MoE layers through the expert-parallel
+    exchange (uocr_ep_*, a world of this GPU alone) against the plain step on
+    the same state: int8 activations bit for bit, FP32 activations within the
+    decode tolerance, over steps that wrap the cache ring."""
+    from uocr_q8.decoder import DecodeState, Decoder, decode_step
+    from uocr_q8.expert_parallel import decoder_peer_experts
+    cfg = small_config()
+    dec = Decoder.random(ctx, cfg, seed=60 + mode)
+    batch, prefix = 3, 5
+    states = [DecodeState(dec, batch, prefix) for _ in range(2)]
+    rng = np.random.default_rng(61)
+    for b in range(batch):
+        for li in range(cfg.layers):
+            k = dev(rng.standard_normal((prefix, cfg.hidden)).astype(np.float32))
+            v = dev(rng.standard_normal((prefix, cfg.hidden)).astype(np.float32))
+            for st in states:
+                st.caches[li].prefill(b, k, v)
+    eps = decoder_peer_experts(dec, batch)
+    assert sum(e is not None for e in eps) == cfg.layers - cfg.first_dense
+    for step in range(6):
+        tokens = dev(rng.integers(0, cfg.vocab, batch).astype(np.int64))
+        plain = host(decode_step(dec, states[0], tokens, mode))
+        peer = host(decode_step(dec, states[1], tokens, mode, experts=eps))
+        ctx.sync()
+        if mode == 2:
+            assert bits_equal(peer, plain), step
+        else:
+            scale = float(np.max(np.abs(plain)))
+            assert float(np.max(np.abs(peer.astype(np.float64) - plain))) <= 1e-3 * scale, step
+    for e in eps:
+        if e is not None:
+            e.free()
+    for st in states:
+        st.free()
+
+
 def test_logits_checksum_wraps_like_the_reference(ctx):
     """uocr_bits_checksum: the u64 wrapping sum of the logits' bit patterns
     (src/model/benchmark.rs:43-47), accumulated over calls."""

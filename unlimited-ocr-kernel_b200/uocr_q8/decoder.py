@@ -209,9 +209,14 @@ class DecodeState:
         self.rope.free()
 
 
-def decode_step(decoder: Decoder, state: DecodeState, tokens_t, mode: int = 0, logits_t=None):
+def decode_step(decoder: Decoder, state: DecodeState, tokens_t, mode: int = 0, logits_t=None,
+                experts=None):
     """One decode step for every sequence: tokens_t int64 [batch] -> logits
-    [batch x vocab] (device, asynchronous)."""
+    [batch x vocab] (device, asynchronous).  ``experts``: optional, per layer
+    index, an object whose ``forward_device(x, logits, mode)`` replaces the
+    layer's own MoE (a ``PeerExpertParallel`` holding this GPU's share of the
+    routed experts: attention and projections run on this GPU's sequences,
+    the MoE layers over the GPUs of the node)."""
     import torch
     ctx, cfg = decoder.ctx, decoder.cfg
     rowwise = mode in (QuantizationMode.DYNAMIC_ACTIVATIONS, QuantizationMode.DYNAMIC_ROWWISE)
@@ -219,7 +224,7 @@ def decode_step(decoder: Decoder, state: DecodeState, tokens_t, mode: int = 0, l
     H = cfg.hidden
     x = decoder.embedding.index_select(0, tokens_t).float()
     y = None  # the previous layer's FFN output, added to x before the next norm
-    for layer, cache in zip(decoder.layers, state.caches):
+    for li, (layer, cache) in enumerate(zip(decoder.layers, state.caches)):
         # attention half of Decoder::layer (src/decoder/mod.rs:266-347); each
         # residual add runs fused with the RMSNorm of its sum
         if y is None:
@@ -233,7 +238,8 @@ def decode_step(decoder: Decoder, state: DecodeState, tokens_t, mode: int = 0, l
         n = add_rms_norm_device(ctx, r, x, layer.post_norm, cfg.eps, sum_t=r)  # r += x
         if layer.moe is not None:
             logits = linear_bf16_device(ctx, layer.router, n)
-            y = layer.moe.forward_device(n, logits, lin_mode)
+            moe = experts[li] if experts is not None and experts[li] is not None else layer.moe
+            y = moe.forward_device(n, logits, lin_mode)
         else:
             y = feed_forward_device(ctx, *layer.dense, n, lin_mode)
         x = r  # x + y is formed by the next norm

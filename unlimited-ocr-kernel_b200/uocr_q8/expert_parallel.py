@@ -245,3 +245,34 @@ def peer_expert_parallel(ctx, local_layer, n_experts: int, top_k: int, max_token
     dist.all_gather_object(handles, ep.handle(), group=group)
     ep.connect(handles)
     return ep
+
+
+def decoder_peer_experts(decoder, max_tokens: int, group=None):
+    """Per layer of ``decoder``, this rank's connected PeerExpertParallel over
+    the ranks of ``group`` (None for dense layers), built from the layer's
+    shared expert and this rank's share of its routed experts (the decoder's
+    weights are the same on every rank).  Without an initialised process
+    group the world is this GPU alone (connected locally)."""
+    import uocr_q8
+    world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+    rank = dist.get_rank(group) if world > 1 else 0
+    cfg = decoder.cfg
+    bounds = expert_bounds(cfg.experts, world)
+    out = []
+    for layer in decoder.layers:
+        if layer.moe is None:
+            out.append(None)
+            continue
+        shared, experts = layer.moe._keep
+        local = uocr_q8.MoeLayer(decoder.ctx, shared, experts[bounds[rank]:bounds[rank + 1]], 1)
+        ep = uocr_q8.PeerExpertParallel(decoder.ctx, local, cfg.experts, cfg.top_k, bounds, rank,
+                                        max_tokens, cfg.normalize, cfg.routed_scale)
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, ep.handle(), group=group)
+            ep.connect(handles)
+        else:
+            uocr_q8.PeerExpertParallel.connect_local([ep])
+        out.append(ep)
+    return out
+
