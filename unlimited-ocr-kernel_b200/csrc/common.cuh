@@ -391,6 +391,34 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Launch on `st` as a programmatic dependent of the previous kernel in the
+// stream (cudaLaunchAttributeProgrammaticStreamSerialization), so that its
+// launch overlaps the previous kernel's end.  The kernel must call
+// pdl_wait_prior_grids() before it reads or writes anything the previous
+// kernel touches (the chain kernels below call it first thing).  Falls back
+// to ordinary stream order when the attribute is refused.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                    cudaStream_t st, Args... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    cfg.numAttrs = 0;
+    e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+  }
+  return e;
+}
+
 // Programmatic dependent launch controls (no-ops when launched without PDL).
 __device__ __forceinline__ void pdl_wait_prior_grids() {
   asm volatile("griddepcontrol.wait;" ::: "memory");

@@ -289,6 +289,8 @@ __global__ void __launch_bounds__(kRdWarps * 32) ep_route_dispatch_kernel(
 // Owner side: wait for every source's dispatch of this step, take the counts,
 // mark the unused slots of each source block with id -1.  One CTA.
 __global__ void __launch_bounds__(kEpThreads) ep_recv_wait_kernel(const __grid_constant__ EpDev d) {
+  pdl_launch_dependents();  // launched as a programmatic dependent (launch_dependent):
+  pdl_wait_prior_grids();   // nothing is touched before the previous kernel completes
   __shared__ int cnt[kEpMaxWorld];
   const int tid = threadIdx.x;
   const unsigned step = d.ctr[kCtrStep] + 1u;
@@ -322,6 +324,8 @@ __global__ void __launch_bounds__(kEpThreads) ep_recv_wait_kernel(const __grid_c
 __global__ void __launch_bounds__(kEpThreads) ep_return_kernel(const __grid_constant__ EpDev d,
                                                                const float* __restrict__ rows,
                                                                const int* __restrict__ token_pos) {
+  pdl_launch_dependents();  // launched as a programmatic dependent (launch_dependent):
+  pdl_wait_prior_grids();   // nothing is touched before the previous kernel completes
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const unsigned step = d.ctr[kCtrStep] + 1u;
   const int* pair = reinterpret_cast<const int*>(d.peers[d.rank] + d.L.recv_pair);
@@ -363,6 +367,8 @@ __global__ void __launch_bounds__(128) ep_combine_kernel(const __grid_constant__
                                                          const int32_t* __restrict__ ids,
                                                          const float* __restrict__ wts, int tokens,
                                                          float* __restrict__ y) {
+  pdl_launch_dependents();  // launched as a programmatic dependent (launch_dependent):
+  pdl_wait_prior_grids();   // nothing is touched before the previous kernel completes
   const unsigned step = d.ctr[kCtrStep] + 1u;
   const char* own = d.peers[d.rank];
   for (int r = threadIdx.x; r < d.world; r += blockDim.x)
@@ -615,8 +621,7 @@ int enqueue_dispatch(uocr_ctx* ctx, uocr_ep* ep, int mode, const float* x, const
 // Enqueues wait + routed experts + return on `rs`.
 int enqueue_experts(uocr_ctx* ctx, uocr_ep* ep, int mode, cudaStream_t rs) {
   const EpDev d = ep_dev(ep, ctx);
-  ep_recv_wait_kernel<<<1, kEpThreads, 0, rs>>>(d);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_dependent(ep_recv_wait_kernel, dim3(1), dim3(kEpThreads), 0, rs, d);
   if (e != cudaSuccess) return cuda_err(e, "expert-parallel wait");
   const float* rows = ep->out_slots;
   const int* token_pos = nullptr;
@@ -639,8 +644,7 @@ int enqueue_experts(uocr_ctx* ctx, uocr_ep* ep, int mode, cudaStream_t rs) {
   const int total_warps = ep->world * ep->cap;
   int grid = (total_warps + kEpWarps - 1) / kEpWarps;
   if (grid > 2 * ctx->sms) grid = 2 * ctx->sms;
-  ep_return_kernel<<<grid, kEpThreads, 0, rs>>>(d, rows, token_pos);
-  e = cudaGetLastError();
+  e = launch_dependent(ep_return_kernel, dim3(grid), dim3(kEpThreads), 0, rs, d, rows, token_pos);
   if (e != cudaSuccess) return cuda_err(e, "expert-parallel return");
   return UOCR_OK;
 }
@@ -649,8 +653,9 @@ int enqueue_combine(uocr_ctx* ctx, uocr_ep* ep, int tokens, float* y, int32_t* i
                     float* wts_out, cudaStream_t st) {
   const EpDev d = ep_dev(ep, ctx);
   const dim3 grid(tokens > 0 ? tokens : 1, (ep->hidden / 4 + 127) / 128);
-  ep_combine_kernel<<<grid, 128, 0, st>>>(d, ep->ids, ep->wts, tokens, y);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_dependent(ep_combine_kernel, grid, dim3(128), 0, st, d,
+                                   static_cast<const int32_t*>(ep->ids),
+                                   static_cast<const float*>(ep->wts), tokens, y);
   if (e != cudaSuccess) return cuda_err(e, "expert-parallel combine");
   const size_t rb = sizeof(float) * static_cast<size_t>(tokens) * ep->top_k;
   if (ids_out && tokens > 0) e = cudaMemcpyAsync(ids_out, ep->ids, rb, cudaMemcpyDeviceToDevice, st);

@@ -35,6 +35,8 @@ __global__ void __launch_bounds__(kGroupThreads) group_pairs_kernel(
     int n_experts, int skip_negative, int* __restrict__ counts, int* __restrict__ offsets,
     int* __restrict__ pair_token, float* __restrict__ pair_weight, int* __restrict__ token_pos,
     int* __restrict__ items, int items_max, unsigned* status) {
+  pdl_launch_dependents();  // launched as a programmatic dependent (launch_dependent):
+  pdl_wait_prior_grids();   // nothing is touched before the previous kernel completes
   __shared__ int cnt[kGroupThreads / 32][kMaxGroupExperts];
   __shared__ int base[kMaxGroupExperts];
   __shared__ int off[kMaxGroupExperts + 1];
@@ -929,14 +931,13 @@ cudaError_t launch_moe_prefill(int mode, const MoePrefillArgs& a, int sms, cudaS
     if (!a.route_given)
       launch_route(a.logits, T, E, k, a.normalize, a.scale, a.route_ids, a.route_weights,
                    a.status, sms, rs);
-    group_pairs_kernel<<<1, kGroupThreads, 0, rs>>>(a.route_ids, a.route_weights, T, k, E,
-                                                   a.skip_negative_ids, w.counts, w.offsets,
-                                                   w.pair_token, w.pair_weight, w.token_pos,
-                                                   path == Path::CudaCore ? nullptr : w.items,
-                                                   path == Path::TcMixed
-                                                       ? (small_group_rows(a) > 2 ? small_group_rows(a) : 2)
-                                                       : small_group_rows(a),
-                                                   a.status);
+    launch_dependent(group_pairs_kernel, dim3(1), dim3(kGroupThreads), 0, rs, a.route_ids,
+                     a.route_weights, T, k, E, static_cast<int>(a.skip_negative_ids), w.counts,
+                     w.offsets, w.pair_token, w.pair_weight, w.token_pos,
+                     path == Path::CudaCore ? nullptr : w.items,
+                     path == Path::TcMixed ? (small_group_rows(a) > 2 ? small_group_rows(a) : 2)
+                                           : small_group_rows(a),
+                     a.status);
   }
   if (a.skip_negative_ids && !a.skip_routed && path == Path::CudaCore) {
     // unused rows belong to no group and are never written by the projections:

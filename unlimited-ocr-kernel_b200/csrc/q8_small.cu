@@ -133,6 +133,8 @@ __global__ void __launch_bounds__(kSmThreads, 3)
                       const __grid_constant__ CUtensorMap tw2,  // single: second matrix
                       const __grid_constant__ CUtensorMap tws2,
                       const SmallArgs a) {
+  pdl_launch_dependents();  // launched as a programmatic dependent (launch_dependent):
+  pdl_wait_prior_grids();   // nothing is touched before the previous kernel completes
   constexpr int kStage = INT8 ? kSmStageI : kSmStageF;
   extern __shared__ unsigned char smem_raw[];
   // offset from the shared array itself: derived pointers stay shared-memory
@@ -421,10 +423,10 @@ cudaError_t launch_small_rows(bool int8, const void* maps, const Q8View* single,
   a.status = status;
   const dim3 grid((N / kSmRows) * (y2 ? 2 : 1), items ? max_items : chunks * groups);
   if (int8)
-    small_rows_kernel<true><<<grid, kSmThreads, kSmSmemI, st>>>(tw, tws, tx, txs, tw2, tws2, a);
-  else
-    small_rows_kernel<false><<<grid, kSmThreads, kSmSmemF, st>>>(tw, tws, tx, txs, tw2, tws2, a);
-  return cudaGetLastError();
+    return launch_dependent(small_rows_kernel<true>, grid, dim3(kSmThreads), kSmSmemI, st, tw, tws,
+                            tx, txs, tw2, tws2, a);
+  return launch_dependent(small_rows_kernel<false>, grid, dim3(kSmThreads), kSmSmemF, st, tw, tws,
+                          tx, txs, tw2, tws2, a);
 }
 
 }  // namespace uocr

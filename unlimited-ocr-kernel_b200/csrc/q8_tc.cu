@@ -799,6 +799,8 @@ __global__ void __launch_bounds__(kSplitThreads) split_rows_cta_kernel(
     const float* __restrict__ x, long long ld_x, const int* __restrict__ src,
     const float* __restrict__ u, int rows, int cols, uint16_t* __restrict__ pieces,
     float* __restrict__ rinv, long long piece_elems, const int* __restrict__ live) {
+  pdl_launch_dependents();  // launched as a programmatic dependent (launch_dependent):
+  pdl_wait_prior_grids();   // nothing is touched before the previous kernel completes
   __shared__ float wmax[kSplitThreads / 32];
   const int r = blockIdx.x;
   if (r >= rows || (live && r >= *live)) return;
@@ -1202,8 +1204,9 @@ void launch_split_rows(const float* x, long long ld_x, const int* src, int rows,
                        uint16_t* pieces, float* rinv, int sms, cudaStream_t st, const int* live) {
   if (rows <= 0) return;
   if (cols <= 4 * kSplitThreads * kSplitMaxV)
-    split_rows_cta_kernel<false><<<rows, kSplitThreads, 0, st>>>(
-        x, ld_x, src, nullptr, rows, cols, pieces, rinv, static_cast<long long>(rows) * cols, live);
+    launch_dependent(split_rows_cta_kernel<false>, dim3(rows), dim3(kSplitThreads), 0, st, x, ld_x,
+                     src, static_cast<const float*>(nullptr), rows, cols, pieces, rinv,
+                     static_cast<long long>(rows) * cols, live);
   else
     split_rows_kernel<<<grid_for(static_cast<long long>(rows) * 32, sms), 256, 0, st>>>(
         x, ld_x, src, rows, cols, pieces, rinv, static_cast<long long>(rows) * cols, live);
@@ -1213,8 +1216,9 @@ void launch_swiglu_split(const float* g, const float* u, int rows, int cols, uin
                          float* rinv, int sms, cudaStream_t st, const int* live) {
   if (rows <= 0) return;
   if (cols <= 4 * kSplitThreads * kSplitMaxV)
-    split_rows_cta_kernel<true><<<rows, kSplitThreads, 0, st>>>(
-        g, cols, nullptr, u, rows, cols, pieces, rinv, static_cast<long long>(rows) * cols, live);
+    launch_dependent(split_rows_cta_kernel<true>, dim3(rows), dim3(kSplitThreads), 0, st, g,
+                     static_cast<long long>(cols), static_cast<const int*>(nullptr), u, rows, cols,
+                     pieces, rinv, static_cast<long long>(rows) * cols, live);
   else
     swiglu_split_kernel<<<grid_for(static_cast<long long>(rows) * 32, sms), 256, 0, st>>>(
         g, u, rows, cols, pieces, rinv, static_cast<long long>(rows) * cols, live);
