@@ -198,6 +198,36 @@ def test_forward_single_rank_and_graph(ctx, layer4):
     ep.free()
 
 
+@pytest.mark.parametrize("mode", [0, 2])
+def test_forward_host_matches_device(ctx, layer4, mode):
+    """uocr_ep_forward_host at world 1, several calls in a row (different tokens
+    each time, pinned buffers copied directly or ordinary ones through the
+    staging mirror, two token counts): every call equals the device-buffer
+    forward on the same tokens, bit for bit."""
+    import torch
+    shared, experts, full = layer4
+    eps, locs = make_ranks(ctx, shared, experts, 1, 64)
+    ep = eps[0]
+    rng = np.random.default_rng(9 + mode)
+    for tokens, pinned in ((64, True), (64, True), (64, False), (64, True), (17, False), (17, True),
+                           (17, True)):
+        x = rng.standard_normal((tokens, 1280)).astype(np.float32)
+        lg = rng.standard_normal((tokens, 64)).astype(np.float32)
+        if pinned:
+            xh = torch.from_numpy(x).pin_memory()
+            lh = torch.from_numpy(lg).pin_memory()
+            yh = torch.empty_like(xh).pin_memory()
+            ep.forward_host_ptrs(xh.data_ptr(), lh.data_ptr(), tokens, yh.data_ptr(), mode)
+            y = yh.numpy()
+        else:
+            y = ep.forward(x, lg, mode)
+        ref = torch.empty((tokens, 1280), device="cuda")
+        ep.forward_device(torch.from_numpy(x).cuda(), torch.from_numpy(lg).cuda(), mode, ref)
+        ctx.sync()
+        assert np.array_equal(y.view(np.uint32), ref.cpu().numpy().view(np.uint32)), (tokens, pinned)
+    ep.free()
+
+
 def test_timeout_when_a_rank_never_dispatches(ctx):
     """A bounded wait that expires: rank 1 never dispatches, so rank 0's
     wait for its rows gives up after the limit and the next synchronising
