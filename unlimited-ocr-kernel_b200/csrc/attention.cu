@@ -63,6 +63,8 @@ __global__ void __launch_bounds__(kNormThreads)
     rms_norm_kernel(const float* x, long long ld_x, int width, const float* __restrict__ w,
                     float eps, float* out, long long ld_out, const float* res, float* sum,
                     unsigned* status) {
+  pdl_launch_dependents();  // launched as a programmatic dependent (launch_dependent):
+  pdl_wait_prior_grids();   // nothing is touched before the previous kernel completes
   extern __shared__ __align__(16) float sq[];  // width squares
   __shared__ float s_scale;
   const long long row = blockIdx.x;
@@ -108,8 +110,8 @@ void launch_rms_norm(const float* x, long long ld_x, int rows, int width, const 
   configured.run([] {
     cudaFuncSetAttribute(rms_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   });
-  rms_norm_kernel<<<rows, kNormThreads, smem, st>>>(x, ld_x, width, w, eps, out, ld_out, res, sum,
-                                                    status);
+  launch_dependent(rms_norm_kernel, dim3(rows), dim3(kNormThreads), smem, st, x, ld_x, width, w,
+                   eps, out, ld_out, res, sum, status);
 }
 
 // ---- rotary embedding ---------------------------------------------------------
@@ -214,6 +216,8 @@ __global__ void kv_rope_push_kernel(float* keys, float* values, int* state, cons
                                     int window, const float* __restrict__ qkv, float* q_out,
                                     const float2* __restrict__ table, int max_pos,
                                     unsigned* status) {
+  pdl_launch_dependents();  // launched as a programmatic dependent (launch_dependent):
+  pdl_wait_prior_grids();   // nothing is touched before the previous kernel completes
   const int b = blockIdx.x;
   const int prefix = state[2 * b], gen = state[2 * b + 1];
   if (prefix <= 0) {
@@ -259,8 +263,8 @@ void launch_kv_rope_push(float* keys, float* values, int* state, int batch, cons
                          int window, const float* qkv, float* q_out, const float2* table,
                          int max_pos, unsigned* status, cudaStream_t st) {
   if (batch <= 0) return;
-  kv_rope_push_kernel<<<batch, 256, 0, st>>>(keys, values, state, L, window, qkv, q_out, table,
-                                             max_pos, status);
+  launch_dependent(kv_rope_push_kernel, dim3(batch), dim3(256), 0, st, keys, values, state, L,
+                   window, qkv, q_out, table, max_pos, status);
 }
 
 // One block per token row: token-major [tokens][heads*dim] into the layout.
@@ -783,6 +787,7 @@ __global__ void __launch_bounds__(kSplitChunk) attn_split_scores_kernel(const At
   __shared__ __align__(16) float qs[256];
   const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   pdl_launch_dependents();  // the values kernel waits for this grid before reading scores
+  pdl_wait_prior_grids();   // launched as a programmatic dependent itself (launch_dependent)
   bool ok;
   const int T = split_tokens(a, b, &ok);
   if (!ok) {
@@ -988,8 +993,8 @@ cudaError_t launch_attention_split(const AttnArgs& a, int batch, int max_tokens,
                          static_cast<int>(kAttnMaxSmem));
   });
   const int chunks = (max_tokens + kSplitChunk - 1) / kSplitChunk;
-  attn_split_scores_kernel<<<dim3(chunks, a.heads, batch), kSplitChunk, 0, st>>>(a);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_dependent(attn_split_scores_kernel, dim3(chunks, a.heads, batch),
+                                   dim3(kSplitChunk), 0, st, a);
   if (e != cudaSuccess) return e;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -176,6 +176,10 @@ __host__ __device__ inline int bf16_x_stride(int k) { return k + 4; }  // floats
 __global__ void __launch_bounds__(kBf16Threads)
     linear_bf16_kernel(const uint16_t* __restrict__ w, int n, int k, const float* __restrict__ x,
                        int batch, float* y, int bulk, unsigned* status) {
+  // launched as a programmatic dependent (launch_dependent), nothing touched
+  // before the previous kernel completes; no early launch of its own dependents
+  // (the cooperative decode kernel that follows the router needs every SM)
+  pdl_wait_prior_grids();
   extern __shared__ __align__(16) unsigned char smem_b[];
   __shared__ __align__(8) uint64_t bar;
   const int kw = bf16_w_stride(k), kx = bf16_x_stride(k);
@@ -263,9 +267,9 @@ cudaError_t launch_linear_bf16(const uint16_t* w, int n, int k, const float* x, 
   configured.run([] {
     cudaFuncSetAttribute(linear_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   });
-  linear_bf16_kernel<<<dim3((n + kBf16Out - 1) / kBf16Out, (batch + kBf16Rows - 1) / kBf16Rows),
-                       kBf16Threads, smem, st>>>(w, n, k, x, batch, y, bulk, status);
-  return cudaGetLastError();
+  return launch_dependent(linear_bf16_kernel,
+                          dim3((n + kBf16Out - 1) / kBf16Out, (batch + kBf16Rows - 1) / kBf16Rows),
+                          dim3(kBf16Threads), smem, st, w, n, k, x, batch, y, bulk, status);
 }
 
 // ---- logits checksum -----------------------------------------------------------

@@ -105,6 +105,8 @@ struct GemvTmaParams {
 
 template <int MODE>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const __grid_constant__ GemvTmaParams p) {
+  pdl_launch_dependents();  // launched as a programmatic dependent (launch_dependent):
+  pdl_wait_prior_grids();   // nothing is touched before the previous kernel completes
   extern __shared__ __align__(128) unsigned char smem[];
   const int cols = p.cols, nb = cols >> 5, TR = p.tile_rows;
   const int w_bytes = TR * cols, s_bytes = TR * nb * 4;
@@ -264,7 +266,7 @@ static void launch_gemv_tma(const Q8View* mats, int n, const float* x, float* co
                          static_cast<int>(kGemvSmemLimit));
   });
   const int grid = tiles < sms ? tiles : sms;
-  gemv_tma_kernel<MODE><<<grid, kGemvThreads, smem, st>>>(p);
+  launch_dependent(gemv_tma_kernel<MODE>, dim3(grid), dim3(kGemvThreads), smem, st, p);
 }
 
 static void dispatch_gemv_tma(int mode, const Q8View* mats, int n, const float* x,
