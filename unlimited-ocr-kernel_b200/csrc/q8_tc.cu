@@ -261,8 +261,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           mma_i8(tmem + buf * kBM, smem_desc_sw128(st + 32 * j),
                  smem_desc_sw128(st + kABytes + 32 * j), kIdescI8);
-          mma_commit(&tfull[buf]);
         }
+        if (!ok) break;
+        // one commit for the stage's four blocks (a commit per block made
+        // this thread, not the tensor core, the limit): stage ks arrives on
+        // tfull[ks % 2]
+        mma_commit(&tfull[ks & 1]);
         mma_commit(&empty[s]);  // one of the slot's arrivals: its MMAs are done
       }
     }
@@ -293,7 +297,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (b + 1 < nbk) {
         const int b1 = b + 1, buf1 = b1 % kAccBufs, ks1 = b1 >> 2;
         if ((b1 & 3) == 0 && ok) ok = mbar_wait_try(&full[ks1 % kStages], (ks1 / kStages) & 1, a.status);
-        if (ok) ok = mbar_wait_try(&tfull[buf1], (b1 / kAccBufs) & 1, a.status);
+        // the four blocks of stage ks1 land together (one commit per stage,
+        // alternating between two barriers)
+        if ((b1 & 3) == 0 && ok) ok = mbar_wait_try(&tfull[ks1 & 1], (ks1 >> 1) & 1, a.status);
         tc_fence_after();
         tmem_ld16(tlane + buf1 * kBM, next);
       }
