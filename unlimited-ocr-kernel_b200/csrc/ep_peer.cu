@@ -211,9 +211,16 @@ __global__ void __launch_bounds__(kRdWarps * 32) ep_route_dispatch_kernel(
     unsigned* __restrict__ send_cnt) {
   extern __shared__ float rd_smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, k = d.top_k;
+  // up to 64 experts: the warp-collective form (route_row_warp64, the same
+  // IEEE sequence with the max, the selection and the sums on the warp's
+  // reductions instead of shared-memory loops); otherwise the general form
+  const bool warp64 = d.n_experts <= 64;  // top_k <= 8 (uocr_ep_create)
+  __shared__ __align__(16) float r64p[kRdWarps][64];
+  __shared__ int r64ids[kRdWarps][8], r64sorted[kRdWarps][8];
+  __shared__ float r64wts[kRdWarps][8], r64sorted_w[kRdWarps][8];
   float* p = rd_smem + warp * (d.n_experts + 2 * k);
-  int* sel = reinterpret_cast<int*>(p + d.n_experts);
-  float* sw = p + d.n_experts + k;
+  int* sel = warp64 ? r64ids[warp] : reinterpret_cast<int*>(p + d.n_experts);
+  float* sw = warp64 ? r64wts[warp] : p + d.n_experts + k;
   __shared__ unsigned cta_cnt[kEpMaxWorld], cta_base[kEpMaxWorld];
   const unsigned step = d.ctr[kCtrStep] + 1u;
   const int h4 = d.hidden >> 2;
@@ -228,8 +235,10 @@ __global__ void __launch_bounds__(kRdWarps * 32) ep_route_dispatch_kernel(
   bool ok = false;
   int e = 0, o = 0, local = 0;
   if (t < tokens) {
-    ok = route_row_warp(logits + static_cast<long long>(t) * d.n_experts, d.n_experts, k,
-                        normalize, scale, p, sel, sw, d.status);
+    const float* lrow = logits + static_cast<long long>(t) * d.n_experts;
+    ok = warp64 ? route_row_warp64(lrow, d.n_experts, k, normalize, scale, r64p[warp], sel, sw,
+                                   r64sorted[warp], r64sorted_w[warp], d.status)
+                : route_row_warp(lrow, d.n_experts, k, normalize, scale, p, sel, sw, d.status);
     for (int r = lane; r < k; r += 32) {
       ids[static_cast<long long>(t) * k + r] = ok ? sel[r] : -1;
       wts[static_cast<long long>(t) * k + r] = ok ? sw[r] : 0.0f;

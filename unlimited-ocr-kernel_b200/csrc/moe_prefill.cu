@@ -37,14 +37,16 @@ __global__ void __launch_bounds__(kGroupThreads) group_pairs_kernel(
     int* __restrict__ items, int items_max, unsigned* status) {
   pdl_launch_dependents();  // launched as a programmatic dependent (launch_dependent):
   pdl_wait_prior_grids();   // nothing is touched before the previous kernel completes
-  __shared__ int cnt[kGroupThreads / 32][kMaxGroupExperts];
+  // per-warp counts, padded so that a warp reading one expert's column (a
+  // lane per source warp) touches 32 banks
+  __shared__ int cnt[kGroupThreads / 32][kMaxGroupExperts + 1];
   __shared__ int base[kMaxGroupExperts];
   __shared__ int off[kMaxGroupExperts + 1];
   __shared__ int first[kMaxGroupExperts + 1];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int npairs = tokens * top_k;
   for (int e = tid; e < n_experts; e += blockDim.x) base[e] = 0;
-  for (int i = tid; i < (kGroupThreads / 32) * kMaxGroupExperts; i += blockDim.x)
+  for (int i = tid; i < (kGroupThreads / 32) * (kMaxGroupExperts + 1); i += blockDim.x)
     (&cnt[0][0])[i] = 0;
   __syncthreads();
   // pass 1: histogram
@@ -58,24 +60,50 @@ __global__ void __launch_bounds__(kGroupThreads) group_pairs_kernel(
     atomicAdd(&base[e], 1);
   }
   __syncthreads();
-  if (tid == 0) {
-    int run = 0;
-    for (int e = 0; e < n_experts; ++e) {
-      off[e] = run;
-      counts[e] = base[e];
-      offsets[e] = run;
-      run += base[e];
-      base[e] = 0;
+  if (warp == 0) {
+    // exclusive prefix sums over the experts of the group sizes and of the
+    // groups' 8-row chunk counts (first list position of each group's chunks;
+    // groups of more than items_max rows have none: the tensor-core GEMMs).
+    // Lane l sums experts [8l, 8l + 8) in order, a warp scan adds the lanes.
+    constexpr int kPer = kMaxGroupExperts / 32;
+    int c[kPer];
+    int s = 0, sc = 0;
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int e = kPer * lane + u;
+      c[u] = e < n_experts ? base[e] : 0;
+      s += c[u];
+      sc += c[u] <= items_max ? (c[u] + 7) / 8 : 0;
     }
-    off[n_experts] = run;
-    offsets[n_experts] = run;
-    int chunks = 0;  // first list position of each group's 8-row chunks
-    for (int e = 0; e < n_experts; ++e) {
-      first[e] = chunks;
-      const int c = off[e + 1] - off[e];
-      if (c <= items_max) chunks += (c + 7) / 8;  // larger groups: the tensor-core GEMMs
+    int is = s, isc = sc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, is, o);
+      const int w = __shfl_up_sync(0xffffffffu, isc, o);
+      if (lane >= o) {
+        is += v;
+        isc += w;
+      }
     }
-    first[n_experts] = chunks;
+    int run = is - s, chunks = isc - sc;
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int e = kPer * lane + u;
+      if (e < n_experts) {
+        off[e] = run;
+        counts[e] = c[u];
+        offsets[e] = run;
+        first[e] = chunks;
+        base[e] = 0;
+      }
+      run += c[u];
+      chunks += c[u] <= items_max ? (c[u] + 7) / 8 : 0;
+    }
+    if (lane == 31) {  // the totals
+      off[n_experts] = is;
+      offsets[n_experts] = is;
+      first[n_experts] = isc;
+    }
   }
   __syncthreads();
   if (items) {
@@ -96,14 +124,20 @@ __global__ void __launch_bounds__(kGroupThreads) group_pairs_kernel(
     const int rank = __popc(peers & ((1u << lane) - 1));
     if (valid && rank == 0) cnt[warp][e] = __popc(peers);
     __syncthreads();
-    for (int x = tid; x < n_experts; x += blockDim.x) {
-      int run = base[x];
-      for (int w = 0; w < kGroupThreads / 32; ++w) {
-        const int v = cnt[w][x];
-        cnt[w][x] = run;
-        run += v;
+    // expert x's running base over the warps in order: a warp per expert,
+    // lane w holding warp w's count, an exclusive warp scan
+    for (int x = warp; x < n_experts; x += kGroupThreads / 32) {
+      const int v = cnt[lane][x];
+      const int b = base[x];
+      int inc = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += u;
       }
-      base[x] = run;
+      cnt[lane][x] = b + inc - v;
+      __syncwarp();
+      if (lane == 31) base[x] = b + inc;
     }
     __syncthreads();
     if (valid) {
