@@ -787,6 +787,14 @@ __global__ void __launch_bounds__(kSplitChunk) attn_split_scores_kernel(const At
   __shared__ __align__(16) float qs[256];
   const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   pdl_launch_dependents();  // the values kernel waits for this grid before reading scores
+  if (threadIdx.x == 0 && a.tiled) {
+    // this chunk's keys (contiguous in the tiled layout) into L2 while the
+    // push finishes (prefetch_l2_bulk: safe before the wait)
+    const int t0 = c * kSplitChunk, t1 = min(t0 + kSplitChunk, static_cast<int>(a.cap));
+    if (t1 > t0)
+      prefetch_l2_bulk(a.keys + b * a.seq_stride + h * a.head_stride + static_cast<long long>(t0) * a.dim,
+                       static_cast<uint32_t>(t1 - t0) * a.dim * 4);
+  }
   pdl_wait_prior_grids();   // launched as a programmatic dependent itself (launch_dependent)
   bool ok;
   const int T = split_tokens(a, b, &ok);
@@ -857,6 +865,21 @@ __global__ void __launch_bounds__(kSplitThreads) attn_split_values_kernel(const 
   const int j = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nb = a.dim >> 5;
+  const float* vh = a.values + b * a.seq_stride + h * a.head_stride;
+  // This kernel may start while the cache push two launches back is still
+  // running (the scores kernel between them lets it launch before waiting for
+  // the push itself), so nothing of the cache is read before the wait.  Before
+  // it, the slice's value sub-blocks only go into L2 (prefetch_l2_bulk), sized
+  // by a state read that may predate the push (L2-only load, not reused).
+  if (warp == 3 && lane == 0 && a.state && a.cap >= 32) {
+    const int prefix = __ldcg(a.state + 2 * b), gen = __ldcg(a.state + 2 * b + 1);
+    const int t_est = prefix + (gen < a.window ? gen : a.window) + 1;
+    const int n0 = prefix > 0 ? min((t_est + 31) >> 5, static_cast<int>(a.cap >> 5)) : 0;
+    for (int it = 0; it < n0; ++it)
+      prefetch_l2_bulk(vh + (static_cast<long long>(it) * nb + j) * 1024, kSplitSubBytes);
+  }
+  // the scores grid has completed, and with it the push it waited for
+  pdl_wait_prior_grids();
   bool ok;
   const int T = split_tokens(a, b, &ok);
   if (!ok) return;  // flagged by the scores kernel
@@ -870,10 +893,8 @@ __global__ void __launch_bounds__(kSplitThreads) attn_split_values_kernel(const 
   }
   __syncthreads();
   if (warp == 3) {
-    // ---- producer: the slice's sub-blocks in token order (written by the
-    // cache kernels before the scores kernel, so readable before its end)
+    // ---- producer: the slice's sub-blocks in token order
     if (lane == 0) {
-      const float* vh = a.values + b * a.seq_stride + h * a.head_stride;
       int it = 0;
       for (; it < ntiles; ++it) {
         const int st = it % kSplitStages;
@@ -890,7 +911,6 @@ __global__ void __launch_bounds__(kSplitThreads) attn_split_values_kernel(const 
     return;
   }
   // ---- softmax_backend (src/cpu/ops.rs:139-187) over the scores
-  pdl_wait_prior_grids();
   // the scores row (16-byte aligned: cap is a multiple of 32), four 16-byte
   // loads in flight per thread
   const float4* src4 =

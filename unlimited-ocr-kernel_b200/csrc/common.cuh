@@ -427,6 +427,16 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Bulk prefetch of [p, p + bytes) into L2 (p 16-byte aligned, bytes a
+// multiple of 16).  Issued before pdl_wait_prior_grids() by kernels whose
+// first tiles are weights or cached keys: the fetch overlaps the previous
+// kernel's tail.  It is safe even when the previous kernel writes those
+// bytes: L2 is where every store of the GPU lands, so a line fetched early is
+// updated by such a store, and the kernel reads it only after the wait.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // Reference quantizer element (src/cpu/quantized.rs:64-69): 0 for a zero
 // scale, else clamp(round_half_even(v / scale), -127, 127).
 __device__ __forceinline__ int8_t quantize_elem(float v, float scale) {
