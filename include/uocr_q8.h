@@ -112,7 +112,9 @@ int uocr_q8_from_parts(uocr_ctx *ctx, size_t rows, size_t cols, const int8_t *we
                        uocr_q8 **out);
 /* Same validation for device-resident storage; the handle borrows (does not
  * free) the memory.  Scale validation runs on the device and is reported
- * synchronously. */
+ * synchronously.  Like Int8Matrix, the matrix is immutable: the memory must
+ * not be written while the handle lives (the one-token MoE kernel starts
+ * streaming weights before the previous kernel in the stream has finished). */
 int uocr_q8_from_device(uocr_ctx *ctx, size_t rows, size_t cols, const int8_t *weights_dev,
                         const float *scales_dev, uocr_q8 **out);
 /* Int8Matrix::quantize (:43-74) of a host float matrix, on the device. */

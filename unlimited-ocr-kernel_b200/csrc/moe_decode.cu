@@ -372,7 +372,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const __grid_co
       bulk_g2s(smem + L.w_off(u), dm.w + static_cast<long long>(i0) * K, nr * K, down_bar);
       bulk_g2s(smem + L.s_off(u), dm.s + static_cast<long long>(i0) * nbK, nr * nbK * 4, down_bar);
     };
-    // Token-independent copies first.
+    // Token-independent copies first, before any wait for the previous
+    // kernel: the descriptor table and the weights are written only when the
+    // layer and its matrices are created (matrices are immutable while their
+    // handles live), never by a kernel this launch may overlap.
     const int desc_bytes = a.n_experts * static_cast<int>(sizeof(FfnView));
     mbar_arrive_expect_tx(desc_bar, desc_bytes);
     bulk_g2s(edesc, a.experts, desc_bytes, desc_bar);
