@@ -56,7 +56,12 @@ constexpr int kBBytes = kBM * kBK;     // 8 KB activations
 constexpr int kWsBytes = kBN * 4 * 4;  // weight scales [128][4]
 constexpr int kXsBytes = kBM * 4 * 4;  // activation scales [64][4]
 constexpr int kStageBytes = kABytes + kBBytes + kWsBytes + kXsBytes;  // 27 KB (1024-multiple)
-constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*alignment*/ + 512 /*barriers*/;
+// Persistent CTAs: one per SM walks a list of tiles (at most kMaxCtaTiles,
+// {group, first row, rows, first weight row} each, built once per CTA).
+constexpr int kMaxCtaTiles = 128;
+constexpr int kTileListBytes = kMaxCtaTiles * 16;
+constexpr int kSmemBytes =
+    kStages * kStageBytes + 1024 /*alignment*/ + 512 /*barriers*/ + kTileListBytes;
 static_assert(kStageBytes % 1024 == 0, "swizzled tiles need 1024-byte alignment");
 
 
@@ -158,6 +163,17 @@ constexpr uint32_t kIdescI8 = (2u << 4)               // D format: s32
                               | ((kBN >> 4) << 24);   // M
 
 // ---- the kernel --------------------------------------------------------------
+// Persistent: CTA c takes the tiles c, c + gridDim.x, c + 2 gridDim.x, ... of
+// the linear order L = (row tile) * (N / kBN) + (weight tile), so that the
+// CTAs working at the same time share activation tiles and a group's weight
+// tiles.  The TMA ring, the MMA's TMEM buffers and the epilogue's block
+// sequence all run on across tile boundaries: a tile's first stages load while
+// the previous tile's last blocks are applied, and the pipeline fills once per
+// CTA instead of once per tile.
+struct TileRef {
+  int group, row0, rows, n0;
+};
+
 __global__ void __launch_bounds__(kThreads, 1)
     q8_tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
                          const __grid_constant__ CUtensorMap tmap_ws,
@@ -172,41 +188,53 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + kAccBufs;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + kAccBufs);
-  int* tile = reinterpret_cast<int*>(tmem_holder + 1);  // group, first row, rows
+  int* ntiles_s = reinterpret_cast<int*>(tmem_holder + 1);
+  TileRef* tiles = reinterpret_cast<TileRef*>(smem + kStages * kStageBytes + 512);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kBN;
+  const int ntn = a.N / kBN;
   const int nbk = a.K >> 5, kstages = a.K / kBK;
-  // this CTA's 64-row tile: blockIdx.y counts tiles over the groups in order.
   // The group counts are copied to shared memory by all threads first (one
-  // thread walking them in global memory pays an L2 round trip per group).
-  int* scount = reinterpret_cast<int*>(smem);  // the ring, before any copy lands there
+  // thread walking them in global memory pays an L2 round trip per group),
+  // into the ring, before any copy lands there.
+  int* scount = reinterpret_cast<int*>(smem);
   if (a.counts)
     for (int g = threadIdx.x; g < a.groups; g += blockDim.x) scount[g] = a.counts[g];
   __syncthreads();
   if (threadIdx.x == 0) {
-    int g = 0, r0 = blockIdx.y * kBM, rows = a.M - blockIdx.y * kBM;
-    if (a.counts) {
-      int t = blockIdx.y;
-      rows = 0;
-      for (g = 0; g < a.groups; ++g) {
-        const int c = scount[g], tiles = (c + kBM - 1) / kBM;
-        if (t < tiles) {
-          r0 = a.offsets[g] + t * kBM;
-          rows = c - t * kBM;
-          break;
+    // this CTA's tiles in order; the row tiles of the groups are numbered
+    // group by group (a group of c rows has ceil(c / kBM) of them)
+    int n = 0, g = 0, before = 0;  // `before`: row tiles of the groups before g
+    const int single_tiles = (a.M + kBM - 1) / kBM;
+    for (long long L = blockIdx.x; n < kMaxCtaTiles; L += gridDim.x) {
+      const int ty = static_cast<int>(L / ntn), nx = static_cast<int>(L % ntn);
+      int grp = 0, r0, rows;
+      if (a.counts) {
+        while (g < a.groups && ty >= before + (scount[g] + kBM - 1) / kBM) {
+          before += (scount[g] + kBM - 1) / kBM;
+          ++g;
         }
-        t -= tiles;
+        if (g >= a.groups) break;
+        grp = g;
+        r0 = a.offsets[g] + (ty - before) * kBM;
+        rows = scount[g] - (ty - before) * kBM;
+      } else {
+        if (ty >= single_tiles) break;
+        r0 = ty * kBM;
+        rows = a.M - r0;
       }
+      tiles[n].group = grp;
+      tiles[n].row0 = r0;
+      tiles[n].rows = rows > kBM ? kBM : rows;
+      tiles[n].n0 = nx * kBN;
+      ++n;
     }
-    tile[0] = g;
-    tile[1] = r0;
-    tile[2] = rows > kBM ? kBM : rows;
+    *ntiles_s = n;
   }
   fence_proxy_async_smem();  // the scratch reads come before the copies that overwrite it
   __syncthreads();
-  const int group = tile[0], row0 = tile[1], rows = tile[2];
-  if (rows <= 0) return;  // past the last tile (the grid is an upper bound)
+  const int ntiles = *ntiles_s;
+  if (ntiles == 0) return;  // nothing for this CTA (the grid is an upper bound)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -224,21 +252,30 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  // stages and blocks are counted over the CTA's whole tile sequence: stage
+  // gs = i * kstages + ks of tile i, block gb = 4 gs + j
+  const int total_stages = ntiles * kstages;
 
   if (warp == 0) {
     // ---- TMA producer: operands and their block scales, one barrier a stage
     if (lane == 0) {
-      const CUtensorMap* wmap = a.counts ? &a.maps[group].w_sw128 : &tmap_w;
-      const CUtensorMap* smap = a.counts ? &a.maps[group].ws : &tmap_ws;
-      for (int ks = 0; ks < kstages; ++ks) {
-        const int s = ks % kStages;
-        if (ks >= kStages && !mbar_wait_try(&empty[s], ((ks / kStages) - 1) & 1, a.status)) break;
+      int i = 0, ks = 0;
+      for (int gs = 0; gs < total_stages; ++gs) {
+        const int s = gs % kStages;
+        if (gs >= kStages && !mbar_wait_try(&empty[s], ((gs / kStages) - 1) & 1, a.status)) break;
+        const TileRef t = tiles[i];
+        const CUtensorMap* wmap = a.counts ? &a.maps[t.group].w_sw128 : &tmap_w;
+        const CUtensorMap* smap = a.counts ? &a.maps[t.group].ws : &tmap_ws;
         unsigned char* st = smem + s * kStageBytes;
         mbar_arrive_expect_tx(&full[s], kStageBytes);
-        tma_load_2d(st, wmap, ks * kBK, n0, &full[s]);
-        tma_load_2d(st + kABytes, &tmap_x, ks * kBK, row0, &full[s]);
-        tma_load_2d(st + kABytes + kBBytes, smap, 4 * ks, n0, &full[s]);
-        tma_load_2d(st + kABytes + kBBytes + kWsBytes, &tmap_xs, 4 * ks, row0, &full[s]);
+        tma_load_2d(st, wmap, ks * kBK, t.n0, &full[s]);
+        tma_load_2d(st + kABytes, &tmap_x, ks * kBK, t.row0, &full[s]);
+        tma_load_2d(st + kABytes + kBBytes, smap, 4 * ks, t.n0, &full[s]);
+        tma_load_2d(st + kABytes + kBBytes + kWsBytes, &tmap_xs, 4 * ks, t.row0, &full[s]);
+        if (++ks == kstages) {
+          ks = 0;
+          ++i;
+        }
       }
     }
   } else if (warp == 1) {
@@ -246,9 +283,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int blk = 0;
       bool ok = true;
-      for (int ks = 0; ks < kstages && ok; ++ks) {
-        const int s = ks % kStages;
-        ok = mbar_wait_try(&full[s], (ks / kStages) & 1, a.status);
+      for (int gs = 0; gs < total_stages && ok; ++gs) {
+        const int s = gs % kStages;
+        ok = mbar_wait_try(&full[s], (gs / kStages) & 1, a.status);
         if (!ok) break;
         tc_fence_after();
         const unsigned char* st = smem + s * kStageBytes;
@@ -264,9 +301,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         // one commit for the stage's four blocks (a commit per block made
-        // this thread, not the tensor core, the limit): stage ks arrives on
-        // tfull[ks % 2]
-        mma_commit(&tfull[ks & 1]);
+        // this thread, not the tensor core, the limit): stage gs arrives on
+        // tfull[gs % 2]
+        mma_commit(&tfull[gs & 1]);
         mma_commit(&empty[s]);  // one of the slot's arrivals: its MMAs are done
       }
     }
@@ -275,8 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // may access) and kEpiCols of the 64 columns; one weight row per thread.
     // The TMEM load of block b + 1 is in flight while block b is applied.
     const int q = warp & 3, part = (warp - 2) / 4;
-    const int rl = 32 * q + lane, n = n0 + rl, c0 = kEpiCols * part;
-    const bool row_ok = n < a.N;
+    const int rl = 32 * q + lane, c0 = kEpiCols * part;
     const uint32_t tlane = tmem + (static_cast<uint32_t>(32 * q) << 16) + c0;
     // running sums of two neighbouring columns per register pair: the
     // conversion and the two products run as packed f32x2 instructions (each
@@ -286,27 +322,34 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int i = 0; i < kEpiCols / 2; ++i) acc[i] = make_float2(-0.0f, -0.0f);
     bool ok = true;
-    // Block b: its S values are in `now`; start loading block b + 1 into
-    // `next`, apply block b, then wait for the load.  Called with the two
-    // register sets alternating, so no copies are needed.
-    auto step = [&](uint32_t (&now)[kEpiCols], uint32_t (&next)[kEpiCols], int b) {
-      const int buf = b % kAccBufs, ks = b >> 2, jb = b & 3, s = ks % kStages;
+    const int total_blocks = ntiles * nbk;
+    int rows = 0;  // the current tile's activation rows
+    float4 ws4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);  // this row's scales of the stage's blocks
+    // Block gb: its S values are in `now`; start loading block gb + 1 into
+    // `next` (across a tile boundary too), apply block gb, then wait for the
+    // load.  Called with the two register sets alternating, so no copies are
+    // needed.
+    // (jb = gb % 4 is passed as a literal, so that the scale selection and
+    // the stage-boundary branches fold)
+    auto step = [&](uint32_t (&now)[kEpiCols], uint32_t (&next)[kEpiCols], int gb, int jb) {
+      const int buf = gb % kAccBufs, gks = gb >> 2, s = gks % kStages;
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[buf]);  // block b is in registers
-      if (b + 1 < nbk) {
-        const int b1 = b + 1, buf1 = b1 % kAccBufs, ks1 = b1 >> 2;
-        if ((b1 & 3) == 0 && ok) ok = mbar_wait_try(&full[ks1 % kStages], (ks1 / kStages) & 1, a.status);
+      if (lane == 0) mbar_arrive(&tempty[buf]);  // block gb is in registers
+      if (gb + 1 < total_blocks) {
+        const int b1 = gb + 1, buf1 = b1 % kAccBufs, ks1 = b1 >> 2;
+        if (jb == 3 && ok) ok = mbar_wait_try(&full[ks1 % kStages], (ks1 / kStages) & 1, a.status);
         // the four blocks of stage ks1 land together (one commit per stage,
         // alternating between two barriers)
-        if ((b1 & 3) == 0 && ok) ok = mbar_wait_try(&tfull[ks1 & 1], (ks1 >> 1) & 1, a.status);
+        if (jb == 3 && ok) ok = mbar_wait_try(&tfull[ks1 & 1], (ks1 >> 1) & 1, a.status);
         tc_fence_after();
         tmem_ld16(tlane + buf1 * kBM, next);
       }
       const unsigned char* st = smem + s * kStageBytes;
-      const float* ws_s = reinterpret_cast<const float*>(st + kABytes + kBBytes);  // [128][4]
       const float* xs_s = reinterpret_cast<const float*>(st + kABytes + kBBytes + kWsBytes);  // [64][4]
-      const float wsb = ws_s[4 * rl + jb];
+      if (jb == 0)  // the weight row's scales of the stage's four blocks, one load
+        ws4 = *reinterpret_cast<const float4*>(st + kABytes + kBBytes + 16 * rl);
+      const float wsb = jb == 0 ? ws4.x : jb == 1 ? ws4.y : jb == 2 ? ws4.z : ws4.w;
       const float2 ws2 = make_float2(wsb, wsb);
       const float2 magic = make_float2(-12582912.0f, -12582912.0f);
       // columns past the tile's last row are padding: nothing to apply
@@ -330,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the slot's scales
       }
-      if (b + 1 < nbk) tmem_ld_wait(next);
+      if (gb + 1 < total_blocks) tmem_ld_wait(next);
     };
     uint32_t ra[kEpiCols], rb[kEpiCols];
     // block 0: its stage and its TMEM buffer
@@ -338,15 +381,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_ld16(tlane, ra);
     tmem_ld_wait(ra);
-    for (int b = 0; b < nbk; b += 2) {  // nbk is a multiple of 4
-      step(ra, rb, b);
-      step(rb, ra, b + 1);
-    }
-    if (row_ok) {
+    for (int ti = 0, gb0 = 0; ti < ntiles; ++ti, gb0 += nbk) {
+      const TileRef t = tiles[ti];
+      rows = t.rows;
+      // nbk is a multiple of 4: every tile starts with its first block in ra
+      for (int b = 0; b < nbk; b += 4) {
+        step(ra, rb, gb0 + b, 0);
+        step(rb, ra, gb0 + b + 1, 1);
+        step(ra, rb, gb0 + b + 2, 2);
+        step(rb, ra, gb0 + b + 3, 3);
+      }
+      // the tile's outputs, then the next tile's sums from -0.0
+      const int n = t.n0 + rl;
+      if (n < a.N) {
 #pragma unroll
-      for (int i = 0; i < kEpiCols; ++i)
-        if (c0 + i < rows)
-          a.y[static_cast<long long>(row0 + c0 + i) * a.ldy + n] = (i & 1) ? acc[i / 2].y : acc[i / 2].x;
+        for (int i = 0; i < kEpiCols; ++i)
+          if (c0 + i < t.rows)
+            a.y[static_cast<long long>(t.row0 + c0 + i) * a.ldy + n] =
+                (i & 1) ? acc[i / 2].y : acc[i / 2].x;
+      }
+#pragma unroll
+      for (int i = 0; i < kEpiCols / 2; ++i) acc[i] = make_float2(-0.0f, -0.0f);
     }
   }
   tc_fence_before();
@@ -356,7 +411,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_dealloc(tmem, kTmemCols);
   }
 }
-
 
 // ---- FP32 activations ------------------------------------------------------------
 // Int8Matrix::linear for many rows (src/cpu/quantized.rs:101-153; for a batch
@@ -911,6 +965,22 @@ void configure() {
 
 bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
 
+// Grid of the persistent int8 kernel for `tiles` (an upper bound on the
+// tiles): one CTA per SM, more only if a CTA would otherwise own more than
+// kMaxCtaTiles tiles.
+int persistent_grid(long long tiles) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) {
+    cudaGetLastError();
+    sms = 148;
+  }
+  long long g = tiles < sms ? tiles : sms;
+  if (g < 1) g = 1;
+  if ((tiles + g - 1) / g > kMaxCtaTiles) g = (tiles + kMaxCtaTiles - 1) / kMaxCtaTiles;
+  return static_cast<int>(g);
+}
+
 // ---- BF16 weights, FP32 activations (ops::linear_weight, BF16 branch) ---------
 // y[m][n] = sum_k x[m][k] * w[n][k] for a large BF16 weight (the lm_head,
 // 129,280 x 1280 at a decode batch of 64).  The weights need no conversion:
@@ -1116,8 +1186,8 @@ cudaError_t launch_q8_tc_single_i8(const Q8View& m, const int8_t* xq, const floa
   a.K = K;
   a.ldy = static_cast<int>(ldy);
   a.status = status;
-  q8_tc_gemm_i8_kernel<<<dim3(N / kBN, (batch + kBM - 1) / kBM), kThreads, kSmemBytes, st>>>(
-      mm.w_sw128, mm.ws, tx, txs, a);
+  q8_tc_gemm_i8_kernel<<<persistent_grid(static_cast<long long>(N / kBN) * ((batch + kBM - 1) / kBM)),
+                         kThreads, kSmemBytes, st>>>(mm.w_sw128, mm.ws, tx, txs, a);
   return cudaGetLastError();
 }
 
@@ -1144,7 +1214,8 @@ cudaError_t launch_q8_tc_grouped_i8(const void* maps, int groups, const int* cou
   a.ldy = static_cast<int>(ldy);
   a.status = status;
   // the weight-map parameters are unused when grouped (the maps array is)
-  q8_tc_gemm_i8_kernel<<<dim3(N / kBN, max_tiles), kThreads, kSmemBytes, st>>>(tx, txs, tx, txs, a);
+  q8_tc_gemm_i8_kernel<<<persistent_grid(static_cast<long long>(N / kBN) * max_tiles), kThreads,
+                         kSmemBytes, st>>>(tx, txs, tx, txs, a);
   return cudaGetLastError();
 }
 
