@@ -50,7 +50,10 @@ constexpr int kAccBufs = 8;    // TMEM buffers of kBM columns: all of TMEM (one 
 constexpr int kTmemCols = kAccBufs * kBM;  // 512
 constexpr int kEpiWarps = 16;  // four per TMEM lane quarter, 16 columns each
 constexpr int kEpiCols = kBM / (kEpiWarps / 4);
-constexpr int kThreads = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, epilogue
+// warp 0 TMA, warp 1 MMA, warps 2 .. 2 + kEpiWarps - 1 epilogue, then one warp
+// that writes each stage's activation-scale tile transposed ([block][row])
+constexpr int kThreads = 64 + 32 * kEpiWarps + 32;
+constexpr int kXposeWarp = 2 + kEpiWarps;
 constexpr int kABytes = kBN * kBK;     // 16 KB weights
 constexpr int kBBytes = kBM * kBK;     // 8 KB activations
 constexpr int kWsBytes = kBN * 4 * 4;  // weight scales [128][4]
@@ -60,8 +63,9 @@ constexpr int kStageBytes = kABytes + kBBytes + kWsBytes + kXsBytes;  // 27 KB (
 // {group, first row, rows, first weight row} each, built once per CTA).
 constexpr int kMaxCtaTiles = 128;
 constexpr int kTileListBytes = kMaxCtaTiles * 16;
-constexpr int kSmemBytes =
-    kStages * kStageBytes + 1024 /*alignment*/ + 512 /*barriers*/ + kTileListBytes;
+constexpr int kXsTBytes = kStages * kXsBytes;  // the transposed scale tiles, one per stage
+constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*alignment*/ + 512 /*barriers*/ +
+                           kTileListBytes + kXsTBytes;
 static_assert(kStageBytes % 1024 == 0, "swizzled tiles need 1024-byte alignment");
 
 
@@ -187,9 +191,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + kAccBufs;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + kAccBufs);
+  uint64_t* xsready = tempty + kAccBufs;  // stage's transposed scales written
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(xsready + kStages);
   int* ntiles_s = reinterpret_cast<int*>(tmem_holder + 1);
   TileRef* tiles = reinterpret_cast<TileRef*>(smem + kStages * kStageBytes + 512);
+  float* xs_t = reinterpret_cast<float*>(smem + kStages * kStageBytes + 512 + kTileListBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntn = a.N / kBN;
@@ -245,6 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], kEpiWarps);
     }
+    for (int s = 0; s < kStages; ++s) mbar_init(&xsready[s], 1);
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(tmem_holder, kTmemCols);
@@ -307,6 +314,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(&empty[s]);  // one of the slot's arrivals: its MMAs are done
       }
     }
+  } else if (warp == kXposeWarp) {
+    // ---- the stage's activation scales [64 rows][4 blocks] rewritten as
+    // [4 blocks][64 rows], so that an epilogue thread loads its 16 columns'
+    // scales of a block with four 16-byte loads.  The slot's next refill waits
+    // for the epilogue, which waits for this (xsready), so the tile is read
+    // here before it is overwritten, and xs_t[s] before it is rewritten.
+    bool ok = true;
+    for (int gs = 0; gs < total_stages && ok; ++gs) {
+      const int s = gs % kStages;
+      ok = mbar_wait_try(&full[s], (gs / kStages) & 1, a.status);
+      const float4* src =
+          reinterpret_cast<const float4*>(smem + s * kStageBytes + kABytes + kBBytes + kWsBytes);
+      float* dst = xs_t + s * (kXsBytes / 4);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int r = lane + 32 * h;
+        const float4 v = src[r];
+        dst[r] = v.x;
+        dst[64 + r] = v.y;
+        dst[128 + r] = v.z;
+        dst[192 + r] = v.w;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xsready[s]);
+    }
   } else {
     // ---- epilogue: warp w reads TMEM lanes 32*(w % 4) .. + 31 (the rows it
     // may access) and kEpiCols of the 64 columns; one weight row per thread.
@@ -339,6 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (gb + 1 < total_blocks) {
         const int b1 = gb + 1, buf1 = b1 % kAccBufs, ks1 = b1 >> 2;
         if (jb == 3 && ok) ok = mbar_wait_try(&full[ks1 % kStages], (ks1 / kStages) & 1, a.status);
+        if (jb == 3 && ok) ok = mbar_wait_try(&xsready[ks1 % kStages], (ks1 / kStages) & 1, a.status);
         // the four blocks of stage ks1 land together (one commit per stage,
         // alternating between two barriers)
         if (jb == 3 && ok) ok = mbar_wait_try(&tfull[ks1 & 1], (ks1 >> 1) & 1, a.status);
@@ -346,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld16(tlane + buf1 * kBM, next);
       }
       const unsigned char* st = smem + s * kStageBytes;
-      const float* xs_s = reinterpret_cast<const float*>(st + kABytes + kBBytes + kWsBytes);  // [64][4]
+      const float4* xs4 = reinterpret_cast<const float4*>(xs_t + s * (kXsBytes / 4) + 64 * jb + c0);
       if (jb == 0)  // the weight row's scales of the stage's four blocks, one load
         ws4 = *reinterpret_cast<const float4*>(st + kABytes + kBBytes + 16 * rl);
       const float wsb = jb == 0 ? ws4.x : jb == 1 ? ws4.y : jb == 2 ? ws4.z : ws4.w;
@@ -354,9 +387,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float2 magic = make_float2(-12582912.0f, -12582912.0f);
       // columns past the tile's last row are padding: nothing to apply
       // (the warp still takes part in every barrier)
+      float4 xv[kEpiCols / 4];
+      if (c0 < rows) {
+#pragma unroll
+        for (int u = 0; u < kEpiCols / 4; ++u) xv[u] = xs4[u];
+      }
 #pragma unroll
       for (int c = 0; c < kEpiCols && c0 < rows; c += 2) {
-        const float2 xs2 = make_float2(xs_s[4 * (c0 + c) + jb], xs_s[4 * (c0 + c + 1) + jb]);
+        const float4 x4 = xv[c / 4];
+        const float2 xs2 = (c & 2) ? make_float2(x4.z, x4.w) : make_float2(x4.x, x4.y);
         // exact int32 -> float: |S| < 2^22 (32 * 127 * 127), 2^23 + 2^22 + S
         // minus 2^23 + 2^22
         const float2 sf =
@@ -377,7 +416,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     uint32_t ra[kEpiCols], rb[kEpiCols];
     // block 0: its stage and its TMEM buffer
-    ok = mbar_wait_try(&full[0], 0, a.status) && mbar_wait_try(&tfull[0], 0, a.status);
+    ok = mbar_wait_try(&full[0], 0, a.status) && mbar_wait_try(&xsready[0], 0, a.status) &&
+         mbar_wait_try(&tfull[0], 0, a.status);
     tc_fence_after();
     tmem_ld16(tlane, ra);
     tmem_ld_wait(ra);
