@@ -735,9 +735,12 @@ __global__ void __launch_bounds__(kFThreads, 1)
     const bool active = c0 < rows;  // warp-uniform
     const uint32_t tlane = tmem + (static_cast<uint32_t>(32 * q) << 16) + c0;
     const float* srow = (a.counts ? a.maps[group].s : a.s) + static_cast<long long>(n) * nbk;
-    float acc[kEpiCols];
+    // two neighbouring columns per register pair: the piece sums and the
+    // scale fma run as packed f32x2 instructions, each lane rounded as the
+    // scalar operation
+    float2 acc[kEpiCols / 2];
 #pragma unroll
-    for (int i = 0; i < kEpiCols; ++i) acc[i] = 0.0f;
+    for (int i = 0; i < kEpiCols / 2; ++i) acc[i] = make_float2(0.0f, 0.0f);
     bool ok = true;
     int buf = 0, sl = 0, lap = 0;
     for (int b = 0; b < nbk; ++b) {
@@ -757,8 +760,12 @@ __global__ void __launch_bounds__(kFThreads, 1)
         tmem_ld_wait(ra);
         tmem_ld_wait(rb);
 #pragma unroll
-        for (int c = 0; c < kEpiCols; ++c)
-          ra[c] = __float_as_uint(__fadd_rn(__uint_as_float(ra[c]), __uint_as_float(rb[c])));
+        for (int c = 0; c < kEpiCols; c += 2) {
+          const float2 t = f2_add(make_float2(__uint_as_float(ra[c]), __uint_as_float(ra[c + 1])),
+                                  make_float2(__uint_as_float(rb[c]), __uint_as_float(rb[c + 1])));
+          ra[c] = __float_as_uint(t.x);
+          ra[c + 1] = __float_as_uint(t.y);
+        }
         tmem_ld16(tb, rb);
         tmem_ld_wait(rb);
       }
@@ -766,9 +773,12 @@ __global__ void __launch_bounds__(kFThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
       if (active) {
+        const float2 sc2 = make_float2(sc, sc);
 #pragma unroll
-        for (int c = 0; c < kEpiCols; ++c)
-          acc[c] = fmaf(__fadd_rn(__uint_as_float(ra[c]), __uint_as_float(rb[c])), sc, acc[c]);
+        for (int c = 0; c < kEpiCols; c += 2)
+          acc[c / 2] = f2_fma(f2_add(make_float2(__uint_as_float(ra[c]), __uint_as_float(ra[c + 1])),
+                                     make_float2(__uint_as_float(rb[c]), __uint_as_float(rb[c + 1]))),
+                              sc2, acc[c / 2]);
       }
       if (++buf == nbuf) buf = 0;
       if (b & 1) {
@@ -783,7 +793,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
       for (int i = 0; i < kEpiCols; ++i)
         if (c0 + i < rows)
           a.y[static_cast<long long>(row0 + c0 + i) * a.ldy + n] =
-              __fmul_rn(acc[i], __ldg(a.rinv + row0 + c0 + i));
+              __fmul_rn((i & 1) ? acc[i / 2].y : acc[i / 2].x, __ldg(a.rinv + row0 + c0 + i));
     }
   }
   tc_fence_before();
