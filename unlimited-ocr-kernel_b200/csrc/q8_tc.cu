@@ -491,7 +491,7 @@ constexpr int kFW8Slots = 8;                                    // int8 weight r
 constexpr int kFWbf = kBN * kFK * 2;                            // 16 KB bf16 weights
 constexpr int kFSRing = 160 * 1024;                             // MMA-stage ring
 constexpr int kFMaxS = 8;
-constexpr int kFSmemBytes = kFW8Slots * kFWi8 + kFSRing + 1024 + 512;
+constexpr int kFSmemBytes = kFW8Slots * kFWi8 + kFSRing + 1024 + 512 + 512 /*tile list*/;
 
 // kind::f16 with bf16 A and B, f32 D, both K-major, M = 128 (N is added at run time).
 constexpr uint32_t kIdescBf16 = (1u << 4)              // D format: f32
@@ -528,14 +528,27 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint6
 // most 8 significant bits, so its bf16 is the float's high half.
 __device__ __forceinline__ uint2 i8x4_to_bf16x4(uint32_t w) {
   const uint32_t u = w ^ 0x80808080u;
-  const float magic = 8388736.0f;  // 2^23 + 128
-  const float f0 = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440)), magic);
-  const float f1 = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441)), magic);
-  const float f2 = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442)), magic);
-  const float f3 = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443)), magic);
-  return make_uint2(__byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632),
-                    __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632));
+  const float2 magic = make_float2(-8388736.0f, -8388736.0f);  // -(2^23 + 128), two lanes per add
+  const float2 lo = f2_add(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440)),
+                                       __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441))),
+                           magic);
+  const float2 hi = f2_add(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442)),
+                                       __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443))),
+                           magic);
+  return make_uint2(__byte_perm(__float_as_uint(lo.x), __float_as_uint(lo.y), 0x7632),
+                    __byte_perm(__float_as_uint(hi.x), __float_as_uint(hi.y), 0x7632));
 }
+
+// Persistent, like the int8 kernel: CTA c takes the tiles c, c + gridDim.x,
+// ... of the same linear order, listed once per CTA ({first row, group | rows
+// << 8 | weight tile << 16}, 8 bytes each: shared memory is nearly full).
+// The activation box is the largest its tiles need, fixed for the CTA, so the
+// stage-slot layout never changes; every ring, the TMEM buffers and the
+// epilogue run on across tile boundaries.
+struct FTile {
+  int row0, packed;
+};
+constexpr int kFMaxCtaTiles = 64;
 
 __global__ void __launch_bounds__(kFThreads, 1)
     q8_tc_gemm_f32_kernel(const __grid_constant__ CUtensorMap tmap_w,
@@ -555,51 +568,64 @@ __global__ void __launch_bounds__(kFThreads, 1)
   uint64_t* empty = conv + kFMaxS;
   uint64_t* tempty = empty + kFMaxS;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + kAccBufs);
-  int* tile = reinterpret_cast<int*>(tmem_holder + 1);
+  int* tile = reinterpret_cast<int*>(tmem_holder + 1);  // tile count, box
+  FTile* ftiles = reinterpret_cast<FTile*>(sring + kFSRing + 512);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kBN;
+  const int ntn = a.N / kBN;
   const int nbk = a.K >> 5, kstages = a.K / kFK;
-  // the tile lookup, over group counts staged in shared memory (as in the int8 kernel)
+  // the tile list, over group counts staged in shared memory (as in the int8 kernel)
   int* scount = reinterpret_cast<int*>(sring);
   if (a.counts)
     for (int g = threadIdx.x; g < a.groups; g += blockDim.x) scount[g] = a.counts[g];
   __syncthreads();
   if (threadIdx.x == 0) {
-    int g = 0, r0 = blockIdx.y * kBM, rows = a.M - blockIdx.y * kBM;
-    if (a.counts) {
-      int t = blockIdx.y;
-      rows = 0;
-      for (g = 0; g < a.groups; ++g) {
-        const int c = scount[g], tiles = (c + kBM - 1) / kBM;
-        if (t < tiles) {
-          r0 = a.offsets[g] + t * kBM;
-          rows = c - t * kBM;
-          break;
+    int n = 0, g = 0, before = 0, maxrows = 0;
+    const int single_tiles = (a.M + kBM - 1) / kBM;
+    for (long long L = blockIdx.x; n < kFMaxCtaTiles; L += gridDim.x) {
+      const int ty = static_cast<int>(L / ntn), nx = static_cast<int>(L % ntn);
+      int grp = 0, r0, rows;
+      if (a.counts) {
+        while (g < a.groups && ty >= before + (scount[g] + kBM - 1) / kBM) {
+          before += (scount[g] + kBM - 1) / kBM;
+          ++g;
         }
-        t -= tiles;
+        if (g >= a.groups) break;
+        grp = g;
+        r0 = a.offsets[g] + (ty - before) * kBM;
+        rows = scount[g] - (ty - before) * kBM;
+      } else {
+        if (ty >= single_tiles) break;
+        r0 = ty * kBM;
+        rows = a.M - r0;
       }
+      rows = rows > kBM ? kBM : rows;
+      maxrows = rows > maxrows ? rows : maxrows;
+      ftiles[n].row0 = r0;
+      ftiles[n].packed = grp | (rows << 8) | (nx << 16);
+      ++n;
     }
-    tile[0] = g;
-    tile[1] = r0;
-    tile[2] = rows > kBM ? kBM : rows;
+    tile[0] = n;
+    tile[1] = maxrows <= 16 ? 16 : maxrows <= 32 ? 32 : 64;
   }
   fence_proxy_async_smem();  // the scratch reads come before the copies that overwrite it
   __syncthreads();
-  const int group = tile[0], row0 = tile[1], rows = tile[2];
-  if (rows <= 0) return;
-  // The activation tile's height: the rows rounded up to 16, 32 or 64.  The
-  // three pieces sit one above the other as one B operand of 3 * box rows, so
-  // one MMA per 16 elements of K covers all three (the MMA instruction, not
-  // the tensor-core arithmetic, is what a stage pays for with small tiles);
-  // a block's sums take 3 * box TMEM columns and the epilogue adds the pieces.
-  const int box = rows <= 16 ? 16 : rows <= 32 ? 32 : 64;
+  const int ntiles = tile[0];
+  if (ntiles == 0) return;  // nothing for this CTA (the grid is an upper bound)
+  // The activation box: the CTA's largest tile rounded up to 16, 32 or 64.
+  // The three pieces sit one above the other as one B operand of 3 * box
+  // rows, so one MMA per 16 elements of K covers all three (the MMA
+  // instruction, not the tensor-core arithmetic, is what a stage pays for
+  // with small tiles); a block's sums take 3 * box TMEM columns and the
+  // epilogue adds the pieces.
+  const int box = tile[1];
   const int bufcols = 3 * box;
   const int nbuf = kTmemCols / bufcols < kAccBufs ? kTmemCols / bufcols : kAccBufs;  // 8, 5 or 2
   // MMA-stage slots: bf16 weights then the pieces; 7, 5 or 4 of them
   const int sbytes = kFWbf + 3 * box * 128;
   const int ns_raw = kFSRing / sbytes;
   const int nS = ns_raw < kFMaxS ? ns_raw : kFMaxS;
+  const int total_stages = ntiles * kstages;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kFW8Slots; ++i) {
@@ -623,14 +649,20 @@ __global__ void __launch_bounds__(kFThreads, 1)
   if (warp == 0) {
     // ---- int8 weights: a deep ring whose slots free as soon as they are converted
     if (lane == 0) {
-      const CUtensorMap* wmap = a.counts ? &a.maps[group].w_rows64 : &tmap_w;
-      for (int ks = 0; ks < kstages; ++ks) {
-        const int w = ks % kFW8Slots;
-        if (ks >= kFW8Slots &&
-            !mbar_wait_spin(&empty8[w], ((ks / kFW8Slots) - 1) & 1, a.status))
+      int i = 0, ks = 0;
+      for (int gs = 0; gs < total_stages; ++gs) {
+        const int w = gs % kFW8Slots;
+        if (gs >= kFW8Slots &&
+            !mbar_wait_spin(&empty8[w], ((gs / kFW8Slots) - 1) & 1, a.status))
           break;
+        const int packed = ftiles[i].packed;
+        const CUtensorMap* wmap = a.counts ? &a.maps[packed & 255].w_rows64 : &tmap_w;
         mbar_arrive_expect_tx(&full8[w], kFWi8);
-        tma_load_2d(w8ring + w * kFWi8, wmap, ks * kFK, n0, &full8[w]);
+        tma_load_2d(w8ring + w * kFWi8, wmap, ks * kFK, (packed >> 16) * kBN, &full8[w]);
+        if (++ks == kstages) {
+          ks = 0;
+          ++i;
+        }
       }
     }
   } else if (warp == 2) {
@@ -638,10 +670,11 @@ __global__ void __launch_bounds__(kFThreads, 1)
     if (lane == 0) {
       const CUtensorMap* xmap = box == 16 ? &tmap_xp16 : box == 32 ? &tmap_xp32 : &tmap_xp;
       const uint32_t tx = 3 * box * 128;
-      int sl = 0, lap = 0;
-      for (int ks = 0; ks < kstages; ++ks) {
+      int sl = 0, lap = 0, i = 0, ks = 0;
+      for (int gs = 0; gs < total_stages; ++gs) {
         if (lap > 0 && !mbar_wait_spin(&empty[sl], (lap - 1) & 1, a.status)) break;
         unsigned char* st = sring + sl * sbytes;
+        const int row0 = ftiles[i].row0;
         mbar_arrive_expect_tx(&fullx[sl], tx);
 #pragma unroll
         for (int p = 0; p < 3; ++p)
@@ -650,6 +683,10 @@ __global__ void __launch_bounds__(kFThreads, 1)
         if (++sl == nS) {
           sl = 0;
           ++lap;
+        }
+        if (++ks == kstages) {
+          ks = 0;
+          ++i;
         }
       }
     }
@@ -662,7 +699,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
       const uint32_t idesc = kIdescBf16 | (static_cast<uint32_t>(bufcols >> 3) << 17);
       int buf = 0, blap = 0, sl = 0, lap = 0;
       bool ok = true;
-      for (int ks = 0; ks < kstages && ok; ++ks) {
+      for (int gs = 0; gs < total_stages && ok; ++gs) {
         ok = mbar_wait_spin(&fullx[sl], lap & 1, a.status) &&
              mbar_wait_spin(&conv[sl], lap & 1, a.status);
         if (!ok) break;
@@ -699,9 +736,9 @@ __global__ void __launch_bounds__(kFThreads, 1)
     // j sits at (r / 8) * 1024 + (r % 8) * 128 + ((j ^ (r % 8)) * 16).
     const int ct = threadIdx.x - 96;
     int sl = 0, lap = 0;
-    for (int ks = 0; ks < kstages; ++ks) {
-      const int w = ks % kFW8Slots;
-      if (!mbar_wait_spin(&full8[w], (ks / kFW8Slots) & 1, a.status)) break;
+    for (int gs = 0; gs < total_stages; ++gs) {
+      const int w = gs % kFW8Slots;
+      if (!mbar_wait_spin(&full8[w], (gs / kFW8Slots) & 1, a.status)) break;
       if (lap > 0 && !mbar_wait_spin(&empty[sl], (lap - 1) & 1, a.status)) break;
       unsigned char* st = sring + sl * sbytes;
       const unsigned char* wi8 = w8ring + w * kFWi8;
@@ -731,69 +768,74 @@ __global__ void __launch_bounds__(kFThreads, 1)
     // block, the three pieces' sums (smallest first) times the block scale
     const int ew = warp - 3 - kFConvWarps;
     const int q = warp & 3, part = ew / 4;
-    const int rl = 32 * q + lane, n = n0 + rl, c0 = kEpiCols * part;
-    const bool active = c0 < rows;  // warp-uniform
+    const int rl = 32 * q + lane, c0 = kEpiCols * part;
     const uint32_t tlane = tmem + (static_cast<uint32_t>(32 * q) << 16) + c0;
-    const float* srow = (a.counts ? a.maps[group].s : a.s) + static_cast<long long>(n) * nbk;
-    // two neighbouring columns per register pair: the piece sums and the
-    // scale fma run as packed f32x2 instructions, each lane rounded as the
-    // scalar operation
-    float2 acc[kEpiCols / 2];
-#pragma unroll
-    for (int i = 0; i < kEpiCols / 2; ++i) acc[i] = make_float2(0.0f, 0.0f);
     bool ok = true;
     int buf = 0, sl = 0, lap = 0;
-    for (int b = 0; b < nbk; ++b) {
-      const float sc = __ldg(srow + b);  // its latency hides behind the wait
-      // the stage's commit (its slot's `empty` phase): the MMA cannot
-      // complete this slot's next stage before this warp has released the
-      // stage's TMEM buffers, so the phase waited for is the latest one
-      if (ok) ok = mbar_wait_try(&empty[sl], lap & 1, a.status);
-      tc_fence_after();
-      // the two small pieces' sums first, then the leading piece's (two
-      // rounds of loads keep the epilogue within the register budget)
-      uint32_t ra[kEpiCols], rb[kEpiCols];
-      if (active) {
-        const uint32_t tb = tlane + buf * bufcols;
-        tmem_ld16(tb + 2 * box, ra);
-        tmem_ld16(tb + box, rb);
-        tmem_ld_wait(ra);
-        tmem_ld_wait(rb);
+    for (int ti = 0; ti < ntiles; ++ti) {
+      const FTile t = ftiles[ti];
+      const int group = t.packed & 255, rows = (t.packed >> 8) & 255;
+      const int n = (t.packed >> 16) * kBN + rl;
+      const bool active = c0 < rows;  // warp-uniform
+      const float* srow = (a.counts ? a.maps[group].s : a.s) + static_cast<long long>(n) * nbk;
+      // two neighbouring columns per register pair: the piece sums and the
+      // scale fma run as packed f32x2 instructions, each lane rounded as the
+      // scalar operation
+      float2 acc[kEpiCols / 2];
 #pragma unroll
-        for (int c = 0; c < kEpiCols; c += 2) {
-          const float2 t = f2_add(make_float2(__uint_as_float(ra[c]), __uint_as_float(ra[c + 1])),
-                                  make_float2(__uint_as_float(rb[c]), __uint_as_float(rb[c + 1])));
-          ra[c] = __float_as_uint(t.x);
-          ra[c + 1] = __float_as_uint(t.y);
+      for (int i = 0; i < kEpiCols / 2; ++i) acc[i] = make_float2(0.0f, 0.0f);
+      for (int b = 0; b < nbk; ++b) {
+        const float sc = __ldg(srow + b);  // its latency hides behind the wait
+        // the stage's commit (its slot's `empty` phase): the MMA cannot
+        // complete this slot's next stage before this warp has released the
+        // stage's TMEM buffers, so the phase waited for is the latest one
+        if (ok) ok = mbar_wait_try(&empty[sl], lap & 1, a.status);
+        tc_fence_after();
+        // the two small pieces' sums first, then the leading piece's (two
+        // rounds of loads keep the epilogue within the register budget)
+        uint32_t ra[kEpiCols], rb[kEpiCols];
+        if (active) {
+          const uint32_t tb = tlane + buf * bufcols;
+          tmem_ld16(tb + 2 * box, ra);
+          tmem_ld16(tb + box, rb);
+          tmem_ld_wait(ra);
+          tmem_ld_wait(rb);
+#pragma unroll
+          for (int c = 0; c < kEpiCols; c += 2) {
+            const float2 s2 = f2_add(make_float2(__uint_as_float(ra[c]), __uint_as_float(ra[c + 1])),
+                                     make_float2(__uint_as_float(rb[c]), __uint_as_float(rb[c + 1])));
+            ra[c] = __float_as_uint(s2.x);
+            ra[c + 1] = __float_as_uint(s2.y);
+          }
+          tmem_ld16(tb, rb);
+          tmem_ld_wait(rb);
         }
-        tmem_ld16(tb, rb);
-        tmem_ld_wait(rb);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[buf]);
-      if (active) {
-        const float2 sc2 = make_float2(sc, sc);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
+        if (active) {
+          const float2 sc2 = make_float2(sc, sc);
 #pragma unroll
-        for (int c = 0; c < kEpiCols; c += 2)
-          acc[c / 2] = f2_fma(f2_add(make_float2(__uint_as_float(ra[c]), __uint_as_float(ra[c + 1])),
-                                     make_float2(__uint_as_float(rb[c]), __uint_as_float(rb[c + 1]))),
-                              sc2, acc[c / 2]);
-      }
-      if (++buf == nbuf) buf = 0;
-      if (b & 1) {
-        if (++sl == nS) {
-          sl = 0;
-          ++lap;
+          for (int c = 0; c < kEpiCols; c += 2)
+            acc[c / 2] = f2_fma(f2_add(make_float2(__uint_as_float(ra[c]), __uint_as_float(ra[c + 1])),
+                                       make_float2(__uint_as_float(rb[c]), __uint_as_float(rb[c + 1]))),
+                                sc2, acc[c / 2]);
+        }
+        if (++buf == nbuf) buf = 0;
+        if (b & 1) {
+          if (++sl == nS) {
+            sl = 0;
+            ++lap;
+          }
         }
       }
-    }
-    if (active) {
+      if (active) {
 #pragma unroll
-      for (int i = 0; i < kEpiCols; ++i)
-        if (c0 + i < rows)
-          a.y[static_cast<long long>(row0 + c0 + i) * a.ldy + n] =
-              __fmul_rn((i & 1) ? acc[i / 2].y : acc[i / 2].x, __ldg(a.rinv + row0 + c0 + i));
+        for (int i = 0; i < kEpiCols; ++i)
+          if (c0 + i < rows)
+            a.y[static_cast<long long>(t.row0 + c0 + i) * a.ldy + n] =
+                __fmul_rn((i & 1) ? acc[i / 2].y : acc[i / 2].x, __ldg(a.rinv + t.row0 + c0 + i));
+      }
     }
   }
   tc_fence_before();
@@ -1015,10 +1057,10 @@ void configure() {
 
 bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
 
-// Grid of the persistent int8 kernel for `tiles` (an upper bound on the
-// tiles): one CTA per SM, more only if a CTA would otherwise own more than
-// kMaxCtaTiles tiles.
-int persistent_grid(long long tiles) {
+// Grid of a persistent GEMM for `tiles` (an upper bound on the tiles): one
+// CTA per SM, more only if a CTA would otherwise own more than max_per_cta
+// tiles (the length of its tile list).
+int persistent_grid(long long tiles, int max_per_cta) {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) {
@@ -1027,7 +1069,7 @@ int persistent_grid(long long tiles) {
   }
   long long g = tiles < sms ? tiles : sms;
   if (g < 1) g = 1;
-  if ((tiles + g - 1) / g > kMaxCtaTiles) g = (tiles + kMaxCtaTiles - 1) / kMaxCtaTiles;
+  if ((tiles + g - 1) / g > max_per_cta) g = (tiles + max_per_cta - 1) / max_per_cta;
   return static_cast<int>(g);
 }
 
@@ -1236,7 +1278,7 @@ cudaError_t launch_q8_tc_single_i8(const Q8View& m, const int8_t* xq, const floa
   a.K = K;
   a.ldy = static_cast<int>(ldy);
   a.status = status;
-  q8_tc_gemm_i8_kernel<<<persistent_grid(static_cast<long long>(N / kBN) * ((batch + kBM - 1) / kBM)),
+  q8_tc_gemm_i8_kernel<<<persistent_grid(static_cast<long long>(N / kBN) * ((batch + kBM - 1) / kBM), kMaxCtaTiles),
                          kThreads, kSmemBytes, st>>>(mm.w_sw128, mm.ws, tx, txs, a);
   return cudaGetLastError();
 }
@@ -1264,7 +1306,7 @@ cudaError_t launch_q8_tc_grouped_i8(const void* maps, int groups, const int* cou
   a.ldy = static_cast<int>(ldy);
   a.status = status;
   // the weight-map parameters are unused when grouped (the maps array is)
-  q8_tc_gemm_i8_kernel<<<persistent_grid(static_cast<long long>(N / kBN) * max_tiles), kThreads,
+  q8_tc_gemm_i8_kernel<<<persistent_grid(static_cast<long long>(N / kBN) * max_tiles, kMaxCtaTiles), kThreads,
                          kSmemBytes, st>>>(tx, txs, tx, txs, a);
   return cudaGetLastError();
 }
@@ -1276,6 +1318,7 @@ cudaError_t launch_q8_tc_single_f32(const Q8View& m, const uint16_t* pieces, con
     return cudaErrorInvalidValue;
   if (!aligned16(m.w) || !aligned16(m.s) || !aligned16(pieces)) return cudaErrorMisalignedAddress;
   const int N = static_cast<int>(m.rows), K = static_cast<int>(m.cols);
+  if (N / kBN > 32767) return cudaErrorInvalidValue;  // the tile list packs the weight tile in 15 bits
   CUtensorMap tw, tp, tp16, tp32;
   if (!make_map_w_rows64(&tw, m.w, N, K) || !make_map_pieces(&tp, pieces, batch, K, kBM) ||
       !make_map_pieces(&tp16, pieces, batch, K, 16) || !make_map_pieces(&tp32, pieces, batch, K, 32))
@@ -1292,8 +1335,9 @@ cudaError_t launch_q8_tc_single_f32(const Q8View& m, const uint16_t* pieces, con
   a.ldy = static_cast<int>(ldy);
   a.piece_rows = batch;
   a.status = status;
-  q8_tc_gemm_f32_kernel<<<dim3(N / kBN, (batch + kBM - 1) / kBM), kFThreads, kFSmemBytes, st>>>(
-      tw, tp, tp16, tp32, a);
+  q8_tc_gemm_f32_kernel<<<persistent_grid(static_cast<long long>(N / kBN) * ((batch + kBM - 1) / kBM),
+                                           kFMaxCtaTiles),
+                          kFThreads, kFSmemBytes, st>>>(tw, tp, tp16, tp32, a);
   return cudaGetLastError();
 }
 
@@ -1301,7 +1345,8 @@ cudaError_t launch_q8_tc_grouped_f32(const void* maps, int groups, const int* co
                                      const int* offsets, int max_tiles, int N, int K,
                                      const uint16_t* pieces, const float* rinv, int total_rows,
                                      float* y, long long ldy, unsigned* status, cudaStream_t st) {
-  if (N % kBN || K % kBK || total_rows < 1 || max_tiles < 1) return cudaErrorInvalidValue;
+  if (N % kBN || K % kBK || total_rows < 1 || max_tiles < 1 || N / kBN > 32767 || groups > 256)
+    return cudaErrorInvalidValue;
   if (!aligned16(pieces) || reinterpret_cast<uintptr_t>(maps) % 64) return cudaErrorMisalignedAddress;
   CUtensorMap tp, tp16, tp32;
   if (!make_map_pieces(&tp, pieces, total_rows, K, kBM) ||
@@ -1323,7 +1368,8 @@ cudaError_t launch_q8_tc_grouped_f32(const void* maps, int groups, const int* co
   a.piece_rows = total_rows;
   a.status = status;
   // the weight-map parameter is unused when grouped (the maps array is)
-  q8_tc_gemm_f32_kernel<<<dim3(N / kBN, max_tiles), kFThreads, kFSmemBytes, st>>>(tp, tp, tp16, tp32, a);
+  q8_tc_gemm_f32_kernel<<<persistent_grid(static_cast<long long>(N / kBN) * max_tiles, kFMaxCtaTiles),
+                          kFThreads, kFSmemBytes, st>>>(tp, tp, tp16, tp32, a);
   return cudaGetLastError();
 }
 
