@@ -113,9 +113,10 @@ __device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
 // rounding modifiers (about 23% of 2 million random pairs differed from the
 // separately rounded operations, every one equal to the fused result, with or
 // without -fmad=false, and in a running sum even with the product moved
-// through another register first).  Add such a product with __fadd_rn per
-// lane: that pairing stays separately rounded (measured over running sums of
-// 40 blocks), and the bit-exact int8 tests hold it.
+// through another register first; also when the add is written as a packed
+// fma(product, 1, acc)).  Add such a product with __fadd_rn per lane: that
+// pairing stays separately rounded (measured over running sums of 40 blocks),
+// and the bit-exact int8 tests hold it.
 __device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
   float2 d;
   asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
