@@ -37,6 +37,7 @@
 #include "device_once.h"
 #include "kernels.h"
 #include "tc_maps.cuh"
+#include "tile_list.cuh"
 
 namespace uocr {
 
@@ -207,36 +208,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (a.counts)
     for (int g = threadIdx.x; g < a.groups; g += blockDim.x) scount[g] = a.counts[g];
   __syncthreads();
-  if (threadIdx.x == 0) {
-    // this CTA's tiles in order; the row tiles of the groups are numbered
-    // group by group (a group of c rows has ceil(c / kBM) of them)
-    int n = 0, g = 0, before = 0;  // `before`: row tiles of the groups before g
-    const int single_tiles = (a.M + kBM - 1) / kBM;
-    for (long long L = blockIdx.x; n < kMaxCtaTiles; L += gridDim.x) {
-      const int ty = static_cast<int>(L / ntn), nx = static_cast<int>(L % ntn);
-      int grp = 0, r0, rows;
-      if (a.counts) {
-        while (g < a.groups && ty >= before + (scount[g] + kBM - 1) / kBM) {
-          before += (scount[g] + kBM - 1) / kBM;
-          ++g;
-        }
-        if (g >= a.groups) break;
-        grp = g;
-        r0 = a.offsets[g] + (ty - before) * kBM;
-        rows = scount[g] - (ty - before) * kBM;
-      } else {
-        if (ty >= single_tiles) break;
-        r0 = ty * kBM;
-        rows = a.M - r0;
-      }
-      tiles[n].group = grp;
-      tiles[n].row0 = r0;
-      tiles[n].rows = rows > kBM ? kBM : rows;
-      tiles[n].n0 = nx * kBN;
-      ++n;
-    }
-    *ntiles_s = n;
-  }
+  if (threadIdx.x == 0)  // this CTA's tiles in order (tile_list.cuh)
+    *ntiles_s = cta_tile_list(blockIdx.x, gridDim.x, ntn, a.M, a.counts ? scount : nullptr,
+                              a.offsets, a.groups, kBM, kMaxCtaTiles,
+                              [&](int i, const TileSpec& t) {
+                                tiles[i].group = t.group;
+                                tiles[i].row0 = t.row0;
+                                tiles[i].rows = t.rows;
+                                tiles[i].n0 = t.nx * kBN;
+                              });
   fence_proxy_async_smem();  // the scratch reads come before the copies that overwrite it
   __syncthreads();
   const int ntiles = *ntiles_s;
@@ -579,33 +559,14 @@ __global__ void __launch_bounds__(kFThreads, 1)
   if (a.counts)
     for (int g = threadIdx.x; g < a.groups; g += blockDim.x) scount[g] = a.counts[g];
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int n = 0, g = 0, before = 0, maxrows = 0;
-    const int single_tiles = (a.M + kBM - 1) / kBM;
-    for (long long L = blockIdx.x; n < kFMaxCtaTiles; L += gridDim.x) {
-      const int ty = static_cast<int>(L / ntn), nx = static_cast<int>(L % ntn);
-      int grp = 0, r0, rows;
-      if (a.counts) {
-        while (g < a.groups && ty >= before + (scount[g] + kBM - 1) / kBM) {
-          before += (scount[g] + kBM - 1) / kBM;
-          ++g;
-        }
-        if (g >= a.groups) break;
-        grp = g;
-        r0 = a.offsets[g] + (ty - before) * kBM;
-        rows = scount[g] - (ty - before) * kBM;
-      } else {
-        if (ty >= single_tiles) break;
-        r0 = ty * kBM;
-        rows = a.M - r0;
-      }
-      rows = rows > kBM ? kBM : rows;
-      maxrows = rows > maxrows ? rows : maxrows;
-      ftiles[n].row0 = r0;
-      ftiles[n].packed = grp | (rows << 8) | (nx << 16);
-      ++n;
-    }
-    tile[0] = n;
+  if (threadIdx.x == 0) {  // this CTA's tiles in order (tile_list.cuh) and the rows of its largest
+    int maxrows = 0;
+    tile[0] = cta_tile_list(blockIdx.x, gridDim.x, ntn, a.M, a.counts ? scount : nullptr, a.offsets,
+                            a.groups, kBM, kFMaxCtaTiles, [&](int i, const TileSpec& t) {
+                              ftiles[i].row0 = t.row0;
+                              ftiles[i].packed = t.group | (t.rows << 8) | (t.nx << 16);
+                              maxrows = t.rows > maxrows ? t.rows : maxrows;
+                            });
     tile[1] = maxrows <= 16 ? 16 : maxrows <= 32 ? 32 : 64;
   }
   fence_proxy_async_smem();  // the scratch reads come before the copies that overwrite it
@@ -1057,9 +1018,8 @@ void configure() {
 
 bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
 
-// Grid of a persistent GEMM for `tiles` (an upper bound on the tiles): one
-// CTA per SM, more only if a CTA would otherwise own more than max_per_cta
-// tiles (the length of its tile list).
+// Grid of a persistent GEMM for `tiles` (an upper bound on the tiles):
+// persistent_ctas (tile_list.cuh) with this device's SM count.
 int persistent_grid(long long tiles, int max_per_cta) {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) != cudaSuccess ||
@@ -1067,10 +1027,7 @@ int persistent_grid(long long tiles, int max_per_cta) {
     cudaGetLastError();
     sms = 148;
   }
-  long long g = tiles < sms ? tiles : sms;
-  if (g < 1) g = 1;
-  if ((tiles + g - 1) / g > max_per_cta) g = (tiles + max_per_cta - 1) / max_per_cta;
-  return static_cast<int>(g);
+  return persistent_ctas(tiles, sms, max_per_cta);
 }
 
 // ---- BF16 weights, FP32 activations (ops::linear_weight, BF16 branch) ---------
